@@ -1,0 +1,464 @@
+// attn_prefill_sm100.cu -- causal / sliding-window GQA flash attention on the
+// 5th-generation tensor cores (K4).
+//
+// One CTA computes a 128-row query tile of one query head against the key
+// blocks its rows can see, reading K/V straight out of the device cache:
+//
+//   warp 0      TMA producer: Q tile once, then K/V blocks into a 2-stage ring
+//               (cp.async.bulk.tensor, 128-byte swizzle, no multicast)
+//   warp 1      allocates TMEM and issues tcgen05.mma from one thread:
+//                 S_j = Q K_j^T  (M=128, N=BN, K=DH)  into TMEM (two S buffers)
+//                 O  += P_j V_j  (M=128, N=DH, K=BN)  into TMEM (O accumulator)
+//   warps 2..5  softmax: thread i owns query row i, reads its S row from TMEM,
+//               applies the causal/window mask, an online softmax in base 2
+//               (rescaling O in TMEM only when the running max grows by more
+//               than 2^8), writes P as bf16/fp16 in the UMMA K-major swizzled
+//               layout, and at the end normalises O and stores the row.
+//
+// The equation is the reference reduction (nm/src/qwen35.hpp:360-382,
+// nm/src/gemma4.hpp:593-615, :687-709): softmax over visible rows of
+// scale * q.k, then the alpha-weighted sum of values; visibility is
+// CausalWindow (nm/src/attention.hpp:154-176) in closed form per row.
+#include <math.h>
+#include <stdio.h>
+
+#include "attn.cuh"
+#include "tcgen05.cuh"
+
+namespace nmg {
+namespace {
+
+template <int DH>
+struct PfCfg {
+    static constexpr int BM = 128;
+    static constexpr int BN = DH == 128 ? 128 : 64;
+    static constexpr int STAGES = 2;
+    static constexpr int Q_BYTES = BM * DH * 2;
+    static constexpr int K_BYTES = BN * DH * 2;
+    static constexpr int V_BYTES = BN * DH * 2;
+    static constexpr int P_BYTES = BM * BN * 2;
+    static constexpr int Q_OFF = 0;
+    static constexpr int K_OFF = Q_OFF + Q_BYTES;
+    static constexpr int V_OFF = K_OFF + STAGES * K_BYTES;
+    static constexpr int P_OFF = V_OFF + STAGES * V_BYTES;
+    static constexpr int BAR_OFF = P_OFF + P_BYTES;
+    static constexpr int NBARS = 1 + 2 * STAGES + 2 + 2 + 1 + 1;
+    static constexpr int TMEMPTR_OFF = BAR_OFF + NBARS * 8;
+    static constexpr int SMEM = TMEMPTR_OFF + 16 + 1024;  // + slack to align the base to 1024
+    static constexpr uint32_t TMEM_COLS = 512;
+    static constexpr uint32_t O_COL = 2 * BN;
+    static_assert(2 * BN + DH <= 512, "TMEM budget");
+    static_assert(SMEM <= 232448, "shared memory budget");
+};
+
+struct PrefillArgs {
+    CUtensorMap tm_q;  // (d, head, row) over q [rows][hq*DH]
+    CUtensorMap tm_k;  // (d, hkv*slots) over the cache
+    CUtensorMap tm_v;
+    int64_t rows, first_query, window, floor_pos, newest, base, slots;
+    int hq, hkv, g;
+    float scale_log2;
+    void* out;
+    int out_dtype;
+    int* err;
+};
+
+__device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* map, int32_t x, int32_t y, int32_t z,
+                                            uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cta.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+        "[%5];" ::"r"(dev::smem_u32(smem_dst)),
+        "l"(map), "r"(x), "r"(y), "r"(z), "r"(dev::smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ float ex2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+__device__ __forceinline__ uint32_t pack2(float lo, float hi, bool bf16) {
+    if (bf16) {
+        __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+        return *reinterpret_cast<uint32_t*>(&v);
+    }
+    __half2 v = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&v);
+}
+
+__device__ __forceinline__ int64_t vis_lo(const PrefillArgs& a, int64_t q) {
+    int64_t lo = a.floor_pos;
+    if (a.window > 0 && q - a.window + 1 > lo) lo = q - a.window + 1;
+    return lo;
+}
+__device__ __forceinline__ int64_t vis_hi(const PrefillArgs& a, int64_t q) { return q < a.newest ? q : a.newest; }
+
+template <int DH, bool BF16>
+__global__ void __launch_bounds__(192, 1) attn_prefill_kernel(const __grid_constant__ PrefillArgs a) {
+    using C = PfCfg<DH>;
+    constexpr int BM = C::BM, BN = C::BN, ST = C::STAGES;
+    extern __shared__ unsigned char smem_raw[];
+    unsigned char* smem = (unsigned char*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    uint64_t* bars = (uint64_t*)(smem + C::BAR_OFF);
+    uint64_t* q_full = bars;
+    uint64_t* kv_full = bars + 1;
+    uint64_t* kv_empty = bars + 1 + ST;
+    uint64_t* s_full = bars + 1 + 2 * ST;
+    uint64_t* s_free = s_full + 2;
+    uint64_t* p_full = s_free + 2;
+    uint64_t* o_done = p_full + 1;
+    uint32_t* tmem_slot = (uint32_t*)(smem + C::TMEMPTR_OFF);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int tile = gridDim.x - 1 - blockIdx.x;  // heaviest tiles first
+    const int h = blockIdx.y;
+    const int hk = h / a.g;
+    const int64_t t0 = (int64_t)tile * BM;
+    const int64_t t_last = (t0 + BM < a.rows ? t0 + BM : a.rows) - 1;
+    const int64_t q_first = a.first_query + t0, q_last = a.first_query + t_last;
+    const int64_t u_lo = vis_lo(a, q_first) - a.base;
+    const int64_t u_hi = vis_hi(a, q_last) - a.base;
+    const int64_t j_begin = u_lo / BN;
+    const int nblk = (int)(u_hi / BN + 1 - j_begin);
+    // A block needs no mask when every row of the tile sees all of it.
+    const int64_t full_lo = vis_lo(a, q_last), full_hi = vis_hi(a, q_first);
+
+    if (threadIdx.x == 0) {
+        dev::mbar_init(q_full, 1);
+        for (int s = 0; s < ST; ++s) {
+            dev::mbar_init(&kv_full[s], 1);
+            dev::mbar_init(&kv_empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            dev::mbar_init(&s_full[b], 1);
+            dev::mbar_init(&s_free[b], 128);
+        }
+        dev::mbar_init(p_full, 128);
+        dev::mbar_init(o_done, 1);
+        dev::fence_mbar_init();
+    }
+    if (warp == 1) {
+        tc::tmem_alloc(tmem_slot, C::TMEM_COLS);
+        tc::tmem_relinquish();
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ------------------------------------------------ TMA producer
+            dev::prefetch_tensormap(&a.tm_q);
+            dev::prefetch_tensormap(&a.tm_k);
+            dev::prefetch_tensormap(&a.tm_v);
+            dev::mbar_arrive_expect_tx(q_full, C::Q_BYTES);
+#pragma unroll
+            for (int c = 0; c < DH / 64; ++c)
+                tma_load_3d(smem + C::Q_OFF + c * BM * 128, &a.tm_q, c * 64, h, (int32_t)t0, q_full);
+            for (int i = 0; i < nblk; ++i) {
+                const int s = i % ST;
+                if (i >= ST && !dev::mbar_wait(&kv_empty[s], ((i / ST) - 1) & 1, a.err)) break;
+                const int64_t u0 = (j_begin + i) * BN;
+                const int32_t row = (int32_t)(hk * a.slots + u0 % a.slots);
+                dev::mbar_arrive_expect_tx(&kv_full[s], C::K_BYTES + C::V_BYTES);
+#pragma unroll
+                for (int c = 0; c < DH / 64; ++c) {
+                    dev::tma_load_2d(smem + C::K_OFF + s * C::K_BYTES + c * BN * 128, &a.tm_k, c * 64, row, &kv_full[s]);
+                    dev::tma_load_2d(smem + C::V_OFF + s * C::V_BYTES + c * BN * 128, &a.tm_v, c * 64, row, &kv_full[s]);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // ------------------------------------------------ MMA issuer
+            constexpr uint32_t idesc_s = tc::idesc_f16(128, BN, BF16 ? 1 : 0, 0, 0);
+            constexpr uint32_t idesc_o = tc::idesc_f16(128, DH, BF16 ? 1 : 0, 0, 1);
+            const uint32_t sbase = dev::smem_u32(smem);
+            bool ok = dev::mbar_wait(q_full, 0, a.err);
+            auto issue_pv = [&](int i) -> bool {
+                if (!dev::mbar_wait(p_full, i & 1, a.err)) return false;
+                tc::fence_after_sync();
+                const int s = i % ST;
+#pragma unroll
+                for (int k = 0; k < BN / 16; ++k) {
+                    const uint64_t ad = tc::smem_desc_sw128(sbase + C::P_OFF + (k / 4) * BM * 128 + (k % 4) * 32, 16, 1024);
+                    const uint64_t bd =
+                        tc::smem_desc_sw128(sbase + C::V_OFF + s * C::V_BYTES + k * 2048, BN * 128, 1024);
+                    tc::mma_f16_ss(tmem + C::O_COL, ad, bd, idesc_o, (i > 0 || k > 0) ? 1u : 0u);
+                }
+                tc::commit(o_done);
+                tc::commit(&kv_empty[s]);
+                return true;
+            };
+            for (int i = 0; ok && i < nblk; ++i) {
+                const int s = i % ST, sb = i & 1;
+                if (!dev::mbar_wait(&kv_full[s], (i / ST) & 1, a.err)) break;
+                if (i >= 2 && !dev::mbar_wait(&s_free[sb], ((i - 2) >> 1) & 1, a.err)) break;
+                tc::fence_after_sync();
+#pragma unroll
+                for (int k = 0; k < DH / 16; ++k) {
+                    const uint64_t ad = tc::smem_desc_sw128(sbase + C::Q_OFF + (k / 4) * BM * 128 + (k % 4) * 32, 16, 1024);
+                    const uint64_t bd =
+                        tc::smem_desc_sw128(sbase + C::K_OFF + s * C::K_BYTES + (k / 4) * BN * 128 + (k % 4) * 32, 16, 1024);
+                    tc::mma_f16_ss(tmem + sb * BN, ad, bd, idesc_s, k > 0 ? 1u : 0u);
+                }
+                tc::commit(&s_full[sb]);
+                if (i >= 1 && !issue_pv(i - 1)) {
+                    ok = false;
+                    break;
+                }
+            }
+            if (ok && nblk > 0) issue_pv(nblk - 1);
+        }
+    } else {
+        // ---------------------------------------------------- softmax warps
+        const int quad = warp & 3;  // TMEM lane quadrant this warp may access
+        const int row = quad * 32 + lane;
+        const uint32_t t_lane = tmem + ((uint32_t)(quad * 32) << 16);
+        const int64_t qpos = a.first_query + t0 + row;
+        const bool row_valid = t0 + row < a.rows;
+        const int64_t lo = vis_lo(a, qpos), hi = vis_hi(a, qpos);
+        unsigned char* pbuf = smem + C::P_OFF;
+        float m_run = -INFINITY, l_run = 0.f;
+        bool ok = true;
+
+        for (int i = 0; i < nblk; ++i) {
+            const int sb = i & 1;
+            // Waits are voted warp-wide so the .sync.aligned TMEM accesses
+            // below always see a converged warp.
+            if (!__all_sync(0xffffffffu, dev::mbar_wait(&s_full[sb], (i >> 1) & 1, a.err))) {
+                ok = false;
+                break;
+            }
+            tc::fence_after_sync();
+            float x[BN];
+#pragma unroll
+            for (int c = 0; c < BN / 32; ++c) {
+                uint32_t r[32];
+                tc::ld_32x32b_x32(t_lane + sb * BN + c * 32, r);
+#pragma unroll
+                for (int e = 0; e < 32; ++e) x[c * 32 + e] = __uint_as_float(r[e]) * a.scale_log2;
+            }
+            tc::fence_before_sync();
+            dev::mbar_arrive(&s_free[sb]);
+
+            const int64_t p0 = a.base + (j_begin + i) * BN;
+            if (!(p0 >= full_lo && p0 + BN - 1 <= full_hi)) {
+#pragma unroll
+                for (int e = 0; e < BN; ++e) {
+                    const int64_t pos = p0 + e;
+                    if (pos < lo || pos > hi) x[e] = -INFINITY;
+                }
+            }
+            float mb = x[0];
+#pragma unroll
+            for (int e = 1; e < BN; ++e) mb = fmaxf(mb, x[e]);
+            const float m_new = fmaxf(m_run, mb);
+            const bool rescale = m_new > m_run + 8.0f;  // also true for the first finite block
+            float alpha = 1.f;
+            if (rescale) {
+                alpha = (m_run == -INFINITY) ? 0.f : ex2(m_run - m_new);
+                m_run = m_new;
+            }
+            const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
+            float sum = 0.f;
+#pragma unroll
+            for (int e = 0; e < BN; ++e) {
+                x[e] = ex2(x[e] - m_use);
+                sum += x[e];
+            }
+            l_run = l_run * alpha + sum;
+
+            // P_{i-1} . V_{i-1} must be finished before P is overwritten or O rescaled.
+            if (i >= 1 && !__all_sync(0xffffffffu, dev::mbar_wait(o_done, (i - 1) & 1, a.err))) {
+                ok = false;
+                break;
+            }
+            if (i >= 1 && __any_sync(0xffffffffu, rescale)) {
+                tc::fence_after_sync();
+#pragma unroll 1
+                for (int c = 0; c < DH / 32; ++c) {
+                    uint32_t r[32];
+                    tc::ld_32x32b_x32(t_lane + C::O_COL + c * 32, r);
+#pragma unroll
+                    for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * alpha);
+                    tc::st_32x32b_x32(t_lane + C::O_COL + c * 32, r);
+                }
+                tc::wait_st();
+            }
+            // P row -> shared memory, K-major with the 128-byte swizzle.
+#pragma unroll
+            for (int c8 = 0; c8 < BN / 8; ++c8) {
+                const int kb = c8 >> 3, cc = c8 & 7;
+                uint4 v;
+                v.x = pack2(x[c8 * 8 + 0], x[c8 * 8 + 1], BF16);
+                v.y = pack2(x[c8 * 8 + 2], x[c8 * 8 + 3], BF16);
+                v.z = pack2(x[c8 * 8 + 4], x[c8 * 8 + 5], BF16);
+                v.w = pack2(x[c8 * 8 + 6], x[c8 * 8 + 7], BF16);
+                *(uint4*)(pbuf + kb * BM * 128 + row * 128 + ((cc ^ (row & 7)) << 4)) = v;
+            }
+            dev::fence_proxy_async_smem();
+            tc::fence_before_sync();
+            dev::mbar_arrive(p_full);
+        }
+
+        if (ok && nblk > 0 && __all_sync(0xffffffffu, dev::mbar_wait(o_done, (nblk - 1) & 1, a.err))) {
+            tc::fence_after_sync();
+            const float inv = 1.f / l_run;
+            const int64_t obase = ((t0 + row) * (int64_t)a.hq + h) * DH;
+#pragma unroll 1
+            for (int c = 0; c < DH / 32; ++c) {
+                uint32_t r[32];
+                tc::ld_32x32b_x32(t_lane + C::O_COL + c * 32, r);
+                if (row_valid) {
+                    if (a.out_dtype == NMG_F32) {
+                        float4* dst = (float4*)((float*)a.out + obase + c * 32);
+#pragma unroll
+                        for (int e = 0; e < 8; ++e)
+                            dst[e] = make_float4(__uint_as_float(r[4 * e]) * inv, __uint_as_float(r[4 * e + 1]) * inv,
+                                                 __uint_as_float(r[4 * e + 2]) * inv, __uint_as_float(r[4 * e + 3]) * inv);
+                    } else {
+                        uint4* dst = (uint4*)((uint16_t*)a.out + obase + c * 32);
+                        const bool obf = a.out_dtype == NMG_BF16;
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            uint4 v;
+                            uint32_t w[4];
+#pragma unroll
+                            for (int t = 0; t < 4; ++t) {
+                                const float f0 = __uint_as_float(r[8 * e + 2 * t]) * inv;
+                                const float f1 = __uint_as_float(r[8 * e + 2 * t + 1]) * inv;
+                                const uint32_t b0 = obf ? dev::f32_to_bf16_bits(f0) : dev::f32_to_f16_bits(f0);
+                                const uint32_t b1 = obf ? dev::f32_to_bf16_bits(f1) : dev::f32_to_f16_bits(f1);
+                                w[t] = b0 | (b1 << 16);
+                            }
+                            v.x = w[0];
+                            v.y = w[1];
+                            v.z = w[2];
+                            v.w = w[3];
+                            dst[e] = v;
+                        }
+                    }
+                }
+            }
+        }
+    }
+
+    tc::fence_before_sync();
+    __syncthreads();
+    if (warp == 1) {
+        tc::fence_after_sync();
+        tc::tmem_dealloc(tmem, C::TMEM_COLS);
+    }
+}
+
+// ------------------------------------------------------------------ host side
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    if (!fn) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = (EncodeTiledFn)p;
+    }
+    return fn;
+}
+
+template <int DH, bool BF16>
+int launch_prefill(const PrefillArgs& a, dim3 grid, cudaStream_t s) {
+    using C = PfCfg<DH>;
+    auto kern = attn_prefill_kernel<DH, BF16>;
+    static unsigned attr_set = 0;
+    int dev_id = 0;
+    NMG_CUDA_TRY(cudaGetDevice(&dev_id));
+    if (!(attr_set & (1u << (dev_id & 31)))) {
+        NMG_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+        attr_set |= 1u << (dev_id & 31);
+    }
+    kern<<<grid, 192, C::SMEM, s>>>(a);
+    NMG_CUDA_TRY(cudaGetLastError());
+    return NMG_OK;
+}
+
+}  // namespace
+
+bool prefill_supported(const nmg_kv_cache* c, int hq, int q_dtype, int64_t rows) {
+    if (c->dtype == NMG_F32 || q_dtype != c->dtype) return false;
+    if (c->dh != 128 && c->dh != 256) return false;
+    const int bn = c->dh == 128 ? 128 : 64;
+    if (c->slots % bn != 0) return false;
+    if (rows < 64) return false;
+    if ((int64_t)c->hkv * c->slots > 0x7FFFFFFF) return false;
+    return encode_fn() != nullptr;
+}
+
+int attend_rows_prefill(const nmg_kv_cache* c, int hq, const void* q, int q_dtype, int64_t rows, int64_t first_query,
+                        int64_t window, int64_t floor_pos, int64_t newest, float scale, void* out, int out_dtype,
+                        cudaStream_t stream) {
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return set_error(NMG_UNSUPPORTED, "cuTensorMapEncodeTiled unavailable");
+    if (((uintptr_t)q & 15) || ((uintptr_t)c->k & 15) || ((uintptr_t)c->v & 15))
+        return set_error(NMG_UNSUPPORTED, "prefill: 16-byte aligned tensors required");
+    const int dh = c->dh;
+    const CUtensorMapDataType dt = c->dtype == NMG_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    PrefillArgs* a = new PrefillArgs();
+    {
+        cuuint64_t dims[3] = {(cuuint64_t)dh, (cuuint64_t)hq, (cuuint64_t)rows};
+        cuuint64_t strides[2] = {(cuuint64_t)dh * 2, (cuuint64_t)hq * dh * 2};
+        cuuint32_t box[3] = {64, 1, 128};
+        cuuint32_t es[3] = {1, 1, 1};
+        CUresult r = enc(&a->tm_q, dt, 3, (void*)q, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (r != CUDA_SUCCESS) {
+            delete a;
+            return set_error(NMG_CUDA_ERROR, "prefill: Q tensor map (%d)", (int)r);
+        }
+    }
+    const int bn = dh == 128 ? 128 : 64;
+    for (int which = 0; which < 2; ++which) {
+        cuuint64_t dims[2] = {(cuuint64_t)dh, (cuuint64_t)c->hkv * (cuuint64_t)c->slots};
+        cuuint64_t strides[1] = {(cuuint64_t)dh * 2};
+        cuuint32_t box[2] = {64, (cuuint32_t)bn};
+        cuuint32_t es[2] = {1, 1};
+        CUresult r = enc(which ? &a->tm_v : &a->tm_k, dt, 2, which ? c->v : c->k, dims, strides, box, es,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (r != CUDA_SUCCESS) {
+            delete a;
+            return set_error(NMG_CUDA_ERROR, "prefill: K/V tensor map (%d)", (int)r);
+        }
+    }
+    a->rows = rows;
+    a->first_query = first_query;
+    a->window = window;
+    a->floor_pos = floor_pos;
+    a->newest = newest;
+    a->base = c->base;
+    a->slots = c->slots;
+    a->hq = hq;
+    a->hkv = c->hkv;
+    a->g = hq / c->hkv;
+    a->scale_log2 = scale * 1.4426950408889634f;
+    a->out = out;
+    a->out_dtype = out_dtype;
+    int st = device_error_flag(c->device, &a->err);
+    if (st == NMG_OK) {
+        dim3 grid((unsigned)((rows + 127) / 128), (unsigned)hq);
+        if (dh == 128)
+            st = c->dtype == NMG_BF16 ? launch_prefill<128, true>(*a, grid, stream) : launch_prefill<128, false>(*a, grid, stream);
+        else
+            st = c->dtype == NMG_BF16 ? launch_prefill<256, true>(*a, grid, stream) : launch_prefill<256, false>(*a, grid, stream);
+    }
+    delete a;
+    return st;
+}
+
+}  // namespace nmg

@@ -1,0 +1,286 @@
+// delta.cu -- gated delta-rule state, the per-token recurrent step (K6) and
+// the token-sequential prefill; the chunked WY-form prefill (K5) is in
+// delta_chunked.cu.
+//
+// Reference: nm/src/recurrent.hpp:117-177 (DeltaNetState, gated_delta_step)
+// and the head loop of nm/src/qwen35.hpp:436-456 (value head h reads key head
+// h % Hk, qwen35.hpp:172).  Per head and token, with S in R^{Dk x Dv}:
+//     S *= exp(g);  pred = S^T k;  d = (v - pred) * beta;  S += k d^T;  o = S^T q
+// Columns of S evolve independently (column j only needs v_j and column j of
+// S), which is how both kernels split a head across threads and CTAs.
+#include <math.h>
+
+#include "common.cuh"
+
+struct nmg_delta_state {
+    int heads = 0, dk = 0, dv = 0, device = 0;
+    float* data = nullptr;  // [heads][dk][dv]
+};
+
+namespace nmg {
+namespace {
+
+// ---- one token, every head ---------------------------------------------------
+// grid (heads, ceil(dv/32)); 8 warps; lane = column, warp w owns rows
+// [w*RPW, (w+1)*RPW).  Two partial-sum reductions across the 8 warps.
+template <int DK>
+__global__ void __launch_bounds__(256) delta_step_kernel(float* __restrict__ state, int dv, int hk,
+                                                         const float* __restrict__ q, const float* __restrict__ k,
+                                                         const float* __restrict__ v, const float* __restrict__ gate,
+                                                         const float* __restrict__ beta, float* __restrict__ out,
+                                                         int64_t head_stride_q) {
+    constexpr int RPW = (DK + 7) / 8;
+    __shared__ float red[8][32];
+    __shared__ float col[32];
+    const int h = blockIdx.x;
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const int j = blockIdx.y * 32 + lane;
+    const bool cv = j < dv;
+    const int kh = h % hk;
+    const float* kk = k + kh * head_stride_q;
+    const float* qq = q + kh * head_stride_q;
+    float* S = state + (int64_t)h * DK * dv;
+    const float decay = __expf(gate[h]);
+
+    float s[RPW];
+    float part = 0.f;
+#pragma unroll
+    for (int r = 0; r < RPW; ++r) {
+        const int i = w * RPW + r;
+        s[r] = (cv && i < DK) ? S[(int64_t)i * dv + j] * decay : 0.f;
+        if (i < DK) part = fmaf(s[r], __ldg(kk + i), part);
+    }
+    red[w][lane] = part;
+    __syncthreads();
+    if (w == 0) {
+        float p = 0.f;
+#pragma unroll
+        for (int x = 0; x < 8; ++x) p += red[x][lane];
+        col[lane] = cv ? (v[(int64_t)h * dv + j] - p) * beta[h] : 0.f;
+    }
+    __syncthreads();
+    const float d = col[lane];
+    part = 0.f;
+#pragma unroll
+    for (int r = 0; r < RPW; ++r) {
+        const int i = w * RPW + r;
+        if (i < DK) {
+            s[r] = fmaf(__ldg(kk + i), d, s[r]);
+            part = fmaf(s[r], __ldg(qq + i), part);
+            if (cv) S[(int64_t)i * dv + j] = s[r];
+        }
+    }
+    __syncthreads();  // red[] is reused
+    red[w][lane] = part;
+    __syncthreads();
+    if (w == 0 && cv) {
+        float o = 0.f;
+#pragma unroll
+        for (int x = 0; x < 8; ++x) o += red[x][lane];
+        out[(int64_t)h * dv + j] = o;
+    }
+}
+
+// ---- T tokens, state held in registers ---------------------------------------
+// grid (heads, ceil(dv/16)); 128 threads; warp w owns columns 4w..4w+3 of the
+// CTA's 16, lane = (column-in-warp (4) x row group (8)); a row group holds
+// DK/8 rows.  Row reductions are 3 xor-shuffles inside the 8-lane group.
+template <int DK>
+__global__ void __launch_bounds__(128) delta_seq_kernel(float* __restrict__ state, int dv, int hk, int heads, int64_t T,
+                                                        const float* __restrict__ q, const float* __restrict__ k,
+                                                        const float* __restrict__ v, const float* __restrict__ gate,
+                                                        const float* __restrict__ beta, float* __restrict__ out) {
+    constexpr int RPG = (DK + 7) / 8;  // rows per group
+    constexpr int TB = 8;              // tokens staged per refill
+    __shared__ __align__(16) float ks[TB][DK];
+    __shared__ __align__(16) float qs[TB][DK];
+    const int h = blockIdx.x;
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const int grp = lane & 7;
+    const int j = blockIdx.y * 16 + w * 4 + (lane >> 3);
+    const bool cv = j < dv;
+    const int kh = h % hk;
+    float* S = state + (int64_t)h * DK * dv;
+
+    float s[RPG];
+#pragma unroll
+    for (int r = 0; r < RPG; ++r) {
+        const int i = grp * RPG + r;
+        s[r] = (cv && i < DK) ? S[(int64_t)i * dv + j] : 0.f;
+    }
+    for (int64_t t0 = 0; t0 < T; t0 += TB) {
+        const int nt = (int)(T - t0 < TB ? T - t0 : TB);
+        __syncthreads();
+        for (int x = threadIdx.x; x < nt * DK; x += 128) {
+            const int tt = x / DK, i = x % DK;
+            ks[tt][i] = k[((t0 + tt) * hk + kh) * (int64_t)DK + i];
+            qs[tt][i] = q[((t0 + tt) * hk + kh) * (int64_t)DK + i];
+        }
+        __syncthreads();
+        for (int tt = 0; tt < nt; ++tt) {
+            const int64_t t = t0 + tt;
+            const float decay = __expf(gate[t * heads + h]);
+            const float b = beta[t * heads + h];
+            const float vj = cv ? v[(t * heads + h) * (int64_t)dv + j] : 0.f;
+            float part = 0.f;
+#pragma unroll
+            for (int r = 0; r < RPG; ++r) {
+                const int i = grp * RPG + r;
+                s[r] *= decay;
+                if (i < DK) part = fmaf(s[r], ks[tt][i], part);
+            }
+            part += __shfl_xor_sync(0xffffffffu, part, 1);
+            part += __shfl_xor_sync(0xffffffffu, part, 2);
+            part += __shfl_xor_sync(0xffffffffu, part, 4);
+            const float d = (vj - part) * b;
+            float o = 0.f;
+#pragma unroll
+            for (int r = 0; r < RPG; ++r) {
+                const int i = grp * RPG + r;
+                if (i < DK) {
+                    s[r] = fmaf(ks[tt][i], d, s[r]);
+                    o = fmaf(s[r], qs[tt][i], o);
+                }
+            }
+            o += __shfl_xor_sync(0xffffffffu, o, 1);
+            o += __shfl_xor_sync(0xffffffffu, o, 2);
+            o += __shfl_xor_sync(0xffffffffu, o, 4);
+            if (cv && grp == 0) out[(t * heads + h) * (int64_t)dv + j] = o;
+        }
+    }
+#pragma unroll
+    for (int r = 0; r < RPG; ++r) {
+        const int i = grp * RPG + r;
+        if (cv && i < DK) S[(int64_t)i * dv + j] = s[r];
+    }
+}
+
+#define NMG_DK_CASES(KERNEL, GRID, BLOCK, STREAM, ...)                                    \
+    switch (dk) {                                                                         \
+        case 2: KERNEL<2><<<GRID, BLOCK, 0, STREAM>>>(__VA_ARGS__); break;               \
+        case 4: KERNEL<4><<<GRID, BLOCK, 0, STREAM>>>(__VA_ARGS__); break;               \
+        case 8: KERNEL<8><<<GRID, BLOCK, 0, STREAM>>>(__VA_ARGS__); break;               \
+        case 16: KERNEL<16><<<GRID, BLOCK, 0, STREAM>>>(__VA_ARGS__); break;             \
+        case 32: KERNEL<32><<<GRID, BLOCK, 0, STREAM>>>(__VA_ARGS__); break;             \
+        case 64: KERNEL<64><<<GRID, BLOCK, 0, STREAM>>>(__VA_ARGS__); break;             \
+        case 128: KERNEL<128><<<GRID, BLOCK, 0, STREAM>>>(__VA_ARGS__); break;           \
+        case 256: KERNEL<256><<<GRID, BLOCK, 0, STREAM>>>(__VA_ARGS__); break;           \
+        default: return set_error(NMG_UNSUPPORTED, "delta rule: Dk=%d is not built", dk); \
+    }
+
+bool dk_supported(int dk) { return dk == 2 || dk == 4 || dk == 8 || dk == 16 || dk == 32 || dk == 64 || dk == 128 || dk == 256; }
+
+}  // namespace
+
+int delta_prefill_chunked(nmg_delta_state* st, int hk, int64_t T, const float* q, const float* k, const float* v,
+                          const float* gate, const float* beta, float* out, int chunk, cudaStream_t stream);
+
+int delta_prefill_sequential(nmg_delta_state* st, int hk, int64_t T, const float* q, const float* k, const float* v,
+                             const float* gate, const float* beta, float* out, cudaStream_t stream) {
+    const int dk = st->dk;
+    dim3 grid(st->heads, (st->dv + 15) / 16);
+    NMG_DK_CASES(delta_seq_kernel, grid, 128, stream, st->data, st->dv, hk, st->heads, T, q, k, v, gate, beta, out)
+    NMG_CUDA_TRY(cudaGetLastError());
+    return NMG_OK;
+}
+
+}  // namespace nmg
+
+using nmg::set_error;
+
+extern "C" int nmg_delta_create(int heads, int dk, int dv, int device, nmg_delta_state** out) {
+    if (!out) return set_error(NMG_INVALID_ARGUMENT, "nmg_delta_create: null out");
+    *out = nullptr;
+    if (heads <= 0 || dk <= 0 || dv <= 0) return set_error(NMG_INVALID_ARGUMENT, "DeltaNetState: dimensions must be positive");
+    if (!nmg::dk_supported(dk)) return set_error(NMG_UNSUPPORTED, "DeltaNetState: Dk=%d is not built", dk);
+    nmg_delta_state* s = new nmg_delta_state();
+    s->heads = heads;
+    s->dk = dk;
+    s->dv = dv;
+    s->device = device;
+    int prev = 0;
+    cudaError_t e = cudaGetDevice(&prev);
+    if (e == cudaSuccess) e = cudaSetDevice(device);
+    const size_t bytes = (size_t)heads * dk * dv * sizeof(float);
+    if (e == cudaSuccess) e = cudaMalloc(&s->data, bytes);
+    if (e == cudaSuccess) e = cudaMemset(s->data, 0, bytes);  // DeltaNetState() zero-fills (recurrent.hpp:123)
+    cudaSetDevice(prev);
+    if (e != cudaSuccess) {
+        if (s->data) cudaFree(s->data);
+        delete s;
+        return set_error(NMG_CUDA_ERROR, "nmg_delta_create: %s", cudaGetErrorString(e));
+    }
+    *out = s;
+    return NMG_OK;
+}
+
+extern "C" int nmg_delta_destroy(nmg_delta_state* s) {
+    if (!s) return NMG_OK;
+    int prev = 0;
+    cudaGetDevice(&prev);
+    cudaSetDevice(s->device);
+    cudaFree(s->data);
+    cudaSetDevice(prev);
+    delete s;
+    return NMG_OK;
+}
+
+extern "C" int nmg_delta_clear(nmg_delta_state* s, void* stream) {
+    if (!s) return set_error(NMG_INVALID_ARGUMENT, "nmg_delta_clear: null state");
+    NMG_CUDA_TRY(cudaMemsetAsync(s->data, 0, (size_t)s->heads * s->dk * s->dv * sizeof(float), (cudaStream_t)stream));
+    return NMG_OK;
+}
+
+extern "C" int nmg_delta_head(nmg_delta_state* s, int head, float** ptr) {
+    if (!s || !ptr) return set_error(NMG_INVALID_ARGUMENT, "nmg_delta_head: null argument");
+    if (head < 0 || head >= s->heads) return set_error(NMG_OUT_OF_RANGE, "DeltaNetState: head out of range");
+    *ptr = s->data + (size_t)head * s->dk * s->dv;
+    return NMG_OK;
+}
+
+extern "C" int nmg_gated_delta_step(float* state_head, int dk, int dv, const float* q, const float* k, const float* v,
+                                    const float* gate, const float* beta, float* out, void* stream) {
+    if (!state_head || !q || !k || !v || !gate || !beta || !out)
+        return set_error(NMG_INVALID_ARGUMENT, "gated_delta_step: null argument");
+    if (dv <= 0 || !nmg::dk_supported(dk)) return set_error(NMG_UNSUPPORTED, "gated_delta_step: Dk=%d is not built", dk);
+    dim3 grid(1, (dv + 31) / 32);
+    cudaStream_t s = (cudaStream_t)stream;
+    NMG_DK_CASES(nmg::delta_step_kernel, grid, 256, s, state_head, dv, 1, q, k, v, gate, beta, out, (int64_t)dk)
+    NMG_CUDA_TRY(cudaGetLastError());
+    return NMG_OK;
+}
+
+extern "C" int nmg_delta_step(nmg_delta_state* st, int hk, const float* q, const float* k, const float* v,
+                              const float* gate, const float* beta, float* out, void* stream) {
+    if (!st) return set_error(NMG_INVALID_ARGUMENT, "nmg_delta_step: null state");
+    if (hk <= 0 || hk > st->heads) return set_error(NMG_INVALID_ARGUMENT, "nmg_delta_step: bad key-head count %d", hk);
+    const int dk = st->dk;
+    dim3 grid(st->heads, (st->dv + 31) / 32);
+    cudaStream_t s = (cudaStream_t)stream;
+    int prev = 0;
+    NMG_CUDA_TRY(cudaGetDevice(&prev));
+    if (prev != st->device) NMG_CUDA_TRY(cudaSetDevice(st->device));
+    NMG_DK_CASES(nmg::delta_step_kernel, grid, 256, s, st->data, st->dv, hk, q, k, v, gate, beta, out, (int64_t)dk)
+    NMG_CUDA_TRY(cudaGetLastError());
+    if (prev != st->device) NMG_CUDA_TRY(cudaSetDevice(prev));
+    return NMG_OK;
+}
+
+extern "C" int nmg_delta_prefill(nmg_delta_state* st, int hk, int64_t T, const float* q, const float* k, const float* v,
+                                 const float* gate, const float* beta, float* out, int chunk, void* stream) {
+    if (!st) return set_error(NMG_INVALID_ARGUMENT, "nmg_delta_prefill: null state");
+    if (hk <= 0 || hk > st->heads) return set_error(NMG_INVALID_ARGUMENT, "nmg_delta_prefill: bad key-head count %d", hk);
+    if (T < 0) return set_error(NMG_INVALID_ARGUMENT, "nmg_delta_prefill: negative length");
+    if (T == 0) return NMG_OK;
+    if (chunk != 0 && chunk != 64) return set_error(NMG_UNSUPPORTED, "nmg_delta_prefill: chunk must be 0 or 64");
+    int prev = 0;
+    NMG_CUDA_TRY(cudaGetDevice(&prev));
+    if (prev != st->device) NMG_CUDA_TRY(cudaSetDevice(st->device));
+    int r;
+    if (chunk == 0)
+        r = nmg::delta_prefill_sequential(st, hk, T, q, k, v, gate, beta, out, (cudaStream_t)stream);
+    else
+        r = nmg::delta_prefill_chunked(st, hk, T, q, k, v, gate, beta, out, chunk, (cudaStream_t)stream);
+    if (prev != st->device) cudaSetDevice(prev);
+    return r;
+}

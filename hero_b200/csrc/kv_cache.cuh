@@ -1,0 +1,52 @@
+// kv_cache.cuh -- the device KV cache object shared by the cache and attention code.
+#pragma once
+#include "common.cuh"
+
+// Device-resident replacement for FullAttentionCache / LocalAttentionCache
+// (nm/src/attention.hpp:201-395).  Storage is head-major, [hkv][slots][dh]
+// for K and for V, so one head's keys for consecutive positions are one
+// contiguous run (a single bulk copy per tile) and a KV-head group shards by
+// pointer offset.  Position p lives in slot (p - base) mod slots.
+//
+// The logical fields (size, oldest, retention) follow the reference's
+// bookkeeping exactly and are kept on the host, so size()/position()/
+// visible_rows() never touch the device.
+struct nmg_kv_cache {
+    int hkv = 0, dh = 0, dtype = NMG_F32, device = 0;
+    int64_t window = 0;  // 0: full (append-only) cache
+    int64_t slots = 0;   // physical rows per head
+    void* k = nullptr;
+    void* v = nullptr;
+
+    int64_t size = 0;    // logical rows (reference size())
+    int64_t oldest = 0;  // position of chronological row 0
+    int64_t base = 0;    // first position ever appended (slot origin)
+    int64_t total = 0;   // rows ever appended
+    bool retaining = false;
+    int64_t batch_remaining = 0;
+
+    int64_t newest() const { return oldest + size - 1; }
+    // Slot of a position that is physically present.
+    int64_t slot_of(int64_t position) const { return (position - base) % slots; }
+};
+
+namespace nmg {
+
+// Half-open visible position range of a query for a cache as it stands:
+// [max(q - window + 1, floor), min(q, newest)] in positions.
+struct VisibleSpan {
+    int64_t lo, hi;  // inclusive positions; empty when lo > hi
+};
+
+inline VisibleSpan visible_span(int64_t query, int64_t window, int64_t floor_pos, int64_t newest) {
+    int64_t lo = floor_pos;
+    if (window > 0 && query - window + 1 > lo) lo = query - window + 1;
+    int64_t hi = query < newest ? query : newest;
+    return VisibleSpan{lo, hi};
+}
+
+// Append kernel launcher (kv_cache.cu).
+int kv_append_device(nmg_kv_cache* c, int64_t first_position, const void* keys, const void* values, int64_t rows,
+                     int src_dtype, cudaStream_t stream);
+
+}  // namespace nmg

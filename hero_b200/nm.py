@@ -1,0 +1,333 @@
+"""The reference's attention / KV-cache / delta-rule interface, device-resident.
+
+Mirrors the nm engine's types and calls (paths relative to the nm/ project):
+
+* ``FullAttentionCache`` / ``LocalAttentionCache`` -- src/attention.hpp:201-395
+  (append, size, position, visible_rows, key, value, window,
+  can_append_without_eviction, begin/end_batch_retention), same exceptions.
+* ``attend`` -- the per-layer softmax reduction (src/qwen35.hpp:360-382 with a
+  score scale; src/gemma4.hpp:211-235 et al. with none).
+* ``append_attend`` -- a layer's append-then-reduce step with the Gemma local
+  fallback (src/gemma4.hpp:237-253, :617-630).
+* ``scaled_dot_product_attention`` -- src/attention.hpp:124-139.
+* ``DeltaNetState`` / ``gated_delta_step`` -- src/recurrent.hpp:117-177, and
+  ``delta_step`` / ``delta_prefill`` for the head loop of src/qwen35.hpp:436-456.
+
+Every call goes through libnmg.so's C ABI.  Tensors are torch CUDA tensors
+(torch provides device memory and streams only); nothing here computes on the
+host.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+
+import torch
+
+from . import _lib
+from ._lib import BF16, F16, F32, call
+
+_DT = {torch.float32: F32, torch.float16: F16, torch.bfloat16: BF16}
+_TORCH = {F32: torch.float32, F16: torch.float16, BF16: torch.bfloat16}
+
+
+def dtype_code(dt) -> int:
+    if isinstance(dt, int):
+        return dt
+    if isinstance(dt, str):
+        return {"f32": F32, "fp32": F32, "f16": F16, "fp16": F16, "bf16": BF16}[dt]
+    return _DT[dt]
+
+
+def _stream(device) -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def _ptr(t: torch.Tensor) -> ctypes.c_void_p:
+    return ctypes.c_void_p(t.data_ptr())
+
+
+def _dev(t: torch.Tensor) -> torch.Tensor:
+    if not t.is_cuda:
+        raise ValueError("device tensors expected")
+    return t.contiguous()
+
+
+@dataclass(frozen=True)
+class VisibleRows:
+    """Half-open chronological row interval (src/attention.hpp:144-150)."""
+
+    first: int
+    end: int
+
+    def empty(self) -> bool:
+        return self.first == self.end
+
+    def count(self) -> int:
+        return self.end - self.first
+
+
+class _Cache:
+    def __init__(self, hkv: int, head_dim: int, window: int, capacity: int, dtype, device: int):
+        self.hkv, self.head_dim = int(hkv), int(head_dim)
+        self.dtype = dtype_code(dtype)
+        self.device = int(device)
+        h = ctypes.c_void_p()
+        call("nmg_kv_create", self.hkv, self.head_dim, self.dtype, int(window), int(capacity), self.device,
+             ctypes.byref(h))
+        self._h = h
+
+    @property
+    def handle(self) -> ctypes.c_void_p:
+        return self._h
+
+    def __del__(self):
+        h = getattr(self, "_h", None)
+        if h is not None and h.value:
+            try:
+                _lib.lib().nmg_kv_destroy(h)
+            except Exception:
+                pass
+            self._h = None
+
+    @property
+    def width(self) -> int:
+        return self.hkv * self.head_dim
+
+    def size(self) -> int:
+        v = ctypes.c_int64()
+        call("nmg_kv_size", self._h, ctypes.byref(v))
+        return v.value
+
+    def window(self) -> int:
+        v = ctypes.c_int64()
+        call("nmg_kv_window", self._h, ctypes.byref(v))
+        return v.value
+
+    def position(self, chronological_row: int) -> int:
+        v = ctypes.c_int64()
+        call("nmg_kv_position", self._h, int(chronological_row), ctypes.byref(v))
+        return v.value
+
+    def can_append_without_eviction(self, rows: int) -> bool:
+        v = ctypes.c_int()
+        call("nmg_kv_can_append_without_eviction", self._h, int(rows), ctypes.byref(v))
+        return bool(v.value)
+
+    def append(self, position: int, key: torch.Tensor, value: torch.Tensor) -> None:
+        """Append one row ([hkv*head_dim]) or a batch of consecutive rows ([rows, hkv*head_dim])."""
+        key, value = _dev(key), _dev(value)
+        if key.shape != value.shape or key.shape[-1] != self.width:
+            raise _lib.InvalidArgument("append: key/value rows must be [.., hkv*head_dim]")
+        rows = 1 if key.dim() == 1 else key.shape[0]
+        call("nmg_kv_append", self._h, int(position), _ptr(key), _ptr(value), rows, _DT[key.dtype],
+             _stream(key.device))
+
+    def visible_rows(self, query: int) -> VisibleRows:
+        f, e = ctypes.c_int64(), ctypes.c_int64()
+        call("nmg_kv_visible_rows", self._h, int(query), ctypes.byref(f), ctypes.byref(e))
+        return VisibleRows(f.value, e.value)
+
+    def _row(self, chronological_row: int, head: int):
+        k = (ctypes.c_float * self.head_dim)()
+        v = (ctypes.c_float * self.head_dim)()
+        call("nmg_kv_read_row", self._h, int(chronological_row), int(head), k, v, _stream(self.device))
+        return torch.tensor(list(k), dtype=torch.float32), torch.tensor(list(v), dtype=torch.float32)
+
+    def key(self, chronological_row: int, head: int) -> torch.Tensor:
+        """Host copy of one cached key (slow debug accessor; attention.hpp:228-232)."""
+        return self._row(chronological_row, head)[0]
+
+    def value(self, chronological_row: int, head: int) -> torch.Tensor:
+        return self._row(chronological_row, head)[1]
+
+    def storage(self):
+        """(keys_ptr, values_ptr, slots) of the head-major device storage."""
+        k, v, s = ctypes.c_void_p(), ctypes.c_void_p(), ctypes.c_int64()
+        call("nmg_kv_storage", self._h, ctypes.byref(k), ctypes.byref(v), ctypes.byref(s))
+        return k.value, v.value, s.value
+
+
+class FullAttentionCache(_Cache):
+    """Append-only device K/V cache (src/attention.hpp:201-250) of `capacity` rows."""
+
+    def __init__(self, hkv: int, head_dim: int, *, capacity: int, dtype="f32", device: int = 0):
+        super().__init__(hkv, head_dim, 0, capacity, dtype, device)
+
+
+class LocalAttentionCache(_Cache):
+    """Fixed-window ring (src/attention.hpp:252-395).
+
+    ``capacity`` physical rows (default: window rounded up to 128) bound how
+    many rows one batch may append and still be attended as a whole and how
+    large a retained batch may grow; ``append_attend`` chunks larger batches.
+    """
+
+    def __init__(self, hkv: int, head_dim: int, window: int, *, capacity: int | None = None, dtype="f32",
+                 device: int = 0):
+        if window <= 0:
+            raise _lib.InvalidArgument("LocalAttentionCache: window must be positive")
+        if capacity is None:
+            capacity = (window + 127) // 128 * 128
+        super().__init__(hkv, head_dim, window, capacity, dtype, device)
+
+    def begin_batch_retention(self, appended_rows: int) -> None:
+        call("nmg_kv_begin_batch_retention", self._h, int(appended_rows))
+
+    def end_batch_retention(self) -> None:
+        call("nmg_kv_end_batch_retention", self._h)
+
+
+def _out(q: torch.Tensor, out, out_dtype):
+    if out is not None:
+        return out
+    dt = _TORCH[dtype_code(out_dtype)] if out_dtype is not None else q.dtype
+    return torch.empty(q.shape, dtype=dt, device=q.device)
+
+
+def attend(cache: _Cache, q: torch.Tensor, at: int, scale: float | None = None, *, out=None, out_dtype=None):
+    """Reduce query rows q [rows, hq*head_dim] at positions at.. over the cache.
+
+    ``scale=None`` is the Gemma form (scores are plain dot products);
+    otherwise scores are ``scale * dot`` (the Qwen form, scale 1/sqrt(head_dim)).
+    """
+    q = _dev(q)
+    if q.dim() == 1:
+        q = q.unsqueeze(0)
+    if q.shape[-1] % cache.head_dim:
+        raise _lib.InvalidArgument("attend: query width is not a whole number of heads")
+    hq = q.shape[-1] // cache.head_dim
+    out = _out(q, out, out_dtype)
+    call("nmg_attend", cache.handle, hq, _ptr(q), _DT[q.dtype], q.shape[0], int(at),
+         float(scale if scale is not None else 1.0), 0 if scale is None else 1, _ptr(out), _DT[out.dtype],
+         _stream(q.device))
+    return out
+
+
+def append_attend(cache: _Cache, position: int, key: torch.Tensor, value: torch.Tensor, q: torch.Tensor,
+                  scale: float | None = None, *, out=None, out_dtype=None):
+    """Append rows at position.. then reduce the matching queries, as a layer does."""
+    key, value, q = _dev(key), _dev(value), _dev(q)
+    hq = q.shape[-1] // cache.head_dim
+    out = _out(q, out, out_dtype)
+    call("nmg_append_attend", cache.handle, int(position), _ptr(key), _ptr(value), _DT[key.dtype], hq, _ptr(q),
+         _DT[q.dtype], q.shape[0], float(scale if scale is not None else 1.0), 0 if scale is None else 1, _ptr(out),
+         _DT[out.dtype], _stream(q.device))
+    return out
+
+
+def attend_batch(caches, q: torch.Tensor, scale: float | None = None, *, queries_at=None, out=None, out_dtype=None):
+    """One decode query per cache: q [batch, hq*head_dim]."""
+    q = _dev(q)
+    n = len(caches)
+    arr = (ctypes.c_void_p * n)(*[c.handle.value for c in caches])
+    qa = None
+    if queries_at is not None:
+        qa = (ctypes.c_int64 * n)(*[int(x) for x in queries_at])
+    hq = q.shape[-1] // caches[0].head_dim
+    out = _out(q, out, out_dtype)
+    call("nmg_attend_batch", arr, n, qa, hq, _ptr(q), _DT[q.dtype], float(scale if scale is not None else 1.0),
+         0 if scale is None else 1, _ptr(out), _DT[out.dtype], _stream(q.device))
+    return out
+
+
+def scaled_dot_product_attention(q, k, v, heads: int, scale: float, *, out=None, out_dtype=None):
+    """softmax_rows(scale * Q K^T) V per head, no mask (src/attention.hpp:124-139)."""
+    q, k, v = _dev(q), _dev(k), _dev(v)
+    if k.shape[0] != v.shape[0]:
+        raise _lib.InvalidArgument("scaled_dot_product_attention: K/V row mismatch")
+    head_dim = q.shape[-1] // heads
+    out = _out(q, out, out_dtype)
+    call("nmg_sdpa", heads, head_dim, _ptr(q), _ptr(k), _ptr(v), _DT[q.dtype], q.shape[0], k.shape[0], float(scale),
+         _ptr(out), _DT[out.dtype], _stream(q.device))
+    return out
+
+
+class DeltaNetState:
+    """Device fp32 [heads][dk][dv] state, zero-initialised (src/recurrent.hpp:117-138)."""
+
+    def __init__(self, heads: int, dk: int, dv: int, device: int = 0):
+        self.heads, self.dk, self.dv, self.device = int(heads), int(dk), int(dv), int(device)
+        h = ctypes.c_void_p()
+        call("nmg_delta_create", self.heads, self.dk, self.dv, self.device, ctypes.byref(h))
+        self._h = h
+        p = ctypes.c_void_p()
+        call("nmg_delta_head", self._h, 0, ctypes.byref(p))
+        self._base = p.value
+
+    def __del__(self):
+        h = getattr(self, "_h", None)
+        if h is not None and h.value:
+            try:
+                _lib.lib().nmg_delta_destroy(h)
+            except Exception:
+                pass
+            self._h = None
+
+    @property
+    def handle(self):
+        return self._h
+
+    def clear(self) -> None:
+        call("nmg_delta_clear", self._h, _stream(self.device))
+
+    def head_ptr(self, h: int) -> int:
+        p = ctypes.c_void_p()
+        call("nmg_delta_head", self._h, int(h), ctypes.byref(p))
+        return p.value
+
+    def tensor(self) -> torch.Tensor:
+        """A torch view of the whole device state (no copy)."""
+        n = self.heads * self.dk * self.dv
+        storage = _from_ptr(self._base, n, self.device)
+        return storage.view(self.heads, self.dk, self.dv)
+
+    def head(self, h: int) -> torch.Tensor:
+        self.head_ptr(h)  # range check, OutOfRange like recurrent.hpp:128
+        return self.tensor()[h]
+
+
+def _from_ptr(ptr: int, n: int, device: int) -> torch.Tensor:
+    """Wrap n fp32 device values at ptr as a tensor (the owner keeps them alive)."""
+
+    class _Holder:
+        def __init__(self, p, n, dev):
+            self.__cuda_array_interface__ = {"shape": (n,), "typestr": "<f4", "data": (p, False), "version": 3,
+                                             "strides": None}
+            self.dev = dev
+
+    with torch.cuda.device(device):
+        return torch.as_tensor(_Holder(ptr, n, device), device=f"cuda:{device}")
+
+
+def gated_delta_step(state_head: torch.Tensor, q, k, v, gate, beta) -> torch.Tensor:
+    """One head, one token (src/recurrent.hpp:146-177); state_head [dk, dv] updated in place.
+
+    gate/beta are device tensors of one element (so a CUDA graph can replay the step).
+    """
+    dk, dv = state_head.shape
+    out = torch.empty(dv, dtype=torch.float32, device=state_head.device)
+    gate = torch.as_tensor(gate, dtype=torch.float32, device=state_head.device).reshape(1)
+    beta = torch.as_tensor(beta, dtype=torch.float32, device=state_head.device).reshape(1)
+    call("nmg_gated_delta_step", ctypes.c_void_p(state_head.data_ptr()), dk, dv, _ptr(_dev(q)), _ptr(_dev(k)),
+         _ptr(_dev(v)), _ptr(gate), _ptr(beta), _ptr(out), _stream(state_head.device))
+    return out
+
+
+def delta_step(state: DeltaNetState, q, k, v, gate, beta, hk: int, *, out=None) -> torch.Tensor:
+    """One token through every value head (src/qwen35.hpp:449-454)."""
+    if out is None:
+        out = torch.empty(state.heads, state.dv, dtype=torch.float32, device=q.device)
+    call("nmg_delta_step", state.handle, int(hk), _ptr(_dev(q)), _ptr(_dev(k)), _ptr(_dev(v)), _ptr(_dev(gate)),
+         _ptr(_dev(beta)), _ptr(out), _stream(q.device))
+    return out
+
+
+def delta_prefill(state: DeltaNetState, q, k, v, gate, beta, hk: int, *, chunk: int = 64, out=None) -> torch.Tensor:
+    """T tokens of the recurrence: q,k [T,hk,dk], v [T,heads,dv], gate/beta [T,heads]."""
+    T = v.shape[0]
+    if out is None:
+        out = torch.empty(T, state.heads, state.dv, dtype=torch.float32, device=v.device)
+    call("nmg_delta_prefill", state.handle, int(hk), T, _ptr(_dev(q)), _ptr(_dev(k)), _ptr(_dev(v)), _ptr(_dev(gate)),
+         _ptr(_dev(beta)), _ptr(out), int(chunk), _stream(v.device))
+    return out

@@ -1,0 +1,210 @@
+/*
+ * nmg.h -- C ABI of the B200 (sm_100a) attention / KV-cache / gated delta-rule
+ * path for the nm engine.
+ *
+ * Plain pointers and sizes only.  Every function returns an int status:
+ *
+ *   NMG_OK                 0
+ *   NMG_INVALID_ARGUMENT   1  std::invalid_argument (non-consecutive position, bad shape)
+ *   NMG_OUT_OF_RANGE       2  std::out_of_range     (row or head index)
+ *   NMG_RUNTIME_ERROR      3  std::runtime_error    (a query with no visible key)
+ *   NMG_LENGTH_ERROR       4  std::length_error     (capacity exhausted)
+ *   NMG_LOGIC_ERROR        5  std::logic_error      (batch-retention misuse)
+ *   NMG_CUDA_ERROR         6  a CUDA runtime call failed
+ *   NMG_DEVICE_TIMEOUT     7  a bounded device-side wait gave up
+ *   NMG_COMM_ERROR         8  an NCCL call failed
+ *   NMG_UNSUPPORTED        9  shape / dtype combination not built
+ *
+ * nmg_last_error() returns the message of the last failure on this thread.
+ * The exception types are the ones the reference throws at the cited lines;
+ * include/nmg.hpp maps the codes back onto them.
+ *
+ * Device pointers are raw device addresses; `stream` is a cudaStream_t (NULL =
+ * legacy default stream).  Nothing here synchronises the stream unless it says
+ * so.  A handle is used from one host thread and one stream at a time, like the
+ * reference's caches, which are owned by one model thread (src/core.cpp:30-54
+ * runs one par_for job at a time).
+ *
+ * Reference paths are relative to the nm/ project root.
+ */
+#ifndef NMG_H
+#define NMG_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define NMG_API __attribute__((visibility("default")))
+#else
+#define NMG_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define NMG_OK 0
+#define NMG_INVALID_ARGUMENT 1
+#define NMG_OUT_OF_RANGE 2
+#define NMG_RUNTIME_ERROR 3
+#define NMG_LENGTH_ERROR 4
+#define NMG_LOGIC_ERROR 5
+#define NMG_CUDA_ERROR 6
+#define NMG_DEVICE_TIMEOUT 7
+#define NMG_COMM_ERROR 8
+#define NMG_UNSUPPORTED 9
+
+/* Element types.  The reference computes in fp32 (Scalar = float,
+ * src/core.hpp:31) and rounds to fp16/bf16 with src/core.hpp:61-100; the
+ * device rounds with the same bit-exact rules. */
+#define NMG_F32 0
+#define NMG_F16 1
+#define NMG_BF16 2
+
+NMG_API const char* nmg_last_error(void);
+NMG_API const char* nmg_version(void);
+
+/* ---- device KV cache -------------------------------------------------------
+ *
+ * Replaces FullAttentionCache<Hkv,HeadDim> (src/attention.hpp:201-250) when
+ * window == 0, and LocalAttentionCache<Hkv,HeadDim>(window)
+ * (src/attention.hpp:252-395) when window > 0.
+ *
+ * Device layout: K and V are separate buffers [hkv][slots][head_dim] in
+ * `dtype`; the position p lives in slot (p - first position ever appended)
+ * mod slots.  `capacity` is the number of slots.  A full cache fails with
+ * NMG_LENGTH_ERROR once more than `capacity` rows were appended.  A local
+ * cache keeps logical rows exactly as the reference (window-sized ring, batch
+ * retention) while physically holding the last `capacity` rows, so one batch
+ * of up to capacity - window + 1 rows can be attended as a whole.
+ */
+typedef struct nmg_kv_cache nmg_kv_cache;
+
+NMG_API int nmg_kv_create(int hkv, int head_dim, int dtype, int64_t window, int64_t capacity, int device, nmg_kv_cache** out);
+NMG_API int nmg_kv_destroy(nmg_kv_cache* cache);
+
+/* FullAttentionCache::append / LocalAttentionCache::append, for `rows`
+ * consecutive positions first_position.. at once (attention.hpp:215-220,
+ * :320-345).  keys/values: device [rows][hkv*head_dim] in src_dtype (the
+ * reference's token-major row layout); converted to the cache dtype on the
+ * way in.  Positions must continue the cache (NMG_INVALID_ARGUMENT). */
+NMG_API int nmg_kv_append(nmg_kv_cache* cache, int64_t first_position, const void* keys, const void* values, int64_t rows,
+                  int src_dtype, void* stream);
+
+/* size() / position(row) / window() / can_append_without_eviction(rows)
+ * (attention.hpp:207-213, :262-267, :315-318).  Host-side state, no sync. */
+NMG_API int nmg_kv_size(const nmg_kv_cache* cache, int64_t* size);
+NMG_API int nmg_kv_position(const nmg_kv_cache* cache, int64_t chronological_row, int64_t* position);
+NMG_API int nmg_kv_window(const nmg_kv_cache* cache, int64_t* window);
+NMG_API int nmg_kv_can_append_without_eviction(const nmg_kv_cache* cache, int64_t rows, int* answer);
+
+/* visible_rows(query) (attention.hpp:222-226, :347-351): the half-open
+ * chronological row interval; NMG_RUNTIME_ERROR when it is empty. */
+NMG_API int nmg_kv_visible_rows(const nmg_kv_cache* cache, int64_t query_position, int64_t* first, int64_t* end);
+
+/* LocalAttentionCache::begin_batch_retention / end_batch_retention
+ * (attention.hpp:274-313).  NMG_LOGIC_ERROR as the reference throws. */
+NMG_API int nmg_kv_begin_batch_retention(nmg_kv_cache* cache, int64_t appended_rows);
+NMG_API int nmg_kv_end_batch_retention(nmg_kv_cache* cache);
+
+/* key(row, KVHead) / value(row, KVHead) (attention.hpp:228-237, :353-360) as a
+ * synchronous copy-back to host fp32 [head_dim]; a debug accessor. */
+NMG_API int nmg_kv_read_row(const nmg_kv_cache* cache, int64_t chronological_row, int kv_head, float* key_out, float* value_out,
+                    void* stream);
+
+/* Raw device storage, for callers that fuse their own producer. */
+NMG_API int nmg_kv_storage(const nmg_kv_cache* cache, void** keys, void** values, int64_t* slots);
+
+/* ---- attention ---------------------------------------------------------------
+ *
+ * The softmax reduction the reference writes inline per layer
+ * (src/qwen35.hpp:360-382; src/gemma4.hpp:211-235, :302-321, :593-615,
+ * :687-709): for every query row t (position first_query + t) and query head h,
+ *   out[t,h] = sum_j softmax_j(s_j) * V[j, h/(hq/hkv)],
+ *   s_j = scale * dot(q[t,h], K[j, h/(hq/hkv)])        (use_scale != 0, Qwen)
+ *   s_j =         dot(q[t,h], K[j, h/(hq/hkv)])        (use_scale == 0, Gemma)
+ * over the cache's visible_rows(first_query + t) as the cache stands now.
+ * q: device [rows][hq*head_dim] in q_dtype; out: device [rows][hq*head_dim] in
+ * out_dtype.  Dispatches to the tcgen05 flash kernel for 16-bit caches with
+ * head_dim 128/256 and many rows, and to the split-KV decode kernel otherwise.
+ * NMG_RUNTIME_ERROR if any query sees no key (checked on the host first). */
+NMG_API int nmg_attend(const nmg_kv_cache* cache, int hq, const void* q, int q_dtype, int64_t rows, int64_t first_query,
+               float scale, int use_scale, void* out, int out_dtype, void* stream);
+
+/* The append-then-reduce step of a layer in one call.  Equivalent to the
+ * reference's own choice (gemma4.hpp:237-253, :617-630): when the batch fits
+ * without eviction it appends and reduces the batch; otherwise it gives every
+ * query the keys the token-by-token path would (append one row, reduce one
+ * query), computed as one batched kernel, chunking batches larger than the
+ * ring's spare capacity. */
+NMG_API int nmg_append_attend(nmg_kv_cache* cache, int64_t first_position, const void* keys, const void* values, int kv_dtype,
+                      int hq, const void* q, int q_dtype, int64_t rows, float scale, int use_scale, void* out,
+                      int out_dtype, void* stream);
+
+/* Batched single-token decode over `batch` independent caches (one reference
+ * cache per sequence), query b at position queries_at[b] (host array; pass
+ * NULL for "each cache's newest position").  q: device [batch][hq*head_dim];
+ * out: device [batch][hq*head_dim].  All caches share hkv/head_dim/dtype. */
+NMG_API int nmg_attend_batch(const nmg_kv_cache* const* caches, int batch, const int64_t* queries_at, int hq, const void* q,
+                     int q_dtype, float scale, int use_scale, void* out, int out_dtype, void* stream);
+
+/* Dense, unmasked attention scaled_dot_product_attention<Heads,Dqk,Dv>
+ * (src/attention.hpp:124-139) over plain device tensors q [tq][heads*d],
+ * k/v [tk][heads*d] (no cache, no mask; heads == kv heads). */
+NMG_API int nmg_sdpa(int heads, int head_dim, const void* q, const void* k, const void* v, int dtype, int64_t tq, int64_t tk,
+             float scale, void* out, int out_dtype, void* stream);
+
+/* ---- gated delta-rule state -------------------------------------------------
+ *
+ * DeltaNetState<Heads,Dk,Dv> (src/recurrent.hpp:117-138): device fp32
+ * [heads][dk][dv], row i = key dim, column j = value dim, zero-initialised. */
+typedef struct nmg_delta_state nmg_delta_state;
+
+NMG_API int nmg_delta_create(int heads, int dk, int dv, int device, nmg_delta_state** out);
+NMG_API int nmg_delta_destroy(nmg_delta_state* state);
+NMG_API int nmg_delta_clear(nmg_delta_state* state, void* stream);
+/* head(h) (recurrent.hpp:127-134): device pointer to the [dk][dv] block. */
+NMG_API int nmg_delta_head(nmg_delta_state* state, int head, float** head_ptr);
+
+/* gated_delta_step<Dk,Dv> (recurrent.hpp:146-177) for one head and one token:
+ * decay = exp(gate); S *= decay; pred = S^T k; d = (v - pred) * beta;
+ * S += k (x) d; out = S^T q (read after the write).  All device fp32;
+ * gate/beta are device scalars so a graph can replay the step. */
+NMG_API int nmg_gated_delta_step(float* state_head, int dk, int dv, const float* q, const float* k, const float* v,
+                         const float* gate, const float* beta, float* out, void* stream);
+
+/* One token through every value head: the loop of src/qwen35.hpp:449-454.
+ * q,k: [hk][dk] (L2-normalised, q pre-scaled, as recurrent.hpp:144-145
+ * requires), v: [heads][dv], gate/beta: [heads], out: [heads][dv]; value head
+ * h reads key head h % hk (qwen35.hpp:172). */
+NMG_API int nmg_delta_step(nmg_delta_state* state, int hk, const float* q, const float* k, const float* v, const float* gate,
+                   const float* beta, float* out, void* stream);
+
+/* T tokens of the same recurrence (qwen35.hpp:436-456 over a prefill batch):
+ * q,k: [T][hk][dk], v: [T][heads][dv], gate/beta: [T][heads],
+ * out: [T][heads][dv].  chunk = 0 runs the token-sequential kernel; chunk = 64
+ * runs the chunked WY-form kernel (same result within fp32 rounding). */
+NMG_API int nmg_delta_prefill(nmg_delta_state* state, int hk, int64_t T, const float* q, const float* k, const float* v,
+                      const float* gate, const float* beta, float* out, int chunk, void* stream);
+
+/* ---- multi-GPU: KV-head-group sharding + one all-gather --------------------
+ *
+ * The reference has no distributed backend (it runs par_for on one host).
+ * These sit outside it: one process per GPU, NCCL over NVLink.  The unique id
+ * (128 bytes) is made on rank 0 and shipped to the others by the caller. */
+typedef struct nmg_comm nmg_comm;
+
+NMG_API int nmg_comm_unique_id(void* id128);
+NMG_API int nmg_comm_init(const void* id128, int rank, int world, int device, nmg_comm** out);
+NMG_API int nmg_comm_destroy(nmg_comm* comm);
+/* All-gather of equal byte-sized blocks: recv[world][bytes_per_rank]. */
+NMG_API int nmg_allgather(nmg_comm* comm, const void* send, void* recv, int64_t bytes_per_rank, void* stream);
+/* Scatter the gathered per-rank head blocks [world][rows][hq_local*d] into
+ * the reference row layout [rows][world*hq_local*d] (elem_bytes per value). */
+NMG_API int nmg_gather_heads_to_rows(const void* gathered, void* out, int world, int64_t rows, int64_t row_bytes_per_rank,
+                             void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* NMG_H */

@@ -1,0 +1,345 @@
+/*
+ * nm_oracle.c -- CPU restatement of the nm engine's attention / KV-cache /
+ * gated delta-rule arithmetic.
+ *
+ * TEST INFRASTRUCTURE ONLY.  This file is the parity checker for the CUDA
+ * path under hero_b200/.  Only tests/, __graft_entry__.smoke() and the
+ * cpu_baseline leg of bench.py may load it.  Nothing in the product links it.
+ *
+ * Every function restates one piece of the reference (paths relative to the
+ * nm/ project root) and keeps its floating-point operation order, so that the
+ * result matches the reference's own fp32 code up to FMA contraction:
+ *
+ *   nmo_visible_rows        src/attention.hpp:170-176   CausalWindow::visible_rows
+ *   nmo_contains            src/attention.hpp:159-162   CausalWindow::contains
+ *   nmo_attend              src/qwen35.hpp:360-382, src/gemma4.hpp:211-235,
+ *                           tests/property_tests.cpp:33-56 (the reduction:
+ *                           dot -> scale -> Softmax -> scaled_add)
+ *   nmo_softmax_inplace     src/components.hpp:131-141
+ *   nmo_dot                 src/core.hpp:495-500 (sequential fp32 accumulate)
+ *   nmo_gated_delta_step    src/recurrent.hpp:146-177
+ *   nmo_delta_run           src/qwen35.hpp:449-454 (head loop, key head h % Hk)
+ *   nmo_l2_normalize        src/recurrent.hpp:40-48
+ *   nmo_softplus            src/recurrent.hpp:35
+ *   nmo_sigmoid             src/core.hpp:579
+ *   nmo_fp32_to_bf16 etc.   src/core.hpp:34-100
+ *
+ * Inputs are plain row-major fp32 arrays in the reference's own layouts:
+ * activations [rows][heads*dim] (heads contiguous inside a row), cached K/V
+ * [chronological row][Hkv*HeadDim], delta state [head][Dk][Dv].
+ */
+#include <math.h>
+#include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
+#include <pthread.h>
+
+#define NMO_OK 0
+#define NMO_INVALID_ARGUMENT 1
+#define NMO_OUT_OF_RANGE 2
+#define NMO_RUNTIME_ERROR 3
+
+/* ---- fp16 / bf16 conversions: src/core.hpp:34-100 ------------------------ */
+
+float nmo_fp16_to_fp32(uint16_t h) {
+    uint32_t sign = (uint32_t)(h & 0x8000u) << 16;
+    uint32_t e = (h >> 10) & 0x1Fu;
+    uint32_t m = h & 0x3FFu;
+    uint32_t bits;
+    if (e == 0) {
+        if (m == 0) {
+            bits = sign;
+        } else {
+            /* subnormal: normalise the mantissa, counting the shifts */
+            int shifts = -1;
+            do {
+                m <<= 1;
+                ++shifts;
+            } while ((m & 0x400u) == 0);
+            m &= 0x3FFu;
+            bits = sign | ((uint32_t)(112 - shifts) << 23) | (m << 13);
+        }
+    } else if (e == 0x1F) {
+        bits = sign | 0x7F800000u | (m << 13);
+    } else {
+        bits = sign | ((e + 112) << 23) | (m << 13);
+    }
+    float f;
+    memcpy(&f, &bits, 4);
+    return f;
+}
+
+uint16_t nmo_fp32_to_fp16(float f) {
+    uint32_t x;
+    memcpy(&x, &f, 4);
+    uint32_t sign = (x >> 16) & 0x8000u;
+    int32_t e = (int32_t)((x >> 23) & 0xFF) - 127 + 15;
+    uint32_t m = x & 0x7FFFFFu;
+    if (e <= 0) {
+        if (e < -10) return (uint16_t)sign;
+        m |= 0x800000u;
+        uint32_t shift = (uint32_t)(14 - e);
+        uint32_t r = m >> shift;
+        if ((m >> (shift - 1)) & 1u) ++r; /* the reference rounds half up here */
+        return (uint16_t)(sign | r);
+    }
+    if (e >= 0x1F) return (uint16_t)(sign | 0x7C00u);
+    uint16_t h = (uint16_t)(sign | ((uint32_t)e << 10) | (m >> 13));
+    if (m & 0x1000u) ++h;
+    return h;
+}
+
+float nmo_bf16_to_fp32(uint16_t b) {
+    uint32_t bits = (uint32_t)b << 16;
+    float f;
+    memcpy(&f, &bits, 4);
+    return f;
+}
+
+uint16_t nmo_fp32_to_bf16(float f) {
+    uint32_t bits;
+    memcpy(&bits, &f, 4);
+    if ((bits & 0x7FFFFFFFu) > 0x7F800000u) return (uint16_t)((bits >> 16) | 0x0040u);
+    bits += 0x7FFFu + ((bits >> 16) & 1u);
+    return (uint16_t)(bits >> 16);
+}
+
+void nmo_round_bf16(float* x, int64_t n) {
+    for (int64_t i = 0; i < n; ++i) x[i] = nmo_bf16_to_fp32(nmo_fp32_to_bf16(x[i]));
+}
+void nmo_round_fp16(float* x, int64_t n) {
+    for (int64_t i = 0; i < n; ++i) x[i] = nmo_fp16_to_fp32(nmo_fp32_to_fp16(x[i]));
+}
+void nmo_to_bf16(const float* x, uint16_t* y, int64_t n) {
+    for (int64_t i = 0; i < n; ++i) y[i] = nmo_fp32_to_bf16(x[i]);
+}
+void nmo_to_fp16(const float* x, uint16_t* y, int64_t n) {
+    for (int64_t i = 0; i < n; ++i) y[i] = nmo_fp32_to_fp16(x[i]);
+}
+
+/* ---- seeded input generator ------------------------------------------------
+ * SplitMix64 counter stream + Box-Muller.  Element i of stream (seed, stream)
+ * is a pure function of (seed, stream, i), so any slice can be regenerated
+ * independently (the GPU bench uses the same construction on the device). */
+
+static uint64_t splitmix64(uint64_t z) {
+    z += 0x9E3779B97F4A7C15ull;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+
+static double unit_open(uint64_t bits) { /* (0, 1], 53 bits */
+    return ((double)(bits >> 11) + 1.0) * (1.0 / 9007199254740992.0);
+}
+
+void nmo_normal(uint64_t seed, uint64_t stream, uint64_t first, int64_t n, float* out) {
+    const uint64_t key = splitmix64(seed ^ splitmix64(stream + 0x632BE59BD9B4E019ull));
+    for (int64_t j = 0; j < n; ++j) {
+        uint64_t i = first + (uint64_t)j;
+        uint64_t pair = i >> 1;
+        double u1 = unit_open(splitmix64(key + 2 * pair));
+        double u2 = unit_open(splitmix64(key + 2 * pair + 1));
+        double r = sqrt(-2.0 * log(u1));
+        double a = 6.283185307179586 * u2;
+        out[j] = (float)((i & 1) ? r * sin(a) : r * cos(a));
+    }
+}
+
+void nmo_uniform_int(uint64_t seed, uint64_t stream, int64_t n, int64_t lo, int64_t hi, int64_t* out) {
+    const uint64_t key = splitmix64(seed ^ splitmix64(stream + 0x632BE59BD9B4E019ull));
+    const uint64_t span = (uint64_t)(hi - lo + 1);
+    for (int64_t j = 0; j < n; ++j) out[j] = lo + (int64_t)(splitmix64(key + (uint64_t)j) % span);
+}
+
+/* ---- mask: src/attention.hpp:154-176 -------------------------------------- */
+
+int nmo_contains(int64_t width, int64_t key, int64_t query) {
+    if (key > query) return 0;
+    return width == 0 || query - key < width;
+}
+
+void nmo_visible_rows(int64_t width, int64_t query, int64_t oldest, int64_t rows, int64_t* first, int64_t* end) {
+    if (query < oldest) {
+        *first = 0;
+        *end = 0;
+        return;
+    }
+    int64_t distance = query - oldest;
+    int64_t e = rows < distance + 1 ? rows : distance + 1;
+    int64_t b = (width == 0 || distance < width) ? 0 : distance + 1 - width;
+    *first = b < e ? b : e;
+    *end = e;
+}
+
+/* ---- the reduction --------------------------------------------------------- */
+
+float nmo_dot(const float* a, const float* b, int64_t n) {
+    float s = 0.f;
+    for (int64_t i = 0; i < n; ++i) s += a[i] * b[i];
+    return s;
+}
+
+void nmo_softmax_inplace(float* v, int64_t n) {
+    float largest = v[0];
+    for (int64_t i = 1; i < n; ++i)
+        if (v[i] > largest) largest = v[i];
+    float total = 0.f;
+    for (int64_t i = 0; i < n; ++i) {
+        v[i] = expf(v[i] - largest);
+        total += v[i];
+    }
+    for (int64_t i = 0; i < n; ++i) v[i] /= total;
+}
+
+typedef struct {
+    const float* keys;   /* [rows][hkv*dh], chronological */
+    const float* values; /* [rows][hkv*dh] */
+    int64_t rows, oldest, window;
+    int hkv, dh, hq;
+    const float* q; /* [qrows][hq*dh] */
+    int64_t qrows, first_query;
+    float scale;
+    int use_scale; /* 0: Gemma form (no multiply), 1: Qwen form (scale * dot) */
+    float* out;    /* [qrows][hq*dh] */
+    int64_t next_task;
+    pthread_mutex_t lock;
+} attend_job;
+
+static void attend_task(attend_job* J, int64_t task, float* alpha) {
+    const int64_t row = task / J->hq;
+    const int head = (int)(task % J->hq);
+    const int group = head / (J->hq / J->hkv);
+    const int width = J->hkv * J->dh;
+    int64_t first, end;
+    nmo_visible_rows(J->window, J->first_query + row, J->oldest, J->rows, &first, &end);
+    const float* query = J->q + row * (int64_t)J->hq * J->dh + (int64_t)head * J->dh;
+    const int64_t count = end - first;
+    for (int64_t j = first; j < end; ++j) {
+        float d = nmo_dot(query, J->keys + j * width + (int64_t)group * J->dh, J->dh);
+        alpha[j - first] = J->use_scale ? J->scale * d : d;
+    }
+    nmo_softmax_inplace(alpha, count);
+    float* o = J->out + row * (int64_t)J->hq * J->dh + (int64_t)head * J->dh;
+    for (int i = 0; i < J->dh; ++i) o[i] = 0.f;
+    for (int64_t n = 0; n < count; ++n) {
+        const float* v = J->values + (first + n) * width + (int64_t)group * J->dh;
+        const float a = alpha[n];
+        for (int i = 0; i < J->dh; ++i) o[i] += a * v[i];
+    }
+}
+
+static void* attend_worker(void* arg) {
+    attend_job* J = (attend_job*)arg;
+    float* alpha = (float*)malloc(sizeof(float) * (size_t)(J->rows > 0 ? J->rows : 1));
+    for (;;) {
+        pthread_mutex_lock(&J->lock);
+        int64_t t = J->next_task;
+        J->next_task += 1;
+        pthread_mutex_unlock(&J->lock);
+        if (t >= J->qrows * J->hq) break;
+        attend_task(J, t, alpha);
+    }
+    free(alpha);
+    return NULL;
+}
+
+/* Attention of `qrows` query rows at positions first_query.. over a cache whose
+ * `rows` chronological rows start at position `oldest`, visible through a
+ * causal window of `window` (0 = full).  Returns NMO_RUNTIME_ERROR when some
+ * query sees no key (attention.hpp:224, :349) and NMO_INVALID_ARGUMENT for a
+ * head count that is not a whole GQA group. */
+int nmo_attend(const float* keys, const float* values, int64_t rows, int64_t oldest, int64_t window, int hkv, int dh,
+               const float* q, int64_t qrows, int hq, int64_t first_query, float scale, int use_scale, float* out,
+               int threads) {
+    if (hkv <= 0 || dh <= 0 || hq <= 0 || hq % hkv != 0) return NMO_INVALID_ARGUMENT;
+    for (int64_t r = 0; r < qrows; ++r) {
+        int64_t f, e;
+        nmo_visible_rows(window, first_query + r, oldest, rows, &f, &e);
+        if (f == e) return NMO_RUNTIME_ERROR;
+    }
+    attend_job J;
+    J.keys = keys;
+    J.values = values;
+    J.rows = rows;
+    J.oldest = oldest;
+    J.window = window;
+    J.hkv = hkv;
+    J.dh = dh;
+    J.hq = hq;
+    J.q = q;
+    J.qrows = qrows;
+    J.first_query = first_query;
+    J.scale = scale;
+    J.use_scale = use_scale;
+    J.out = out;
+    J.next_task = 0;
+    pthread_mutex_init(&J.lock, NULL);
+    if (threads < 1) threads = 1;
+    if (threads > 256) threads = 256;
+    pthread_t tid[256];
+    for (int t = 1; t < threads; ++t) pthread_create(&tid[t], NULL, attend_worker, &J);
+    attend_worker(&J);
+    for (int t = 1; t < threads; ++t) pthread_join(tid[t], NULL);
+    pthread_mutex_destroy(&J.lock);
+    return NMO_OK;
+}
+
+/* ---- the gated delta rule: src/recurrent.hpp:146-177 ----------------------- */
+
+void nmo_gated_delta_step(float* state, const float* q, const float* k, const float* v, float gate, float beta,
+                          float* out, int dk, int dv, float* scratch /* [2*dv] */) {
+    const float decay = expf(gate);
+    float* predicted = scratch;
+    float* delta = scratch + dv;
+    for (int j = 0; j < dv; ++j) predicted[j] = 0.f;
+    for (int i = 0; i < dk; ++i) {
+        float* row = state + (int64_t)i * dv;
+        const float ki = k[i];
+        for (int j = 0; j < dv; ++j) {
+            row[j] *= decay;
+            predicted[j] += row[j] * ki;
+        }
+    }
+    for (int j = 0; j < dv; ++j) delta[j] = (v[j] - predicted[j]) * beta;
+    for (int j = 0; j < dv; ++j) out[j] = 0.f;
+    for (int i = 0; i < dk; ++i) {
+        float* row = state + (int64_t)i * dv;
+        const float ki = k[i], qi = q[i];
+        for (int j = 0; j < dv; ++j) {
+            row[j] += ki * delta[j];
+            out[j] += row[j] * qi;
+        }
+    }
+}
+
+/* The per-token head loop of src/qwen35.hpp:436-456 after the conv/normalise
+ * prologue: q,k are [T][hk][dk] (already L2-normalised, q already scaled),
+ * v is [T][hv][dv], gate/beta are [T][hv], state is [hv][dk][dv] (in/out),
+ * out is [T][hv][dv].  Value head h reads key head h % hk (qwen35.hpp:172). */
+void nmo_delta_run(float* state, int64_t T, int hk, int hv, int dk, int dv, const float* q, const float* k,
+                   const float* v, const float* gate, const float* beta, float* out) {
+    float* scratch = (float*)malloc(sizeof(float) * 2 * (size_t)dv);
+    for (int64_t t = 0; t < T; ++t) {
+        for (int h = 0; h < hv; ++h) {
+            const int kh = h % hk;
+            nmo_gated_delta_step(state + (int64_t)h * dk * dv, q + (t * hk + kh) * (int64_t)dk,
+                                 k + (t * hk + kh) * (int64_t)dk, v + (t * hv + h) * (int64_t)dv, gate[t * hv + h],
+                                 beta[t * hv + h], out + (t * hv + h) * (int64_t)dv, dk, dv, scratch);
+        }
+    }
+    free(scratch);
+}
+
+/* ---- small pieces: src/recurrent.hpp:35-48, src/core.hpp:579 --------------- */
+
+float nmo_softplus(float x) { return x > 20.f ? x : log1pf(expf(x)); }
+float nmo_sigmoid(float x) { return 1.f / (1.f + expf(-x)); }
+
+void nmo_l2_normalize(const float* x, float* y, int n, float eps) {
+    float ss = 0.f;
+    for (int i = 0; i < n; ++i) ss += x[i] * x[i];
+    float norm = sqrtf(ss);
+    const float scale = 1.f / (norm < eps ? eps : norm); /* std::max(norm, eps) */
+    for (int i = 0; i < n; ++i) y[i] = x[i] * scale;
+}

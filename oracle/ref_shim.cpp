@@ -1,0 +1,293 @@
+// ref_shim.cpp -- a C entry layer over the reference engine's OWN headers.
+//
+// TEST INFRASTRUCTURE ONLY.  This file is compiled against the reference
+// sources where they lie (include path to the reference's nm/src, plus its
+// core.cpp for the par_for pool) by oracle/Makefile into oracle/_ref/.  It
+// is used to pin oracle/nm_oracle.c, to write tests/golden fixtures, and as
+// the timed CPU baseline (bench.py --impl reference).  It copies no reference
+// code: it instantiates the reference's FullAttentionCache, LocalAttentionCache,
+// CausalWindow, Softmax, dot, DeltaNetState, gated_delta_step, l2_normalize and
+// softplus directly.
+//
+// The softmax reduction itself exists in the reference only as a lambda inside
+// each model layer (src/qwen35.hpp:360-382, src/gemma4.hpp:211-235 ...), which
+// cannot be instantiated without a model config.  The reference's own tests
+// therefore mirror it (tests/property_tests.cpp:33-56 with a score scale,
+// tests/gemma4_tests.cpp:34-57 without).  `reduce` below is that same equation
+// over the reference types: visible_rows per query, then per (row, head) task
+// on par_for: scores = [scale *] dot(q, key(j, head / group)), Softmax, and
+// scaled_add of value(j, head / group).
+#include "attention.hpp"
+#include "recurrent.hpp"
+
+#include <cstdint>
+#include <cstdio>
+#include <cstdlib>
+#include <stdexcept>
+#include <vector>
+
+namespace {
+
+enum Status { OK = 0, INVALID_ARGUMENT = 1, OUT_OF_RANGE = 2, RUNTIME_ERROR = 3, LENGTH_ERROR = 4, LOGIC_ERROR = 5 };
+
+template <size_t N>
+Vec<N> vec_from(const float* p) {
+    Vec<N> v;
+    for (size_t i = 0; i < N; ++i) v[i] = p[i];
+    return v;
+}
+
+// The mirrored reduction over a reference cache.  q is [qrows][hq*Dh].
+template <size_t Hkv, size_t Dh, class Cache>
+void reduce(const Cache& cache, const float* q, size_t qrows, size_t hq, Position at, float scale, bool use_scale,
+            float* out) {
+    std::vector<VisibleRows> visible;
+    visible.reserve(qrows);
+    for (size_t row = 0; row < qrows; ++row) visible.push_back(cache.visible_rows(at + row));
+
+    par_for(qrows * hq, [&](size_t task) {
+        const size_t row = task / hq, head = task % hq;
+        const Vec<Dh> query = vec_from<Dh>(q + (row * hq + head) * Dh);
+        const KVHead group{head / (hq / Hkv)};
+        const VisibleRows rows = visible[row];
+
+        std::vector<Scalar> alpha;
+        alpha.reserve(rows.count());
+        for (size_t j = rows.first; j < rows.end; ++j) {
+            const Scalar d = dot(VecView<Dh>(query), cache.key(j, group));
+            alpha.push_back(use_scale ? scale * d : d);
+        }
+        alpha = Softmax{}(std::move(alpha));
+
+        Vec<Dh> head_output;
+        for (size_t n = 0; n < alpha.size(); ++n) head_output.scaled_add(cache.value(rows.first + n, group), alpha[n]);
+        for (size_t i = 0; i < Dh; ++i) out[(row * hq + head) * Dh + i] = head_output[i];
+    });
+}
+
+template <class F>
+int guarded(F&& f) {
+    try {
+        f();
+        return OK;
+    } catch (const std::invalid_argument&) {
+        return INVALID_ARGUMENT;
+    } catch (const std::out_of_range&) {
+        return OUT_OF_RANGE;
+    } catch (const std::length_error&) {
+        return LENGTH_ERROR;
+    } catch (const std::logic_error&) {
+        return LOGIC_ERROR;
+    } catch (const std::runtime_error&) {
+        return RUNTIME_ERROR;
+    }
+}
+
+// Append `rows` K/V rows at positions first.. and reduce `qrows` queries at
+// positions first_query.. over a FullAttentionCache (qwen35.hpp:386-387).
+template <size_t Hkv, size_t Dh>
+int attend_full(const float* k, const float* v, size_t rows, size_t first, const float* q, size_t qrows, size_t hq,
+                size_t first_query, float scale, bool use_scale, float* out) {
+    constexpr size_t W = Hkv * Dh;
+    return guarded([&] {
+        if (hq % Hkv != 0) throw std::invalid_argument("hq is not a multiple of Hkv");
+        FullAttentionCache<Hkv, Dh> cache;
+        for (size_t r = 0; r < rows; ++r) cache.append(Position{first + r}, vec_from<W>(k + r * W), vec_from<W>(v + r * W));
+        reduce<Hkv, Dh>(cache, q, qrows, hq, Position{first_query}, scale, use_scale, out);
+    });
+}
+
+// The Gemma local-layer path (gemma4.hpp:617-630): the whole batch when the
+// ring has room, otherwise append one row and reduce one query at a time.
+// Rows [0, rows - qrows) are history appended before the queried batch.
+template <size_t Hkv, size_t Dh>
+int attend_local(size_t window, const float* k, const float* v, size_t rows, size_t first, const float* q,
+                 size_t qrows, size_t hq, float scale, bool use_scale, float* out) {
+    constexpr size_t W = Hkv * Dh;
+    return guarded([&] {
+        if (qrows > rows) throw std::invalid_argument("more queries than rows");
+        if (hq % Hkv != 0) throw std::invalid_argument("hq is not a multiple of Hkv");
+        LocalAttentionCache<Hkv, Dh> cache(window);
+        const size_t history = rows - qrows;
+        for (size_t r = 0; r < history; ++r) cache.append(Position{first + r}, vec_from<W>(k + r * W), vec_from<W>(v + r * W));
+        const Position at{first + history};
+        if (cache.can_append_without_eviction(qrows)) {
+            for (size_t r = history; r < rows; ++r) cache.append(Position{first + r}, vec_from<W>(k + r * W), vec_from<W>(v + r * W));
+            reduce<Hkv, Dh>(cache, q, qrows, hq, at, scale, use_scale, out);
+        } else {
+            for (size_t t = 0; t < qrows; ++t) {
+                const size_t r = history + t;
+                cache.append(Position{first + r}, vec_from<W>(k + r * W), vec_from<W>(v + r * W));
+                reduce<Hkv, Dh>(cache, q + t * hq * Dh, 1, hq, at + t, scale, use_scale, out + t * hq * Dh);
+            }
+        }
+    });
+}
+
+// A scripted LocalAttentionCache<1,1>: ops are (code, arg) pairs; code 0 =
+// append one row at position arg, 1 = begin_batch_retention(arg), 2 =
+// end_batch_retention().  Afterwards size, window and every chronological
+// row's position are reported (gemma4_tests.cpp:153-172 is one such script).
+int local_script(size_t window, const int64_t* ops, size_t nops, int64_t* size_out, int64_t* positions_out,
+                 size_t max_positions, int64_t* first_failed_op) {
+    *first_failed_op = -1;
+    std::unique_ptr<LocalAttentionCache<1, 1>> cache;
+    int status = guarded([&] { cache = std::make_unique<LocalAttentionCache<1, 1>>(window); });
+    if (status != OK) return status;
+    for (size_t i = 0; i < nops; ++i) {
+        const int64_t code = ops[2 * i], arg = ops[2 * i + 1];
+        status = guarded([&] {
+            if (code == 0) {
+                Vec<1> row;
+                row[0] = float(arg);
+                cache->append(Position{size_t(arg)}, row, row);
+            } else if (code == 1) {
+                cache->begin_batch_retention(size_t(arg));
+            } else if (code == 2) {
+                cache->end_batch_retention();
+            } else {
+                throw std::invalid_argument("unknown op");
+            }
+        });
+        if (status != OK) {
+            *first_failed_op = int64_t(i);
+            return status;
+        }
+    }
+    *size_out = int64_t(cache->size());
+    for (size_t r = 0; r < cache->size() && r < max_positions; ++r) {
+        // position() is a Position; its only numeric face is Position - Position.
+        positions_out[r] = int64_t(cache->position(r) - Position{0});
+    }
+    return OK;
+}
+
+template <size_t Hv, size_t Dk, size_t Dv>
+int delta_run(float* state_io, size_t T, size_t hk, const float* q, const float* k, const float* v, const float* g,
+              const float* beta, float* out) {
+    return guarded([&] {
+        DeltaNetState<Hv, Dk, Dv> state;
+        for (size_t h = 0; h < Hv; ++h)
+            for (size_t i = 0; i < Dk * Dv; ++i) state.head(h)[i] = state_io[h * Dk * Dv + i];
+        for (size_t t = 0; t < T; ++t) {
+            for (size_t h = 0; h < Hv; ++h) {
+                const size_t kh = h % hk;  // qwen35.hpp:172 (tiled key heads)
+                const Vec<Dk> qv = vec_from<Dk>(q + (t * hk + kh) * Dk);
+                const Vec<Dk> kv = vec_from<Dk>(k + (t * hk + kh) * Dk);
+                const Vec<Dv> vv = vec_from<Dv>(v + (t * Hv + h) * Dv);
+                const Vec<Dv> o = gated_delta_step<Dk, Dv>(state.head(h), VecView<Dk>(qv), VecView<Dk>(kv), VecView<Dv>(vv),
+                                                           g[t * Hv + h], beta[t * Hv + h]);
+                for (size_t j = 0; j < Dv; ++j) out[(t * Hv + h) * Dv + j] = o[j];
+            }
+        }
+        for (size_t h = 0; h < Hv; ++h)
+            for (size_t i = 0; i < Dk * Dv; ++i) state_io[h * Dk * Dv + i] = state.head(h)[i];
+    });
+}
+
+}  // namespace
+
+#define NMREF_ATTN_SHAPES(X) \
+    X(1, 1)                  \
+    X(1, 2)                  \
+    X(1, 4)                  \
+    X(2, 4)                  \
+    X(1, 16)                 \
+    X(2, 16)                 \
+    X(2, 32)                 \
+    X(4, 32)                 \
+    X(1, 64)                 \
+    X(2, 64)                 \
+    X(4, 64)                 \
+    X(1, 128)                \
+    X(2, 128)                \
+    X(4, 128)                \
+    X(8, 128)                \
+    X(1, 256)                \
+    X(2, 256)                \
+    X(4, 256)
+
+#define NMREF_DELTA_SHAPES(X) \
+    X(1, 2, 2)                \
+    X(2, 2, 2)                \
+    X(4, 16, 16)              \
+    X(4, 32, 32)              \
+    X(8, 64, 64)              \
+    X(2, 128, 128)            \
+    X(4, 128, 128)            \
+    X(8, 128, 128)            \
+    X(32, 128, 128)
+
+extern "C" {
+
+// Status codes: 0 ok, 1 invalid_argument, 2 out_of_range, 3 runtime_error,
+// 4 length_error, 5 logic_error, 100 shape not instantiated here.
+int nmref_attend_full(int hkv, int dh, const float* k, const float* v, int64_t rows, int64_t first, const float* q,
+                      int64_t qrows, int hq, int64_t first_query, float scale, int use_scale, float* out) {
+#define X(H, D) \
+    if (hkv == H && dh == D) return attend_full<H, D>(k, v, rows, first, q, qrows, hq, first_query, scale, use_scale != 0, out);
+    NMREF_ATTN_SHAPES(X)
+#undef X
+    return 100;
+}
+
+int nmref_attend_local(int hkv, int dh, int64_t window, const float* k, const float* v, int64_t rows, int64_t first,
+                       const float* q, int64_t qrows, int hq, float scale, int use_scale, float* out) {
+#define X(H, D)                       \
+    if (hkv == H && dh == D)          \
+        return attend_local<H, D>(window, k, v, rows, first, q, qrows, hq, scale, use_scale != 0, out);
+    NMREF_ATTN_SHAPES(X)
+#undef X
+    return 100;
+}
+
+int nmref_local_script(int64_t window, const int64_t* ops, int64_t nops, int64_t* size_out, int64_t* positions_out,
+                       int64_t max_positions, int64_t* first_failed_op) {
+    return local_script(size_t(window), ops, size_t(nops), size_out, positions_out, size_t(max_positions), first_failed_op);
+}
+
+int nmref_visible_rows(int64_t width, int64_t query, int64_t oldest, int64_t rows, int64_t* first, int64_t* end) {
+    const VisibleRows r = CausalWindow{size_t(width)}.visible_rows(Position{size_t(query)}, Position{size_t(oldest)}, size_t(rows));
+    *first = int64_t(r.first);
+    *end = int64_t(r.end);
+    return 0;
+}
+
+int nmref_contains(int64_t width, int64_t key, int64_t query) {
+    return CausalWindow{size_t(width)}.contains(Position{size_t(key)}, Position{size_t(query)}) ? 1 : 0;
+}
+
+int nmref_delta_run(int hv, int dk, int dv, float* state, int64_t T, int hk, const float* q, const float* k, const float* v,
+                    const float* g, const float* beta, float* out) {
+#define X(H, DK, DV) \
+    if (hv == H && dk == DK && dv == DV) return delta_run<H, DK, DV>(state, T, hk, q, k, v, g, beta, out);
+    NMREF_DELTA_SHAPES(X)
+#undef X
+    return 100;
+}
+
+float nmref_softplus(float x) { return softplus(x); }
+float nmref_sigmoid(float x) { return sigmoid(x); }
+
+int nmref_l2_normalize(int n, const float* x, float* y) {
+    if (n == 2) {
+        const Vec<2> r = l2_normalize<2>(VecView<2>(vec_from<2>(x)));
+        for (int i = 0; i < 2; ++i) y[i] = r[i];
+        return 0;
+    }
+    if (n == 128) {
+        const Vec<128> r = l2_normalize<128>(VecView<128>(vec_from<128>(x)));
+        for (int i = 0; i < 128; ++i) y[i] = r[i];
+        return 0;
+    }
+    return 100;
+}
+
+uint16_t nmref_fp32_to_bf16(float f) { return fp32_to_bf16(f); }
+uint16_t nmref_fp32_to_fp16(float f) { return fp32_to_fp16(f); }
+float nmref_bf16_to_fp32(uint16_t b) { return bf16_to_fp32(b); }
+float nmref_fp16_to_fp32(uint16_t h) { return fp16_to_fp32(h); }
+
+int nmref_threads(void) { return int(nm_num_threads()); }
+
+}  // extern "C"

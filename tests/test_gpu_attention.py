@@ -1,0 +1,297 @@
+"""Device KV cache + attention parity against the oracle (and the reference's fixtures).
+
+Tolerance (north star): max abs <= 2e-3 and rel L2 <= 1e-3 versus the fp32
+reference path on identical pre-rounded inputs; positions, visible rows and
+window membership exact.
+"""
+import glob
+import os
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from helpers import assert_close, load_attn_fixture
+from hero_b200 import nm
+from hero_b200._lib import InvalidArgument, LengthError, LogicError, NoVisibleKeys, OutOfRange
+
+pytestmark = pytest.mark.gpu
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+def T(a, dev, dtype=torch.float32):
+    return torch.from_numpy(np.ascontiguousarray(a)).to(dev).to(dtype)
+
+
+def TD(a, dev, code):
+    return T(a, dev, {"f32": torch.float32, "bf16": torch.bfloat16, "f16": torch.float16}[code])
+
+
+def rnd(code, seed, stream, shape):
+    x = oracle.normal(seed, stream, int(np.prod(shape))).reshape(shape)
+    if code == "bf16":
+        return oracle.round_bf16(x).reshape(shape)
+    if code == "f16":
+        return oracle.round_fp16(x).reshape(shape)
+    return x
+
+
+# ---- the reference's known-answer tests through the device path ---------------
+
+def test_causal_attention_equation(dev):
+    # property_tests.cpp:187-215
+    cache = nm.FullAttentionCache(1, 2, capacity=8)
+    keys = T([[1, 0], [0, 1]], dev)
+    values = T([[10, 0], [30, 0]], dev)
+    cache.append(0, keys, values)
+    q = T([[1, 0], [0, 1]], dev)
+    scale = float(np.float32(1 / np.sqrt(np.float32(2))))
+    out = nm.attend(cache, q, 0, scale).cpu().numpy()
+    w1 = np.exp(np.float32(scale)) / (1 + np.exp(np.float32(scale)))
+    assert out[0, 0] == 10.0
+    assert abs(out[1, 0] - ((1 - w1) * 10 + w1 * 30)) < 1e-5
+    # the local cache owns its width-1 visibility (property_tests.cpp:217-222)
+    local = nm.LocalAttentionCache(1, 2, 1)
+    local.append(0, keys[0], values[0])
+    local.append(1, keys[1], values[1])
+    assert nm.attend(local, q[1:], 1, scale).cpu().numpy()[0, 0] == 30.0
+
+
+def test_gemma_gqa_window_and_ring(dev):
+    # gemma4_tests.cpp:122-172
+    k0, v0, k1, v1 = T([1, 0], dev), T([10, 20], dev), T([0, 1], dev), T([30, 40], dev)
+    full = nm.FullAttentionCache(1, 2, capacity=4)
+    full.append(0, k0, v0)
+    full.append(1, k1, v1)
+    q = T([[1, 0, 1, 0]], dev)
+    r = nm.attend(full, q, 1).cpu().numpy()
+    p0 = np.exp(np.float32(1)) / (np.exp(np.float32(1)) + 1)
+    assert abs(r[0, 0] - (p0 * 10 + (1 - p0) * 30)) < 1e-5 and r[0, 0] == r[0, 2]
+    local = nm.LocalAttentionCache(1, 2, 1)
+    local.append(0, k0, v0)
+    local.append(1, k1, v1)
+    r = nm.attend(local, q, 1).cpu().numpy()
+    assert r[0, 0] == 30 and r[0, 1] == 40
+    ring = nm.LocalAttentionCache(1, 2, 2)
+    k2, v2 = T([2, 2], dev), T([50, 60], dev)
+    ring.append(0, k0, v0)
+    ring.append(1, k1, v1)
+    ring.append(2, k2, v2)
+    assert ring.size() == 2 and ring.position(0) == 1 and ring.position(1) == 2
+    assert torch.equal(ring.key(0, 0), torch.tensor([0.0, 1.0])) and torch.equal(ring.value(1, 0), torch.tensor([50.0, 60.0]))
+    ring.begin_batch_retention(2)
+    ring.append(3, k0, v0)
+    ring.append(4, k1, v1)
+    assert ring.size() == 4 and ring.position(0) == 1 and ring.position(3) == 4
+    # during retention the rows are all readable, in chronological order
+    assert torch.equal(ring.value(0, 0), torch.tensor([30.0, 40.0])) and torch.equal(ring.value(3, 0), torch.tensor([30.0, 40.0]))
+    ring.end_batch_retention()
+    assert ring.size() == 2 and ring.position(0) == 3 and ring.position(1) == 4
+
+
+def test_errors_match_the_reference(dev):
+    cache = nm.LocalAttentionCache(1, 2, 2)
+    cache.append(0, T([1, 0], dev), T([5, 0], dev))
+    with pytest.raises(NoVisibleKeys):  # property_tests.cpp:301-316
+        cache.visible_rows(9)
+    with pytest.raises(NoVisibleKeys):
+        nm.attend(cache, T([[1, 0]], dev), 9)
+    with pytest.raises(InvalidArgument):  # attention.hpp:322
+        cache.append(5, T([1, 0], dev), T([5, 0], dev))
+    with pytest.raises(OutOfRange):  # attention.hpp:380-385
+        cache.key(3, 0)
+    with pytest.raises(OutOfRange):
+        cache.key(0, 1)
+    with pytest.raises(LogicError):  # attention.hpp:295
+        cache.begin_batch_retention(3)
+        cache.end_batch_retention()
+    empty = nm.FullAttentionCache(1, 2, capacity=2)
+    with pytest.raises(NoVisibleKeys):
+        empty.visible_rows(0)
+    full = nm.FullAttentionCache(1, 2, capacity=2)
+    full.append(0, T([[1, 0], [0, 1]], dev), T([[1, 0], [0, 1]], dev))
+    with pytest.raises(LengthError):  # device capacity
+        full.append(2, T([1, 0], dev), T([1, 0], dev))
+    with pytest.raises(InvalidArgument):  # Hq not a multiple of Hkv
+        nm.attend(nm.FullAttentionCache(2, 2, capacity=2), T([[1, 0]], dev), 0)
+
+
+def test_visible_rows_exhaustive_box(dev):
+    # property_tests.cpp:318-338 through the device cache's bookkeeping
+    for width in range(1, 5):
+        for anchor in range(4):
+            for rows in range(1, 6):
+                c = nm.LocalAttentionCache(1, 2, width, capacity=8)
+                m = oracle.CacheModel(width, local=True)
+                for r in range(rows):
+                    c.append(anchor + r, T([0, 0], dev), T([0, 0], dev))
+                    m.append(anchor + r)
+                assert c.size() == m.size
+                for query in range(10):
+                    try:
+                        want = m.visible_rows(query)
+                    except oracle.NoVisibleKeys:
+                        with pytest.raises(NoVisibleKeys):
+                            c.visible_rows(query)
+                        continue
+                    got = c.visible_rows(query)
+                    assert (got.first, got.end) == want
+
+
+# ---- golden fixtures written by the reference ---------------------------------
+
+@pytest.mark.parametrize("path", sorted(glob.glob(os.path.join(HERE, "golden", "attn_*.npz"))))
+def test_golden_fixtures(dev, path):
+    z = load_attn_fixture(path)
+    hq, hkv, dh = int(z["hq"]), int(z["hkv"]), int(z["dh"])
+    window, first_query, oldest = int(z["window"]), int(z["first_query"]), int(z["oldest"])
+    code = str(z["dtype"]) if dh >= 64 else "f32"
+    rows, qrows = z["k"].shape[0], z["q"].shape[0]
+    scale = float(z["scale"]) if bool(z["use_scale"]) else None
+    if window:
+        cache = nm.LocalAttentionCache(hkv, dh, window, capacity=((rows + window + 127) // 128) * 128, dtype=code)
+        hist = rows - qrows
+        if hist:
+            cache.append(oldest, TD(z["k"][:hist], dev, code), TD(z["v"][:hist], dev, code))
+        out = nm.append_attend(cache, oldest + hist, TD(z["k"][hist:], dev, code), TD(z["v"][hist:], dev, code),
+                               TD(z["q"], dev, code), scale, out_dtype=torch.float32)
+    else:
+        cache = nm.FullAttentionCache(hkv, dh, capacity=((rows + 127) // 128) * 128, dtype=code)
+        cache.append(oldest, TD(z["k"], dev, code), TD(z["v"], dev, code))
+        out = nm.attend(cache, TD(z["q"], dev, code), first_query, scale, out_dtype=torch.float32)
+    assert_close(out.cpu().numpy(), z["out"], what=os.path.basename(path))
+
+
+# ---- seeded random parity at BASELINE shapes -----------------------------------
+
+def test_config1_decode_fp32(dev):
+    hq, hkv, dh, rows = 16, 8, 128, 1024
+    k, v = rnd("f32", 0, 1, (rows, hkv * dh)), rnd("f32", 0, 2, (rows, hkv * dh))
+    q = rnd("f32", 0, 3, (1, hq * dh))
+    cache = nm.FullAttentionCache(hkv, dh, capacity=rows)
+    cache.append(0, T(k, dev), T(v, dev))
+    s = float(np.float32(1 / np.sqrt(np.float32(dh))))
+    out = nm.attend(cache, T(q, dev), rows - 1, s).cpu().numpy()
+    want = oracle.attend(k, v, 0, 0, hkv, dh, q, hq, rows - 1, scale=np.float32(s))
+    assert_close(out, want, what="config 1")
+
+
+@pytest.mark.parametrize("S", [128, 200, 640])
+def test_config2_prefill_bf16(dev, S):
+    hq, hkv, dh = 32, 8, 128
+    k, v = rnd("bf16", 0, 1, (S, hkv * dh)), rnd("bf16", 0, 2, (S, hkv * dh))
+    q = rnd("bf16", 0, 3, (S, hq * dh))
+    cache = nm.FullAttentionCache(hkv, dh, capacity=((S + 127) // 128) * 128, dtype="bf16")
+    s = float(np.float32(1 / np.sqrt(np.float32(dh))))
+    out = nm.append_attend(cache, 0, TD(k, dev, "bf16"), TD(v, dev, "bf16"), TD(q, dev, "bf16"), s,
+                           out_dtype=torch.float32).cpu().numpy()
+    want = oracle.attend(k, v, 0, 0, hkv, dh, q, hq, 0, scale=np.float32(s))
+    assert_close(out, want, what=f"config 2 S={S}")
+
+
+def test_config2_full_size_rows_subset(dev):
+    # S = 4096 through the kernel; the oracle checks a spread of rows (first,
+    # last, tile edges, random) so it finishes in seconds.
+    S, hq, hkv, dh = 4096, 32, 8, 128
+    k, v = rnd("bf16", 0, 1, (S, hkv * dh)), rnd("bf16", 0, 2, (S, hkv * dh))
+    q = rnd("bf16", 0, 3, (S, hq * dh))
+    cache = nm.FullAttentionCache(hkv, dh, capacity=S, dtype="bf16")
+    s = float(np.float32(1 / np.sqrt(np.float32(dh))))
+    out = nm.append_attend(cache, 0, TD(k, dev, "bf16"), TD(v, dev, "bf16"), TD(q, dev, "bf16"), s,
+                           out_dtype=torch.float32).cpu().numpy()
+    rows = sorted({0, 1, 127, 128, 129, 1023, 2048, 4095} | set(np.random.default_rng(0).integers(0, S, 24).tolist()))
+    for r in rows:
+        want = oracle.attend(k, v, 0, 0, hkv, dh, q[r:r + 1], hq, r, scale=np.float32(s))
+        assert_close(out[r:r + 1], want, what=f"config 2 row {r}")
+    # bf16 output (the bench's dtype) stays within bf16 rounding of the fp32 result
+    out16 = nm.attend(cache, TD(q, dev, "bf16"), 0, s).float().cpu().numpy()
+    assert np.abs(out16 - out).max() <= 2.0 ** -8 * max(1.0, np.abs(out).max())
+
+
+@pytest.mark.parametrize("S,window", [(2048, 1024), (1500, 256), (700, 1024)])
+def test_config4_gemma_prefill_window(dev, S, window):
+    # Gemma local layers: scale 1.0, RMS-normed q/k, window 1024, batch larger
+    # than the window -> the reference's token-by-token path.
+    hq, hkv, dh = 8, 4, 256
+
+    def normed(seed, stream, shape):
+        x = oracle.normal(seed, stream, int(np.prod(shape))).reshape(-1, dh).astype(np.float64)
+        x = x / np.sqrt((x * x).mean(axis=1, keepdims=True) + 1e-6)
+        return oracle.round_bf16(x.astype(np.float32)).reshape(shape)
+
+    k, q = normed(4, 1, (S, hkv * dh)), normed(4, 3, (S, hq * dh))
+    v = rnd("bf16", 4, 2, (S, hkv * dh))
+    cache = nm.LocalAttentionCache(hkv, dh, window, capacity=((S + window + 127) // 128) * 128, dtype="bf16")
+    out = nm.append_attend(cache, 0, TD(k, dev, "bf16"), TD(v, dev, "bf16"), TD(q, dev, "bf16"), None,
+                           out_dtype=torch.float32).cpu().numpy()
+    rows = sorted({0, 1, window - 1, window, window + 1, S - 1} & set(range(S)) |
+                  set(np.random.default_rng(1).integers(0, S, 12).tolist()))
+    for r in rows:
+        want = oracle.attend(k[:r + 1], v[:r + 1], 0, window, hkv, dh, q[r:r + 1], hq, r, use_scale=False)
+        assert_close(out[r:r + 1], want, what=f"config 4 row {r}")
+    # the ring now holds the reference's logical window
+    assert cache.size() == min(S, window) and cache.position(0) == S - min(S, window)
+    # and decode continues from it: the global/local decode step of config 4
+    qd = normed(4, 5, (1, hq * dh))
+    kd, vd = normed(4, 6, (1, hkv * dh)), rnd("bf16", 4, 7, (1, hkv * dh))
+    outd = nm.append_attend(cache, S, TD(kd, dev, "bf16"), TD(vd, dev, "bf16"), TD(qd, dev, "bf16"), None,
+                            out_dtype=torch.float32).cpu().numpy()
+    kk, vv = np.concatenate([k, kd]), np.concatenate([v, vd])
+    want = oracle.attend(kk, vv, 0, window, hkv, dh, qd, hq, S, use_scale=False)
+    assert_close(outd, want, what="config 4 decode")
+
+
+def test_config5_ragged_batch_f16_group8(dev):
+    hq, hkv, dh, B = 64, 8, 128, 6
+    lens = [17, 130, 1000, 4096, 5000, 257]
+    caches, ks, vs = [], [], []
+    for b, L in enumerate(lens):
+        k, v = rnd("f16", 5, 10 + 2 * b, (L, hkv * dh)), rnd("f16", 5, 11 + 2 * b, (L, hkv * dh))
+        c = nm.FullAttentionCache(hkv, dh, capacity=L, dtype="f16")
+        c.append(0, TD(k, dev, "f16"), TD(v, dev, "f16"))
+        caches.append(c)
+        ks.append(k)
+        vs.append(v)
+    q = rnd("f16", 5, 1, (B, hq * dh))
+    s = float(np.float32(1 / np.sqrt(np.float32(dh))))
+    out = nm.attend_batch(caches, TD(q, dev, "f16"), s, out_dtype=torch.float32).cpu().numpy()
+    for b, L in enumerate(lens):
+        want = oracle.attend(ks[b], vs[b], 0, 0, hkv, dh, q[b:b + 1], hq, L - 1, scale=np.float32(s))
+        assert_close(out[b:b + 1], want, what=f"config 5 seq {b} len {L}")
+
+
+def test_ring_wraps_across_many_batches(dev):
+    # A local cache whose physical ring wraps many times, attended after every
+    # batch (decode-style and short-batch-style) against the oracle's window.
+    hq, hkv, dh, W = 4, 2, 64, 96
+    cache = nm.LocalAttentionCache(hkv, dh, W, capacity=128, dtype="f32")
+    total = 700
+    k, v = rnd("f32", 6, 1, (total, hkv * dh)), rnd("f32", 6, 2, (total, hkv * dh))
+    q = rnd("f32", 6, 3, (total, hq * dh))
+    pos, sizes = 0, [1, 5, 33, 1, 64, 7, 1, 100, 1, 200, 31, 1, 2]
+    for n in sizes:
+        out = nm.append_attend(cache, pos, T(k[pos:pos + n], dev), T(v[pos:pos + n], dev), T(q[pos:pos + n], dev),
+                               0.125).cpu().numpy()
+        for r in range(n):
+            p = pos + r
+            lo = max(0, p - W + 1)
+            want = oracle.attend(k[lo:p + 1], v[lo:p + 1], lo, W, hkv, dh, q[p:p + 1], hq, p, scale=np.float32(0.125))
+            assert_close(out[r:r + 1], want, what=f"ring pos {p}")
+        pos += n
+    assert cache.size() == W and cache.position(0) == pos - W
+
+
+def test_dense_sdpa(dev):
+    # scaled_dot_product_attention<Heads,D,D> (attention.hpp:124-139): no mask.
+    heads, dh, tq, tk = 4, 64, 37, 300
+    q, k, v = rnd("f32", 8, 1, (tq, heads * dh)), rnd("f32", 8, 2, (tk, heads * dh)), rnd("f32", 8, 3, (tk, heads * dh))
+    out = nm.scaled_dot_product_attention(T(q, dev), T(k, dev), T(v, dev), heads, 0.125).cpu().numpy()
+    want = oracle.attend(k, v, 0, 0, heads, dh, q, heads, tk - 1, scale=np.float32(0.125))
+    assert_close(out, want, what="sdpa")
+    # bf16 through the tensor-core kernel
+    qb, kb, vb = (rnd("bf16", 8, i, s) for i, s in ((4, (256, heads * 128)), (5, (256, heads * 128)), (6, (256, heads * 128))))
+    out = nm.scaled_dot_product_attention(TD(qb, dev, "bf16"), TD(kb, dev, "bf16"), TD(vb, dev, "bf16"), heads, 0.1,
+                                          out_dtype=torch.float32).cpu().numpy()
+    want = oracle.attend(kb, vb, 0, 0, heads, 128, qb, heads, 255, scale=np.float32(0.1))
+    assert_close(out, want, what="sdpa bf16")
