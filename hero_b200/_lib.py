@@ -98,6 +98,7 @@ SIGNATURES = {
     "nmg_kv_end_batch_retention": [_vp],
     "nmg_kv_read_row": [_vp, _i64, _i32, ctypes.POINTER(_f32), ctypes.POINTER(_f32), _vp],
     "nmg_kv_storage": [_vp, ctypes.POINTER(_vp), ctypes.POINTER(_vp), _i64p],
+    "nmg_kv_reset": [_vp],
     "nmg_attend": [_vp, _i32, _vp, _i32, _i64, _i64, _f32, _i32, _vp, _i32, _vp],
     "nmg_append_attend": [_vp, _i64, _vp, _vp, _i32, _i32, _vp, _i32, _i64, _f32, _i32, _vp, _i32, _vp],
     "nmg_attend_batch": [ctypes.POINTER(_vp), _i32, _i64p, _i32, _vp, _i32, _f32, _i32, _vp, _i32, _vp],

@@ -146,6 +146,7 @@ extern "C" int nmg_sdpa(int heads, int head_dim, const void* q, const void* k, c
     view.hkv = heads;
     view.dh = head_dim;
     view.dtype = dtype;
+    view.vdtype = nmg::v_dtype_for(dtype);
     view.device = device;
     view.window = 0;
     view.slots = slots;

@@ -126,6 +126,8 @@ template <int KVDT, int DH, int G, int WARPS>
 __global__ void __launch_bounds__(WARPS * 32) attn_split_kernel(const __grid_constant__ SplitArgs a) {
     using C = SplitCfg<KVDT, DH, G, WARPS>;
     using KT = typename C::KT;
+    // V buffer element type (a bf16 cache keeps V as fp16; same width).
+    constexpr int VDT = KVDT == NMG_BF16 ? NMG_F16 : KVDT;
     extern __shared__ __align__(128) unsigned char smem[];
     float* qs = (float*)(smem + C::Q_OFF);
     float* ps = (float*)(smem + C::P_OFF);
@@ -265,7 +267,7 @@ __global__ void __launch_bounds__(WARPS * 32) attn_split_kernel(const __grid_con
         for (int j = 0; j < nk; ++j) {
             const KT* vrow = vs + (wid * 32 + j) * DH;
             float vv[C::PER];
-            load_row_chunk<KVDT, DH, C::PER>(vrow, lane, vv);
+            load_row_chunk<VDT, DH, C::PER>(vrow, lane, vv);
 #pragma unroll
             for (int g = 0; g < G; ++g) {
                 const float p = pw[g * 32 + j];

@@ -12,8 +12,10 @@
 //   warps 2..5  softmax: thread i owns query row i, reads its S row from TMEM,
 //               applies the causal/window mask, an online softmax in base 2
 //               (rescaling O in TMEM only when the running max grows by more
-//               than 2^8), writes P as bf16/fp16 in the UMMA K-major swizzled
-//               layout, and at the end normalises O and stores the row.
+//               than 2^8), writes P as fp16 in the UMMA K-major swizzled
+//               layout (V is fp16 in every 16-bit cache, so P.V is an fp16
+//               MMA with 11-bit probabilities), and at the end normalises O
+//               and stores the row.
 //
 // The equation is the reference reduction (nm/src/qwen35.hpp:360-382,
 // nm/src/gemma4.hpp:593-615, :687-709): softmax over visible rows of
@@ -174,7 +176,8 @@ __global__ void __launch_bounds__(192, 1) attn_prefill_kernel(const __grid_const
         if (lane == 0) {
             // ------------------------------------------------ MMA issuer
             constexpr uint32_t idesc_s = tc::idesc_f16(128, BN, BF16 ? 1 : 0, 0, 0);
-            constexpr uint32_t idesc_o = tc::idesc_f16(128, DH, BF16 ? 1 : 0, 0, 1);
+            // P.V always runs fp16 x fp16: V of a 16-bit cache is stored fp16.
+            constexpr uint32_t idesc_o = tc::idesc_f16(128, DH, 0, 0, 1);
             const uint32_t sbase = dev::smem_u32(smem);
             bool ok = dev::mbar_wait(q_full, 0, a.err);
             auto issue_pv = [&](int i) -> bool {
@@ -293,10 +296,10 @@ __global__ void __launch_bounds__(192, 1) attn_prefill_kernel(const __grid_const
             for (int c8 = 0; c8 < BN / 8; ++c8) {
                 const int kb = c8 >> 3, cc = c8 & 7;
                 uint4 v;
-                v.x = pack2(x[c8 * 8 + 0], x[c8 * 8 + 1], BF16);
-                v.y = pack2(x[c8 * 8 + 2], x[c8 * 8 + 3], BF16);
-                v.z = pack2(x[c8 * 8 + 4], x[c8 * 8 + 5], BF16);
-                v.w = pack2(x[c8 * 8 + 6], x[c8 * 8 + 7], BF16);
+                v.x = pack2(x[c8 * 8 + 0], x[c8 * 8 + 1], false);
+                v.y = pack2(x[c8 * 8 + 2], x[c8 * 8 + 3], false);
+                v.z = pack2(x[c8 * 8 + 4], x[c8 * 8 + 5], false);
+                v.w = pack2(x[c8 * 8 + 6], x[c8 * 8 + 7], false);
                 *(uint4*)(pbuf + kb * BM * 128 + row * 128 + ((cc ^ (row & 7)) << 4)) = v;
             }
             dev::fence_proxy_async_smem();
@@ -428,7 +431,8 @@ int attend_rows_prefill(const nmg_kv_cache* c, int hq, const void* q, int q_dtyp
         cuuint64_t strides[1] = {(cuuint64_t)dh * 2};
         cuuint32_t box[2] = {64, (cuuint32_t)bn};
         cuuint32_t es[2] = {1, 1};
-        CUresult r = enc(which ? &a->tm_v : &a->tm_k, dt, 2, which ? c->v : c->k, dims, strides, box, es,
+        const CUtensorMapDataType wdt = which ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : dt;
+        CUresult r = enc(which ? &a->tm_v : &a->tm_k, wdt, 2, which ? c->v : c->k, dims, strides, box, es,
                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
         if (r != CUDA_SUCCESS) {

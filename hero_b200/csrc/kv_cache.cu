@@ -21,6 +21,17 @@ namespace {
 
 // One thread per (row, head, 8-element chunk); rows are the last `rows`
 // appended positions, row r going to slot (slot0 + r) mod slots.
+// V of a bf16 cache holds bf16 values stored as fp16: round to bf16 first
+// (the cache's value set), then convert exactly.
+template <int DST>
+__device__ __forceinline__ void store_v(void* vc, int64_t i, float x) {
+    if constexpr (DST == NMG_BF16) {
+        ((uint16_t*)vc)[i] = dev::f32_to_f16_bits(dev::bf16_bits_to_f32(dev::f32_to_bf16_bits(x)));
+    } else {
+        dev::store_from_f32(vc, DST, i, x);
+    }
+}
+
 template <int SRC, int DST>
 __global__ void kv_append_kernel(const void* __restrict__ keys, const void* __restrict__ values, void* __restrict__ kc,
                                  void* __restrict__ vc, int64_t rows, int64_t src_row0, int hkv, int dh, int64_t slots,
@@ -43,13 +54,15 @@ __global__ void kv_append_kernel(const void* __restrict__ keys, const void* __re
                 const float kf = dev::load_as_f32(keys, SRC, src + d0 + e);
                 const float vf = dev::load_as_f32(values, SRC, src + d0 + e);
                 dev::store_from_f32(kc, DST, dst + d0 + e, kf);
-                dev::store_from_f32(vc, DST, dst + d0 + e, vf);
+                store_v<DST>(vc, dst + d0 + e, vf);
             }
         }
     }
 }
 
-// Same-dtype fast path: 16-byte vector copies when a head row is a multiple of 16 bytes.
+// Same-dtype fast path: 16-byte vector copies when a head row is a multiple of
+// 16 bytes; V_TO_F16 converts bf16 V rows to the fp16 V buffer on the way.
+template <bool V_TO_F16>
 __global__ void kv_append_copy16_kernel(const uint4* __restrict__ keys, const uint4* __restrict__ values,
                                         uint4* __restrict__ kc, uint4* __restrict__ vc, int64_t rows, int64_t src_row0,
                                         int hkv, int vecs_per_head, int64_t slots, int64_t slot0) {
@@ -63,7 +76,18 @@ __global__ void kv_append_copy16_kernel(const uint4* __restrict__ keys, const ui
         const int64_t src = ((src_row0 + r) * hkv + h) * vecs_per_head + c;
         const int64_t dst = ((int64_t)h * slots + slot) * vecs_per_head + c;
         kc[dst] = __ldg(keys + src);
-        vc[dst] = __ldg(values + src);
+        uint4 v = __ldg(values + src);
+        if constexpr (V_TO_F16) {
+            uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const uint32_t lo = dev::f32_to_f16_bits(dev::bf16_bits_to_f32(w[i] & 0xFFFFu));
+                const uint32_t hi = dev::f32_to_f16_bits(dev::bf16_bits_to_f32(w[i] >> 16));
+                w[i] = lo | (hi << 16);
+            }
+            v = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+        vc[dst] = v;
     }
 }
 
@@ -97,8 +121,14 @@ int kv_append_device(nmg_kv_cache* c, int64_t first_position, const void* keys, 
         const int vecs = c->dh * es / 16;
         const int64_t work = write * c->hkv * vecs;
         const int blocks = (int)((work + 255) / 256 < 148 * 16 ? (work + 255) / 256 : 148 * 16);
-        kv_append_copy16_kernel<<<blocks, 256, 0, stream>>>((const uint4*)keys, (const uint4*)values, (uint4*)c->k,
-                                                            (uint4*)c->v, write, row0, c->hkv, vecs, c->slots, slot0);
+        if (c->vdtype != c->dtype)
+            kv_append_copy16_kernel<true><<<blocks, 256, 0, stream>>>((const uint4*)keys, (const uint4*)values,
+                                                                      (uint4*)c->k, (uint4*)c->v, write, row0, c->hkv,
+                                                                      vecs, c->slots, slot0);
+        else
+            kv_append_copy16_kernel<false><<<blocks, 256, 0, stream>>>((const uint4*)keys, (const uint4*)values,
+                                                                       (uint4*)c->k, (uint4*)c->v, write, row0, c->hkv,
+                                                                       vecs, c->slots, slot0);
     } else {
         const int64_t work = write * c->hkv * ((c->dh + 7) / 8);
         const int blocks = (int)((work + 255) / 256 < 148 * 16 ? (work + 255) / 256 : 148 * 16);
@@ -136,6 +166,7 @@ extern "C" int nmg_kv_create(int hkv, int head_dim, int dtype, int64_t window, i
     c->dh = head_dim;
     c->dtype = dtype;
     c->device = device;
+    c->vdtype = nmg::v_dtype_for(dtype);
     c->window = window;
     c->slots = capacity;
     int prev = 0;
@@ -317,17 +348,24 @@ extern "C" int nmg_kv_read_row(const nmg_kv_cache* c, int64_t row, int head, flo
             memcpy(&kh, kb.data() + 2 * d, 2);
             memcpy(&vh, vb.data() + 2 * d, 2);
             if (c->dtype == NMG_BF16) {
-                uint32_t kbits = (uint32_t)kh << 16, vbits = (uint32_t)vh << 16;
+                uint32_t kbits = (uint32_t)kh << 16;
                 memcpy(&kf, &kbits, 4);
-                memcpy(&vf, &vbits, 4);
             } else {
                 kf = __half2float(__ushort_as_half(kh));
-                vf = __half2float(__ushort_as_half(vh));
             }
+            vf = __half2float(__ushort_as_half(vh));  // V of a 16-bit cache is fp16
         }
         if (key_out) key_out[d] = kf;
         if (value_out) value_out[d] = vf;
     }
+    return NMG_OK;
+}
+
+extern "C" int nmg_kv_reset(nmg_kv_cache* c) {
+    if (!c) return set_error(NMG_INVALID_ARGUMENT, "nmg_kv_reset: null cache");
+    c->size = c->oldest = c->base = c->total = 0;
+    c->retaining = false;
+    c->batch_remaining = 0;
     return NMG_OK;
 }
 

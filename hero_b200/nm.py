@@ -141,6 +141,10 @@ class _Cache:
     def value(self, chronological_row: int, head: int) -> torch.Tensor:
         return self._row(chronological_row, head)[1]
 
+    def reset(self) -> None:
+        """Forget every row: a new sequence on the same device storage."""
+        call("nmg_kv_reset", self._h)
+
     def storage(self):
         """(keys_ptr, values_ptr, slots) of the head-major device storage."""
         k, v, s = ctypes.c_void_p(), ctypes.c_void_p(), ctypes.c_int64()

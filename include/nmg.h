@@ -111,6 +111,11 @@ NMG_API int nmg_kv_end_batch_retention(nmg_kv_cache* cache);
 NMG_API int nmg_kv_read_row(const nmg_kv_cache* cache, int64_t chronological_row, int kv_head, float* key_out, float* value_out,
                     void* stream);
 
+/* Forget every row (a new sequence on the same device storage), the device
+ * counterpart of dropping a PrefixState's carried caches
+ * (src/transformer.hpp:139-142).  No device work. */
+NMG_API int nmg_kv_reset(nmg_kv_cache* cache);
+
 /* Raw device storage, for callers that fuse their own producer. */
 NMG_API int nmg_kv_storage(const nmg_kv_cache* cache, void** keys, void** values, int64_t* slots);
 

@@ -20,6 +20,7 @@
 #include "attention.hpp"
 #include "recurrent.hpp"
 
+#include <chrono>
 #include <cstdint>
 #include <cstdio>
 #include <cstdlib>
@@ -59,6 +60,33 @@ void reduce(const Cache& cache, const float* q, size_t qrows, size_t hq, Positio
         }
         alpha = Softmax{}(std::move(alpha));
 
+        Vec<Dh> head_output;
+        for (size_t n = 0; n < alpha.size(); ++n) head_output.scaled_add(cache.value(rows.first + n, group), alpha[n]);
+        for (size_t i = 0; i < Dh; ++i) out[(row * hq + head) * Dh + i] = head_output[i];
+    });
+}
+
+// The reduction with a causal window applied to a full cache's rows:
+// CausalWindow{window}.visible_rows over the cache's positions.
+template <size_t Hkv, size_t Dh, class Cache>
+void reduce_window(const Cache& cache, size_t window, const float* q, size_t qrows, size_t hq, Position at, float scale,
+                   bool use_scale, float* out) {
+    std::vector<VisibleRows> visible;
+    visible.reserve(qrows);
+    for (size_t row = 0; row < qrows; ++row)
+        visible.push_back(CausalWindow{window}.visible_rows(at + row, cache.position(0), cache.size()));
+    par_for(qrows * hq, [&](size_t task) {
+        const size_t row = task / hq, head = task % hq;
+        const Vec<Dh> query = vec_from<Dh>(q + (row * hq + head) * Dh);
+        const KVHead group{head / (hq / Hkv)};
+        const VisibleRows rows = visible[row];
+        std::vector<Scalar> alpha;
+        alpha.reserve(rows.count());
+        for (size_t j = rows.first; j < rows.end; ++j) {
+            const Scalar d = dot(VecView<Dh>(query), cache.key(j, group));
+            alpha.push_back(use_scale ? scale * d : d);
+        }
+        alpha = Softmax{}(std::move(alpha));
         Vec<Dh> head_output;
         for (size_t n = 0; n < alpha.size(); ++n) head_output.scaled_add(cache.value(rows.first + n, group), alpha[n]);
         for (size_t i = 0; i < Dh; ++i) out[(row * hq + head) * Dh + i] = head_output[i];
@@ -185,6 +213,35 @@ int delta_run(float* state_io, size_t T, size_t hk, const float* q, const float*
     });
 }
 
+// Timed sample of a prefill: the cache is filled untimed, then the reduction
+// runs for each block [start, start+len) of query rows; only the reductions
+// are timed (seconds_out).  q is the full [rows][hq*Dh] query matrix.
+template <size_t Hkv, size_t Dh>
+int prefill_sample(const float* k, const float* v, size_t rows, const float* q, size_t hq, const int64_t* blocks,
+                   size_t nblocks, float scale, bool use_scale, size_t window, float* out, double* seconds_out) {
+    constexpr size_t W = Hkv * Dh;
+    return guarded([&] {
+        FullAttentionCache<Hkv, Dh> cache;
+        for (size_t r = 0; r < rows; ++r) cache.append(Position{r}, vec_from<W>(k + r * W), vec_from<W>(v + r * W));
+        double total = 0;
+        for (size_t b = 0; b < nblocks; ++b) {
+            const size_t start = size_t(blocks[2 * b]), len = size_t(blocks[2 * b + 1]);
+            const auto t0 = std::chrono::steady_clock::now();
+            if (window == 0) {
+                reduce<Hkv, Dh>(cache, q + start * hq * Dh, len, hq, Position{start}, scale, use_scale, out + start * hq * Dh);
+            } else {
+                // A window only narrows each row's visible interval; the same
+                // reduction over a LocalAttentionCache view is what the Gemma
+                // local layers run (gemma4.hpp:593-615).
+                reduce_window<Hkv, Dh>(cache, window, q + start * hq * Dh, len, hq, Position{start}, scale, use_scale,
+                                       out + start * hq * Dh);
+            }
+            total += std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+        }
+        *seconds_out = total;
+    });
+}
+
 }  // namespace
 
 #define NMREF_ATTN_SHAPES(X) \
@@ -241,6 +298,18 @@ int nmref_attend_local(int hkv, int dh, int64_t window, const float* k, const fl
     return 100;
 }
 
+int nmref_prefill_sample(int hkv, int dh, const float* k, const float* v, int64_t rows, const float* q, int hq,
+                         const int64_t* blocks, int64_t nblocks, float scale, int use_scale, int64_t window, float* out,
+                         double* seconds) {
+#define X(H, D)                                                                                                   \
+    if (hkv == H && dh == D)                                                                                      \
+        return prefill_sample<H, D>(k, v, size_t(rows), q, size_t(hq), blocks, size_t(nblocks), scale, use_scale != 0, \
+                                    size_t(window), out, seconds);
+    NMREF_ATTN_SHAPES(X)
+#undef X
+    return 100;
+}
+
 int nmref_local_script(int64_t window, const int64_t* ops, int64_t nops, int64_t* size_out, int64_t* positions_out,
                        int64_t max_positions, int64_t* first_failed_op) {
     return local_script(size_t(window), ops, size_t(nops), size_out, positions_out, size_t(max_positions), first_failed_op);
@@ -264,6 +333,14 @@ int nmref_delta_run(int hv, int dk, int dv, float* state, int64_t T, int hk, con
     NMREF_DELTA_SHAPES(X)
 #undef X
     return 100;
+}
+
+int nmref_delta_timed(int hv, int dk, int dv, float* state, int64_t T, int hk, const float* q, const float* k,
+                      const float* v, const float* g, const float* beta, float* out, double* seconds) {
+    const auto t0 = std::chrono::steady_clock::now();
+    const int st = nmref_delta_run(hv, dk, dv, state, T, hk, q, k, v, g, beta, out);
+    *seconds = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+    return st;
 }
 
 float nmref_softplus(float x) { return softplus(x); }
