@@ -1,0 +1,664 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 attention / delta-rule path (one JSON line on rank 0).
+
+Headline workload: causal GQA prefill, bf16 in / fp32
+accumulate, batch 1, seq 4096, 32 query heads, 8 KV heads, head_dim 128, RoPE
+pre-applied, K/V written to the device cache.  One step = append the 4096 K/V
+rows into a fresh cache + attention of the 4096 query rows (137.47 GFLOP).
+`value` is TFLOP/s of that step with inputs resident in HBM; `e2e` is the same
+through the C ABI with host (pinned) inputs and outputs copied inside the
+timed region.
+
+At N GPUs (torchrun) each rank owns hkv/N KV heads (and their query heads)
+and the head outputs are all-gathered over NVLink by NCCL, then permuted back
+to the reference's [row][head*dim] layout: total work is fixed ("strong").
+
+Measured extras at N=1 (their own units, each with a roofline fraction):
+config 1 fp32 decode, config 3 delta-rule prefill + 256 decode steps,
+config 4 Gemma hybrid prefill (5 local + 1 global layer) and batch-16 decode,
+config 5 ragged batch-64 long-context f16 decode.
+
+`--impl reference` times the reference engine's own CPU code (oracle/_ref,
+its headers compiled here; the C restatement in oracle/ if that library is
+absent) on a bounded sample of the same workload with every host core.
+"""
+import argparse
+import ctypes
+import json
+import math
+import os
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "decode attn GB/s, prefill TFLOP/s (% roofline); tok/s at 1/2/4/8 B200"
+S2, HQ2, HKV2, DH2 = 4096, 32, 8, 128
+L2_BYTES = 126 * 2**20
+
+
+def c2_flops(S=S2, hq=HQ2, dh=DH2):
+    return 4.0 * dh * hq * (S * (S + 1) // 2)
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        p = json.load(open(path))
+        return {"hbm": float(p["hbm_gbs"]), "bf16": float(p["bf16_tflops"]),
+                "bf16_sustained": float(p.get("bf16_tflops_sustained", p["bf16_tflops"])), "src": "measured"}
+    except Exception:
+        return {"hbm": 6650.0, "bf16": 1590.0, "bf16_sustained": 1400.0, "src": "fallback"}
+
+
+def ncu_traffic(name):
+    """dram bytes per launch from a committed ncu summary (profiles/<name>.md), or None."""
+    path = os.path.join(ROOT, "profiles", name + ".md")
+    if not os.path.exists(path):
+        return None
+    for line in open(path):
+        if line.strip().startswith("dram_bytes_per_launch:"):
+            try:
+                return float(line.split(":", 1)[1].strip().split()[0])
+            except ValueError:
+                return None
+    return None
+
+
+# ---------------------------------------------------------------- clocks
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_id):
+        self.gpu_id = gpu_id
+        self.proc = None
+        self.path = os.path.join("/tmp", f"nmg_clocks_{os.getpid()}.csv")
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu_id), f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+            time.sleep(0.3)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        rows = []
+        try:
+            for line in open(self.path):
+                parts = [x.strip() for x in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+        except Exception:
+            pass
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        smax = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower().startswith("active")})
+        loaded = [s for s in sm if smax and s > 0.5 * max(smax)] or sm
+        return {"sm_mhz": float(np.median(loaded)) if loaded else None, "sm_max_mhz": max(smax) if smax else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def gpu_smi_id(torch, dev):
+    """nvidia-smi's index for this process's device (CUDA_VISIBLE_DEVICES-aware)."""
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES", "").strip()
+    if vis:
+        ids = [x.strip() for x in vis.split(",")]
+        if dev.index < len(ids) and ids[dev.index].isdigit():
+            return ids[dev.index]
+    return str(dev.index)
+
+
+# ---------------------------------------------------------------- CPU baseline
+
+class RefSample:
+    """The reference reduction on a bounded sample of config 2, timed on the host.
+
+    Inputs are generated once; `run()` times the reduction only (the cache is
+    filled untimed inside the reference shim) and returns seconds."""
+
+    def __init__(self, rows_per_block=256, threads=None):
+        import oracle
+
+        self.threads = threads or os.cpu_count() or 1
+        os.environ.setdefault("NM_THREADS", str(self.threads))
+        S, hq, hkv, dh = S2, HQ2, HKV2, DH2
+        self.q = oracle.round_bf16(oracle.normal(0, 3, S * hq * dh)).reshape(S, hq * dh)
+        self.k = oracle.round_bf16(oracle.normal(0, 1, S * hkv * dh)).reshape(S, hkv * dh)
+        self.v = oracle.round_bf16(oracle.normal(0, 2, S * hkv * dh)).reshape(S, hkv * dh)
+        self.blocks = np.array([S // 2 - rows_per_block // 2, rows_per_block, S - rows_per_block, rows_per_block],
+                               np.int64)
+        self.flops = c2_sample_flops(rows_per_block)
+        self.out = np.zeros_like(self.q)
+        self.scale = np.float32(1 / math.sqrt(dh))
+        self.R = oracle.ref()
+        self.oracle = oracle
+        if self.R is not None:
+            self.kind = "reference"
+            self.R.nmref_prefill_sample.argtypes = [
+                ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p,
+                ctypes.c_int, ctypes.c_void_p, ctypes.c_int64, ctypes.c_float, ctypes.c_int, ctypes.c_int64,
+                ctypes.c_void_p, ctypes.POINTER(ctypes.c_double)]
+            self.cores = int(self.R.nmref_threads())
+        else:
+            self.kind = "port"
+            self.cores = self.threads
+        b = self.blocks
+        self.sample = (f"query rows [{b[0]},{b[0] + b[1]}) and [{b[2]},{S2}) of the S=4096 32q/8kv/d128 causal "
+                       f"prefill ({self.flops / 1e9:.1f} GFLOP), reduction only, {self.cores} threads")
+
+    def run(self):
+        if self.R is not None:
+            sec = ctypes.c_double()
+            st = self.R.nmref_prefill_sample(HKV2, DH2, self.k.ctypes.data, self.v.ctypes.data, S2, self.q.ctypes.data,
+                                             HQ2, self.blocks.ctypes.data, 2, self.scale, 1, 0, self.out.ctypes.data,
+                                             ctypes.byref(sec))
+            if st != 0:
+                raise RuntimeError(f"reference sample failed ({st})")
+            return sec.value
+        total = 0.0
+        for b in range(2):
+            s0, n = int(self.blocks[2 * b]), int(self.blocks[2 * b + 1])
+            t0 = time.perf_counter()
+            self.oracle.attend(self.k[:s0 + n], self.v[:s0 + n], 0, 0, HKV2, DH2, self.q[s0:s0 + n], HQ2, s0,
+                               scale=self.scale, threads=self.threads)
+            total += time.perf_counter() - t0
+        return total
+
+
+def reference_arm(args, rank, world):
+    if rank != 0:
+        return
+    t0 = time.perf_counter()
+    ref = RefSample()
+    for _ in range(args.warmup):
+        ref.run()
+    secs = [ref.run() for _ in range(args.steps)]
+    value = ref.flops / float(np.mean(secs)) / 1e12
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * float(np.mean(secs)),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": config2_desc(world),
+            "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": ref.cores, "kind": ref.kind,
+                             "sample": ref.sample},
+            "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "wall_s": time.perf_counter() - t0}
+    print(json.dumps(line), flush=True)
+
+
+def c2_sample_flops(rows_per_block=256):
+    S = S2
+    b0, b1 = S // 2 - rows_per_block // 2, S - rows_per_block
+    pairs = sum(r + 1 for r in range(b0, b0 + rows_per_block)) + sum(r + 1 for r in range(b1, S))
+    return 4.0 * DH2 * HQ2 * pairs
+
+
+def config2_desc(world):
+    return {"workload": "config 2: causal GQA prefill, bf16 in / fp32 accumulate, K/V written to the device cache",
+            "batch": 1, "seq_len": S2, "q_heads": HQ2, "kv_heads": HKV2, "head_dim": DH2,
+            "flop_per_step": c2_flops(),
+            "parallelism": f"kv-head shards x{world}" + (" + NCCL all-gather of head outputs" if world > 1 else ""),
+            "l2": "inputs rotate over sets larger than the 126 MB L2"}
+
+
+# ---------------------------------------------------------------- headline
+
+class Comm:
+    def __init__(self, rank, world, device, torch, dist):
+        from hero_b200 import _lib
+
+        self.lib = _lib
+        uid = (ctypes.c_char * 128)()
+        if rank == 0:
+            _lib.call("nmg_comm_unique_id", uid)
+        obj = [bytes(uid) if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        uid = (ctypes.c_char * 128).from_buffer_copy(obj[0])
+        h = ctypes.c_void_p()
+        _lib.call("nmg_comm_init", uid, rank, world, device, ctypes.byref(h))
+        self.h = h
+        self.world = world
+
+    def allgather(self, send, recv, stream):
+        self.lib.call("nmg_allgather", self.h, ctypes.c_void_p(send.data_ptr()), ctypes.c_void_p(recv.data_ptr()),
+                      send.numel() * send.element_size(), stream)
+
+    def to_rows(self, gathered, out, rows, row_bytes, stream):
+        self.lib.call("nmg_gather_heads_to_rows", ctypes.c_void_p(gathered.data_ptr()), ctypes.c_void_p(out.data_ptr()),
+                      self.world, rows, row_bytes, stream)
+
+    def close(self):
+        self.lib.lib().nmg_comm_destroy(self.h)
+
+
+def bench_prefill(args, torch, dist, rank, world, dev):
+    from hero_b200 import nm
+
+    S, hq, hkv, dh = S2, HQ2, HKV2, DH2
+    hkv_l, hq_l = hkv // world, hq // world
+    scale = 1.0 / math.sqrt(dh)
+    set_bytes = S * (hq_l * dh * 2 * 2 + hkv_l * dh * 2 * 4)
+    R = int(min(64, max(4, math.ceil(3 * L2_BYTES / set_bytes))))
+    g = torch.Generator(device=dev)
+    g.manual_seed(1234 + rank)
+    sets = []
+    for _ in range(R):
+        q = torch.randn(S, hq_l * dh, device=dev, generator=g).to(torch.bfloat16)
+        k = torch.randn(S, hkv_l * dh, device=dev, generator=g).to(torch.bfloat16)
+        v = torch.randn(S, hkv_l * dh, device=dev, generator=g).to(torch.bfloat16)
+        c = nm.FullAttentionCache(hkv_l, dh, capacity=S, dtype="bf16", device=dev.index)
+        o = torch.empty(S, hq_l * dh, device=dev, dtype=torch.bfloat16)
+        sets.append((q, k, v, c, o))
+    comm = None
+    if world > 1:
+        comm = Comm(rank, world, dev.index, torch, dist)
+        gathered = torch.empty(world, S, hq_l * dh, device=dev, dtype=torch.bfloat16)
+        full = torch.empty(S, hq * dh, device=dev, dtype=torch.bfloat16)
+    stream = torch.cuda.current_stream(dev)
+    sp = ctypes.c_void_p(stream.cuda_stream)
+
+    def step(i, ev=None):
+        q, k, v, c, o = sets[i % R]
+        c.reset()
+        c.append(0, k, v)
+        if ev is not None:
+            ev[0].record(stream)
+        nm.attend(c, q, 0, scale, out=o)
+        if ev is not None:
+            ev[1].record(stream)
+        if comm is not None:
+            comm.allgather(o, gathered, sp)
+            comm.to_rows(gathered, full, S, hq_l * dh * 2, sp)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    for i in range(args.warmup):
+        step(i)
+    barrier()
+    kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(gpu_smi_id(torch, dev)) as clk:
+        barrier()
+        t0.record(stream)
+        for i in range(args.steps):
+            step(args.warmup + i, kev[i])
+        t1.record(stream)
+        barrier()
+    ms = t0.elapsed_time(t1)
+    kernel_ms = sum(a.elapsed_time(b) for a, b in kev) / args.steps
+    if world > 1:
+        tt = torch.tensor([ms, kernel_ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        ms, kernel_ms = float(tt[0]), float(tt[1])
+    ms_step = ms / args.steps
+    value = c2_flops() / (ms_step * 1e-3) / 1e12
+
+    # ---- end to end through the C ABI with host buffers
+    pin = lambda t: t.cpu().pin_memory()
+    hq_host, hk_host, hv_host = pin(sets[0][0]), pin(sets[0][1]), pin(sets[0][2])
+    out_host = torch.empty(S, hq * dh, dtype=torch.bfloat16).pin_memory()
+    e2e_steps = max(3, args.steps // 2)
+
+    def e2e_step(i):
+        q, k, v, c, o = sets[i % R]
+        q.copy_(hq_host, non_blocking=True)
+        k.copy_(hk_host, non_blocking=True)
+        v.copy_(hv_host, non_blocking=True)
+        c.reset()
+        c.append(0, k, v)
+        nm.attend(c, q, 0, scale, out=o)
+        if comm is not None:
+            comm.allgather(o, gathered, sp)
+            comm.to_rows(gathered, full, S, hq_l * dh * 2, sp)
+            out_host.copy_(full, non_blocking=True)
+        else:
+            out_host.copy_(o, non_blocking=True)
+
+    for i in range(2):
+        e2e_step(i)
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(e2e_steps):
+        e2e_step(i)
+    e1.record(stream)
+    barrier()
+    e2e_ms = e0.elapsed_time(e1) / e2e_steps
+    if world > 1:
+        tt = torch.tensor([e2e_ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        e2e_ms = float(tt[0])
+    h2d = world * S * (hq_l + 2 * hkv_l) * dh * 2
+    d2h = world * S * hq * dh * 2
+    if comm is not None:
+        comm.close()
+    p = peaks()
+    achieved = c2_flops() / world / (kernel_ms * 1e-3) / 1e12
+    roof = {"bound": "tensor", "kernel": "attn_prefill_kernel<128,bf16>", "achieved": achieved, "peak": p["bf16"],
+            "unit": "TFLOP/s", "frac": achieved / p["bf16"], "peak_src": f"{p['src']} bf16 dense (burst)",
+            "traffic": ncu_traffic("attn_prefill_c2"), "kernel_ms": kernel_ms,
+            "algorithmic_unit": "4*head_dim*q_heads per visible (query,key) pair; 8,390,656 pairs"}
+    launches = args.steps * (2 + (1 if world > 1 else 0))
+    return {"value": value, "ms_per_step": ms_step, "tok_per_s": S / (ms_step * 1e-3), "roofline": roof,
+            "e2e": {"value": c2_flops() / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
+            "clocks": clk.summary(), "gpu_launches": launches, "rotating_sets": R}
+
+
+# ---------------------------------------------------------------- extras (N=1)
+
+def ragged_lengths(seed, n, lo, hi):
+    """n integers uniform in [lo, hi] from a SplitMix64 counter stream (seeded, host-independent)."""
+    M = (1 << 64) - 1
+
+    def mix(z):
+        z = (z + 0x9E3779B97F4A7C15) & M
+        z = ((z ^ (z >> 30)) * 0xBF58476D1CE4E5B9) & M
+        z = ((z ^ (z >> 27)) * 0x94D049BB133111EB) & M
+        return z ^ (z >> 31)
+
+    key = mix(seed ^ mix(0x632BE59BD9B4E019))
+    return [lo + mix((key + j) & M) % (hi - lo + 1) for j in range(n)]
+
+
+def graph_time(torch, dev, fn, reps, inner):
+    """Average ms of fn() when `inner` calls are captured in one CUDA graph and replayed `reps` times."""
+    fn()
+    torch.cuda.synchronize(dev)
+    g = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream(dev)
+    s.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(s):
+        fn()
+        torch.cuda.synchronize(dev)
+        with torch.cuda.graph(g, stream=s):
+            for _ in range(inner):
+                fn()
+    torch.cuda.current_stream(dev).wait_stream(s)
+    torch.cuda.synchronize(dev)
+    g.replay()
+    torch.cuda.synchronize(dev)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(reps):
+        g.replay()
+    b.record()
+    torch.cuda.synchronize(dev)
+    return a.elapsed_time(b) / (reps * inner)
+
+
+def extra_config1(torch, dev, small=False):
+    from hero_b200 import nm
+
+    hq, hkv, dh, rows, NC = 16, 8, 128, 1024, 20
+    caches, qs, outs = [], [], []
+    for i in range(NC):
+        c = nm.FullAttentionCache(hkv, dh, capacity=rows, device=dev.index)
+        c.append(0, torch.randn(rows, hkv * dh, device=dev), torch.randn(rows, hkv * dh, device=dev))
+        caches.append(c)
+        qs.append(torch.randn(1, hq * dh, device=dev))
+        outs.append(torch.empty(1, hq * dh, device=dev))
+    it = [0]
+
+    def fn():
+        for i in range(NC):
+            nm.attend(caches[i], qs[i], rows - 1, 1 / math.sqrt(dh), out=outs[i])
+
+    ms = graph_time(torch, dev, fn, 20, 5) / NC
+    bytes_ = 2 * rows * hkv * dh * 4 + 2 * hq * dh * 4
+    p = peaks()
+    gbs = bytes_ / (ms * 1e-3) / 1e9
+    return {"workload": "config 1: decode, fp32, 16q/8kv, d128, 1024 cached", "value": gbs, "unit": "GB/s",
+            "us_per_call": ms * 1e3, "tok_per_s": 1 / (ms * 1e-3),
+            "roofline": {"bound": "hbm", "achieved": gbs, "peak": p["hbm"], "frac": gbs / p["hbm"],
+                         "bytes_per_call": bytes_},
+            "method": f"{NC} caches (168 MB > L2) rotated in a CUDA graph; kernel time per call"}
+
+
+def extra_config3(torch, dev, small=False):
+    from hero_b200 import nm
+
+    hv, hk, d, T, Tdec = 32, 16, 128, 8192, 256
+    g = torch.Generator(device=dev)
+    g.manual_seed(3)
+    norm = lambda x: x / x.norm(dim=-1, keepdim=True).clamp_min(1e-6)
+    q = norm(torch.randn(T, hk, d, device=dev, generator=g)) / math.sqrt(d)
+    k = norm(torch.randn(T, hk, d, device=dev, generator=g))
+    v = torch.randn(T, hv, d, device=dev, generator=g)
+    gate = -torch.nn.functional.softplus(torch.randn(T, hv, device=dev, generator=g))
+    beta = torch.sigmoid(torch.randn(T, hv, device=dev, generator=g))
+    st = nm.DeltaNetState(hv, d, d, device=dev.index)
+    out = torch.empty(T, hv, d, device=dev)
+    res = {}
+    for chunk in (0, 64):
+        try:
+            nm.delta_prefill(st, q, k, v, gate, beta, hk, chunk=chunk, out=out)
+        except Exception as e:  # a chunk size this build does not provide
+            res[f"prefill_chunk{chunk}"] = {"unavailable": str(e)[:120]}
+            continue
+        torch.cuda.synchronize(dev)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(3):
+            st.clear()
+            nm.delta_prefill(st, q, k, v, gate, beta, hk, chunk=chunk, out=out)
+        b.record()
+        torch.cuda.synchronize(dev)
+        ms = a.elapsed_time(b) / 3
+        seq_flops = 7.0 * d * d * T * hv
+        res[f"prefill_chunk{chunk}"] = {"ms": ms, "tok_per_s": T / (ms * 1e-3),
+                                        "tflops_recurrence_equiv": seq_flops / (ms * 1e-3) / 1e12}
+    # 256 decode steps continue from the final state, graph-captured
+    qd = norm(torch.randn(Tdec, hk, d, device=dev, generator=g)) / math.sqrt(d)
+    kd = norm(torch.randn(Tdec, hk, d, device=dev, generator=g))
+    vd = torch.randn(Tdec, hv, d, device=dev, generator=g)
+    gd = -torch.nn.functional.softplus(torch.randn(Tdec, hv, device=dev, generator=g))
+    bd = torch.sigmoid(torch.randn(Tdec, hv, device=dev, generator=g))
+    od = torch.empty(Tdec, hv, d, device=dev)
+
+    def fn():
+        for t in range(Tdec):
+            nm.delta_step(st, qd[t], kd[t], vd[t], gd[t], bd[t], hk, out=od[t])
+
+    ms = graph_time(torch, dev, fn, 5, 1) / Tdec
+    bytes_ = 2 * hv * d * d * 4 + 2 * hk * d * 4 + 2 * hv * d * 4 + 2 * hv * 4
+    p = peaks()
+    gbs = bytes_ / (ms * 1e-3) / 1e9
+    res["decode"] = {"us_per_step": ms * 1e3, "value": gbs, "unit": "GB/s", "tok_per_s": 1 / (ms * 1e-3),
+                     "roofline": {"bound": "hbm", "achieved": gbs, "peak": p["hbm"], "frac": gbs / p["hbm"],
+                                  "bytes_per_step": bytes_, "note": "2 MB state is L2-resident between steps"}}
+    return {"workload": "config 3: gated delta rule, T=8192, 16 k-heads / 32 v-heads, d128, fp32 state", **res}
+
+
+def extra_config4(torch, dev, small=False):
+    from hero_b200 import nm
+
+    hq, hkv, dh, W, S = 8, 4, 256, 1024, 8192
+    g = torch.Generator(device=dev)
+    g.manual_seed(4)
+    rms = lambda x: x / x.float().pow(2).mean(dim=-1, keepdim=True).add(1e-6).sqrt()
+    q = rms(torch.randn(S, hq, dh, device=dev, generator=g)).reshape(S, hq * dh).to(torch.bfloat16)
+    k = rms(torch.randn(S, hkv, dh, device=dev, generator=g)).reshape(S, hkv * dh).to(torch.bfloat16)
+    v = torch.randn(S, hkv * dh, device=dev, generator=g).to(torch.bfloat16)
+    o = torch.empty(S, hq * dh, device=dev, dtype=torch.bfloat16)
+    local = [nm.LocalAttentionCache(hkv, dh, W, capacity=S + W, dtype="bf16", device=dev.index) for _ in range(5)]
+    glob = nm.FullAttentionCache(hkv, dh, capacity=S, dtype="bf16", device=dev.index)
+
+    def group():
+        for c in local:
+            c.reset()
+            nm.append_attend(c, 0, k, v, q, None, out=o)
+        glob.reset()
+        nm.append_attend(glob, 0, k, v, q, None, out=o)
+
+    group()
+    torch.cuda.synchronize(dev)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(3):
+        group()
+    b.record()
+    torch.cuda.synchronize(dev)
+    ms = a.elapsed_time(b) / 3
+    pairs_g = S * (S + 1) // 2
+    pairs_l = W * (W + 1) // 2 + (S - W) * W
+    flops = 4.0 * dh * hq * (pairs_g + 5 * pairs_l)
+    p = peaks()
+    tf = flops / (ms * 1e-3) / 1e12
+    res = {"prefill": {"ms_per_group": ms, "value": tf, "unit": "TFLOP/s", "tok_per_s": S / (ms * 1e-3),
+                       "roofline": {"bound": "tensor", "achieved": tf, "peak": p["bf16"], "frac": tf / p["bf16"],
+                                    "flop_per_group": flops}}}
+    del local, glob, q, k, v, o
+    # decode: batch 16, 32768 cached rows (query at 32767), global + local layers
+    B, L = (2, 32768) if small else (16, 32768)
+    gcaches, lcaches = [], []
+    for b_ in range(B):
+        kk = torch.randn(L, hkv * dh, device=dev, generator=g).to(torch.bfloat16)
+        vv = torch.randn(L, hkv * dh, device=dev, generator=g).to(torch.bfloat16)
+        c = nm.FullAttentionCache(hkv, dh, capacity=L, dtype="bf16", device=dev.index)
+        c.append(0, kk, vv)
+        gcaches.append(c)
+        lc = nm.LocalAttentionCache(hkv, dh, W, capacity=2 * W, dtype="bf16", device=dev.index)
+        lc.append(L - W, kk[L - W:], vv[L - W:])
+        lcaches.append(lc)
+        del kk, vv
+    qd = torch.randn(B, hq * dh, device=dev, generator=g).to(torch.bfloat16)
+    od = torch.empty(B, hq * dh, device=dev, dtype=torch.float32)
+    ms_g = graph_time(torch, dev, lambda: nm.attend_batch(gcaches, qd, None, out=od), 10, 2)
+    ms_l = graph_time(torch, dev, lambda: nm.attend_batch(lcaches, qd, None, out=od), 10, 20)
+    bytes_g = B * L * hkv * dh * 2 * 2
+    bytes_l = B * W * hkv * dh * 2 * 2
+    gb_g, gb_l = bytes_g / (ms_g * 1e-3) / 1e9, bytes_l / (ms_l * 1e-3) / 1e9
+    grp_ms = ms_g + 5 * ms_l
+    res["decode"] = {"global_us": ms_g * 1e3, "local_us": ms_l * 1e3, "global_GBps": gb_g, "local_GBps": gb_l,
+                     "group_tok_per_s": B / (grp_ms * 1e-3), "value": (bytes_g + 5 * bytes_l) / (grp_ms * 1e-3) / 1e9,
+                     "unit": "GB/s", "roofline": {"bound": "hbm", "achieved": gb_g, "peak": p["hbm"],
+                                                  "frac": gb_g / p["hbm"], "kernel": "global layer decode"}}
+    return {"workload": "config 4: Gemma hybrid bf16, 8q/4kv, d256, scale 1, 5 local (W=1024) : 1 global", **res}
+
+
+def extra_config5(torch, dev, small=False):
+    from hero_b200 import nm
+
+    B, hq, hkv, dh = 64, 64, 8, 128
+    lens = ragged_lengths(1, B, 4096, 131072)
+    if small:  # profiling size: the first 4 sequences
+        B, lens = 4, lens[:4]
+    g = torch.Generator(device=dev)
+    g.manual_seed(5)
+    caches = []
+    for L in lens:
+        c = nm.FullAttentionCache(hkv, dh, capacity=L, dtype="f16", device=dev.index)
+        chunk = 32768
+        for s in range(0, L, chunk):
+            n = min(chunk, L - s)
+            c.append(s, torch.randn(n, hkv * dh, device=dev, generator=g).half(),
+                     torch.randn(n, hkv * dh, device=dev, generator=g).half())
+        caches.append(c)
+    q = torch.randn(B, hq * dh, device=dev, generator=g).half()
+    out = torch.empty(B, hq * dh, device=dev, dtype=torch.float32)
+    ms = graph_time(torch, dev, lambda: nm.attend_batch(caches, q, 1 / math.sqrt(dh), out=out), 5, 1)
+    bytes_ = 4096 * sum(lens) + 2 * B * hq * dh * 2
+    gbs = bytes_ / (ms * 1e-3) / 1e9
+    p = peaks()
+    return {"workload": "config 5: batch 64 ragged (U[4096,131072], seed 1) decode, 64q/8kv, d128, f16 cache",
+            "value": gbs, "unit": "GB/s", "ms_per_call": ms, "tok_per_s": B / (ms * 1e-3), "kv_bytes": 4096 * sum(lens),
+            "roofline": {"bound": "hbm", "achieved": gbs, "peak": p["hbm"], "frac": gbs / p["hbm"]}}
+
+
+# ---------------------------------------------------------------- main
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="nmg", choices=["nmg", "reference"])
+    ap.add_argument("--no-extra", action="store_true", help="headline only")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--only", choices=["c1", "c2", "c3", "c4", "c5"],
+                    help="run one workload alone (profiling); prints its own JSON line")
+    ap.add_argument("--small", action="store_true", help="with --only: profiling-sized variant")
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local = int(os.environ.get("LOCAL_RANK", 0))
+    if args.impl == "reference":
+        reference_arm(args, rank, world)
+        return
+
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    if HKV2 % world:
+        raise SystemExit(f"{world} GPUs do not divide {HKV2} KV heads")
+    import hero_b200
+
+    hero_b200.lib()  # fail loudly before any work if the CUDA library is missing
+    if args.only and args.only != "c2":
+        fn = {"c1": extra_config1, "c3": extra_config3, "c4": extra_config4, "c5": extra_config5}[args.only]
+        print(json.dumps({"only": args.only, "small": args.small, **fn(torch, dev, small=args.small)}), flush=True)
+        return
+    res = bench_prefill(args, torch, dist, rank, world, dev)
+    extra = {}
+    if world == 1 and not args.no_extra and not args.only:
+        for name, fn in (("config1", extra_config1), ("config3", extra_config3), ("config4", extra_config4),
+                         ("config5", extra_config5)):
+            try:
+                extra[name] = fn(torch, dev)
+            except Exception as e:  # report, never hide, a failing extra
+                extra[name] = {"error": f"{type(e).__name__}: {str(e)[:200]}"}
+            torch.cuda.empty_cache()
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        ref = RefSample()
+        ref.run()
+        secs = [ref.run() for _ in range(2)]
+        cpu = {"value": ref.flops / float(np.mean(secs)) / 1e12, "unit": "TFLOP/s", "cores": ref.cores,
+               "kind": ref.kind, "sample": ref.sample, "seconds_per_sample": float(np.mean(secs))}
+    if rank == 0:
+        line = {"metric": METRIC, "value": res["value"], "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": res["ms_per_step"], "higher_is_better": True,
+                "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (torch.randn, seeded)",
+                "config": {**config2_desc(world), "rotating_sets": res["rotating_sets"]},
+                "tok_per_s": res["tok_per_s"], "roofline": res["roofline"], "cpu_baseline": cpu, "e2e": res["e2e"],
+                "clocks": res["clocks"], "gpu_launches": res["gpu_launches"], "extra": extra}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

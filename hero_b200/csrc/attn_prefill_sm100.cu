@@ -4,18 +4,24 @@
 // One CTA computes a 128-row query tile of one query head against the key
 // blocks its rows can see, reading K/V straight out of the device cache:
 //
-//   warp 0      TMA producer: Q tile once, then K/V blocks into a 2-stage ring
+//   warp 0      TMA producer for Q (once) and K blocks (3-stage ring; a K
+//               stage is released as soon as its S MMA completes)
+//   warp 2      TMA producer for V blocks (2-stage ring, released after P.V)
 //               (cp.async.bulk.tensor, 128-byte swizzle, no multicast)
 //   warp 1      allocates TMEM and issues tcgen05.mma from one thread:
 //                 S_j = Q K_j^T  (M=128, N=BN, K=DH)  into TMEM (two S buffers)
-//                 O  += P_j V_j  (M=128, N=DH, K=BN)  into TMEM (O accumulator)
-//   warps 2..5  softmax: thread i owns query row i, reads its S row from TMEM,
-//               applies the causal/window mask, an online softmax in base 2
+//                 O  += P_j V_j  (M=128, N=DH, K=BN)  A = P_j read from TMEM
+//   warps 3..10 softmax: two warps share each 32-row TMEM lane quadrant and
+//               split every S row in halves (columns [0, BN/2) and [BN/2, BN));
+//               the halves swap their block maxima through shared memory, so
+//               both apply the same running max.  Each thread reads its half
+//               row from TMEM, applies the causal/window mask, an online
+//               softmax in base 2
 //               (rescaling O in TMEM only when the running max grows by more
-//               than 2^8), writes P as fp16 in the UMMA K-major swizzled
-//               layout (V is fp16 in every 16-bit cache, so P.V is an fp16
-//               MMA with 11-bit probabilities), and at the end normalises O
-//               and stores the row.
+//               than 2^8), writes P as packed fp16 pairs into TMEM over the
+//               S buffer it came from (V is fp16 in every 16-bit cache, so
+//               P.V is an fp16 MMA with 11-bit probabilities), and at the end
+//               normalises O and stores the row.
 //
 // The equation is the reference reduction (nm/src/qwen35.hpp:360-382,
 // nm/src/gemma4.hpp:593-615, :687-709): softmax over visible rows of
@@ -34,19 +40,23 @@ template <int DH>
 struct PfCfg {
     static constexpr int BM = 128;
     static constexpr int BN = DH == 128 ? 128 : 64;
-    static constexpr int STAGES = 2;
+    static constexpr int KST = DH == 128 ? 3 : 2;  // K stages (K is released as soon as S is computed)
+    static constexpr int VST = 2;  // V stages (released after P.V)
     static constexpr int Q_BYTES = BM * DH * 2;
     static constexpr int K_BYTES = BN * DH * 2;
     static constexpr int V_BYTES = BN * DH * 2;
-    static constexpr int P_BYTES = BM * BN * 2;
     static constexpr int Q_OFF = 0;
     static constexpr int K_OFF = Q_OFF + Q_BYTES;
-    static constexpr int V_OFF = K_OFF + STAGES * K_BYTES;
-    static constexpr int P_OFF = V_OFF + STAGES * V_BYTES;
-    static constexpr int BAR_OFF = P_OFF + P_BYTES;
-    static constexpr int NBARS = 1 + 2 * STAGES + 2 + 2 + 1 + 1;
+    static constexpr int V_OFF = K_OFF + KST * K_BYTES;
+    static constexpr int BAR_OFF = V_OFF + VST * V_BYTES;
+    // q_full, k_full/k_empty[KST], v_full/v_empty[VST], s_full[2], p_full[2], o_done, pair[4]
+    static constexpr int NBARS = 1 + 2 * KST + 2 * VST + 2 + 2 + 1 + 4;
     static constexpr int TMEMPTR_OFF = BAR_OFF + NBARS * 8;
-    static constexpr int SMEM = TMEMPTR_OFF + 16 + 1024;  // + slack to align the base to 1024
+    static constexpr int RED_OFF = TMEMPTR_OFF + 16;              // float [2 parity][2 halves][BM]
+    static constexpr int SMEM = RED_OFF + 2 * 2 * BM * 4 + 1024;  // + slack to align the base to 1024
+    static constexpr int SOFTMAX_THREADS = 256;
+    static constexpr int THREADS = 96 + SOFTMAX_THREADS;  // K producer, MMA, V producer, 8 softmax warps
+    static constexpr int HALF_N = BN / 2, HALF_D = DH / 2;
     static constexpr uint32_t TMEM_COLS = 512;
     static constexpr uint32_t O_COL = 2 * BN;
     static_assert(2 * BN + DH <= 512, "TMEM budget");
@@ -97,19 +107,23 @@ __device__ __forceinline__ int64_t vis_lo(const PrefillArgs& a, int64_t q) {
 __device__ __forceinline__ int64_t vis_hi(const PrefillArgs& a, int64_t q) { return q < a.newest ? q : a.newest; }
 
 template <int DH, bool BF16>
-__global__ void __launch_bounds__(192, 1) attn_prefill_kernel(const __grid_constant__ PrefillArgs a) {
+__global__ void __launch_bounds__(352, 1) attn_prefill_kernel(const __grid_constant__ PrefillArgs a) {
     using C = PfCfg<DH>;
-    constexpr int BM = C::BM, BN = C::BN, ST = C::STAGES;
+    constexpr int BM = C::BM, BN = C::BN, KST = C::KST, VST = C::VST;
     extern __shared__ unsigned char smem_raw[];
     unsigned char* smem = (unsigned char*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     uint64_t* bars = (uint64_t*)(smem + C::BAR_OFF);
     uint64_t* q_full = bars;
-    uint64_t* kv_full = bars + 1;
-    uint64_t* kv_empty = bars + 1 + ST;
-    uint64_t* s_full = bars + 1 + 2 * ST;
-    uint64_t* s_free = s_full + 2;
-    uint64_t* p_full = s_free + 2;
-    uint64_t* o_done = p_full + 1;
+    uint64_t* k_full = q_full + 1;
+    uint64_t* k_empty = k_full + KST;
+    uint64_t* v_full = k_empty + KST;
+    uint64_t* v_empty = v_full + VST;
+    uint64_t* s_full = v_empty + VST;  // [2]
+    // p_full[b] completes once per block of parity b: the softmax can never be
+    // two phases ahead of the MMA thread's wait on it.
+    uint64_t* p_full = s_full + 2;  // [2]
+    uint64_t* o_done = p_full + 2;
+    uint64_t* pair_bar = o_done + 1;  // [4], 64 arrivals each
     uint32_t* tmem_slot = (uint32_t*)(smem + C::TMEMPTR_OFF);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -128,16 +142,20 @@ __global__ void __launch_bounds__(192, 1) attn_prefill_kernel(const __grid_const
 
     if (threadIdx.x == 0) {
         dev::mbar_init(q_full, 1);
-        for (int s = 0; s < ST; ++s) {
-            dev::mbar_init(&kv_full[s], 1);
-            dev::mbar_init(&kv_empty[s], 1);
+        for (int s = 0; s < KST; ++s) {
+            dev::mbar_init(&k_full[s], 1);
+            dev::mbar_init(&k_empty[s], 1);
         }
-        for (int b = 0; b < 2; ++b) {
-            dev::mbar_init(&s_full[b], 1);
-            dev::mbar_init(&s_free[b], 128);
+        for (int s = 0; s < VST; ++s) {
+            dev::mbar_init(&v_full[s], 1);
+            dev::mbar_init(&v_empty[s], 1);
         }
-        dev::mbar_init(p_full, 128);
+        dev::mbar_init(&s_full[0], 1);
+        dev::mbar_init(&s_full[1], 1);
+        dev::mbar_init(&p_full[0], C::SOFTMAX_THREADS);
+        dev::mbar_init(&p_full[1], C::SOFTMAX_THREADS);
         dev::mbar_init(o_done, 1);
+        for (int q = 0; q < 4; ++q) dev::mbar_init(&pair_bar[q], 64);
         dev::fence_mbar_init();
     }
     if (warp == 1) {
@@ -149,57 +167,74 @@ __global__ void __launch_bounds__(192, 1) attn_prefill_kernel(const __grid_const
     tc::fence_after_sync();
     const uint32_t tmem = *tmem_slot;
 
+    auto kv_row = [&](int i) -> int32_t {
+        const int64_t u0 = (j_begin + i) * BN;
+        return (int32_t)(hk * a.slots + u0 % a.slots);
+    };
+
     if (warp == 0) {
         if (lane == 0) {
-            // ------------------------------------------------ TMA producer
+            // ------------------------------------------------ Q and K producer
             dev::prefetch_tensormap(&a.tm_q);
             dev::prefetch_tensormap(&a.tm_k);
-            dev::prefetch_tensormap(&a.tm_v);
             dev::mbar_arrive_expect_tx(q_full, C::Q_BYTES);
 #pragma unroll
             for (int c = 0; c < DH / 64; ++c)
                 tma_load_3d(smem + C::Q_OFF + c * BM * 128, &a.tm_q, c * 64, h, (int32_t)t0, q_full);
             for (int i = 0; i < nblk; ++i) {
-                const int s = i % ST;
-                if (i >= ST && !dev::mbar_wait(&kv_empty[s], ((i / ST) - 1) & 1, a.err)) break;
-                const int64_t u0 = (j_begin + i) * BN;
-                const int32_t row = (int32_t)(hk * a.slots + u0 % a.slots);
-                dev::mbar_arrive_expect_tx(&kv_full[s], C::K_BYTES + C::V_BYTES);
+                const int s = i % KST;
+                if (i >= KST && !dev::mbar_wait(&k_empty[s], ((i / KST) - 1) & 1, a.err)) break;
+                dev::mbar_arrive_expect_tx(&k_full[s], C::K_BYTES);
+                const int32_t row = kv_row(i);
 #pragma unroll
-                for (int c = 0; c < DH / 64; ++c) {
-                    dev::tma_load_2d(smem + C::K_OFF + s * C::K_BYTES + c * BN * 128, &a.tm_k, c * 64, row, &kv_full[s]);
-                    dev::tma_load_2d(smem + C::V_OFF + s * C::V_BYTES + c * BN * 128, &a.tm_v, c * 64, row, &kv_full[s]);
-                }
+                for (int c = 0; c < DH / 64; ++c)
+                    dev::tma_load_2d(smem + C::K_OFF + s * C::K_BYTES + c * BN * 128, &a.tm_k, c * 64, row, &k_full[s]);
+            }
+        }
+    } else if (warp == 2) {
+        if (lane == 0) {
+            // ------------------------------------------------ V producer
+            dev::prefetch_tensormap(&a.tm_v);
+            for (int i = 0; i < nblk; ++i) {
+                const int s = i % VST;
+                if (i >= VST && !dev::mbar_wait(&v_empty[s], ((i / VST) - 1) & 1, a.err)) break;
+                dev::mbar_arrive_expect_tx(&v_full[s], C::V_BYTES);
+                const int32_t row = kv_row(i);
+#pragma unroll
+                for (int c = 0; c < DH / 64; ++c)
+                    dev::tma_load_2d(smem + C::V_OFF + s * C::V_BYTES + c * BN * 128, &a.tm_v, c * 64, row, &v_full[s]);
             }
         }
     } else if (warp == 1) {
         if (lane == 0) {
             // ------------------------------------------------ MMA issuer
             constexpr uint32_t idesc_s = tc::idesc_f16(128, BN, BF16 ? 1 : 0, 0, 0);
-            // P.V always runs fp16 x fp16: V of a 16-bit cache is stored fp16.
+            // P.V runs fp16 x fp16 (V of a 16-bit cache is stored fp16), A = P from TMEM.
             constexpr uint32_t idesc_o = tc::idesc_f16(128, DH, 0, 0, 1);
             const uint32_t sbase = dev::smem_u32(smem);
             bool ok = dev::mbar_wait(q_full, 0, a.err);
             auto issue_pv = [&](int i) -> bool {
-                if (!dev::mbar_wait(p_full, i & 1, a.err)) return false;
+                const int s = i % VST;
+                if (!dev::mbar_wait(&p_full[i & 1], (i >> 1) & 1, a.err)) return false;
+                if (!dev::mbar_wait(&v_full[s], (i / VST) & 1, a.err)) return false;
                 tc::fence_after_sync();
-                const int s = i % ST;
+                const uint32_t p_tmem = tmem + (i & 1) * BN;  // P_i overwrote S_i, 2 values per column
 #pragma unroll
                 for (int k = 0; k < BN / 16; ++k) {
-                    const uint64_t ad = tc::smem_desc_sw128(sbase + C::P_OFF + (k / 4) * BM * 128 + (k % 4) * 32, 16, 1024);
                     const uint64_t bd =
                         tc::smem_desc_sw128(sbase + C::V_OFF + s * C::V_BYTES + k * 2048, BN * 128, 1024);
-                    tc::mma_f16_ss(tmem + C::O_COL, ad, bd, idesc_o, (i > 0 || k > 0) ? 1u : 0u);
+                    tc::mma_f16_ts(tmem + C::O_COL, p_tmem + k * 8, bd, idesc_o, (i > 0 || k > 0) ? 1u : 0u);
                 }
                 tc::commit(o_done);
-                tc::commit(&kv_empty[s]);
+                tc::commit(&v_empty[s]);
                 return true;
             };
             for (int i = 0; ok && i < nblk; ++i) {
-                const int s = i % ST, sb = i & 1;
-                if (!dev::mbar_wait(&kv_full[s], (i / ST) & 1, a.err)) break;
-                if (i >= 2 && !dev::mbar_wait(&s_free[sb], ((i - 2) >> 1) & 1, a.err)) break;
+                const int s = i % KST, sb = i & 1;
+                if (!dev::mbar_wait(&k_full[s], (i / KST) & 1, a.err)) break;
                 tc::fence_after_sync();
+                // S_i overwrites buffer sb, which held P_{i-2}; P_{i-2}.V was issued
+                // earlier and the tensor pipe executes in order.
 #pragma unroll
                 for (int k = 0; k < DH / 16; ++k) {
                     const uint64_t ad = tc::smem_desc_sw128(sbase + C::Q_OFF + (k / 4) * BM * 128 + (k % 4) * 32, 16, 1024);
@@ -208,6 +243,7 @@ __global__ void __launch_bounds__(192, 1) attn_prefill_kernel(const __grid_const
                     tc::mma_f16_ss(tmem + sb * BN, ad, bd, idesc_s, k > 0 ? 1u : 0u);
                 }
                 tc::commit(&s_full[sb]);
+                tc::commit(&k_empty[s]);
                 if (i >= 1 && !issue_pv(i - 1)) {
                     ok = false;
                     break;
@@ -217,47 +253,67 @@ __global__ void __launch_bounds__(192, 1) attn_prefill_kernel(const __grid_const
         }
     } else {
         // ---------------------------------------------------- softmax warps
-        const int quad = warp & 3;  // TMEM lane quadrant this warp may access
+        const int quad = warp & 3;          // TMEM lane quadrant this warp may access
+        const int half = (warp - 3) >> 2;   // which half of each S / O row
         const int row = quad * 32 + lane;
         const uint32_t t_lane = tmem + ((uint32_t)(quad * 32) << 16);
         const int64_t qpos = a.first_query + t0 + row;
         const bool row_valid = t0 + row < a.rows;
         const int64_t lo = vis_lo(a, qpos), hi = vis_hi(a, qpos);
-        unsigned char* pbuf = smem + C::P_OFF;
+        float* red = (float*)(smem + C::RED_OFF);  // [parity][half][row]
+        const int col0 = half * C::HALF_N;
         float m_run = -INFINITY, l_run = 0.f;
         bool ok = true;
+        // The two warps of one quadrant exchange through red[] and meet on
+        // their pair mbarrier (completion k = exchange k; bounded wait).
+        int pair_phase = 0;
+        // The fences order this warp's TMEM reads before the partner's TMEM
+        // writes (P of one half lands on S columns of the other half).
+        auto pair_sync = [&]() -> bool {
+            tc::fence_before_sync();
+            dev::mbar_arrive(&pair_bar[quad]);
+            const bool done = __all_sync(0xffffffffu, dev::mbar_wait(&pair_bar[quad], pair_phase & 1, a.err));
+            tc::fence_after_sync();
+            ++pair_phase;
+            return done;
+        };
 
         for (int i = 0; i < nblk; ++i) {
             const int sb = i & 1;
             // Waits are voted warp-wide so the .sync.aligned TMEM accesses
-            // below always see a converged warp.
+            // below always see a converged warp.  S_i complete also means
+            // P_{i-2}.V is complete (issued before it, in order).
             if (!__all_sync(0xffffffffu, dev::mbar_wait(&s_full[sb], (i >> 1) & 1, a.err))) {
                 ok = false;
                 break;
             }
             tc::fence_after_sync();
-            float x[BN];
+            float x[C::HALF_N];
 #pragma unroll
-            for (int c = 0; c < BN / 32; ++c) {
+            for (int c = 0; c < C::HALF_N / 32; ++c) {
                 uint32_t r[32];
-                tc::ld_32x32b_x32(t_lane + sb * BN + c * 32, r);
+                tc::ld_32x32b_x32(t_lane + sb * BN + col0 + c * 32, r);
 #pragma unroll
                 for (int e = 0; e < 32; ++e) x[c * 32 + e] = __uint_as_float(r[e]) * a.scale_log2;
             }
-            tc::fence_before_sync();
-            dev::mbar_arrive(&s_free[sb]);
 
-            const int64_t p0 = a.base + (j_begin + i) * BN;
-            if (!(p0 >= full_lo && p0 + BN - 1 <= full_hi)) {
+            const int64_t p0 = a.base + (j_begin + i) * BN + col0;
+            if (!(p0 - col0 >= full_lo && p0 - col0 + BN - 1 <= full_hi)) {
 #pragma unroll
-                for (int e = 0; e < BN; ++e) {
+                for (int e = 0; e < C::HALF_N; ++e) {
                     const int64_t pos = p0 + e;
                     if (pos < lo || pos > hi) x[e] = -INFINITY;
                 }
             }
             float mb = x[0];
 #pragma unroll
-            for (int e = 1; e < BN; ++e) mb = fmaxf(mb, x[e]);
+            for (int e = 1; e < C::HALF_N; ++e) mb = fmaxf(mb, x[e]);
+            red[(sb * 2 + half) * BM + row] = mb;
+            if (!pair_sync()) {
+                ok = false;
+                break;
+            }
+            mb = fmaxf(mb, red[(sb * 2 + (half ^ 1)) * BM + row]);
             const float m_new = fmaxf(m_run, mb);
             const bool rescale = m_new > m_run + 8.0f;  // also true for the first finite block
             float alpha = 1.f;
@@ -267,54 +323,59 @@ __global__ void __launch_bounds__(192, 1) attn_prefill_kernel(const __grid_const
             }
             const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
             float sum = 0.f;
+            uint32_t pk[C::HALF_N / 2];
 #pragma unroll
-            for (int e = 0; e < BN; ++e) {
-                x[e] = ex2(x[e] - m_use);
-                sum += x[e];
+            for (int e = 0; e < C::HALF_N; e += 2) {
+                const float p0v = ex2(x[e] - m_use), p1v = ex2(x[e + 1] - m_use);
+                sum += p0v + p1v;
+                pk[e / 2] = pack2(p0v, p1v, false);
             }
             l_run = l_run * alpha + sum;
 
-            // P_{i-1} . V_{i-1} must be finished before P is overwritten or O rescaled.
-            if (i >= 1 && !__all_sync(0xffffffffu, dev::mbar_wait(o_done, (i - 1) & 1, a.err))) {
-                ok = false;
-                break;
-            }
+            // O is rescaled only after P_{i-1}.V has landed in it.
             if (i >= 1 && __any_sync(0xffffffffu, rescale)) {
+                if (!__all_sync(0xffffffffu, dev::mbar_wait(o_done, (i - 1) & 1, a.err))) {
+                    ok = false;
+                    break;
+                }
                 tc::fence_after_sync();
 #pragma unroll 1
-                for (int c = 0; c < DH / 32; ++c) {
+                for (int c = 0; c < C::HALF_D / 32; ++c) {
                     uint32_t r[32];
-                    tc::ld_32x32b_x32(t_lane + C::O_COL + c * 32, r);
+                    const uint32_t col = C::O_COL + half * C::HALF_D + c * 32;
+                    tc::ld_32x32b_x32(t_lane + col, r);
 #pragma unroll
                     for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * alpha);
-                    tc::st_32x32b_x32(t_lane + C::O_COL + c * 32, r);
+                    tc::st_32x32b_x32(t_lane + col, r);
                 }
-                tc::wait_st();
             }
-            // P row -> shared memory, K-major with the 128-byte swizzle.
-#pragma unroll
-            for (int c8 = 0; c8 < BN / 8; ++c8) {
-                const int kb = c8 >> 3, cc = c8 & 7;
-                uint4 v;
-                v.x = pack2(x[c8 * 8 + 0], x[c8 * 8 + 1], false);
-                v.y = pack2(x[c8 * 8 + 2], x[c8 * 8 + 3], false);
-                v.z = pack2(x[c8 * 8 + 4], x[c8 * 8 + 5], false);
-                v.w = pack2(x[c8 * 8 + 6], x[c8 * 8 + 7], false);
-                *(uint4*)(pbuf + kb * BM * 128 + row * 128 + ((cc ^ (row & 7)) << 4)) = v;
+            // P_i (fp16 pairs) over the first half of S_i's columns: this half
+            // row's keys [col0, col0 + HALF_N) -> columns [col0/2, col0/2 + HALF_N/2).
+            const uint32_t pcol = t_lane + sb * BN + col0 / 2;
+            if constexpr (C::HALF_N / 2 == 32) {
+                tc::st_32x32b_x32(pcol, *reinterpret_cast<const uint32_t(*)[32]>(pk));
+            } else {
+                tc::st_32x32b_x16(pcol, pk);
             }
-            dev::fence_proxy_async_smem();
+            tc::wait_st();
             tc::fence_before_sync();
-            dev::mbar_arrive(p_full);
+            dev::mbar_arrive(&p_full[sb]);
         }
 
+        // Row sum = both halves' partial sums.  The slot of parity nblk & 1 was
+        // last read for block nblk - 2, which both warps are past.
+        const int ls = nblk & 1;
+        red[(ls * 2 + half) * BM + row] = l_run;
+        if (ok) ok = pair_sync();
+        const float l_row = l_run + red[(ls * 2 + (half ^ 1)) * BM + row];
         if (ok && nblk > 0 && __all_sync(0xffffffffu, dev::mbar_wait(o_done, (nblk - 1) & 1, a.err))) {
             tc::fence_after_sync();
-            const float inv = 1.f / l_run;
-            const int64_t obase = ((t0 + row) * (int64_t)a.hq + h) * DH;
+            const float inv = 1.f / l_row;
+            const int64_t obase = ((t0 + row) * (int64_t)a.hq + h) * DH + half * C::HALF_D;
 #pragma unroll 1
-            for (int c = 0; c < DH / 32; ++c) {
+            for (int c = 0; c < C::HALF_D / 32; ++c) {
                 uint32_t r[32];
-                tc::ld_32x32b_x32(t_lane + C::O_COL + c * 32, r);
+                tc::ld_32x32b_x32(t_lane + C::O_COL + half * C::HALF_D + c * 32, r);
                 if (row_valid) {
                     if (a.out_dtype == NMG_F32) {
                         float4* dst = (float4*)((float*)a.out + obase + c * 32);
@@ -327,7 +388,6 @@ __global__ void __launch_bounds__(192, 1) attn_prefill_kernel(const __grid_const
                         const bool obf = a.out_dtype == NMG_BF16;
 #pragma unroll
                         for (int e = 0; e < 4; ++e) {
-                            uint4 v;
                             uint32_t w[4];
 #pragma unroll
                             for (int t = 0; t < 4; ++t) {
@@ -337,11 +397,7 @@ __global__ void __launch_bounds__(192, 1) attn_prefill_kernel(const __grid_const
                                 const uint32_t b1 = obf ? dev::f32_to_bf16_bits(f1) : dev::f32_to_f16_bits(f1);
                                 w[t] = b0 | (b1 << 16);
                             }
-                            v.x = w[0];
-                            v.y = w[1];
-                            v.z = w[2];
-                            v.w = w[3];
-                            dst[e] = v;
+                            dst[e] = make_uint4(w[0], w[1], w[2], w[3]);
                         }
                     }
                 }
@@ -386,7 +442,7 @@ int launch_prefill(const PrefillArgs& a, dim3 grid, cudaStream_t s) {
         NMG_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
         attr_set |= 1u << (dev_id & 31);
     }
-    kern<<<grid, 192, C::SMEM, s>>>(a);
+    kern<<<grid, C::THREADS, C::SMEM, s>>>(a);
     NMG_CUDA_TRY(cudaGetLastError());
     return NMG_OK;
 }
