@@ -86,6 +86,7 @@ _i64p = ctypes.POINTER(ctypes.c_int64)
 
 # name -> (argtypes)
 SIGNATURES = {
+    "nmg_device_status": [_i32, _vp],
     "nmg_kv_create": [_i32, _i32, _i32, _i64, _i64, _i32, ctypes.POINTER(_vp)],
     "nmg_kv_destroy": [_vp],
     "nmg_kv_append": [_vp, _i64, _vp, _vp, _i64, _i32, _vp],

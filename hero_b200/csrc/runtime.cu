@@ -103,3 +103,12 @@ int check_device_flag(int device, cudaStream_t stream) {
 
 extern "C" const char* nmg_last_error(void) { return nmg::g_last_error; }
 extern "C" const char* nmg_version(void) { return "nmg 0.1 sm_100a"; }
+
+extern "C" int nmg_device_status(int device, void* stream) {
+    int prev = 0;
+    NMG_CUDA_TRY(cudaGetDevice(&prev));
+    if (prev != device) NMG_CUDA_TRY(cudaSetDevice(device));
+    const int st = nmg::check_device_flag(device, (cudaStream_t)stream);
+    if (prev != device) cudaSetDevice(prev);
+    return st;
+}

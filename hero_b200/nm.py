@@ -53,6 +53,11 @@ def _dev(t: torch.Tensor) -> torch.Tensor:
     return t.contiguous()
 
 
+def device_status(device: int = 0) -> None:
+    """Synchronise and raise DeviceTimeout if a kernel gave up a bounded device-side wait."""
+    call("nmg_device_status", int(device), _stream(device))
+
+
 @dataclass(frozen=True)
 class VisibleRows:
     """Half-open chronological row interval (src/attention.hpp:144-150)."""

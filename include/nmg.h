@@ -63,6 +63,13 @@ extern "C" {
 NMG_API const char* nmg_last_error(void);
 NMG_API const char* nmg_version(void);
 
+/* Synchronises the current stream of `device` work issued through this
+ * library (the legacy default stream is used when stream is NULL) and reports
+ * NMG_DEVICE_TIMEOUT if any kernel since the last call gave up a bounded
+ * device-side wait (a kernel that gives up returns early instead of hanging).
+ * Clears the flag. */
+NMG_API int nmg_device_status(int device, void* stream);
+
 /* ---- device KV cache -------------------------------------------------------
  *
  * Replaces FullAttentionCache<Hkv,HeadDim> (src/attention.hpp:201-250) when
