@@ -1,0 +1,186 @@
+// nmg.hpp -- C++ face of the nmg C ABI with the nm engine's own names.
+//
+// Header-only.  A maintainer of the nm engine swaps
+//   FullAttentionCache<Hkv, HeadDim>       (nm/src/attention.hpp:201-250)
+//   LocalAttentionCache<Hkv, HeadDim>      (nm/src/attention.hpp:252-395)
+//   the per-layer softmax reduction         (nm/src/qwen35.hpp:360-382, nm/src/gemma4.hpp:211-235, ...)
+//   DeltaNetState<Heads, Dk, Dv>, gated_delta_step (nm/src/recurrent.hpp:117-177)
+// for the types below, which keep the method names and throw the same
+// exception types; storage and arithmetic live on the GPU behind include/nmg.h.
+// Rows are device pointers in the reference's token-major layout
+// [rows][heads * head_dim]; every call takes the CUDA stream it runs on.
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <stdexcept>
+#include <string>
+#include <utility>
+
+#include "nmg.h"
+
+namespace nmg {
+
+enum class Dtype : int { f32 = NMG_F32, f16 = NMG_F16, bf16 = NMG_BF16 };
+
+// Status -> the exception type the reference throws in the same situation.
+inline void check(int status) {
+    if (status == NMG_OK) return;
+    const std::string msg = nmg_last_error();
+    switch (status) {
+        case NMG_INVALID_ARGUMENT: throw std::invalid_argument(msg);
+        case NMG_OUT_OF_RANGE: throw std::out_of_range(msg);
+        case NMG_LENGTH_ERROR: throw std::length_error(msg);
+        case NMG_LOGIC_ERROR: throw std::logic_error(msg);
+        default: throw std::runtime_error(msg);  // no visible key, CUDA, NCCL, device timeout
+    }
+}
+
+struct VisibleRows {  // attention.hpp:144-150
+    size_t first;
+    size_t end;
+    bool empty() const { return first == end; }
+    size_t count() const { return end - first; }
+};
+
+namespace detail {
+
+class Cache {
+public:
+    Cache(const Cache&) = delete;
+    Cache& operator=(const Cache&) = delete;
+    Cache(Cache&& o) noexcept : h_(std::exchange(o.h_, nullptr)) {}
+    ~Cache() { nmg_kv_destroy(h_); }
+
+    size_t size() const {
+        int64_t v = 0;
+        check(nmg_kv_size(h_, &v));
+        return size_t(v);
+    }
+    size_t position(size_t chronological_row) const {
+        int64_t p = 0;
+        check(nmg_kv_position(h_, int64_t(chronological_row), &p));
+        return size_t(p);
+    }
+    bool can_append_without_eviction(size_t rows) const {
+        int yes = 0;
+        check(nmg_kv_can_append_without_eviction(h_, int64_t(rows), &yes));
+        return yes != 0;
+    }
+    // append() for one row or a batch of consecutive rows.
+    void append(size_t position, const void* keys, const void* values, size_t rows, Dtype src, void* stream) {
+        check(nmg_kv_append(h_, int64_t(position), keys, values, int64_t(rows), int(src), stream));
+    }
+    VisibleRows visible_rows(size_t query) const {
+        int64_t f = 0, e = 0;
+        check(nmg_kv_visible_rows(h_, int64_t(query), &f, &e));
+        return VisibleRows{size_t(f), size_t(e)};
+    }
+    // key()/value() as a synchronous copy-back (debug only).
+    void read_row(size_t chronological_row, size_t kv_head, float* key, float* value, void* stream) const {
+        check(nmg_kv_read_row(h_, int64_t(chronological_row), int(kv_head), key, value, stream));
+    }
+    void reset() { check(nmg_kv_reset(h_)); }
+    nmg_kv_cache* handle() const { return h_; }
+
+protected:
+    Cache(int hkv, int head_dim, Dtype dtype, size_t window, size_t capacity, int device) {
+        check(nmg_kv_create(hkv, head_dim, int(dtype), int64_t(window), int64_t(capacity), device, &h_));
+    }
+    nmg_kv_cache* h_ = nullptr;
+};
+
+}  // namespace detail
+
+template <size_t Hkv, size_t HeadDim>
+class FullAttentionCache : public detail::Cache {
+public:
+    static constexpr size_t kv_heads = Hkv, head_dim = HeadDim;
+    explicit FullAttentionCache(size_t capacity, Dtype dtype = Dtype::f32, int device = 0)
+        : Cache(int(Hkv), int(HeadDim), dtype, 0, capacity, device) {}
+};
+
+template <size_t Hkv, size_t HeadDim>
+class LocalAttentionCache : public detail::Cache {
+public:
+    static constexpr size_t kv_heads = Hkv, head_dim = HeadDim;
+    // `capacity` physical rows >= window; one batch of up to
+    // capacity - window + 1 rows is attended as a whole.
+    LocalAttentionCache(size_t window, size_t capacity, Dtype dtype = Dtype::f32, int device = 0)
+        : Cache(int(Hkv), int(HeadDim), dtype, window, capacity, device) {}
+    size_t window() const {
+        int64_t w = 0;
+        check(nmg_kv_window(h_, &w));
+        return size_t(w);
+    }
+    void begin_batch_retention(size_t appended_rows) { check(nmg_kv_begin_batch_retention(h_, int64_t(appended_rows))); }
+    void end_batch_retention() { check(nmg_kv_end_batch_retention(h_)); }
+};
+
+// The layer reduction over `rows` queries at positions at.. (qwen35.hpp:360-382
+// with a score scale; pass no scale for the Gemma form, gemma4.hpp:211-235).
+template <size_t Hq, class Cache>
+void attend(const Cache& cache, const void* queries, Dtype q_dtype, size_t rows, size_t at, void* out, Dtype out_dtype,
+            void* stream) {
+    static_assert(Hq % Cache::kv_heads == 0, "query heads must be a whole number of GQA groups");
+    check(nmg_attend(cache.handle(), int(Hq), queries, int(q_dtype), int64_t(rows), int64_t(at), 1.f, 0, out,
+                     int(out_dtype), stream));
+}
+template <size_t Hq, class Cache>
+void attend(const Cache& cache, const void* queries, Dtype q_dtype, size_t rows, size_t at, float score_scale,
+            void* out, Dtype out_dtype, void* stream) {
+    static_assert(Hq % Cache::kv_heads == 0, "query heads must be a whole number of GQA groups");
+    check(nmg_attend(cache.handle(), int(Hq), queries, int(q_dtype), int64_t(rows), int64_t(at), score_scale, 1, out,
+                     int(out_dtype), stream));
+}
+
+// A layer's append-then-reduce, including the local ring's token-by-token
+// windows when the batch would evict (gemma4.hpp:237-253, :617-630).
+template <size_t Hq, class Cache>
+void append_attend(Cache& cache, size_t position, const void* keys, const void* values, Dtype kv_dtype,
+                   const void* queries, Dtype q_dtype, size_t rows, const float* score_scale, void* out,
+                   Dtype out_dtype, void* stream) {
+    check(nmg_append_attend(cache.handle(), int64_t(position), keys, values, int(kv_dtype), int(Hq), queries,
+                            int(q_dtype), int64_t(rows), score_scale ? *score_scale : 1.f, score_scale ? 1 : 0, out,
+                            int(out_dtype), stream));
+}
+
+template <size_t Heads, size_t Dk, size_t Dv>
+class DeltaNetState {  // recurrent.hpp:117-138, fp32 [head][Dk][Dv] on the device
+public:
+    static constexpr size_t floats_per_head = Dk * Dv;
+    static constexpr size_t floats = Heads * floats_per_head;
+    explicit DeltaNetState(int device = 0) { check(nmg_delta_create(int(Heads), int(Dk), int(Dv), device, &h_)); }
+    DeltaNetState(const DeltaNetState&) = delete;
+    DeltaNetState& operator=(const DeltaNetState&) = delete;
+    ~DeltaNetState() { nmg_delta_destroy(h_); }
+    void clear(void* stream) { check(nmg_delta_clear(h_, stream)); }
+    float* head(size_t h) {  // device pointer; out_of_range like recurrent.hpp:128
+        float* p = nullptr;
+        check(nmg_delta_head(h_, int(h), &p));
+        return p;
+    }
+    // One token through every value head; value head h reads key head h % Hk.
+    void step(size_t hk, const float* q, const float* k, const float* v, const float* gate, const float* beta,
+              float* out, void* stream) {
+        check(nmg_delta_step(h_, int(hk), q, k, v, gate, beta, out, stream));
+    }
+    void prefill(size_t hk, size_t tokens, const float* q, const float* k, const float* v, const float* gate,
+                 const float* beta, float* out, int chunk, void* stream) {
+        check(nmg_delta_prefill(h_, int(hk), int64_t(tokens), q, k, v, gate, beta, out, chunk, stream));
+    }
+    nmg_delta_state* handle() const { return h_; }
+
+private:
+    nmg_delta_state* h_ = nullptr;
+};
+
+// gated_delta_step<Dk, Dv> (recurrent.hpp:146-177) on one device head block;
+// gate and beta are device scalars.
+template <size_t Dk, size_t Dv>
+void gated_delta_step(float* state, const float* q, const float* k, const float* v, const float* gate,
+                      const float* beta, float* out, void* stream) {
+    check(nmg_gated_delta_step(state, int(Dk), int(Dv), q, k, v, gate, beta, out, stream));
+}
+
+}  // namespace nmg
