@@ -102,6 +102,7 @@ SIGNATURES = {
     "nmg_kv_reset": [_vp],
     "nmg_attend": [_vp, _i32, _vp, _i32, _i64, _i64, _f32, _i32, _vp, _i32, _vp],
     "nmg_append_attend": [_vp, _i64, _vp, _vp, _i32, _i32, _vp, _i32, _i64, _f32, _i32, _vp, _i32, _vp],
+    "nmg_attend_noalloc": [_vp, _i32, _vp, _i32, _i64, _i64, _f32, _i32, _vp, _i32, _vp],
     "nmg_attend_batch": [ctypes.POINTER(_vp), _i32, _i64p, _i32, _vp, _i32, _f32, _i32, _vp, _i32, _vp],
     "nmg_sdpa": [_i32, _i32, _vp, _vp, _vp, _i32, _i64, _i64, _f32, _vp, _i32, _vp],
     "nmg_delta_create": [_i32, _i32, _i32, _i32, ctypes.POINTER(_vp)],

@@ -18,6 +18,7 @@
 // sum of alpha_j * v_j, with GQA group head / (Hq / Hkv).
 #include <algorithm>
 #include <math.h>
+#include <mutex>
 #include <stdio.h>
 #include <vector>
 
@@ -579,3 +580,132 @@ int attend_batch_split(const nmg_kv_cache* const* caches, int batch, const int64
 }
 
 }  // namespace nmg
+
+// ------------------------------------------------ no-allocation decode entry
+//
+// Some callers cannot call cudaMalloc at all: an engine whose device memory
+// is carved out by its own arena allocator and may not be grown behind its
+// back, or a serving loop that must never hit the device-wide synchronisation
+// cudaMalloc/cudaFree can cause.  nmg_attend_noalloc serves them: the same
+// split-KV attention as nmg_attend's decode path, but its scratch (row
+// tickets and per-split partial results) lives in the fixed array below, so
+// no call allocates device memory.  The caller still owns q and out.
+//
+// The array is shared by every call in the process on a given device and keeps
+// what the last call left; calls whose kernels overlap on that device (two
+// streams, two host threads) race on it and must be serialised by the caller.
+namespace nmg {
+namespace {
+
+constexpr size_t kNoallocScratchBytes = size_t(4) << 20;  // 4 MiB per device, held until exit
+constexpr size_t kNoallocFlagBytes = 256;                   // device-side wait flag, then the counters
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoallocScratchBytes];
+
+std::mutex g_noalloc_mu;
+void* g_noalloc_addr[64] = {};  // device address of g_noalloc_scratch, per device
+
+// Host code may not use the array's name as a device address; look it up once
+// per device with that device current.
+int noalloc_scratch(int device, void** ptr) {
+    if (device < 0 || device >= 64) return set_error(NMG_INVALID_ARGUMENT, "nmg_attend_noalloc: device %d", device);
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (!g_noalloc_addr[device]) {
+        void* p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess || !p)
+            return set_error(NMG_CUDA_ERROR, "nmg_attend_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+        g_noalloc_addr[device] = p;
+    }
+    *ptr = g_noalloc_addr[device];
+    return NMG_OK;
+}
+
+}  // namespace
+}  // namespace nmg
+
+extern "C" int nmg_attend_noalloc(const nmg_kv_cache* c, int hq, const void* q, int q_dtype, int64_t rows,
+                                  int64_t first_query, float scale, int use_scale, void* out, int out_dtype,
+                                  void* stream) {
+    using namespace nmg;
+    if (!c) return set_error(NMG_INVALID_ARGUMENT, "nmg_attend_noalloc: null cache");
+    if (hq <= 0 || hq % c->hkv != 0)
+        return set_error(NMG_INVALID_ARGUMENT, "attention: %d query heads is not a multiple of %d K/V heads", hq, c->hkv);
+    if (!dtype_valid(q_dtype) || !dtype_valid(out_dtype)) return set_error(NMG_INVALID_ARGUMENT, "attention: bad dtype");
+    if (rows < 0) return set_error(NMG_INVALID_ARGUMENT, "nmg_attend_noalloc: negative row count");
+    if (rows == 0) return NMG_OK;
+    if (!q || !out) return set_error(NMG_INVALID_ARGUMENT, "nmg_attend_noalloc: null tensor");
+    if (c->size == 0 && c->total == 0)
+        return set_error(NMG_RUNTIME_ERROR, "%s: query has no visible keys", c->window ? "LocalAttentionCache" : "FullAttentionCache");
+    const int64_t newest = c->newest();
+    for (int64_t t : {(int64_t)0, rows - 1}) {
+        const VisibleSpan sp = visible_span(first_query + t, c->window, c->oldest, newest);
+        if (sp.lo > sp.hi)
+            return set_error(NMG_RUNTIME_ERROR, "%s: query has no visible keys",
+                             c->window ? "LocalAttentionCache" : "FullAttentionCache");
+    }
+    int prev = 0;
+    NMG_CUDA_TRY(cudaGetDevice(&prev));
+    if (prev != c->device) NMG_CUDA_TRY(cudaSetDevice(c->device));
+    void* base = nullptr;
+    int st = noalloc_scratch(c->device, &base);
+    if (st == NMG_OK) {
+        // Same work split as nmg_attend's decode path.
+        const int gtot = hq / c->hkv, gt = pick_gt(gtot), zdim = gtot / gt;
+        int64_t longest = 0, total_keys = 0;
+        for (int64_t t = 0; t < rows; ++t) {
+            const VisibleSpan sp = visible_span(first_query + t, c->window, c->oldest, newest);
+            longest = std::max(longest, sp.hi - sp.lo + 1);
+            total_keys += sp.hi - sp.lo + 1;
+        }
+        const int64_t split_len = pick_split_len(total_keys * c->hkv * zdim, warps_runtime(c->dtype, c->dh));
+        const int64_t max_splits = (longest + split_len - 1) / split_len;
+        const int64_t work = rows * max_splits;
+        const int64_t cnt_bytes = rows * c->hkv * zdim * 4;
+        const size_t need = kNoallocFlagBytes + (size_t)(cnt_bytes + 255) / 256 * 256 +
+                            (size_t)work * c->hkv * zdim * gt * (c->dh + 2) * 4;
+        if (need > kNoallocScratchBytes || work > (int64_t)0x7FFFFFFF) {
+            st = set_error(NMG_LENGTH_ERROR,
+                           "nmg_attend_noalloc: this call needs %zu bytes of scratch, more than the fixed %zu; "
+                           "use nmg_attend or fewer query rows",
+                           need, kNoallocScratchBytes);
+        } else {
+            SplitArgs a;  // on the stack: nothing is allocated
+            a.mode = 0;
+            a.hkv = c->hkv;
+            a.hq = hq;
+            a.gtot = gtot;
+            a.zdim = zdim;
+            a.split_len = split_len;
+            a.k = c->k;
+            a.v = c->v;
+            a.slots = c->slots;
+            a.base = c->base;
+            a.rows = rows;
+            a.first_query = first_query;
+            a.window = c->window;
+            a.floor_pos = c->oldest;
+            a.newest = newest;
+            a.max_splits = (int32_t)max_splits;
+            a.nseq = 0;
+            a.row_offset = 0;
+            a.q = q;
+            a.q_dtype = q_dtype;
+            a.out = out;
+            a.out_dtype = out_dtype;
+            a.scale = use_scale ? scale : 1.f;
+            a.err = (int*)base;
+            a.counters = (int*)((char*)base + kNoallocFlagBytes);
+            a.part = (float*)((char*)base + kNoallocFlagBytes + (cnt_bytes + 255) / 256 * 256);
+            // The row tickets must start at zero; a kernel that gave up a
+            // wait may have left some set, so clear them (and the flag).
+            cudaError_t e = cudaMemsetAsync(base, 0, kNoallocFlagBytes + (size_t)cnt_bytes, (cudaStream_t)stream);
+            if (e != cudaSuccess)
+                st = set_error(NMG_CUDA_ERROR, "nmg_attend_noalloc: cudaMemsetAsync: %s", cudaGetErrorString(e));
+            else
+                st = dispatch_split(c->dtype, c->dh, gt, a, dim3((unsigned)work, c->hkv, zdim), (cudaStream_t)stream);
+        }
+    }
+    if (prev != c->device) cudaSetDevice(prev);
+    return st;
+}

@@ -159,6 +159,19 @@ NMG_API int nmg_append_attend(nmg_kv_cache* cache, int64_t first_position, const
 NMG_API int nmg_attend_batch(const nmg_kv_cache* const* caches, int batch, const int64_t* queries_at, int hq, const void* q,
                      int q_dtype, float scale, int use_scale, void* out, int out_dtype, void* stream);
 
+/* nmg_attend for callers that cannot allocate device memory (no counterpart in
+ * the reference: its CPU path never allocates device memory).  Same result as
+ * nmg_attend on the split-KV decode kernel, with that kernel's scratch in a
+ * fixed 4 MiB device array per device instead of library-allocated memory;
+ * nothing is allocated on any call.  Calls needing more scratch than that
+ * fail with NMG_LENGTH_ERROR (one decode row over a long cache needs well
+ * under 1 MiB).  The first call on a device looks the array up
+ * (cudaGetSymbolAddress); make that first call before any stream capture.
+ * The array is shared by all calls on a device: calls whose kernels overlap
+ * on the GPU race on it and must be serialised by the caller. */
+NMG_API int nmg_attend_noalloc(const nmg_kv_cache* cache, int hq, const void* q, int q_dtype, int64_t rows,
+                               int64_t first_query, float scale, int use_scale, void* out, int out_dtype, void* stream);
+
 /* Dense, unmasked attention scaled_dot_product_attention<Heads,Dqk,Dv>
  * (src/attention.hpp:124-139) over plain device tensors q [tq][heads*d],
  * k/v [tk][heads*d] (no cache, no mask; heads == kv heads). */
