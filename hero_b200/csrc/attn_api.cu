@@ -37,6 +37,9 @@ int dispatch_rows(const nmg_kv_cache* c, int hq, const void* q, int q_dtype, int
     if (nmg::prefill_supported(c, hq, q_dtype, rows))
         st = nmg::attend_rows_prefill(c, hq, q, q_dtype, rows, first_query, window, floor_pos, newest, scale, out,
                                       out_dtype, stream);
+    else if (nmg::decode_mma_supported(c, q_dtype))
+        st = nmg::attend_rows_mma(c, hq, q, rows, first_query, window, floor_pos, newest, scale, out, out_dtype,
+                                  stream);
     else
         st = nmg::attend_rows_split(c, hq, q, q_dtype, rows, first_query, window, floor_pos, newest, scale, out,
                                     out_dtype, stream, nullptr, 0);
@@ -124,8 +127,14 @@ extern "C" int nmg_attend_batch(const nmg_kv_cache* const* caches, int batch, co
     int prev = 0;
     NMG_CUDA_TRY(cudaGetDevice(&prev));
     if (prev != c0->device) NMG_CUDA_TRY(cudaSetDevice(c0->device));
-    st = nmg::attend_batch_split(caches, batch, queries_at, hq, q, q_dtype, use_scale ? scale : 1.f, out, out_dtype,
-                                 (cudaStream_t)stream);
+    bool mma = true;
+    for (int b = 0; b < batch; ++b) mma = mma && nmg::decode_mma_supported(caches[b], q_dtype);
+    if (mma)
+        st = nmg::attend_batch_mma(caches, batch, queries_at, hq, q, use_scale ? scale : 1.f, out, out_dtype,
+                                   (cudaStream_t)stream);
+    else
+        st = nmg::attend_batch_split(caches, batch, queries_at, hq, q, q_dtype, use_scale ? scale : 1.f, out, out_dtype,
+                                     (cudaStream_t)stream);
     if (prev != c0->device) cudaSetDevice(prev);
     return st;
 }

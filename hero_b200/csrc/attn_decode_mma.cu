@@ -1,0 +1,561 @@
+// attn_decode_mma.cu -- split-KV decode on tensor cores for 16-bit caches (K2, K3).
+//
+// Decode reads every visible K/V row once and does ~8-16 flops per byte
+// (query heads per KV head x 2 x 2), which at HBM speed is more than the CUDA
+// cores can issue comfortably; warp-level mma.sync keeps the math off the
+// critical path so the kernel is bound by the bytes it streams.
+//
+// One CTA owns (query row, KV head, 16-head subgroup, key split).  Key tiles
+// of 64 positions (64-aligned in slot space, so a tile never straddles the
+// ring end) arrive by 2-D TMA with the 128-byte swizzle into a 2-3 stage ring.
+// Each of the 4 warps takes 16 keys of a tile:
+//   S^T-free form: S[16 heads x 16 keys] = Q[16 x D] K^T   (m16n8k16, A = Q
+//                  fragments held in registers, B = K via ldmatrix)
+//   online softmax on the accumulator fragments (rows = query heads; heads
+//                  beyond the group are zero rows), P -> fp16 A fragments
+//   O[16 x D] += P V                                        (B = V via ldmatrix.trans)
+// Warps merge through shared memory; rows with several splits merge their
+// partials in the last CTA of the row (atomic ticket), as the CUDA-core kernel.
+// The reduction is the reference's (nm/src/qwen35.hpp:360-382,
+// nm/src/gemma4.hpp:211-235 ...): [scale *] dot(q, k), softmax, sum alpha v.
+#include <algorithm>
+#include <math.h>
+#include <vector>
+
+#include "attn.cuh"
+
+namespace nmg {
+namespace {
+
+constexpr int kMmaMaxBatch = 48;  // sequences per launch (tensor maps ride in the parameter block)
+constexpr int KT = 64;            // keys per tile (4 warps x 16)
+
+struct MmaSeq {
+    int64_t base, slots, lo, hi;  // visible positions [lo, hi]
+    int32_t work_first, nsplit, qrow, map;
+};
+
+struct MmaArgs {
+    CUtensorMap tm_k[kMmaMaxBatch];  // K of each distinct cache, (d, hkv*slots)
+    CUtensorMap tm_v[kMmaMaxBatch];
+    int mode;  // 0: one cache, rows first_query..; 1: table
+    int hkv, hq, gtot, zdim;
+    int64_t blocks_per_split;
+    // mode 0
+    int64_t base, slots, rows, first_query, window, floor_pos, newest;
+    int32_t max_splits;
+    // mode 1
+    int nseq;
+    MmaSeq seq[kMmaMaxBatch];
+    // common
+    const void* q;
+    void* out;
+    int out_dtype;
+    float scale_log2;
+    float* part;
+    int* counters;
+    int* err;
+};
+
+struct MmaRow {
+    int64_t base, slots, lo, hi, work_first, nsplit, qrow, s;
+    int map;
+};
+
+__device__ __forceinline__ bool mma_row(const MmaArgs& a, int64_t w, MmaRow& r) {
+    if (a.mode == 0) {
+        const int64_t row = w / a.max_splits;
+        r.s = w % a.max_splits;
+        const int64_t q = a.first_query + row;
+        int64_t lo = a.floor_pos;
+        if (a.window > 0 && q - a.window + 1 > lo) lo = q - a.window + 1;
+        r.lo = lo;
+        r.hi = q < a.newest ? q : a.newest;
+        r.base = a.base;
+        r.slots = a.slots;
+        const int64_t nblk = (r.hi - r.base) / KT - (r.lo - r.base) / KT + 1;
+        r.nsplit = (nblk + a.blocks_per_split - 1) / a.blocks_per_split;
+        r.work_first = row * a.max_splits;
+        r.qrow = row;
+        r.map = 0;
+        return r.s < r.nsplit;
+    }
+    int b = 0;
+    while (b + 1 < a.nseq && a.seq[b + 1].work_first <= w) ++b;
+    const MmaSeq& e = a.seq[b];
+    r.base = e.base;
+    r.slots = e.slots;
+    r.lo = e.lo;
+    r.hi = e.hi;
+    r.nsplit = e.nsplit;
+    r.work_first = e.work_first;
+    r.qrow = e.qrow;
+    r.map = e.map;
+    r.s = w - e.work_first;
+    return r.s < r.nsplit;
+}
+
+template <int DH>
+struct MmaCfg {
+    static constexpr int STAGES = DH <= 128 ? 3 : 2;
+    static constexpr int TILE_BYTES = KT * DH * 2;  // one of K or V
+    static constexpr int STAGE_BYTES = 2 * TILE_BYTES;
+    static constexpr int Q_OFF = STAGES * STAGE_BYTES;          // 16 x DH, 16-bit, padded rows
+    static constexpr int Q_PITCH = DH * 2 + 16;                 // bytes per staged query row
+    // The warp merge ([4][16][DH + 2] fp32) reuses the stage memory, idle by then.
+    static constexpr int C_OFF = 0;
+    static_assert(4 * 16 * (DH + 2) * 4 <= STAGES * STAGE_BYTES, "merge buffer fits the stages");
+    static constexpr int BAR_OFF = Q_OFF + 16 * Q_PITCH;
+    static constexpr int SMEM = BAR_OFF + 64 + 1024;            // + alignment slack
+};
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
+
+template <bool BF16>
+__device__ __forceinline__ void mma_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    if constexpr (BF16) {
+        asm volatile(
+            "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+            "{%0,%1,%2,%3};"
+            : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+            : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+    } else {
+        asm volatile(
+            "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+            "{%0,%1,%2,%3};"
+            : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+            : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+    }
+}
+
+__device__ __forceinline__ float ex2f(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+__device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
+    __half2 v = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&v);
+}
+
+// Byte offset of 16-byte chunk `chunk` (8 elements of d) of tile row `key` in
+// a K or V tile stored as DH/64 swizzled boxes of [64 keys][128 B].
+template <int DH>
+__device__ __forceinline__ uint32_t tile_off(int key, int chunk) {
+    return (uint32_t)((chunk >> 3) * (KT * 128) + key * 128 + (((chunk & 7) ^ (key & 7)) << 4));
+}
+
+template <int DH, bool BF16>
+__global__ void __launch_bounds__(128) attn_decode_mma_kernel(const __grid_constant__ MmaArgs a) {
+    using C = MmaCfg<DH>;
+    constexpr int ST = C::STAGES;
+    extern __shared__ unsigned char smem_raw[];
+    unsigned char* smem = (unsigned char*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    uint64_t* full = (uint64_t*)(smem + C::BAR_OFF);
+    float* cs = (float*)(smem + C::C_OFF);
+    __shared__ int s_last;
+
+    const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+    const int h = blockIdx.y, z = blockIdx.z;
+    MmaRow r;
+    if (!mma_row(a, blockIdx.x, r)) return;
+    const int G = a.gtot - z * 16 < 16 ? a.gtot - z * 16 : 16;  // valid query heads of this subgroup
+    const int qh0 = h * a.gtot + z * 16;
+    const int64_t u_lo = r.lo - r.base, u_hi = r.hi - r.base;
+    const int64_t jb = u_lo / KT + r.s * a.blocks_per_split;
+    const int64_t je = min(u_lo / KT + (r.s + 1) * a.blocks_per_split, u_hi / KT + 1);
+    const int ntiles = (int)(je - jb);
+    const CUtensorMap* tmk = &a.tm_k[r.map];
+    const CUtensorMap* tmv = &a.tm_v[r.map];
+
+    if (tid == 0) {
+        for (int s = 0; s < ST; ++s) dev::mbar_init(&full[s], 1);
+        dev::fence_mbar_init();
+    }
+    // Stage the query heads as 16-bit rows (rows past the group are zero).
+    for (int i = tid; i < 16 * (DH / 8); i += 128) {
+        const int g = i / (DH / 8), c8 = i % (DH / 8);
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (g < G) v = *(const uint4*)((const uint16_t*)a.q + (r.qrow * (int64_t)a.hq + qh0 + g) * DH + c8 * 8);
+        *(uint4*)(smem + C::Q_OFF + g * C::Q_PITCH + c8 * 16) = v;
+    }
+    __syncthreads();
+
+    auto issue = [&](int t, int st) {
+        if (tid == 0) {
+            const int64_t u0 = (jb + t) * KT;
+            const int32_t row = (int32_t)(h * r.slots + u0 % r.slots);
+            dev::fence_proxy_async_smem();
+            dev::mbar_arrive_expect_tx(&full[st], C::STAGE_BYTES);
+#pragma unroll
+            for (int c = 0; c < DH / 64; ++c) {
+                dev::tma_load_2d(smem + st * C::STAGE_BYTES + c * KT * 128, tmk, c * 64, row, &full[st]);
+                dev::tma_load_2d(smem + st * C::STAGE_BYTES + C::TILE_BYTES + c * KT * 128, tmv, c * 64, row, &full[st]);
+            }
+        }
+    };
+
+    // A fragments of Q (m16k16 per 16 columns of d), rows g = lane/4 (+8).
+    uint32_t qa[DH / 16][4];
+    {
+        const uint32_t qbase = dev::smem_u32(smem + C::Q_OFF);
+#pragma unroll
+        for (int kk = 0; kk < DH / 16; ++kk) {
+            // matrices: (rows 0-7, k 0-7), (rows 8-15, k 0-7), (rows 0-7, k 8-15), (rows 8-15, k 8-15)
+            const int mrow = (lane & 7) + ((lane >> 3) & 1) * 8;
+            const int kc = kk * 2 + (lane >> 4);
+            ldsm_x4(qbase + mrow * C::Q_PITCH + kc * 16, qa[kk][0], qa[kk][1], qa[kk][2], qa[kk][3]);
+        }
+    }
+
+    float o[DH / 8][4];
+#pragma unroll
+    for (int n = 0; n < DH / 8; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+    float m_r[2] = {-INFINITY, -INFINITY}, l_r[2] = {0.f, 0.f};  // rows lane/4 and lane/4 + 8
+
+    bool aborted = false;
+    for (int t = 0; t < ST - 1 && t < ntiles; ++t) issue(t, t);
+    for (int t = 0; t < ntiles; ++t) {
+        const int st = t % ST;
+        if (t + ST - 1 < ntiles) issue(t + ST - 1, (t + ST - 1) % ST);
+        const bool ok = dev::mbar_wait(&full[st], (t / ST) & 1, a.err);
+        if (__syncthreads_or(!ok)) {
+            aborted = true;
+            break;
+        }
+        const uint32_t kbase = dev::smem_u32(smem + st * C::STAGE_BYTES);
+        const uint32_t vbase = kbase + C::TILE_BYTES;
+        const int key0 = wid * 16;  // this warp's keys within the tile
+
+        // S = Q K^T over this warp's 16 keys: two n8 tiles.
+        float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+        for (int kk = 0; kk < DH / 16; ++kk) {
+            // matrices: (keys 0-7, d lo), (keys 0-7, d hi), (keys 8-15, d lo), (keys 8-15, d hi)
+            const int key = key0 + (lane & 7) + (lane >> 4) * 8;
+            const int chunk = kk * 2 + ((lane >> 3) & 1);
+            uint32_t b0, b1, b2, b3;
+            ldsm_x4(kbase + tile_off<DH>(key, chunk), b0, b1, b2, b3);
+            mma_16816<BF16>(sc[0], qa[kk], b0, b1);
+            mma_16816<BF16>(sc[1], qa[kk], b2, b3);
+        }
+        // mask + scale: accumulator element (row, key) with key = 8n + 2*(lane%4) + {0,1}
+        const int64_t p_tile = r.base + (jb + t) * KT + key0;
+        float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+        for (int n = 0; n < 2; ++n)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int64_t pos = p_tile + 8 * n + 2 * (lane & 3) + (e & 1);
+                float x = sc[n][e] * a.scale_log2;
+                if (pos < r.lo || pos > r.hi) x = -INFINITY;
+                sc[n][e] = x;
+                mx[e >> 1] = fmaxf(mx[e >> 1], x);
+            }
+        float alpha[2];
+#pragma unroll
+        for (int hr = 0; hr < 2; ++hr) {
+            mx[hr] = fmaxf(mx[hr], __shfl_xor_sync(0xffffffffu, mx[hr], 1));
+            mx[hr] = fmaxf(mx[hr], __shfl_xor_sync(0xffffffffu, mx[hr], 2));
+            const float m_new = fmaxf(m_r[hr], mx[hr]);
+            alpha[hr] = (m_new == -INFINITY) ? 1.f : ex2f(m_r[hr] - m_new);  // ex2(-inf) = 0 for the first block
+            m_r[hr] = m_new;
+        }
+        float ps[2] = {0.f, 0.f};
+        uint32_t pa[4];
+#pragma unroll
+        for (int n = 0; n < 2; ++n) {
+            float p[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const float m = m_r[e >> 1];
+                p[e] = (m == -INFINITY) ? 0.f : ex2f(sc[n][e] - m);
+                ps[e >> 1] += p[e];
+            }
+            pa[2 * n] = pack_h2(p[0], p[1]);      // row g, keys of n-tile n
+            pa[2 * n + 1] = pack_h2(p[2], p[3]);  // row g + 8
+        }
+        l_r[0] = l_r[0] * alpha[0] + ps[0];
+        l_r[1] = l_r[1] * alpha[1] + ps[1];
+        // A operand order for m16k16: a0 (g, k0-7) a1 (g+8, k0-7) a2 (g, k8-15) a3 (g+8, k8-15)
+        const uint32_t pfrag[4] = {pa[0], pa[1], pa[2], pa[3]};
+#pragma unroll
+        for (int n = 0; n < DH / 8; ++n) {
+            o[n][0] *= alpha[0];
+            o[n][1] *= alpha[0];
+            o[n][2] *= alpha[1];
+            o[n][3] *= alpha[1];
+        }
+        // O += P V: per 16 columns of d one ldmatrix.trans (x4) and two MMAs.
+#pragma unroll
+        for (int dd = 0; dd < DH / 16; ++dd) {
+            // matrices: (keys 0-7, d lo), (keys 8-15, d lo), (keys 0-7, d hi), (keys 8-15, d hi)
+            const int key = key0 + (lane & 7) + ((lane >> 3) & 1) * 8;
+            const int chunk = dd * 2 + (lane >> 4);
+            uint32_t b0, b1, b2, b3;
+            ldsm_x4_t(vbase + tile_off<DH>(key, chunk), b0, b1, b2, b3);
+            mma_16816<false>(o[2 * dd], pfrag, b0, b1);
+            mma_16816<false>(o[2 * dd + 1], pfrag, b2, b3);
+        }
+        __syncthreads();  // the stage is refilled next iteration
+    }
+    if (aborted) return;
+
+    // ---- merge the 4 warps: row sums over the quad, then through shared memory
+#pragma unroll
+    for (int hr = 0; hr < 2; ++hr) {
+        l_r[hr] += __shfl_xor_sync(0xffffffffu, l_r[hr], 1);
+        l_r[hr] += __shfl_xor_sync(0xffffffffu, l_r[hr], 2);
+    }
+    const int g0 = lane >> 2;
+    float* cw = cs + wid * 16 * (DH + 2);
+#pragma unroll
+    for (int n = 0; n < DH / 8; ++n) {
+        const int c0 = 8 * n + 2 * (lane & 3);
+        cw[g0 * (DH + 2) + c0] = o[n][0];
+        cw[g0 * (DH + 2) + c0 + 1] = o[n][1];
+        cw[(g0 + 8) * (DH + 2) + c0] = o[n][2];
+        cw[(g0 + 8) * (DH + 2) + c0 + 1] = o[n][3];
+    }
+    if ((lane & 3) == 0) {
+        cw[g0 * (DH + 2) + DH] = m_r[0];
+        cw[g0 * (DH + 2) + DH + 1] = l_r[0];
+        cw[(g0 + 8) * (DH + 2) + DH] = m_r[1];
+        cw[(g0 + 8) * (DH + 2) + DH + 1] = l_r[1];
+    }
+    __syncthreads();
+
+    const bool single = r.nsplit == 1;
+    const int64_t cnt_idx = (r.qrow * (int64_t)a.hkv + h) * a.zdim + z;
+    float* my_part = a.part + ((((int64_t)blockIdx.x) * a.hkv + h) * a.zdim + z) * (int64_t)(16 * (DH + 2));
+    for (int i = tid; i < G * DH; i += 128) {
+        const int g = i / DH, d = i % DH;
+        float M = -INFINITY;
+        for (int w2 = 0; w2 < 4; ++w2) M = fmaxf(M, cs[(w2 * 16 + g) * (DH + 2) + DH]);
+        float L = 0.f, O = 0.f;
+        if (M != -INFINITY) {
+            for (int w2 = 0; w2 < 4; ++w2) {
+                const float* c = cs + (w2 * 16 + g) * (DH + 2);
+                if (c[DH] == -INFINITY) continue;
+                const float f = ex2f(c[DH] - M);
+                L += c[DH + 1] * f;
+                O += c[d] * f;
+            }
+        }
+        if (single) {
+            dev::store_from_f32(a.out, a.out_dtype, (r.qrow * (int64_t)a.hq + qh0 + g) * DH + d, O / L);
+        } else {
+            my_part[g * (DH + 2) + d] = O;
+            if (d == 0) {
+                my_part[g * (DH + 2) + DH] = M;
+                my_part[g * (DH + 2) + DH + 1] = L;
+            }
+        }
+    }
+    if (single) return;
+
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) s_last = (atomicAdd(&a.counters[cnt_idx], 1) == (int)r.nsplit - 1);
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    for (int i = tid; i < G * DH; i += 128) {
+        const int g = i / DH, d = i % DH;
+        float M = -INFINITY;
+        for (int64_t sp = 0; sp < r.nsplit; ++sp) {
+            const float* pp = a.part + (((r.work_first + sp) * a.hkv + h) * a.zdim + z) * (int64_t)(16 * (DH + 2));
+            M = fmaxf(M, __ldcg(pp + g * (DH + 2) + DH));
+        }
+        float L = 0.f, O = 0.f;
+        for (int64_t sp = 0; sp < r.nsplit; ++sp) {
+            const float* pp = a.part + (((r.work_first + sp) * a.hkv + h) * a.zdim + z) * (int64_t)(16 * (DH + 2));
+            const float mi = __ldcg(pp + g * (DH + 2) + DH);
+            if (mi == -INFINITY) continue;
+            const float f = ex2f(mi - M);
+            L += __ldcg(pp + g * (DH + 2) + DH + 1) * f;
+            O += __ldcg(pp + g * (DH + 2) + d) * f;
+        }
+        dev::store_from_f32(a.out, a.out_dtype, (r.qrow * (int64_t)a.hq + qh0 + g) * DH + d, O / L);
+    }
+    if (tid == 0) a.counters[cnt_idx] = 0;
+}
+
+template <int DH, bool BF16>
+int launch_mma(const MmaArgs& a, dim3 grid, cudaStream_t s) {
+    using C = MmaCfg<DH>;
+    auto kern = attn_decode_mma_kernel<DH, BF16>;
+    static unsigned attr_set = 0;
+    int dev_id = 0;
+    NMG_CUDA_TRY(cudaGetDevice(&dev_id));
+    if (!(attr_set & (1u << (dev_id & 31)))) {
+        NMG_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+        attr_set |= 1u << (dev_id & 31);
+    }
+    kern<<<grid, 128, C::SMEM, s>>>(a);
+    NMG_CUDA_TRY(cudaGetLastError());
+    return NMG_OK;
+}
+
+int dispatch_mma(const nmg_kv_cache* c, const MmaArgs& a, dim3 grid, cudaStream_t s) {
+    const bool bf = c->dtype == NMG_BF16;
+    switch (c->dh) {
+        case 64: return bf ? launch_mma<64, true>(a, grid, s) : launch_mma<64, false>(a, grid, s);
+        case 128: return bf ? launch_mma<128, true>(a, grid, s) : launch_mma<128, false>(a, grid, s);
+        case 256: return bf ? launch_mma<256, true>(a, grid, s) : launch_mma<256, false>(a, grid, s);
+    }
+    return set_error(NMG_UNSUPPORTED, "tensor-core decode: head_dim %d", c->dh);
+}
+
+int64_t mma_blocks_per_split(int64_t total_blocks) {
+    // about 6 CTAs per SM of work; at least 1 tile, at most 128 tiles (8192 keys) per split
+    int64_t b = total_blocks / (148 * 6);
+    return std::max<int64_t>(1, std::min<int64_t>(128, b));
+}
+
+int mma_scratch(int device, int64_t work, int hkv, int zdim, int dh, int64_t counter_rows, float** part,
+                int** counters) {
+    const int64_t part_floats = work * hkv * zdim * 16 * (int64_t)(dh + 2);
+    const int64_t cnt_ints = counter_rows * hkv * zdim;
+    void* base = nullptr;
+    const int st = device_scratch(device, (size_t)cnt_ints * 4 + 256 + (size_t)part_floats * 4, &base);
+    if (st != NMG_OK) return st;
+    *counters = (int*)base;
+    *part = (float*)((char*)base + ((size_t)cnt_ints * 4 + 255) / 256 * 256);
+    return NMG_OK;
+}
+
+}  // namespace
+
+bool decode_mma_supported(const nmg_kv_cache* c, int q_dtype) {
+    if (c->dtype == NMG_F32 || q_dtype != c->dtype) return false;
+    if (c->dh != 64 && c->dh != 128 && c->dh != 256) return false;
+    if (c->window > 0 && c->slots % KT != 0) return false;  // a tile must not straddle the ring end
+    if ((int64_t)c->hkv * c->slots > 0x7FFFFFFF) return false;
+    return true;
+}
+
+int attend_rows_mma(const nmg_kv_cache* c, int hq, const void* q, int64_t rows, int64_t first_query, int64_t window,
+                    int64_t floor_pos, int64_t newest, float scale, void* out, int out_dtype, cudaStream_t stream) {
+    MmaArgs* a = new MmaArgs();
+    int st = make_kv_tensor_maps(c, KT, &a->tm_k[0], &a->tm_v[0]);
+    const int gtot = hq / c->hkv;
+    const int zdim = (gtot + 15) / 16;
+    int64_t longest = 0, total_blocks = 0;
+    for (int64_t t = 0; st == NMG_OK && t < rows; ++t) {
+        const VisibleSpan sp = visible_span(first_query + t, window, floor_pos, newest);
+        const int64_t nb = (sp.hi - c->base) / KT - (sp.lo - c->base) / KT + 1;
+        longest = std::max(longest, nb);
+        total_blocks += nb;
+    }
+    const int64_t bps = mma_blocks_per_split(total_blocks * c->hkv * zdim);
+    const int64_t max_splits = (longest + bps - 1) / bps;
+    const int64_t work = rows * max_splits;
+    if (st == NMG_OK && work > 0x7FFFFFFF) st = set_error(NMG_UNSUPPORTED, "decode: too many work items");
+    if (st == NMG_OK) st = mma_scratch(c->device, work, c->hkv, zdim, c->dh, rows, &a->part, &a->counters);
+    if (st == NMG_OK) st = device_error_flag(c->device, &a->err);
+    if (st == NMG_OK) {
+        a->mode = 0;
+        a->hkv = c->hkv;
+        a->hq = hq;
+        a->gtot = gtot;
+        a->zdim = zdim;
+        a->blocks_per_split = bps;
+        a->base = c->base;
+        a->slots = c->slots;
+        a->rows = rows;
+        a->first_query = first_query;
+        a->window = window;
+        a->floor_pos = floor_pos;
+        a->newest = newest;
+        a->max_splits = (int32_t)max_splits;
+        a->nseq = 0;
+        a->q = q;
+        a->out = out;
+        a->out_dtype = out_dtype;
+        a->scale_log2 = scale * 1.4426950408889634f;
+        st = dispatch_mma(c, *a, dim3((unsigned)work, c->hkv, zdim), stream);
+    }
+    delete a;
+    return st;
+}
+
+int attend_batch_mma(const nmg_kv_cache* const* caches, int batch, const int64_t* queries_at, int hq, const void* q,
+                     float scale, void* out, int out_dtype, cudaStream_t stream) {
+    const nmg_kv_cache* c0 = caches[0];
+    const int gtot = hq / c0->hkv;
+    const int zdim = (gtot + 15) / 16;
+    std::vector<VisibleSpan> spans(batch);
+    int64_t total_blocks = 0;
+    for (int b = 0; b < batch; ++b) {
+        const nmg_kv_cache* c = caches[b];
+        const int64_t qpos = queries_at ? queries_at[b] : c->newest();
+        spans[b] = visible_span(qpos, c->window, c->oldest, c->newest());
+        total_blocks += (spans[b].hi - c->base) / KT - (spans[b].lo - c->base) / KT + 1;
+    }
+    const int64_t bps = mma_blocks_per_split(total_blocks * c0->hkv * zdim);
+    int64_t all_work = 0;
+    std::vector<int32_t> nsplit(batch);
+    for (int b = 0; b < batch; ++b) {
+        const nmg_kv_cache* c = caches[b];
+        const int64_t nb = (spans[b].hi - c->base) / KT - (spans[b].lo - c->base) / KT + 1;
+        nsplit[b] = (int32_t)((nb + bps - 1) / bps);
+        all_work += nsplit[b];
+    }
+    float* part = nullptr;
+    int* counters = nullptr;
+    int st = mma_scratch(c0->device, all_work, c0->hkv, zdim, c0->dh, batch, &part, &counters);
+    int* err = nullptr;
+    if (st == NMG_OK) st = device_error_flag(c0->device, &err);
+    MmaArgs* a = new MmaArgs();
+    int64_t work_base = 0;
+    for (int b0 = 0; st == NMG_OK && b0 < batch; b0 += kMmaMaxBatch) {
+        const int nb = std::min(kMmaMaxBatch, batch - b0);
+        int64_t w = 0;
+        for (int i = 0; st == NMG_OK && i < nb; ++i) {
+            const nmg_kv_cache* c = caches[b0 + i];
+            st = make_kv_tensor_maps(c, KT, &a->tm_k[i], &a->tm_v[i]);
+            MmaSeq& e = a->seq[i];
+            e.base = c->base;
+            e.slots = c->slots;
+            e.lo = spans[b0 + i].lo;
+            e.hi = spans[b0 + i].hi;
+            e.nsplit = nsplit[b0 + i];
+            e.work_first = (int32_t)w;
+            e.qrow = b0 + i;
+            e.map = i;
+            w += e.nsplit;
+        }
+        if (st != NMG_OK) break;
+        a->mode = 1;
+        a->hkv = c0->hkv;
+        a->hq = hq;
+        a->gtot = gtot;
+        a->zdim = zdim;
+        a->blocks_per_split = bps;
+        a->nseq = nb;
+        a->q = q;
+        a->out = out;
+        a->out_dtype = out_dtype;
+        a->scale_log2 = scale * 1.4426950408889634f;
+        a->part = part + work_base * c0->hkv * zdim * 16 * (int64_t)(c0->dh + 2);
+        a->counters = counters;
+        a->err = err;
+        st = dispatch_mma(c0, *a, dim3((unsigned)w, c0->hkv, zdim), stream);
+        work_base += w;
+    }
+    delete a;
+    return st;
+}
+
+}  // namespace nmg

@@ -779,6 +779,28 @@ int launch_prefill_h2(const PrefillArgs& a, dim3 grid, cudaStream_t s) {
 
 }  // namespace
 
+int make_kv_tensor_maps(const nmg_kv_cache* c, int box_rows, CUtensorMap* k, CUtensorMap* v) {
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return set_error(NMG_UNSUPPORTED, "cuTensorMapEncodeTiled unavailable");
+    if (((uintptr_t)c->k & 15) || ((uintptr_t)c->v & 15)) return set_error(NMG_UNSUPPORTED, "unaligned cache");
+    for (int which = 0; which < 2; ++which) {
+        const int dt = which ? c->vdtype : c->dtype;
+        const CUtensorMapDataType t = dt == NMG_BF16   ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                      : dt == NMG_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                      : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+        const int es = dtype_size(dt);
+        cuuint64_t dims[2] = {(cuuint64_t)c->dh, (cuuint64_t)c->hkv * (cuuint64_t)c->slots};
+        cuuint64_t strides[1] = {(cuuint64_t)c->dh * es};
+        cuuint32_t box[2] = {(cuuint32_t)(128 / es), (cuuint32_t)box_rows};
+        cuuint32_t estr[2] = {1, 1};
+        const CUresult r = enc(which ? v : k, t, 2, which ? c->v : c->k, dims, strides, box, estr,
+                               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (r != CUDA_SUCCESS) return set_error(NMG_CUDA_ERROR, "K/V tensor map (%d)", (int)r);
+    }
+    return NMG_OK;
+}
+
 bool prefill_supported(const nmg_kv_cache* c, int hq, int q_dtype, int64_t rows) {
     if (c->dtype == NMG_F32 || q_dtype != c->dtype) return false;
     if (c->dh != 128 && c->dh != 256) return false;
