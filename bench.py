@@ -472,6 +472,16 @@ def extra_config3(torch, dev, small=False):
         seq_flops = 7.0 * d * d * T * hv
         res[f"prefill_chunk{chunk}"] = {"ms": ms, "tok_per_s": T / (ms * 1e-3),
                                         "tflops_recurrence_equiv": seq_flops / (ms * 1e-3) / 1e12}
+        if chunk:
+            # chunked algorithm per (value head, chunk): 5*2C^2D + 3*2CD^2 + (2/3)C^3 FLOP
+            C = chunk
+            alg = (5 * 2 * C * C * d + 3 * 2 * C * d * d + 2 * C ** 3 / 3) * hv * (T // C)
+            tf = alg / (ms * 1e-3) / 1e12
+            tf32_peak = peaks()["bf16"] / 2  # tf32 runs at half the bf16 rate
+            res[f"prefill_chunk{chunk}"].update(
+                {"tflops_chunked_alg": tf, "alg_flop": alg,
+                 "roofline": {"bound": "tensor", "achieved": tf, "peak": tf32_peak, "unit": "TFLOP/s",
+                              "frac": tf / tf32_peak, "note": "tf32 peak taken as half the measured bf16 peak"}})
     # 256 decode steps continue from the final state, graph-captured
     qd = norm(torch.randn(Tdec, hk, d, device=dev, generator=g)) / math.sqrt(d)
     kd = norm(torch.randn(Tdec, hk, d, device=dev, generator=g))

@@ -75,15 +75,6 @@ struct PrefillArgs {
     int* err;
 };
 
-__device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* map, int32_t x, int32_t y, int32_t z,
-                                            uint64_t* bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.3d.shared::cta.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
-        "[%5];" ::"r"(dev::smem_u32(smem_dst)),
-        "l"(map), "r"(x), "r"(y), "r"(z), "r"(dev::smem_u32(bar))
-        : "memory");
-}
-
 __device__ __forceinline__ float ex2(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -180,7 +171,7 @@ __global__ void __launch_bounds__(352, 1) attn_prefill_kernel(const __grid_const
             dev::mbar_arrive_expect_tx(q_full, C::Q_BYTES);
 #pragma unroll
             for (int c = 0; c < DH / 64; ++c)
-                tma_load_3d(smem + C::Q_OFF + c * BM * 128, &a.tm_q, c * 64, h, (int32_t)t0, q_full);
+                dev::tma_load_3d(smem + C::Q_OFF + c * BM * 128, &a.tm_q, c * 64, h, (int32_t)t0, q_full);
             for (int i = 0; i < nblk; ++i) {
                 const int s = i % KST;
                 if (i >= KST && !dev::mbar_wait(&k_empty[s], ((i / KST) - 1) & 1, a.err)) break;
@@ -520,7 +511,7 @@ __global__ void __launch_bounds__(352, 1) attn_prefill_h2_kernel(const __grid_co
             for (int x = 0; x < 2; ++x)
 #pragma unroll
                 for (int c = 0; c < DH / 64; ++c)
-                    tma_load_3d(smem + C::Q_OFF + x * C::Q_BYTES + c * BM * 128, &a.tm_q, c * 64, h0 + x, (int32_t)t0,
+                    dev::tma_load_3d(smem + C::Q_OFF + x * C::Q_BYTES + c * BM * 128, &a.tm_q, c * 64, h0 + x, (int32_t)t0,
                                 q_full);
             for (int i = 0; i < nblk; ++i) {
                 const int s = i % KST;
@@ -730,21 +721,6 @@ __global__ void __launch_bounds__(352, 1) attn_prefill_h2_kernel(const __grid_co
 
 // ------------------------------------------------------------------ host side
 
-typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiledFn encode_fn() {
-    static EncodeTiledFn fn = nullptr;
-    if (!fn) {
-        void* p = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = (EncodeTiledFn)p;
-    }
-    return fn;
-}
 
 template <int DH, bool BF16>
 int launch_prefill(const PrefillArgs& a, dim3 grid, cudaStream_t s) {
@@ -780,7 +756,7 @@ int launch_prefill_h2(const PrefillArgs& a, dim3 grid, cudaStream_t s) {
 }  // namespace
 
 int make_kv_tensor_maps(const nmg_kv_cache* c, int box_rows, CUtensorMap* k, CUtensorMap* v) {
-    EncodeTiledFn enc = encode_fn();
+    EncodeTiledFn enc = encode_tiled_fn();
     if (!enc) return set_error(NMG_UNSUPPORTED, "cuTensorMapEncodeTiled unavailable");
     if (((uintptr_t)c->k & 15) || ((uintptr_t)c->v & 15)) return set_error(NMG_UNSUPPORTED, "unaligned cache");
     for (int which = 0; which < 2; ++which) {
@@ -808,13 +784,13 @@ bool prefill_supported(const nmg_kv_cache* c, int hq, int q_dtype, int64_t rows)
     if (c->slots % bn != 0) return false;
     if (rows < 64) return false;
     if ((int64_t)c->hkv * c->slots > 0x7FFFFFFF) return false;
-    return encode_fn() != nullptr;
+    return encode_tiled_fn() != nullptr;
 }
 
 int attend_rows_prefill(const nmg_kv_cache* c, int hq, const void* q, int q_dtype, int64_t rows, int64_t first_query,
                         int64_t window, int64_t floor_pos, int64_t newest, float scale, void* out, int out_dtype,
                         cudaStream_t stream) {
-    EncodeTiledFn enc = encode_fn();
+    EncodeTiledFn enc = encode_tiled_fn();
     if (!enc) return set_error(NMG_UNSUPPORTED, "cuTensorMapEncodeTiled unavailable");
     if (((uintptr_t)q & 15) || ((uintptr_t)c->k & 15) || ((uintptr_t)c->v & 15))
         return set_error(NMG_UNSUPPORTED, "prefill: 16-byte aligned tensors required");

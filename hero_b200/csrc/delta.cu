@@ -10,12 +10,7 @@
 // S), which is how both kernels split a head across threads and CTAs.
 #include <math.h>
 
-#include "common.cuh"
-
-struct nmg_delta_state {
-    int heads = 0, dk = 0, dv = 0, device = 0;
-    float* data = nullptr;  // [heads][dk][dv]
-};
+#include "delta.cuh"
 
 namespace nmg {
 namespace {
@@ -172,9 +167,6 @@ bool dk_supported(int dk) { return dk == 2 || dk == 4 || dk == 8 || dk == 16 || 
 
 }  // namespace
 
-int delta_prefill_chunked(nmg_delta_state* st, int hk, int64_t T, const float* q, const float* k, const float* v,
-                          const float* gate, const float* beta, float* out, int chunk, cudaStream_t stream);
-
 int delta_prefill_sequential(nmg_delta_state* st, int hk, int64_t T, const float* q, const float* k, const float* v,
                              const float* gate, const float* beta, float* out, cudaStream_t stream) {
     const int dk = st->dk;
@@ -277,7 +269,8 @@ extern "C" int nmg_delta_prefill(nmg_delta_state* st, int hk, int64_t T, const f
     NMG_CUDA_TRY(cudaGetDevice(&prev));
     if (prev != st->device) NMG_CUDA_TRY(cudaSetDevice(st->device));
     int r;
-    if (chunk == 0)
+    const bool aligned = !(((uintptr_t)q | (uintptr_t)k | (uintptr_t)v | (uintptr_t)out) & 15);
+    if (chunk == 0 || !aligned || !nmg::delta_chunked_supported(st))
         r = nmg::delta_prefill_sequential(st, hk, T, q, k, v, gate, beta, out, (cudaStream_t)stream);
     else
         r = nmg::delta_prefill_chunked(st, hk, T, q, k, v, gate, beta, out, chunk, (cudaStream_t)stream);

@@ -99,6 +99,18 @@ int check_device_flag(int device, cudaStream_t stream) {
     return NMG_OK;
 }
 
+EncodeTiledFn encode_tiled_fn() {
+    static EncodeTiledFn fn = nullptr;
+    if (!fn) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = (EncodeTiledFn)p;
+    }
+    return fn;
+}
+
 }  // namespace nmg
 
 extern "C" const char* nmg_last_error(void) { return nmg::g_last_error; }

@@ -50,6 +50,29 @@ __host__ __device__ constexpr uint32_t idesc_f16(int m, int n, int ab_bf16, int 
            | ((uint32_t)(m >> 4) << 24);   // M / 16
 }
 
+// Instruction descriptor for kind::tf32 (fp32 storage, tf32 multiply) with an
+// fp32 accumulator.  a_mn/b_mn: 1 = MN-major operand.
+__host__ __device__ constexpr uint32_t idesc_tf32(int m, int n, int a_mn, int b_mn) {
+    return (1u << 4)                       // D format: f32
+           | (2u << 7)                     // A format: tf32
+           | (2u << 10)                    // B format: tf32
+           | ((uint32_t)a_mn << 15)        // A major
+           | ((uint32_t)b_mn << 16)        // B major
+           | ((uint32_t)(n >> 3) << 17)    // N / 8
+           | ((uint32_t)(m >> 4) << 24);   // M / 16
+}
+
+// D[tmem] (+)= A[smem] * B[smem], kind::tf32 (K = 8 per instruction), one thread.
+__device__ __forceinline__ void mma_tf32_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                            uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
 // D[tmem] (+)= A[smem] * B[smem]^T, issued by one thread.
 __device__ __forceinline__ void mma_f16_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
                                            uint32_t accumulate) {

@@ -37,7 +37,7 @@ def test_delta_rule_known_answers(dev):
 
 
 @pytest.mark.parametrize("path", sorted(glob.glob(os.path.join(HERE, "golden", "delta_*.npz"))))
-@pytest.mark.parametrize("chunk", [0])
+@pytest.mark.parametrize("chunk", [0, 64])
 def test_golden_fixtures(dev, path, chunk):
     z = np.load(path)
     hv, d = z["state0"].shape[0], z["state0"].shape[1]
@@ -77,3 +77,72 @@ def test_step_equals_prefill(dev):
                       .cpu().numpy() for t in range(n)])
     assert np.abs(whole - steps).max() < 1e-4
     assert np.abs(a.tensor().cpu().numpy() - c.tensor().cpu().numpy()).max() < 1e-4
+
+
+def _random_state(seed, hv, d):
+    return (oracle.normal(seed, 7, hv * d * d).reshape(hv, d, d) * np.float32(0.05)).astype(np.float32)
+
+
+@pytest.mark.parametrize("n", [1, 12, 63, 64, 65, 130, 700])
+def test_chunked_prefill_matches_oracle(dev, n):
+    # Chunk 64, tcgen05 tf32 path: ragged last chunk, single partial chunk,
+    # exact multiples; a non-zero starting state; value heads over tiled key heads.
+    hv, hk, d = 4, 2, 128
+    q, k, v, g, b = delta_inputs(11 + n, n, hk, hv, d)
+    s0 = _random_state(n, hv, d)
+    st = nm.DeltaNetState(hv, d, d)
+    st.tensor().copy_(T(s0, dev))
+    out = nm.delta_prefill(st, T(q, dev), T(k, dev), T(v, dev), T(g, dev), T(b, dev), hk, chunk=64).cpu().numpy()
+    want, ws = oracle.delta_run(s0, q, k, v, g, b, hk)
+    assert_close(out, want, what=f"chunked out T={n}")
+    assert_close(st.tensor().cpu().numpy(), ws, what=f"chunked state T={n}")
+
+
+@pytest.mark.parametrize("hv,hk,dv", [(3, 2, 64), (2, 1, 96)])
+def test_chunked_prefill_other_head_layouts(dev, hv, hk, dv):
+    # value heads not a multiple of key heads; Dv of 2 and 3 column slices
+    d, n = 128, 150
+    q, k, _, g, b = delta_inputs(5, n, hk, hv, d)
+    v = oracle.normal(5, 9, n * hv * dv).reshape(n, hv, dv)
+    st = nm.DeltaNetState(hv, d, dv)
+    out = nm.delta_prefill(st, T(q, dev), T(k, dev), T(v, dev), T(g, dev), T(b, dev), hk, chunk=64).cpu().numpy()
+    want, ws = oracle.delta_run(np.zeros((hv, d, dv), np.float32), q, k, v, g, b, hk)
+    assert_close(out, want, what="out")
+    assert_close(st.tensor().cpu().numpy(), ws, what="state")
+
+
+def test_chunked_config3_heads_then_decode(dev):
+    # Config 3's head layout (32 value heads, 16 key heads, 128 x 128 states)
+    # over 1024 prefill tokens in 16 chunks, then decode steps continue from
+    # the chunked kernel's final state.
+    hv, hk, d, Tp, Td = 32, 16, 128, 1024, 8
+    q, k, v, g, b = delta_inputs(3, Tp + Td, hk, hv, d)
+    st = nm.DeltaNetState(hv, d, d)
+    out = nm.delta_prefill(st, T(q[:Tp], dev), T(k[:Tp], dev), T(v[:Tp], dev), T(g[:Tp], dev), T(b[:Tp], dev), hk,
+                           chunk=64).cpu().numpy()
+    want, ws = oracle.delta_run(np.zeros((hv, d, d), np.float32), q[:Tp], k[:Tp], v[:Tp], g[:Tp], b[:Tp], hk)
+    assert_close(out, want, what="prefill out")
+    assert_close(st.tensor().cpu().numpy(), ws, what="prefill state")
+    for t in range(Tp, Tp + Td):
+        o = nm.delta_step(st, T(q[t], dev), T(k[t], dev), T(v[t], dev), T(g[t], dev), T(b[t], dev), hk).cpu().numpy()
+        wo, ws = oracle.delta_run(ws, q[t:t + 1], k[t:t + 1], v[t:t + 1], g[t:t + 1], b[t:t + 1], hk)
+        assert_close(o, wo[0], what=f"decode step {t}")
+
+
+def test_chunked_equals_sequential_at_full_length(dev):
+    # Config 3 at its full 8192 tokens: the chunked kernel against the
+    # token-sequential kernel (both on the device; the oracle would take
+    # minutes here), outputs and final state.
+    hv, hk, d, n = 32, 16, 128, 8192
+    gen = torch.Generator(device="cpu").manual_seed(0)
+    q = torch.nn.functional.normalize(torch.randn(n, hk, d, generator=gen), dim=-1) / d ** 0.5
+    k = torch.nn.functional.normalize(torch.randn(n, hk, d, generator=gen), dim=-1)
+    v = torch.randn(n, hv, d, generator=gen)
+    g = -torch.nn.functional.softplus(torch.randn(n, hv, generator=gen))
+    b = torch.sigmoid(torch.randn(n, hv, generator=gen))
+    q, k, v, g, b = (x.to(dev) for x in (q, k, v, g, b))
+    a, s = nm.DeltaNetState(hv, d, d), nm.DeltaNetState(hv, d, d)
+    oc = nm.delta_prefill(a, q, k, v, g, b, hk, chunk=64).cpu().numpy()
+    os_ = nm.delta_prefill(s, q, k, v, g, b, hk, chunk=0).cpu().numpy()
+    assert_close(oc, os_, what="chunked vs sequential out")
+    assert_close(a.tensor().cpu().numpy(), s.tensor().cpu().numpy(), what="chunked vs sequential state")
