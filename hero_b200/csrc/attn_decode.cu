@@ -440,19 +440,22 @@ int scratch_for(int device, int64_t work, int hkv, int zdim, int gt, int dh, int
                 int** counters, void* caller_scratch, int64_t caller_bytes) {
     const int64_t part_floats = work * hkv * zdim * (int64_t)gt * (dh + 2);
     const int64_t cnt_ints = counter_rows * hkv * zdim;
-    const size_t bytes = (size_t)cnt_ints * 4 + 256 + (size_t)part_floats * 4;
-    void* base = nullptr;
-    if (caller_scratch) {
+    if (caller_scratch) {  // the caller zeroes the tickets at the start of its memory
+        const size_t bytes = (size_t)cnt_ints * 4 + 256 + (size_t)part_floats * 4;
         if ((int64_t)bytes > caller_bytes)
             return set_error(NMG_LENGTH_ERROR, "attention needs %zu bytes of scratch, %lld given", bytes,
                              (long long)caller_bytes);
-        base = caller_scratch;
-    } else {
-        int st = device_scratch(device, bytes, &base);
-        if (st != NMG_OK) return st;
+        *counters = (int*)caller_scratch;
+        *part = (float*)((char*)caller_scratch + ((size_t)cnt_ints * 4 + 255) / 256 * 256);
+        return NMG_OK;
     }
-    *counters = (int*)base;
-    *part = (float*)((char*)base + ((size_t)cnt_ints * 4 + 255) / 256 * 256);
+    void* tickets = nullptr;
+    void* base = nullptr;
+    int st = device_tickets(device, (size_t)cnt_ints * 4, &tickets);
+    if (st == NMG_OK) st = device_scratch(device, (size_t)part_floats * 4, &base);
+    if (st != NMG_OK) return st;
+    *counters = (int*)tickets;
+    *part = (float*)base;
     return NMG_OK;
 }
 

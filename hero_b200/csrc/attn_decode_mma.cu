@@ -427,11 +427,13 @@ int mma_scratch(int device, int64_t work, int hkv, int zdim, int dh, int64_t cou
                 int** counters) {
     const int64_t part_floats = work * hkv * zdim * 16 * (int64_t)(dh + 2);
     const int64_t cnt_ints = counter_rows * hkv * zdim;
+    void* tickets = nullptr;
     void* base = nullptr;
-    const int st = device_scratch(device, (size_t)cnt_ints * 4 + 256 + (size_t)part_floats * 4, &base);
+    int st = device_tickets(device, (size_t)cnt_ints * 4, &tickets);
+    if (st == NMG_OK) st = device_scratch(device, (size_t)part_floats * 4, &base);
     if (st != NMG_OK) return st;
-    *counters = (int*)base;
-    *part = (float*)((char*)base + ((size_t)cnt_ints * 4 + 255) / 256 * 256);
+    *counters = (int*)tickets;
+    *part = (float*)base;
     return NMG_OK;
 }
 

@@ -40,6 +40,10 @@ int device_scratch(int device, size_t bytes, void** ptr);
 // A second, independent pool for staging copies (never the same memory as
 // device_scratch, so a kernel may use both).
 int device_staging(int device, size_t bytes, void** ptr);
+// Zero-initialised int32 counters (the split-KV merge tickets).  Every kernel
+// that takes a ticket returns it to zero before it exits, so the pool is all
+// zeros between launches; nothing else may write it.
+int device_tickets(int device, size_t bytes, void** ptr);
 // A zero-initialised int32 error flag per device (device-side wait timeouts).
 int device_error_flag(int device, int** flag);
 // Copies the device error flag back (synchronising `stream`), clears it, and

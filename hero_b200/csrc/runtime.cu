@@ -17,7 +17,7 @@ struct Pool {
     size_t bytes = 0;
 };
 struct DeviceResources {
-    Pool scratch, staging;
+    Pool scratch, staging, tickets;
     int* error_flag = nullptr;
 };
 std::mutex g_mu;
@@ -63,6 +63,11 @@ int grow(int device, Pool& p, size_t bytes, void** ptr) {
 int device_scratch(int device, size_t bytes, void** ptr) {
     std::lock_guard<std::mutex> lk(g_mu);
     return grow(device, resources(device).scratch, bytes, ptr);
+}
+
+int device_tickets(int device, size_t bytes, void** ptr) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    return grow(device, resources(device).tickets, bytes, ptr);
 }
 
 int device_staging(int device, size_t bytes, void** ptr) {

@@ -146,3 +146,26 @@ def test_chunked_equals_sequential_at_full_length(dev):
     os_ = nm.delta_prefill(s, q, k, v, g, b, hk, chunk=0).cpu().numpy()
     assert_close(oc, os_, what="chunked vs sequential out")
     assert_close(a.tensor().cpu().numpy(), s.tensor().cpu().numpy(), what="chunked vs sequential state")
+
+
+@pytest.mark.parametrize("dtype", ["f32", "f16"])
+def test_decode_attention_after_chunked_prefill(dev, dtype):
+    # The chunked prefill leaves its tiles in the library's device scratch; the
+    # split-KV decode kernels that run next (CUDA-core f32, tensor-core f16)
+    # keep their merge tickets elsewhere and must be unaffected.
+    hv, hk, d, n = 4, 2, 128, 300
+    q, k, v, g, b = delta_inputs(17, n, hk, hv, d)
+    st = nm.DeltaNetState(hv, d, d)
+    nm.delta_prefill(st, T(q, dev), T(k, dev), T(v, dev), T(g, dev), T(b, dev), hk, chunk=64)
+    hq, hkv, dh, rows = 8, 4, 128, 5000
+    rnd = oracle.round_fp16 if dtype == "f16" else (lambda x: x)
+    tdt = torch.float16 if dtype == "f16" else torch.float32
+    kk = rnd(oracle.normal(23, 1, rows * hkv * dh).reshape(rows, -1))
+    vv = rnd(oracle.normal(23, 2, rows * hkv * dh).reshape(rows, -1))
+    qq = rnd(oracle.normal(23, 3, hq * dh).reshape(1, -1))
+    cache = nm.FullAttentionCache(hkv, dh, capacity=rows, dtype=dtype)
+    cache.append(0, T(kk, dev).to(tdt), T(vv, dev).to(tdt))
+    want = oracle.attend(kk, vv, 0, 0, hkv, dh, qq, hq, rows - 1, scale=np.float32(dh ** -0.5))
+    for _ in range(2):
+        got = nm.attend(cache, T(qq, dev).to(tdt), rows - 1, dh ** -0.5, out_dtype=torch.float32).cpu().numpy()
+        assert_close(got, want, what=f"{dtype} decode after chunked prefill")
