@@ -176,10 +176,26 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     return ok != 0;
 }
 
+// Non-blocking probe: has the phase with `parity` completed?
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
 // Bounded wait for the phase with `parity` to complete.  Returns false (and
 // raises the kernel's error flag) when it gives up; callers then skip the
-// remaining work and fall through to their normal exit.
+// remaining work and fall through to their normal exit.  A phase that has
+// already completed is seen by the non-blocking probe, which costs far less
+// than a try_wait.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err_flag) {
+    if (mbar_test_wait(bar, parity)) return true;
     for (long long i = 0; i < kMaxPolls; ++i)
         if (mbar_try_wait(bar, parity)) return true;
     if (err_flag) atomicExch(err_flag, kErrWaitTimeout);

@@ -20,16 +20,16 @@
 //   key head, the [K;Q] tile and its K^T, rounded to tf32 -- each as the exact
 //   shared-memory image phase 2 multiplies from, so phase 2 fetches it with one
 //   bulk copy.
-// Phase 2, delta_scan_kernel: one CTA per (value head, 32 state columns); walks
-//   the chunks in order with its state slice in registers:
-//     MMA1 [K;Q] S -> (K S, Q S);  R -> smem;  MMA2 [T;MT] R -> (D, M T R);
-//     O -> global;  f D -> smem;  MMA3 K^T (f D);  S <- exp(G_last) S + that.
+// Phase 2, delta_scan_kernel: one CTA per (value head, 128 value columns);
+//   walks the chunks in order with the state (transposed) resident in TMEM:
+//     MMA1 S^T [K;Q]^T -> (K S | Q S)^T;  R^T -> TMEM;  MMA2 R^T [T;MT]^T ->
+//     (D | M T R)^T;  (f D)^T -> TMEM;  MMA3 S^T += (f D)^T K  (S^T rescaled by
+//     exp(G_last) beforehand);  O = e (Q S) + M T R -> global.
 //   A producer warp streams the next chunk's tiles meanwhile.
 //
-// Operand layouts: every tensor-core operand is K-major with the 128-byte
+// Operand layouts: every shared-memory operand is K-major with the 128-byte
 // swizzle (a tf32 operand stored MN-major in that swizzle is not multiplied by
-// this hardware), so the contraction over the chunk's tokens reads K^T, and
-// the state, R and f D images are written transposed (column per thread).
+// this hardware), so the contraction over the chunk's tokens reads K^T.
 // Precision: each operand is rounded to the nearest tf32 value (10-bit
 // mantissa) before it is multiplied; every sum is fp32 and the state stays fp32.
 #include "delta.cuh"
@@ -40,12 +40,10 @@ namespace {
 
 constexpr int kC = 64;                         // tokens per chunk
 constexpr int kDK = 128;                       // key dimension the images are laid out for
-constexpr int kSlice = 32;                     // state columns per phase-2 CTA
 constexpr uint32_t kKQBytes = 65536;           // [K;Q]: 4 boxes (32 d each) x 128 rows x 128 B
 constexpr uint32_t kKTBytes = 32768;           // K^T: 2 boxes (32 tokens each) x 128 rows (d) x 128 B
 constexpr uint32_t kTMBytes = 32768;           // [T;MT]: 2 boxes (32 tokens each) x 128 rows x 128 B
 constexpr uint32_t kAuxBytes = 1024;           // beta[64], e[64], f[64], exp(G_last), zero pad
-constexpr uint32_t kVBytes = kC * kSlice * 4;  // one chunk of one value-column slice
 
 __device__ __forceinline__ float tf32r(float x) {
     uint32_t r;
@@ -63,21 +61,6 @@ __device__ __forceinline__ uint32_t sw_elem(uint32_t row, uint32_t col) {
 
 __device__ __forceinline__ float4 tf32r4(float a, float b, float c, float d) {
     return make_float4(tf32r(a), tf32r(b), tf32r(c), tf32r(d));
-}
-
-// Barrier over the 128 compute threads (named barrier 1) that also returns
-// whether any of them passed `pred`.
-__device__ __forceinline__ bool bar_any_128(bool pred) {
-    uint32_t r;
-    asm volatile(
-        "{\n\t.reg .pred p, q;\n\t"
-        "setp.ne.u32 p, %1, 0;\n\t"
-        "bar.red.or.pred q, 1, 128, p;\n\t"
-        "selp.u32 %0, 1, 0, q;\n\t}"
-        : "=r"(r)
-        : "r"((uint32_t)pred)
-        : "memory");
-    return r != 0;
 }
 
 // K-major, 128-byte-swizzle descriptor for k-step `kk` (8 tf32 values) of an
@@ -117,7 +100,7 @@ __global__ void __launch_bounds__(128) delta_wy_kernel(const __grid_constant__ W
     uint64_t* bars = (uint64_t*)(smem + P1_BAR);  // 0: [K;Q] landed, 1: first MMA, 2: second MMA
     uint32_t* tmem_slot = (uint32_t*)(bars + 4);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int c = blockIdx.x, h = blockIdx.y, kh = h % a.hk;
+    const int h = (int)(blockIdx.x % (unsigned)a.hv), c = (int)(blockIdx.x / (unsigned)a.hv), kh = h % a.hk;
     const bool publish = h < a.hk;  // value head h == its key head: writes the K images once
     const int64_t t0 = (int64_t)c * kC;
 
@@ -323,7 +306,7 @@ __global__ void __launch_bounds__(128) delta_wy_kernel(const __grid_constant__ W
         dev::bulk_s2g(a.tm_img + rec * (kTMBytes / 4), IM, kTMBytes);
         dev::bulk_s2g(a.aux + rec * (kAuxBytes / 4), aux_s, kAuxBytes);
         dev::bulk_commit();
-        dev::bulk_wait_all();
+        dev::bulk_wait_read();  // the stores are complete for the next kernel once this grid ends
     }
     if (warp == 0) {
         tc::fence_after_sync();
@@ -346,213 +329,278 @@ struct ScanArgs {
     int* err;
 };
 
-// Shared memory.  The three big tiles are single-buffered (each is refilled as
-// soon as its MMA of the current chunk completes, a whole chunk before its next
-// use); V and aux are double-buffered.  The state image is S^T (row j = column
-// j of the slice, 4 boxes of 32 k); the R image holds R^T, later (f D)^T (row j,
-// 2 boxes of 32 tokens).
+// The scan works in the transposed orientation: TMEM lane j is value column
+// j (128 per CTA) and every product is a TS-form MMA (A in TMEM) with N = 128.
+//   MMA1  P    = S^T [K;Q]^T        A = S^T (TMEM),  B = [K;Q] image   -> (K S)^T | (Q S)^T
+//   MMA2  D2   = R^T [T;MT]^T       A = R^T (TMEM),  B = [T;MT] image  -> D^T | (M T R)^T
+//   MMA3  S^T += (f D)^T K          A = (f D)^T,     B = K^T image     (S^T pre-scaled by exp(G_last))
+// Warpgroup 0 runs the chain (R, f D, MMA issue); warpgroup 1 rescales the
+// state between MMA1 and MMA3 and forms O = e (Q S) + M T R; warp 8 loads.
+constexpr int kCols = 128;  // value columns per CTA (TMEM lanes)
+constexpr uint32_t kVTile = kC * kCols * 4;  // 4 boxes of 32 columns x 64 tokens
+constexpr uint32_t TM_S = 0, TM_P = 128, TM_RD = 256, TM_D2 = 320;  // TMEM columns
 constexpr uint32_t P2_KQ = 0,                //
     P2_KT = P2_KQ + kKQBytes,                //
     P2_TM = P2_KT + kKTBytes,                //
     P2_V = P2_TM + kTMBytes,                 // 2 stages
-    P2_S = P2_V + 2 * kVBytes,               // 4 boxes x 32 rows x 128 B
-    P2_R = P2_S + kDK * kSlice * 4,          // 2 boxes x 32 rows x 128 B
-    P2_AUX = P2_R + kC * kSlice * 4,         // 2 stages
-    P2_BAR = P2_AUX + 2 * kAuxBytes, P2_END = P2_BAR + 128;
+    P2_AUX = P2_V + 2 * kVTile,              // 2 stages
+    P2_BAR = P2_AUX + 2 * kAuxBytes, P2_END = P2_BAR + 256;
 constexpr uint32_t P2_SMEM = 1024 + P2_END;
 static_assert(P2_SMEM <= 227 * 1024, "phase-2 shared memory");
 
-// Column `col` (a k index) of a transposed 32-row image: element j of `v`
-// goes to row j, column col; boxes of 32 columns `box_bytes` apart.
-__device__ __forceinline__ void store_col_image(uint8_t* img, int col, uint32_t box_bytes, const float (&v)[kSlice]) {
-    uint8_t* base = img + (col >> 5) * box_bytes;
-#pragma unroll
-    for (int j = 0; j < kSlice; ++j) *(float*)(base + sw_elem(j, col & 31)) = tf32r(v[j]);
-}
+enum : int {
+    B_KQ_FULL, B_KQ_EMPTY, B_KT_FULL, B_KT_EMPTY, B_TM_FULL, B_TM_EMPTY, B_VA_FULL0, B_VA_FULL1, B_VA_EMPTY0,
+    B_VA_EMPTY1, B_MMA1, B_MMA2, B_MMA3, B_SCALED, B_ODONE, B_COUNT
+};
 
-__global__ void __launch_bounds__(160, 1) delta_scan_kernel(const __grid_constant__ ScanArgs a) {
+__device__ __forceinline__ void named_bar(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
+
+__global__ void __launch_bounds__(288, 1) delta_scan_kernel(const __grid_constant__ ScanArgs a) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-    uint64_t* bars = (uint64_t*)(smem + P2_BAR);
-    uint64_t* kq_full = bars + 0;
-    uint64_t* kq_empty = bars + 1;
-    uint64_t* kt_full = bars + 2;
-    uint64_t* kt_empty = bars + 3;
-    uint64_t* tm_full = bars + 4;
-    uint64_t* tm_empty = bars + 5;
-    uint64_t* va_full = bars + 6;   // [2]: V and aux of a chunk landed
-    uint64_t* va_empty = bars + 8;  // [2]: the chunk's V and aux were read
-    uint64_t* mma_done = bars + 10;  // [3]
-    uint32_t* tmem_slot = (uint32_t*)(bars + 13);
+    uint64_t* bar = (uint64_t*)(smem + P2_BAR);
+    uint32_t* tmem_slot = (uint32_t*)(bar + B_COUNT);
+    volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int h = blockIdx.y, kh = h % a.hk;
-    const int col0 = blockIdx.x * kSlice;
+    const int col0 = blockIdx.x * kCols;
+    const int n = a.nchunks;
 
     if (tid == 0) {
-        for (int i = 0; i < 13; ++i) dev::mbar_init(&bars[i], 1);
+        for (int i = 0; i < B_COUNT; ++i) dev::mbar_init(&bar[i], 1);
+        dev::mbar_init(&bar[B_VA_EMPTY0], 2);
+        dev::mbar_init(&bar[B_VA_EMPTY1], 2);
+        dev::mbar_init(&bar[B_SCALED], 4);
+        dev::mbar_init(&bar[B_ODONE], 4);
+        *abort_flag = 0;
         dev::fence_mbar_init();
         dev::prefetch_tensormap(&a.tm_v);
     }
     if (warp == 0) {
-        tc::tmem_alloc(tmem_slot, 128);
+        tc::tmem_alloc(tmem_slot, 512);
         tc::tmem_relinquish();
     }
     tc::fence_before_sync();
     __syncthreads();
     tc::fence_after_sync();
     const uint32_t tmem = *tmem_slot;
+    int* err = a.err;
+    auto wait = [&](int b, uint32_t parity) -> bool {
+        if (dev::mbar_wait(&bar[b], parity, err)) return true;
+        *abort_flag = 1;
+        return false;
+    };
 
-    if (warp == 4) {
+    if (warp == 8) {  // ---------------------------------------------- producer
         if (lane == 0) {
-            const int64_t krec = (int64_t)kh * a.nchunks, rec = (int64_t)h * a.nchunks;
-            for (int c = 0; c < a.nchunks; ++c) {
+            const int64_t krec = (int64_t)kh * n, rec = (int64_t)h * n;
+            for (int c = 0; c < n && !*abort_flag; ++c) {
                 const int s = c & 1;
-                if (c >= 2 && !dev::mbar_wait(&va_empty[s], ((c >> 1) - 1) & 1, a.err)) break;
-                dev::mbar_arrive_expect_tx(&va_full[s], kAuxBytes + kVBytes);
-                dev::bulk_g2s(smem + P2_AUX + s * kAuxBytes, a.aux + (rec + c) * (kAuxBytes / 4), kAuxBytes,
-                              &va_full[s]);
-                dev::tma_load_3d(smem + P2_V + s * kVBytes, &a.tm_v, col0, h, c * kC, &va_full[s]);
                 const uint32_t prev = (uint32_t)(c - 1) & 1u;
-                if (c >= 1 && !dev::mbar_wait(kq_empty, prev, a.err)) break;
-                dev::mbar_arrive_expect_tx(kq_full, kKQBytes);
-                dev::bulk_g2s(smem + P2_KQ, a.kq_img + (krec + c) * (kKQBytes / 4), kKQBytes, kq_full);
-                if (c >= 1 && !dev::mbar_wait(tm_empty, prev, a.err)) break;
-                dev::mbar_arrive_expect_tx(tm_full, kTMBytes);
-                dev::bulk_g2s(smem + P2_TM, a.tm_img + (rec + c) * (kTMBytes / 4), kTMBytes, tm_full);
-                if (c >= 1 && !dev::mbar_wait(kt_empty, prev, a.err)) break;
-                dev::mbar_arrive_expect_tx(kt_full, kKTBytes);
-                dev::bulk_g2s(smem + P2_KT, a.kt_img + (krec + c) * (kKTBytes / 4), kKTBytes, kt_full);
+                if (c >= 2 && !wait(B_VA_EMPTY0 + s, (uint32_t)((c >> 1) - 1) & 1u)) break;
+                dev::mbar_arrive_expect_tx(&bar[B_VA_FULL0 + s], kAuxBytes + kVTile);
+                dev::bulk_g2s(smem + P2_AUX + s * kAuxBytes, a.aux + (rec + c) * (kAuxBytes / 4), kAuxBytes,
+                              &bar[B_VA_FULL0 + s]);
+                for (int b = 0; b < 4; ++b)
+                    dev::tma_load_3d(smem + P2_V + s * kVTile + b * 8192, &a.tm_v, col0 + 32 * b, h, c * kC,
+                                     &bar[B_VA_FULL0 + s]);
+                if (c >= 1 && !wait(B_KQ_EMPTY, prev)) break;
+                dev::mbar_arrive_expect_tx(&bar[B_KQ_FULL], kKQBytes);
+                dev::bulk_g2s(smem + P2_KQ, a.kq_img + (krec + c) * (kKQBytes / 4), kKQBytes, &bar[B_KQ_FULL]);
+                if (c >= 1 && !wait(B_TM_EMPTY, prev)) break;
+                dev::mbar_arrive_expect_tx(&bar[B_TM_FULL], kTMBytes);
+                dev::bulk_g2s(smem + P2_TM, a.tm_img + (rec + c) * (kTMBytes / 4), kTMBytes, &bar[B_TM_FULL]);
+                if (c >= 1 && !wait(B_KT_EMPTY, prev)) break;
+                dev::mbar_arrive_expect_tx(&bar[B_KT_FULL], kKTBytes);
+                dev::bulk_g2s(smem + P2_KT, a.kt_img + (krec + c) * (kKTBytes / 4), kKTBytes, &bar[B_KT_FULL]);
             }
         }
     } else {
-        const uint32_t lanes = (uint32_t)(warp * 32) << 16;
-        uint8_t* Simg = smem + P2_S;
-        uint8_t* Rimg = smem + P2_R;
-        const uint32_t s_addr = dev::smem_u32(Simg), r_addr = dev::smem_u32(Rimg);
+        const int j = tid & 127;                     // value column (TMEM lane)
+        const uint32_t lanes = (uint32_t)((warp & 3) * 32) << 16;
+        const bool col_ok = col0 + j < a.dv;
         const uint32_t kq_addr = dev::smem_u32(smem + P2_KQ), kt_addr = dev::smem_u32(smem + P2_KT),
                        tm_addr = dev::smem_u32(smem + P2_TM);
-        constexpr uint32_t id = tc::idesc_tf32(128, kSlice, 0, 0);
-        float S[kSlice];  // state row k = tid, columns col0..col0+31
-        float* srow = a.state + ((int64_t)h * kDK + tid) * a.dv + col0;
-#pragma unroll
-        for (int q = 0; q < 8; ++q) {
-            const float4 x = ((const float4*)srow)[q];
-            S[4 * q] = x.x, S[4 * q + 1] = x.y, S[4 * q + 2] = x.z, S[4 * q + 3] = x.w;
-        }
-        store_col_image(Simg, tid, 4096, S);
-        dev::fence_proxy_async_smem();
-        tc::fence_before_sync();
-        bool failed = false;
-        bar_any_128(false);
+        constexpr uint32_t id = tc::idesc_tf32(128, 128, 0, 0);
+        float* scol = a.state + (int64_t)h * kDK * a.dv + col0 + j;  // state column j, stride dv
 
-        for (int c = 0; c < a.nchunks; ++c) {
-            const int s = c & 1;
-            const uint32_t ph = (uint32_t)c & 1u;
-            const float* AUX = (const float*)(smem + P2_AUX + s * kAuxBytes);
-            const uint8_t* V = smem + P2_V + s * kVBytes;
-            failed |= !dev::mbar_wait(&va_full[s], (uint32_t)(c >> 1) & 1u, a.err);
-            if (tid == 0) {  // MMA1: [K;Q] x S -> columns 0..31
-                tc::fence_after_sync();
-                failed |= !dev::mbar_wait(kq_full, ph, a.err);
+        if (warp < 4) {  // initial state: S^T row j <- state column j
+#pragma unroll
+            for (int b = 0; b < 4; ++b) {
+                uint32_t v[32];
+#pragma unroll
+                for (int d = 0; d < 32; ++d) v[d] = __float_as_uint(col_ok ? scol[(int64_t)(32 * b + d) * a.dv] : 0.f);
+                tc::st_32x32b_x32(tmem + lanes + TM_S + 32 * b, v);
+            }
+            tc::wait_st();
+        }
+        tc::fence_before_sync();
+        named_bar(2, 256);
+        tc::fence_after_sync();
+
+        if (warp < 4) {  // ------------------------------------- chain warpgroup
+            // The tensor pipe runs one thread's MMAs in order and an M = 128
+            // MMA costs about the same for any N up to 128, so each product is
+            // one N = 128 sequence: X | QS, then D | M T R, then the state.
+            auto issue_mma1 = [&](int c) {
+                if (!wait(B_KQ_FULL, (uint32_t)c & 1u)) return;
 #pragma unroll
                 for (int kk = 0; kk < kDK / 8; ++kk)
-                    tc::mma_tf32_ss(tmem, kmajor_desc(kq_addr, kk, 16384), kmajor_desc(s_addr, kk, 4096), id, kk > 0);
-                tc::commit(&mma_done[0]);
-                tc::commit(kq_empty);
-            }
-            failed |= !dev::mbar_wait(&mma_done[0], ph, a.err);
-            tc::fence_after_sync();
-            uint32_t x[32];  // (K S) row tid, or (Q S) row tid - 64
-            tc::ld_32x32b_x32(tmem + lanes, x);
-            const float gamma = AUX[192];
-            if (tid < kC) {
-                const float bt = AUX[tid], et = AUX[64 + tid];
-                float rr[kSlice];
-#pragma unroll
-                for (int q = 0; q < 8; ++q) {
-                    const float4 vv = *(const float4*)(V + sw_chunk(tid, q));
-                    rr[4 * q + 0] = bt * (vv.x - et * __uint_as_float(x[4 * q + 0]));
-                    rr[4 * q + 1] = bt * (vv.y - et * __uint_as_float(x[4 * q + 1]));
-                    rr[4 * q + 2] = bt * (vv.z - et * __uint_as_float(x[4 * q + 2]));
-                    rr[4 * q + 3] = bt * (vv.w - et * __uint_as_float(x[4 * q + 3]));
-                }
-                store_col_image(Rimg, tid, 4096, rr);
-            }
-            dev::fence_proxy_async_smem();
-            tc::fence_before_sync();
-            if (bar_any_128(failed)) break;
-
-            if (tid == 0) {  // MMA2: [T;MT] x R -> columns 32..63
+                    tc::mma_tf32_ts(tmem + TM_P, tmem + TM_S + 8 * kk, kmajor_desc(kq_addr, kk, 16384), id, kk > 0);
+                tc::commit(&bar[B_MMA1]);
+                tc::commit(&bar[B_KQ_EMPTY]);
+            };
+            if (tid == 0) issue_mma1(0);
+            for (int c = 0; c < n; ++c) {
+                if (*abort_flag) break;
+                const int s = c & 1;
+                const uint32_t ph = (uint32_t)c & 1u;
+                const float4* AUX4 = (const float4*)(smem + P2_AUX + s * kAuxBytes);
+                const uint8_t* V = smem + P2_V + s * kVTile + (j >> 5) * 8192;
+                wait(B_VA_FULL0 + s, (uint32_t)(c >> 1) & 1u);
+                wait(B_MMA1, ph);
                 tc::fence_after_sync();
-                failed |= !dev::mbar_wait(tm_full, ph, a.err);
+                // R^T row j: beta_t (V[t][j] - e_t X[t][j])
 #pragma unroll
-                for (int kk = 0; kk < kC / 8; ++kk)
-                    tc::mma_tf32_ss(tmem + 32, kmajor_desc(tm_addr, kk, 16384), kmajor_desc(r_addr, kk, 4096), id,
-                                    kk > 0);
-                tc::commit(&mma_done[1]);
-                tc::commit(tm_empty);
-            }
-            failed |= !dev::mbar_wait(&mma_done[1], ph, a.err);
-            tc::fence_after_sync();
-            uint32_t y[32];  // D row tid, or (M T R) row tid - 64
-            tc::ld_32x32b_x32(tmem + lanes + 32, y);
-            if (tid < kC) {
-                const float ft = AUX[128 + tid];
-                float dd[kSlice];
+                for (int half = 0; half < 2; ++half) {
+                    uint32_t x[32];
+                    tc::ld_32x32b_x32(tmem + lanes + TM_P + 32 * half, x);
 #pragma unroll
-                for (int j = 0; j < kSlice; ++j) dd[j] = ft * __uint_as_float(y[j]);
-                store_col_image(Rimg, tid, 4096, dd);
-            } else {
-                const int t = tid - kC;
-                const int64_t row = (int64_t)c * kC + t;
-                const float et = AUX[64 + t];
-                if (row < a.T) {
-                    float4* o = (float4*)(a.out + (row * a.hv + h) * a.dv + col0);
+                    for (int i4 = 0; i4 < 8; ++i4) {
+                        const float4 b4 = AUX4[8 * half + i4], e4 = AUX4[16 + 8 * half + i4];
+                        const float bb[4] = {b4.x, b4.y, b4.z, b4.w}, ee[4] = {e4.x, e4.y, e4.z, e4.w};
 #pragma unroll
-                    for (int q = 0; q < 8; ++q)
-                        o[q] = make_float4(fmaf(et, __uint_as_float(x[4 * q + 0]), __uint_as_float(y[4 * q + 0])),
-                                           fmaf(et, __uint_as_float(x[4 * q + 1]), __uint_as_float(y[4 * q + 1])),
-                                           fmaf(et, __uint_as_float(x[4 * q + 2]), __uint_as_float(y[4 * q + 2])),
-                                           fmaf(et, __uint_as_float(x[4 * q + 3]), __uint_as_float(y[4 * q + 3])));
+                        for (int u = 0; u < 4; ++u) {
+                            const int i = 4 * i4 + u, t = 32 * half + i;
+                            const float vt = *(const float*)(V + sw_elem(t, j & 31));
+                            x[i] = __float_as_uint(tf32r(bb[u] * (vt - ee[u] * __uint_as_float(x[i]))));
+                        }
+                    }
+                    tc::st_32x32b_x32(tmem + lanes + TM_RD + 32 * half, x);
+                }
+                tc::wait_st();
+                tc::fence_before_sync();
+                named_bar(1, 128);
+                if (tid == 0) {  // MMA2 (after O has read the previous M T R)
+                    tc::fence_after_sync();
+                    if (c >= 1) wait(B_ODONE, (uint32_t)(c - 1) & 1u);
+                    wait(B_TM_FULL, ph);
+#pragma unroll
+                    for (int kk = 0; kk < kC / 8; ++kk)
+                        tc::mma_tf32_ts(tmem + TM_D2, tmem + TM_RD + 8 * kk, kmajor_desc(tm_addr, kk, 16384), id,
+                                        kk > 0);
+                    tc::commit(&bar[B_MMA2]);
+                    tc::commit(&bar[B_TM_EMPTY]);
+                }
+                wait(B_MMA2, ph);
+                tc::fence_after_sync();
+                // (f D)^T row j, over R^T
+#pragma unroll
+                for (int half = 0; half < 2; ++half) {
+                    uint32_t y[32];
+                    tc::ld_32x32b_x32(tmem + lanes + TM_D2 + 32 * half, y);
+#pragma unroll
+                    for (int i4 = 0; i4 < 8; ++i4) {
+                        const float4 f4 = AUX4[32 + 8 * half + i4];
+                        const float ff[4] = {f4.x, f4.y, f4.z, f4.w};
+#pragma unroll
+                        for (int u = 0; u < 4; ++u)
+                            y[4 * i4 + u] = __float_as_uint(tf32r(ff[u] * __uint_as_float(y[4 * i4 + u])));
+                    }
+                    tc::st_32x32b_x32(tmem + lanes + TM_RD + 32 * half, y);
+                }
+                tc::wait_st();
+                tc::fence_before_sync();
+                named_bar(1, 128);
+                if (tid == 0) {  // MMA3 (onto the rescaled state), then the next chunk's MMA1
+                    tc::fence_after_sync();
+                    dev::mbar_arrive(&bar[B_VA_EMPTY0 + s]);
+                    wait(B_SCALED, ph);
+                    wait(B_KT_FULL, ph);
+#pragma unroll
+                    for (int kk = 0; kk < kC / 8; ++kk)
+                        tc::mma_tf32_ts(tmem + TM_S, tmem + TM_RD + 8 * kk, kmajor_desc(kt_addr, kk, 16384), id, 1);
+                    tc::commit(&bar[B_KT_EMPTY]);
+                    if (c + 1 < n)
+                        issue_mma1(c + 1);
+                    else
+                        tc::commit(&bar[B_MMA3]);
                 }
             }
-            dev::fence_proxy_async_smem();
-            tc::fence_before_sync();
-            if (bar_any_128(failed)) break;
-
-            if (tid == 0) {  // MMA3: K^T x (f D) -> columns 64..95
+        } else {  // --------------------------------------- state / output warpgroup
+            for (int c = 0; c < n; ++c) {
+                if (*abort_flag) break;
+                const int s = c & 1;
+                const uint32_t ph = (uint32_t)c & 1u;
+                const float* AUX = (const float*)(smem + P2_AUX + s * kAuxBytes);
+                wait(B_VA_FULL0 + s, (uint32_t)(c >> 1) & 1u);
+                wait(B_MMA1, ph);
                 tc::fence_after_sync();
-                dev::mbar_arrive(&va_empty[s]);
-                failed |= !dev::mbar_wait(kt_full, ph, a.err);
+                float o[kC];  // e_t (Q S)[t][j], then + (M T R)[t][j]
 #pragma unroll
-                for (int kk = 0; kk < kC / 8; ++kk)
-                    tc::mma_tf32_ss(tmem + 64, kmajor_desc(kt_addr, kk, 16384), kmajor_desc(r_addr, kk, 4096), id,
-                                    kk > 0);
-                tc::commit(&mma_done[2]);
-                tc::commit(kt_empty);
+                for (int half = 0; half < 2; ++half) {
+                    uint32_t x[32];
+                    tc::ld_32x32b_x32(tmem + lanes + TM_P + 64 + 32 * half, x);
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) o[32 * half + i] = AUX[64 + 32 * half + i] * __uint_as_float(x[i]);
+                }
+                const float gamma = AUX[192];
+#pragma unroll
+                for (int b = 0; b < 4; ++b) {  // S^T <- exp(G_last) S^T before MMA3 adds the chunk
+                    uint32_t v[32];
+                    tc::ld_32x32b_x32(tmem + lanes + TM_S + 32 * b, v);
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) v[i] = __float_as_uint(gamma * __uint_as_float(v[i]));
+                    tc::st_32x32b_x32(tmem + lanes + TM_S + 32 * b, v);
+                }
+                tc::wait_st();
+                tc::fence_before_sync();
+                __syncwarp();
+                if (lane == 0) dev::mbar_arrive(&bar[B_SCALED]);
+                wait(B_MMA2, ph);
+                tc::fence_after_sync();
+#pragma unroll
+                for (int half = 0; half < 2; ++half) {
+                    uint32_t y[32];
+                    tc::ld_32x32b_x32(tmem + lanes + TM_D2 + 64 + 32 * half, y);
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) o[32 * half + i] += __uint_as_float(y[i]);
+                }
+                tc::fence_before_sync();
+                __syncwarp();
+                if (lane == 0) dev::mbar_arrive(&bar[B_ODONE]);
+                if (tid == 128) dev::mbar_arrive(&bar[B_VA_EMPTY0 + s]);
+                if (col_ok) {
+                    const int64_t t0 = (int64_t)c * kC;
+                    const int tn = a.T - t0 < kC ? (int)(a.T - t0) : kC;
+                    float* op = a.out + (t0 * a.hv + h) * (int64_t)a.dv + col0 + j;
+                    const int64_t step = (int64_t)a.hv * a.dv;
+#pragma unroll
+                    for (int t = 0; t < kC; ++t)
+                        if (t < tn) op[t * step] = o[t];
+                }
             }
-            failed |= !dev::mbar_wait(&mma_done[2], ph, a.err);
-            tc::fence_after_sync();
-            uint32_t u[32];
-            tc::ld_32x32b_x32(tmem + lanes + 64, u);
-#pragma unroll
-            for (int j = 0; j < kSlice; ++j) S[j] = fmaf(gamma, S[j], __uint_as_float(u[j]));
-            store_col_image(Simg, tid, 4096, S);
-            dev::fence_proxy_async_smem();
-            tc::fence_before_sync();
-            if (bar_any_128(failed)) break;
         }
-        if (!failed) {
+        // final state: S^T row j -> state column j
+        if (warp < 4) {
+            if (!*abort_flag && wait(B_MMA3, 0)) {
+                tc::fence_after_sync();
 #pragma unroll
-            for (int q = 0; q < 8; ++q)
-                ((float4*)srow)[q] = make_float4(S[4 * q], S[4 * q + 1], S[4 * q + 2], S[4 * q + 3]);
+                for (int b = 0; b < 4; ++b) {
+                    uint32_t v[32];
+                    tc::ld_32x32b_x32(tmem + lanes + TM_S + 32 * b, v);
+                    if (col_ok)
+#pragma unroll
+                        for (int d = 0; d < 32; ++d) scol[(int64_t)(32 * b + d) * a.dv] = __uint_as_float(v[d]);
+                }
+            }
         }
     }
     tc::fence_before_sync();
     __syncthreads();
     if (warp == 0) {
         tc::fence_after_sync();
-        tc::tmem_dealloc(tmem, 128);
+        tc::tmem_dealloc(tmem, 512);
     }
 }
 
@@ -570,14 +618,14 @@ int encode_f32_3d(EncodeTiledFn enc, CUtensorMap* map, const float* base, int in
 
 }  // namespace
 
-bool delta_chunked_supported(const nmg_delta_state* st) { return st->dk == kDK && st->dv % kSlice == 0; }
+bool delta_chunked_supported(const nmg_delta_state* st) { return st->dk == kDK && st->dv % 32 == 0; }
 
 int delta_prefill_chunked(nmg_delta_state* st, int hk, int64_t T, const float* q, const float* k, const float* v,
                           const float* gate, const float* beta, float* out, int chunk, cudaStream_t stream) {
     if (chunk != kC) return set_error(NMG_UNSUPPORTED, "chunked delta prefill: chunk must be %d", kC);
     if (!delta_chunked_supported(st))
         return set_error(NMG_UNSUPPORTED, "chunked delta prefill: built for Dk=%d and Dv a multiple of %d (got %d, %d)",
-                         kDK, kSlice, st->dk, st->dv);
+                         kDK, 32, st->dk, st->dv);
     if (!q || !k || !v || !gate || !beta || !out)
         return set_error(NMG_INVALID_ARGUMENT, "nmg_delta_prefill: null argument");
     if (((uintptr_t)q | (uintptr_t)k | (uintptr_t)v | (uintptr_t)out) & 15)
@@ -634,9 +682,11 @@ int delta_prefill_chunked(nmg_delta_state* st, int hk, int64_t T, const float* q
         NMG_CUDA_TRY(cudaFuncSetAttribute(delta_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, P2_SMEM));
         attr_set |= dbit;
     }
-    delta_wy_kernel<<<dim3(nchunks, hv), 128, P1_SMEM, stream>>>(wa);
+    // one CTA per (value head, chunk); the heads of a chunk run side by side so
+    // the value heads that share a key head read its tiles while L2 holds them
+    delta_wy_kernel<<<(unsigned)((int64_t)nchunks * hv), 128, P1_SMEM, stream>>>(wa);
     NMG_CUDA_TRY(cudaGetLastError());
-    delta_scan_kernel<<<dim3(dv / kSlice, hv), 160, P2_SMEM, stream>>>(sa);
+    delta_scan_kernel<<<dim3((dv + kCols - 1) / kCols, hv), 288, P2_SMEM, stream>>>(sa);
     NMG_CUDA_TRY(cudaGetLastError());
     return NMG_OK;
 }
