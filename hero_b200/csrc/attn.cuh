@@ -71,6 +71,86 @@ __device__ __forceinline__ void load_row_chunk(const typename dev::Elem<DT>::T* 
     }
 }
 
+// ---- merging split-KV partials -------------------------------------------
+// Block-wide max / sum over NT threads; `red` holds NT / 32 floats.
+template <int NT>
+__device__ __forceinline__ float block_max(float v, float* red) {
+    v = dev::warp_max(v);
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+    __syncthreads();
+    float r = red[0];
+#pragma unroll
+    for (int i = 1; i < NT / 32; ++i) r = fmaxf(r, red[i]);
+    return r;
+}
+template <int NT>
+__device__ __forceinline__ float block_sum(float v, float* red) {
+    v = dev::warp_sum(v);
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+    __syncthreads();
+    float r = red[0];
+#pragma unroll
+    for (int i = 1; i < NT / 32; ++i) r += red[i];
+    return r;
+}
+
+constexpr int kMergeChunk = 256;  // split weights staged per pass
+
+// The last CTA of a query row combines the row's split partials.  Split sp's
+// record for group g sits at part + sp * sp_stride + g * (DH + 2): DH
+// weighted sums, then the split's running max m and sum l (natural-log units,
+// or base-2 units when LOG2).  Weights go through shared memory in chunks so
+// the loads of each pass are independent of one another (a serial walk over
+// the splits pays the L2 latency once per split).  `red` holds NT / 32
+// floats, `wbuf` kMergeChunk floats; store(g, d, value) writes the result.
+template <int NT, int DH, bool LOG2, class Store>
+__device__ void merge_partials(const float* part, int64_t sp_stride, int64_t nsplit, int ng, float* red, float* wbuf,
+                               Store&& store) {
+    constexpr int PER = (DH + NT - 1) / NT;
+    const int tid = threadIdx.x;
+    for (int g = 0; g < ng; ++g) {
+        const float* pg = part + g * (DH + 2);
+        float mx = -INFINITY;
+        for (int64_t sp = tid; sp < nsplit; sp += NT) mx = fmaxf(mx, __ldcg(pg + sp * sp_stride + DH));
+        const float M = block_max<NT>(mx, red);
+        float acc[PER];
+#pragma unroll
+        for (int k = 0; k < PER; ++k) acc[k] = 0.f;
+        float lsum = 0.f;
+        for (int64_t base = 0; base < nsplit; base += kMergeChunk) {
+            const int cnt = (int)(nsplit - base < kMergeChunk ? nsplit - base : kMergeChunk);
+            __syncthreads();
+            for (int i = tid; i < cnt; i += NT) {
+                const float* pp = pg + (base + i) * sp_stride;
+                const float m = __ldcg(pp + DH);
+                float w = 0.f;
+                if (m != -INFINITY) w = LOG2 ? exp2f(m - M) : __expf(m - M);
+                wbuf[i] = w;
+                lsum = fmaf(w, __ldcg(pp + DH + 1), lsum);
+            }
+            __syncthreads();
+#pragma unroll 4
+            for (int i = 0; i < cnt; ++i) {
+                const float w = wbuf[i];
+                const float* pp = pg + (base + i) * sp_stride;
+#pragma unroll
+                for (int k = 0; k < PER; ++k) {
+                    const int d = tid + k * NT;
+                    if (d < DH) acc[k] = fmaf(w, __ldcg(pp + d), acc[k]);
+                }
+            }
+        }
+        const float L = block_sum<NT>(lsum, red);
+#pragma unroll
+        for (int k = 0; k < PER; ++k) {
+            const int d = tid + k * NT;
+            if (d < DH) store(g, d, acc[k] / L);
+        }
+    }
+}
+
 // Split-KV launcher over one cache: rows first_query.. with visible positions
 // [max(q - window + 1, floor), min(q, newest)].  caller_scratch/bytes: when
 // non-null the kernel uses that memory instead of the library's scratch.

@@ -370,23 +370,14 @@ __global__ void __launch_bounds__(128) attn_decode_mma_kernel(const __grid_const
     __syncthreads();
     if (!s_last) return;
     __threadfence();
-    for (int i = tid; i < G * DH; i += 128) {
-        const int g = i / DH, d = i % DH;
-        float M = -INFINITY;
-        for (int64_t sp = 0; sp < r.nsplit; ++sp) {
-            const float* pp = a.part + (((r.work_first + sp) * a.hkv + h) * a.zdim + z) * (int64_t)(16 * (DH + 2));
-            M = fmaxf(M, __ldcg(pp + g * (DH + 2) + DH));
-        }
-        float L = 0.f, O = 0.f;
-        for (int64_t sp = 0; sp < r.nsplit; ++sp) {
-            const float* pp = a.part + (((r.work_first + sp) * a.hkv + h) * a.zdim + z) * (int64_t)(16 * (DH + 2));
-            const float mi = __ldcg(pp + g * (DH + 2) + DH);
-            if (mi == -INFINITY) continue;
-            const float f = ex2f(mi - M);
-            L += __ldcg(pp + g * (DH + 2) + DH + 1) * f;
-            O += __ldcg(pp + g * (DH + 2) + d) * f;
-        }
-        dev::store_from_f32(a.out, a.out_dtype, (r.qrow * (int64_t)a.hq + qh0 + g) * DH + d, O / L);
+    {
+        __shared__ float red[4], wbuf[kMergeChunk];
+        const float* first = a.part + (((r.work_first) * a.hkv + h) * a.zdim + z) * (int64_t)(16 * (DH + 2));
+        merge_partials<128, DH, true>(first, (int64_t)a.hkv * a.zdim * (16 * (DH + 2)), r.nsplit, G, red, wbuf,
+                                      [&](int g, int d, float v) {
+                                          dev::store_from_f32(a.out, a.out_dtype,
+                                                              (r.qrow * (int64_t)a.hq + qh0 + g) * DH + d, v);
+                                      });
     }
     if (tid == 0) a.counters[cnt_idx] = 0;
 }
