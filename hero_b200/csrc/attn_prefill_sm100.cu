@@ -11,12 +11,13 @@
 //   warp 1      allocates TMEM and issues tcgen05.mma from one thread:
 //                 S_j = Q K_j^T  (M=128, N=BN, K=DH)  into TMEM (two S buffers)
 //                 O  += P_j V_j  (M=128, N=DH, K=BN)  A = P_j read from TMEM
-//   warps 3..10 softmax: two warps share each 32-row TMEM lane quadrant and
-//               split every S row in halves (columns [0, BN/2) and [BN/2, BN));
-//               the halves swap their block maxima through shared memory, so
-//               both apply the same running max.  Each thread reads its half
-//               row from TMEM, applies the causal/window mask, an online
-//               softmax in base 2
+//   warps 3..   softmax: PARTS warps (4 for head_dim 128, 2 for 256) share
+//               each 32-row TMEM lane quadrant and split every S row into
+//               PARTS column ranges; they swap their block maxima through
+//               shared memory, so all apply the same running max (four warps
+//               per scheduler hide each other's TMEM and barrier latency).
+//               Each thread reads its part of the row from TMEM, applies the
+//               causal/window mask, an online softmax in base 2
 //               (rescaling O in TMEM only when the running max grows by more
 //               than 2^8), writes P as packed fp16 pairs into TMEM over the
 //               S buffer it came from (V is fp16 in every 16-bit cache, so
@@ -49,14 +50,17 @@ struct PfCfg {
     static constexpr int K_OFF = Q_OFF + Q_BYTES;
     static constexpr int V_OFF = K_OFF + KST * K_BYTES;
     static constexpr int BAR_OFF = V_OFF + VST * V_BYTES;
-    // q_full, k_full/k_empty[KST], v_full/v_empty[VST], s_full[2], p_full[2], o_done, pair[4]
+    // q_full, k_full/k_empty[KST], v_full/v_empty[VST], s_full[2], p_full[2], o_done, quad[4]
     static constexpr int NBARS = 1 + 2 * KST + 2 * VST + 2 + 2 + 1 + 4;
     static constexpr int TMEMPTR_OFF = BAR_OFF + NBARS * 8;
-    static constexpr int RED_OFF = TMEMPTR_OFF + 16;              // float [2 parity][2 halves][BM]
-    static constexpr int SMEM = RED_OFF + 2 * 2 * BM * 4 + 1024;  // + slack to align the base to 1024
-    static constexpr int SOFTMAX_THREADS = 256;
-    static constexpr int THREADS = 96 + SOFTMAX_THREADS;  // K producer, MMA, V producer, 8 softmax warps
-    static constexpr int HALF_N = BN / 2, HALF_D = DH / 2;
+    // Softmax warps per TMEM lane quadrant: each owns PART_N keys of a score
+    // row and PART_D columns of its output row.
+    static constexpr int PARTS = DH == 128 ? 4 : 2;
+    static constexpr int RED_OFF = TMEMPTR_OFF + 16;                  // float [2 parity][PARTS][BM]
+    static constexpr int SMEM = RED_OFF + 2 * PARTS * BM * 4 + 1024;  // + slack to align the base to 1024
+    static constexpr int SOFTMAX_THREADS = 128 * PARTS;
+    static constexpr int THREADS = 96 + SOFTMAX_THREADS;  // K producer, MMA, V producer, softmax warps
+    static constexpr int PART_N = BN / PARTS, PART_D = DH / PARTS;
     static constexpr uint32_t TMEM_COLS = 512;
     static constexpr uint32_t O_COL = 2 * BN;
     static_assert(O_COL + DH <= 512, "TMEM budget");
@@ -98,7 +102,7 @@ __device__ __forceinline__ int64_t vis_lo(const PrefillArgs& a, int64_t q) {
 __device__ __forceinline__ int64_t vis_hi(const PrefillArgs& a, int64_t q) { return q < a.newest ? q : a.newest; }
 
 template <int DH, bool BF16>
-__global__ void __launch_bounds__(352, 1) attn_prefill_kernel(const __grid_constant__ PrefillArgs a) {
+__global__ void __launch_bounds__(PfCfg<DH>::THREADS, 1) attn_prefill_kernel(const __grid_constant__ PrefillArgs a) {
     using C = PfCfg<DH>;
     constexpr int BM = C::BM, BN = C::BN, KST = C::KST, VST = C::VST;
     extern __shared__ unsigned char smem_raw[];
@@ -114,7 +118,7 @@ __global__ void __launch_bounds__(352, 1) attn_prefill_kernel(const __grid_const
     // two phases ahead of the MMA thread's wait on it.
     uint64_t* p_full = s_full + 2;  // [2]
     uint64_t* o_done = p_full + 2;
-    uint64_t* pair_bar = o_done + 1;  // [4], 64 arrivals each
+    uint64_t* quad_bar = o_done + 1;  // [4], one arrival per softmax thread of the quadrant
     uint32_t* tmem_slot = (uint32_t*)(smem + C::TMEMPTR_OFF);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -146,7 +150,7 @@ __global__ void __launch_bounds__(352, 1) attn_prefill_kernel(const __grid_const
         dev::mbar_init(&p_full[0], C::SOFTMAX_THREADS);
         dev::mbar_init(&p_full[1], C::SOFTMAX_THREADS);
         dev::mbar_init(o_done, 1);
-        for (int q = 0; q < 4; ++q) dev::mbar_init(&pair_bar[q], 64);
+        for (int q = 0; q < 4; ++q) dev::mbar_init(&quad_bar[q], 32 * C::PARTS);
         dev::fence_mbar_init();
     }
     if (warp == 1) {
@@ -203,6 +207,10 @@ __global__ void __launch_bounds__(352, 1) attn_prefill_kernel(const __grid_const
             // P.V runs fp16 x fp16 (V of a 16-bit cache is stored fp16), A = P from TMEM.
             constexpr uint32_t idesc_o = tc::idesc_f16(128, DH, 0, 0, 1);
             const uint32_t sbase = dev::smem_u32(smem);
+            // Descriptors are built once; each MMA only advances a start address.
+            const uint64_t q_desc = tc::smem_desc_sw128(sbase + C::Q_OFF, 16, 1024);
+            const uint64_t k_desc = tc::smem_desc_sw128(sbase + C::K_OFF, 16, 1024);
+            const uint64_t v_desc = tc::smem_desc_sw128(sbase + C::V_OFF, BN * 128, 1024);
             bool ok = dev::mbar_wait(q_full, 0, a.err);
             auto issue_pv = [&](int i) -> bool {
                 const int s = i % VST;
@@ -210,12 +218,11 @@ __global__ void __launch_bounds__(352, 1) attn_prefill_kernel(const __grid_const
                 if (!dev::mbar_wait(&v_full[s], (i / VST) & 1, a.err)) return false;
                 tc::fence_after_sync();
                 const uint32_t p_tmem = tmem + (i & 1) * BN;  // P_i overwrote S_i, 2 values per column
+                const uint64_t vs = tc::desc_advance(v_desc, s * C::V_BYTES);
 #pragma unroll
-                for (int k = 0; k < BN / 16; ++k) {
-                    const uint64_t bd =
-                        tc::smem_desc_sw128(sbase + C::V_OFF + s * C::V_BYTES + k * 2048, BN * 128, 1024);
-                    tc::mma_f16_ts(tmem + C::O_COL, p_tmem + k * 8, bd, idesc_o, (i > 0 || k > 0) ? 1u : 0u);
-                }
+                for (int k = 0; k < BN / 16; ++k)
+                    tc::mma_f16_ts(tmem + C::O_COL, p_tmem + k * 8, tc::desc_advance(vs, k * 2048), idesc_o,
+                                   (i > 0 || k > 0) ? 1u : 0u);
                 tc::commit(o_done);
                 tc::commit(&v_empty[s]);
                 return true;
@@ -226,13 +233,11 @@ __global__ void __launch_bounds__(352, 1) attn_prefill_kernel(const __grid_const
                 tc::fence_after_sync();
                 // S_i overwrites buffer sb, which held P_{i-2}; P_{i-2}.V was issued
                 // earlier and the tensor pipe executes in order.
+                const uint64_t ks = tc::desc_advance(k_desc, s * C::K_BYTES);
 #pragma unroll
-                for (int k = 0; k < DH / 16; ++k) {
-                    const uint64_t ad = tc::smem_desc_sw128(sbase + C::Q_OFF + (k / 4) * BM * 128 + (k % 4) * 32, 16, 1024);
-                    const uint64_t bd =
-                        tc::smem_desc_sw128(sbase + C::K_OFF + s * C::K_BYTES + (k / 4) * BN * 128 + (k % 4) * 32, 16, 1024);
-                    tc::mma_f16_ss(tmem + sb * BN, ad, bd, idesc_s, k > 0 ? 1u : 0u);
-                }
+                for (int k = 0; k < DH / 16; ++k)
+                    tc::mma_f16_ss(tmem + sb * BN, tc::desc_advance(q_desc, (k / 4) * BM * 128 + (k % 4) * 32),
+                                   tc::desc_advance(ks, (k / 4) * BN * 128 + (k % 4) * 32), idesc_s, k > 0 ? 1u : 0u);
                 tc::commit(&s_full[sb]);
                 tc::commit(&k_empty[s]);
                 if (i >= 1 && !issue_pv(i - 1)) {
@@ -245,27 +250,27 @@ __global__ void __launch_bounds__(352, 1) attn_prefill_kernel(const __grid_const
     } else {
         // ---------------------------------------------------- softmax warps
         const int quad = warp & 3;          // TMEM lane quadrant this warp may access
-        const int half = (warp - 3) >> 2;   // which half of each S / O row
+        const int part = (warp - 3) >> 2;   // which PART_N keys / PART_D output columns of the row
         const int row = quad * 32 + lane;
         const uint32_t t_lane = tmem + ((uint32_t)(quad * 32) << 16);
         const int64_t qpos = a.first_query + t0 + row;
         const bool row_valid = t0 + row < a.rows;
         const int64_t lo = vis_lo(a, qpos), hi = vis_hi(a, qpos);
-        float* red = (float*)(smem + C::RED_OFF);  // [parity][half][row]
-        const int col0 = half * C::HALF_N;
+        float* red = (float*)(smem + C::RED_OFF);  // [parity][part][row]
+        const int col0 = part * C::PART_N;
         float m_run = -INFINITY, l_run = 0.f;
         bool ok = true;
-        // The two warps of one quadrant exchange through red[] and meet on
-        // their pair mbarrier (completion k = exchange k; bounded wait).
-        int pair_phase = 0;
-        // The fences order this warp's TMEM reads before the partner's TMEM
-        // writes (P of one half lands on S columns of the other half).
-        auto pair_sync = [&]() -> bool {
+        // The PARTS warps of one quadrant exchange through red[] and meet on
+        // their quadrant mbarrier (completion k = exchange k; bounded wait).
+        int quad_phase = 0;
+        // The fences order this warp's TMEM reads before the other warps'
+        // TMEM writes (P of one part lands on S columns of another).
+        auto quad_sync = [&]() -> bool {
             tc::fence_before_sync();
-            dev::mbar_arrive(&pair_bar[quad]);
-            const bool done = __all_sync(0xffffffffu, dev::mbar_wait(&pair_bar[quad], pair_phase & 1, a.err));
+            dev::mbar_arrive(&quad_bar[quad]);
+            const bool done = __all_sync(0xffffffffu, dev::mbar_wait(&quad_bar[quad], quad_phase & 1, a.err));
             tc::fence_after_sync();
-            ++pair_phase;
+            ++quad_phase;
             return done;
         };
 
@@ -279,32 +284,36 @@ __global__ void __launch_bounds__(352, 1) attn_prefill_kernel(const __grid_const
                 break;
             }
             tc::fence_after_sync();
-            float x[C::HALF_N];
+            // Raw scores: the maximum is taken before scaling (scale_log2 > 0)
+            // and the scale is folded into the exponent's FFMA below.
+            float x[C::PART_N];
 #pragma unroll
-            for (int c = 0; c < C::HALF_N / 32; ++c) {
+            for (int c = 0; c < C::PART_N / 32; ++c) {
                 uint32_t r[32];
                 tc::ld_32x32b_x32(t_lane + sb * BN + col0 + c * 32, r);
 #pragma unroll
-                for (int e = 0; e < 32; ++e) x[c * 32 + e] = __uint_as_float(r[e]) * a.scale_log2;
+                for (int e = 0; e < 32; ++e) x[c * 32 + e] = __uint_as_float(r[e]);
             }
 
             const int64_t p0 = a.base + (j_begin + i) * BN + col0;
             if (!(p0 - col0 >= full_lo && p0 - col0 + BN - 1 <= full_hi)) {
 #pragma unroll
-                for (int e = 0; e < C::HALF_N; ++e) {
+                for (int e = 0; e < C::PART_N; ++e) {
                     const int64_t pos = p0 + e;
                     if (pos < lo || pos > hi) x[e] = -INFINITY;
                 }
             }
             float mb = x[0];
 #pragma unroll
-            for (int e = 1; e < C::HALF_N; ++e) mb = fmaxf(mb, x[e]);
-            red[(sb * 2 + half) * BM + row] = mb;
-            if (!pair_sync()) {
+            for (int e = 1; e < C::PART_N; ++e) mb = fmaxf(mb, x[e]);
+            mb *= a.scale_log2;
+            red[(sb * C::PARTS + part) * BM + row] = mb;
+            if (!quad_sync()) {
                 ok = false;
                 break;
             }
-            mb = fmaxf(mb, red[(sb * 2 + (half ^ 1)) * BM + row]);
+#pragma unroll
+            for (int q2 = 0; q2 < C::PARTS; ++q2) mb = fmaxf(mb, red[(sb * C::PARTS + q2) * BM + row]);
             const float m_new = fmaxf(m_run, mb);
             const bool rescale = m_new > m_run + 8.0f;  // also true for the first finite block
             float alpha = 1.f;
@@ -314,10 +323,10 @@ __global__ void __launch_bounds__(352, 1) attn_prefill_kernel(const __grid_const
             }
             const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
             float sum = 0.f;
-            uint32_t pk[C::HALF_N / 2];
+            uint32_t pk[C::PART_N / 2];
 #pragma unroll
-            for (int e = 0; e < C::HALF_N; e += 2) {
-                const float p0v = ex2(x[e] - m_use), p1v = ex2(x[e + 1] - m_use);
+            for (int e = 0; e < C::PART_N; e += 2) {
+                const float p0v = ex2(fmaf(x[e], a.scale_log2, -m_use)), p1v = ex2(fmaf(x[e + 1], a.scale_log2, -m_use));
                 sum += p0v + p1v;
                 pk[e / 2] = pack2(p0v, p1v, false);
             }
@@ -335,19 +344,19 @@ __global__ void __launch_bounds__(352, 1) attn_prefill_kernel(const __grid_const
             if (i >= 1 && __any_sync(0xffffffffu, rescale)) {
                 tc::fence_after_sync();
 #pragma unroll 1
-                for (int c = 0; c < C::HALF_D / 32; ++c) {
+                for (int c = 0; c < C::PART_D / 32; ++c) {
                     uint32_t r[32];
-                    const uint32_t col = C::O_COL + half * C::HALF_D + c * 32;
+                    const uint32_t col = C::O_COL + part * C::PART_D + c * 32;
                     tc::ld_32x32b_x32(t_lane + col, r);
 #pragma unroll
                     for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * alpha);
                     tc::st_32x32b_x32(t_lane + col, r);
                 }
             }
-            // P_i (fp16 pairs) over the first half of S_i's columns: this half
-            // row's keys [col0, col0 + HALF_N) -> columns [col0/2, col0/2 + HALF_N/2).
+            // P_i (fp16 pairs) over the first half of S_i's columns: this
+            // part's keys [col0, col0 + PART_N) -> columns [col0/2, col0/2 + PART_N/2).
             const uint32_t pcol = t_lane + sb * BN + col0 / 2;
-            if constexpr (C::HALF_N / 2 == 32) {
+            if constexpr (C::PART_N / 2 == 32) {
                 tc::st_32x32b_x32(pcol, *reinterpret_cast<const uint32_t(*)[32]>(pk));
             } else {
                 tc::st_32x32b_x16(pcol, pk);
@@ -357,20 +366,22 @@ __global__ void __launch_bounds__(352, 1) attn_prefill_kernel(const __grid_const
             dev::mbar_arrive(&p_full[sb]);
         }
 
-        // Row sum = both halves' partial sums.  The slot of parity nblk & 1 was
-        // last read for block nblk - 2, which both warps are past.
+        // Row sum = the parts' partial sums.  The slot of parity nblk & 1 was
+        // last read for block nblk - 2, which every part is past.
         const int ls = nblk & 1;
-        red[(ls * 2 + half) * BM + row] = l_run;
-        if (ok) ok = pair_sync();
-        const float l_row = l_run + red[(ls * 2 + (half ^ 1)) * BM + row];
+        red[(ls * C::PARTS + part) * BM + row] = l_run;
+        if (ok) ok = quad_sync();
+        float l_row = 0.f;
+#pragma unroll
+        for (int q2 = 0; q2 < C::PARTS; ++q2) l_row += red[(ls * C::PARTS + q2) * BM + row];
         if (ok && nblk > 0 && __all_sync(0xffffffffu, dev::mbar_wait(o_done, (nblk - 1) & 1, a.err))) {
             tc::fence_after_sync();
             const float inv = 1.f / l_row;
-            const int64_t obase = ((t0 + row) * (int64_t)a.hq + h) * DH + half * C::HALF_D;
+            const int64_t obase = ((t0 + row) * (int64_t)a.hq + h) * DH + part * C::PART_D;
 #pragma unroll 1
-            for (int c = 0; c < C::HALF_D / 32; ++c) {
+            for (int c = 0; c < C::PART_D / 32; ++c) {
                 uint32_t r[32];
-                tc::ld_32x32b_x32(t_lane + C::O_COL + half * C::HALF_D + c * 32, r);
+                tc::ld_32x32b_x32(t_lane + C::O_COL + part * C::PART_D + c * 32, r);
                 if (row_valid) {
                     if (a.out_dtype == NMG_F32) {
                         float4* dst = (float4*)((float*)a.out + obase + c * 32);

@@ -38,6 +38,11 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr, uint32_t lbo
     return d;
 }
 
+// A descriptor advanced by `bytes` (a multiple of 16) along its start
+// address; valid while the address stays inside the 256 KB the 14-bit field
+// spans, so no carry reaches the other fields.
+__device__ __forceinline__ uint64_t desc_advance(uint64_t desc, uint32_t bytes) { return desc + (bytes >> 4); }
+
 // Instruction descriptor for kind::f16 with an fp32 accumulator.
 //   ab_bf16: 1 = bf16 operands, 0 = fp16;  a_mn/b_mn: 1 = MN-major operand.
 __host__ __device__ constexpr uint32_t idesc_f16(int m, int n, int ab_bf16, int a_mn, int b_mn) {
