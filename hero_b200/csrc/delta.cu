@@ -16,64 +16,80 @@ namespace nmg {
 namespace {
 
 // ---- one token, every head ---------------------------------------------------
-// grid (heads, ceil(dv/32)); 8 warps; lane = column, warp w owns rows
-// [w*RPW, (w+1)*RPW).  Two partial-sum reductions across the 8 warps.
+// grid (heads, ceil(dv/32)); 4 warps, each owning 8 value columns.  Lane =
+// (column cg = lane & 7) x (row group rg = lane >> 3): a thread holds rows
+// [rg * RPT, (rg + 1) * RPT) of one state column in registers, so both
+// reductions over the Dk rows are two xor-shuffles (no shared memory, no
+// block barrier).  Launched with programmatic stream serialisation: the wait
+// below lets the launch overlap the previous kernel's tail, and no input is
+// read before it (the previous kernel may be the one producing q, k, v).
 template <int DK>
-__global__ void __launch_bounds__(256) delta_step_kernel(float* __restrict__ state, int dv, int hk,
+__global__ void __launch_bounds__(128) delta_step_kernel(float* __restrict__ state, int dv, int hk,
                                                          const float* __restrict__ q, const float* __restrict__ k,
                                                          const float* __restrict__ v, const float* __restrict__ gate,
                                                          const float* __restrict__ beta, float* __restrict__ out,
                                                          int64_t head_stride_q) {
-    constexpr int RPW = (DK + 7) / 8;
-    __shared__ float red[8][32];
-    __shared__ float col[32];
+    constexpr int RPT = (DK + 3) / 4;
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const int h = blockIdx.x;
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-    const int j = blockIdx.y * 32 + lane;
+    const int cg = lane & 7, rg = lane >> 3;
+    const int j = blockIdx.y * 32 + w * 8 + cg;
     const bool cv = j < dv;
     const int kh = h % hk;
-    const float* kk = k + kh * head_stride_q;
-    const float* qq = q + kh * head_stride_q;
-    float* S = state + (int64_t)h * DK * dv;
+    const int i0 = rg * RPT;
+    const float* kk = k + kh * head_stride_q + i0;
+    const float* qq = q + kh * head_stride_q + i0;
+    float* S = state + ((int64_t)h * DK + i0) * dv + j;
     const float decay = __expf(gate[h]);
+    const float b = beta[h];
+    const float vj = cv ? v[(int64_t)h * dv + j] : 0.f;
 
-    float s[RPW];
+    float kr[RPT], qr[RPT], s[RPT];
+#pragma unroll
+    for (int r = 0; r < RPT; ++r) {
+        const bool in = i0 + r < DK;
+        kr[r] = in ? __ldg(kk + r) : 0.f;
+        qr[r] = in ? __ldg(qq + r) : 0.f;
+        s[r] = (in && cv) ? S[(int64_t)r * dv] : 0.f;
+    }
     float part = 0.f;
 #pragma unroll
-    for (int r = 0; r < RPW; ++r) {
-        const int i = w * RPW + r;
-        s[r] = (cv && i < DK) ? S[(int64_t)i * dv + j] * decay : 0.f;
-        if (i < DK) part = fmaf(s[r], __ldg(kk + i), part);
+    for (int r = 0; r < RPT; ++r) {
+        s[r] *= decay;
+        part = fmaf(s[r], kr[r], part);
     }
-    red[w][lane] = part;
-    __syncthreads();
-    if (w == 0) {
-        float p = 0.f;
+    part += __shfl_xor_sync(0xffffffffu, part, 8);
+    part += __shfl_xor_sync(0xffffffffu, part, 16);
+    const float d = (vj - part) * b;
+    float o = 0.f;
 #pragma unroll
-        for (int x = 0; x < 8; ++x) p += red[x][lane];
-        col[lane] = cv ? (v[(int64_t)h * dv + j] - p) * beta[h] : 0.f;
+    for (int r = 0; r < RPT; ++r) {
+        s[r] = fmaf(kr[r], d, s[r]);
+        o = fmaf(s[r], qr[r], o);
+        if (cv && i0 + r < DK) S[(int64_t)r * dv] = s[r];
     }
-    __syncthreads();
-    const float d = col[lane];
-    part = 0.f;
-#pragma unroll
-    for (int r = 0; r < RPW; ++r) {
-        const int i = w * RPW + r;
-        if (i < DK) {
-            s[r] = fmaf(__ldg(kk + i), d, s[r]);
-            part = fmaf(s[r], __ldg(qq + i), part);
-            if (cv) S[(int64_t)i * dv + j] = s[r];
-        }
-    }
-    __syncthreads();  // red[] is reused
-    red[w][lane] = part;
-    __syncthreads();
-    if (w == 0 && cv) {
-        float o = 0.f;
-#pragma unroll
-        for (int x = 0; x < 8; ++x) o += red[x][lane];
-        out[(int64_t)h * dv + j] = o;
-    }
+    o += __shfl_xor_sync(0xffffffffu, o, 8);
+    o += __shfl_xor_sync(0xffffffffu, o, 16);
+    if (rg == 0 && cv) out[(int64_t)h * dv + j] = o;
+}
+
+// Launch with programmatic stream serialisation (the kernel waits on its
+// predecessor with griddepcontrol.wait before reading anything).
+template <class... KArgs, class... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, cudaStream_t s, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
 }
 
 // ---- T tokens, state held in registers ---------------------------------------
@@ -163,6 +179,19 @@ __global__ void __launch_bounds__(128) delta_seq_kernel(float* __restrict__ stat
         default: return set_error(NMG_UNSUPPORTED, "delta rule: Dk=%d is not built", dk); \
     }
 
+#define NMG_DK_CASES_PDL(KERNEL, GRID, BLOCK, STREAM, ...)                                 \
+    switch (dk) {                                                                           \
+        case 2: NMG_CUDA_TRY(::nmg::launch_pdl(KERNEL<2>, GRID, BLOCK, STREAM, __VA_ARGS__)); break;     \
+        case 4: NMG_CUDA_TRY(::nmg::launch_pdl(KERNEL<4>, GRID, BLOCK, STREAM, __VA_ARGS__)); break;     \
+        case 8: NMG_CUDA_TRY(::nmg::launch_pdl(KERNEL<8>, GRID, BLOCK, STREAM, __VA_ARGS__)); break;     \
+        case 16: NMG_CUDA_TRY(::nmg::launch_pdl(KERNEL<16>, GRID, BLOCK, STREAM, __VA_ARGS__)); break;   \
+        case 32: NMG_CUDA_TRY(::nmg::launch_pdl(KERNEL<32>, GRID, BLOCK, STREAM, __VA_ARGS__)); break;   \
+        case 64: NMG_CUDA_TRY(::nmg::launch_pdl(KERNEL<64>, GRID, BLOCK, STREAM, __VA_ARGS__)); break;   \
+        case 128: NMG_CUDA_TRY(::nmg::launch_pdl(KERNEL<128>, GRID, BLOCK, STREAM, __VA_ARGS__)); break; \
+        case 256: NMG_CUDA_TRY(::nmg::launch_pdl(KERNEL<256>, GRID, BLOCK, STREAM, __VA_ARGS__)); break; \
+        default: return set_error(NMG_UNSUPPORTED, "delta rule: Dk=%d is not built", dk);   \
+    }
+
 bool dk_supported(int dk) { return dk == 2 || dk == 4 || dk == 8 || dk == 16 || dk == 32 || dk == 64 || dk == 128 || dk == 256; }
 
 }  // namespace
@@ -237,7 +266,7 @@ extern "C" int nmg_gated_delta_step(float* state_head, int dk, int dv, const flo
     if (dv <= 0 || !nmg::dk_supported(dk)) return set_error(NMG_UNSUPPORTED, "gated_delta_step: Dk=%d is not built", dk);
     dim3 grid(1, (dv + 31) / 32);
     cudaStream_t s = (cudaStream_t)stream;
-    NMG_DK_CASES(nmg::delta_step_kernel, grid, 256, s, state_head, dv, 1, q, k, v, gate, beta, out, (int64_t)dk)
+    NMG_DK_CASES_PDL(nmg::delta_step_kernel, grid, dim3(128), s, state_head, dv, 1, q, k, v, gate, beta, out, (int64_t)dk)
     NMG_CUDA_TRY(cudaGetLastError());
     return NMG_OK;
 }
@@ -252,7 +281,7 @@ extern "C" int nmg_delta_step(nmg_delta_state* st, int hk, const float* q, const
     int prev = 0;
     NMG_CUDA_TRY(cudaGetDevice(&prev));
     if (prev != st->device) NMG_CUDA_TRY(cudaSetDevice(st->device));
-    NMG_DK_CASES(nmg::delta_step_kernel, grid, 256, s, st->data, st->dv, hk, q, k, v, gate, beta, out, (int64_t)dk)
+    NMG_DK_CASES_PDL(nmg::delta_step_kernel, grid, dim3(128), s, st->data, st->dv, hk, q, k, v, gate, beta, out, (int64_t)dk)
     NMG_CUDA_TRY(cudaGetLastError());
     if (prev != st->device) NMG_CUDA_TRY(cudaSetDevice(prev));
     return NMG_OK;
