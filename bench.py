@@ -72,6 +72,11 @@ def ncu_traffic(name):
 # ---------------------------------------------------------------- clocks
 
 class ClockSampler:
+    """SM clocks and clock-event reasons sampled while the timed region runs.
+
+    NVML (read-only queries) from a background thread every ~2 ms; nvidia-smi
+    at 200 ms when NVML is unavailable.  Nothing here changes a GPU setting."""
+
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
@@ -79,9 +84,38 @@ class ClockSampler:
     def __init__(self, gpu_id):
         self.gpu_id = gpu_id
         self.proc = None
+        self.thread = None
+        self.rows = []  # (sm_mhz, max_mhz, set of reason names)
         self.path = os.path.join("/tmp", f"nmg_clocks_{os.getpid()}.csv")
 
+    def _nvml_loop(self, nv, h, stop):
+        bits = {"hw_slowdown": nv.nvmlClocksEventReasonHwSlowdown,
+                "hw_thermal_slowdown": nv.nvmlClocksEventReasonHwThermalSlowdown,
+                "sw_thermal_slowdown": nv.nvmlClocksEventReasonSwThermalSlowdown,
+                "sw_power_cap": nv.nvmlClocksEventReasonSwPowerCap}
+        smax = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+        while not stop.is_set():
+            try:
+                sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+                r = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                self.rows.append((float(sm), float(smax), {n for n, b in bits.items() if r & b}))
+            except Exception:
+                break
+            stop.wait(0.002)
+
     def __enter__(self):
+        import threading
+        try:
+            import pynvml as nv
+            nv.nvmlInit()
+            h = nv.nvmlDeviceGetHandleByIndex(int(self.gpu_id))
+            self.stop = threading.Event()
+            self.thread = threading.Thread(target=self._nvml_loop, args=(nv, h, self.stop), daemon=True)
+            self.thread.start()
+            time.sleep(0.01)
+            return self
+        except Exception:
+            self.thread = None
         try:
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu_id), f"--query-gpu={self.FIELDS}",
                                           "--format=csv,noheader,nounits", "-lms", "200"],
@@ -92,6 +126,9 @@ class ClockSampler:
         return self
 
     def __exit__(self, *exc):
+        if self.thread is not None:
+            self.stop.set()
+            self.thread.join(timeout=2)
         if self.proc is not None:
             time.sleep(0.25)
             self.proc.terminate()
@@ -101,23 +138,27 @@ class ClockSampler:
                 self.proc.kill()
 
     def summary(self):
-        rows = []
-        try:
-            for line in open(self.path):
-                parts = [x.strip() for x in line.split(",")]
-                if len(parts) >= 9:
-                    rows.append(parts)
-        except Exception:
-            pass
+        rows = list(self.rows)
+        src = "nvml"
+        if not rows:
+            src = "nvidia-smi"
+            names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+            try:
+                for line in open(self.path):
+                    p = [x.strip() for x in line.split(",")]
+                    if len(p) >= 9 and p[1].replace(".", "").isdigit() and p[2].replace(".", "").isdigit():
+                        rows.append((float(p[1]), float(p[2]),
+                                     {names[i] for i in range(4) if p[5 + i].lower().startswith("active")}))
+            except Exception:
+                pass
         if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
-        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
-        smax = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower().startswith("active")})
-        loaded = [s for s in sm if smax and s > 0.5 * max(smax)] or sm
-        return {"sm_mhz": float(np.median(loaded)) if loaded else None, "sm_max_mhz": max(smax) if smax else None,
-                "reasons": reasons, "samples": len(rows)}
+        sm = [r[0] for r in rows]
+        smax = max(r[1] for r in rows)
+        loaded = [x for x in sm if x > 0.5 * smax] or sm
+        reasons = sorted(set().union(*[r[2] for r in rows]))
+        return {"sm_mhz": float(np.median(loaded)), "sm_max_mhz": smax, "reasons": reasons, "samples": len(rows),
+                "source": src}
 
 
 def gpu_smi_id(torch, dev):
@@ -138,7 +179,7 @@ class RefSample:
     Inputs are generated once; `run()` times the reduction only (the cache is
     filled untimed inside the reference shim) and returns seconds."""
 
-    def __init__(self, rows_per_block=256, threads=None):
+    def __init__(self, rows_per_block=256, threads=None, full=False):
         import oracle
 
         self.threads = threads or os.cpu_count() or 1
@@ -147,9 +188,15 @@ class RefSample:
         self.q = oracle.round_bf16(oracle.normal(0, 3, S * hq * dh)).reshape(S, hq * dh)
         self.k = oracle.round_bf16(oracle.normal(0, 1, S * hkv * dh)).reshape(S, hkv * dh)
         self.v = oracle.round_bf16(oracle.normal(0, 2, S * hkv * dh)).reshape(S, hkv * dh)
-        self.blocks = np.array([S // 2 - rows_per_block // 2, rows_per_block, S - rows_per_block, rows_per_block],
-                               np.int64)
-        self.flops = c2_sample_flops(rows_per_block)
+        if full:  # every query row: the whole config-2 workload
+            self.blocks = np.array([0, S, S, 0], np.int64)
+            self.nblocks = 1
+            self.flops = c2_flops()
+        else:
+            self.blocks = np.array([S // 2 - rows_per_block // 2, rows_per_block, S - rows_per_block, rows_per_block],
+                                   np.int64)
+            self.nblocks = 2
+            self.flops = c2_sample_flops(rows_per_block)
         self.out = np.zeros_like(self.q)
         self.scale = np.float32(1 / math.sqrt(dh))
         self.R = oracle.ref()
@@ -165,20 +212,24 @@ class RefSample:
             self.kind = "port"
             self.cores = self.threads
         b = self.blocks
-        self.sample = (f"query rows [{b[0]},{b[0] + b[1]}) and [{b[2]},{S2}) of the S=4096 32q/8kv/d128 causal "
-                       f"prefill ({self.flops / 1e9:.1f} GFLOP), reduction only, {self.cores} threads")
+        if full:
+            self.sample = (f"all 4096 query rows of the S=4096 32q/8kv/d128 causal prefill "
+                           f"({self.flops / 1e9:.1f} GFLOP), reduction only, {self.cores} threads")
+        else:
+            self.sample = (f"query rows [{b[0]},{b[0] + b[1]}) and [{b[2]},{S2}) of the S=4096 32q/8kv/d128 causal "
+                           f"prefill ({self.flops / 1e9:.1f} GFLOP), reduction only, {self.cores} threads")
 
     def run(self):
         if self.R is not None:
             sec = ctypes.c_double()
             st = self.R.nmref_prefill_sample(HKV2, DH2, self.k.ctypes.data, self.v.ctypes.data, S2, self.q.ctypes.data,
-                                             HQ2, self.blocks.ctypes.data, 2, self.scale, 1, 0, self.out.ctypes.data,
+                                             HQ2, self.blocks.ctypes.data, self.nblocks, self.scale, 1, 0, self.out.ctypes.data,
                                              ctypes.byref(sec))
             if st != 0:
                 raise RuntimeError(f"reference sample failed ({st})")
             return sec.value
         total = 0.0
-        for b in range(2):
+        for b in range(self.nblocks):
             s0, n = int(self.blocks[2 * b]), int(self.blocks[2 * b + 1])
             t0 = time.perf_counter()
             self.oracle.attend(self.k[:s0 + n], self.v[:s0 + n], 0, 0, HKV2, DH2, self.q[s0:s0 + n], HQ2, s0,
@@ -191,7 +242,10 @@ def reference_arm(args, rank, world):
     if rank != 0:
         return
     t0 = time.perf_counter()
-    ref = RefSample()
+    # Each step is the whole config-2 workload (~1.5 s on 16 host threads)
+    # while the run stays within about two minutes; longer runs time the
+    # 512-row sample instead.
+    ref = RefSample(full=(args.steps + args.warmup) * 1.6 <= 120)
     for _ in range(args.warmup):
         ref.run()
     secs = [ref.run() for _ in range(args.steps)]
@@ -605,7 +659,7 @@ def extra_config5(torch, dev, small=False):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="nmg", choices=["nmg", "reference"])
     ap.add_argument("--no-extra", action="store_true", help="headline only")
@@ -652,11 +706,14 @@ def main():
             torch.cuda.empty_cache()
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
-        ref = RefSample()
-        ref.run()
-        secs = [ref.run() for _ in range(2)]
+        ref = RefSample(full=True)
+        ref.run()  # warm-up
+        secs = []
+        while sum(secs) < 10.0 or len(secs) < 2:  # about 10 s of host work
+            secs.append(ref.run())
         cpu = {"value": ref.flops / float(np.mean(secs)) / 1e12, "unit": "TFLOP/s", "cores": ref.cores,
-               "kind": ref.kind, "sample": ref.sample, "seconds_per_sample": float(np.mean(secs))}
+               "kind": ref.kind, "sample": ref.sample + f", {len(secs)} timed runs",
+               "seconds_per_sample": float(np.mean(secs))}
     if rank == 0:
         line = {"metric": METRIC, "value": res["value"], "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": res["ms_per_step"], "higher_is_better": True,
