@@ -272,7 +272,8 @@ def config2_desc(world):
     return {"workload": "config 2: causal GQA prefill, bf16 in / fp32 accumulate, K/V written to the device cache",
             "batch": 1, "seq_len": S2, "q_heads": HQ2, "kv_heads": HKV2, "head_dim": DH2,
             "flop_per_step": c2_flops(),
-            "parallelism": f"kv-head shards x{world}" + (" + NCCL all-gather of head outputs" if world > 1 else ""),
+            "parallelism": f"kv-head shards x{world}" + (" + head outputs stored into every GPU's rows by the "
+                                                          "attention epilogue (NVLink)" if world > 1 else ""),
             "l2": "inputs rotate over sets larger than the 126 MB L2"}
 
 
@@ -302,6 +303,9 @@ class Comm:
         self.lib.call("nmg_gather_heads_to_rows", ctypes.c_void_p(gathered.data_ptr()), ctypes.c_void_p(out.data_ptr()),
                       self.world, rows, row_bytes, stream)
 
+    def barrier(self, stream):
+        self.lib.call("nmg_comm_barrier", self.h, stream)
+
     def close(self):
         self.lib.lib().nmg_comm_destroy(self.h)
 
@@ -329,6 +333,15 @@ def bench_prefill(args, torch, dist, rank, world, dev):
         comm = Comm(rank, world, dev.index, torch, dist)
         gathered = torch.empty(world, S, hq_l * dh, device=dev, dtype=torch.bfloat16)
         full = torch.empty(S, hq * dh, device=dev, dtype=torch.bfloat16)
+        # Two row buffers per rank, mapped by every rank: the attention
+        # epilogue of each rank writes its heads of every row into all of
+        # them (NVLink stores), then a stream-ordered barrier.
+        shared = [nm.SharedRows(S, hq * dh, torch.bfloat16, dev.index) for _ in range(2)]
+        peers = []
+        for b in range(2):
+            handles = [None] * world
+            dist.all_gather_object(handles, shared[b].handle)
+            peers.append([shared[b].ptr if r == rank else nm.open_peer(handles[r], dev.index) for r in range(world)])
     stream = torch.cuda.current_stream(dev)
     sp = ctypes.c_void_p(stream.cuda_stream)
 
@@ -338,12 +351,22 @@ def bench_prefill(args, torch, dist, rank, world, dev):
         c.append(0, k, v)
         if ev is not None:
             ev[0].record(stream)
-        nm.attend(c, q, 0, scale, out=o)
+        if comm is None:
+            nm.attend(c, q, 0, scale, out=o)
+        else:
+            nm.attend_fanout(c, q, 0, scale, peers[i & 1], hq * dh, rank * hq_l * dh)
         if ev is not None:
             ev[1].record(stream)
         if comm is not None:
-            comm.allgather(o, gathered, sp)
-            comm.to_rows(gathered, full, S, hq_l * dh * 2, sp)
+            comm.barrier(sp)
+
+    def step_nccl(i):  # the unfused alternative: attend, NCCL all-gather, permute
+        q, k, v, c, o = sets[i % R]
+        c.reset()
+        c.append(0, k, v)
+        nm.attend(c, q, 0, scale, out=o)
+        comm.allgather(o, gathered, sp)
+        comm.to_rows(gathered, full, S, hq_l * dh * 2, sp)
 
     def barrier():
         if world > 1:
@@ -370,6 +393,24 @@ def bench_prefill(args, torch, dist, rank, world, dev):
         ms, kernel_ms = float(tt[0]), float(tt[1])
     ms_step = ms / args.steps
     value = c2_flops() / (ms_step * 1e-3) / 1e12
+    collective = None
+    if comm is not None:
+        for i in range(2):
+            step_nccl(i)
+        barrier()
+        n_cmp = max(3, args.steps // 4)
+        u0, u1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        u0.record(stream)
+        for i in range(n_cmp):
+            step_nccl(i)
+        u1.record(stream)
+        barrier()
+        tt = torch.tensor([u0.elapsed_time(u1) / n_cmp], device=dev, dtype=torch.float64)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        collective = {"fused_epilogue_ms_per_step": ms_step, "nccl_allgather_ms_per_step": float(tt[0]),
+                      "attention_only_ms": kernel_ms,
+                      "note": "fused: NVLink stores from the attention epilogue + one stream-ordered barrier; "
+                              "nccl: attention, ncclAllGather, head-to-row permutation"}
 
     # ---- end to end through the C ABI with host buffers
     pin = lambda t: t.cpu().pin_memory()
@@ -384,12 +425,12 @@ def bench_prefill(args, torch, dist, rank, world, dev):
         v.copy_(hv_host, non_blocking=True)
         c.reset()
         c.append(0, k, v)
-        nm.attend(c, q, 0, scale, out=o)
         if comm is not None:
-            comm.allgather(o, gathered, sp)
-            comm.to_rows(gathered, full, S, hq_l * dh * 2, sp)
-            out_host.copy_(full, non_blocking=True)
+            nm.attend_fanout(c, q, 0, scale, peers[i & 1], hq * dh, rank * hq_l * dh)
+            comm.barrier(sp)
+            out_host.copy_(shared[i & 1].tensor(), non_blocking=True)
         else:
+            nm.attend(c, q, 0, scale, out=o)
             out_host.copy_(o, non_blocking=True)
 
     for i in range(2):
@@ -409,6 +450,15 @@ def bench_prefill(args, torch, dist, rank, world, dev):
     h2d = world * S * (hq_l + 2 * hkv_l) * dh * 2
     d2h = world * S * hq * dh * 2
     if comm is not None:
+        torch.cuda.synchronize(dev)
+        dist.barrier()  # every rank is done writing into the mapped buffers
+        for b in range(2):
+            for r, ptr in enumerate(peers[b]):
+                if r != rank:
+                    nm.close_peer(ptr)
+        dist.barrier()
+        for b in range(2):
+            shared[b].close()
         comm.close()
     p = peaks()
     achieved = c2_flops() / world / (kernel_ms * 1e-3) / 1e12
@@ -416,8 +466,9 @@ def bench_prefill(args, torch, dist, rank, world, dev):
             "unit": "TFLOP/s", "frac": achieved / p["bf16"], "peak_src": f"{p['src']} bf16 dense (burst)",
             "traffic": ncu_traffic("attn_prefill_c2"), "kernel_ms": kernel_ms,
             "algorithmic_unit": "4*head_dim*q_heads per visible (query,key) pair; 8,390,656 pairs"}
-    launches = args.steps * (2 + (1 if world > 1 else 0))
+    launches = args.steps * 2
     return {"value": value, "ms_per_step": ms_step, "tok_per_s": S / (ms_step * 1e-3), "roofline": roof,
+            "collective": collective,
             "e2e": {"value": c2_flops() / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
             "clocks": clk.summary(), "gpu_launches": launches, "rotating_sets": R}
@@ -721,6 +772,8 @@ def main():
                 "config": {**config2_desc(world), "rotating_sets": res["rotating_sets"]},
                 "tok_per_s": res["tok_per_s"], "roofline": res["roofline"], "cpu_baseline": cpu, "e2e": res["e2e"],
                 "clocks": res["clocks"], "gpu_launches": res["gpu_launches"], "extra": extra}
+        if res.get("collective"):
+            line["collective"] = res["collective"]
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()

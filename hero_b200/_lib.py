@@ -117,6 +117,13 @@ SIGNATURES = {
     "nmg_comm_destroy": [_vp],
     "nmg_allgather": [_vp, _vp, _vp, _i64, _vp],
     "nmg_gather_heads_to_rows": [_vp, _vp, _i32, _i64, _i64, _vp],
+    "nmg_comm_barrier": [_vp, _vp],
+    "nmg_shared_alloc": [_i64, _i32, ctypes.POINTER(_vp), _vp],
+    "nmg_shared_free": [_vp],
+    "nmg_ipc_open": [_vp, _i32, ctypes.POINTER(_vp)],
+    "nmg_ipc_close": [_vp],
+    "nmg_attend_fanout": [_vp, _i32, _vp, _i32, _i64, _i64, _f32, _i32, ctypes.POINTER(_vp), _i32, _i64, _i64, _i32,
+                          _vp],
 }
 
 

@@ -175,8 +175,11 @@ int attend_batch_mma(const nmg_kv_cache* const* caches, int batch, const int64_t
 // tcgen05 flash prefill (attn_prefill_sm100.cu).  Returns NMG_UNSUPPORTED
 // when the shape is not one it was built for.
 bool prefill_supported(const nmg_kv_cache* c, int hq, int q_dtype, int64_t rows);
+// Row t's hq*dh outputs go to outs[i] + t * out_row_elems + out_col0 for
+// every i < nout (at most 8; the caller's buffer and, for head-sharded
+// multi-GPU runs, peer buffers).
 int attend_rows_prefill(const nmg_kv_cache* c, int hq, const void* q, int q_dtype, int64_t rows, int64_t first_query,
-                        int64_t window, int64_t floor_pos, int64_t newest, float scale, void* out, int out_dtype,
-                        cudaStream_t stream);
+                        int64_t window, int64_t floor_pos, int64_t newest, float scale, void* const* outs, int nout,
+                        int64_t out_row_elems, int64_t out_col0, int out_dtype, cudaStream_t stream);
 
 }  // namespace nmg

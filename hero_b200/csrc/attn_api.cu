@@ -35,8 +35,8 @@ int dispatch_rows(const nmg_kv_cache* c, int hq, const void* q, int q_dtype, int
     if (prev != c->device) NMG_CUDA_TRY(cudaSetDevice(c->device));
     int st;
     if (nmg::prefill_supported(c, hq, q_dtype, rows))
-        st = nmg::attend_rows_prefill(c, hq, q, q_dtype, rows, first_query, window, floor_pos, newest, scale, out,
-                                      out_dtype, stream);
+        st = nmg::attend_rows_prefill(c, hq, q, q_dtype, rows, first_query, window, floor_pos, newest, scale, &out, 1,
+                                      (int64_t)hq * c->dh, 0, out_dtype, stream);
     else if (nmg::decode_mma_supported(c, q_dtype))
         st = nmg::attend_rows_mma(c, hq, q, rows, first_query, window, floor_pos, newest, scale, out, out_dtype,
                                   stream);
@@ -70,6 +70,51 @@ extern "C" int nmg_attend(const nmg_kv_cache* c, int hq, const void* q, int q_dt
     if (st != NMG_OK) return st;
     return dispatch_rows(c, hq, q, q_dtype, rows, first_query, c->window, c->oldest, newest, use_scale ? scale : 1.f,
                          out, out_dtype, (cudaStream_t)stream);
+}
+
+extern "C" int nmg_attend_fanout(const nmg_kv_cache* c, int hq, const void* q, int q_dtype, int64_t rows,
+                                 int64_t first_query, float scale, int use_scale, void* const* outs, int nout,
+                                 int64_t out_row_elems, int64_t out_col0, int out_dtype, void* stream) {
+    if (!c) return set_error(NMG_INVALID_ARGUMENT, "nmg_attend_fanout: null cache");
+    int st = validate_heads(c, hq, q_dtype, out_dtype);
+    if (st != NMG_OK) return st;
+    if (rows < 0) return set_error(NMG_INVALID_ARGUMENT, "nmg_attend_fanout: negative row count");
+    if (rows == 0) return NMG_OK;
+    if (!q || !outs || nout < 1 || nout > 8) return set_error(NMG_INVALID_ARGUMENT, "nmg_attend_fanout: 1..8 outputs");
+    for (int i = 0; i < nout; ++i)
+        if (!outs[i]) return set_error(NMG_INVALID_ARGUMENT, "nmg_attend_fanout: null output %d", i);
+    const int64_t width = (int64_t)hq * c->dh;
+    if (out_col0 < 0 || out_row_elems < out_col0 + width)
+        return set_error(NMG_INVALID_ARGUMENT, "nmg_attend_fanout: %lld output columns at %lld do not fit rows of %lld",
+                         (long long)width, (long long)out_col0, (long long)out_row_elems);
+    const int64_t newest = c->newest();
+    st = check_visible(c, rows, first_query, c->window, c->oldest, newest);
+    if (st != NMG_OK) return st;
+    const float sc = use_scale ? scale : 1.f;
+    cudaStream_t s = (cudaStream_t)stream;
+    int prev = 0;
+    NMG_CUDA_TRY(cudaGetDevice(&prev));
+    if (prev != c->device) NMG_CUDA_TRY(cudaSetDevice(c->device));
+    const int es = nmg::dtype_size(out_dtype);
+    const bool aligned = !(((out_row_elems * es) | (out_col0 * es)) & 15);
+    if (aligned && nmg::prefill_supported(c, hq, q_dtype, rows)) {
+        st = nmg::attend_rows_prefill(c, hq, q, q_dtype, rows, first_query, c->window, c->oldest, newest, sc, outs,
+                                      nout, out_row_elems, out_col0, out_dtype, s);
+    } else {
+        // Other shapes: reduce into staging, then one strided copy per output.
+        void* tmp = nullptr;
+        st = nmg::device_staging(c->device, (size_t)rows * width * es, &tmp);
+        if (st == NMG_OK)
+            st = dispatch_rows(c, hq, q, q_dtype, rows, first_query, c->window, c->oldest, newest, sc, tmp, out_dtype, s);
+        for (int i = 0; st == NMG_OK && i < nout; ++i) {
+            const cudaError_t e = cudaMemcpy2DAsync((char*)outs[i] + out_col0 * es, (size_t)out_row_elems * es, tmp,
+                                                    (size_t)width * es, (size_t)width * es, (size_t)rows,
+                                                    cudaMemcpyDeviceToDevice, s);
+            if (e != cudaSuccess) st = set_error(NMG_CUDA_ERROR, "nmg_attend_fanout: copy: %s", cudaGetErrorString(e));
+        }
+    }
+    if (prev != c->device) cudaSetDevice(prev);
+    return st;
 }
 
 extern "C" int nmg_append_attend(nmg_kv_cache* c, int64_t first, const void* keys, const void* values, int kv_dtype,

@@ -3,7 +3,7 @@
 //
 // One CTA owns (query row, kv head, q-head subgroup, key split).  Key tiles of
 // 32*WARPS consecutive positions arrive in shared memory by bulk TMA copies
-// (cp.async.bulk, no multicast) into a 2-stage ring; each warp takes 32 keys
+// (cp.async.bulk, one CTA per copy) into a 2-stage ring; each warp takes 32 keys
 // of a tile: lane = key for the scores (q rows broadcast from shared memory,
 // 16-byte chunks read in a lane-rotated order so the 32 key rows hit distinct
 // banks), an online softmax per query head, then lane = value column for P.V.

@@ -7,7 +7,7 @@
 //   warp 0      TMA producer for Q (once) and K blocks (3-stage ring; a K
 //               stage is released as soon as its S MMA completes)
 //   warp 2      TMA producer for V blocks (2-stage ring, released after P.V)
-//               (cp.async.bulk.tensor, 128-byte swizzle, no multicast)
+//               (cp.async.bulk.tensor, 128-byte swizzle, one CTA per copy)
 //   warp 1      allocates TMEM and issues tcgen05.mma from one thread:
 //                 S_j = Q K_j^T  (M=128, N=BN, K=DH)  into TMEM (two S buffers)
 //                 O  += P_j V_j  (M=128, N=DH, K=BN)  A = P_j read from TMEM
@@ -67,6 +67,8 @@ struct PfCfg {
     static_assert(SMEM <= 232448, "shared memory budget");
 };
 
+constexpr int kMaxFanout = 8;
+
 struct PrefillArgs {
     CUtensorMap tm_q;  // (d, head, row) over q [rows][hq*DH]
     CUtensorMap tm_k;  // (d, hkv*slots) over the cache
@@ -74,7 +76,13 @@ struct PrefillArgs {
     int64_t rows, first_query, window, floor_pos, newest, base, slots;
     int hq, hkv, g;
     float scale_log2;
-    void* out;
+    // Output row t of this call goes to outs[i] + t * out_row_elems + out_col0
+    // (elements) for every i < nout: the caller's buffer and, when the heads
+    // are sharded across GPUs, the other GPUs' buffers (peer pointers), so
+    // the gather of head outputs rides on the epilogue's stores.
+    void* outs[kMaxFanout];
+    int nout;
+    int64_t out_row_elems, out_col0;
     int out_dtype;
     int* err;
 };
@@ -377,348 +385,40 @@ __global__ void __launch_bounds__(PfCfg<DH>::THREADS, 1) attn_prefill_kernel(con
         if (ok && nblk > 0 && __all_sync(0xffffffffu, dev::mbar_wait(o_done, (nblk - 1) & 1, a.err))) {
             tc::fence_after_sync();
             const float inv = 1.f / l_row;
-            const int64_t obase = ((t0 + row) * (int64_t)a.hq + h) * DH + part * C::PART_D;
+            const int64_t obase = (t0 + row) * a.out_row_elems + a.out_col0 + (int64_t)h * DH + part * C::PART_D;
 #pragma unroll 1
             for (int c = 0; c < C::PART_D / 32; ++c) {
                 uint32_t r[32];
                 tc::ld_32x32b_x32(t_lane + C::O_COL + part * C::PART_D + c * 32, r);
                 if (row_valid) {
                     if (a.out_dtype == NMG_F32) {
-                        float4* dst = (float4*)((float*)a.out + obase + c * 32);
 #pragma unroll
-                        for (int e = 0; e < 8; ++e)
-                            dst[e] = make_float4(__uint_as_float(r[4 * e]) * inv, __uint_as_float(r[4 * e + 1]) * inv,
-                                                 __uint_as_float(r[4 * e + 2]) * inv, __uint_as_float(r[4 * e + 3]) * inv);
+                        for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * inv);
+                        for (int o = 0; o < a.nout; ++o) {
+                            uint4* dst = (uint4*)((float*)a.outs[o] + obase + c * 32);
+#pragma unroll
+                            for (int e = 0; e < 8; ++e) dst[e] = make_uint4(r[4 * e], r[4 * e + 1], r[4 * e + 2], r[4 * e + 3]);
+                        }
                     } else {
-                        uint4* dst = (uint4*)((uint16_t*)a.out + obase + c * 32);
                         const bool obf = a.out_dtype == NMG_BF16;
+                        uint32_t w[16];
 #pragma unroll
-                        for (int e = 0; e < 4; ++e) {
-                            uint32_t w[4];
+                        for (int t = 0; t < 16; ++t) {
+                            const float f0 = __uint_as_float(r[2 * t]) * inv, f1 = __uint_as_float(r[2 * t + 1]) * inv;
+                            const uint32_t b0 = obf ? dev::f32_to_bf16_bits(f0) : dev::f32_to_f16_bits(f0);
+                            const uint32_t b1 = obf ? dev::f32_to_bf16_bits(f1) : dev::f32_to_f16_bits(f1);
+                            w[t] = b0 | (b1 << 16);
+                        }
+                        for (int o = 0; o < a.nout; ++o) {
+                            uint4* dst = (uint4*)((uint16_t*)a.outs[o] + obase + c * 32);
 #pragma unroll
-                            for (int t = 0; t < 4; ++t) {
-                                const float f0 = __uint_as_float(r[8 * e + 2 * t]) * inv;
-                                const float f1 = __uint_as_float(r[8 * e + 2 * t + 1]) * inv;
-                                const uint32_t b0 = obf ? dev::f32_to_bf16_bits(f0) : dev::f32_to_f16_bits(f0);
-                                const uint32_t b1 = obf ? dev::f32_to_bf16_bits(f1) : dev::f32_to_f16_bits(f1);
-                                w[t] = b0 | (b1 << 16);
-                            }
-                            dst[e] = make_uint4(w[0], w[1], w[2], w[3]);
+                            for (int e = 0; e < 4; ++e) dst[e] = make_uint4(w[4 * e], w[4 * e + 1], w[4 * e + 2], w[4 * e + 3]);
                         }
                     }
                 }
             }
-        }
-    }
-
-    tc::fence_before_sync();
-    __syncthreads();
-    if (warp == 1) {
-        tc::fence_after_sync();
-        tc::tmem_dealloc(tmem, C::TMEM_COLS);
-    }
-}
-
-// ------------------------------------------------------------------ two heads
-//
-// head_dim 128 with an even GQA group: one CTA computes the same 128-row tile
-// for two query heads of one KV head, so every K/V block is fetched once for
-// both (half the L2->SMEM traffic per FLOP) and the tensor pipe alternates
-// between the heads: while one head's softmax runs, the other head's P.V and
-// next S are in flight.  TMEM: S_A | S_B | O_A | O_B (4 x 128 columns).
-//
-//   warp 0       Q (both heads) + K producer, 3 K stages
-//   warp 1       TMEM owner + MMA issuer: PV_A(i-1), S_A(i), PV_B(i-1), S_B(i)
-//   warp 2       V producer, 2 V stages
-//   warps 3..6   softmax, head A (one warp per TMEM lane quadrant, whole rows)
-//   warps 7..10  softmax, head B
-struct H2Cfg {
-    static constexpr int DH = 128, BM = 128, BN = 128, KST = 3, VST = 2;
-    static constexpr int Q_BYTES = BM * DH * 2;
-    static constexpr int K_BYTES = BN * DH * 2;
-    static constexpr int V_BYTES = BN * DH * 2;
-    static constexpr int Q_OFF = 0;  // head A, then head B
-    static constexpr int K_OFF = 2 * Q_BYTES;
-    static constexpr int V_OFF = K_OFF + KST * K_BYTES;
-    static constexpr int BAR_OFF = V_OFF + VST * V_BYTES;
-    // q_full, k_full/k_empty[KST], v_full/v_empty[VST], s_full[2], p_full[2], o_done[2]
-    static constexpr int NBARS = 1 + 2 * KST + 2 * VST + 2 + 2 + 2;
-    static constexpr int TMEMPTR_OFF = BAR_OFF + NBARS * 8;
-    static constexpr int SMEM = TMEMPTR_OFF + 16 + 1024;
-    static constexpr int THREADS = 96 + 256;
-    static constexpr uint32_t TMEM_COLS = 512;
-    static_assert(SMEM <= 232448, "shared memory budget");
-};
-
-template <bool BF16>
-__global__ void __launch_bounds__(352, 1) attn_prefill_h2_kernel(const __grid_constant__ PrefillArgs a) {
-    using C = H2Cfg;
-    constexpr int BM = C::BM, BN = C::BN, DH = C::DH, KST = C::KST, VST = C::VST;
-    extern __shared__ unsigned char smem_raw[];
-    unsigned char* smem = (unsigned char*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-    uint64_t* bars = (uint64_t*)(smem + C::BAR_OFF);
-    uint64_t* q_full = bars;
-    uint64_t* k_full = q_full + 1;
-    uint64_t* k_empty = k_full + KST;
-    uint64_t* v_full = k_empty + KST;
-    uint64_t* v_empty = v_full + VST;
-    // One S buffer per head: S_x(i+1) is issued only after P_x(i).V, so each
-    // of these completes at most one phase ahead of its waiter.
-    uint64_t* s_full = v_empty + VST;  // [head]
-    uint64_t* p_full = s_full + 2;     // [head]
-    uint64_t* o_done = p_full + 2;     // [head]
-    uint32_t* tmem_slot = (uint32_t*)(smem + C::TMEMPTR_OFF);
-
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int tile = gridDim.x - 1 - blockIdx.x;  // heaviest tiles first
-    const int h0 = 2 * blockIdx.y;                // heads h0, h0 + 1 share KV head h0 / g
-    const int hk = h0 / a.g;
-    const int64_t t0 = (int64_t)tile * BM;
-    const int64_t t_last = (t0 + BM < a.rows ? t0 + BM : a.rows) - 1;
-    const int64_t q_first = a.first_query + t0, q_last = a.first_query + t_last;
-    const int64_t u_lo = vis_lo(a, q_first) - a.base;
-    const int64_t u_hi = vis_hi(a, q_last) - a.base;
-    const int64_t j_begin = u_lo / BN;
-    const int nblk = (int)(u_hi / BN + 1 - j_begin);
-    const int64_t full_lo = vis_lo(a, q_last), full_hi = vis_hi(a, q_first);
-
-    if (threadIdx.x == 0) {
-        dev::mbar_init(q_full, 1);
-        for (int s = 0; s < KST; ++s) {
-            dev::mbar_init(&k_full[s], 1);
-            dev::mbar_init(&k_empty[s], 1);
-        }
-        for (int s = 0; s < VST; ++s) {
-            dev::mbar_init(&v_full[s], 1);
-            dev::mbar_init(&v_empty[s], 1);
-        }
-        for (int x = 0; x < 2; ++x) {
-            dev::mbar_init(&s_full[x], 1);
-            dev::mbar_init(&p_full[x], 128);
-            dev::mbar_init(&o_done[x], 1);
-        }
-        dev::fence_mbar_init();
-    }
-    if (warp == 1) {
-        tc::tmem_alloc(tmem_slot, C::TMEM_COLS);
-        tc::tmem_relinquish();
-    }
-    tc::fence_before_sync();
-    __syncthreads();
-    tc::fence_after_sync();
-    const uint32_t tmem = *tmem_slot;
-
-    auto kv_row = [&](int i) -> int32_t {
-        const int64_t u0 = (j_begin + i) * BN;
-        return (int32_t)(hk * a.slots + u0 % a.slots);
-    };
-
-    if (warp == 0) {
-        if (lane == 0) {
-            dev::prefetch_tensormap(&a.tm_q);
-            dev::prefetch_tensormap(&a.tm_k);
-            dev::mbar_arrive_expect_tx(q_full, 2 * C::Q_BYTES);
-#pragma unroll
-            for (int x = 0; x < 2; ++x)
-#pragma unroll
-                for (int c = 0; c < DH / 64; ++c)
-                    dev::tma_load_3d(smem + C::Q_OFF + x * C::Q_BYTES + c * BM * 128, &a.tm_q, c * 64, h0 + x, (int32_t)t0,
-                                q_full);
-            for (int i = 0; i < nblk; ++i) {
-                const int s = i % KST;
-                if (i >= KST && !dev::mbar_wait(&k_empty[s], ((i / KST) - 1) & 1, a.err)) break;
-                dev::mbar_arrive_expect_tx(&k_full[s], C::K_BYTES);
-                const int32_t row = kv_row(i);
-#pragma unroll
-                for (int c = 0; c < DH / 64; ++c)
-                    dev::tma_load_2d(smem + C::K_OFF + s * C::K_BYTES + c * BN * 128, &a.tm_k, c * 64, row, &k_full[s]);
-            }
-        }
-    } else if (warp == 2) {
-        if (lane == 0) {
-            dev::prefetch_tensormap(&a.tm_v);
-            for (int i = 0; i < nblk; ++i) {
-                const int s = i % VST;
-                if (i >= VST && !dev::mbar_wait(&v_empty[s], ((i / VST) - 1) & 1, a.err)) break;
-                dev::mbar_arrive_expect_tx(&v_full[s], C::V_BYTES);
-                const int32_t row = kv_row(i);
-#pragma unroll
-                for (int c = 0; c < DH / 64; ++c)
-                    dev::tma_load_2d(smem + C::V_OFF + s * C::V_BYTES + c * BN * 128, &a.tm_v, c * 64, row, &v_full[s]);
-            }
-        }
-    } else if (warp == 1) {
-        if (lane == 0) {
-            constexpr uint32_t idesc_s = tc::idesc_f16(128, BN, BF16 ? 1 : 0, 0, 0);
-            constexpr uint32_t idesc_o = tc::idesc_f16(128, DH, 0, 0, 1);
-            const uint32_t sbase = dev::smem_u32(smem);
-            bool ok = dev::mbar_wait(q_full, 0, a.err);
-            // P_x(i).V_i into O_x; V_i is released after head B's product.
-            auto issue_pv = [&](int x, int i) -> bool {
-                const int s = i % VST;
-                if (!dev::mbar_wait(&p_full[x], i & 1, a.err)) return false;
-                if (x == 0 && !dev::mbar_wait(&v_full[s], (i / VST) & 1, a.err)) return false;
-                tc::fence_after_sync();
-#pragma unroll
-                for (int k = 0; k < BN / 16; ++k) {
-                    const uint64_t bd =
-                        tc::smem_desc_sw128(sbase + C::V_OFF + s * C::V_BYTES + k * 2048, BN * 128, 1024);
-                    tc::mma_f16_ts(tmem + 2 * BN + x * DH, tmem + x * BN + k * 8, bd, idesc_o,
-                                   (i > 0 || k > 0) ? 1u : 0u);
-                }
-                tc::commit(&o_done[x]);
-                if (x == 1) tc::commit(&v_empty[s]);
-                return true;
-            };
-            auto issue_s = [&](int x, int i) {
-                const int s = i % KST;
-#pragma unroll
-                for (int k = 0; k < DH / 16; ++k) {
-                    const uint64_t ad = tc::smem_desc_sw128(
-                        sbase + C::Q_OFF + x * C::Q_BYTES + (k / 4) * BM * 128 + (k % 4) * 32, 16, 1024);
-                    const uint64_t bd =
-                        tc::smem_desc_sw128(sbase + C::K_OFF + s * C::K_BYTES + (k / 4) * BN * 128 + (k % 4) * 32, 16, 1024);
-                    tc::mma_f16_ss(tmem + x * BN, ad, bd, idesc_s, k > 0 ? 1u : 0u);
-                }
-                tc::commit(&s_full[x]);
-            };
-            for (int i = 0; ok && i < nblk; ++i) {
-                const int s = i % KST;
-                if (!dev::mbar_wait(&k_full[s], (i / KST) & 1, a.err)) break;
-                tc::fence_after_sync();
-                // S_x(i) overwrites P_x(i-1), so P_x(i-1).V goes first (in order).
-                if (i >= 1 && !issue_pv(0, i - 1)) { ok = false; break; }
-                issue_s(0, i);
-                if (i >= 1 && !issue_pv(1, i - 1)) { ok = false; break; }
-                issue_s(1, i);
-                tc::commit(&k_empty[s]);
-            }
-            if (ok && nblk > 0 && issue_pv(0, nblk - 1)) issue_pv(1, nblk - 1);
-        }
-    } else {
-        // ---------------------------------------------------- softmax warps
-        const int x = (warp - 3) >> 2;  // head of this warp: 0 -> A, 1 -> B
-        const int quad = warp & 3;
-        const int row = quad * 32 + lane;
-        const uint32_t t_lane = tmem + ((uint32_t)(quad * 32) << 16);
-        const uint32_t s_col = x * BN, o_col = 2 * BN + x * DH;
-        const int64_t qpos = a.first_query + t0 + row;
-        const bool row_valid = t0 + row < a.rows;
-        const int64_t lo = vis_lo(a, qpos), hi = vis_hi(a, qpos);
-        float m_run = -INFINITY, l_run = 0.f;
-        bool ok = true;
-
-        for (int i = 0; i < nblk; ++i) {
-            if (!__all_sync(0xffffffffu, dev::mbar_wait(&s_full[x], i & 1, a.err))) {
-                ok = false;
-                break;
-            }
-            tc::fence_after_sync();
-            const int64_t p0 = a.base + (j_begin + i) * BN;
-            const bool masked = !(p0 >= full_lo && p0 + BN - 1 <= full_hi);
-            // visible columns of this block for this row: [clo, chi]
-            const int clo = (int)max((int64_t)-1, min((int64_t)BN, lo - p0));
-            const int chi = (int)max((int64_t)-1, min((int64_t)BN, hi - p0));
-            // pass 1: the row maximum
-            float mb = -INFINITY;
-#pragma unroll
-            for (int c = 0; c < BN / 32; ++c) {
-                uint32_t r[32];
-                tc::ld_32x32b_x32(t_lane + s_col + c * 32, r);
-#pragma unroll
-                for (int e = 0; e < 32; ++e) {
-                    float v = __uint_as_float(r[e]);
-                    if (masked && (c * 32 + e < clo || c * 32 + e > chi)) v = -INFINITY;
-                    mb = fmaxf(mb, v);
-                }
-            }
-            mb *= a.scale_log2;  // scale_log2 > 0 keeps the maximum in place
-            const float m_new = fmaxf(m_run, mb);
-            const bool rescale = m_new > m_run + 8.0f;
-            float alpha = 1.f;
-            if (rescale) {
-                alpha = (m_run == -INFINITY) ? 0.f : ex2(m_run - m_new);
-                m_run = m_new;
-            }
-            const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
-            // pass 2: exponentials, row sum, P as fp16 pairs over the S columns
-            float sum = 0.f;
-#pragma unroll
-            for (int c = 0; c < BN / 32; ++c) {
-                uint32_t r[32];
-                tc::ld_32x32b_x32(t_lane + s_col + c * 32, r);
-                uint32_t pk[16];
-#pragma unroll
-                for (int e = 0; e < 32; e += 2) {
-                    float v0 = __uint_as_float(r[e]) * a.scale_log2, v1 = __uint_as_float(r[e + 1]) * a.scale_log2;
-                    if (masked) {
-                        const int col = c * 32 + e;
-                        if (col < clo || col > chi) v0 = -INFINITY;
-                        if (col + 1 < clo || col + 1 > chi) v1 = -INFINITY;
-                    }
-                    const float e0 = ex2(v0 - m_use), e1 = ex2(v1 - m_use);
-                    sum += e0 + e1;
-                    pk[e / 2] = pack2(e0, e1, false);
-                }
-                tc::st_32x32b_x16(t_lane + s_col + c * 16, pk);
-            }
-            l_run = l_run * alpha + sum;
-            // Every o_done phase is waited for, in order (parity waits cannot
-            // skip phases safely).
-            if (i >= 1 && !__all_sync(0xffffffffu, dev::mbar_wait(&o_done[x], (i - 1) & 1, a.err))) {
-                ok = false;
-                break;
-            }
-            if (i >= 1 && __any_sync(0xffffffffu, rescale)) {
-                tc::fence_after_sync();
-#pragma unroll 1
-                for (int c = 0; c < DH / 32; ++c) {
-                    uint32_t r[32];
-                    tc::ld_32x32b_x32(t_lane + o_col + c * 32, r);
-#pragma unroll
-                    for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * alpha);
-                    tc::st_32x32b_x32(t_lane + o_col + c * 32, r);
-                }
-            }
-            tc::wait_st();
-            tc::fence_before_sync();
-            dev::mbar_arrive(&p_full[x]);
-        }
-
-        if (ok && nblk > 0 && __all_sync(0xffffffffu, dev::mbar_wait(&o_done[x], (nblk - 1) & 1, a.err))) {
-            tc::fence_after_sync();
-            const float inv = 1.f / l_run;
-            const int64_t obase = ((t0 + row) * (int64_t)a.hq + h0 + x) * DH;
-#pragma unroll 1
-            for (int c = 0; c < DH / 32; ++c) {
-                uint32_t r[32];
-                tc::ld_32x32b_x32(t_lane + o_col + c * 32, r);
-                if (row_valid) {
-                    if (a.out_dtype == NMG_F32) {
-                        float4* dst = (float4*)((float*)a.out + obase + c * 32);
-#pragma unroll
-                        for (int e = 0; e < 8; ++e)
-                            dst[e] = make_float4(__uint_as_float(r[4 * e]) * inv, __uint_as_float(r[4 * e + 1]) * inv,
-                                                 __uint_as_float(r[4 * e + 2]) * inv, __uint_as_float(r[4 * e + 3]) * inv);
-                    } else {
-                        uint4* dst = (uint4*)((uint16_t*)a.out + obase + c * 32);
-                        const bool obf = a.out_dtype == NMG_BF16;
-#pragma unroll
-                        for (int e = 0; e < 4; ++e) {
-                            uint32_t w[4];
-#pragma unroll
-                            for (int t = 0; t < 4; ++t) {
-                                const float f0 = __uint_as_float(r[8 * e + 2 * t]) * inv;
-                                const float f1 = __uint_as_float(r[8 * e + 2 * t + 1]) * inv;
-                                const uint32_t b0 = obf ? dev::f32_to_bf16_bits(f0) : dev::f32_to_f16_bits(f0);
-                                const uint32_t b1 = obf ? dev::f32_to_bf16_bits(f1) : dev::f32_to_f16_bits(f1);
-                                w[t] = b0 | (b1 << 16);
-                            }
-                            dst[e] = make_uint4(w[0], w[1], w[2], w[3]);
-                        }
-                    }
-                }
-            }
+            // Stores to other GPUs' memory are visible system-wide before this grid completes.
+            if (a.nout > 1) __threadfence_system();
         }
     }
 
@@ -745,21 +445,6 @@ int launch_prefill(const PrefillArgs& a, dim3 grid, cudaStream_t s) {
         attr_set |= 1u << (dev_id & 31);
     }
     kern<<<grid, C::THREADS, C::SMEM, s>>>(a);
-    NMG_CUDA_TRY(cudaGetLastError());
-    return NMG_OK;
-}
-
-template <bool BF16>
-int launch_prefill_h2(const PrefillArgs& a, dim3 grid, cudaStream_t s) {
-    auto kern = attn_prefill_h2_kernel<BF16>;
-    static unsigned attr_set = 0;
-    int dev_id = 0;
-    NMG_CUDA_TRY(cudaGetDevice(&dev_id));
-    if (!(attr_set & (1u << (dev_id & 31)))) {
-        NMG_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, H2Cfg::SMEM));
-        attr_set |= 1u << (dev_id & 31);
-    }
-    kern<<<grid, H2Cfg::THREADS, H2Cfg::SMEM, s>>>(a);
     NMG_CUDA_TRY(cudaGetLastError());
     return NMG_OK;
 }
@@ -799,8 +484,14 @@ bool prefill_supported(const nmg_kv_cache* c, int hq, int q_dtype, int64_t rows)
 }
 
 int attend_rows_prefill(const nmg_kv_cache* c, int hq, const void* q, int q_dtype, int64_t rows, int64_t first_query,
-                        int64_t window, int64_t floor_pos, int64_t newest, float scale, void* out, int out_dtype,
-                        cudaStream_t stream) {
+                        int64_t window, int64_t floor_pos, int64_t newest, float scale, void* const* outs, int nout,
+                        int64_t out_row_elems, int64_t out_col0, int out_dtype, cudaStream_t stream) {
+    if (nout < 1 || nout > kMaxFanout) return set_error(NMG_INVALID_ARGUMENT, "prefill: %d outputs (1..%d)", nout, kMaxFanout);
+    const int es = dtype_size(out_dtype);
+    if (((out_row_elems * es) | (out_col0 * es)) & 15)
+        return set_error(NMG_UNSUPPORTED, "prefill: output rows and column offset must be 16-byte multiples");
+    for (int i = 0; i < nout; ++i)
+        if (!outs[i] || ((uintptr_t)outs[i] & 15)) return set_error(NMG_INVALID_ARGUMENT, "prefill: output %d unaligned", i);
     EncodeTiledFn enc = encode_tiled_fn();
     if (!enc) return set_error(NMG_UNSUPPORTED, "cuTensorMapEncodeTiled unavailable");
     if (((uintptr_t)q & 15) || ((uintptr_t)c->k & 15) || ((uintptr_t)c->v & 15))
@@ -846,16 +537,15 @@ int attend_rows_prefill(const nmg_kv_cache* c, int hq, const void* q, int q_dtyp
     a->hkv = c->hkv;
     a->g = hq / c->hkv;
     a->scale_log2 = scale * 1.4426950408889634f;
-    a->out = out;
+    for (int i = 0; i < nout; ++i) a->outs[i] = outs[i];
+    a->nout = nout;
+    a->out_row_elems = out_row_elems;
+    a->out_col0 = out_col0;
     a->out_dtype = out_dtype;
     int st = device_error_flag(c->device, &a->err);
     if (st == NMG_OK) {
         dim3 grid((unsigned)((rows + 127) / 128), (unsigned)hq);
-        if (false && dh == 128 && a->g % 2 == 0) {
-            // two query heads of one KV group per CTA
-            grid.y = (unsigned)(hq / 2);
-            st = c->dtype == NMG_BF16 ? launch_prefill_h2<true>(*a, grid, stream) : launch_prefill_h2<false>(*a, grid, stream);
-        } else if (dh == 128)
+        if (dh == 128)
             st = c->dtype == NMG_BF16 ? launch_prefill<128, true>(*a, grid, stream) : launch_prefill<128, false>(*a, grid, stream);
         else
             st = c->dtype == NMG_BF16 ? launch_prefill<256, true>(*a, grid, stream) : launch_prefill<256, false>(*a, grid, stream);

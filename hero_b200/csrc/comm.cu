@@ -83,6 +83,7 @@ struct nmg_comm {
     Nccl* nccl = nullptr;
     nccl_comm comm = nullptr;
     int rank = 0, world = 1, device = 0;
+    unsigned char* bar = nullptr;  // world bytes for the stream-ordered barrier
 };
 
 extern "C" int nmg_comm_unique_id(void* id128) {
@@ -112,8 +113,13 @@ extern "C" int nmg_comm_init(const void* id128, int rank, int world, int device,
     c->rank = rank;
     c->world = world;
     c->device = device;
+    if (cudaMalloc(&c->bar, (size_t)world) != cudaSuccess || cudaMemset(c->bar, 0, (size_t)world) != cudaSuccess) {
+        delete c;
+        return set_error(NMG_CUDA_ERROR, "nmg_comm_init: barrier buffer");
+    }
     const nccl_result r = n->comm_init_rank(&c->comm, world, uid, rank);
     if (r != 0) {
+        cudaFree(c->bar);
         delete c;
         return set_error(NMG_COMM_ERROR, "ncclCommInitRank: %s", nccl_msg(n, r));
     }
@@ -124,7 +130,62 @@ extern "C" int nmg_comm_init(const void* id128, int rank, int world, int device,
 extern "C" int nmg_comm_destroy(nmg_comm* c) {
     if (!c) return NMG_OK;
     if (c->comm) c->nccl->comm_destroy(c->comm);
+    if (c->bar) cudaFree(c->bar);
     delete c;
+    return NMG_OK;
+}
+
+extern "C" int nmg_comm_barrier(nmg_comm* c, void* stream) {
+    if (!c) return set_error(NMG_INVALID_ARGUMENT, "nmg_comm_barrier: null communicator");
+    // An in-place one-byte all-gather: it completes on a rank only after every
+    // rank has reached it, i.e. after each rank's earlier work on its stream.
+    const nccl_result r = c->nccl->all_gather(c->bar + c->rank, c->bar, 1, /*ncclUint8*/ 1, c->comm, (cudaStream_t)stream);
+    if (r != 0) return set_error(NMG_COMM_ERROR, "nmg_comm_barrier: %s", nccl_msg(c->nccl, r));
+    return NMG_OK;
+}
+
+// ---- device buffers shared between the processes of one node (CUDA IPC) ----
+
+extern "C" int nmg_shared_alloc(int64_t bytes, int device, void** ptr, void* handle64) {
+    if (!ptr || !handle64 || bytes <= 0) return set_error(NMG_INVALID_ARGUMENT, "nmg_shared_alloc: bad argument");
+    *ptr = nullptr;
+    int prev = 0;
+    NMG_CUDA_TRY(cudaGetDevice(&prev));
+    NMG_CUDA_TRY(cudaSetDevice(device));
+    void* p = nullptr;
+    cudaError_t e = cudaMalloc(&p, (size_t)bytes);
+    if (e == cudaSuccess) e = cudaMemset(p, 0, (size_t)bytes);
+    if (e == cudaSuccess) e = cudaIpcGetMemHandle((cudaIpcMemHandle_t*)handle64, p);
+    cudaSetDevice(prev);
+    if (e != cudaSuccess) {
+        if (p) cudaFree(p);
+        return set_error(NMG_CUDA_ERROR, "nmg_shared_alloc: %s", cudaGetErrorString(e));
+    }
+    *ptr = p;
+    return NMG_OK;
+}
+
+extern "C" int nmg_shared_free(void* ptr) {
+    if (ptr) NMG_CUDA_TRY(cudaFree(ptr));
+    return NMG_OK;
+}
+
+extern "C" int nmg_ipc_open(const void* handle64, int device, void** ptr) {
+    if (!handle64 || !ptr) return set_error(NMG_INVALID_ARGUMENT, "nmg_ipc_open: null argument");
+    *ptr = nullptr;
+    int prev = 0;
+    NMG_CUDA_TRY(cudaGetDevice(&prev));
+    NMG_CUDA_TRY(cudaSetDevice(device));
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handle64, sizeof(h));
+    const cudaError_t e = cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+    cudaSetDevice(prev);
+    if (e != cudaSuccess) return set_error(NMG_CUDA_ERROR, "nmg_ipc_open: %s", cudaGetErrorString(e));
+    return NMG_OK;
+}
+
+extern "C" int nmg_ipc_close(void* ptr) {
+    if (ptr) NMG_CUDA_TRY(cudaIpcCloseMemHandle(ptr));
     return NMG_OK;
 }
 

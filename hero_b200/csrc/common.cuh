@@ -211,7 +211,7 @@ __device__ __forceinline__ void bulk_g2s(void* smem_dst, const void* gmem_src, u
         : "memory");
 }
 
-// 2-D tiled TMA load (no multicast) with an L2 cache hint.
+// 2-D tiled TMA load into this CTA's shared memory.
 __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, int32_t x, int32_t y,
                                             uint64_t* bar) {
     asm volatile(
@@ -221,7 +221,7 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* m
         : "memory");
 }
 
-// 3-D tiled TMA load (no multicast).
+// 3-D tiled TMA load into this CTA's shared memory.
 __device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* map, int32_t x, int32_t y, int32_t z,
                                             uint64_t* bar) {
     asm volatile(

@@ -1,5 +1,5 @@
 // tcgen05.cuh -- inline-PTX wrappers for the 5th-generation tensor core path
-// (tcgen05.* + TMEM) on sm_100a, cta_group::1 only, no cluster multicast.
+// (tcgen05.* + TMEM) on sm_100a, cta_group::1 only.
 #pragma once
 #include <stdint.h>
 

@@ -296,17 +296,20 @@ class DeltaNetState:
         return self.tensor()[h]
 
 
-def _from_ptr(ptr: int, n: int, device: int) -> torch.Tensor:
-    """Wrap n fp32 device values at ptr as a tensor (the owner keeps them alive)."""
+def _from_ptr(ptr: int, n: int, device: int, dtype=torch.float32) -> torch.Tensor:
+    """Wrap n device values at ptr as a tensor (the owner keeps them alive)."""
+    typestr, view = {torch.float32: ("<f4", None), torch.float16: ("<f2", None),
+                     torch.bfloat16: ("<i2", torch.bfloat16)}[dtype]
 
     class _Holder:
         def __init__(self, p, n, dev):
-            self.__cuda_array_interface__ = {"shape": (n,), "typestr": "<f4", "data": (p, False), "version": 3,
+            self.__cuda_array_interface__ = {"shape": (n,), "typestr": typestr, "data": (p, False), "version": 3,
                                              "strides": None}
             self.dev = dev
 
     with torch.cuda.device(device):
-        return torch.as_tensor(_Holder(ptr, n, device), device=f"cuda:{device}")
+        t = torch.as_tensor(_Holder(ptr, n, device), device=f"cuda:{device}")
+    return t.view(view) if view is not None else t
 
 
 def gated_delta_step(state_head: torch.Tensor, q, k, v, gate, beta) -> torch.Tensor:
@@ -340,3 +343,57 @@ def delta_prefill(state: DeltaNetState, q, k, v, gate, beta, hk: int, *, chunk: 
     call("nmg_delta_prefill", state.handle, int(hk), T, _ptr(_dev(q)), _ptr(_dev(k)), _ptr(_dev(v)), _ptr(_dev(gate)),
          _ptr(_dev(beta)), _ptr(out), int(chunk), _stream(v.device))
     return out
+
+
+# ---- multi-GPU: output rows assembled by the attention epilogue -------------
+
+class SharedRows:
+    """A [rows, width] device buffer other processes of the node can map.
+
+    ``handle`` (64 bytes) goes to the other ranks, which pass it to
+    :func:`open_peer`; every rank then hands all ranks' pointers to
+    :func:`attend_fanout`, whose epilogue writes its heads into each of them."""
+
+    def __init__(self, rows: int, width: int, dtype=torch.bfloat16, device: int = 0):
+        self.rows, self.width, self.dtype, self.device = int(rows), int(width), dtype, int(device)
+        nbytes = self.rows * self.width * torch.tensor([], dtype=dtype).element_size()
+        self._ptr = ctypes.c_void_p()
+        h = (ctypes.c_char * 64)()
+        call("nmg_shared_alloc", nbytes, self.device, ctypes.byref(self._ptr), h)
+        self.handle = bytes(h)
+
+    @property
+    def ptr(self) -> int:
+        return self._ptr.value
+
+    def tensor(self) -> torch.Tensor:
+        return _from_ptr(self.ptr, self.rows * self.width, self.device, self.dtype).view(self.rows, self.width)
+
+    def close(self):
+        if self._ptr.value:
+            call("nmg_shared_free", self._ptr)
+            self._ptr = ctypes.c_void_p()
+
+
+def open_peer(handle: bytes, device: int) -> int:
+    """Map another process's SharedRows into this one; returns the device pointer."""
+    h = (ctypes.c_char * 64).from_buffer_copy(handle)
+    p = ctypes.c_void_p()
+    call("nmg_ipc_open", h, int(device), ctypes.byref(p))
+    return p.value
+
+
+def close_peer(ptr: int) -> None:
+    call("nmg_ipc_close", ctypes.c_void_p(ptr))
+
+
+def attend_fanout(cache: _Cache, q: torch.Tensor, at: int, scale: float | None, outs, row_elems: int, col0: int,
+                  out_dtype=torch.bfloat16) -> None:
+    """attend() with each output row written to every pointer in ``outs`` at
+    column ``col0`` of rows ``row_elems`` elements long."""
+    q = _dev(q)
+    hq = q.shape[-1] // cache.head_dim
+    arr = (ctypes.c_void_p * len(outs))(*[int(p) for p in outs])
+    call("nmg_attend_fanout", cache.handle, hq, _ptr(q), _DT[q.dtype], q.shape[0], int(at),
+         ctypes.c_float(scale if scale is not None else 1.0), 0 if scale is None else 1, arr, len(outs),
+         int(row_elems), int(col0), _DT[out_dtype], _stream(q.device))

@@ -231,6 +231,30 @@ NMG_API int nmg_allgather(nmg_comm* comm, const void* send, void* recv, int64_t 
  * the reference row layout [rows][world*hq_local*d] (elem_bytes per value). */
 NMG_API int nmg_gather_heads_to_rows(const void* gathered, void* out, int world, int64_t rows, int64_t row_bytes_per_rank,
                              void* stream);
+/* Stream-ordered barrier: completes on each rank once every rank's earlier
+ * work on its stream has completed (used after nmg_attend_fanout wrote into
+ * the other ranks' buffers). */
+NMG_API int nmg_comm_barrier(nmg_comm* comm, void* stream);
+
+/* ---- the gather fused into the attention epilogue ---------------------------
+ *
+ * No reference counterpart (the reference is single-process).  Each rank
+ * allocates its output buffer with nmg_shared_alloc and ships the 64-byte
+ * handle to the other ranks of the node, which map it with nmg_ipc_open.
+ * nmg_attend_fanout then writes this rank's heads of every output row into
+ * all mapped buffers at once (NVLink stores from the epilogue), so the
+ * reference's [rows][H*D] rows assemble on every GPU without a separate
+ * all-gather; nmg_comm_barrier orders the stores before the rows are read. */
+NMG_API int nmg_shared_alloc(int64_t bytes, int device, void** ptr, void* handle64);
+NMG_API int nmg_shared_free(void* ptr);
+NMG_API int nmg_ipc_open(const void* handle64, int device, void** ptr);
+NMG_API int nmg_ipc_close(void* ptr);
+/* nmg_attend for the cache's heads, each output row t (hq*head_dim values)
+ * written to outs[i] + t*out_row_elems + out_col0 (elements) for i < nout
+ * (1..8 device pointers, this GPU's or mapped peers'). */
+NMG_API int nmg_attend_fanout(const nmg_kv_cache* cache, int hq, const void* q, int q_dtype, int64_t rows,
+                              int64_t first_query, float scale, int use_scale, void* const* outs, int nout,
+                              int64_t out_row_elems, int64_t out_col0, int out_dtype, void* stream);
 
 #ifdef __cplusplus
 }

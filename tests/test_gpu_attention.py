@@ -325,3 +325,35 @@ print(float((out.view(T, hq, dh) - ref).abs().max()))
         r = subprocess.run([sys.executable, "-c", code, str(seed)], capture_output=True, text=True, timeout=120)
         assert r.returncode == 0, r.stderr[-2000:]
         assert float(r.stdout.strip().splitlines()[-1]) < 2e-3
+
+
+@pytest.mark.parametrize("rows", [256, 3])
+def test_attend_fanout_writes_every_output(dev, rows):
+    # The multi-GPU gather rides on this: each output row lands in every
+    # buffer at the given column offset (tcgen05 epilogue for 256 rows, the
+    # staged copy for a decode-sized call), bit-identical to nmg_attend.
+    hq, hkv, dh, S = 8, 2, 128, 512
+    g = torch.Generator(device=dev)
+    g.manual_seed(rows)
+    cache = nm.FullAttentionCache(hkv, dh, capacity=S, dtype="bf16")
+    cache.append(0, torch.randn(S, hkv * dh, device=dev, generator=g).bfloat16(),
+                 torch.randn(S, hkv * dh, device=dev, generator=g).bfloat16())
+    q = torch.randn(rows, hq * dh, device=dev, generator=g).bfloat16()
+    at = S - rows
+    want = nm.attend(cache, q, at, dh ** -0.5, out_dtype=torch.bfloat16)
+    width, col0 = 3 * hq * dh, hq * dh
+    outs = [torch.full((rows, width), float("nan"), device=dev, dtype=torch.bfloat16) for _ in range(2)]
+    nm.attend_fanout(cache, q, at, dh ** -0.5, [o.data_ptr() for o in outs], width, col0, torch.bfloat16)
+    torch.cuda.synchronize(dev)
+    for o in outs:
+        assert torch.equal(o[:, col0:col0 + hq * dh], want)
+        assert torch.isnan(o[:, :col0].float()).all() and torch.isnan(o[:, col0 + hq * dh:].float()).all()
+
+
+def test_attend_fanout_rejects_columns_that_do_not_fit(dev):
+    cache = nm.FullAttentionCache(2, 128, capacity=128, dtype="bf16")
+    cache.append(0, torch.zeros(128, 256, device=dev).bfloat16(), torch.zeros(128, 256, device=dev).bfloat16())
+    q = torch.zeros(128, 8 * 128, device=dev).bfloat16()
+    o = torch.empty(128, 8 * 128, device=dev, dtype=torch.bfloat16)
+    with pytest.raises(InvalidArgument):
+        nm.attend_fanout(cache, q, 0, 1.0, [o.data_ptr()], 8 * 128, 128, torch.bfloat16)
