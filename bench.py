@@ -86,6 +86,7 @@ class ClockSampler:
         self.proc = None
         self.thread = None
         self.rows = []  # (sm_mhz, max_mhz, set of reason names)
+        self.err = None
         self.path = os.path.join("/tmp", f"nmg_clocks_{os.getpid()}.csv")
 
     def _nvml_loop(self, nv, h, stop):
@@ -99,7 +100,8 @@ class ClockSampler:
                 sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
                 r = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
                 self.rows.append((float(sm), float(smax), {n for n, b in bits.items() if r & b}))
-            except Exception:
+            except Exception as e:
+                self.err = f"{type(e).__name__}: {e}"
                 break
             stop.wait(0.002)
 
@@ -129,6 +131,14 @@ class ClockSampler:
         if self.thread is not None:
             self.stop.set()
             self.thread.join(timeout=2)
+            if not self.rows:  # a region shorter than the thread's first wake-up: sample once more now
+                try:
+                    import pynvml as nv
+                    h = nv.nvmlDeviceGetHandleByIndex(int(self.gpu_id))
+                    self.rows.append((float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)),
+                                      float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)), set()))
+                except Exception as e:
+                    self.err = self.err or f"{type(e).__name__}: {e}"
         if self.proc is not None:
             time.sleep(0.25)
             self.proc.terminate()
@@ -152,7 +162,7 @@ class ClockSampler:
             except Exception:
                 pass
         if not rows:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0, "error": self.err}
         sm = [r[0] for r in rows]
         smax = max(r[1] for r in rows)
         loaded = [x for x in sm if x > 0.5 * smax] or sm

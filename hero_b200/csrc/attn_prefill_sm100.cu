@@ -262,7 +262,6 @@ __global__ void __launch_bounds__(PfCfg<DH>::THREADS, 1) attn_prefill_kernel(con
         const int row = quad * 32 + lane;
         const uint32_t t_lane = tmem + ((uint32_t)(quad * 32) << 16);
         const int64_t qpos = a.first_query + t0 + row;
-        const bool row_valid = t0 + row < a.rows;
         const int64_t lo = vis_lo(a, qpos), hi = vis_hi(a, qpos);
         float* red = (float*)(smem + C::RED_OFF);  // [parity][part][row]
         const int col0 = part * C::PART_N;
@@ -382,40 +381,103 @@ __global__ void __launch_bounds__(PfCfg<DH>::THREADS, 1) attn_prefill_kernel(con
         float l_row = 0.f;
 #pragma unroll
         for (int q2 = 0; q2 < C::PARTS; ++q2) l_row += red[(ls * C::PARTS + q2) * BM + row];
-        if (ok && nblk > 0 && __all_sync(0xffffffffu, dev::mbar_wait(o_done, (nblk - 1) & 1, a.err))) {
+        // Epilogue: normalise O.  With one local output every thread stores
+        // its own row part.  With several (other GPUs' memory among them) the
+        // tile is staged in shared memory (the Q and K stages are idle now:
+        // every MMA has completed) and all softmax threads copy whole row
+        // segments (DH * out_es contiguous bytes per row) to each output, so
+        // a warp writes two or more full segments per store instead of 32
+        // rows' 16-byte pieces, which NVLink carries far less efficiently.
+        const bool have_o = ok && nblk > 0 && __all_sync(0xffffffffu, dev::mbar_wait(o_done, (nblk - 1) & 1, a.err));
+        const int oes = a.out_dtype == NMG_F32 ? 4 : 2;
+        const int cpr = DH * oes / 16;  // 16-byte chunks per row: 16, 32 or 64
+        unsigned char* tile = smem + C::Q_OFF;
+        if (have_o && a.nout == 1) {  // one local output: each thread stores its own row part
             tc::fence_after_sync();
             const float inv = 1.f / l_row;
+            const bool row_valid = t0 + row < a.rows;
             const int64_t obase = (t0 + row) * a.out_row_elems + a.out_col0 + (int64_t)h * DH + part * C::PART_D;
 #pragma unroll 1
             for (int c = 0; c < C::PART_D / 32; ++c) {
                 uint32_t r[32];
                 tc::ld_32x32b_x32(t_lane + C::O_COL + part * C::PART_D + c * 32, r);
-                if (row_valid) {
-                    if (a.out_dtype == NMG_F32) {
+                if (!row_valid) continue;
+                if (a.out_dtype == NMG_F32) {
+                    uint4* dst = (uint4*)((float*)a.outs[0] + obase + c * 32);
 #pragma unroll
-                        for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * inv);
-                        for (int o = 0; o < a.nout; ++o) {
-                            uint4* dst = (uint4*)((float*)a.outs[o] + obase + c * 32);
+                    for (int e = 0; e < 8; ++e)
+                        dst[e] = make_uint4(__float_as_uint(__uint_as_float(r[4 * e]) * inv),
+                                            __float_as_uint(__uint_as_float(r[4 * e + 1]) * inv),
+                                            __float_as_uint(__uint_as_float(r[4 * e + 2]) * inv),
+                                            __float_as_uint(__uint_as_float(r[4 * e + 3]) * inv));
+                } else {
+                    const bool obf = a.out_dtype == NMG_BF16;
+                    uint4* dst = (uint4*)((uint16_t*)a.outs[0] + obase + c * 32);
 #pragma unroll
-                            for (int e = 0; e < 8; ++e) dst[e] = make_uint4(r[4 * e], r[4 * e + 1], r[4 * e + 2], r[4 * e + 3]);
-                        }
-                    } else {
-                        const bool obf = a.out_dtype == NMG_BF16;
-                        uint32_t w[16];
+                    for (int e = 0; e < 4; ++e) {
+                        uint32_t w[4];
 #pragma unroll
-                        for (int t = 0; t < 16; ++t) {
-                            const float f0 = __uint_as_float(r[2 * t]) * inv, f1 = __uint_as_float(r[2 * t + 1]) * inv;
+                        for (int t = 0; t < 4; ++t) {
+                            const float f0 = __uint_as_float(r[8 * e + 2 * t]) * inv;
+                            const float f1 = __uint_as_float(r[8 * e + 2 * t + 1]) * inv;
                             const uint32_t b0 = obf ? dev::f32_to_bf16_bits(f0) : dev::f32_to_f16_bits(f0);
                             const uint32_t b1 = obf ? dev::f32_to_bf16_bits(f1) : dev::f32_to_f16_bits(f1);
                             w[t] = b0 | (b1 << 16);
                         }
-                        for (int o = 0; o < a.nout; ++o) {
-                            uint4* dst = (uint4*)((uint16_t*)a.outs[o] + obase + c * 32);
-#pragma unroll
-                            for (int e = 0; e < 4; ++e) dst[e] = make_uint4(w[4 * e], w[4 * e + 1], w[4 * e + 2], w[4 * e + 3]);
-                        }
+                        dst[e] = make_uint4(w[0], w[1], w[2], w[3]);
                     }
                 }
+            }
+        } else if (have_o) {
+            tc::fence_after_sync();
+            const float inv = 1.f / l_row;
+#pragma unroll 1
+            for (int c = 0; c < C::PART_D / 32; ++c) {
+                uint32_t r[32];
+                tc::ld_32x32b_x32(t_lane + C::O_COL + part * C::PART_D + c * 32, r);
+                const int col = part * C::PART_D + c * 32;  // first of this thread's 32 columns
+                if (a.out_dtype == NMG_F32) {
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) {
+                        const int ch = col / 4 + e;
+                        *(uint4*)(tile + row * cpr * 16 + ((ch ^ (row & 15)) << 4)) =
+                            make_uint4(__float_as_uint(__uint_as_float(r[4 * e]) * inv),
+                                       __float_as_uint(__uint_as_float(r[4 * e + 1]) * inv),
+                                       __float_as_uint(__uint_as_float(r[4 * e + 2]) * inv),
+                                       __float_as_uint(__uint_as_float(r[4 * e + 3]) * inv));
+                    }
+                } else {
+                    const bool obf = a.out_dtype == NMG_BF16;
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        uint32_t w[4];
+#pragma unroll
+                        for (int t = 0; t < 4; ++t) {
+                            const float f0 = __uint_as_float(r[8 * e + 2 * t]) * inv;
+                            const float f1 = __uint_as_float(r[8 * e + 2 * t + 1]) * inv;
+                            const uint32_t b0 = obf ? dev::f32_to_bf16_bits(f0) : dev::f32_to_f16_bits(f0);
+                            const uint32_t b1 = obf ? dev::f32_to_bf16_bits(f1) : dev::f32_to_f16_bits(f1);
+                            w[t] = b0 | (b1 << 16);
+                        }
+                        const int ch = col / 8 + e;
+                        *(uint4*)(tile + row * cpr * 16 + ((ch ^ (row & 15)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+                    }
+                }
+            }
+        }
+        // Every softmax thread reaches this barrier (have_o is uniform across
+        // the CTA: the o_done wait is the same for all, and a timeout sets the
+        // error flag but still arrives here).
+        asm volatile("bar.sync 2, %0;" ::"r"(C::SOFTMAX_THREADS) : "memory");
+        if (have_o && a.nout > 1) {
+            const int sid = threadIdx.x - 96;  // 0 .. SOFTMAX_THREADS - 1
+            const int valid_rows = (int)(t_last - t0 + 1);
+            const int64_t col_base = a.out_col0 + (int64_t)h * DH;
+            for (int idx = sid; idx < valid_rows * cpr; idx += C::SOFTMAX_THREADS) {
+                const int rr = idx / cpr, ch = idx - rr * cpr;
+                const uint4 val = *(const uint4*)(tile + rr * cpr * 16 + ((ch ^ (rr & 15)) << 4));
+                const int64_t off = ((t0 + rr) * a.out_row_elems + col_base) * oes + ch * 16;
+                for (int o = 0; o < a.nout; ++o) *(uint4*)((unsigned char*)a.outs[o] + off) = val;
             }
             // Stores to other GPUs' memory are visible system-wide before this grid completes.
             if (a.nout > 1) __threadfence_system();
