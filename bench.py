@@ -323,8 +323,11 @@ class Comm:
 def bench_prefill(args, torch, dist, rank, world, dev):
     from hero_b200 import nm
 
+    from hero_b200.shard import exchange, kv_shard
+
     S, hq, hkv, dh = S2, HQ2, HKV2, DH2
-    hkv_l, hq_l = hkv // world, hq // world
+    sh = kv_shard(rank, world, hkv, hq)
+    hkv_l, hq_l = sh.kv1 - sh.kv0, sh.q1 - sh.q0
     scale = 1.0 / math.sqrt(dh)
     set_bytes = S * (hq_l * dh * 2 * 2 + hkv_l * dh * 2 * 4)
     R = int(min(64, max(4, math.ceil(3 * L2_BYTES / set_bytes))))
@@ -349,8 +352,7 @@ def bench_prefill(args, torch, dist, rank, world, dev):
         shared = [nm.SharedRows(S, hq * dh, torch.bfloat16, dev.index) for _ in range(2)]
         peers = []
         for b in range(2):
-            handles = [None] * world
-            dist.all_gather_object(handles, shared[b].handle)
+            handles = exchange(dist, shared[b].handle)
             peers.append([shared[b].ptr if r == rank else nm.open_peer(handles[r], dev.index) for r in range(world)])
     stream = torch.cuda.current_stream(dev)
     sp = ctypes.c_void_p(stream.cuda_stream)
@@ -364,7 +366,7 @@ def bench_prefill(args, torch, dist, rank, world, dev):
         if comm is None:
             nm.attend(c, q, 0, scale, out=o)
         else:
-            nm.attend_fanout(c, q, 0, scale, peers[i & 1], hq * dh, rank * hq_l * dh)
+            nm.attend_fanout(c, q, 0, scale, peers[i & 1], hq * dh, sh.out_col0(dh))
         if ev is not None:
             ev[1].record(stream)
         if comm is not None:
@@ -436,7 +438,7 @@ def bench_prefill(args, torch, dist, rank, world, dev):
         c.reset()
         c.append(0, k, v)
         if comm is not None:
-            nm.attend_fanout(c, q, 0, scale, peers[i & 1], hq * dh, rank * hq_l * dh)
+            nm.attend_fanout(c, q, 0, scale, peers[i & 1], hq * dh, sh.out_col0(dh))
             comm.barrier(sp)
             out_host.copy_(shared[i & 1].tensor(), non_blocking=True)
         else:
