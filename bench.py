@@ -355,7 +355,9 @@ def bench_prefill(args, torch, dist, rank, world, dev):
             handles = exchange(dist, shared[b].handle)
             peers.append([shared[b].ptr if r == rank else nm.open_peer(handles[r], dev.index) for r in range(world)])
     stream = torch.cuda.current_stream(dev)
-    sp = ctypes.c_void_p(stream.cuda_stream)
+
+    def cur():  # the stream a call is issued on (the capture stream while a graph records)
+        return ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
 
     def step(i, ev=None):
         q, k, v, c, o = sets[i % R]
@@ -370,35 +372,56 @@ def bench_prefill(args, torch, dist, rank, world, dev):
         if ev is not None:
             ev[1].record(stream)
         if comm is not None:
-            comm.barrier(sp)
+            comm.barrier(cur())
 
     def step_nccl(i):  # the unfused alternative: attend, NCCL all-gather, permute
         q, k, v, c, o = sets[i % R]
         c.reset()
         c.append(0, k, v)
         nm.attend(c, q, 0, scale, out=o)
-        comm.allgather(o, gathered, sp)
-        comm.to_rows(gathered, full, S, hq_l * dh * 2, sp)
+        comm.allgather(o, gathered, cur())
+        comm.to_rows(gathered, full, S, hq_l * dh * 2, cur())
 
     def barrier():
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize(dev)
 
+    def capture(fn, n, first):
+        """A CUDA graph of n steps fn(first), fn(first + 1), ...: the host work of
+        each call (argument checks, tensor maps, the NCCL launch) happens once,
+        here, instead of inside the timed region."""
+        g = torch.cuda.CUDAGraph()
+        cs = torch.cuda.Stream(dev)
+        cs.wait_stream(stream)
+        with torch.cuda.graph(g, stream=cs):
+            for i in range(n):
+                fn(first + i)
+        stream.wait_stream(cs)
+        return g
+
     for i in range(args.warmup):
         step(i)
     barrier()
-    kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    # attention-kernel time, CUDA events around each eager call of one rotation
+    kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(R)]
+    for i in range(R):
+        step(i, kev[i])
+    barrier()
+    kernel_ms = sum(a.elapsed_time(b) for a, b in kev) / R
+    # the timed region: exactly args.steps steps, replayed from one graph
+    graph = capture(step, args.steps, args.warmup)
+    graph.replay()  # untimed first replay
+    barrier()
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(gpu_smi_id(torch, dev)) as clk:
         barrier()
         t0.record(stream)
-        for i in range(args.steps):
-            step(args.warmup + i, kev[i])
+        graph.replay()
         t1.record(stream)
         barrier()
     ms = t0.elapsed_time(t1)
-    kernel_ms = sum(a.elapsed_time(b) for a, b in kev) / args.steps
+    del graph
     if world > 1:
         tt = torch.tensor([ms, kernel_ms], device=dev, dtype=torch.float64)
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
@@ -407,22 +430,25 @@ def bench_prefill(args, torch, dist, rank, world, dev):
     value = c2_flops() / (ms_step * 1e-3) / 1e12
     collective = None
     if comm is not None:
+        n_cmp = max(3, args.steps // 4)
         for i in range(2):
             step_nccl(i)
         barrier()
-        n_cmp = max(3, args.steps // 4)
+        g2 = capture(step_nccl, n_cmp, 0)
+        g2.replay()
+        barrier()
         u0, u1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         u0.record(stream)
-        for i in range(n_cmp):
-            step_nccl(i)
+        g2.replay()
         u1.record(stream)
         barrier()
+        del g2
         tt = torch.tensor([u0.elapsed_time(u1) / n_cmp], device=dev, dtype=torch.float64)
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         collective = {"fused_epilogue_ms_per_step": ms_step, "nccl_allgather_ms_per_step": float(tt[0]),
                       "attention_only_ms": kernel_ms,
                       "note": "fused: NVLink stores from the attention epilogue + one stream-ordered barrier; "
-                              "nccl: attention, ncclAllGather, head-to-row permutation"}
+                              "nccl: attention, ncclAllGather, head-to-row permutation; both timed as CUDA graphs"}
 
     # ---- end to end through the C ABI with host buffers
     pin = lambda t: t.cpu().pin_memory()
@@ -439,8 +465,9 @@ def bench_prefill(args, torch, dist, rank, world, dev):
         c.append(0, k, v)
         if comm is not None:
             nm.attend_fanout(c, q, 0, scale, peers[i & 1], hq * dh, sh.out_col0(dh))
-            comm.barrier(sp)
-            out_host.copy_(shared[i & 1].tensor(), non_blocking=True)
+            comm.barrier(cur())
+            if rank == 0:  # every GPU holds the assembled rows; one copy goes to the host
+                out_host.copy_(shared[i & 1].tensor(), non_blocking=True)
         else:
             nm.attend(c, q, 0, scale, out=o)
             out_host.copy_(o, non_blocking=True)
@@ -460,7 +487,7 @@ def bench_prefill(args, torch, dist, rank, world, dev):
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         e2e_ms = float(tt[0])
     h2d = world * S * (hq_l + 2 * hkv_l) * dh * 2
-    d2h = world * S * hq * dh * 2
+    d2h = S * hq * dh * 2
     if comm is not None:
         torch.cuda.synchronize(dev)
         dist.barrier()  # every rank is done writing into the mapped buffers

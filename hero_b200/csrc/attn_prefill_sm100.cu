@@ -479,8 +479,9 @@ __global__ void __launch_bounds__(PfCfg<DH>::THREADS, 1) attn_prefill_kernel(con
                 const int64_t off = ((t0 + rr) * a.out_row_elems + col_base) * oes + ch * 16;
                 for (int o = 0; o < a.nout; ++o) *(uint4*)((unsigned char*)a.outs[o] + off) = val;
             }
-            // Stores to other GPUs' memory are visible system-wide before this grid completes.
-            if (a.nout > 1) __threadfence_system();
+            // No fence here: the caller orders these stores before any read of
+            // the rows with a stream-ordered barrier (nmg_comm_barrier), which
+            // starts only after this grid, stores included, has completed.
         }
     }
 
