@@ -29,6 +29,8 @@
 // scale * q.k, then the alpha-weighted sum of values; visibility is
 // CausalWindow (nm/src/attention.hpp:154-176) in closed form per row.
 #include <math.h>
+#include <algorithm>
+#include <vector>
 #include <stdio.h>
 
 #include "attn.cuh"
@@ -68,6 +70,8 @@ struct PfCfg {
 };
 
 constexpr int kMaxFanout = 8;
+constexpr int kMaxItems = 2048;  // work items of a split launch
+constexpr int kMaxTiles = 1024;  // query tiles of a split launch
 
 struct PrefillArgs {
     CUtensorMap tm_q;  // (d, head, row) over q [rows][hq*DH]
@@ -85,6 +89,18 @@ struct PrefillArgs {
     int64_t out_row_elems, out_col0;
     int out_dtype;
     int* err;
+    // Key splits (n_items > 0): CTA x takes items[x] = tile << 12 | split << 6 |
+    // nsplit, keys blocks [split * split_blocks, +split_blocks) of the tile's
+    // range.  A split tile's CTAs leave (O, m, l) partials in part (slot
+    // part_base[tile] + split of head h: [BM][DH + 4] fp32, O then m, l, with
+    // rows padded to 16 bytes) and the last one
+    // to finish (ticket per head and tile) merges them.  n_items == 0: one
+    // CTA per tile, heaviest tile first.
+    int n_items, split_blocks, nparts, ntiles;
+    float* part;
+    int* tickets;
+    uint32_t items[kMaxItems];
+    uint32_t part_base[kMaxTiles];
 };
 
 __device__ __forceinline__ float ex2(float x) {
@@ -130,7 +146,15 @@ __global__ void __launch_bounds__(PfCfg<DH>::THREADS, 1) attn_prefill_kernel(con
     uint32_t* tmem_slot = (uint32_t*)(smem + C::TMEMPTR_OFF);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int tile = gridDim.x - 1 - blockIdx.x;  // heaviest tiles first
+    int tile, split = 0, nsplit = 1;
+    if (a.n_items > 0) {
+        const uint32_t it = a.items[blockIdx.x];
+        tile = (int)(it >> 12);
+        split = (int)((it >> 6) & 63u);
+        nsplit = (int)(it & 63u);
+    } else {
+        tile = gridDim.x - 1 - blockIdx.x;  // heaviest tiles first
+    }
     const int h = blockIdx.y;
     const int hk = h / a.g;
     const int64_t t0 = (int64_t)tile * BM;
@@ -138,8 +162,9 @@ __global__ void __launch_bounds__(PfCfg<DH>::THREADS, 1) attn_prefill_kernel(con
     const int64_t q_first = a.first_query + t0, q_last = a.first_query + t_last;
     const int64_t u_lo = vis_lo(a, q_first) - a.base;
     const int64_t u_hi = vis_hi(a, q_last) - a.base;
-    const int64_t j_begin = u_lo / BN;
-    const int nblk = (int)(u_hi / BN + 1 - j_begin);
+    const int nblk_all = (int)(u_hi / BN + 1 - u_lo / BN);
+    const int64_t j_begin = u_lo / BN + (int64_t)split * a.split_blocks;
+    const int nblk = nsplit == 1 ? nblk_all : min(a.split_blocks, nblk_all - split * a.split_blocks);
     // A block needs no mask when every row of the tile sees all of it.
     const int64_t full_lo = vis_lo(a, q_last), full_hi = vis_hi(a, q_first);
 
@@ -389,10 +414,85 @@ __global__ void __launch_bounds__(PfCfg<DH>::THREADS, 1) attn_prefill_kernel(con
         // a warp writes two or more full segments per store instead of 32
         // rows' 16-byte pieces, which NVLink carries far less efficiently.
         const bool have_o = ok && nblk > 0 && __all_sync(0xffffffffu, dev::mbar_wait(o_done, (nblk - 1) & 1, a.err));
+        if (nsplit > 1) {
+            // A split of a tile: leave the unnormalised O with its m and l
+            // (base-2 units), and the last split of the tile merges them.
+            float* mine = a.part + (((int64_t)h * a.nparts + a.part_base[tile] + split) * BM + row) * (DH + 4);
+            if (have_o) {
+                tc::fence_after_sync();
+#pragma unroll 1
+                for (int c = 0; c < C::PART_D / 32; ++c) {
+                    uint32_t r[32];
+                    tc::ld_32x32b_x32(t_lane + C::O_COL + part * C::PART_D + c * 32, r);
+                    float4* dst = (float4*)(mine + part * C::PART_D + c * 32);
+#pragma unroll
+                    for (int e = 0; e < 8; ++e)
+                        dst[e] = make_float4(__uint_as_float(r[4 * e]), __uint_as_float(r[4 * e + 1]),
+                                             __uint_as_float(r[4 * e + 2]), __uint_as_float(r[4 * e + 3]));
+                }
+                if (part == 0) {
+                    mine[DH] = m_run;
+                    mine[DH + 1] = l_row;
+                }
+            }
+            __threadfence();
+            asm volatile("bar.sync 2, %0;" ::"r"(C::SOFTMAX_THREADS) : "memory");
+            int* last_flag = (int*)(smem + C::RED_OFF);  // red[] is no longer read
+            if (threadIdx.x == 96) {
+                int* ticket = a.tickets + (int64_t)h * a.ntiles + tile;
+                const int prev = atomicAdd(ticket, 1);
+                const bool last = prev == nsplit - 1;
+                if (last) *ticket = 0;  // ready for the next launch
+                *last_flag = last;
+            }
+            asm volatile("bar.sync 2, %0;" ::"r"(C::SOFTMAX_THREADS) : "memory");
+            if (*last_flag) {
+                __threadfence();
+                const int sid = threadIdx.x - 96;
+                const int valid_rows = (int)(t_last - t0 + 1);
+                const float* base = a.part + ((int64_t)h * a.nparts + a.part_base[tile]) * BM * (DH + 4);
+                const int64_t slot = (int64_t)BM * (DH + 4);
+                const int oes = a.out_dtype == NMG_F32 ? 4 : 2;
+                // 4 output columns per work unit
+                for (int idx = sid; idx < valid_rows * (DH / 4); idx += C::SOFTMAX_THREADS) {
+                    const int rr = idx / (DH / 4), d0 = (idx - rr * (DH / 4)) * 4;
+                    float M = -INFINITY;
+                    for (int sp = 0; sp < nsplit; ++sp) M = fmaxf(M, __ldcg(base + sp * slot + rr * (DH + 4) + DH));
+                    float L = 0.f, o4[4] = {0.f, 0.f, 0.f, 0.f};
+                    for (int sp = 0; sp < nsplit; ++sp) {
+                        const float* rp = base + sp * slot + rr * (DH + 4);
+                        const float m = __ldcg(rp + DH);
+                        if (m == -INFINITY) continue;
+                        const float w = ex2(m - M);
+                        L = fmaf(w, __ldcg(rp + DH + 1), L);
+                        const float4 v = __ldcg((const float4*)(rp + d0));
+                        o4[0] = fmaf(w, v.x, o4[0]), o4[1] = fmaf(w, v.y, o4[1]);
+                        o4[2] = fmaf(w, v.z, o4[2]), o4[3] = fmaf(w, v.w, o4[3]);
+                    }
+                    const float inv = 1.f / L;
+                    const int64_t off = ((t0 + rr) * a.out_row_elems + a.out_col0 + (int64_t)h * DH + d0) * oes;
+                    if (a.out_dtype == NMG_F32) {
+                        const float4 v = make_float4(o4[0] * inv, o4[1] * inv, o4[2] * inv, o4[3] * inv);
+                        for (int o = 0; o < a.nout; ++o) *(float4*)((unsigned char*)a.outs[o] + off) = v;
+                    } else {
+                        const bool obf = a.out_dtype == NMG_BF16;
+                        uint32_t w[2];
+#pragma unroll
+                        for (int t = 0; t < 2; ++t) {
+                            const float f0 = o4[2 * t] * inv, f1 = o4[2 * t + 1] * inv;
+                            const uint32_t b0 = obf ? dev::f32_to_bf16_bits(f0) : dev::f32_to_f16_bits(f0);
+                            const uint32_t b1 = obf ? dev::f32_to_bf16_bits(f1) : dev::f32_to_f16_bits(f1);
+                            w[t] = b0 | (b1 << 16);
+                        }
+                        for (int o = 0; o < a.nout; ++o) *(uint2*)((unsigned char*)a.outs[o] + off) = make_uint2(w[0], w[1]);
+                    }
+                }
+            }
+        }
         const int oes = a.out_dtype == NMG_F32 ? 4 : 2;
         const int cpr = DH * oes / 16;  // 16-byte chunks per row: 16, 32 or 64
-        unsigned char* tile = smem + C::Q_OFF;
-        if (have_o && a.nout == 1) {  // one local output: each thread stores its own row part
+        unsigned char* stage = smem + C::Q_OFF;
+        if (nsplit == 1 && have_o && a.nout == 1) {  // one local output: each thread stores its own row part
             tc::fence_after_sync();
             const float inv = 1.f / l_row;
             const bool row_valid = t0 + row < a.rows;
@@ -428,7 +528,7 @@ __global__ void __launch_bounds__(PfCfg<DH>::THREADS, 1) attn_prefill_kernel(con
                     }
                 }
             }
-        } else if (have_o) {
+        } else if (nsplit == 1 && have_o) {
             tc::fence_after_sync();
             const float inv = 1.f / l_row;
 #pragma unroll 1
@@ -440,7 +540,7 @@ __global__ void __launch_bounds__(PfCfg<DH>::THREADS, 1) attn_prefill_kernel(con
 #pragma unroll
                     for (int e = 0; e < 8; ++e) {
                         const int ch = col / 4 + e;
-                        *(uint4*)(tile + row * cpr * 16 + ((ch ^ (row & 15)) << 4)) =
+                        *(uint4*)(stage + row * cpr * 16 + ((ch ^ (row & 15)) << 4)) =
                             make_uint4(__float_as_uint(__uint_as_float(r[4 * e]) * inv),
                                        __float_as_uint(__uint_as_float(r[4 * e + 1]) * inv),
                                        __float_as_uint(__uint_as_float(r[4 * e + 2]) * inv),
@@ -460,7 +560,7 @@ __global__ void __launch_bounds__(PfCfg<DH>::THREADS, 1) attn_prefill_kernel(con
                             w[t] = b0 | (b1 << 16);
                         }
                         const int ch = col / 8 + e;
-                        *(uint4*)(tile + row * cpr * 16 + ((ch ^ (row & 15)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+                        *(uint4*)(stage + row * cpr * 16 + ((ch ^ (row & 15)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
                     }
                 }
             }
@@ -468,14 +568,14 @@ __global__ void __launch_bounds__(PfCfg<DH>::THREADS, 1) attn_prefill_kernel(con
         // Every softmax thread reaches this barrier (have_o is uniform across
         // the CTA: the o_done wait is the same for all, and a timeout sets the
         // error flag but still arrives here).
-        asm volatile("bar.sync 2, %0;" ::"r"(C::SOFTMAX_THREADS) : "memory");
-        if (have_o && a.nout > 1) {
+        if (nsplit == 1) asm volatile("bar.sync 2, %0;" ::"r"(C::SOFTMAX_THREADS) : "memory");
+        if (nsplit == 1 && have_o && a.nout > 1) {
             const int sid = threadIdx.x - 96;  // 0 .. SOFTMAX_THREADS - 1
             const int valid_rows = (int)(t_last - t0 + 1);
             const int64_t col_base = a.out_col0 + (int64_t)h * DH;
             for (int idx = sid; idx < valid_rows * cpr; idx += C::SOFTMAX_THREADS) {
                 const int rr = idx / cpr, ch = idx - rr * cpr;
-                const uint4 val = *(const uint4*)(tile + rr * cpr * 16 + ((ch ^ (rr & 15)) << 4));
+                const uint4 val = *(const uint4*)(stage + rr * cpr * 16 + ((ch ^ (rr & 15)) << 4));
                 const int64_t off = ((t0 + rr) * a.out_row_elems + col_base) * oes + ch * 16;
                 for (int o = 0; o < a.nout; ++o) *(uint4*)((unsigned char*)a.outs[o] + off) = val;
             }
@@ -600,6 +700,62 @@ int attend_rows_prefill(const nmg_kv_cache* c, int hq, const void* q, int q_dtyp
     a->hkv = c->hkv;
     a->g = hq / c->hkv;
     a->scale_log2 = scale * 1.4426950408889634f;
+    // Key splits when one CTA per query tile would leave the GPU's 148 SMs
+    // waiting on the heaviest tiles (a causal tile sees as many key blocks
+    // as its index): under two waves of CTAs, cut the tiles into pieces for
+    // about two waves.  With more CTAs the heavy-first order already
+    // balances the grid and the partials' round trip would only cost.
+    const int ntiles = (int)((rows + 127) / 128);
+    a->n_items = 0;
+    a->split_blocks = 0;
+    a->nparts = 0;
+    a->ntiles = ntiles;
+    a->part = nullptr;
+    a->tickets = nullptr;
+    if (ntiles <= kMaxTiles && (int64_t)ntiles * hq < 2 * 148) {
+        std::vector<int> nb(ntiles);
+        int64_t total = 0;
+        int maxb = 0;
+        for (int t = 0; t < ntiles; ++t) {
+            const int64_t qf = first_query + (int64_t)t * 128, ql = first_query + std::min<int64_t>((int64_t)t * 128 + 128, rows) - 1;
+            int64_t lo = floor_pos;
+            if (window > 0 && qf - window + 1 > lo) lo = qf - window + 1;
+            const int64_t hi = ql < newest ? ql : newest;
+            nb[t] = (int)((hi - c->base) / bn + 1 - (lo - c->base) / bn);
+            total += (int64_t)nb[t] * hq;
+            maxb = std::max(maxb, nb[t]);
+        }
+        int sb = (int)std::max<int64_t>(8, (total + 2 * 148 - 1) / (2 * 148));
+        sb = std::max(sb, (maxb + 62) / 63);  // at most 63 splits per tile
+        if (maxb > sb) {
+            std::vector<std::pair<int, uint32_t>> items;  // (blocks, packed item)
+            int parts = 0;
+            for (int t = 0; t < ntiles; ++t) {
+                const int ns = (nb[t] + sb - 1) / sb;
+                a->part_base[t] = (uint32_t)parts;
+                parts += ns;
+                for (int sp = 0; sp < ns; ++sp)
+                    items.push_back({std::min(sb, nb[t] - sp * sb), ((uint32_t)t << 12) | ((uint32_t)sp << 6) | (uint32_t)ns});
+            }
+            if ((int)items.size() <= kMaxItems) {
+                std::stable_sort(items.begin(), items.end(), [](const std::pair<int, uint32_t>& x, const std::pair<int, uint32_t>& y) { return x.first > y.first; });
+                for (size_t i = 0; i < items.size(); ++i) a->items[i] = items[i].second;
+                void* part = nullptr;
+                void* tickets = nullptr;
+                int st = device_scratch(c->device, (size_t)hq * parts * 128 * (dh + 4) * sizeof(float), &part);
+                if (st == NMG_OK) st = device_tickets(c->device, (size_t)hq * ntiles * sizeof(int), &tickets);
+                if (st != NMG_OK) {
+                    delete a;
+                    return st;
+                }
+                a->n_items = (int)items.size();
+                a->split_blocks = sb;
+                a->nparts = parts;
+                a->part = (float*)part;
+                a->tickets = (int*)tickets;
+            }
+        }
+    }
     for (int i = 0; i < nout; ++i) a->outs[i] = outs[i];
     a->nout = nout;
     a->out_row_elems = out_row_elems;
@@ -607,7 +763,7 @@ int attend_rows_prefill(const nmg_kv_cache* c, int hq, const void* q, int q_dtyp
     a->out_dtype = out_dtype;
     int st = device_error_flag(c->device, &a->err);
     if (st == NMG_OK) {
-        dim3 grid((unsigned)((rows + 127) / 128), (unsigned)hq);
+        dim3 grid(a->n_items > 0 ? (unsigned)a->n_items : (unsigned)ntiles, (unsigned)hq);
         if (dh == 128)
             st = c->dtype == NMG_BF16 ? launch_prefill<128, true>(*a, grid, stream) : launch_prefill<128, false>(*a, grid, stream);
         else

@@ -357,3 +357,40 @@ def test_attend_fanout_rejects_columns_that_do_not_fit(dev):
     o = torch.empty(128, 8 * 128, device=dev, dtype=torch.bfloat16)
     with pytest.raises(InvalidArgument):
         nm.attend_fanout(cache, q, 0, 1.0, [o.data_ptr()], 8 * 128, 128, torch.bfloat16)
+
+
+def test_prefill_key_splits_match_oracle(dev):
+    # 4 query heads over 4096 causal rows is little work for the GPU, so the
+    # heavy query tiles are split over several CTAs (8 key blocks each) whose
+    # partials the last CTA merges; the heaviest and lightest tiles against
+    # the reference reduction.
+    hq, hkv, dh, S = 4, 2, 128, 4096
+    k, v, q = rnd("bf16", 31, 1, (S, hkv * dh)), rnd("bf16", 31, 2, (S, hkv * dh)), rnd("bf16", 31, 3, (S, hq * dh))
+    cache = nm.FullAttentionCache(hkv, dh, capacity=S, dtype="bf16")
+    cache.append(0, TD(k, dev, "bf16"), TD(v, dev, "bf16"))
+    scale = dh ** -0.5
+    out = nm.attend(cache, TD(q, dev, "bf16"), 0, scale, out_dtype=torch.float32).cpu().numpy()
+    for r0, r1 in ((S - 256, S), (0, 128)):
+        want = oracle.attend(k, v, 0, 0, hkv, dh, q[r0:r1], hq, r0, scale=np.float32(scale))
+        assert_close(out[r0:r1], want, what=f"rows {r0}:{r1}")
+    for _ in range(2):  # tickets return to zero: the same result again
+        again = nm.attend(cache, TD(q, dev, "bf16"), 0, scale, out_dtype=torch.float32).cpu().numpy()
+        assert np.array_equal(again, out)
+
+
+def test_prefill_key_splits_with_fanout(dev):
+    hq, hkv, dh, S = 4, 2, 128, 4096
+    g = torch.Generator(device=dev)
+    g.manual_seed(5)
+    cache = nm.FullAttentionCache(hkv, dh, capacity=S, dtype="bf16")
+    cache.append(0, torch.randn(S, hkv * dh, device=dev, generator=g).bfloat16(),
+                 torch.randn(S, hkv * dh, device=dev, generator=g).bfloat16())
+    q = torch.randn(S, hq * dh, device=dev, generator=g).bfloat16()
+    want = nm.attend(cache, q, 0, dh ** -0.5, out_dtype=torch.bfloat16)
+    width, col0 = 2 * hq * dh, hq * dh
+    outs = [torch.zeros(S, width, device=dev, dtype=torch.bfloat16) for _ in range(2)]
+    nm.attend_fanout(cache, q, 0, dh ** -0.5, [o.data_ptr() for o in outs], width, col0, torch.bfloat16)
+    torch.cuda.synchronize(dev)
+    for o in outs:
+        assert torch.equal(o[:, col0:], want)
+        assert not o[:, :col0].any()
