@@ -409,8 +409,12 @@ int dispatch_mma(const nmg_kv_cache* c, const MmaArgs& a, dim3 grid, cudaStream_
 }
 
 int64_t mma_blocks_per_split(int64_t total_blocks) {
-    // about 6 CTAs per SM of work; at least 1 tile, at most 128 tiles (8192 keys) per split
+    // About 6 CTAs per SM of work, at most 128 tiles (8192 keys) per split.
+    // Small launches (a sliding window, a short cache) still give each CTA up
+    // to 4 tiles while that leaves a CTA per SM: a CTA of one tile pays its
+    // load latency with nothing to overlap it and adds a split to merge.
     int64_t b = total_blocks / (148 * 6);
+    b = std::max<int64_t>(b, std::min<int64_t>(4, total_blocks / 148));
     return std::max<int64_t>(1, std::min<int64_t>(128, b));
 }
 
