@@ -146,16 +146,18 @@ __global__ void __launch_bounds__(PfCfg<DH>::THREADS, 1) attn_prefill_kernel(con
     uint32_t* tmem_slot = (uint32_t*)(smem + C::TMEMPTR_OFF);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    // The grid is (head, work item) with the head fastest, so CTAs start in
+    // order of decreasing work over all heads (longest-first balancing).
     int tile, split = 0, nsplit = 1;
     if (a.n_items > 0) {
-        const uint32_t it = a.items[blockIdx.x];
+        const uint32_t it = a.items[blockIdx.y];
         tile = (int)(it >> 12);
         split = (int)((it >> 6) & 63u);
         nsplit = (int)(it & 63u);
     } else {
-        tile = gridDim.x - 1 - blockIdx.x;  // heaviest tiles first
+        tile = gridDim.y - 1 - blockIdx.y;  // heaviest tiles first
     }
-    const int h = blockIdx.y;
+    const int h = blockIdx.x;
     const int hk = h / a.g;
     const int64_t t0 = (int64_t)tile * BM;
     const int64_t t_last = (t0 + BM < a.rows ? t0 + BM : a.rows) - 1;
@@ -641,7 +643,7 @@ bool prefill_supported(const nmg_kv_cache* c, int hq, int q_dtype, int64_t rows)
     if (c->dh != 128 && c->dh != 256) return false;
     const int bn = c->dh == 128 ? 128 : 64;
     if (c->slots % bn != 0) return false;
-    if (rows < 64) return false;
+    if (rows < 64 || (rows + 127) / 128 > 65535) return false;  // query tiles index the grid's y
     if ((int64_t)c->hkv * c->slots > 0x7FFFFFFF) return false;
     return encode_tiled_fn() != nullptr;
 }
@@ -763,7 +765,7 @@ int attend_rows_prefill(const nmg_kv_cache* c, int hq, const void* q, int q_dtyp
     a->out_dtype = out_dtype;
     int st = device_error_flag(c->device, &a->err);
     if (st == NMG_OK) {
-        dim3 grid(a->n_items > 0 ? (unsigned)a->n_items : (unsigned)ntiles, (unsigned)hq);
+        dim3 grid((unsigned)hq, a->n_items > 0 ? (unsigned)a->n_items : (unsigned)ntiles);
         if (dh == 128)
             st = c->dtype == NMG_BF16 ? launch_prefill<128, true>(*a, grid, stream) : launch_prefill<128, false>(*a, grid, stream);
         else

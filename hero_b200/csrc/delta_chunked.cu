@@ -13,13 +13,14 @@
 //   S_C = exp(G_last) S0 + K^T (f D)
 // which is the same recurrence reassociated over the chunk.
 //
-// Phase 1, delta_wy_kernel: one CTA per (value head, chunk), all in parallel.
-//   [K;Q] K^T on the tensor core; A and M on the CUDA cores; T by fp32 forward
-//   substitution (one column per thread); [I;M] T = [T;MT] on the tensor core.
-//   Writes the [T;MT] tile, the chunk's (beta, e, f, exp(G_last)) and, once per
-//   key head, the [K;Q] tile and its K^T, rounded to tf32 -- each as the exact
-//   shared-memory image phase 2 multiplies from, so phase 2 fetches it with one
-//   bulk copy.
+// Phase 1, delta_wy_kernel: one CTA per (key head, chunk), all in parallel.
+//   [K;Q] K^T on the tensor core once for the value heads that share the key
+//   head; per value head, A and M on the CUDA cores, T by a blocked fp32
+//   triangular inverse and [I;M] T = [T;MT] on the tensor core.  Writes the
+//   [K;Q] tile and its K^T, and per value head the [T;MT] tile and the
+//   chunk's (beta, e, f, exp(G_last)), rounded to tf32 -- each as the exact
+//   shared-memory image phase 2 multiplies from, so phase 2 fetches it with
+//   one bulk copy.
 // Phase 2, delta_scan_kernel: one CTA per (value head, 128 value columns);
 //   walks the chunks in order with the state (transposed) resident in TMEM:
 //     MMA1 S^T [K;Q]^T -> (K S | Q S)^T;  R^T -> TMEM;  MMA2 R^T [T;MT]^T ->
@@ -84,25 +85,118 @@ struct WyArgs {
     int* err;
 };
 
-// Shared memory: region 0 (64 KB) holds the [K;Q] image; once the first MMA
-// and the image's store are done it is reused for A (rows of 64 floats, chunk
-// q of row i at q ^ (i & 15)), the [I;M] image (later the [T;MT] image) and the
-// T^T image (row j = column j of T).  K^T is built beside it.
-constexpr uint32_t P1_A = 0, P1_IM = 16384, P1_TI = 49152, P1_KT = 65536, P1_G = P1_KT + kKTBytes,
-                   P1_AUX = P1_G + 256, P1_BAR = P1_AUX + kAuxBytes, P1_END = P1_BAR + 64;
+// Shared memory of one (key head, chunk) CTA.  R0 (64 KB) holds the [K;Q]
+// image and R1 (32 KB) its K^T until their stores have read them; then R0
+// holds A (fp32 rows of 64, chunk q of row i at q ^ (i & 15)), the T^T image
+// (row j = column j of T, fp32 while T is solved, then rounded) and the [I;M]
+// image of even value heads, R1 the [I;M] image of odd ones, so the store of
+// one head's [T;MT] overlaps the next head's work.  G holds the chunk's 64
+// cumulative gates and, at [64], the first warp's total for the scan.
+constexpr uint32_t P1_A = 0, P1_TI = 16384, P1_IM0 = 32768, P1_R1 = 65536, P1_IM1 = P1_R1,
+                   P1_Y = P1_R1 + kKTBytes, P1_G = P1_Y + 3 * 1024, P1_AUX = P1_G + 512,
+                   P1_BAR = P1_AUX + 2 * kAuxBytes, P1_END = P1_BAR + 64;
 constexpr uint32_t P1_SMEM = 1024 + P1_END;
 
+// Byte offset of T[i][j] .. T[i + 3][j] (i a multiple of 4) in the T^T image:
+// row j, K-major over i in two boxes of 32.
+__device__ __forceinline__ uint32_t ti_off4(uint32_t i, uint32_t j) { return (i >> 5) * 8192u + sw_chunk(j, (i & 31u) >> 2); }
+__device__ __forceinline__ uint32_t ti_off(uint32_t i, uint32_t j) { return (i >> 5) * 8192u + sw_elem(j, i & 31u); }
+// Float index of A[i][4 q .. 4 q + 3].
+__device__ __forceinline__ int a_idx4(int i, int q) { return i * 64 + ((q ^ (i & 15)) << 2); }
+
+__device__ __forceinline__ float dot4(float4 a, float4 b, float acc) {
+    return fmaf(a.w, b.w, fmaf(a.z, b.z, fmaf(a.y, b.y, fmaf(a.x, b.x, acc))));
+}
+
+// T = (I + A)^-1 for the strictly lower triangular 64 x 64 A, by 16 x 16
+// blocks: the diagonal blocks by forward substitution (one column per
+// thread), then the off-diagonal blocks one block diagonal at a time,
+//   T_ij = -T_ii sum_{j <= k < i} A_ik T_kj,
+// with all 128 threads on each step.  fp32 throughout; T lands in the T^T
+// image unrounded.  Y holds 3 blocks of partial sums.
+__device__ __forceinline__ void wy_invert(const float* A, uint8_t* TI, float* Y, int tid) {
+    if (tid < 64) {
+        const int b = tid >> 4, c = tid & 15, j = 16 * b + c;
+        float t[16];
+#pragma unroll
+        for (int r = 0; r < 16; ++r) {
+            float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                if (4 * q < r) {
+                    const float4 av = *(const float4*)(A + a_idx4(16 * b + r, 4 * b + q));
+                    if (4 * q + 0 < r) s0 = fmaf(av.x, t[4 * q + 0], s0);
+                    if (4 * q + 1 < r) s1 = fmaf(av.y, t[4 * q + 1], s1);
+                    if (4 * q + 2 < r) s0 = fmaf(av.z, t[4 * q + 2], s0);
+                    if (4 * q + 3 < r) s1 = fmaf(av.w, t[4 * q + 3], s1);
+                }
+            }
+            t[r] = r == c ? 1.f : (r < c ? 0.f : -(s0 + s1));
+        }
+        for (int i = 0; i < 16 * b; i += 4) *(float4*)(TI + ti_off4(i, j)) = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int m = 0; m < 4; ++m)
+            *(float4*)(TI + ti_off4(16 * b + 4 * m, j)) = make_float4(t[4 * m], t[4 * m + 1], t[4 * m + 2], t[4 * m + 3]);
+    }
+#pragma unroll 1
+    for (int L = 1; L < 4; ++L) {
+        const int pairs = (4 - L) * 128;  // (block, row r and r + 8, column) per thread
+        __syncthreads();
+        for (int p = tid; p < pairs; p += 128) {
+            const int blk = p >> 7, r = (p >> 4) & 7, c = p & 15;
+            const int bi = blk + L, j = 16 * blk + c;
+            float y0 = 0.f, y1 = 0.f;
+#pragma unroll 1
+            for (int k = blk; k < bi; ++k) {
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const float4 tv = *(const float4*)(TI + ti_off4(16 * k + 4 * u, j));
+                    y0 = dot4(*(const float4*)(A + a_idx4(16 * bi + r, 4 * k + u)), tv, y0);
+                    y1 = dot4(*(const float4*)(A + a_idx4(16 * bi + r + 8, 4 * k + u)), tv, y1);
+                }
+            }
+            Y[(blk * 16 + r) * 16 + c] = y0;
+            Y[(blk * 16 + r + 8) * 16 + c] = y1;
+        }
+        __syncthreads();
+        for (int p = tid; p < pairs; p += 128) {
+            const int blk = p >> 7, r = (p >> 4) & 7, c = p & 15;
+            const int bi = blk + L, j = 16 * blk + c;
+            float z0 = 0.f, z1 = 0.f;
+#pragma unroll
+            for (int rp = 0; rp < 16; ++rp) {  // T_ii is lower triangular: its upper entries are stored zeros
+                const float yv = Y[(blk * 16 + rp) * 16 + c];
+                z0 = fmaf(*(const float*)(TI + ti_off(16 * bi + r, 16 * bi + rp)), yv, z0);
+                z1 = fmaf(*(const float*)(TI + ti_off(16 * bi + r + 8, 16 * bi + rp)), yv, z1);
+            }
+            *(float*)(TI + ti_off(16 * bi + r, j)) = -z0;
+            *(float*)(TI + ti_off(16 * bi + r + 8, j)) = -z1;
+        }
+    }
+    __syncthreads();
+    float4* ti4 = (float4*)TI;
+#pragma unroll
+    for (int i = tid; i < 1024; i += 128) {
+        const float4 x = ti4[i];
+        ti4[i] = tf32r4(x.x, x.y, x.z, x.w);
+    }
+}
+
+// One CTA per (key head, chunk): the value heads kh, kh + hk, ... share the
+// chunk's [K;Q] K^T product, so it is loaded, rounded and multiplied once.
 __global__ void __launch_bounds__(128) delta_wy_kernel(const __grid_constant__ WyArgs a) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    float* A_s = (float*)(smem + P1_A);
+    uint8_t* TI = smem + P1_TI;
+    float* Y_s = (float*)(smem + P1_Y);
     float* G_s = (float*)(smem + P1_G);
-    float* aux_s = (float*)(smem + P1_AUX);
-    uint64_t* bars = (uint64_t*)(smem + P1_BAR);  // 0: [K;Q] landed, 1: first MMA, 2: second MMA
+    uint64_t* bars = (uint64_t*)(smem + P1_BAR);  // 0: [K;Q] landed, 1: first MMA, 2: second MMA (once per value head)
     uint32_t* tmem_slot = (uint32_t*)(bars + 4);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int h = (int)(blockIdx.x % (unsigned)a.hv), c = (int)(blockIdx.x / (unsigned)a.hv), kh = h % a.hk;
-    const bool publish = h < a.hk;  // value head h == its key head: writes the K images once
+    const int kh = (int)(blockIdx.x % (unsigned)a.hk), c = (int)(blockIdx.x / (unsigned)a.hk);
     const int64_t t0 = (int64_t)c * kC;
+    const int64_t rec_k = (int64_t)kh * a.nchunks + c;
 
     if (tid == 0) {
         dev::prefetch_tensormap(&a.tm_q);
@@ -120,37 +214,14 @@ __global__ void __launch_bounds__(128) delta_wy_kernel(const __grid_constant__ W
         tc::tmem_alloc(tmem_slot, 128);
         tc::tmem_relinquish();
     }
-
-    // Gate and beta of the chunk's tokens (zero past the end), inclusive scan of the gate.
-    float gsum = 0.f, bt = 0.f;
-    if (tid < kC) {
-        const int64_t t = t0 + tid;
-        if (t < a.T) {
-            gsum = a.gate[t * a.hv + h];
-            bt = a.beta[t * a.hv + h];
-        }
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            const float n = __shfl_up_sync(0xffffffffu, gsum, o);
-            if (lane >= o) gsum += n;
-        }
-        if (tid == 31) G_s[0] = gsum;
-    }
+    // gate and beta of the first value head's tokens (zero past the end)
+    const bool tok = tid < kC && t0 + tid < a.T;
+    float g_raw = tok ? a.gate[(t0 + tid) * a.hv + kh] : 0.f;
+    float b_raw = tok ? a.beta[(t0 + tid) * a.hv + kh] : 0.f;
     tc::fence_before_sync();
     __syncthreads();
     tc::fence_after_sync();
     const uint32_t tmem = *tmem_slot;
-    if (tid >= 32 && tid < kC) gsum += G_s[0];
-    __syncthreads();
-    if (tid < kC) G_s[tid] = gsum;
-    __syncthreads();
-    if (tid < kC) {
-        aux_s[tid] = bt;
-        aux_s[64 + tid] = expf(gsum);
-        aux_s[128 + tid] = expf(G_s[kC - 1] - gsum);
-    } else {
-        aux_s[128 + tid] = tid == kC ? expf(G_s[kC - 1]) : 0.f;  // [192] = exp(G_last), then zeros
-    }
 
     // Round the [K;Q] tile to tf32 in place.
     dev::mbar_wait(&bars[0], 0, a.err);
@@ -165,7 +236,6 @@ __global__ void __launch_bounds__(128) delta_wy_kernel(const __grid_constant__ W
     dev::fence_proxy_async_smem();
     tc::fence_before_sync();
     __syncthreads();
-
     if (tid == 0) {
         tc::fence_after_sync();
         const uint32_t base = dev::smem_u32(smem);
@@ -177,29 +247,24 @@ __global__ void __launch_bounds__(128) delta_wy_kernel(const __grid_constant__ W
         }
         tc::commit(&bars[1]);
     }
-    if (publish) {
+    {
         // K^T image: row d holds K[0..63][d] (two boxes of 32 tokens).
-        uint8_t* KT = smem + P1_KT;
+        uint8_t* KT = smem + P1_R1;
         const int d = tid;
         const uint8_t* kcol = smem + (d >> 5) * 16384;
 #pragma unroll
         for (int q = 0; q < 16; ++q) {
             float x[4];
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const int t = 4 * q + e;
-                x[e] = *(const float*)(kcol + sw_elem(t, d & 31));
-            }
+            for (int e = 0; e < 4; ++e) x[e] = *(const float*)(kcol + sw_elem(4 * q + e, d & 31));
             *(float4*)(KT + (q >> 3) * 16384 + sw_chunk(d, q & 7)) = make_float4(x[0], x[1], x[2], x[3]);
         }
         dev::fence_proxy_async_smem();
         __syncthreads();
         if (tid == 0) {
-            const int64_t rec = (int64_t)kh * a.nchunks + c;
-            dev::bulk_s2g(a.kq_img + rec * (kKQBytes / 4), smem, kKQBytes);
-            dev::bulk_s2g(a.kt_img + rec * (kKTBytes / 4), KT, kKTBytes);
+            dev::bulk_s2g(a.kq_img + rec_k * (kKQBytes / 4), smem, kKQBytes);
+            dev::bulk_s2g(a.kt_img + rec_k * (kKTBytes / 4), KT, kKTBytes);
             dev::bulk_commit();
-            dev::bulk_wait_read();
         }
     }
     dev::mbar_wait(&bars[1], 0, a.err);
@@ -210,104 +275,115 @@ __global__ void __launch_bounds__(128) delta_wy_kernel(const __grid_constant__ W
         tc::ld_32x32b_x32(taddr, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
         tc::ld_32x32b_x32(taddr + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
     }
-    __syncthreads();  // region 0 is free from here on (thread 0 waited for the stores to read it)
-
-    float* A_s = (float*)(smem + P1_A);
-    uint8_t* IM = smem + P1_IM;
-    uint8_t* TI = smem + P1_TI;
-    if (tid < kC) {
-        const int i = tid;
-        const float gi = G_s[i];
-#pragma unroll
-        for (int q = 0; q < 16; ++q) {
-            float o[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const int j = 4 * q + e;
-                o[e] = j < i ? bt * __expf(gi - G_s[j]) * __uint_as_float(r[j]) : 0.f;
-            }
-            *(float4*)(A_s + i * 64 + ((q ^ (i & 15)) << 2)) = make_float4(o[0], o[1], o[2], o[3]);
-            // identity row i of the [I;M] image
-            const int j0 = 4 * q;
-            *(float4*)(IM + (q >> 3) * 16384 + sw_chunk(i, q & 7)) =
-                make_float4(j0 == i ? 1.f : 0.f, j0 + 1 == i ? 1.f : 0.f, j0 + 2 == i ? 1.f : 0.f, j0 + 3 == i ? 1.f : 0.f);
-        }
-    } else {
-        const int i = tid - kC;
-        const float gi = G_s[i];
-#pragma unroll
-        for (int q = 0; q < 16; ++q) {
-            float o[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const int j = 4 * q + e;
-                o[e] = j <= i ? __expf(gi - G_s[j]) * __uint_as_float(r[j]) : 0.f;
-            }
-            *(float4*)(IM + (q >> 3) * 16384 + sw_chunk(tid, q & 7)) = tf32r4(o[0], o[1], o[2], o[3]);
-        }
-    }
+    if (tid == 0) dev::bulk_wait_read();  // R0 and R1 are free once the image stores have read them
     __syncthreads();
 
-    // T = (I + A)^-1 by forward substitution; thread j < 64 owns column j:
-    // T_ij = [i == j] - sum_{k < i} A_ik T_kj (zero above the diagonal).
-    if (tid < kC) {
-        const int j = tid;
-        float t[kC];
+    int gi = 0;
+    for (int h = kh; h < a.hv; h += a.hk, ++gi) {
+        uint8_t* IM = smem + ((gi & 1) ? P1_IM1 : P1_IM0);
+        float* aux_s = (float*)(smem + P1_AUX + (gi & 1) * kAuxBytes);
+        // Inclusive scan of the gate over the chunk.
+        float gsum = g_raw;
+        const float bt = b_raw;
+        if (tid < kC) {
 #pragma unroll
-        for (int i = 0; i < kC; ++i) {
-            float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
-#pragma unroll
-            for (int q = 0; q < (i + 3) / 4; ++q) {
-                const float4 av = *(const float4*)(A_s + i * 64 + ((q ^ (i & 15)) << 2));
-                if (4 * q + 0 < i) s0 = fmaf(av.x, t[4 * q + 0], s0);
-                if (4 * q + 1 < i) s1 = fmaf(av.y, t[4 * q + 1], s1);
-                if (4 * q + 2 < i) s2 = fmaf(av.z, t[4 * q + 2], s2);
-                if (4 * q + 3 < i) s3 = fmaf(av.w, t[4 * q + 3], s3);
+            for (int o = 1; o < 32; o <<= 1) {
+                const float n = __shfl_up_sync(0xffffffffu, gsum, o);
+                if (lane >= o) gsum += n;
             }
-            t[i] = i == j ? 1.f : -((s0 + s1) + (s2 + s3));
+            if (tid == 31) G_s[64] = gsum;
         }
-        // column j of T is row j of the K-major B operand (two boxes of 32 k)
+        // The next value head's gate and beta, in flight meanwhile.
+        const int hn = h + a.hk;
+        if (tok && hn < a.hv) {
+            g_raw = a.gate[(t0 + tid) * a.hv + hn];
+            b_raw = a.beta[(t0 + tid) * a.hv + hn];
+        }
+        // The buffers of head gi - 2 must have been read by their stores.
+        if (tid == 0) dev::bulk_wait_read1();
+        __syncthreads();
+        if (tid >= 32 && tid < kC) gsum += G_s[64];
+        if (tid < kC) G_s[tid] = gsum;
+        __syncthreads();
+        if (tid < kC) {
+            aux_s[tid] = bt;
+            aux_s[64 + tid] = expf(gsum);
+            aux_s[128 + tid] = expf(G_s[kC - 1] - gsum);
+        } else {
+            aux_s[128 + tid] = tid == kC ? expf(G_s[kC - 1]) : 0.f;  // [192] = exp(G_last), then zeros
+        }
+        if (tid < kC) {
+            const int i = tid;
+#pragma unroll
+            for (int q = 0; q < 16; ++q) {
+                float o[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int j = 4 * q + e;
+                    o[e] = j < i ? bt * __expf(gsum - G_s[j]) * __uint_as_float(r[j]) : 0.f;
+                }
+                *(float4*)(A_s + a_idx4(i, q)) = make_float4(o[0], o[1], o[2], o[3]);
+                // identity row i of the [I;M] image
+                const int j0 = 4 * q;
+                *(float4*)(IM + (q >> 3) * 16384 + sw_chunk(i, q & 7)) =
+                    make_float4(j0 == i ? 1.f : 0.f, j0 + 1 == i ? 1.f : 0.f, j0 + 2 == i ? 1.f : 0.f, j0 + 3 == i ? 1.f : 0.f);
+            }
+        } else {
+            const int i = tid - kC;
+            const float gq = G_s[i];
+#pragma unroll
+            for (int q = 0; q < 16; ++q) {
+                float o[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int j = 4 * q + e;
+                    o[e] = j <= i ? __expf(gq - G_s[j]) * __uint_as_float(r[j]) : 0.f;
+                }
+                *(float4*)(IM + (q >> 3) * 16384 + sw_chunk(tid, q & 7)) = tf32r4(o[0], o[1], o[2], o[3]);
+            }
+        }
+        __syncthreads();
+        wy_invert(A_s, TI, Y_s, tid);
+        dev::fence_proxy_async_smem();
+        tc::fence_before_sync();
+        __syncthreads();
+
+        if (tid == 0) {
+            tc::fence_after_sync();
+            const uint32_t im = dev::smem_u32(IM), ti = dev::smem_u32(TI);
+            constexpr uint32_t id = tc::idesc_tf32(128, 64, 0, 0);
+#pragma unroll
+            for (int kk = 0; kk < kC / 8; ++kk)  // [I;M] x T
+                tc::mma_tf32_ss(tmem + 64, kmajor_desc(im, kk, 16384), kmajor_desc(ti, kk, 8192), id, kk > 0);
+            tc::commit(&bars[2]);
+        }
+        dev::mbar_wait(&bars[2], gi & 1, a.err);
+        tc::fence_after_sync();
+        uint32_t y[64];
+        {
+            const uint32_t taddr = tmem + ((uint32_t)(warp * 32) << 16) + 64;
+            tc::ld_32x32b_x32(taddr, *reinterpret_cast<uint32_t(*)[32]>(&y[0]));
+            tc::ld_32x32b_x32(taddr + 32, *reinterpret_cast<uint32_t(*)[32]>(&y[32]));
+        }
+        // row tid of [T;MT], rounded, over the consumed [I;M] image
 #pragma unroll
         for (int q = 0; q < 16; ++q)
-            *(float4*)(TI + (q >> 3) * 8192 + sw_chunk(j, q & 7)) =
-                tf32r4(t[4 * q], t[4 * q + 1], t[4 * q + 2], t[4 * q + 3]);
+            *(float4*)(IM + (q >> 3) * 16384 + sw_chunk(tid, q & 7)) =
+                tf32r4(__uint_as_float(y[4 * q]), __uint_as_float(y[4 * q + 1]), __uint_as_float(y[4 * q + 2]),
+                       __uint_as_float(y[4 * q + 3]));
+        dev::fence_proxy_async_smem();
+        tc::fence_before_sync();
+        __syncthreads();
+        if (tid == 0) {
+            const int64_t rec = (int64_t)h * a.nchunks + c;
+            dev::bulk_s2g(a.tm_img + rec * (kTMBytes / 4), IM, kTMBytes);
+            dev::bulk_s2g(a.aux + rec * (kAuxBytes / 4), aux_s, kAuxBytes);
+            dev::bulk_commit();
+        }
     }
-    dev::fence_proxy_async_smem();
+    if (tid == 0) dev::bulk_wait_read();  // the stores are complete for the next kernel once this grid ends
     tc::fence_before_sync();
     __syncthreads();
-
-    if (tid == 0) {
-        tc::fence_after_sync();
-        const uint32_t im = dev::smem_u32(IM), ti = dev::smem_u32(TI);
-        constexpr uint32_t id = tc::idesc_tf32(128, 64, 0, 0);
-#pragma unroll
-        for (int kk = 0; kk < kC / 8; ++kk)  // [I;M] x T
-            tc::mma_tf32_ss(tmem + 64, kmajor_desc(im, kk, 16384), kmajor_desc(ti, kk, 8192), id, kk > 0);
-        tc::commit(&bars[2]);
-    }
-    dev::mbar_wait(&bars[2], 0, a.err);
-    tc::fence_after_sync();
-    {
-        const uint32_t taddr = tmem + ((uint32_t)(warp * 32) << 16) + 64;
-        tc::ld_32x32b_x32(taddr, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
-        tc::ld_32x32b_x32(taddr + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
-    }
-    // row tid of [T;MT], rounded, over the consumed [I;M] image
-#pragma unroll
-    for (int q = 0; q < 16; ++q)
-        *(float4*)(IM + (q >> 3) * 16384 + sw_chunk(tid, q & 7)) =
-            tf32r4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]), __uint_as_float(r[4 * q + 2]),
-                   __uint_as_float(r[4 * q + 3]));
-    dev::fence_proxy_async_smem();
-    tc::fence_before_sync();
-    __syncthreads();
-    if (tid == 0) {
-        const int64_t rec = (int64_t)h * a.nchunks + c;
-        dev::bulk_s2g(a.tm_img + rec * (kTMBytes / 4), IM, kTMBytes);
-        dev::bulk_s2g(a.aux + rec * (kAuxBytes / 4), aux_s, kAuxBytes);
-        dev::bulk_commit();
-        dev::bulk_wait_read();  // the stores are complete for the next kernel once this grid ends
-    }
     if (warp == 0) {
         tc::fence_after_sync();
         tc::tmem_dealloc(tmem, 128);
@@ -682,9 +758,8 @@ int delta_prefill_chunked(nmg_delta_state* st, int hk, int64_t T, const float* q
         NMG_CUDA_TRY(cudaFuncSetAttribute(delta_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, P2_SMEM));
         attr_set |= dbit;
     }
-    // one CTA per (value head, chunk); the heads of a chunk run side by side so
-    // the value heads that share a key head read its tiles while L2 holds them
-    delta_wy_kernel<<<(unsigned)((int64_t)nchunks * hv), 128, P1_SMEM, stream>>>(wa);
+    // one CTA per (key head, chunk), the key heads of a chunk side by side
+    delta_wy_kernel<<<(unsigned)((int64_t)nchunks * hk), 128, P1_SMEM, stream>>>(wa);
     NMG_CUDA_TRY(cudaGetLastError());
     delta_scan_kernel<<<dim3((dv + kCols - 1) / kCols, hv), 288, P2_SMEM, stream>>>(sa);
     NMG_CUDA_TRY(cudaGetLastError());
