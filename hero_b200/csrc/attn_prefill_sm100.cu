@@ -52,21 +52,29 @@ struct PfCfg {
     static constexpr int K_OFF = Q_OFF + Q_BYTES;
     static constexpr int V_OFF = K_OFF + KST * K_BYTES;
     static constexpr int BAR_OFF = V_OFF + VST * V_BYTES;
-    // q_full, k_full/k_empty[KST], v_full/v_empty[VST], s_full[2], p_full[2], o_done, quad[4]
-    static constexpr int NBARS = 1 + 2 * KST + 2 * VST + 2 + 2 + 1 + 4;
-    static constexpr int TMEMPTR_OFF = BAR_OFF + NBARS * 8;
+    // q_full, q_empty, k_full/k_empty[KST], v_full/v_empty[VST], s_full[2], p_full[2], o_done,
+    // o_final[2], o_free[2], l_full[2], quad[4]
+    static constexpr int NBARS = 2 + 2 * KST + 2 * VST + 2 + 2 + 1 + 2 + 2 + 2 + 4;
+    static constexpr int FLAGS_OFF = BAR_OFF + NBARS * 8;  // TMEM address, abort flag, last-split flag
     // Softmax warps per TMEM lane quadrant: each owns PART_N keys of a score
     // row and PART_D columns of its output row.
-    static constexpr int PARTS = DH == 128 ? 4 : 2;
-    static constexpr int RED_OFF = TMEMPTR_OFF + 16;                  // float [2 parity][PARTS][BM]
-    static constexpr int SMEM = RED_OFF + 2 * PARTS * BM * 4 + 1024;  // + slack to align the base to 1024
+    static constexpr int PARTS = 2;
+    static constexpr int RED_OFF = FLAGS_OFF + 16;                  // float [3][PARTS][BM]: max (2 parities), sum
+    static constexpr int STATS_OFF = RED_OFF + 3 * PARTS * BM * 4;  // float2 [2][BM]: a work's (l, m) per row
+    static constexpr int STAGE_OFF = (STATS_OFF + 2 * BM * 8 + 127) / 128 * 128;  // 4 epilogue warps x 32 rows x 128 B
+    static constexpr int SMEM = STAGE_OFF + 4 * 32 * 128 + 1024;    // + slack to align the base to 1024
     static constexpr int SOFTMAX_THREADS = 128 * PARTS;
-    static constexpr int THREADS = 96 + SOFTMAX_THREADS;  // K producer, MMA, V producer, softmax warps
+    static constexpr int EPI_WARP0 = 3 + SOFTMAX_THREADS / 32;
+    static constexpr int THREADS = 96 + SOFTMAX_THREADS + 128;  // K producer, MMA, V producer, softmax, epilogue
     static constexpr int PART_N = BN / PARTS, PART_D = DH / PARTS;
     static constexpr uint32_t TMEM_COLS = 512;
     static constexpr uint32_t O_COL = 2 * BN;
-    static_assert(O_COL + DH <= 512, "TMEM budget");
+    // Two O accumulators when TMEM has room: the epilogue of one work reads
+    // one while the next work's P.V accumulates into the other.
+    static constexpr int OBUF = O_COL + 2 * DH <= 512 ? 2 : 1;
+    static_assert(O_COL + OBUF * DH <= 512, "TMEM budget");
     static_assert(SMEM <= 232448, "shared memory budget");
+    static_assert(STATS_OFF % 8 == 0 && STAGE_OFF % 16 == 0, "vector accesses");
 };
 
 constexpr int kMaxFanout = 8;
@@ -89,13 +97,15 @@ struct PrefillArgs {
     int64_t out_row_elems, out_col0;
     int out_dtype;
     int* err;
-    // Key splits (n_items > 0): CTA x takes items[x] = tile << 12 | split << 6 |
-    // nsplit, keys blocks [split * split_blocks, +split_blocks) of the tile's
-    // range.  A split tile's CTAs leave (O, m, l) partials in part (slot
-    // part_base[tile] + split of head h: [BM][DH + 4] fp32, O then m, l, with
-    // rows padded to 16 bytes) and the last one
-    // to finish (ticket per head and tile) merges them.  n_items == 0: one
-    // CTA per tile, heaviest tile first.
+    // Work list: n_work = (n_items or ntiles) * hq units, heaviest first,
+    // head fastest.  Key splits (n_items > 0): unit u takes items[u / hq] =
+    // tile << 12 | split << 6 | nsplit, key blocks [split * split_blocks,
+    // +split_blocks) of the tile's range.  A split tile's units leave (O, m,
+    // l) partials in part (slot part_base[tile] + split of head h: [BM][DH +
+    // 4] fp32, O then m, l, with rows padded to 16 bytes) and the last one to
+    // finish (ticket per head and tile) merges them.  n_items == 0: one unit
+    // per (tile, head).
+    int64_t n_work;
     int n_items, split_blocks, nparts, ntiles;
     float* part;
     int* tickets;
@@ -118,6 +128,46 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi, bool bf16) {
     return *reinterpret_cast<uint32_t*>(&v);
 }
 
+// Output conversions with the reference's rounding (dev::f32_to_bf16_bits,
+// dev::f32_to_f16_bits), for two values packed low first.
+__device__ __forceinline__ uint32_t pack_out(float lo, float hi, int dtype) {
+    if (dtype == NMG_BF16) return (uint32_t)dev::f32_to_bf16_bits(lo) | ((uint32_t)dev::f32_to_bf16_bits(hi) << 16);
+    return (uint32_t)dev::f32_to_f16_bits(lo) | ((uint32_t)dev::f32_to_f16_bits(hi) << 16);
+}
+// The same without branches for the values the epilogue meets almost
+// always; a warp with any other value takes pack_out instead.
+//   bf16: round to nearest even, which the hardware conversion gives for
+//         every value but NaN (the reference quiets NaN its own way).
+//   f16:  results in the normal range (fp32 exponent 113..142), where the
+//         reference rounds half up on bit 12 of the mantissa.
+__device__ __forceinline__ bool bf16_fast_ok(float x) { return x == x; }
+__device__ __forceinline__ bool f16_fast_ok(float x) { return ((__float_as_uint(x) >> 23) & 0xFFu) - 113u <= 29u; }
+__device__ __forceinline__ uint32_t pack_bf16_fast(float lo, float hi) {
+    uint32_t r;
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+    return r;
+}
+__device__ __forceinline__ uint32_t f16_fast(float x) {
+    const uint32_t b = __float_as_uint(x);
+    const uint32_t h = ((b >> 16) & 0x8000u) | ((((b >> 23) & 0xFFu) - 112u) << 10) | ((b >> 13) & 0x3FFu);
+    return h + ((b >> 12) & 1u);
+}
+__device__ __forceinline__ uint32_t pack_f16_fast(float lo, float hi) { return f16_fast(lo) | (f16_fast(hi) << 16); }
+
+// AND of `v` over the `count` threads that meet on named barrier `id`.
+__device__ __forceinline__ bool bar_and(int id, int count, bool v) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 q, %1, 0;\n\t"
+        "bar.red.and.pred p, %2, %3, q;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(r)
+        : "r"((uint32_t)v), "r"(id), "r"(count)
+        : "memory");
+    return r != 0;
+}
+
 __device__ __forceinline__ int64_t vis_lo(const PrefillArgs& a, int64_t q) {
     int64_t lo = a.floor_pos;
     if (a.window > 0 && q - a.window + 1 > lo) lo = q - a.window + 1;
@@ -125,53 +175,78 @@ __device__ __forceinline__ int64_t vis_lo(const PrefillArgs& a, int64_t q) {
 }
 __device__ __forceinline__ int64_t vis_hi(const PrefillArgs& a, int64_t q) { return q < a.newest ? q : a.newest; }
 
+// One unit of work: a query tile (or a key split of one) of one head.
+struct Work {
+    int h, tile, split, nsplit, nblk;
+    int64_t t0, t_last, j_begin, full_lo, full_hi;
+};
+
+// The k-th unit of this CTA.  CTAs walk the heavy-first list in snake order
+// (k even: unit k * G + b, k odd: k * G + G - 1 - b), which evens out the
+// per-CTA totals of a list sorted by decreasing work.  Every role of the CTA
+// decodes the same sequence.
+template <int BM, int BN>
+__device__ __forceinline__ bool decode_work(const PrefillArgs& a, int k, Work& w) {
+    const int G = gridDim.x, b = blockIdx.x;
+    const int64_t idx = (int64_t)k * G + ((k & 1) ? G - 1 - b : b);
+    if (idx >= a.n_work) return false;
+    w.h = (int)(idx % a.hq);
+    const int it = (int)(idx / a.hq);
+    if (a.n_items > 0) {
+        const uint32_t item = a.items[it];
+        w.tile = (int)(item >> 12);
+        w.split = (int)((item >> 6) & 63u);
+        w.nsplit = (int)(item & 63u);
+    } else {
+        w.tile = a.ntiles - 1 - it;
+        w.split = 0;
+        w.nsplit = 1;
+    }
+    w.t0 = (int64_t)w.tile * BM;
+    w.t_last = (w.t0 + BM < a.rows ? w.t0 + BM : a.rows) - 1;
+    const int64_t q_first = a.first_query + w.t0, q_last = a.first_query + w.t_last;
+    const int64_t u_lo = vis_lo(a, q_first) - a.base, u_hi = vis_hi(a, q_last) - a.base;
+    const int nblk_all = (int)(u_hi / BN + 1 - u_lo / BN);
+    w.j_begin = u_lo / BN + (int64_t)w.split * a.split_blocks;
+    w.nblk = w.nsplit == 1 ? nblk_all : min(a.split_blocks, nblk_all - w.split * a.split_blocks);
+    // A block needs no mask when every row of the tile sees all of it.
+    w.full_lo = vis_lo(a, q_last);
+    w.full_hi = vis_hi(a, q_first);
+    return true;
+}
+
 template <int DH, bool BF16>
 __global__ void __launch_bounds__(PfCfg<DH>::THREADS, 1) attn_prefill_kernel(const __grid_constant__ PrefillArgs a) {
     using C = PfCfg<DH>;
-    constexpr int BM = C::BM, BN = C::BN, KST = C::KST, VST = C::VST;
+    constexpr int BM = C::BM, BN = C::BN, KST = C::KST, VST = C::VST, OBUF = C::OBUF;
     extern __shared__ unsigned char smem_raw[];
     unsigned char* smem = (unsigned char*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     uint64_t* bars = (uint64_t*)(smem + C::BAR_OFF);
     uint64_t* q_full = bars;
-    uint64_t* k_full = q_full + 1;
+    uint64_t* q_empty = q_full + 1;  // completes once per unit: its last S has read Q
+    uint64_t* k_full = q_empty + 1;
     uint64_t* k_empty = k_full + KST;
     uint64_t* v_full = k_empty + KST;
     uint64_t* v_empty = v_full + VST;
     uint64_t* s_full = v_empty + VST;  // [2]
     // p_full[b] completes once per block of parity b: the softmax can never be
     // two phases ahead of the MMA thread's wait on it.
-    uint64_t* p_full = s_full + 2;  // [2]
-    uint64_t* o_done = p_full + 2;
-    uint64_t* quad_bar = o_done + 1;  // [4], one arrival per softmax thread of the quadrant
-    uint32_t* tmem_slot = (uint32_t*)(smem + C::TMEMPTR_OFF);
+    uint64_t* p_full = s_full + 2;    // [2]
+    uint64_t* o_done = p_full + 2;    // P.V of every block but a unit's last
+    uint64_t* o_final = o_done + 1;   // [OBUF] a unit's last P.V
+    uint64_t* o_free = o_final + 2;   // [OBUF] the epilogue has read O and the row statistics
+    uint64_t* l_full = o_free + 2;    // [OBUF] the softmax has left a unit's (l, m)
+    uint64_t* quad_bar = l_full + 2;  // [4], one arrival per softmax thread of the quadrant
+    uint32_t* tmem_slot = (uint32_t*)(smem + C::FLAGS_OFF);
+    volatile int* abort_flag = (volatile int*)(smem + C::FLAGS_OFF + 4);
+    volatile int* last_flag = (volatile int*)(smem + C::FLAGS_OFF + 8);
+    float2* stats = (float2*)(smem + C::STATS_OFF);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    // The grid is (head, work item) with the head fastest, so CTAs start in
-    // order of decreasing work over all heads (longest-first balancing).
-    int tile, split = 0, nsplit = 1;
-    if (a.n_items > 0) {
-        const uint32_t it = a.items[blockIdx.y];
-        tile = (int)(it >> 12);
-        split = (int)((it >> 6) & 63u);
-        nsplit = (int)(it & 63u);
-    } else {
-        tile = gridDim.y - 1 - blockIdx.y;  // heaviest tiles first
-    }
-    const int h = blockIdx.x;
-    const int hk = h / a.g;
-    const int64_t t0 = (int64_t)tile * BM;
-    const int64_t t_last = (t0 + BM < a.rows ? t0 + BM : a.rows) - 1;
-    const int64_t q_first = a.first_query + t0, q_last = a.first_query + t_last;
-    const int64_t u_lo = vis_lo(a, q_first) - a.base;
-    const int64_t u_hi = vis_hi(a, q_last) - a.base;
-    const int nblk_all = (int)(u_hi / BN + 1 - u_lo / BN);
-    const int64_t j_begin = u_lo / BN + (int64_t)split * a.split_blocks;
-    const int nblk = nsplit == 1 ? nblk_all : min(a.split_blocks, nblk_all - split * a.split_blocks);
-    // A block needs no mask when every row of the tile sees all of it.
-    const int64_t full_lo = vis_lo(a, q_last), full_hi = vis_hi(a, q_first);
 
     if (threadIdx.x == 0) {
         dev::mbar_init(q_full, 1);
+        dev::mbar_init(q_empty, 1);
         for (int s = 0; s < KST; ++s) {
             dev::mbar_init(&k_full[s], 1);
             dev::mbar_init(&k_empty[s], 1);
@@ -180,12 +255,17 @@ __global__ void __launch_bounds__(PfCfg<DH>::THREADS, 1) attn_prefill_kernel(con
             dev::mbar_init(&v_full[s], 1);
             dev::mbar_init(&v_empty[s], 1);
         }
-        dev::mbar_init(&s_full[0], 1);
-        dev::mbar_init(&s_full[1], 1);
-        dev::mbar_init(&p_full[0], C::SOFTMAX_THREADS);
-        dev::mbar_init(&p_full[1], C::SOFTMAX_THREADS);
+        for (int b = 0; b < 2; ++b) {
+            dev::mbar_init(&s_full[b], 1);
+            dev::mbar_init(&p_full[b], C::SOFTMAX_THREADS);
+            dev::mbar_init(&o_final[b], 1);
+            dev::mbar_init(&o_free[b], 128);
+            dev::mbar_init(&l_full[b], 128);
+        }
         dev::mbar_init(o_done, 1);
         for (int q = 0; q < 4; ++q) dev::mbar_init(&quad_bar[q], 32 * C::PARTS);
+        *abort_flag = 0;
+        *last_flag = 0;
         dev::fence_mbar_init();
     }
     if (warp == 1) {
@@ -197,42 +277,78 @@ __global__ void __launch_bounds__(PfCfg<DH>::THREADS, 1) attn_prefill_kernel(con
     tc::fence_after_sync();
     const uint32_t tmem = *tmem_slot;
 
-    auto kv_row = [&](int i) -> int32_t {
-        const int64_t u0 = (j_begin + i) * BN;
-        return (int32_t)(hk * a.slots + u0 % a.slots);
+    // Bounded wait; once any role gave up, every later wait that would block
+    // returns at once (a completed phase is taken without reading the flag).
+    auto wait = [&](uint64_t* bar, uint32_t parity) -> bool {
+        if (dev::mbar_test_wait(bar, parity)) return true;
+        if (*abort_flag) return false;
+        if (dev::mbar_wait(bar, parity, a.err)) return true;
+        *abort_flag = 1;
+        return false;
+    };
+    auto kv_row = [&](const Work& w, int i) -> int32_t {
+        const int64_t u0 = (w.j_begin + i) * BN;
+        return (int32_t)((w.h / a.g) * a.slots + u0 % a.slots);
     };
 
+    Work w;
     if (warp == 0) {
         if (lane == 0) {
             // ------------------------------------------------ Q and K producer
             dev::prefetch_tensormap(&a.tm_q);
             dev::prefetch_tensormap(&a.tm_k);
-            dev::mbar_arrive_expect_tx(q_full, C::Q_BYTES);
-#pragma unroll
-            for (int c = 0; c < DH / 64; ++c)
-                dev::tma_load_3d(smem + C::Q_OFF + c * BM * 128, &a.tm_q, c * 64, h, (int32_t)t0, q_full);
-            for (int i = 0; i < nblk; ++i) {
-                const int s = i % KST;
-                if (i >= KST && !dev::mbar_wait(&k_empty[s], ((i / KST) - 1) & 1, a.err)) break;
-                dev::mbar_arrive_expect_tx(&k_full[s], C::K_BYTES);
-                const int32_t row = kv_row(i);
+            uint32_t g = 0;  // key blocks loaded so far (all units)
+            int kn = 0;      // units with key blocks so far
+            bool ok = true;
+            for (int k = 0; ok && decode_work<BM, BN>(a, k, w); ++k) {
+                if (w.nblk <= 0) continue;
+                if (kn >= 1 && !wait(q_empty, (kn - 1) & 1)) break;  // the previous unit's S MMAs are done with Q
+                dev::mbar_arrive_expect_tx(q_full, C::Q_BYTES);
 #pragma unroll
                 for (int c = 0; c < DH / 64; ++c)
-                    dev::tma_load_2d(smem + C::K_OFF + s * C::K_BYTES + c * BN * 128, &a.tm_k, c * 64, row, &k_full[s]);
+                    dev::tma_load_3d(smem + C::Q_OFF + c * BM * 128, &a.tm_q, c * 64, w.h, (int32_t)w.t0, q_full);
+                {
+                    // The next unit's Q tile comes from HBM once: start it towards
+                    // L2 now, so its load after this unit's last S finds it there.
+                    Work nx;
+                    if (decode_work<BM, BN>(a, k + 1, nx) && nx.nblk > 0)
+#pragma unroll
+                        for (int c = 0; c < DH / 64; ++c) dev::tma_prefetch_3d(&a.tm_q, c * 64, nx.h, (int32_t)nx.t0);
+                }
+                for (int i = 0; i < w.nblk; ++i, ++g) {
+                    const int s = g % KST;
+                    if (g >= KST && !wait(&k_empty[s], ((g / KST) - 1) & 1)) {
+                        ok = false;
+                        break;
+                    }
+                    dev::mbar_arrive_expect_tx(&k_full[s], C::K_BYTES);
+                    const int32_t row = kv_row(w, i);
+#pragma unroll
+                    for (int c = 0; c < DH / 64; ++c)
+                        dev::tma_load_2d(smem + C::K_OFF + s * C::K_BYTES + c * BN * 128, &a.tm_k, c * 64, row, &k_full[s]);
+                }
+                ++kn;
             }
         }
     } else if (warp == 2) {
         if (lane == 0) {
             // ------------------------------------------------ V producer
             dev::prefetch_tensormap(&a.tm_v);
-            for (int i = 0; i < nblk; ++i) {
-                const int s = i % VST;
-                if (i >= VST && !dev::mbar_wait(&v_empty[s], ((i / VST) - 1) & 1, a.err)) break;
-                dev::mbar_arrive_expect_tx(&v_full[s], C::V_BYTES);
-                const int32_t row = kv_row(i);
+            uint32_t g = 0;
+            bool ok = true;
+            for (int k = 0; ok && decode_work<BM, BN>(a, k, w); ++k) {
+                for (int i = 0; i < w.nblk; ++i, ++g) {
+                    const int s = g % VST;
+                    if (g >= VST && !wait(&v_empty[s], ((g / VST) - 1) & 1)) {
+                        ok = false;
+                        break;
+                    }
+                    dev::mbar_arrive_expect_tx(&v_full[s], C::V_BYTES);
+                    const int32_t row = kv_row(w, i);
 #pragma unroll
-                for (int c = 0; c < DH / 64; ++c)
-                    dev::tma_load_2d(smem + C::V_OFF + s * C::V_BYTES + c * BN * 128, &a.tm_v, c * 64, row, &v_full[s]);
+                    for (int c = 0; c < DH / 64; ++c)
+                        dev::tma_load_2d(smem + C::V_OFF + s * C::V_BYTES + c * BN * 128, &a.tm_v, c * 64, row, &v_full[s]);
+                }
             }
         }
     } else if (warp == 1) {
@@ -246,54 +362,77 @@ __global__ void __launch_bounds__(PfCfg<DH>::THREADS, 1) attn_prefill_kernel(con
             const uint64_t q_desc = tc::smem_desc_sw128(sbase + C::Q_OFF, 16, 1024);
             const uint64_t k_desc = tc::smem_desc_sw128(sbase + C::K_OFF, 16, 1024);
             const uint64_t v_desc = tc::smem_desc_sw128(sbase + C::V_OFF, BN * 128, 1024);
-            bool ok = dev::mbar_wait(q_full, 0, a.err);
-            auto issue_pv = [&](int i) -> bool {
-                const int s = i % VST;
-                if (!dev::mbar_wait(&p_full[i & 1], (i >> 1) & 1, a.err)) return false;
-                if (!dev::mbar_wait(&v_full[s], (i / VST) & 1, a.err)) return false;
+            // P_gg . V_gg into O buffer ob; `first` starts the accumulator, the
+            // unit's last P.V completes o_final[ob] instead of o_done.
+            auto issue_pv = [&](uint32_t gg, bool first, bool last, int ob, int use) -> bool {
+                const int s = gg % VST;
+                if (!wait(&p_full[gg & 1], (gg >> 1) & 1)) return false;
+                if (!wait(&v_full[s], (gg / VST) & 1)) return false;
+                // the epilogue of the buffer's previous unit has read O
+                if (first && use >= 1 && !wait(&o_free[ob], (use - 1) & 1)) return false;
                 tc::fence_after_sync();
-                const uint32_t p_tmem = tmem + (i & 1) * BN;  // P_i overwrote S_i, 2 values per column
+                const uint32_t p_tmem = tmem + (gg & 1) * BN;  // P overwrote S, 2 values per column
                 const uint64_t vs = tc::desc_advance(v_desc, s * C::V_BYTES);
 #pragma unroll
                 for (int k = 0; k < BN / 16; ++k)
-                    tc::mma_f16_ts(tmem + C::O_COL, p_tmem + k * 8, tc::desc_advance(vs, k * 2048), idesc_o,
-                                   (i > 0 || k > 0) ? 1u : 0u);
-                tc::commit(o_done);
+                    tc::mma_f16_ts(tmem + C::O_COL + ob * DH, p_tmem + k * 8, tc::desc_advance(vs, k * 2048), idesc_o,
+                                   (!first || k > 0) ? 1u : 0u);
+                tc::commit(last ? &o_final[ob] : o_done);
                 tc::commit(&v_empty[s]);
                 return true;
             };
-            for (int i = 0; ok && i < nblk; ++i) {
-                const int s = i % KST, sb = i & 1;
-                if (!dev::mbar_wait(&k_full[s], (i / KST) & 1, a.err)) break;
-                tc::fence_after_sync();
-                // S_i overwrites buffer sb, which held P_{i-2}; P_{i-2}.V was issued
-                // earlier and the tensor pipe executes in order.
-                const uint64_t ks = tc::desc_advance(k_desc, s * C::K_BYTES);
+            // One stream over all units: S_g, then P_{g-1}.V, so the next
+            // unit's first S runs while the softmax finishes this unit's last
+            // block (Q of the next unit is loaded once this unit's last S is done).
+            uint32_t g = 0;
+            int kn = 0;
+            bool ok = true;
+            bool pend = false;  // P_{g-1}.V still to issue, with its flags:
+            bool pv_first = false, pv_last = false;
+            int pv_ob = 0, pv_use = 0;
+            for (int k = 0; ok && decode_work<BM, BN>(a, k, w); ++k) {
+                if (w.nblk <= 0) continue;
+                const int ob = kn % OBUF, use = kn / OBUF;
+                if (!wait(q_full, kn & 1)) break;
+                for (int i = 0; i < w.nblk; ++i, ++g) {
+                    const int s = g % KST, sb = g & 1;
+                    if (!wait(&k_full[s], (g / KST) & 1)) {
+                        ok = false;
+                        break;
+                    }
+                    tc::fence_after_sync();
+                    // S_g overwrites buffer sb, which held P_{g-2}; P_{g-2}.V was issued
+                    // earlier and the tensor pipe executes in order.
+                    const uint64_t ks = tc::desc_advance(k_desc, s * C::K_BYTES);
 #pragma unroll
-                for (int k = 0; k < DH / 16; ++k)
-                    tc::mma_f16_ss(tmem + sb * BN, tc::desc_advance(q_desc, (k / 4) * BM * 128 + (k % 4) * 32),
-                                   tc::desc_advance(ks, (k / 4) * BN * 128 + (k % 4) * 32), idesc_s, k > 0 ? 1u : 0u);
-                tc::commit(&s_full[sb]);
-                tc::commit(&k_empty[s]);
-                if (i >= 1 && !issue_pv(i - 1)) {
-                    ok = false;
-                    break;
+                    for (int kk = 0; kk < DH / 16; ++kk)
+                        tc::mma_f16_ss(tmem + sb * BN, tc::desc_advance(q_desc, (kk / 4) * BM * 128 + (kk % 4) * 32),
+                                       tc::desc_advance(ks, (kk / 4) * BN * 128 + (kk % 4) * 32), idesc_s, kk > 0 ? 1u : 0u);
+                    tc::commit(&s_full[sb]);
+                    tc::commit(&k_empty[s]);
+                    if (i == w.nblk - 1) tc::commit(q_empty);
+                    if (pend && !issue_pv(g - 1, pv_first, pv_last, pv_ob, pv_use)) {
+                        ok = false;
+                        break;
+                    }
+                    pend = true;
+                    pv_first = i == 0;
+                    pv_last = i == w.nblk - 1;
+                    pv_ob = ob;
+                    pv_use = use;
                 }
+                ++kn;
             }
-            if (ok && nblk > 0) issue_pv(nblk - 1);
+            if (ok && pend) issue_pv(g - 1, pv_first, pv_last, pv_ob, pv_use);
         }
-    } else {
+    } else if (warp < C::EPI_WARP0) {
         // ---------------------------------------------------- softmax warps
         const int quad = warp & 3;          // TMEM lane quadrant this warp may access
         const int part = (warp - 3) >> 2;   // which PART_N keys / PART_D output columns of the row
         const int row = quad * 32 + lane;
         const uint32_t t_lane = tmem + ((uint32_t)(quad * 32) << 16);
-        const int64_t qpos = a.first_query + t0 + row;
-        const int64_t lo = vis_lo(a, qpos), hi = vis_hi(a, qpos);
-        float* red = (float*)(smem + C::RED_OFF);  // [parity][part][row]
+        float* red = (float*)(smem + C::RED_OFF);  // [slot][part][row]; slots 0, 1: block maxima by parity, 2: sums
         const int col0 = part * C::PART_N;
-        float m_run = -INFINITY, l_run = 0.f;
-        bool ok = true;
         // The PARTS warps of one quadrant exchange through red[] and meet on
         // their quadrant mbarrier (completion k = exchange k; bounded wait).
         int quad_phase = 0;
@@ -302,288 +441,292 @@ __global__ void __launch_bounds__(PfCfg<DH>::THREADS, 1) attn_prefill_kernel(con
         auto quad_sync = [&]() -> bool {
             tc::fence_before_sync();
             dev::mbar_arrive(&quad_bar[quad]);
-            const bool done = __all_sync(0xffffffffu, dev::mbar_wait(&quad_bar[quad], quad_phase & 1, a.err));
+            const bool done = __all_sync(0xffffffffu, wait(&quad_bar[quad], quad_phase & 1));
             tc::fence_after_sync();
             ++quad_phase;
             return done;
         };
-
-        for (int i = 0; i < nblk; ++i) {
-            const int sb = i & 1;
-            // Waits are voted warp-wide so the .sync.aligned TMEM accesses
-            // below always see a converged warp.  S_i complete also means
-            // P_{i-2}.V is complete (issued before it, in order).
-            if (!__all_sync(0xffffffffu, dev::mbar_wait(&s_full[sb], (i >> 1) & 1, a.err))) {
-                ok = false;
-                break;
-            }
-            tc::fence_after_sync();
-            // Raw scores: the maximum is taken before scaling (scale_log2 > 0)
-            // and the scale is folded into the exponent's FFMA below.
-            float x[C::PART_N];
-#pragma unroll
-            for (int c = 0; c < C::PART_N / 32; ++c) {
-                uint32_t r[32];
-                tc::ld_32x32b_x32(t_lane + sb * BN + col0 + c * 32, r);
-#pragma unroll
-                for (int e = 0; e < 32; ++e) x[c * 32 + e] = __uint_as_float(r[e]);
-            }
-
-            const int64_t p0 = a.base + (j_begin + i) * BN + col0;
-            if (!(p0 - col0 >= full_lo && p0 - col0 + BN - 1 <= full_hi)) {
-#pragma unroll
-                for (int e = 0; e < C::PART_N; ++e) {
-                    const int64_t pos = p0 + e;
-                    if (pos < lo || pos > hi) x[e] = -INFINITY;
+        uint32_t g = 0, od = 0;
+        int kn = 0;
+        bool ok = true;
+        for (int k = 0; ok && decode_work<BM, BN>(a, k, w); ++k) {
+            if (w.nblk <= 0) continue;
+            const int ob = kn % OBUF, use = kn / OBUF;
+            const uint32_t o_col = C::O_COL + ob * DH;
+            const int64_t qpos = a.first_query + w.t0 + row;
+            const int64_t lo = vis_lo(a, qpos), hi = vis_hi(a, qpos);
+            float m_run = -INFINITY, l_run = 0.f;
+            for (int i = 0; i < w.nblk; ++i, ++g) {
+                const int sb = g & 1;
+                // Waits are voted warp-wide so the .sync.aligned TMEM accesses
+                // below always see a converged warp.  S_g complete also means
+                // P_{g-2}.V is complete (issued before it, in order).
+                if (!__all_sync(0xffffffffu, wait(&s_full[sb], (g >> 1) & 1))) {
+                    ok = false;
+                    break;
                 }
-            }
-            float mb = x[0];
-#pragma unroll
-            for (int e = 1; e < C::PART_N; ++e) mb = fmaxf(mb, x[e]);
-            mb *= a.scale_log2;
-            red[(sb * C::PARTS + part) * BM + row] = mb;
-            if (!quad_sync()) {
-                ok = false;
-                break;
-            }
-#pragma unroll
-            for (int q2 = 0; q2 < C::PARTS; ++q2) mb = fmaxf(mb, red[(sb * C::PARTS + q2) * BM + row]);
-            const float m_new = fmaxf(m_run, mb);
-            const bool rescale = m_new > m_run + 8.0f;  // also true for the first finite block
-            float alpha = 1.f;
-            if (rescale) {
-                alpha = (m_run == -INFINITY) ? 0.f : ex2(m_run - m_new);
-                m_run = m_new;
-            }
-            const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
-            float sum = 0.f;
-            uint32_t pk[C::PART_N / 2];
-#pragma unroll
-            for (int e = 0; e < C::PART_N; e += 2) {
-                const float p0v = ex2(fmaf(x[e], a.scale_log2, -m_use)), p1v = ex2(fmaf(x[e + 1], a.scale_log2, -m_use));
-                sum += p0v + p1v;
-                pk[e / 2] = pack2(p0v, p1v, false);
-            }
-            l_run = l_run * alpha + sum;
-
-            // Every o_done phase is waited for, in order: a parity wait only
-            // tells the current phase from the previous one, so a waiter that
-            // skipped a phase could mistake an unfinished P.V for a finished
-            // one.  P_{i-1}.V is normally long done by now.
-            if (i >= 1 && !__all_sync(0xffffffffu, dev::mbar_wait(o_done, (i - 1) & 1, a.err))) {
-                ok = false;
-                break;
-            }
-            // O is rescaled only after P_{i-1}.V has landed in it.
-            if (i >= 1 && __any_sync(0xffffffffu, rescale)) {
                 tc::fence_after_sync();
-#pragma unroll 1
-                for (int c = 0; c < C::PART_D / 32; ++c) {
-                    uint32_t r[32];
-                    const uint32_t col = C::O_COL + part * C::PART_D + c * 32;
-                    tc::ld_32x32b_x32(t_lane + col, r);
+                // Raw scores: the maximum is taken before scaling (scale_log2 > 0)
+                // and the scale is folded into the exponent's FFMA below.
+                float x[C::PART_N];
 #pragma unroll
-                    for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * alpha);
-                    tc::st_32x32b_x32(t_lane + col, r);
+                for (int c = 0; c < C::PART_N / 32; ++c) {
+                    uint32_t r[32];
+                    tc::ld_32x32b_x32(t_lane + sb * BN + col0 + c * 32, r);
+#pragma unroll
+                    for (int e = 0; e < 32; ++e) x[c * 32 + e] = __uint_as_float(r[e]);
                 }
+                const int64_t p0 = a.base + (w.j_begin + i) * BN + col0;
+                if (!(p0 - col0 >= w.full_lo && p0 - col0 + BN - 1 <= w.full_hi)) {
+#pragma unroll
+                    for (int e = 0; e < C::PART_N; ++e) {
+                        const int64_t pos = p0 + e;
+                        if (pos < lo || pos > hi) x[e] = -INFINITY;
+                    }
+                }
+                float mb = x[0];
+#pragma unroll
+                for (int e = 1; e < C::PART_N; ++e) mb = fmaxf(mb, x[e]);
+                mb *= a.scale_log2;
+                red[(sb * C::PARTS + part) * BM + row] = mb;
+                if (!quad_sync()) {
+                    ok = false;
+                    break;
+                }
+#pragma unroll
+                for (int q2 = 0; q2 < C::PARTS; ++q2) mb = fmaxf(mb, red[(sb * C::PARTS + q2) * BM + row]);
+                const float m_new = fmaxf(m_run, mb);
+                const bool rescale = m_new > m_run + 8.0f;  // also true for the first finite block
+                float alpha = 1.f;
+                if (rescale) {
+                    alpha = (m_run == -INFINITY) ? 0.f : ex2(m_run - m_new);
+                    m_run = m_new;
+                }
+                const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
+                float sum = 0.f;
+                uint32_t pk[C::PART_N / 2];
+#pragma unroll
+                for (int e = 0; e < C::PART_N; e += 2) {
+                    const float p0v = ex2(fmaf(x[e], a.scale_log2, -m_use)), p1v = ex2(fmaf(x[e + 1], a.scale_log2, -m_use));
+                    sum += p0v + p1v;
+                    pk[e / 2] = pack2(p0v, p1v, false);
+                }
+                l_run = l_run * alpha + sum;
+
+                // Every o_done phase is waited for, in order: a parity wait only
+                // tells the current phase from the previous one, so a waiter that
+                // skipped a phase could mistake an unfinished P.V for a finished
+                // one.  The MMA thread completes o_done for every P.V but a
+                // unit's last, exactly the ones waited for here.
+                if (i >= 1) {
+                    if (!__all_sync(0xffffffffu, wait(o_done, od & 1))) {
+                        ok = false;
+                        break;
+                    }
+                    ++od;
+                }
+                // O is rescaled only after the previous P.V has landed in it.
+                if (i >= 1 && __any_sync(0xffffffffu, rescale)) {
+                    tc::fence_after_sync();
+#pragma unroll 1
+                    for (int c = 0; c < C::PART_D / 32; ++c) {
+                        uint32_t r[32];
+                        const uint32_t col = o_col + part * C::PART_D + c * 32;
+                        tc::ld_32x32b_x32(t_lane + col, r);
+#pragma unroll
+                        for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * alpha);
+                        tc::st_32x32b_x32(t_lane + col, r);
+                    }
+                }
+                // P (fp16 pairs) over the first half of S's columns: this
+                // part's keys [col0, col0 + PART_N) -> columns [col0/2, col0/2 + PART_N/2).
+                const uint32_t pcol = t_lane + sb * BN + col0 / 2;
+                if constexpr (C::PART_N / 2 == 32) {
+                    tc::st_32x32b_x32(pcol, *reinterpret_cast<const uint32_t(*)[32]>(pk));
+                } else {
+                    tc::st_32x32b_x16(pcol, pk);
+                }
+                tc::wait_st();
+                tc::fence_before_sync();
+                dev::mbar_arrive(&p_full[sb]);
             }
-            // P_i (fp16 pairs) over the first half of S_i's columns: this
-            // part's keys [col0, col0 + PART_N) -> columns [col0/2, col0/2 + PART_N/2).
-            const uint32_t pcol = t_lane + sb * BN + col0 / 2;
-            if constexpr (C::PART_N / 2 == 32) {
-                tc::st_32x32b_x32(pcol, *reinterpret_cast<const uint32_t(*)[32]>(pk));
-            } else {
-                tc::st_32x32b_x16(pcol, pk);
+            if (!ok) break;
+            // Row sum = the parts' partial sums (slot 2; the previous unit's
+            // readers are past a block exchange since).
+            red[(2 * C::PARTS + part) * BM + row] = l_run;
+            if (!quad_sync()) break;
+            float l_row = 0.f;
+#pragma unroll
+            for (int q2 = 0; q2 < C::PARTS; ++q2) l_row += red[(2 * C::PARTS + q2) * BM + row];
+            // The epilogue of the buffer's previous unit has read its statistics.
+            if (use >= 1 && !__all_sync(0xffffffffu, wait(&o_free[ob], (use - 1) & 1))) break;
+            if (part == 0) {
+                stats[ob * BM + row] = make_float2(l_row, m_run);
+                dev::mbar_arrive(&l_full[ob]);
             }
-            tc::wait_st();
-            tc::fence_before_sync();
-            dev::mbar_arrive(&p_full[sb]);
+            ++kn;
         }
-
-        // Row sum = the parts' partial sums.  The slot of parity nblk & 1 was
-        // last read for block nblk - 2, which every part is past.
-        const int ls = nblk & 1;
-        red[(ls * C::PARTS + part) * BM + row] = l_run;
-        if (ok) ok = quad_sync();
-        float l_row = 0.f;
-#pragma unroll
-        for (int q2 = 0; q2 < C::PARTS; ++q2) l_row += red[(ls * C::PARTS + q2) * BM + row];
-        // Epilogue: normalise O.  With one local output every thread stores
-        // its own row part.  With several (other GPUs' memory among them) the
-        // tile is staged in shared memory (the Q and K stages are idle now:
-        // every MMA has completed) and all softmax threads copy whole row
-        // segments (DH * out_es contiguous bytes per row) to each output, so
-        // a warp writes two or more full segments per store instead of 32
-        // rows' 16-byte pieces, which NVLink carries far less efficiently.
-        const bool have_o = ok && nblk > 0 && __all_sync(0xffffffffu, dev::mbar_wait(o_done, (nblk - 1) & 1, a.err));
-        if (nsplit > 1) {
-            // A split of a tile: leave the unnormalised O with its m and l
-            // (base-2 units), and the last split of the tile merges them.
-            float* mine = a.part + (((int64_t)h * a.nparts + a.part_base[tile] + split) * BM + row) * (DH + 4);
-            if (have_o) {
-                tc::fence_after_sync();
+    } else {
+        // ---------------------------------------------------- epilogue warps
+        // One warp per TMEM lane quadrant: normalise a unit's O rows and store
+        // them (or leave split partials and merge), while the softmax warps
+        // already work on the next unit.
+        const int quad = warp & 3;
+        const int row = quad * 32 + lane;
+        const int eid = threadIdx.x - 32 * C::EPI_WARP0;  // 0 .. 127
+        const uint32_t t_lane = tmem + ((uint32_t)(quad * 32) << 16);
+        uint4* stage = (uint4*)(smem + C::STAGE_OFF + (warp - C::EPI_WARP0) * 4096);  // [32 rows][8 chunks]
+        const int oes = a.out_dtype == NMG_F32 ? 4 : 2;
+        const int cpc = 128 / oes;  // output columns per 128-byte row piece
+        int kn = 0;
+        for (int k = 0; decode_work<BM, BN>(a, k, w); ++k) {
+            if (w.nblk <= 0) continue;
+            const int ob = kn % OBUF, use = kn / OBUF;
+            const uint32_t o_col = C::O_COL + ob * DH;
+            // Waits are bounded, so all four warps reach the vote; a unit is
+            // skipped by all of them or by none (the split path meets on
+            // named barrier 1 below).
+            bool have = wait(&l_full[ob], use & 1);
+            have = wait(&o_final[ob], use & 1) && have;
+            if (!bar_and(1, 128, __all_sync(0xffffffffu, have))) break;
+            tc::fence_after_sync();
+            const float2 st = stats[ob * BM + row];
+            const float l_row = st.x, m_run = st.y;
+            const int valid_rows = (int)(w.t_last - w.t0 + 1);
+            if (w.nsplit == 1) {
+                // Normalise 128 bytes of output per row at a time, stage the
+                // warp's 32 rows, then store whole 128-byte row pieces (four
+                // rows per instruction) to every output.
+                const float inv = 1.f / l_row;
+                const int64_t row_bytes = a.out_row_elems * oes;
+                const int64_t base_off =
+                    ((w.t0 + quad * 32 + (lane >> 3)) * a.out_row_elems + a.out_col0 + (int64_t)w.h * DH) * oes +
+                    (lane & 7) * 16;
 #pragma unroll 1
-                for (int c = 0; c < C::PART_D / 32; ++c) {
+                for (int c0 = 0; c0 < DH; c0 += cpc) {
+                    uint32_t r[64];
+                    tc::ld_32x32b_x32(t_lane + o_col + c0, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
+                    if (oes == 2) tc::ld_32x32b_x32(t_lane + o_col + c0 + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
+#pragma unroll
+                    for (int e = 0; e < 64; ++e)
+                        if (e < cpc) r[e] = __float_as_uint(__uint_as_float(r[e]) * inv);
+                    auto f = [&](int e) { return __uint_as_float(r[e]); };
+                    if (oes == 4) {
+#pragma unroll
+                        for (int j = 0; j < 8; ++j)
+                            stage[lane * 8 + (j ^ (lane & 7))] = make_uint4(r[4 * j], r[4 * j + 1],
+                                                                            r[4 * j + 2], r[4 * j + 3]);
+                    } else {
+                        const bool bf = a.out_dtype == NMG_BF16;
+                        bool fast = true;
+#pragma unroll
+                        for (int e = 0; e < 64; ++e) fast &= bf ? bf16_fast_ok(f(e)) : f16_fast_ok(f(e));
+                        if (!__all_sync(0xffffffffu, fast)) {
+#pragma unroll
+                            for (int j = 0; j < 8; ++j)
+                                stage[lane * 8 + (j ^ (lane & 7))] =
+                                    make_uint4(pack_out(f(8 * j), f(8 * j + 1), a.out_dtype), pack_out(f(8 * j + 2), f(8 * j + 3), a.out_dtype),
+                                               pack_out(f(8 * j + 4), f(8 * j + 5), a.out_dtype), pack_out(f(8 * j + 6), f(8 * j + 7), a.out_dtype));
+                        } else if (bf) {
+#pragma unroll
+                            for (int j = 0; j < 8; ++j)
+                                stage[lane * 8 + (j ^ (lane & 7))] =
+                                    make_uint4(pack_bf16_fast(f(8 * j), f(8 * j + 1)), pack_bf16_fast(f(8 * j + 2), f(8 * j + 3)),
+                                               pack_bf16_fast(f(8 * j + 4), f(8 * j + 5)), pack_bf16_fast(f(8 * j + 6), f(8 * j + 7)));
+                        } else {
+#pragma unroll
+                            for (int j = 0; j < 8; ++j)
+                                stage[lane * 8 + (j ^ (lane & 7))] =
+                                    make_uint4(pack_f16_fast(f(8 * j), f(8 * j + 1)), pack_f16_fast(f(8 * j + 2), f(8 * j + 3)),
+                                               pack_f16_fast(f(8 * j + 4), f(8 * j + 5)), pack_f16_fast(f(8 * j + 6), f(8 * j + 7)));
+                        }
+                    }
+                    if (c0 + cpc >= DH) {  // O and the statistics are read: the buffer is free
+                        tc::fence_before_sync();
+                        dev::mbar_arrive(&o_free[ob]);
+                    }
+                    __syncwarp();
+                    uint4 v[8];
+#pragma unroll
+                    for (int m = 0; m < 8; ++m) {
+                        const int rr = m * 4 + (lane >> 3);
+                        v[m] = stage[rr * 8 + ((lane & 7) ^ (rr & 7))];
+                    }
+                    __syncwarp();
+                    for (int o = 0; o < a.nout; ++o) {
+                        unsigned char* p = (unsigned char*)a.outs[o] + base_off + c0 * oes;
+#pragma unroll
+                        for (int m = 0; m < 8; ++m)
+                            if (quad * 32 + m * 4 + (lane >> 3) < valid_rows) *(uint4*)(p + m * 4 * row_bytes) = v[m];
+                    }
+                }
+                // No fence: a caller that reads the rows on another GPU orders
+                // these stores with a stream-ordered barrier (nmg_comm_barrier),
+                // which starts only after this grid, stores included, has completed.
+            } else {
+                // A split of a tile: leave the unnormalised O with its m and l
+                // (base-2 units), and the last split of the tile merges them.
+                float* mine = a.part + (((int64_t)w.h * a.nparts + a.part_base[w.tile] + w.split) * BM + row) * (DH + 4);
+#pragma unroll 1
+                for (int c = 0; c < DH / 32; ++c) {
                     uint32_t r[32];
-                    tc::ld_32x32b_x32(t_lane + C::O_COL + part * C::PART_D + c * 32, r);
-                    float4* dst = (float4*)(mine + part * C::PART_D + c * 32);
+                    tc::ld_32x32b_x32(t_lane + o_col + c * 32, r);
+                    float4* dst = (float4*)(mine + c * 32);
 #pragma unroll
                     for (int e = 0; e < 8; ++e)
                         dst[e] = make_float4(__uint_as_float(r[4 * e]), __uint_as_float(r[4 * e + 1]),
                                              __uint_as_float(r[4 * e + 2]), __uint_as_float(r[4 * e + 3]));
                 }
-                if (part == 0) {
-                    mine[DH] = m_run;
-                    mine[DH + 1] = l_row;
-                }
-            }
-            __threadfence();
-            asm volatile("bar.sync 2, %0;" ::"r"(C::SOFTMAX_THREADS) : "memory");
-            int* last_flag = (int*)(smem + C::RED_OFF);  // red[] is no longer read
-            if (threadIdx.x == 96) {
-                int* ticket = a.tickets + (int64_t)h * a.ntiles + tile;
-                const int prev = atomicAdd(ticket, 1);
-                const bool last = prev == nsplit - 1;
-                if (last) *ticket = 0;  // ready for the next launch
-                *last_flag = last;
-            }
-            asm volatile("bar.sync 2, %0;" ::"r"(C::SOFTMAX_THREADS) : "memory");
-            if (*last_flag) {
+                mine[DH] = m_run;
+                mine[DH + 1] = l_row;
+                tc::fence_before_sync();
+                dev::mbar_arrive(&o_free[ob]);
                 __threadfence();
-                const int sid = threadIdx.x - 96;
-                const int valid_rows = (int)(t_last - t0 + 1);
-                const float* base = a.part + ((int64_t)h * a.nparts + a.part_base[tile]) * BM * (DH + 4);
-                const int64_t slot = (int64_t)BM * (DH + 4);
-                const int oes = a.out_dtype == NMG_F32 ? 4 : 2;
-                // 4 output columns per work unit
-                for (int idx = sid; idx < valid_rows * (DH / 4); idx += C::SOFTMAX_THREADS) {
-                    const int rr = idx / (DH / 4), d0 = (idx - rr * (DH / 4)) * 4;
-                    float M = -INFINITY;
-                    for (int sp = 0; sp < nsplit; ++sp) M = fmaxf(M, __ldcg(base + sp * slot + rr * (DH + 4) + DH));
-                    float L = 0.f, o4[4] = {0.f, 0.f, 0.f, 0.f};
-                    for (int sp = 0; sp < nsplit; ++sp) {
-                        const float* rp = base + sp * slot + rr * (DH + 4);
-                        const float m = __ldcg(rp + DH);
-                        if (m == -INFINITY) continue;
-                        const float w = ex2(m - M);
-                        L = fmaf(w, __ldcg(rp + DH + 1), L);
-                        const float4 v = __ldcg((const float4*)(rp + d0));
-                        o4[0] = fmaf(w, v.x, o4[0]), o4[1] = fmaf(w, v.y, o4[1]);
-                        o4[2] = fmaf(w, v.z, o4[2]), o4[3] = fmaf(w, v.w, o4[3]);
-                    }
-                    const float inv = 1.f / L;
-                    const int64_t off = ((t0 + rr) * a.out_row_elems + a.out_col0 + (int64_t)h * DH + d0) * oes;
-                    if (a.out_dtype == NMG_F32) {
-                        const float4 v = make_float4(o4[0] * inv, o4[1] * inv, o4[2] * inv, o4[3] * inv);
-                        for (int o = 0; o < a.nout; ++o) *(float4*)((unsigned char*)a.outs[o] + off) = v;
-                    } else {
-                        const bool obf = a.out_dtype == NMG_BF16;
-                        uint32_t w[2];
-#pragma unroll
-                        for (int t = 0; t < 2; ++t) {
-                            const float f0 = o4[2 * t] * inv, f1 = o4[2 * t + 1] * inv;
-                            const uint32_t b0 = obf ? dev::f32_to_bf16_bits(f0) : dev::f32_to_f16_bits(f0);
-                            const uint32_t b1 = obf ? dev::f32_to_bf16_bits(f1) : dev::f32_to_f16_bits(f1);
-                            w[t] = b0 | (b1 << 16);
+                asm volatile("bar.sync 1, 128;" ::: "memory");
+                if (eid == 0) {
+                    int* ticket = a.tickets + (int64_t)w.h * a.ntiles + w.tile;
+                    const int prev = atomicAdd(ticket, 1);
+                    const bool last = prev == w.nsplit - 1;
+                    if (last) *ticket = 0;  // ready for the next launch
+                    *last_flag = last;
+                }
+                asm volatile("bar.sync 1, 128;" ::: "memory");
+                const bool last = *last_flag;
+                asm volatile("bar.sync 1, 128;" ::: "memory");  // every thread has read the flag
+                if (last) {
+                    __threadfence();
+                    const float* base = a.part + ((int64_t)w.h * a.nparts + a.part_base[w.tile]) * BM * (DH + 4);
+                    const int64_t slot = (int64_t)BM * (DH + 4);
+                    // 4 output columns per work unit
+                    for (int idx = eid; idx < valid_rows * (DH / 4); idx += 128) {
+                        const int rr = idx / (DH / 4), d0 = (idx - rr * (DH / 4)) * 4;
+                        float M = -INFINITY;
+                        for (int sp = 0; sp < w.nsplit; ++sp) M = fmaxf(M, __ldcg(base + sp * slot + rr * (DH + 4) + DH));
+                        float L = 0.f, o4[4] = {0.f, 0.f, 0.f, 0.f};
+                        for (int sp = 0; sp < w.nsplit; ++sp) {
+                            const float* rp = base + sp * slot + rr * (DH + 4);
+                            const float m = __ldcg(rp + DH);
+                            if (m == -INFINITY) continue;
+                            const float wgt = ex2(m - M);
+                            L = fmaf(wgt, __ldcg(rp + DH + 1), L);
+                            const float4 v = __ldcg((const float4*)(rp + d0));
+                            o4[0] = fmaf(wgt, v.x, o4[0]), o4[1] = fmaf(wgt, v.y, o4[1]);
+                            o4[2] = fmaf(wgt, v.z, o4[2]), o4[3] = fmaf(wgt, v.w, o4[3]);
                         }
-                        for (int o = 0; o < a.nout; ++o) *(uint2*)((unsigned char*)a.outs[o] + off) = make_uint2(w[0], w[1]);
+                        const float inv = 1.f / L;
+                        const int64_t off = ((w.t0 + rr) * a.out_row_elems + a.out_col0 + (int64_t)w.h * DH + d0) * oes;
+                        if (a.out_dtype == NMG_F32) {
+                            const float4 v = make_float4(o4[0] * inv, o4[1] * inv, o4[2] * inv, o4[3] * inv);
+                            for (int o = 0; o < a.nout; ++o) *(float4*)((unsigned char*)a.outs[o] + off) = v;
+                        } else {
+                            const uint2 v = make_uint2(pack_out(o4[0] * inv, o4[1] * inv, a.out_dtype),
+                                                       pack_out(o4[2] * inv, o4[3] * inv, a.out_dtype));
+                            for (int o = 0; o < a.nout; ++o) *(uint2*)((unsigned char*)a.outs[o] + off) = v;
+                        }
                     }
                 }
             }
-        }
-        const int oes = a.out_dtype == NMG_F32 ? 4 : 2;
-        const int cpr = DH * oes / 16;  // 16-byte chunks per row: 16, 32 or 64
-        unsigned char* stage = smem + C::Q_OFF;
-        if (nsplit == 1 && have_o && a.nout == 1) {  // one local output: each thread stores its own row part
-            tc::fence_after_sync();
-            const float inv = 1.f / l_row;
-            const bool row_valid = t0 + row < a.rows;
-            const int64_t obase = (t0 + row) * a.out_row_elems + a.out_col0 + (int64_t)h * DH + part * C::PART_D;
-#pragma unroll 1
-            for (int c = 0; c < C::PART_D / 32; ++c) {
-                uint32_t r[32];
-                tc::ld_32x32b_x32(t_lane + C::O_COL + part * C::PART_D + c * 32, r);
-                if (!row_valid) continue;
-                if (a.out_dtype == NMG_F32) {
-                    uint4* dst = (uint4*)((float*)a.outs[0] + obase + c * 32);
-#pragma unroll
-                    for (int e = 0; e < 8; ++e)
-                        dst[e] = make_uint4(__float_as_uint(__uint_as_float(r[4 * e]) * inv),
-                                            __float_as_uint(__uint_as_float(r[4 * e + 1]) * inv),
-                                            __float_as_uint(__uint_as_float(r[4 * e + 2]) * inv),
-                                            __float_as_uint(__uint_as_float(r[4 * e + 3]) * inv));
-                } else {
-                    const bool obf = a.out_dtype == NMG_BF16;
-                    uint4* dst = (uint4*)((uint16_t*)a.outs[0] + obase + c * 32);
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        uint32_t w[4];
-#pragma unroll
-                        for (int t = 0; t < 4; ++t) {
-                            const float f0 = __uint_as_float(r[8 * e + 2 * t]) * inv;
-                            const float f1 = __uint_as_float(r[8 * e + 2 * t + 1]) * inv;
-                            const uint32_t b0 = obf ? dev::f32_to_bf16_bits(f0) : dev::f32_to_f16_bits(f0);
-                            const uint32_t b1 = obf ? dev::f32_to_bf16_bits(f1) : dev::f32_to_f16_bits(f1);
-                            w[t] = b0 | (b1 << 16);
-                        }
-                        dst[e] = make_uint4(w[0], w[1], w[2], w[3]);
-                    }
-                }
-            }
-        } else if (nsplit == 1 && have_o) {
-            tc::fence_after_sync();
-            const float inv = 1.f / l_row;
-#pragma unroll 1
-            for (int c = 0; c < C::PART_D / 32; ++c) {
-                uint32_t r[32];
-                tc::ld_32x32b_x32(t_lane + C::O_COL + part * C::PART_D + c * 32, r);
-                const int col = part * C::PART_D + c * 32;  // first of this thread's 32 columns
-                if (a.out_dtype == NMG_F32) {
-#pragma unroll
-                    for (int e = 0; e < 8; ++e) {
-                        const int ch = col / 4 + e;
-                        *(uint4*)(stage + row * cpr * 16 + ((ch ^ (row & 15)) << 4)) =
-                            make_uint4(__float_as_uint(__uint_as_float(r[4 * e]) * inv),
-                                       __float_as_uint(__uint_as_float(r[4 * e + 1]) * inv),
-                                       __float_as_uint(__uint_as_float(r[4 * e + 2]) * inv),
-                                       __float_as_uint(__uint_as_float(r[4 * e + 3]) * inv));
-                    }
-                } else {
-                    const bool obf = a.out_dtype == NMG_BF16;
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        uint32_t w[4];
-#pragma unroll
-                        for (int t = 0; t < 4; ++t) {
-                            const float f0 = __uint_as_float(r[8 * e + 2 * t]) * inv;
-                            const float f1 = __uint_as_float(r[8 * e + 2 * t + 1]) * inv;
-                            const uint32_t b0 = obf ? dev::f32_to_bf16_bits(f0) : dev::f32_to_f16_bits(f0);
-                            const uint32_t b1 = obf ? dev::f32_to_bf16_bits(f1) : dev::f32_to_f16_bits(f1);
-                            w[t] = b0 | (b1 << 16);
-                        }
-                        const int ch = col / 8 + e;
-                        *(uint4*)(stage + row * cpr * 16 + ((ch ^ (row & 15)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
-                    }
-                }
-            }
-        }
-        // Every softmax thread reaches this barrier (have_o is uniform across
-        // the CTA: the o_done wait is the same for all, and a timeout sets the
-        // error flag but still arrives here).
-        if (nsplit == 1) asm volatile("bar.sync 2, %0;" ::"r"(C::SOFTMAX_THREADS) : "memory");
-        if (nsplit == 1 && have_o && a.nout > 1) {
-            const int sid = threadIdx.x - 96;  // 0 .. SOFTMAX_THREADS - 1
-            const int valid_rows = (int)(t_last - t0 + 1);
-            const int64_t col_base = a.out_col0 + (int64_t)h * DH;
-            for (int idx = sid; idx < valid_rows * cpr; idx += C::SOFTMAX_THREADS) {
-                const int rr = idx / cpr, ch = idx - rr * cpr;
-                const uint4 val = *(const uint4*)(stage + rr * cpr * 16 + ((ch ^ (rr & 15)) << 4));
-                const int64_t off = ((t0 + rr) * a.out_row_elems + col_base) * oes + ch * 16;
-                for (int o = 0; o < a.nout; ++o) *(uint4*)((unsigned char*)a.outs[o] + off) = val;
-            }
-            // No fence here: the caller orders these stores before any read of
-            // the rows with a stream-ordered barrier (nmg_comm_barrier), which
-            // starts only after this grid, stores included, has completed.
+            ++kn;
         }
     }
 
@@ -643,7 +786,7 @@ bool prefill_supported(const nmg_kv_cache* c, int hq, int q_dtype, int64_t rows)
     if (c->dh != 128 && c->dh != 256) return false;
     const int bn = c->dh == 128 ? 128 : 64;
     if (c->slots % bn != 0) return false;
-    if (rows < 64 || (rows + 127) / 128 > 65535) return false;  // query tiles index the grid's y
+    if (rows < 64) return false;
     if ((int64_t)c->hkv * c->slots > 0x7FFFFFFF) return false;
     return encode_tiled_fn() != nullptr;
 }
@@ -765,7 +908,11 @@ int attend_rows_prefill(const nmg_kv_cache* c, int hq, const void* q, int q_dtyp
     a->out_dtype = out_dtype;
     int st = device_error_flag(c->device, &a->err);
     if (st == NMG_OK) {
-        dim3 grid((unsigned)hq, a->n_items > 0 ? (unsigned)a->n_items : (unsigned)ntiles);
+        // Persistent CTAs, one per SM, walk the unit list (heaviest first).
+        a->n_work = (int64_t)(a->n_items > 0 ? a->n_items : ntiles) * hq;
+        int nsm = 148;
+        if (cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, c->device) != cudaSuccess) nsm = 148;
+        const dim3 grid((unsigned)std::min<int64_t>(a->n_work, nsm));
         if (dh == 128)
             st = c->dtype == NMG_BF16 ? launch_prefill<128, true>(*a, grid, stream) : launch_prefill<128, false>(*a, grid, stream);
         else

@@ -231,6 +231,13 @@ __device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* m
         : "memory");
 }
 
+// Prefetch one tile of a 3-D tensor map into L2 (no shared memory, no completion).
+__device__ __forceinline__ void tma_prefetch_3d(const CUtensorMap* map, int32_t x, int32_t y, int32_t z) {
+    asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];" ::"l"(map), "r"(x), "r"(y),
+                 "r"(z)
+                 : "memory");
+}
+
 // Untiled bulk copy shared -> global in the thread's bulk group; both
 // addresses 16-byte aligned, `bytes` a multiple of 16.
 __device__ __forceinline__ void bulk_s2g(void* gmem_dst, const void* smem_src, uint32_t bytes) {
