@@ -91,10 +91,11 @@ struct WyArgs {
 // (row j = column j of T, fp32 while T is solved, then rounded) and the [I;M]
 // image of even value heads, R1 the [I;M] image of odd ones, so the store of
 // one head's [T;MT] overlaps the next head's work.  G holds the chunk's 64
-// cumulative gates and, at [64], the first warp's total for the scan.
+// cumulative gates and, at [64], the first warp's total for the scan; D the
+// four 16 x 16 diagonal blocks of T row-major, for the block products.
 constexpr uint32_t P1_A = 0, P1_TI = 16384, P1_IM0 = 32768, P1_R1 = 65536, P1_IM1 = P1_R1,
                    P1_Y = P1_R1 + kKTBytes, P1_G = P1_Y + 3 * 1024, P1_AUX = P1_G + 512,
-                   P1_BAR = P1_AUX + 2 * kAuxBytes, P1_END = P1_BAR + 64;
+                   P1_D = P1_AUX + 2 * kAuxBytes, P1_BAR = P1_D + 4096, P1_END = P1_BAR + 64;
 constexpr uint32_t P1_SMEM = 1024 + P1_END;
 
 // Byte offset of T[i][j] .. T[i + 3][j] (i a multiple of 4) in the T^T image:
@@ -113,8 +114,9 @@ __device__ __forceinline__ float dot4(float4 a, float4 b, float acc) {
 // thread), then the off-diagonal blocks one block diagonal at a time,
 //   T_ij = -T_ii sum_{j <= k < i} A_ik T_kj,
 // with all 128 threads on each step.  fp32 throughout; T lands in the T^T
-// image unrounded.  Y holds 3 blocks of partial sums.
-__device__ __forceinline__ void wy_invert(const float* A, uint8_t* TI, float* Y, int tid) {
+// image unrounded.  Y holds 3 blocks of partial sums, D the diagonal blocks
+// T_ii row-major ([4][16][16]).
+__device__ __forceinline__ void wy_invert(const float* A, uint8_t* TI, float* Y, float* D, int tid) {
     if (tid < 64) {
         const int b = tid >> 4, c = tid & 15, j = 16 * b + c;
         float t[16];
@@ -134,6 +136,8 @@ __device__ __forceinline__ void wy_invert(const float* A, uint8_t* TI, float* Y,
             t[r] = r == c ? 1.f : (r < c ? 0.f : -(s0 + s1));
         }
         for (int i = 0; i < 16 * b; i += 4) *(float4*)(TI + ti_off4(i, j)) = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int r = 0; r < 16; ++r) D[(b * 16 + r) * 16 + c] = t[r];
 #pragma unroll
         for (int m = 0; m < 4; ++m)
             *(float4*)(TI + ti_off4(16 * b + 4 * m, j)) = make_float4(t[4 * m], t[4 * m + 1], t[4 * m + 2], t[4 * m + 3]);
@@ -163,11 +167,15 @@ __device__ __forceinline__ void wy_invert(const float* A, uint8_t* TI, float* Y,
             const int blk = p >> 7, r = (p >> 4) & 7, c = p & 15;
             const int bi = blk + L, j = 16 * blk + c;
             float z0 = 0.f, z1 = 0.f;
+            const float4* d0 = (const float4*)(D + (bi * 16 + r) * 16);
+            const float4* d1 = (const float4*)(D + (bi * 16 + r + 8) * 16);
 #pragma unroll
-            for (int rp = 0; rp < 16; ++rp) {  // T_ii is lower triangular: its upper entries are stored zeros
-                const float yv = Y[(blk * 16 + rp) * 16 + c];
-                z0 = fmaf(*(const float*)(TI + ti_off(16 * bi + r, 16 * bi + rp)), yv, z0);
-                z1 = fmaf(*(const float*)(TI + ti_off(16 * bi + r + 8, 16 * bi + rp)), yv, z1);
+            for (int q = 0; q < 4; ++q) {  // T_ii is lower triangular: its upper entries are stored zeros
+                const float4 t0 = d0[q], t1 = d1[q];
+                const float y0 = Y[(blk * 16 + 4 * q) * 16 + c], y1 = Y[(blk * 16 + 4 * q + 1) * 16 + c];
+                const float y2 = Y[(blk * 16 + 4 * q + 2) * 16 + c], y3 = Y[(blk * 16 + 4 * q + 3) * 16 + c];
+                z0 = fmaf(t0.w, y3, fmaf(t0.z, y2, fmaf(t0.y, y1, fmaf(t0.x, y0, z0))));
+                z1 = fmaf(t1.w, y3, fmaf(t1.z, y2, fmaf(t1.y, y1, fmaf(t1.x, y0, z1))));
             }
             *(float*)(TI + ti_off(16 * bi + r, j)) = -z0;
             *(float*)(TI + ti_off(16 * bi + r + 8, j)) = -z1;
@@ -191,6 +199,7 @@ __global__ void __launch_bounds__(128) delta_wy_kernel(const __grid_constant__ W
     uint8_t* TI = smem + P1_TI;
     float* Y_s = (float*)(smem + P1_Y);
     float* G_s = (float*)(smem + P1_G);
+    float* D_s = (float*)(smem + P1_D);
     uint64_t* bars = (uint64_t*)(smem + P1_BAR);  // 0: [K;Q] landed, 1: first MMA, 2: second MMA (once per value head)
     uint32_t* tmem_slot = (uint32_t*)(bars + 4);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -343,7 +352,7 @@ __global__ void __launch_bounds__(128) delta_wy_kernel(const __grid_constant__ W
             }
         }
         __syncthreads();
-        wy_invert(A_s, TI, Y_s, tid);
+        wy_invert(A_s, TI, Y_s, D_s, tid);
         dev::fence_proxy_async_smem();
         tc::fence_before_sync();
         __syncthreads();
