@@ -7,11 +7,16 @@ pre-applied, K/V written to the device cache.  One step = append the 4096 K/V
 rows into a fresh cache + attention of the 4096 query rows (137.47 GFLOP).
 `value` is TFLOP/s of that step with inputs resident in HBM; `e2e` is the same
 through the C ABI with host (pinned) inputs and outputs copied inside the
-timed region.
+timed region, every step's copies included, pipelined over three streams the
+way a serving loop runs (step i + 1's inputs cross PCIe while step i
+computes and step i - 1's rows come back).
 
-At N GPUs (torchrun) each rank owns hkv/N KV heads (and their query heads)
-and the head outputs are all-gathered over NVLink by NCCL, then permuted back
-to the reference's [row][head*dim] layout: total work is fixed ("strong").
+At N GPUs (torchrun) each rank owns hkv/N KV heads (and their query heads);
+the attention epilogue stores the rank's heads of every output row into all
+ranks' row buffers over NVLink and a stream-ordered barrier closes the step,
+so each GPU holds the reference's [row][head*dim] rows: total work is fixed
+("strong").  The line also times the unfused alternative (attention, NCCL
+all-gather, permutation) for comparison.
 
 Measured extras at N=1 (their own units, each with a roofline fraction):
 config 1 fp32 decode, config 3 delta-rule prefill + 256 decode steps,
@@ -456,29 +461,60 @@ def bench_prefill(args, torch, dist, rank, world, dev):
     out_host = torch.empty(S, hq * dh, dtype=torch.bfloat16).pin_memory()
     e2e_steps = max(3, args.steps // 2)
 
+    # Three streams, as a serving loop would run them: the inputs of step i + 1
+    # cross PCIe while step i computes and step i - 1's rows come back (with
+    # shards the rows come back in stream order on rank 0).  Every step's own
+    # copies stay inside the timed region.
+    s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    ev_in = [torch.cuda.Event() for _ in range(R)]     # set b's inputs are on the GPU
+    ev_used = [torch.cuda.Event() for _ in range(R)]   # set b's inputs were consumed, its rows written
+    nob = 2 if comm is not None else R                 # output buffers
+    ev_out = [torch.cuda.Event() for _ in range(nob)]  # output buffer copied to the host
+
     def e2e_step(i):
-        q, k, v, c, o = sets[i % R]
-        q.copy_(hq_host, non_blocking=True)
-        k.copy_(hk_host, non_blocking=True)
-        v.copy_(hv_host, non_blocking=True)
+        b = i % R
+        q, k, v, c, o = sets[b]
+        ob = (i & 1) if comm is not None else b
+        with torch.cuda.stream(s_in):
+            s_in.wait_event(ev_used[b])
+            q.copy_(hq_host, non_blocking=True)
+            k.copy_(hk_host, non_blocking=True)
+            v.copy_(hv_host, non_blocking=True)
+            ev_in[b].record(s_in)
+        stream.wait_event(ev_in[b])
+        stream.wait_event(ev_out[ob])
         c.reset()
         c.append(0, k, v)
         if comm is not None:
-            nm.attend_fanout(c, q, 0, scale, peers[i & 1], hq * dh, sh.out_col0(dh))
+            nm.attend_fanout(c, q, 0, scale, peers[ob], hq * dh, sh.out_col0(dh))
             comm.barrier(cur())
-            if rank == 0:  # every GPU holds the assembled rows; one copy goes to the host
-                out_host.copy_(shared[i & 1].tensor(), non_blocking=True)
         else:
             nm.attend(c, q, 0, scale, out=o)
-            out_host.copy_(o, non_blocking=True)
+        ev_used[b].record(stream)
+        if comm is not None:
+            # Every GPU holds the assembled rows; rank 0 copies them to the
+            # host in stream order, before its next barrier lets the other
+            # ranks write the buffer again.
+            if rank == 0:
+                out_host.copy_(shared[ob].tensor(), non_blocking=True)
+        else:
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(ev_used[b])
+                out_host.copy_(o, non_blocking=True)
+                ev_out[ob].record(s_out)
 
     for i in range(2):
         e2e_step(i)
+    torch.cuda.synchronize(dev)
     barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
+    s_in.wait_event(e0)
+    s_out.wait_event(e0)
     for i in range(e2e_steps):
         e2e_step(i)
+    stream.wait_stream(s_in)
+    stream.wait_stream(s_out)
     e1.record(stream)
     barrier()
     e2e_ms = e0.elapsed_time(e1) / e2e_steps
