@@ -1,28 +1,34 @@
 // attn_prefill_sm100.cu -- causal / sliding-window GQA flash attention on the
 // 5th-generation tensor cores (K4).
 //
-// One CTA computes a 128-row query tile of one query head against the key
-// blocks its rows can see, reading K/V straight out of the device cache:
+// A persistent kernel: one CTA per SM walks a list of units -- a 128-row
+// query tile of one query head (or a key split of one) against the key
+// blocks its rows can see -- heaviest first, reading K/V straight out of the
+// device cache:
 //
-//   warp 0      TMA producer for Q (once) and K blocks (3-stage ring; a K
-//               stage is released as soon as its S MMA completes)
+//   warp 0      TMA producer for Q (one tile per unit; the next unit's tile
+//               is prefetched into L2) and K blocks (3-stage ring; a K stage
+//               is released as soon as its S MMA completes)
 //   warp 2      TMA producer for V blocks (2-stage ring, released after P.V)
 //               (cp.async.bulk.tensor, 128-byte swizzle, one CTA per copy)
-//   warp 1      allocates TMEM and issues tcgen05.mma from one thread:
-//                 S_j = Q K_j^T  (M=128, N=BN, K=DH)  into TMEM (two S buffers)
-//                 O  += P_j V_j  (M=128, N=DH, K=BN)  A = P_j read from TMEM
-//   warps 3..   softmax: PARTS warps (4 for head_dim 128, 2 for 256) share
-//               each 32-row TMEM lane quadrant and split every S row into
-//               PARTS column ranges; they swap their block maxima through
-//               shared memory, so all apply the same running max (four warps
-//               per scheduler hide each other's TMEM and barrier latency).
-//               Each thread reads its part of the row from TMEM, applies the
-//               causal/window mask, an online softmax in base 2
-//               (rescaling O in TMEM only when the running max grows by more
-//               than 2^8), writes P as packed fp16 pairs into TMEM over the
-//               S buffer it came from (V is fp16 in every 16-bit cache, so
-//               P.V is an fp16 MMA with 11-bit probabilities), and at the end
-//               normalises O and stores the row.
+//   warp 1      allocates TMEM and issues tcgen05.mma from one thread, one
+//               stream over all units:
+//                 S_g = Q K_g^T  (M=128, N=BN, K=DH)  into TMEM (two S buffers)
+//                 O  += P_g V_g  (M=128, N=DH, K=BN)  A = P_g read from TMEM,
+//                 O one of two accumulators by unit parity (head_dim 128)
+//   warps 3..   softmax: two warps share each 32-row TMEM lane quadrant and
+//               split every S row into two column ranges; they swap their
+//               block maxima through shared memory, so both apply the same
+//               running max.  Each thread reads its part of the row from
+//               TMEM, applies the causal/window mask, an online softmax in
+//               base 2 (rescaling O in TMEM only when the running max grows
+//               by more than 2^8), writes P as packed fp16 pairs into TMEM
+//               over the S buffer it came from (V is fp16 in every 16-bit
+//               cache, so P.V is an fp16 MMA with 11-bit probabilities), and
+//               leaves each unit's row sum and max for the epilogue.
+//   last 4      epilogue: one warp per quadrant normalises a finished unit's
+//               O and stores the rows (or split partials) while the softmax
+//               works on the next unit.
 //
 // The equation is the reference reduction (nm/src/qwen35.hpp:360-382,
 // nm/src/gemma4.hpp:593-615, :687-709): softmax over visible rows of
@@ -104,7 +110,7 @@ struct PrefillArgs {
     // l) partials in part (slot part_base[tile] + split of head h: [BM][DH +
     // 4] fp32, O then m, l, with rows padded to 16 bytes) and the last one to
     // finish (ticket per head and tile) merges them.  n_items == 0: one unit
-    // per (tile, head).
+    // per (tile, head), unit u = tile ntiles - 1 - u / hq of head u % hq.
     int64_t n_work;
     int n_items, split_blocks, nparts, ntiles;
     float* part;
