@@ -394,3 +394,33 @@ def test_prefill_key_splits_with_fanout(dev):
     for o in outs:
         assert torch.equal(o[:, col0:], want)
         assert not o[:, :col0].any()
+
+
+def test_prefill_many_units_per_cta_match_oracle(dev):
+    # 10 query tiles x 32 heads = 320 units on at most 148 persistent CTAs:
+    # each CTA takes two or three units in snake order, alternating its two
+    # O accumulators, so unit boundaries, the overlapped epilogue and the
+    # next unit's first S all run; every row against the reference.
+    hq, hkv, dh, S = 32, 8, 128, 1280
+    k, v, q = rnd("bf16", 41, 1, (S, hkv * dh)), rnd("bf16", 41, 2, (S, hkv * dh)), rnd("bf16", 41, 3, (S, hq * dh))
+    cache = nm.FullAttentionCache(hkv, dh, capacity=S, dtype="bf16")
+    cache.append(0, TD(k, dev, "bf16"), TD(v, dev, "bf16"))
+    scale = dh ** -0.5
+    out = nm.attend(cache, TD(q, dev, "bf16"), 0, scale, out_dtype=torch.float32).cpu().numpy()
+    want = oracle.attend(k, v, 0, 0, hkv, dh, q, hq, 0, scale=np.float32(scale))
+    assert_close(out, want, what="all rows")
+    bf = nm.attend(cache, TD(q, dev, "bf16"), 0, scale, out_dtype=torch.bfloat16)
+    assert torch.equal(bf, torch.from_numpy(out).to(dev).to(torch.bfloat16))  # the epilogue rounds like a cast
+
+
+def test_prefill_head_dim_256_window_many_units(dev):
+    # head_dim 256 (one O accumulator: each unit's epilogue is waited for
+    # before the next unit's first P.V) with a sliding window, 304 units.
+    hq, hkv, dh, S, W = 8, 4, 256, 4864, 1024
+    k, v, q = rnd("bf16", 43, 1, (S, hkv * dh)), rnd("bf16", 43, 2, (S, hkv * dh)), rnd("bf16", 43, 3, (S, hq * dh))
+    cache = nm.LocalAttentionCache(hkv, dh, W, capacity=((S + W + 127) // 128) * 128, dtype="bf16")
+    out = nm.append_attend(cache, 0, TD(k, dev, "bf16"), TD(v, dev, "bf16"), TD(q, dev, "bf16"), None,
+                           out_dtype=torch.float32).cpu().numpy()
+    for r0, r1 in ((0, 256), (2304, 2560), (S - 256, S)):
+        want = oracle.attend(k[:r1], v[:r1], 0, W, hkv, dh, q[r0:r1], hq, r0, use_scale=False)
+        assert_close(out[r0:r1], want, what=f"rows {r0}:{r1}")
