@@ -86,9 +86,8 @@ def _random_state(seed, hv, d):
 @pytest.mark.parametrize("n", [1, 12, 63, 64, 65, 130, 700, 2100, 4100])
 def test_chunked_prefill_matches_oracle(dev, n):
     # Chunk 64, tcgen05 tf32 path: ragged last chunk, single partial chunk,
-    # exact multiples; a non-zero starting state; value heads over tiled key heads.
-    # 2100 and 4100 tokens (33 and 65 chunks) run in 2 and 4 segments whose
-    # phase-2 launches hand the state on through memory.
+    # exact multiples; a non-zero starting state; value heads over tiled key heads;
+    # 2100 and 4100 tokens (33 and 65 chunks) for longer state chains.
     hv, hk, d = 4, 2, 128
     q, k, v, g, b = delta_inputs(11 + n, n, hk, hv, d)
     s0 = _random_state(n, hv, d)
