@@ -681,6 +681,52 @@ def extra_config3(torch, dev, small=False):
     res["decode"] = {"us_per_step": ms * 1e3, "value": gbs, "unit": "GB/s", "tok_per_s": 1 / (ms * 1e-3),
                      "roofline": {"bound": "hbm", "achieved": gbs, "peak": p["hbm"], "frac": gbs / p["hbm"],
                                   "bytes_per_step": bytes_, "note": "2 MB state is L2-resident between steps"}}
+    del qd, kd, vd, gd, bd, od
+    # the steps either side of the recurrence over the same T tokens: conv +
+    # SiLU + L2 norms + gates from the packed projection, and the gated RMS norm
+    C, W = 2 * hk * d + hv * d, 4
+    conv = nm.ConvState(C, W, device=dev.index)
+    cw = torch.randn(C, W, device=dev, generator=g) * 0.5
+    qkv = torch.randn(T, C, device=dev, generator=g)
+    br, ar = torch.randn(T, hv, device=dev, generator=g), torch.randn(T, hv, device=dev, generator=g)
+    dtb, dsc = torch.randn(hv, device=dev, generator=g), -torch.rand(hv, device=dev, generator=g)
+
+    def pro():
+        conv.clear()
+        nm.delta_prologue(conv, cw, qkv, br, ar, dtb, dsc, hk, hv, d, d)
+
+    pro()
+    torch.cuda.synchronize(dev)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(5):
+        pro()
+    b.record()
+    torch.cuda.synchronize(dev)
+    ms_p = a.elapsed_time(b) / 5
+    bytes_p = 4 * (T * C + C * W + 2 * T * hv + 2 * hv + 2 * T * hk * d + T * hv * d + 2 * T * hv)
+    del qkv
+    o = torch.randn(T, hv, d, device=dev, generator=g)
+    z = torch.randn(T, hv, d, device=dev, generator=g)
+    gamma = torch.randn(d, device=dev, generator=g)
+    eo = torch.empty_like(o)
+    nm.delta_epilogue(o, z, gamma, 1e-6, out=eo)
+    torch.cuda.synchronize(dev)
+    a.record()
+    for _ in range(5):
+        nm.delta_epilogue(o, z, gamma, 1e-6, out=eo)
+    b.record()
+    torch.cuda.synchronize(dev)
+    ms_e = a.elapsed_time(b) / 5
+    bytes_e = 4 * (3 * T * hv * d + d)
+    gb_p, gb_e = bytes_p / (ms_p * 1e-3) / 1e9, bytes_e / (ms_e * 1e-3) / 1e9
+    res["prologue"] = {"us": ms_p * 1e3, "value": gb_p, "unit": "GB/s",
+                       "roofline": {"bound": "hbm", "achieved": gb_p, "peak": p["hbm"], "frac": gb_p / p["hbm"],
+                                    "bytes": bytes_p, "note": "conv width 4 + SiLU + per-head L2 norms + gates, "
+                                                              "inputs 268 MB > L2"}}
+    res["epilogue"] = {"us": ms_e * 1e3, "value": gb_e, "unit": "GB/s",
+                       "roofline": {"bound": "hbm", "achieved": gb_e, "peak": p["hbm"], "frac": gb_e / p["hbm"],
+                                    "bytes": bytes_e, "note": "per-head RMS norm times SiLU(z)"}}
     return {"workload": "config 3: gated delta rule, T=8192, 16 k-heads / 32 v-heads, d128, fp32 state", **res}
 
 

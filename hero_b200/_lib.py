@@ -112,6 +112,13 @@ SIGNATURES = {
     "nmg_gated_delta_step": [_vp, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp],
     "nmg_delta_step": [_vp, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp],
     "nmg_delta_prefill": [_vp, _i32, _i64, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _vp],
+    "nmg_conv_create": [_i32, _i32, _i32, ctypes.POINTER(_vp)],
+    "nmg_conv_destroy": [_vp],
+    "nmg_conv_clear": [_vp, _vp],
+    "nmg_conv_history": [_vp, ctypes.POINTER(_vp)],
+    "nmg_conv_step": [_vp, _vp, _vp, _i64, _vp, _i32, _vp],
+    "nmg_delta_prologue": [_vp, _vp, _i32, _i32, _i32, _i32, _i64] + [_vp] * 10 + [_vp],
+    "nmg_delta_epilogue": [_i32, _i32, _i64, _vp, _vp, _vp, ctypes.c_float, _vp, _vp],
     "nmg_comm_unique_id": [_vp],
     "nmg_comm_init": [_vp, _i32, _i32, _i32, ctypes.POINTER(_vp)],
     "nmg_comm_destroy": [_vp],

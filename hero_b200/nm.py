@@ -345,6 +345,81 @@ def delta_prefill(state: DeltaNetState, q, k, v, gate, beta, hk: int, *, chunk: 
     return out
 
 
+# ---- the steps either side of the recurrence (src/qwen35.hpp:420-461) -------
+
+class ConvState:
+    """Device CausalConv1dState<channels, width> (src/recurrent.hpp:63-110): the
+    last width - 1 inputs of a depthwise causal conv, zero (the causal pad)."""
+
+    def __init__(self, channels: int, width: int, device: int = 0):
+        self.channels, self.width, self.device = int(channels), int(width), int(device)
+        h = ctypes.c_void_p()
+        call("nmg_conv_create", self.channels, self.width, self.device, ctypes.byref(h))
+        self._h = h
+
+    def __del__(self):
+        h = getattr(self, "_h", None)
+        if h is not None and h.value:
+            try:
+                _lib.lib().nmg_conv_destroy(h)
+            except Exception:
+                pass
+            self._h = None
+
+    @property
+    def handle(self):
+        return self._h
+
+    def clear(self) -> None:
+        call("nmg_conv_clear", self._h, _stream(self.device))
+
+    def history(self) -> torch.Tensor:
+        """A torch view [width - 1, channels] of the carried inputs, oldest first (no copy)."""
+        p = ctypes.c_void_p()
+        call("nmg_conv_history", self._h, ctypes.byref(p))
+        rows = max(self.width - 1, 1)
+        return _from_ptr(p.value, rows * self.channels, self.device).view(rows, self.channels)
+
+    def step(self, weights, x, *, silu: bool = False, out=None) -> torch.Tensor:
+        """step() over T tokens: x [T, channels] -> y [T, channels]; weights [channels, width]."""
+        x = _dev(x)
+        if x.dim() == 1:
+            x = x.unsqueeze(0)
+        if out is None:
+            out = torch.empty_like(x, dtype=torch.float32)
+        call("nmg_conv_step", self._h, _ptr(_dev(weights)), _ptr(x), x.shape[0], _ptr(out), 1 if silu else 0,
+             _stream(x.device))
+        return out
+
+
+def delta_prologue(conv: ConvState, conv_weights, qkv, beta_raw, alpha_raw, dt_bias, decay_scale, hk: int, hv: int,
+                   dk: int, dv: int):
+    """The packed projection qkv [T, 2*hk*dk + hv*dv] -> (q [T,hk,dk], k [T,hk,dk],
+    v [T,hv,dv], beta [T,hv], gate [T,hv]) as qwen35.hpp:396-446 builds them."""
+    qkv = _dev(qkv)
+    T, dev = qkv.shape[0], qkv.device
+    q = torch.empty(T, hk, dk, dtype=torch.float32, device=dev)
+    k = torch.empty(T, hk, dk, dtype=torch.float32, device=dev)
+    v = torch.empty(T, hv, dv, dtype=torch.float32, device=dev)
+    beta = torch.empty(T, hv, dtype=torch.float32, device=dev)
+    gate = torch.empty(T, hv, dtype=torch.float32, device=dev)
+    call("nmg_delta_prologue", conv.handle, _ptr(_dev(conv_weights)), int(hk), int(hv), int(dk), int(dv), T, _ptr(qkv),
+         _ptr(_dev(beta_raw)), _ptr(_dev(alpha_raw)), _ptr(_dev(dt_bias)), _ptr(_dev(decay_scale)), _ptr(q), _ptr(k),
+         _ptr(v), _ptr(beta), _ptr(gate), _stream(dev))
+    return q, k, v, beta, gate
+
+
+def delta_epilogue(o, z, gamma, eps: float = 1e-6, *, out=None) -> torch.Tensor:
+    """RMSNorm per head then SiLU(z) gate (qwen35.hpp:458-460): o, z [T, hv, dv], gamma [dv]."""
+    o, z = _dev(o), _dev(z)
+    T, hv, dv = o.shape
+    if out is None:
+        out = torch.empty_like(o)
+    call("nmg_delta_epilogue", int(hv), int(dv), T, _ptr(o), _ptr(z), _ptr(_dev(gamma)), float(eps), _ptr(out),
+         _stream(o.device))
+    return out
+
+
 # ---- multi-GPU: output rows assembled by the attention epilogue -------------
 
 class SharedRows:

@@ -215,6 +215,47 @@ NMG_API int nmg_delta_step(nmg_delta_state* state, int hk, const float* q, const
 NMG_API int nmg_delta_prefill(nmg_delta_state* state, int hk, int64_t T, const float* q, const float* k, const float* v,
                       const float* gate, const float* beta, float* out, int chunk, void* stream);
 
+/* ---- the steps either side of the recurrence ---------------------------------
+ *
+ * A Qwen 3.5 recurrent layer around gated_delta_step (src/qwen35.hpp:420-461).
+ *
+ * CausalConv1dState<Channels,Width> (src/recurrent.hpp:63-110): the last
+ * width - 1 inputs of a depthwise causal conv, zero-initialised (the causal
+ * pad), on the device as [width - 1][channels] fp32, oldest row first. */
+typedef struct nmg_conv_state nmg_conv_state;
+
+NMG_API int nmg_conv_create(int channels, int width, int device, nmg_conv_state** out);
+NMG_API int nmg_conv_destroy(nmg_conv_state* state);
+NMG_API int nmg_conv_clear(nmg_conv_state* state, void* stream);
+/* Device pointer to the history rows (for inspection and tests). */
+NMG_API int nmg_conv_history(const nmg_conv_state* state, float** hist);
+/* CausalConv1dState::step (recurrent.hpp:76-88) over T tokens:
+ * y[t][c] = sum_i w[c][i] x[c][t - (W-1) + i], x/y: [T][channels] fp32,
+ * weights: [channels][width] (one row of taps per channel, tap 0 oldest);
+ * silu != 0 applies x / (1 + e^-x) to y (Silu, src/components.hpp:102-105).
+ * The history advances by the T inputs.  At most 65535 * 16 tokens a call. */
+NMG_API int nmg_conv_step(nmg_conv_state* state, const float* weights, const float* x, int64_t T, float* y, int silu,
+                          void* stream);
+
+/* The delta-net prologue of T tokens (qwen35.hpp:396-415, :436-446): the
+ * packed projection qkv [T][2*hk*dk + hv*dv] ([q | k | v] channels) through
+ * the conv state and SiLU; q and k L2-normalised per key head (eps 1e-6,
+ * recurrent.hpp:40-48) and q scaled by 1/sqrt(dk); beta = sigmoid(beta_raw),
+ * gate = decay_scale[h] * softplus(alpha_raw + dt_bias[h]) (recurrent.hpp:35,
+ * core.hpp:579).  Outputs in the layouts nmg_delta_prefill takes: q,k
+ * [T][hk][dk], v [T][hv][dv], beta/gate [T][hv].  dk and dv multiples of 32
+ * up to 1024; at most 65535 * 16 tokens a call. */
+NMG_API int nmg_delta_prologue(nmg_conv_state* conv, const float* conv_weights, int hk, int hv, int dk, int dv, int64_t T,
+                               const float* qkv, const float* beta_raw, const float* alpha_raw, const float* dt_bias,
+                               const float* decay_scale, float* q, float* k, float* v, float* beta, float* gate,
+                               void* stream);
+/* The gated output norm (qwen35.hpp:458-460): out[t][h][j] =
+ * gamma[j] * o[t][h][j] * inv_rms(o[t][h]) * SiLU(z[t][h][j]) with
+ * inv_rms = 1 / sqrt(mean(o^2) + eps) (RMSNorm, components.hpp:167-180, per
+ * head, :248-281).  o, z, out: [T][hv][dv]; gamma: [dv]. */
+NMG_API int nmg_delta_epilogue(int hv, int dv, int64_t T, const float* o, const float* z, const float* gamma, float eps,
+                               float* out, void* stream);
+
 /* ---- multi-GPU: KV-head-group sharding + one all-gather --------------------
  *
  * The reference has no distributed backend (it runs par_for on one host).

@@ -75,6 +75,12 @@ def lib():
             L.nmo_sigmoid.argtypes = [ctypes.c_float]
             L.nmo_sigmoid.restype = ctypes.c_float
             L.nmo_l2_normalize.argtypes = [_f32p, _f32p, ctypes.c_int, ctypes.c_float]
+            L.nmo_conv_run.argtypes = [_f32p, ctypes.c_int, ctypes.c_int, _f32p, ctypes.c_int64, _f32p, _f32p]
+            L.nmo_silu.argtypes = [ctypes.c_float]
+            L.nmo_silu.restype = ctypes.c_float
+            L.nmo_delta_prologue.argtypes = ([_f32p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                              ctypes.c_int64] + [_f32p] * 11)
+            L.nmo_delta_epilogue.argtypes = [ctypes.c_int64, ctypes.c_int, _f32p, _f32p, _f32p, ctypes.c_float, _f32p]
             L.nmo_normal.argtypes = [ctypes.c_uint64, ctypes.c_uint64, ctypes.c_uint64, _i64, _f32p]
             L.nmo_uniform_int.argtypes = [ctypes.c_uint64, ctypes.c_uint64, _i64, _i64, _i64, _i64p]
             L.nmo_round_bf16.argtypes = [_f32p, _i64]
@@ -115,6 +121,9 @@ def ref():
                 R.nmref_sigmoid.argtypes = [ctypes.c_float]
                 R.nmref_sigmoid.restype = ctypes.c_float
                 R.nmref_l2_normalize.argtypes = [ctypes.c_int, _f32p, _f32p]
+                R.nmref_conv_run.argtypes = [ctypes.c_int, ctypes.c_int, _f32p, _f32p, _i64, _f32p]
+                R.nmref_silu.argtypes = [_i64, _f32p, _f32p]
+                R.nmref_rmsnorm.argtypes = [ctypes.c_int, _i64, _f32p, ctypes.c_float, _f32p, _f32p]
                 R.nmref_fp32_to_bf16.argtypes = [ctypes.c_float]
                 R.nmref_fp32_to_bf16.restype = ctypes.c_uint16
                 R.nmref_fp32_to_fp16.argtypes = [ctypes.c_float]
@@ -234,6 +243,56 @@ def l2_normalize(x, eps=1e-6):
     for r in range(flat.shape[0]):
         lib().nmo_l2_normalize(_fp(flat[r]), _fp(y[r]), flat.shape[1], eps)
     return y.reshape(x.shape)
+
+
+def conv_run(weights, x, history=None):
+    """CausalConv1dState::step over T tokens (src/recurrent.hpp:76-104).
+
+    weights [C][W] (tap 0 oldest), x [T][C], history [W-1][C] oldest first (zero
+    when None); returns (y [T][C], the advanced history)."""
+    w = np.ascontiguousarray(weights, dtype=np.float32)
+    C, W = w.shape
+    x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1, C)
+    hist = np.zeros((max(W - 1, 1), C), np.float32) if history is None else np.array(history, np.float32, order="C")
+    y = np.empty_like(x)
+    lib().nmo_conv_run(_fp(w), C, W, _fp(x), x.shape[0], _fp(hist), _fp(y))
+    return y, hist
+
+
+def silu(x):
+    """x / (1 + e^-x) elementwise (src/components.hpp:102-105)."""
+    x = np.asarray(x, dtype=np.float32)
+    with np.errstate(over="ignore"):  # e^-x overflows to inf for x < -88: the result is -0, as in fp32
+        return np.vectorize(lambda e: lib().nmo_silu(float(e)), otypes=[np.float32])(x).astype(np.float32)
+
+
+def delta_prologue(weights, qkv, beta_raw, alpha_raw, dt_bias, decay_scale, hk, hv, dk, dv, history=None):
+    """qwen35.hpp:396-446 for T tokens: returns (q [T,hk,dk], k, v [T,hv,dv], beta [T,hv], gate [T,hv], history)."""
+    w = np.ascontiguousarray(weights, dtype=np.float32)
+    C, W = w.shape
+    qkv = np.ascontiguousarray(qkv, dtype=np.float32).reshape(-1, C)
+    T = qkv.shape[0]
+    hist = np.zeros((max(W - 1, 1), C), np.float32) if history is None else np.array(history, np.float32, order="C")
+    f = lambda a: np.ascontiguousarray(a, dtype=np.float32)
+    q = np.empty((T, hk, dk), np.float32)
+    k = np.empty((T, hk, dk), np.float32)
+    v = np.empty((T, hv, dv), np.float32)
+    beta = np.empty((T, hv), np.float32)
+    gate = np.empty((T, hv), np.float32)
+    lib().nmo_delta_prologue(_fp(w), W, hk, hv, dk, dv, T, _fp(qkv), _fp(hist), _fp(f(beta_raw)), _fp(f(alpha_raw)),
+                             _fp(f(dt_bias)), _fp(f(decay_scale)), _fp(q), _fp(k), _fp(v), _fp(beta), _fp(gate))
+    return q, k, v, beta, gate, hist
+
+
+def delta_epilogue(o, z, gamma, eps=1e-6):
+    """RMSNorm per head then the SiLU(z) gate (qwen35.hpp:458-460); o, z [..., dv]."""
+    o = np.ascontiguousarray(o, dtype=np.float32)
+    z = np.ascontiguousarray(z, dtype=np.float32)
+    dv = o.shape[-1]
+    out = np.empty_like(o)
+    lib().nmo_delta_epilogue(o.size // dv, dv, _fp(o), _fp(z), _fp(np.ascontiguousarray(gamma, dtype=np.float32)),
+                             float(eps), _fp(out))
+    return out
 
 
 def softplus(x: float) -> float:

@@ -22,6 +22,10 @@
  *   nmo_l2_normalize        src/recurrent.hpp:40-48
  *   nmo_softplus            src/recurrent.hpp:35
  *   nmo_sigmoid             src/core.hpp:579
+ *   nmo_conv_run            src/recurrent.hpp:63-110 (CausalConv1dState::step over T tokens)
+ *   nmo_silu                src/components.hpp:102-105
+ *   nmo_delta_prologue      src/qwen35.hpp:396-415, :436-446 (conv, SiLU, L2 norms, gates)
+ *   nmo_delta_epilogue      src/qwen35.hpp:458-460, src/components.hpp:167-180, :248-281
  *   nmo_fp32_to_bf16 etc.   src/core.hpp:34-100
  *
  * Inputs are plain row-major fp32 arrays in the reference's own layouts:
@@ -342,4 +346,74 @@ void nmo_l2_normalize(const float* x, float* y, int n, float eps) {
     float norm = sqrtf(ss);
     const float scale = 1.f / (norm < eps ? eps : norm); /* std::max(norm, eps) */
     for (int i = 0; i < n; ++i) y[i] = x[i] * scale;
+}
+
+/* ---- the steps either side of the recurrence ----------------------------- */
+
+/* CausalConv1dState<C,W>::step over T tokens (recurrent.hpp:76-104).  hist
+ * [W-1][C] holds the carried inputs, oldest first, and is advanced in place;
+ * per channel the current sample's tap comes first, then taps 0 .. W-2
+ * (recurrent.hpp:80-83). */
+void nmo_conv_run(const float* w, int C, int W, const float* x, int64_t T, float* hist, float* y) {
+    const int H = W - 1;
+    float* win = (float*)malloc(sizeof(float) * (size_t)(H > 0 ? H : 1));
+    for (int c = 0; c < C; ++c) {
+        for (int i = 0; i < H; ++i) win[i] = hist[(size_t)i * C + c];
+        for (int64_t t = 0; t < T; ++t) {
+            const float xin = x[(size_t)t * C + c];
+            float sum = w[(size_t)c * W + H] * xin;
+            for (int tap = 0; tap < H; ++tap) sum += w[(size_t)c * W + tap] * win[tap];
+            y[(size_t)t * C + c] = sum;
+            for (int i = 0; i + 1 < H; ++i) win[i] = win[i + 1];
+            if (H > 0) win[H - 1] = xin;
+        }
+        for (int i = 0; i < H; ++i) hist[(size_t)i * C + c] = win[i];
+    }
+    free(win);
+}
+
+float nmo_silu(float x) { return x / (1.f + expf(-x)); } /* not x * sigmoid(x): components.hpp:104 */
+
+/* The delta-net prologue of T tokens: conv + SiLU over the packed [q | k | v]
+ * channels, q and k L2-normalised per key head (q then scaled by 1/sqrt(dk),
+ * qwen35.hpp:427, :443-445), beta = sigmoid, gate = decay_scale * softplus(a +
+ * dt_bias) (qwen35.hpp:400-415). */
+void nmo_delta_prologue(const float* w, int W, int hk, int hv, int dk, int dv, int64_t T, const float* qkv, float* hist,
+                        const float* beta_raw, const float* alpha_raw, const float* dt_bias, const float* decay_scale,
+                        float* q, float* k, float* v, float* beta, float* gate) {
+    const int C = 2 * hk * dk + hv * dv;
+    float* y = (float*)malloc(sizeof(float) * (size_t)T * C);
+    nmo_conv_run(w, C, W, qkv, T, hist, y);
+    const float q_scale = 1.f / sqrtf((float)dk);
+    for (int64_t t = 0; t < T; ++t) {
+        float* row = y + (size_t)t * C;
+        for (int c = 0; c < C; ++c) row[c] = nmo_silu(row[c]);
+        for (int h = 0; h < hk; ++h) {
+            float* qo = q + ((size_t)t * hk + h) * dk;
+            float* ko = k + ((size_t)t * hk + h) * dk;
+            nmo_l2_normalize(row + (size_t)h * dk, qo, dk, 1e-6f);
+            for (int i = 0; i < dk; ++i) qo[i] *= q_scale;
+            nmo_l2_normalize(row + (size_t)hk * dk + (size_t)h * dk, ko, dk, 1e-6f);
+        }
+        memcpy(v + (size_t)t * hv * dv, row + (size_t)2 * hk * dk, sizeof(float) * (size_t)hv * dv);
+        for (int h = 0; h < hv; ++h) {
+            const size_t i = (size_t)t * hv + h;
+            beta[i] = nmo_sigmoid(beta_raw[i]);
+            gate[i] = decay_scale[h] * nmo_softplus(alpha_raw[i] + dt_bias[h]);
+        }
+    }
+    free(y);
+}
+
+/* out = RMSNorm(o; gamma, eps) per head, times SiLU(z) (qwen35.hpp:458-460):
+ * inverse_rms = 1 / sqrt(dot(o, o) / dv + eps), out = gamma * o * inverse_rms
+ * * silu(z) (components.hpp:174-176). */
+void nmo_delta_epilogue(int64_t rows, int dv, const float* o, const float* z, const float* gamma, float eps, float* out) {
+    for (int64_t r = 0; r < rows; ++r) {
+        const float* x = o + (size_t)r * dv;
+        float ss = 0.f;
+        for (int i = 0; i < dv; ++i) ss += x[i] * x[i];
+        const float inv = 1.f / sqrtf(ss / (float)dv + eps);
+        for (int i = 0; i < dv; ++i) out[(size_t)r * dv + i] = gamma[i] * x[i] * inv * nmo_silu(z[(size_t)r * dv + i]);
+    }
 }

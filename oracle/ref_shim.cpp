@@ -24,6 +24,7 @@
 #include <cstdint>
 #include <cstdio>
 #include <cstdlib>
+#include <memory>
 #include <stdexcept>
 #include <vector>
 
@@ -357,6 +358,51 @@ int nmref_l2_normalize(int n, const float* x, float* y) {
         for (int i = 0; i < 128; ++i) y[i] = r[i];
         return 0;
     }
+    return 100;
+}
+
+// CausalConv1dState<C, W>::step over T tokens from a fresh (zero) state.
+int nmref_conv_run(int channels, int width, const float* weights, const float* x, int64_t T, float* y) {
+#define X(C, W)                                                                              \
+    if (channels == C && width == W) {                                                       \
+        Matrix<W> taps;                                                                      \
+        taps.reserve(C);                                                                     \
+        for (int c = 0; c < C; ++c) taps.append(VecView<W>(vec_from<W>(weights + (size_t)c * W))); \
+        auto conv = std::make_unique<CausalConv1dState<C, W>>();                             \
+        for (int64_t t = 0; t < T; ++t) {                                                    \
+            const Vec<C> out = conv->step(VecView<C>(vec_from<C>(x + (size_t)t * C)), taps);   \
+            for (int c = 0; c < C; ++c) y[(size_t)t * C + c] = out[c];                       \
+        }                                                                                    \
+        return 0;                                                                            \
+    }
+    X(2, 3) X(24, 4) X(1024, 4) X(8192, 4)
+#undef X
+    return 100;
+}
+
+// Silu (components.hpp:102-105), one element at a time through the reference type.
+void nmref_silu(int64_t n, const float* x, float* y) {
+    for (int64_t i = 0; i < n; ++i) {
+        Vec<1> v;
+        v[0] = x[i];
+        Silu{}(MutVecView<1>(v));
+        y[i] = v[0];
+    }
+}
+
+// RMSNorm<N> (components.hpp:167-180) of each of `rows` rows.
+int nmref_rmsnorm(int n, int64_t rows, const float* gamma, float eps, const float* x, float* y) {
+#define X(N)                                                                   \
+    if (n == N) {                                                              \
+        const RMSNorm<N> norm(vec_from<N>(gamma), eps);                        \
+        for (int64_t r = 0; r < rows; ++r) {                                   \
+            const Vec<N> out = norm(VecView<N>(vec_from<N>(x + (size_t)r * N))); \
+            for (int i = 0; i < N; ++i) y[(size_t)r * N + i] = out[i];         \
+        }                                                                      \
+        return 0;                                                              \
+    }
+    X(2) X(64) X(128)
+#undef X
     return 100;
 }
 
