@@ -175,6 +175,42 @@ private:
     nmg_delta_state* h_ = nullptr;
 };
 
+// CausalConv1dState<Channels, Width> (recurrent.hpp:63-110): the carried last
+// Width - 1 inputs of the depthwise causal conv, on the device.
+template <size_t Channels, size_t Width>
+class CausalConv1dState {
+public:
+    explicit CausalConv1dState(int device = 0) { check(nmg_conv_create(int(Channels), int(Width), device, &h_)); }
+    CausalConv1dState(const CausalConv1dState&) = delete;
+    CausalConv1dState& operator=(const CausalConv1dState&) = delete;
+    ~CausalConv1dState() { nmg_conv_destroy(h_); }
+    void clear(void* stream) { check(nmg_conv_clear(h_, stream)); }
+    // step() over `tokens` rows: x, y [tokens][Channels]; weights [Channels][Width].
+    void step(const float* weights, const float* x, size_t tokens, float* y, bool silu, void* stream) {
+        check(nmg_conv_step(h_, weights, x, int64_t(tokens), y, silu ? 1 : 0, stream));
+    }
+    nmg_conv_state* handle() const { return h_; }
+
+private:
+    nmg_conv_state* h_ = nullptr;
+};
+
+// The delta-net prologue of qwen35.hpp:396-446 (conv + SiLU over the packed
+// [q | k | v] projection, per-head L2 norms, gates) into the layouts
+// DeltaNetState::prefill takes, and the gated RMS norm of qwen35.hpp:458-460.
+template <size_t Hk, size_t Hv, size_t Dk, size_t Dv, size_t Width>
+void delta_prologue(CausalConv1dState<2 * Hk * Dk + Hv * Dv, Width>& conv, const float* conv_weights, size_t tokens,
+                    const float* qkv, const float* beta_raw, const float* alpha_raw, const float* dt_bias,
+                    const float* decay_scale, float* q, float* k, float* v, float* beta, float* gate, void* stream) {
+    check(nmg_delta_prologue(conv.handle(), conv_weights, int(Hk), int(Hv), int(Dk), int(Dv), int64_t(tokens), qkv,
+                             beta_raw, alpha_raw, dt_bias, decay_scale, q, k, v, beta, gate, stream));
+}
+template <size_t Hv, size_t Dv>
+void delta_epilogue(size_t tokens, const float* o, const float* z, const float* gamma, float eps, float* out,
+                    void* stream) {
+    check(nmg_delta_epilogue(int(Hv), int(Dv), int64_t(tokens), o, z, gamma, eps, out, stream));
+}
+
 // gated_delta_step<Dk, Dv> (recurrent.hpp:146-177) on one device head block;
 // gate and beta are device scalars.
 template <size_t Dk, size_t Dv>

@@ -5,6 +5,14 @@
 
 #include "nmg.hpp"
 
+// The delta-net prologue/epilogue templates instantiate at a Qwen 3.5 shape
+// (only compiled here: running them needs a GPU).
+[[maybe_unused]] static auto* const prologue_fn = &nmg::delta_prologue<16, 32, 128, 128, 4>;
+[[maybe_unused]] static auto* const epilogue_fn = &nmg::delta_epilogue<32, 128>;
+[[maybe_unused]] static void (nmg::CausalConv1dState<8192, 4>::*const conv_step_fn)(const float*, const float*, size_t,
+                                                                                    float*, bool, void*) =
+    &nmg::CausalConv1dState<8192, 4>::step;
+
 int main() {
     int failures = 0;
     try {
