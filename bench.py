@@ -730,6 +730,55 @@ def extra_config3(torch, dev, small=False):
     return {"workload": "config 3: gated delta rule, T=8192, 16 k-heads / 32 v-heads, d128, fp32 state", **res}
 
 
+def extra_attn_io(torch, dev, small=False):
+    """The steps either side of a Qwen 3.5 attention reduction at T=8192: the
+    prologue (per-head RMSNorm + partial RoPE of Q and K, append to a bf16 cache)
+    and the output gate, both HBM-bound."""
+    from hero_b200 import nm
+
+    hq, hkv, dh, T = 16, 4, 256, (1024 if small else 8192)
+    g = torch.Generator(device=dev)
+    g.manual_seed(6)
+    qg = torch.randn(T, 2 * hq * dh, device=dev, generator=g)
+    k = torch.randn(T, hkv * dh, device=dev, generator=g)
+    v = torch.randn(T, hkv * dh, device=dev, generator=g)
+    qgam, kgam = torch.randn(dh, device=dev, generator=g), torch.randn(dh, device=dev, generator=g)
+    cache = nm.FullAttentionCache(hkv, dh, capacity=T, dtype="bf16", device=dev.index)
+    a = torch.randn(T, hq * dh, device=dev, generator=g).to(torch.bfloat16)
+
+    def pro():
+        cache.reset()
+        return nm.attn_prologue(cache, 0, qg, k, v, qgam, kgam, 1e-6, 1e7, 1, 4)
+
+    def timed(fn, n=5):
+        fn()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(n):
+            fn()
+        e1.record()
+        torch.cuda.synchronize(dev)
+        return e0.elapsed_time(e1) / n
+
+    ms_p = timed(pro)
+    ms_g = timed(lambda: nm.attn_gate(qg, a, dh))
+    # prologue: read the Q halves of qg, K and V (fp32); write Q (bf16) and the cache rows (bf16 K, fp16 V)
+    bytes_p = 4 * T * hq * dh + 2 * 4 * T * hkv * dh + 2 * T * hq * dh + 2 * 2 * T * hkv * dh
+    # gate: read the gate halves of qg (fp32), read and write A (bf16)
+    bytes_g = 4 * T * hq * dh + 2 * 2 * T * hq * dh
+    p = peaks()
+    gb_p, gb_g = bytes_p / (ms_p * 1e-3) / 1e9, bytes_g / (ms_g * 1e-3) / 1e9
+    return {"workload": f"Qwen 3.5 attention prologue and gate, T={T}, 16 q-heads / 4 kv-heads, d256, bf16 cache",
+            "prologue": {"us": ms_p * 1e3, "value": gb_p, "unit": "GB/s",
+                         "roofline": {"bound": "hbm", "achieved": gb_p, "peak": p["hbm"], "frac": gb_p / p["hbm"],
+                                      "bytes": bytes_p, "note": "the K rows pass through an fp32 staging buffer on "
+                                                                "their way to nmg_kv_append (not counted)"}},
+            "gate": {"us": ms_g * 1e3, "value": gb_g, "unit": "GB/s",
+                     "roofline": {"bound": "hbm", "achieved": gb_g, "peak": p["hbm"], "frac": gb_g / p["hbm"],
+                                  "bytes": bytes_g}}}
+
+
 def extra_config4(torch, dev, small=False):
     from hero_b200 import nm
 
@@ -836,7 +885,7 @@ def main():
     ap.add_argument("--impl", default="nmg", choices=["nmg", "reference"])
     ap.add_argument("--no-extra", action="store_true", help="headline only")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
-    ap.add_argument("--only", choices=["c1", "c2", "c3", "c4", "c5"],
+    ap.add_argument("--only", choices=["c1", "c2", "c3", "c4", "c5", "io"],
                     help="run one workload alone (profiling); prints its own JSON line")
     ap.add_argument("--small", action="store_true", help="with --only: profiling-sized variant")
     args = ap.parse_args()
@@ -863,14 +912,15 @@ def main():
 
     hero_b200.lib()  # fail loudly before any work if the CUDA library is missing
     if args.only and args.only != "c2":
-        fn = {"c1": extra_config1, "c3": extra_config3, "c4": extra_config4, "c5": extra_config5}[args.only]
+        fn = {"c1": extra_config1, "c3": extra_config3, "c4": extra_config4, "c5": extra_config5,
+              "io": extra_attn_io}[args.only]
         print(json.dumps({"only": args.only, "small": args.small, **fn(torch, dev, small=args.small)}), flush=True)
         return
     res = bench_prefill(args, torch, dist, rank, world, dev)
     extra = {}
     if world == 1 and not args.no_extra and not args.only:
         for name, fn in (("config1", extra_config1), ("config3", extra_config3), ("config4", extra_config4),
-                         ("config5", extra_config5)):
+                         ("config5", extra_config5), ("attn_io", extra_attn_io)):
             try:
                 extra[name] = fn(torch, dev)
             except Exception as e:  # report, never hide, a failing extra

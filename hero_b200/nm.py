@@ -12,6 +12,11 @@ Mirrors the nm engine's types and calls (paths relative to the nm/ project):
 * ``scaled_dot_product_attention`` -- src/attention.hpp:124-139.
 * ``DeltaNetState`` / ``gated_delta_step`` -- src/recurrent.hpp:117-177, and
   ``delta_step`` / ``delta_prefill`` for the head loop of src/qwen35.hpp:436-456.
+* ``attn_prologue`` / ``attn_prepare`` / ``attn_gate`` -- the steps either side
+  of the attention reduction (src/qwen35.hpp:343-352, :390-393;
+  src/gemma4.hpp:206-209, :676-680).
+* ``ConvState`` / ``delta_prologue`` / ``delta_epilogue`` -- the steps either
+  side of the delta rule (src/recurrent.hpp:63-110; src/qwen35.hpp:396-461).
 
 Every call goes through libnmg.so's C ABI.  Tensors are torch CUDA tensors
 (torch provides device memory and streams only); nothing here computes on the
@@ -343,6 +348,60 @@ def delta_prefill(state: DeltaNetState, q, k, v, gate, beta, hk: int, *, chunk: 
     call("nmg_delta_prefill", state.handle, int(hk), T, _ptr(_dev(q)), _ptr(_dev(k)), _ptr(_dev(v)), _ptr(_dev(gate)),
          _ptr(_dev(beta)), _ptr(out), int(chunk), _stream(v.device))
     return out
+
+
+# ---- the steps either side of the attention reduction (src/qwen35.hpp:343-393)
+
+def attn_prologue(cache: _Cache, position: int, q, k, v, q_gamma, k_gamma, eps: float, rope_base: float,
+                  rotary_num: int = 1, rotary_den: int = 1, *, gated: bool = True, v_norm: bool = False,
+                  q_dtype=None) -> torch.Tensor:
+    """Prepare one attention layer's Q, K, V for the reduction and append K, V to the cache.
+
+    Q = rope(rmsnorm_per_head(q)), K = rope(rmsnorm_per_head(k)); V as given, or
+    rmsnorm_no_scale_per_head(v) with v_norm (Gemma 4).  With gated (Qwen 3.5),
+    q is the [T, 2*hq*dh] query projection in head-major [q | gate] pairs;
+    otherwise q is [T, hq*dh].  Returns Q [T, hq*dh] in q_dtype (default: the
+    cache's dtype); the cache gains rows position .. position + T - 1."""
+    q = _dev(q)
+    T = q.shape[0]
+    hq = q.shape[1] // ((2 if gated else 1) * cache.head_dim)
+    q_dtype = q_dtype or _TORCH[cache.dtype]
+    out = torch.empty(T, hq * cache.head_dim, dtype=q_dtype, device=q.device)
+    call("nmg_attn_prologue", cache.handle, int(hq), int(position), T, _ptr(q), int(bool(gated)), _ptr(_dev(k)),
+         _ptr(_dev(v)), _ptr(_dev(q_gamma)), _ptr(_dev(k_gamma)), int(bool(v_norm)), float(eps), float(rope_base),
+         int(rotary_num), int(rotary_den), _ptr(out), _DT[q_dtype], _stream(q.device))
+    return out
+
+
+def attn_prepare(hkv: int, head_dim: int, position: int, q, k, v, q_gamma, k_gamma, eps: float, rope_base: float,
+                 rotary_num: int = 1, rotary_den: int = 1, *, gated: bool = True, v_norm: bool = False,
+                 q_dtype=torch.float32):
+    """attn_prologue without a cache: returns (Q [T, hq*dh] in q_dtype, K [T, hkv*dh] fp32,
+    V [T, hkv*dh] fp32 -- v itself unless v_norm), for nm.append_attend."""
+    q, k, v = _dev(q), _dev(k), _dev(v)
+    T = q.shape[0]
+    hq = q.shape[1] // ((2 if gated else 1) * head_dim)
+    qo = torch.empty(T, hq * head_dim, dtype=q_dtype, device=q.device)
+    ko = torch.empty(T, hkv * head_dim, dtype=torch.float32, device=q.device)
+    vo = torch.empty_like(ko) if v_norm else v
+    call("nmg_attn_prepare", int(hq), int(hkv), int(head_dim), int(position), T, _ptr(q), int(bool(gated)), _ptr(k),
+         _ptr(v), _ptr(_dev(q_gamma)), _ptr(_dev(k_gamma)), int(bool(v_norm)), float(eps), float(rope_base),
+         int(rotary_num), int(rotary_den), _ptr(qo), _DT[q_dtype], _ptr(ko), _ptr(vo) if v_norm else None,
+         _stream(q.device))
+    return qo, ko, vo
+
+
+def attn_gate(qg, a: torch.Tensor, head_dim: int) -> torch.Tensor:
+    """a [T, hq*head_dim] *= sigmoid(gate) in place, the gates the second halves of qg's
+    [T, 2*hq*head_dim] head pairs; returns a."""
+    qg = _dev(qg)
+    a2 = a.reshape(a.shape[0], -1) if a.is_contiguous() else None
+    if a2 is None or not a.is_cuda or a2.shape[0] != qg.shape[0] or 2 * a2.shape[1] != qg.shape[1] \
+            or a2.shape[1] % head_dim:
+        raise ValueError("attn_gate: a must be a contiguous device tensor [T, hq*head_dim] beside qg [T, 2*hq*head_dim]")
+    call("nmg_attn_gate", a2.shape[0], a2.shape[1] // head_dim, int(head_dim), _ptr(qg), _ptr(a2), _DT[a.dtype],
+         _stream(a.device))
+    return a
 
 
 # ---- the steps either side of the recurrence (src/qwen35.hpp:420-461) -------

@@ -215,6 +215,41 @@ NMG_API int nmg_delta_step(nmg_delta_state* state, int hk, const float* q, const
 NMG_API int nmg_delta_prefill(nmg_delta_state* state, int hk, int64_t T, const float* q, const float* k, const float* v,
                       const float* gate, const float* beta, float* out, int chunk, void* stream);
 
+/* ---- the steps either side of the attention reduction -------------------------
+ *
+ * Before the reduction (replaces the Q/K/V preparation of qwen35.hpp:343-352 and
+ * gemma4.hpp:206-209, :676-680):
+ *   Q = rope(rmsnorm_per_head(q; q_gamma, eps)) written to q_out [T][hq*head_dim]
+ *       in q_dtype (the reference's fp32 -> bf16/fp16 rounding);
+ *   K = rope(rmsnorm_per_head(k; k_gamma, eps)) and V (v_norm = 0), or
+ *   V = rmsnorm_no_scale_per_head(v; eps) (v_norm = 1, Gemma 4, components.hpp:204-215)
+ *       appended to the cache at position.. (nmg_kv_append's rules).
+ * q is [T][hq*head_dim], or with q_gated = 1 the Qwen 3.5 query projection
+ * [T][2*hq*head_dim] in head-major pairs q_0 | gate_0 | q_1 | gate_1 ...
+ * (attention.hpp:31-57); k and v are [T][hkv*head_dim] fp32 (k == v is allowed,
+ * Gemma's unified projection).  RMSNorm<HeadDim> per head (components.hpp:167-180,
+ * :248-281); RoPE half-split, inv_freq_i = rope_base^(-2i/head_dim) rounded from
+ * double for the first rotary_num/rotary_den of the planes and 0 for the rest,
+ * angle = float(position + t) * inv_freq_i (RotaryEmbedding<HeadDim,Base,Num,Den>,
+ * attention.hpp:68-101).  head_dim a multiple of 64 up to 512.  Uses the
+ * library's staging memory: calls on one GPU are ordered by their stream. */
+NMG_API int nmg_attn_prologue(nmg_kv_cache* cache, int hq, int64_t position, int64_t T, const float* q, int q_gated,
+                              const float* k, const float* v, const float* q_gamma, const float* k_gamma, int v_norm,
+                              float eps, double rope_base, int rotary_num, int rotary_den, void* q_out, int q_dtype,
+                              void* stream);
+/* The same preparation without a cache: K (rotated) to k_out and, with v_norm, V
+ * (normed) to v_out, both fp32 [T][hkv*head_dim]; v_out is unused (may be NULL)
+ * without v_norm.  For callers that append through nmg_append_attend, e.g. a
+ * Gemma 4 sliding-window layer whose batch would evict (gemma4.hpp:237-253). */
+NMG_API int nmg_attn_prepare(int hq, int hkv, int head_dim, int64_t position, int64_t T, const float* q, int q_gated,
+                             const float* k, const float* v, const float* q_gamma, const float* k_gamma, int v_norm,
+                             float eps, double rope_base, int rotary_num, int rotary_den, void* q_out, int q_dtype,
+                             float* k_out, float* v_out, void* stream);
+/* After the reduction (qwen35.hpp:390-393): a[t][h*head_dim + i] *= sigmoid(gate_h[i]),
+ * the gates the second halves of qg's [T][2*hq*head_dim] head pairs; a [T][hq*head_dim]
+ * in a_dtype, in place. */
+NMG_API int nmg_attn_gate(int64_t T, int hq, int head_dim, const float* qg, void* a, int a_dtype, void* stream);
+
 /* ---- the steps either side of the recurrence ---------------------------------
  *
  * A Qwen 3.5 recurrent layer around gated_delta_step (src/qwen35.hpp:420-461).

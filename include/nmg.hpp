@@ -211,6 +211,29 @@ void delta_epilogue(size_t tokens, const float* o, const float* z, const float* 
     check(nmg_delta_epilogue(int(Hv), int(Dv), int64_t(tokens), o, z, gamma, eps, out, stream));
 }
 
+// Before an attention reduction: Q = rope(rmsnorm_per_head(q)) into q_out,
+// K = rope(rmsnorm_per_head(k)) and V (scale-free per-head RMS norm when
+// v_norm, Gemma 4) appended at position.. , with RotaryEmbedding<HeadDim, Base,
+// RotaryNum, RotaryDen> (attention.hpp:68-101).  gated: q is the Qwen 3.5
+// query projection in head-major [q | gate] pairs (qwen35.hpp:343-352);
+// otherwise plain [tokens][Hq * HeadDim] (gemma4.hpp:206-209, :676-680).
+template <size_t Hq, size_t Base, size_t RotaryNum = 1, size_t RotaryDen = 1, class Cache>
+void attention_prologue(Cache& cache, size_t position, size_t tokens, const float* q, bool gated, const float* k,
+                        const float* v, const float* q_gamma, const float* k_gamma, bool v_norm, float eps, void* q_out,
+                        Dtype q_dtype, void* stream) {
+    static_assert(Hq % Cache::kv_heads == 0, "query heads must be a whole number of GQA groups");
+    static_assert(RotaryDen != 0 && RotaryNum <= RotaryDen, "the rotary fraction is at most one");
+    check(nmg_attn_prologue(cache.handle(), int(Hq), int64_t(position), int64_t(tokens), q, gated ? 1 : 0, k, v,
+                            q_gamma, k_gamma, v_norm ? 1 : 0, eps, double(Base), int(RotaryNum), int(RotaryDen), q_out,
+                            int(q_dtype), stream));
+}
+// After it: attended *= sigmoid(gate), the gates the second halves of the
+// [q | gate] pairs (qwen35.hpp:390-393).
+template <size_t Hq, size_t HeadDim>
+void attention_gate(size_t tokens, const float* query_gate, void* attended, Dtype dtype, void* stream) {
+    check(nmg_attn_gate(int64_t(tokens), int(Hq), int(HeadDim), query_gate, attended, int(dtype), stream));
+}
+
 // gated_delta_step<Dk, Dv> (recurrent.hpp:146-177) on one device head block;
 // gate and beta are device scalars.
 template <size_t Dk, size_t Dv>

@@ -81,6 +81,14 @@ def lib():
             L.nmo_delta_prologue.argtypes = ([_f32p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                               ctypes.c_int64] + [_f32p] * 11)
             L.nmo_delta_epilogue.argtypes = [ctypes.c_int64, ctypes.c_int, _f32p, _f32p, _f32p, ctypes.c_float, _f32p]
+            L.nmo_rope_freqs.argtypes = [ctypes.c_int, ctypes.c_double, ctypes.c_int, ctypes.c_int, _f32p]
+            L.nmo_rope.argtypes = [_f32p, ctypes.c_int, _f32p, ctypes.c_int64]
+            L.nmo_rmsnorm.argtypes = [ctypes.c_int, _f32p, ctypes.c_float, _f32p, _f32p]
+            L.nmo_attn_prologue.argtypes = ([ctypes.c_int64, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int64,
+                                             _f32p, ctypes.c_int, _f32p, _f32p, _f32p, _f32p, ctypes.c_int,
+                                             ctypes.c_float, ctypes.c_double, ctypes.c_int, ctypes.c_int,
+                                             _f32p, _f32p, _f32p])
+            L.nmo_attn_gate.argtypes = [ctypes.c_int64, ctypes.c_int, ctypes.c_int, _f32p, _f32p]
             L.nmo_normal.argtypes = [ctypes.c_uint64, ctypes.c_uint64, ctypes.c_uint64, _i64, _f32p]
             L.nmo_uniform_int.argtypes = [ctypes.c_uint64, ctypes.c_uint64, _i64, _i64, _i64, _i64p]
             L.nmo_round_bf16.argtypes = [_f32p, _i64]
@@ -124,6 +132,10 @@ def ref():
                 R.nmref_conv_run.argtypes = [ctypes.c_int, ctypes.c_int, _f32p, _f32p, _i64, _f32p]
                 R.nmref_silu.argtypes = [_i64, _f32p, _f32p]
                 R.nmref_rmsnorm.argtypes = [ctypes.c_int, _i64, _f32p, ctypes.c_float, _f32p, _f32p]
+                R.nmref_rope.argtypes = [ctypes.c_int, ctypes.c_int64, ctypes.c_int, ctypes.c_int, ctypes.c_int, _i64,
+                                         _i64, _f32p]
+                R.nmref_head_norm.argtypes = [ctypes.c_int, ctypes.c_int, _i64, _f32p, ctypes.c_float, _f32p, _f32p]
+                R.nmref_sigmoid_n.argtypes = [_i64, _f32p, _f32p]
                 R.nmref_fp32_to_bf16.argtypes = [ctypes.c_float]
                 R.nmref_fp32_to_bf16.restype = ctypes.c_uint16
                 R.nmref_fp32_to_fp16.argtypes = [ctypes.c_float]
@@ -292,6 +304,65 @@ def delta_epilogue(o, z, gamma, eps=1e-6):
     out = np.empty_like(o)
     lib().nmo_delta_epilogue(o.size // dv, dv, _fp(o), _fp(z), _fp(np.ascontiguousarray(gamma, dtype=np.float32)),
                              float(eps), _fp(out))
+    return out
+
+
+def rope_freqs(head_dim, base, num=1, den=1):
+    """RotaryEmbedding<head_dim, base, num, den>'s inv_freq table (src/attention.hpp:76-80)."""
+    out = np.empty(head_dim // 2, np.float32)
+    lib().nmo_rope_freqs(int(head_dim), float(base), int(num), int(den), _fp(out))
+    return out
+
+
+def rope(x, first_position, base, num=1, den=1):
+    """Half-split RoPE of every head of x [..., rows, heads, head_dim], row r at
+    first_position + r (src/attention.hpp:82-101)."""
+    x = np.array(x, dtype=np.float32, order="C")
+    dh = x.shape[-1]
+    freqs = rope_freqs(dh, base, num, den)
+    rows = x.reshape(-1, x.shape[-2], dh)
+    for r in range(rows.shape[0]):
+        for h in range(rows.shape[1]):
+            lib().nmo_rope(_fp(rows[r, h]), dh, _fp(freqs), int(first_position) + r)
+    return x
+
+
+def rmsnorm(x, gamma=None, eps=1e-6):
+    """RMSNorm over the last axis (src/components.hpp:167-180), or RMSNormNoScale
+    (:204-215) when gamma is None."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    n = x.shape[-1]
+    flat, y = x.reshape(-1, n), np.empty(x.shape, np.float32).reshape(-1, n)
+    g = None if gamma is None else np.ascontiguousarray(gamma, dtype=np.float32)
+    for r in range(flat.shape[0]):
+        lib().nmo_rmsnorm(n, None if g is None else _fp(g), float(eps), _fp(flat[r]), _fp(y[r]))
+    return y.reshape(x.shape)
+
+
+def attn_prologue(q, k, v, q_gamma, k_gamma, hq, hkv, head_dim, position, eps, base, num=1, den=1, *, gated=True,
+                  v_norm=False):
+    """Q, K, V of an attention layer (qwen35.hpp:343-352; gemma4.hpp:206-209, :676-680).
+
+    q [T, (2 if gated) * hq * head_dim] (gated: head-major [q | gate] pairs),
+    k, v [T, hkv * head_dim]; returns (Q [T, hq*dh], K [T, hkv*dh], V [T, hkv*dh])."""
+    f = lambda a: np.ascontiguousarray(a, dtype=np.float32)
+    q, k, v = f(q), f(k), f(v)
+    T = q.shape[0]
+    qo = np.empty((T, hq * head_dim), np.float32)
+    ko = np.empty((T, hkv * head_dim), np.float32)
+    vo = np.empty((T, hkv * head_dim), np.float32)
+    lib().nmo_attn_prologue(T, hq, hkv, head_dim, int(position), _fp(q), int(bool(gated)), _fp(k), _fp(v),
+                            _fp(f(q_gamma)), _fp(f(k_gamma)), int(bool(v_norm)), float(eps), float(base), int(num),
+                            int(den), _fp(qo), _fp(ko), _fp(vo))
+    return qo, ko, vo
+
+
+def attn_gate(qg, a, head_dim):
+    """a * sigmoid(gate) (qwen35.hpp:390-393); qg [T, 2*hq*dh] head-major [q | gate] pairs, a [T, hq*dh]."""
+    out = np.array(a, dtype=np.float32, order="C")
+    T = out.shape[0]
+    lib().nmo_attn_gate(T, out.shape[1] // head_dim, int(head_dim), _fp(np.ascontiguousarray(qg, dtype=np.float32)),
+                        _fp(out))
     return out
 
 

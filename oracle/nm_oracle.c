@@ -26,6 +26,10 @@
  *   nmo_silu                src/components.hpp:102-105
  *   nmo_delta_prologue      src/qwen35.hpp:396-415, :436-446 (conv, SiLU, L2 norms, gates)
  *   nmo_delta_epilogue      src/qwen35.hpp:458-460, src/components.hpp:167-180, :248-281
+ *   nmo_rope_freqs, nmo_rope src/attention.hpp:68-92 (RotaryEmbedding table, one head)
+ *   nmo_rmsnorm             src/components.hpp:167-180 (RMSNorm), :204-215 (RMSNormNoScale)
+ *   nmo_attn_prologue       src/qwen35.hpp:343-352, src/gemma4.hpp:206-209, :676-680
+ *   nmo_attn_gate           src/qwen35.hpp:390-393
  *   nmo_fp32_to_bf16 etc.   src/core.hpp:34-100
  *
  * Inputs are plain row-major fp32 arrays in the reference's own layouts:
@@ -416,4 +420,71 @@ void nmo_delta_epilogue(int64_t rows, int dv, const float* o, const float* z, co
         const float inv = 1.f / sqrtf(ss / (float)dv + eps);
         for (int i = 0; i < dv; ++i) out[(size_t)r * dv + i] = gamma[i] * x[i] * inv * nmo_silu(z[(size_t)r * dv + i]);
     }
+}
+
+/* ---- the steps either side of the attention reduction ------------------- */
+
+/* RotaryEmbedding<dh, base, num, den>'s table (attention.hpp:76-80): planes
+ * below num*dh/den/2 get float(base^(-2i/dh)) computed in double, the rest 0. */
+void nmo_rope_freqs(int dh, double base, int num, int den, float* inv_freq) {
+    const int rotary = (int)((int64_t)num * dh / den / 2);
+    for (int i = 0; i < dh / 2; ++i) inv_freq[i] = i < rotary ? (float)pow(base, -(double)(2 * i) / (double)dh) : 0.f;
+}
+
+/* One head rotated at `position` (attention.hpp:82-92): plane i couples
+ * (i, i + dh/2); the angle is float(position) * inv_freq_i. */
+void nmo_rope(float* x, int dh, const float* inv_freq, int64_t position) {
+    const int planes = dh / 2;
+    for (int i = 0; i < planes; ++i) {
+        const float angle = (float)position * inv_freq[i];
+        const float c = cosf(angle), s = sinf(angle);
+        const float a = x[i], b = x[i + planes];
+        x[i] = a * c - b * s;
+        x[i + planes] = b * c + a * s;
+    }
+}
+
+/* RMSNorm<n> (components.hpp:174-176) of one row, or RMSNormNoScale<n>
+ * (:212-213) when gamma is NULL. */
+void nmo_rmsnorm(int n, const float* gamma, float eps, const float* x, float* y) {
+    float ss = 0.f;
+    for (int i = 0; i < n; ++i) ss += x[i] * x[i];
+    const float inv = 1.f / sqrtf(ss / (float)n + eps);
+    for (int i = 0; i < n; ++i) y[i] = gamma ? gamma[i] * x[i] * inv : x[i] * inv;
+}
+
+/* Q, K and V of an attention layer for T tokens at position.. (qwen35.hpp:343-352,
+ * gemma4.hpp:206-209, :676-680): q_out = rope(rmsnorm(q head; q_gamma)) with q
+ * the head-major [q | gate] pairs when q_gated, k_out = rope(rmsnorm(k head;
+ * k_gamma)), v_out = rmsnorm_no_scale(v head) when v_norm, else v. */
+void nmo_attn_prologue(int64_t T, int hq, int hkv, int dh, int64_t position, const float* q, int q_gated, const float* k,
+                       const float* v, const float* q_gamma, const float* k_gamma, int v_norm, float eps, double base,
+                       int num, int den, float* q_out, float* k_out, float* v_out) {
+    float* freqs = (float*)malloc(sizeof(float) * (size_t)(dh / 2));
+    nmo_rope_freqs(dh, base, num, den, freqs);
+    const int qstride = (q_gated ? 2 : 1) * dh;
+    for (int64_t t = 0; t < T; ++t) {
+        for (int h = 0; h < hq; ++h) {
+            float* y = q_out + ((size_t)t * hq + h) * dh;
+            nmo_rmsnorm(dh, q_gamma, eps, q + ((size_t)t * hq + h) * qstride, y);
+            nmo_rope(y, dh, freqs, position + t);
+        }
+        for (int h = 0; h < hkv; ++h) {
+            const size_t o = ((size_t)t * hkv + h) * dh;
+            nmo_rmsnorm(dh, k_gamma, eps, k + o, k_out + o);
+            nmo_rope(k_out + o, dh, freqs, position + t);
+            if (v_norm)
+                nmo_rmsnorm(dh, NULL, eps, v + o, v_out + o);
+            else
+                memcpy(v_out + o, v + o, sizeof(float) * (size_t)dh);
+        }
+    }
+    free(freqs);
+}
+
+/* a *= sigmoid(gate) (qwen35.hpp:390-393), the gate of row r = t*hq + h being
+ * the second half of qg's head pair r. */
+void nmo_attn_gate(int64_t T, int hq, int dh, const float* qg, float* a) {
+    for (int64_t r = 0; r < T * hq; ++r)
+        for (int i = 0; i < dh; ++i) a[(size_t)r * dh + i] *= nmo_sigmoid(qg[((size_t)2 * r + 1) * dh + i]);
 }

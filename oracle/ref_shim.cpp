@@ -18,6 +18,7 @@
 // on par_for: scores = [scale *] dot(q, key(j, head / group)), Softmax, and
 // scaled_add of value(j, head / group).
 #include "attention.hpp"
+#include "components.hpp"
 #include "recurrent.hpp"
 
 #include <chrono>
@@ -404,6 +405,47 @@ int nmref_rmsnorm(int n, int64_t rows, const float* gamma, float eps, const floa
     X(2) X(64) X(128)
 #undef X
     return 100;
+}
+
+// RotaryEmbedding<HeadDim, Base, Num, Den> (attention.hpp:68-101) applied to
+// each head of each row of x [rows][heads*HeadDim] at position first + row,
+// through the reference's own Matrix overload.
+int nmref_rope(int head_dim, int64_t base, int num, int den, int heads, int64_t rows, int64_t first, float* x) {
+#define X(DH, B, N, D, H)                                                                       \
+    if (head_dim == DH && base == B && num == N && den == D && heads == H) {                    \
+        Matrix<DH * H> m = Matrix<DH * H>::from_row_major(std::vector<Scalar>(x, x + (size_t)rows * DH * H)); \
+        m = RotaryEmbedding<DH, B, N, D>{}(std::move(m), Position{(size_t)first});              \
+        for (int64_t r = 0; r < rows; ++r)                                                      \
+            for (int i = 0; i < DH * H; ++i) x[(size_t)r * DH * H + i] = m.row((size_t)r)[i];   \
+        return 0;                                                                               \
+    }
+    X(8, 10000, 1, 2, 1) X(8, 10000, 1, 1, 1) X(256, 10000000, 1, 4, 2) X(256, 10000, 1, 1, 2) X(512, 1000000, 1, 4, 1)
+    X(64, 10000, 1, 1, 3)
+#undef X
+    return 100;
+}
+
+// PerHeadNorm<RMSNorm<N>> (gamma given) or PerHeadNorm<RMSNormNoScale<N>>
+// (gamma null) over `heads` heads of each row (components.hpp:167-215, :248-281).
+int nmref_head_norm(int n, int heads, int64_t rows, const float* gamma, float eps, const float* x, float* y) {
+#define X(N, H)                                                                                  \
+    if (n == N && heads == H) {                                                                  \
+        for (int64_t r = 0; r < rows; ++r) {                                                     \
+            const Vec<N * H> row = vec_from<N * H>(x + (size_t)r * N * H);                       \
+            const Vec<N * H> out = gamma ? PerHeadNorm<RMSNorm<N>>(RMSNorm<N>(vec_from<N>(gamma), eps))(VecView<N * H>(row)) \
+                                         : PerHeadNorm<RMSNormNoScale<N>>(RMSNormNoScale<N>(eps))(VecView<N * H>(row));      \
+            for (int i = 0; i < N * H; ++i) y[(size_t)r * N * H + i] = out[i];                   \
+        }                                                                                        \
+        return 0;                                                                                \
+    }
+    X(256, 2) X(512, 1) X(64, 3) X(4, 1)
+#undef X
+    return 100;
+}
+
+// sigmoid (core.hpp:579) of each element.
+void nmref_sigmoid_n(int64_t n, const float* x, float* y) {
+    for (int64_t i = 0; i < n; ++i) y[i] = sigmoid(x[i]);
 }
 
 uint16_t nmref_fp32_to_bf16(float f) { return fp32_to_bf16(f); }

@@ -9,6 +9,9 @@
 // (only compiled here: running them needs a GPU).
 [[maybe_unused]] static auto* const prologue_fn = &nmg::delta_prologue<16, 32, 128, 128, 4>;
 [[maybe_unused]] static auto* const epilogue_fn = &nmg::delta_epilogue<32, 128>;
+[[maybe_unused]] static auto* const attn_prologue_fn =
+    &nmg::attention_prologue<16, 10000000, 1, 4, nmg::FullAttentionCache<4, 256>>;
+[[maybe_unused]] static auto* const attn_gate_fn = &nmg::attention_gate<16, 256>;
 [[maybe_unused]] static void (nmg::CausalConv1dState<8192, 4>::*const conv_step_fn)(const float*, const float*, size_t,
                                                                                     float*, bool, void*) =
     &nmg::CausalConv1dState<8192, 4>::step;
