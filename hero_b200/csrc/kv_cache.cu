@@ -21,17 +21,6 @@ namespace {
 
 // One thread per (row, head, 8-element chunk); rows are the last `rows`
 // appended positions, row r going to slot (slot0 + r) mod slots.
-// V of a bf16 cache holds bf16 values stored as fp16: round to bf16 first
-// (the cache's value set), then convert exactly.
-template <int DST>
-__device__ __forceinline__ void store_v(void* vc, int64_t i, float x) {
-    if constexpr (DST == NMG_BF16) {
-        ((uint16_t*)vc)[i] = dev::f32_to_f16_bits(dev::bf16_bits_to_f32(dev::f32_to_bf16_bits(x)));
-    } else {
-        dev::store_from_f32(vc, DST, i, x);
-    }
-}
-
 template <int SRC, int DST>
 __global__ void kv_append_kernel(const void* __restrict__ keys, const void* __restrict__ values, void* __restrict__ kc,
                                  void* __restrict__ vc, int64_t rows, int64_t src_row0, int hkv, int dh, int64_t slots,
@@ -54,7 +43,7 @@ __global__ void kv_append_kernel(const void* __restrict__ keys, const void* __re
                 const float kf = dev::load_as_f32(keys, SRC, src + d0 + e);
                 const float vf = dev::load_as_f32(values, SRC, src + d0 + e);
                 dev::store_from_f32(kc, DST, dst + d0 + e, kf);
-                store_v<DST>(vc, dst + d0 + e, vf);
+                store_cache_v(vc, DST, dst + d0 + e, vf);
             }
         }
     }
@@ -110,9 +99,9 @@ int kv_append_device(nmg_kv_cache* c, int64_t first_position, const void* keys, 
     if (rows <= 0) return NMG_OK;
     // Only the newest `slots` rows of a batch can survive in the ring; writing
     // just those keeps one launch free of same-slot write races.
-    const int64_t write = rows < c->slots ? rows : c->slots;
-    const int64_t row0 = rows - write;
-    const int64_t slot0 = ((first_position + row0 - c->base) % c->slots + c->slots) % c->slots;
+    int64_t row0 = 0, slot0 = 0;
+    kv_append_slots(c, first_position, rows, &row0, &slot0);
+    const int64_t write = rows - row0;
     int prev = 0;
     NMG_CUDA_TRY(cudaGetDevice(&prev));
     if (prev != c->device) NMG_CUDA_TRY(cudaSetDevice(c->device));
@@ -201,6 +190,51 @@ extern "C" int nmg_kv_destroy(nmg_kv_cache* c) {
     return NMG_OK;
 }
 
+namespace nmg {
+
+int kv_append_begin(nmg_kv_cache* c, int64_t first, int64_t rows, int64_t* accepted, int* deferred) {
+    *accepted = 0;
+    *deferred = NMG_OK;
+    const char* kind = c->window ? "LocalAttentionCache" : "FullAttentionCache";
+    if (first < 0) return set_error(NMG_INVALID_ARGUMENT, "%s: negative position", kind);
+    if (c->size == 0 && c->total == 0) {
+        c->base = first;
+        c->oldest = first;
+    } else if (first != c->oldest + c->size) {
+        return set_error(NMG_INVALID_ARGUMENT, "%s: positions must be consecutive", kind);
+    }
+    int64_t take = rows;
+    if (c->window == 0) {
+        if (c->total + rows > c->slots)
+            return set_error(NMG_LENGTH_ERROR, "FullAttentionCache: device capacity of %lld rows exhausted",
+                             (long long)c->slots);
+    } else if (c->retaining) {
+        if (rows > c->batch_remaining) {
+            take = c->batch_remaining;  // the reference appends these, then throws
+            *deferred = set_error(NMG_LENGTH_ERROR, "LocalAttentionCache: retained batch received too many rows");
+        }
+    }
+    *accepted = take;
+    return NMG_OK;
+}
+
+void kv_append_commit(nmg_kv_cache* c, int64_t first, int64_t accepted) {
+    if (accepted <= 0) return;
+    if (c->window == 0) {
+        c->size += accepted;
+    } else if (c->retaining) {
+        c->size += accepted;
+        c->batch_remaining -= accepted;
+    } else {
+        const int64_t newest = first + accepted - 1;
+        c->size = c->size + accepted < c->window ? c->size + accepted : c->window;
+        c->oldest = newest - c->size + 1;
+    }
+    c->total += accepted;
+}
+
+}  // namespace nmg
+
 extern "C" int nmg_kv_append(nmg_kv_cache* c, int64_t first, const void* keys, const void* values, int64_t rows,
                              int src_dtype, void* stream) {
     if (!c) return set_error(NMG_INVALID_ARGUMENT, "nmg_kv_append: null cache");
@@ -208,42 +242,16 @@ extern "C" int nmg_kv_append(nmg_kv_cache* c, int64_t first, const void* keys, c
     if (rows == 0) return NMG_OK;
     if (!keys || !values) return set_error(NMG_INVALID_ARGUMENT, "nmg_kv_append: null rows");
     if (!nmg::dtype_valid(src_dtype)) return set_error(NMG_INVALID_ARGUMENT, "nmg_kv_append: bad dtype");
-    const char* who = c->window ? "LocalAttentionCache" : "FullAttentionCache";
-    if (first < 0) return set_error(NMG_INVALID_ARGUMENT, "%s: negative position", who);
-    if (c->size == 0 && c->total == 0) {
-        c->base = first;
-        c->oldest = first;
-    } else if (first != c->oldest + c->size) {
-        return set_error(NMG_INVALID_ARGUMENT, "%s: positions must be consecutive", who);
-    }
-    int64_t accepted = rows;
-    int status = NMG_OK;
-    if (c->window == 0) {
-        if (c->total + rows > c->slots)
-            return set_error(NMG_LENGTH_ERROR, "FullAttentionCache: device capacity of %lld rows exhausted",
-                             (long long)c->slots);
-    } else if (c->retaining) {
-        if (rows > c->batch_remaining) {
-            accepted = c->batch_remaining;  // the reference appends these, then throws
-            status = set_error(NMG_LENGTH_ERROR, "LocalAttentionCache: retained batch received too many rows");
-        }
-    }
+    int64_t accepted = 0;
+    int deferred = NMG_OK;
+    int st = nmg::kv_append_begin(c, first, rows, &accepted, &deferred);
+    if (st != NMG_OK) return st;
     if (accepted > 0) {
-        int st = nmg::kv_append_device(c, first, keys, values, accepted, src_dtype, (cudaStream_t)stream);
+        st = nmg::kv_append_device(c, first, keys, values, accepted, src_dtype, (cudaStream_t)stream);
         if (st != NMG_OK) return st;
-        if (c->window == 0) {
-            c->size += accepted;
-        } else if (c->retaining) {
-            c->size += accepted;
-            c->batch_remaining -= accepted;
-        } else {
-            const int64_t newest = first + accepted - 1;
-            c->size = c->size + accepted < c->window ? c->size + accepted : c->window;
-            c->oldest = newest - c->size + 1;
-        }
-        c->total += accepted;
+        nmg::kv_append_commit(c, first, accepted);
     }
-    return status;
+    return deferred;
 }
 
 extern "C" int nmg_kv_size(const nmg_kv_cache* c, int64_t* size) {

@@ -55,4 +55,30 @@ inline VisibleSpan visible_span(int64_t query, int64_t window, int64_t floor_pos
 int kv_append_device(nmg_kv_cache* c, int64_t first_position, const void* keys, const void* values, int64_t rows,
                      int src_dtype, cudaStream_t stream);
 
+// nmg_kv_append in two halves for kernels that write the rows themselves.
+// kv_append_begin validates an append of `rows` rows at `first` (setting the
+// first position of an empty cache) and returns how many rows the cache
+// takes (*accepted; fewer than rows only for an overfull retained batch, whose
+// error *deferred carries, as the reference appends those rows then throws).
+// The accepted rows' device writes go to kv_append_slots' slots, then
+// kv_append_commit updates size/oldest/retention.
+int kv_append_begin(nmg_kv_cache* c, int64_t first, int64_t rows, int64_t* accepted, int* deferred);
+void kv_append_commit(nmg_kv_cache* c, int64_t first, int64_t accepted);
+// Of `rows` rows appended at `first`, rows row0.. survive in the ring (at
+// most `slots` of them); row row0 + i goes to slot (slot0 + i) % slots.
+inline void kv_append_slots(const nmg_kv_cache* c, int64_t first, int64_t rows, int64_t* row0, int64_t* slot0) {
+    const int64_t write = rows < c->slots ? rows : c->slots;
+    *row0 = rows - write;
+    *slot0 = ((first + *row0 - c->base) % c->slots + c->slots) % c->slots;
+}
+
+// A value stored into a cache of dtype `cache_dtype`.  A bf16 cache holds
+// bf16 values and keeps V as fp16: round to bf16 first, then convert exactly.
+__device__ __forceinline__ void store_cache_v(void* vc, int cache_dtype, int64_t i, float x) {
+    if (cache_dtype == NMG_BF16)
+        ((uint16_t*)vc)[i] = dev::f32_to_f16_bits(dev::bf16_bits_to_f32(dev::f32_to_bf16_bits(x)));
+    else
+        dev::store_from_f32(vc, cache_dtype, i, x);
+}
+
 }  // namespace nmg

@@ -96,7 +96,7 @@ def test_prologue_rounds_q_like_the_reference(dev, dtype):
     want = (oracle.round_bf16 if dtype == "bf16" else oracle.round_fp16)(wq.copy()).reshape(wq.shape)
     g = got.float().cpu().numpy()
     assert np.mean(g == want) > 0.999
-    ulp = np.float32(2.0 ** (-8 if dtype == "bf16" else -11))
+    ulp = np.float32(2.0 ** (-7 if dtype == "bf16" else -10))  # one ulp, relative, at worst
     assert np.all(np.abs(g - want) <= ulp * np.maximum(np.abs(want), np.float32(2.0 ** -14)))
 
 
@@ -117,7 +117,7 @@ def test_gate_matches_oracle(dev, dtype, hq, dh):
         assert_close(out.cpu().numpy(), want, max_abs=1e-6, rel=1e-6, what="gate")
     else:
         want = (oracle.round_bf16 if dtype == "bf16" else oracle.round_fp16)(want.copy()).reshape(want.shape)
-        ulp = np.float32(2.0 ** (-8 if dtype == "bf16" else -11))
+        ulp = np.float32(2.0 ** (-7 if dtype == "bf16" else -10))  # one ulp, relative, at worst
         diff = np.abs(out.float().cpu().numpy() - want)
         assert np.all(diff <= ulp * np.maximum(np.abs(want), np.float32(2.0 ** -14)))
 
@@ -130,9 +130,9 @@ def test_gated_attention_chain_matches_oracle(dev, cache_dtype):
     Tt = 161
     q, k, v, qgam, kgam = _inputs(86, Tt, hq, hkv, dh, True)
     wq, wk, wv = oracle.attn_prologue(q, k, v, qgam, kgam, hq, hkv, dh, 0, 1e-6, 1e7, 1, 4)
-    if cache_dtype == "bf16":  # what a bf16 cache stores: Q and K in bf16, V in fp16
+    if cache_dtype == "bf16":  # what a bf16 cache holds: bf16 Q, K and V values (V stored exactly as fp16)
         wq, wk = oracle.round_bf16(wq.copy()).reshape(wq.shape), oracle.round_bf16(wk.copy()).reshape(wk.shape)
-        wv = oracle.round_fp16(wv.copy()).reshape(wv.shape)
+        wv = oracle.round_bf16(wv.copy()).reshape(wv.shape)
     scale = float(np.float32(1) / np.sqrt(np.float32(dh)))
     want = oracle.attn_gate(q, oracle.attend(wk, wv, 0, 0, hkv, dh, wq, hq, 0, scale), dh)
     cache = nm.FullAttentionCache(hkv, dh, capacity=256, dtype=cache_dtype)
