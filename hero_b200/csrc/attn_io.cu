@@ -51,6 +51,7 @@ struct QkArgs {
     int64_t slots, slot0, row0, kv_rows;  // tokens row0 .. kv_rows-1 are written, token row0 to slot0
     int64_t T, position, rows;
     int hq, hkv, dh, q_dtype, kv_dtype, q_pair, v_norm;
+    int idx32;  // row and slot arithmetic fits 32 bits (one divide instead of a 64-bit sequence)
     float eps;
     float inv_freq[kMaxPlanes];
 };
@@ -105,7 +106,7 @@ struct Row {
 __device__ __forceinline__ Row row_at(const QkArgs& a, int64_t r, int per_token, int64_t total) {
     Row w{-1, 0, 0, 0, nullptr};
     if (r >= total) return w;
-    w.t = r / per_token;
+    w.t = a.idx32 ? (int64_t)((uint32_t)r / (uint32_t)per_token) : r / per_token;
     int c = (int)(r - w.t * per_token);
     w.kind = c < a.hq ? 0 : c < a.hq + a.hkv ? 1 : 2;
     const int h = w.kind == 0 ? c : w.kind == 1 ? c - a.hq : c - a.hq - a.hkv;
@@ -115,7 +116,13 @@ __device__ __forceinline__ Row row_at(const QkArgs& a, int64_t r, int per_token,
             w.kind = -1;
             return w;
         }
-        w.dst = a.slots ? ((int64_t)h * a.slots + (a.slot0 + (w.t - a.row0)) % a.slots) * a.dh : w.rr * a.dh;
+        if (a.slots) {
+            const int64_t ring = a.slot0 + (w.t - a.row0);
+            const int64_t slot = a.idx32 ? (int64_t)((uint32_t)ring % (uint32_t)a.slots) : ring % a.slots;
+            w.dst = ((int64_t)h * a.slots + slot) * a.dh;
+        } else {
+            w.dst = w.rr * a.dh;
+        }
     }
     w.src = w.kind == 0 ? a.q + w.rr * a.q_pair * a.dh : (w.kind == 1 ? a.k : a.v) + w.rr * a.dh;
     return w;
@@ -358,6 +365,7 @@ int launch_prepare(const char* who, int hq, int hkv, int dh, int64_t position, i
     a.v_norm = v_norm ? 1 : 0;
     a.eps = eps;
     a.rows = T * (int64_t)(hq + (d.v ? 2 : 1) * hkv);
+    a.idx32 = a.rows < (1ll << 31) && d.slot0 + T < (1ll << 31) && d.slots < (1ll << 31) ? 1 : 0;
     // RotaryEmbedding's table (attention.hpp:76-80): double pow, then fp32;
     // the last table built on this thread is reused (a layer stack repeats one).
     struct Table {
