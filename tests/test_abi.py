@@ -55,3 +55,39 @@ def test_errors_map_to_reference_exception_types():
     with pytest.raises(_lib.InvalidArgument):
         # argument checking happens before any device work
         _lib.call("nmg_kv_create", 0, 128, 0, 0, 16, 0, None)
+
+
+def test_layer_steps_check_arguments_before_device_work():
+    # The steps either side of the reductions reject bad shapes with the
+    # reference's exception types before touching a device.
+    from hero_b200 import _lib
+
+    p = 16  # any non-null address: nothing is dereferenced on these paths
+    with pytest.raises(_lib.InvalidArgument):  # Hq not a multiple of Hkv
+        _lib.call("nmg_attn_prepare", 3, 2, 128, 0, 4, p, 1, p, p, p, p, 0, 1e-6, 1e4, 1, 1, p, 0, p, None, None)
+    with pytest.raises(_lib.InvalidArgument):  # rotary fraction above one
+        _lib.call("nmg_attn_prepare", 4, 2, 128, 0, 4, p, 1, p, p, p, p, 0, 1e-6, 1e4, 5, 4, p, 0, p, None, None)
+    with pytest.raises(_lib.InvalidArgument):  # a RoPE base must be positive
+        _lib.call("nmg_attn_prepare", 4, 2, 128, 0, 4, p, 1, p, p, p, p, 0, 1e-6, 0.0, 1, 1, p, 0, p, None, None)
+    with pytest.raises(_lib.Unsupported):  # head_dim not a multiple of 64
+        _lib.call("nmg_attn_prepare", 4, 2, 96, 0, 4, p, 1, p, p, p, p, 0, 1e-6, 1e4, 1, 1, p, 0, p, None, None)
+    with pytest.raises(_lib.InvalidArgument):  # V normed without a place to put it
+        _lib.call("nmg_attn_prepare", 4, 2, 128, 0, 4, p, 0, p, p, p, p, 1, 1e-6, 1e4, 1, 1, p, 0, p, None, None)
+    with pytest.raises(_lib.InvalidArgument):
+        _lib.call("nmg_attn_prologue", None, 4, 0, 4, p, 1, p, p, p, p, 0, 1e-6, 1e4, 1, 1, p, 0, None)
+    with pytest.raises(_lib.InvalidArgument):
+        _lib.call("nmg_attn_gate", -1, 4, 128, p, p, 0, None)
+    with pytest.raises(_lib.InvalidArgument):
+        _lib.call("nmg_attn_gate", 4, 4, 128, p, p, 7, None)  # not a dtype
+    _lib.call("nmg_attn_gate", 0, 4, 128, None, None, 0, None)  # zero rows: nothing to do
+    import ctypes
+
+    h = ctypes.c_void_p()
+    with pytest.raises(_lib.InvalidArgument):
+        _lib.call("nmg_conv_create", 0, 4, 0, ctypes.byref(h))  # CausalConv1dState needs channels
+    with pytest.raises(_lib.Unsupported):
+        _lib.call("nmg_conv_create", 8, 64, 0, ctypes.byref(h))  # a width no kernel is built for
+    with pytest.raises(_lib.InvalidArgument):
+        _lib.call("nmg_delta_prologue", None, p, 1, 2, 128, 128, 4, *([p] * 10), None)
+    with pytest.raises(_lib.InvalidArgument):
+        _lib.call("nmg_delta_epilogue", 0, 128, 4, p, p, p, 1e-6, p, None)
