@@ -81,13 +81,27 @@ __device__ __forceinline__ void store_vec(void* base, int dt, int64_t i, const f
         return;
     }
     uint32_t b[VW];
+    if (dt == NMG_BF16 && !v_cache && VW >= 2) {
+        // Hardware round-to-nearest-even equals core.hpp:92-100 for every
+        // non-NaN input; a NaN takes the reference's own quieting.
 #pragma unroll
-    for (int w = 0; w < VW; ++w) {
-        if (dt == NMG_BF16)
-            b[w] = v_cache ? dev::f32_to_f16_bits(dev::bf16_bits_to_f32(dev::f32_to_bf16_bits(x[w])))
-                           : dev::f32_to_bf16_bits(x[w]);
-        else
-            b[w] = dev::f32_to_f16_bits(x[w]);
+        for (int w = 0; w < VW; w += 2) {
+            uint32_t r;
+            asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(x[w + 1]), "f"(x[w]));
+            if (x[w] != x[w] || x[w + 1] != x[w + 1])
+                r = (uint32_t)dev::f32_to_bf16_bits(x[w]) | ((uint32_t)dev::f32_to_bf16_bits(x[w + 1]) << 16);
+            b[w] = r & 0xFFFFu;
+            b[w + 1] = r >> 16;
+        }
+    } else {
+#pragma unroll
+        for (int w = 0; w < VW; ++w) {
+            if (dt == NMG_BF16)
+                b[w] = v_cache ? dev::f32_to_f16_bits(dev::bf16_bits_to_f32(dev::f32_to_bf16_bits(x[w])))
+                               : dev::f32_to_bf16_bits(x[w]);
+            else
+                b[w] = dev::f32_to_f16_bits(x[w]);
+        }
     }
     uint16_t* p = (uint16_t*)base + i;
     if constexpr (VW == 4) *reinterpret_cast<uint2*>(p) = make_uint2(b[0] | (b[1] << 16), b[2] | (b[3] << 16));
@@ -103,21 +117,20 @@ struct Row {
     const float* src;
 };
 
-__device__ __forceinline__ Row row_at(const QkArgs& a, int64_t r, int per_token, int64_t total) {
-    Row w{-1, 0, 0, 0, nullptr};
-    if (r >= total) return w;
-    w.t = a.idx32 ? (int64_t)((uint32_t)r / (uint32_t)per_token) : r / per_token;
-    int c = (int)(r - w.t * per_token);
+// Row c of token t (c < per_token); t >= T means no row.
+__device__ __forceinline__ Row row_at(const QkArgs& a, int64_t t, int c) {
+    Row w{-1, 0, t, 0, nullptr};
+    if (t >= a.T) return w;
     w.kind = c < a.hq ? 0 : c < a.hq + a.hkv ? 1 : 2;
     const int h = w.kind == 0 ? c : w.kind == 1 ? c - a.hq : c - a.hq - a.hkv;
-    w.rr = w.t * (w.kind == 0 ? a.hq : a.hkv) + h;
+    w.rr = t * (w.kind == 0 ? a.hq : a.hkv) + h;
     if (w.kind != 0) {
-        if (w.t < a.row0 || w.t >= a.kv_rows) {  // evicted within the batch, or refused
+        if (t < a.row0 || t >= a.kv_rows) {  // evicted within the batch, or refused
             w.kind = -1;
             return w;
         }
         if (a.slots) {
-            const int64_t ring = a.slot0 + (w.t - a.row0);
+            const int64_t ring = a.slot0 + (t - a.row0);
             const int64_t slot = a.idx32 ? (int64_t)((uint32_t)ring % (uint32_t)a.slots) : ring % a.slots;
             w.dst = ((int64_t)h * a.slots + slot) * a.dh;
         } else {
@@ -126,6 +139,12 @@ __device__ __forceinline__ Row row_at(const QkArgs& a, int64_t r, int per_token,
     }
     w.src = w.kind == 0 ? a.q + w.rr * a.q_pair * a.dh : (w.kind == 1 ? a.k : a.v) + w.rr * a.dh;
     return w;
+}
+
+// (token, row-in-token) of global row r.
+__device__ __forceinline__ void token_of(const QkArgs& a, int64_t r, int per_token, int64_t* t, int* c) {
+    *t = a.idx32 ? (int64_t)((uint32_t)r / (uint32_t)per_token) : r / per_token;
+    *c = (int)(r - *t * per_token);
 }
 
 template <int VW, int M>
@@ -198,7 +217,12 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(const __grid_constant
     const int64_t warps = (int64_t)gridDim.x * 8;
     int64_t item = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
     int k = 0;
-    Row cur = row_at(a, item * kRowsPerItem, per_token, total);
+    // (nt, nc): token and row-in-token of the row being fetched; one division
+    // when a warp moves to its next item, increments within an item.
+    int64_t nt = 0;
+    int nc = 0;
+    if (item < items) token_of(a, item * kRowsPerItem, per_token, &nt, &nc);
+    Row cur = item < items && item * kRowsPerItem < total ? row_at(a, nt, nc) : Row{-1, 0, 0, 0, nullptr};
     float x[J][VW];
     if (cur.kind >= 0) {
 #pragma unroll
@@ -209,8 +233,14 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(const __grid_constant
     while (item < items) {
         int64_t nitem = item;
         int nk = k + 1;
-        if (nk == kRowsPerItem) nitem += warps, nk = 0;
-        const Row nxt = nitem < items ? row_at(a, nitem * kRowsPerItem + nk, per_token, total) : Row{-1, 0, 0, 0, nullptr};
+        if (nk == kRowsPerItem) {
+            nitem += warps, nk = 0;
+            if (nitem < items) token_of(a, nitem * kRowsPerItem, per_token, &nt, &nc);
+        } else if (++nc == per_token) {
+            ++nt, nc = 0;
+        }
+        const bool more = nitem < items && nitem * kRowsPerItem + nk < total;
+        const Row nxt = more ? row_at(a, nt, nc) : Row{-1, 0, 0, 0, nullptr};
         float y[J][VW];
         if (nxt.kind >= 0) {
 #pragma unroll
