@@ -136,6 +136,8 @@ def ref():
                                          _i64, _f32p]
                 R.nmref_head_norm.argtypes = [ctypes.c_int, ctypes.c_int, _i64, _f32p, ctypes.c_float, _f32p, _f32p]
                 R.nmref_sigmoid_n.argtypes = [_i64, _f32p, _f32p]
+                R.nmref_sdpa.argtypes = [ctypes.c_int, ctypes.c_int, _i64, _i64, _f32p, _f32p, _f32p, ctypes.c_float,
+                                         _f32p]
                 R.nmref_fp32_to_bf16.argtypes = [ctypes.c_float]
                 R.nmref_fp32_to_bf16.restype = ctypes.c_uint16
                 R.nmref_fp32_to_fp16.argtypes = [ctypes.c_float]

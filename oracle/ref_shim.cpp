@@ -443,6 +443,26 @@ int nmref_head_norm(int n, int heads, int64_t rows, const float* gamma, float ep
     return 100;
 }
 
+// scaled_dot_product_attention<Heads, D, D> (attention.hpp:124-139): dense,
+// unmasked, Q [tq][Heads*D], K/V [tk][Heads*D]; the vision ViT's call
+// (gemma4_vision.hpp:167) is <12, 64, 64> with scale 1.
+int nmref_sdpa(int heads, int d, int64_t tq, int64_t tk, const float* q, const float* k, const float* v, float scale,
+               float* out) {
+#define X(H, D)                                                                                               \
+    if (heads == H && d == D) {                                                                               \
+        const auto Q = Matrix<H * D>::from_row_major(std::vector<Scalar>(q, q + (size_t)tq * H * D));        \
+        const auto K = Matrix<H * D>::from_row_major(std::vector<Scalar>(k, k + (size_t)tk * H * D));        \
+        const auto V = Matrix<H * D>::from_row_major(std::vector<Scalar>(v, v + (size_t)tk * H * D));        \
+        const auto A = scaled_dot_product_attention<H, D, D>(Q.view(), K.view(), V.view(), scale);           \
+        for (int64_t r = 0; r < tq; ++r)                                                                      \
+            for (int i = 0; i < H * D; ++i) out[(size_t)r * H * D + i] = A.row((size_t)r)[i];               \
+        return 0;                                                                                             \
+    }
+    X(12, 64) X(4, 64)
+#undef X
+    return 100;
+}
+
 // sigmoid (core.hpp:579) of each element.
 void nmref_sigmoid_n(int64_t n, const float* x, float* y) {
     for (int64_t i = 0; i < n; ++i) y[i] = sigmoid(x[i]);

@@ -251,3 +251,20 @@ def test_oracle_matches_golden_delta(path):
 
 def test_golden_fixtures_exist():
     assert len(glob.glob(os.path.join(GOLDEN, "*.npz"))) >= 6
+
+
+@pytest.mark.skipif(oracle.ref() is None, reason="reference library not built")
+@pytest.mark.parametrize("heads,tq,tk,scale", [(12, 40, 360, 1.0), (4, 37, 300, 0.125)])
+def test_dense_attention_is_the_reference_sdpa(heads, tq, tk, scale):
+    # scaled_dot_product_attention<Heads, 64, 64> (attention.hpp:124-139), the
+    # vision ViT's call at 12 heads and scale 1 (gemma4_vision.hpp:167): the
+    # oracle's reduction with every key visible (all queries at the newest row).
+    d = 64
+    q = oracle.normal(91, 1, tq * heads * d).reshape(tq, heads * d)
+    k = oracle.normal(91, 2, tk * heads * d).reshape(tk, heads * d)
+    v = oracle.normal(91, 3, tk * heads * d).reshape(tk, heads * d)
+    want = np.empty_like(q)
+    fp = lambda a: a.ctypes.data_as(ctypes.POINTER(ctypes.c_float))
+    assert oracle.ref().nmref_sdpa(heads, d, tq, tk, fp(q), fp(k), fp(v), scale, fp(want)) == 0
+    got = oracle.attend(k, v, 0, 0, heads, d, q, heads, tk - 1, scale=np.float32(scale))
+    np.testing.assert_allclose(got, want, rtol=2e-6, atol=2e-6)
