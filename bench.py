@@ -781,6 +781,27 @@ def extra_attn_io(torch, dev, small=False):
                                   "bytes": bytes_g}}}
 
 
+def extra_vit(torch, dev, small=False):
+    """Dense attention of the vision ViT (scaled_dot_product_attention<12, 64, 64>,
+    scale 1) at its largest image, 2520 patch tokens, bf16 on the tensor cores."""
+    from hero_b200 import nm
+
+    heads, dh, n = 12, 64, 2520
+    g = torch.Generator(device=dev)
+    g.manual_seed(7)
+    q, k, v = (torch.randn(n, heads * dh, device=dev, generator=g).to(torch.bfloat16) for _ in range(3))
+    out = torch.empty(n, heads * dh, device=dev, dtype=torch.bfloat16)
+    ms = graph_time(torch, dev, lambda: nm.scaled_dot_product_attention(q, k, v, heads, 1.0, out=out), 20, 10)
+    flops = 4 * dh * heads * n * n
+    p = peaks()
+    tf = flops / (ms * 1e-3) / 1e12
+    return {"workload": "vision ViT attention: 12 heads, head_dim 64, 2520 tokens, no mask, bf16", "us": ms * 1e3,
+            "value": tf, "unit": "TFLOP/s",
+            "roofline": {"bound": "tensor", "achieved": tf, "peak": p["bf16"], "frac": tf / p["bf16"], "flops": flops},
+            "method": "10 calls captured in a CUDA graph, replayed 20 times; each call stages K/V head-major, then "
+                      "the tensor-core kernel"}
+
+
 def extra_config4(torch, dev, small=False):
     from hero_b200 import nm
 
@@ -887,7 +908,7 @@ def main():
     ap.add_argument("--impl", default="nmg", choices=["nmg", "reference"])
     ap.add_argument("--no-extra", action="store_true", help="headline only")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
-    ap.add_argument("--only", choices=["c1", "c2", "c3", "c4", "c5", "io"],
+    ap.add_argument("--only", choices=["c1", "c2", "c3", "c4", "c5", "io", "vit"],
                     help="run one workload alone (profiling); prints its own JSON line")
     ap.add_argument("--small", action="store_true", help="with --only: profiling-sized variant")
     args = ap.parse_args()
@@ -915,14 +936,14 @@ def main():
     hero_b200.lib()  # fail loudly before any work if the CUDA library is missing
     if args.only and args.only != "c2":
         fn = {"c1": extra_config1, "c3": extra_config3, "c4": extra_config4, "c5": extra_config5,
-              "io": extra_attn_io}[args.only]
+              "io": extra_attn_io, "vit": extra_vit}[args.only]
         print(json.dumps({"only": args.only, "small": args.small, **fn(torch, dev, small=args.small)}), flush=True)
         return
     res = bench_prefill(args, torch, dist, rank, world, dev)
     extra = {}
     if world == 1 and not args.no_extra and not args.only:
         for name, fn in (("config1", extra_config1), ("config3", extra_config3), ("config4", extra_config4),
-                         ("config5", extra_config5), ("attn_io", extra_attn_io)):
+                         ("config5", extra_config5), ("attn_io", extra_attn_io), ("vit", extra_vit)):
             try:
                 extra[name] = fn(torch, dev)
             except Exception as e:  # report, never hide, a failing extra

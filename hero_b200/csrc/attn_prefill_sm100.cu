@@ -48,8 +48,8 @@ namespace {
 template <int DH>
 struct PfCfg {
     static constexpr int BM = 128;
-    static constexpr int BN = DH == 128 ? 128 : 64;
-    static constexpr int KST = DH == 128 ? 3 : 2;  // K stages (K is released as soon as S is computed)
+    static constexpr int BN = DH == 256 ? 64 : 128;
+    static constexpr int KST = DH == 256 ? 2 : 3;  // K stages (K is released as soon as S is computed)
     static constexpr int VST = 2;  // V stages (released after P.V)
     static constexpr int Q_BYTES = BM * DH * 2;
     static constexpr int K_BYTES = BN * DH * 2;
@@ -789,8 +789,8 @@ int make_kv_tensor_maps(const nmg_kv_cache* c, int box_rows, CUtensorMap* k, CUt
 
 bool prefill_supported(const nmg_kv_cache* c, int hq, int q_dtype, int64_t rows) {
     if (c->dtype == NMG_F32 || q_dtype != c->dtype) return false;
-    if (c->dh != 128 && c->dh != 256) return false;
-    const int bn = c->dh == 128 ? 128 : 64;
+    if (c->dh != 64 && c->dh != 128 && c->dh != 256) return false;
+    const int bn = c->dh == 256 ? 64 : 128;
     if (c->slots % bn != 0) return false;
     if (rows < 64) return false;
     if ((int64_t)c->hkv * c->slots > 0x7FFFFFFF) return false;
@@ -825,7 +825,7 @@ int attend_rows_prefill(const nmg_kv_cache* c, int hq, const void* q, int q_dtyp
             return set_error(NMG_CUDA_ERROR, "prefill: Q tensor map (%d)", (int)r);
         }
     }
-    const int bn = dh == 128 ? 128 : 64;
+    const int bn = dh == 256 ? 64 : 128;
     for (int which = 0; which < 2; ++which) {
         cuuint64_t dims[2] = {(cuuint64_t)dh, (cuuint64_t)c->hkv * (cuuint64_t)c->slots};
         cuuint64_t strides[1] = {(cuuint64_t)dh * 2};
@@ -919,7 +919,9 @@ int attend_rows_prefill(const nmg_kv_cache* c, int hq, const void* q, int q_dtyp
         int nsm = 148;
         if (cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, c->device) != cudaSuccess) nsm = 148;
         const dim3 grid((unsigned)std::min<int64_t>(a->n_work, nsm));
-        if (dh == 128)
+        if (dh == 64)
+            st = c->dtype == NMG_BF16 ? launch_prefill<64, true>(*a, grid, stream) : launch_prefill<64, false>(*a, grid, stream);
+        else if (dh == 128)
             st = c->dtype == NMG_BF16 ? launch_prefill<128, true>(*a, grid, stream) : launch_prefill<128, false>(*a, grid, stream);
         else
             st = c->dtype == NMG_BF16 ? launch_prefill<256, true>(*a, grid, stream) : launch_prefill<256, false>(*a, grid, stream);

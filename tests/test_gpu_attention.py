@@ -424,3 +424,30 @@ def test_prefill_head_dim_256_window_many_units(dev):
     for r0, r1 in ((0, 256), (2304, 2560), (S - 256, S)):
         want = oracle.attend(k[:r1], v[:r1], 0, W, hkv, dh, q[r0:r1], hq, r0, use_scale=False)
         assert_close(out[r0:r1], want, what=f"rows {r0}:{r1}")
+
+
+@pytest.mark.parametrize("dtype,window", [("bf16", 0), ("f16", 0), ("bf16", 200)])
+def test_prefill_head_dim_64_matches_oracle(dev, dtype, window):
+    # head_dim 64 through the tensor-core kernel (128-key blocks, P.V with N = 64).
+    hq, hkv, dh, S = 6, 2, 64, 700
+    k, v, q = rnd(dtype, 44, 1, (S, hkv * dh)), rnd(dtype, 44, 2, (S, hkv * dh)), rnd(dtype, 44, 3, (S, hq * dh))
+    if window:
+        cache = nm.LocalAttentionCache(hkv, dh, window, capacity=((S + window + 127) // 128) * 128, dtype=dtype)
+    else:
+        cache = nm.FullAttentionCache(hkv, dh, capacity=768, dtype=dtype)
+    out = nm.append_attend(cache, 0, TD(k, dev, dtype), TD(v, dev, dtype), TD(q, dev, dtype), 0.125,
+                           out_dtype=torch.float32).cpu().numpy()
+    want = oracle.attend(k, v, 0, window, hkv, dh, q, hq, 0, scale=np.float32(0.125))
+    assert_close(out, want, what=f"head_dim 64 {dtype} window {window}")
+
+
+def test_sdpa_vision_shape(dev):
+    # scaled_dot_product_attention<12, 64, 64> with scale 1 (gemma4_vision.hpp:167)
+    # at the ViT's largest image, 2520 patch tokens, in bf16 on the tensor cores.
+    heads, dh, n = 12, 64, 2520
+    q, k, v = (rnd("bf16", 45, i, (n, heads * dh)) for i in (1, 2, 3))
+    q = oracle.round_bf16(q * np.float32(0.125)).reshape(q.shape)  # normed Q/K keep scale-1 scores moderate
+    out = nm.scaled_dot_product_attention(TD(q, dev, "bf16"), TD(k, dev, "bf16"), TD(v, dev, "bf16"), heads, 1.0,
+                                          out_dtype=torch.float32).cpu().numpy()
+    want = oracle.attend(k, v, 0, 0, heads, dh, q, heads, n - 1, scale=np.float32(1.0))
+    assert_close(out, want, what="vision sdpa")
