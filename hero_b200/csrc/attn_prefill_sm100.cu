@@ -703,31 +703,60 @@ __global__ void __launch_bounds__(PfCfg<DH>::THREADS, 1) attn_prefill_kernel(con
                     __threadfence();
                     const float* base = a.part + ((int64_t)w.h * a.nparts + a.part_base[w.tile]) * BM * (DH + 4);
                     const int64_t slot = (int64_t)BM * (DH + 4);
-                    // 4 output columns per work unit
-                    for (int idx = eid; idx < valid_rows * (DH / 4); idx += 128) {
-                        const int rr = idx / (DH / 4), d0 = (idx - rr * (DH / 4)) * 4;
+                    // One thread per row: the row's maximum and sum over the
+                    // splits first, then 16-column chunks in which every
+                    // split's loads are independent of its weight, so each
+                    // split costs about one L2 round trip per chunk.
+                    const int rr = eid;
+                    if (rr < valid_rows) {
+                        const float* rowp = base + rr * (DH + 4);
                         float M = -INFINITY;
-                        for (int sp = 0; sp < w.nsplit; ++sp) M = fmaxf(M, __ldcg(base + sp * slot + rr * (DH + 4) + DH));
-                        float L = 0.f, o4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 4
+                        for (int sp = 0; sp < w.nsplit; ++sp) M = fmaxf(M, __ldcg(rowp + sp * slot + DH));
+                        float L = 0.f;
+#pragma unroll 4
                         for (int sp = 0; sp < w.nsplit; ++sp) {
-                            const float* rp = base + sp * slot + rr * (DH + 4);
-                            const float m = __ldcg(rp + DH);
-                            if (m == -INFINITY) continue;
-                            const float wgt = ex2(m - M);
-                            L = fmaf(wgt, __ldcg(rp + DH + 1), L);
-                            const float4 v = __ldcg((const float4*)(rp + d0));
-                            o4[0] = fmaf(wgt, v.x, o4[0]), o4[1] = fmaf(wgt, v.y, o4[1]);
-                            o4[2] = fmaf(wgt, v.z, o4[2]), o4[3] = fmaf(wgt, v.w, o4[3]);
+                            const float m = __ldcg(rowp + sp * slot + DH);
+                            if (m != -INFINITY) L = fmaf(ex2(m - M), __ldcg(rowp + sp * slot + DH + 1), L);
                         }
                         const float inv = 1.f / L;
-                        const int64_t off = ((w.t0 + rr) * a.out_row_elems + a.out_col0 + (int64_t)w.h * DH + d0) * oes;
-                        if (a.out_dtype == NMG_F32) {
-                            const float4 v = make_float4(o4[0] * inv, o4[1] * inv, o4[2] * inv, o4[3] * inv);
-                            for (int o = 0; o < a.nout; ++o) *(float4*)((unsigned char*)a.outs[o] + off) = v;
-                        } else {
-                            const uint2 v = make_uint2(pack_out(o4[0] * inv, o4[1] * inv, a.out_dtype),
-                                                       pack_out(o4[2] * inv, o4[3] * inv, a.out_dtype));
-                            for (int o = 0; o < a.nout; ++o) *(uint2*)((unsigned char*)a.outs[o] + off) = v;
+                        const int64_t off0 = ((w.t0 + rr) * a.out_row_elems + a.out_col0 + (int64_t)w.h * DH) * oes;
+#pragma unroll 1
+                        for (int c = 0; c < DH / 16; ++c) {
+                            float o[16];
+#pragma unroll
+                            for (int e = 0; e < 16; ++e) o[e] = 0.f;
+#pragma unroll 1
+                            for (int sp = 0; sp < w.nsplit; ++sp) {
+                                const float* rp = rowp + sp * slot;
+                                float4 v[4];
+#pragma unroll
+                                for (int e = 0; e < 4; ++e) v[e] = __ldcg((const float4*)(rp + c * 16) + e);
+                                const float m = __ldcg(rp + DH);
+                                const float wgt = m == -INFINITY ? 0.f : ex2(m - M);
+#pragma unroll
+                                for (int e = 0; e < 4; ++e) {
+                                    o[4 * e] = fmaf(wgt, v[e].x, o[4 * e]), o[4 * e + 1] = fmaf(wgt, v[e].y, o[4 * e + 1]);
+                                    o[4 * e + 2] = fmaf(wgt, v[e].z, o[4 * e + 2]), o[4 * e + 3] = fmaf(wgt, v[e].w, o[4 * e + 3]);
+                                }
+                            }
+                            const int64_t off = off0 + (int64_t)c * 16 * oes;
+                            for (int oi = 0; oi < a.nout; ++oi) {
+                                unsigned char* dst = (unsigned char*)a.outs[oi] + off;
+                                if (a.out_dtype == NMG_F32) {
+#pragma unroll
+                                    for (int e = 0; e < 4; ++e)
+                                        ((float4*)dst)[e] = make_float4(o[4 * e] * inv, o[4 * e + 1] * inv,
+                                                                        o[4 * e + 2] * inv, o[4 * e + 3] * inv);
+                                } else {
+#pragma unroll
+                                    for (int e = 0; e < 2; ++e)
+                                        ((uint4*)dst)[e] = make_uint4(pack_out(o[8 * e] * inv, o[8 * e + 1] * inv, a.out_dtype),
+                                                                      pack_out(o[8 * e + 2] * inv, o[8 * e + 3] * inv, a.out_dtype),
+                                                                      pack_out(o[8 * e + 4] * inv, o[8 * e + 5] * inv, a.out_dtype),
+                                                                      pack_out(o[8 * e + 6] * inv, o[8 * e + 7] * inv, a.out_dtype));
+                                }
+                            }
                         }
                     }
                 }
