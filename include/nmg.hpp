@@ -227,6 +227,19 @@ void attention_prologue(Cache& cache, size_t position, size_t tokens, const floa
                             q_gamma, k_gamma, v_norm ? 1 : 0, eps, double(Base), int(RotaryNum), int(RotaryDen), q_out,
                             int(q_dtype), stream));
 }
+// The same preparation without a cache: K (and V when v_norm) to fp32 rows
+// [tokens][Hkv * HeadDim], for append_attend (a Gemma sliding-window layer
+// whose batch would evict, gemma4.hpp:617-630).
+template <size_t Hq, size_t Hkv, size_t HeadDim, size_t Base, size_t RotaryNum = 1, size_t RotaryDen = 1>
+void attention_prepare(size_t position, size_t tokens, const float* q, bool gated, const float* k, const float* v,
+                       const float* q_gamma, const float* k_gamma, bool v_norm, float eps, void* q_out, Dtype q_dtype,
+                       float* k_out, float* v_out, void* stream) {
+    static_assert(Hq % Hkv == 0, "query heads must be a whole number of GQA groups");
+    static_assert(RotaryDen != 0 && RotaryNum <= RotaryDen, "the rotary fraction is at most one");
+    check(nmg_attn_prepare(int(Hq), int(Hkv), int(HeadDim), int64_t(position), int64_t(tokens), q, gated ? 1 : 0, k, v,
+                           q_gamma, k_gamma, v_norm ? 1 : 0, eps, double(Base), int(RotaryNum), int(RotaryDen), q_out,
+                           int(q_dtype), k_out, v_out, stream));
+}
 // After it: attended *= sigmoid(gate), the gates the second halves of the
 // [q | gate] pairs (qwen35.hpp:390-393).
 template <size_t Hq, size_t HeadDim>

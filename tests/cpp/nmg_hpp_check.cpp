@@ -12,6 +12,7 @@
 [[maybe_unused]] static auto* const attn_prologue_fn =
     &nmg::attention_prologue<16, 10000000, 1, 4, nmg::FullAttentionCache<4, 256>>;
 [[maybe_unused]] static auto* const attn_gate_fn = &nmg::attention_gate<16, 256>;
+[[maybe_unused]] static auto* const attn_prepare_fn = &nmg::attention_prepare<8, 4, 256, 10000>;
 [[maybe_unused]] static void (nmg::CausalConv1dState<8192, 4>::*const conv_step_fn)(const float*, const float*, size_t,
                                                                                     float*, bool, void*) =
     &nmg::CausalConv1dState<8192, 4>::step;
