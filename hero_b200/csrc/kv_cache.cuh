@@ -13,9 +13,11 @@
 // visible_rows() never touch the device.
 struct nmg_kv_cache {
     int hkv = 0, dh = 0, dtype = NMG_F32, device = 0;
-    // Element type of the V buffer.  A bf16 cache keeps V as fp16: each bf16
-    // value within +-65504 is exactly representable in fp16, and fp16 V lets
-    // P.V run fp16 x fp16 with 11-bit probabilities (bf16 P would carry 8).
+    // Element type of the V buffer.  A bf16 cache keeps V as fp16: a bf16
+    // value in fp16's normal range (magnitude 2^-14 .. 65504) is exactly
+    // representable in fp16 (smaller ones round to its subnormal grid, error
+    // <= 2^-25), and fp16 V lets P.V run fp16 x fp16 with 11-bit probabilities
+    // (bf16 P would carry 8).
     int vdtype = NMG_F32;
     int64_t window = 0;  // 0: full (append-only) cache
     int64_t slots = 0;   // physical rows per head
