@@ -898,6 +898,395 @@ def extra_config5(torch, dev, small=False):
             "roofline": {"bound": "hbm", "achieved": gbs, "peak": p["hbm"], "frac": gbs / p["hbm"]}}
 
 
+# ---------------------------------------------------------------- extras (N>1)
+
+class Ranks:
+    """The ranks of a multi-GPU extra: barriers, max-over-ranks timing, and
+    the all-gather of equal per-rank blocks followed by the head-to-row
+    permutation (both through the C ABI, on the current stream)."""
+
+    def __init__(self, torch, dist, dev, rank, world):
+        self.torch, self.dist, self.dev, self.rank, self.world = torch, dist, dev, rank, world
+        self.comm = Comm(rank, world, dev.index, torch, dist)
+
+    def cur(self):
+        return ctypes.c_void_p(self.torch.cuda.current_stream(self.dev).cuda_stream)
+
+    def barrier(self):
+        self.dist.barrier()
+        self.torch.cuda.synchronize(self.dev)
+
+    def max_over(self, *vals):
+        t = self.torch.tensor(vals, device=self.dev, dtype=self.torch.float64)
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+        return [float(x) for x in t.tolist()]
+
+    def all_ok(self, ok):
+        """True on every rank when every rank reports ok (one collective that
+        every rank reaches, failed or not, so the ranks stay in step)."""
+        t = self.torch.tensor([0 if ok else 1], device=self.dev, dtype=self.torch.int32)
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+        return int(t.item()) == 0
+
+    def gather(self, send, gathered):
+        self.comm.allgather(send, gathered, self.cur())
+
+    def to_rows(self, gathered, out, world, rows, row_bytes):
+        from hero_b200 import _lib
+
+        _lib.call("nmg_gather_heads_to_rows", ctypes.c_void_p(gathered.data_ptr()), ctypes.c_void_p(out.data_ptr()),
+                  world, rows, row_bytes, self.cur())
+
+    def graph_ms(self, fn, reps, inner):
+        """Max over ranks of the average ms of fn() when `inner` calls are
+        captured in one CUDA graph and replayed `reps` times, every rank
+        starting together after a barrier."""
+        torch, dev = self.torch, self.dev
+        fn()
+        self.barrier()
+        g = torch.cuda.CUDAGraph()
+        s = torch.cuda.Stream(dev)
+        s.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(s):
+            with torch.cuda.graph(g, stream=s):
+                for _ in range(inner):
+                    fn()
+        torch.cuda.current_stream(dev).wait_stream(s)
+        self.barrier()
+        g.replay()
+        self.barrier()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(reps):
+            g.replay()
+        b.record()
+        self.barrier()
+        ms = a.elapsed_time(b) / (reps * inner)
+        del g
+        return self.max_over(ms)[0]
+
+    def event_ms(self, fn, reps):
+        """Max over ranks of the average ms of `reps` eager calls of fn()."""
+        torch = self.torch
+        fn()
+        self.barrier()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(reps):
+            fn()
+        b.record()
+        self.barrier()
+        return self.max_over(a.elapsed_time(b) / reps)[0]
+
+    def close(self):
+        self.torch.cuda.synchronize(self.dev)
+        self.dist.barrier()
+        self.comm.close()
+
+
+def sharded_config1(rk):
+    """Config 1 split by KV head: each rank reduces its heads of the query
+    over its share of the fp32 cache, then the head outputs are all-gathered
+    and laid into the [1][16*128] row."""
+    from hero_b200 import nm
+    from hero_b200.shard import kv_shard
+
+    torch, dev, world = rk.torch, rk.dev, rk.world
+    hq, hkv, dh, rows = 16, 8, 128, 1024
+    sh = kv_shard(rk.rank, world, hkv, hq)
+    hkv_l, hq_l = sh.kv1 - sh.kv0, sh.q1 - sh.q0
+    NC = 20 * world  # rotated caches: NC * 8.4 MB / world per GPU > L2
+    caches, qs, outs = [], [], []
+    for _ in range(NC):
+        c = nm.FullAttentionCache(hkv_l, dh, capacity=rows, device=dev.index)
+        c.append(0, torch.randn(rows, hkv_l * dh, device=dev), torch.randn(rows, hkv_l * dh, device=dev))
+        caches.append(c)
+        qs.append(torch.randn(1, hq_l * dh, device=dev))
+        outs.append(torch.empty(1, hq_l * dh, device=dev))
+    gathered = torch.empty(world, 1, hq_l * dh, device=dev)
+    full = torch.empty(1, hq * dh, device=dev)
+    scale = 1 / math.sqrt(dh)
+
+    def local():
+        for i in range(NC):
+            nm.attend(caches[i], qs[i], rows - 1, scale, out=outs[i])
+
+    def whole():
+        for i in range(NC):
+            nm.attend(caches[i], qs[i], rows - 1, scale, out=outs[i])
+            rk.gather(outs[i], gathered)
+            rk.to_rows(gathered, full, world, 1, hq_l * dh * 4)
+
+    ms_local = rk.graph_ms(local, 20, 5) / NC
+    ms = rk.graph_ms(whole, 20, 5) / NC
+    bytes_ = 2 * rows * hkv * dh * 4 + 2 * hq * dh * 4
+    p = peaks()
+    gbs = bytes_ / (ms * 1e-3) / 1e9
+    gbs_local = bytes_ / world / (ms_local * 1e-3) / 1e9
+    return {"workload": "config 1: decode, fp32, 16q/8kv, d128, 1024 cached", "parallelism": f"kv-head shards x{world}",
+            "value": gbs, "unit": "GB/s", "us_per_call": ms * 1e3, "tok_per_s": 1 / (ms * 1e-3),
+            "attention_only_us": ms_local * 1e3,
+            "roofline": {"bound": "hbm", "achieved": gbs_local, "peak": p["hbm"], "frac": gbs_local / p["hbm"],
+                         "per": "GPU, attention kernel alone"},
+            "method": f"{NC} caches rotated in a CUDA graph; each call = attention + ncclAllGather of the head "
+                      "outputs + head-to-row permutation; time = max over ranks"}
+
+
+def sharded_config3(rk):
+    """Config 3 split by key-head group: a rank owns key heads [k0, k1) and the
+    value heads that read them (h % 16), so prefill and decode run with no
+    exchange; the head outputs are all-gathered into [T][32*128] rows."""
+    from hero_b200 import nm
+    from hero_b200.shard import delta_shard
+
+    torch, dev, world = rk.torch, rk.dev, rk.world
+    hv, hk, d, T, Tdec = 32, 16, 128, 8192, 256
+    sd = delta_shard(rk.rank, world, hk, hv)
+    hs = torch.tensor(sd.v_heads, device=dev)
+    R = hv // hk
+    g = torch.Generator(device=dev)
+    g.manual_seed(3)  # the single-GPU inputs; each rank keeps its heads
+    norm = lambda x: x / x.norm(dim=-1, keepdim=True).clamp_min(1e-6)
+    q = (norm(torch.randn(T, hk, d, device=dev, generator=g)) / math.sqrt(d))[:, sd.k0:sd.k1].contiguous()
+    k = norm(torch.randn(T, hk, d, device=dev, generator=g))[:, sd.k0:sd.k1].contiguous()
+    v = torch.randn(T, hv, d, device=dev, generator=g).index_select(1, hs).contiguous()
+    gate = (-torch.nn.functional.softplus(torch.randn(T, hv, device=dev, generator=g))).index_select(1, hs).contiguous()
+    beta = torch.sigmoid(torch.randn(T, hv, device=dev, generator=g)).index_select(1, hs).contiguous()
+    st = nm.DeltaNetState(sd.hv, d, d, device=dev.index)
+    out = torch.empty(T, sd.hv, d, device=dev)
+    gathered = torch.empty(world, T, sd.hv * d, device=dev)
+    full = torch.empty(T, hv * d, device=dev)
+
+    def prefill_local():
+        st.clear()
+        nm.delta_prefill(st, q, k, v, gate, beta, sd.hk, chunk=64, out=out)
+
+    def prefill():
+        prefill_local()
+        rk.gather(out, gathered)
+        rk.to_rows(gathered, full, world, T * R, sd.hk * d * 4)
+
+    ms_pl = rk.event_ms(prefill_local, 3)
+    ms_p = rk.event_ms(prefill, 3)
+    C = 64
+    alg = (5 * 2 * C * C * d + 3 * 2 * C * d * d + 2 * C ** 3 / 3) * hv * (T // C)
+    p = peaks()
+    tf32_peak = p["bf16"] / 2
+    tf_local = alg / world / (ms_pl * 1e-3) / 1e12
+    res = {"prefill_chunk64": {"ms": ms_p, "tok_per_s": T / (ms_p * 1e-3), "tflops_chunked_alg": alg / (ms_p * 1e-3) / 1e12,
+                               "recurrence_only_ms": ms_pl,
+                               "roofline": {"bound": "tensor", "achieved": tf_local, "peak": tf32_peak, "unit": "TFLOP/s",
+                                            "frac": tf_local / tf32_peak, "per": "GPU, recurrence alone",
+                                            "note": "tf32 peak taken as half the measured bf16 peak"}}}
+    del q, k, v, gate, beta, gathered, full
+    qd = (norm(torch.randn(Tdec, hk, d, device=dev, generator=g)) / math.sqrt(d))[:, sd.k0:sd.k1].contiguous()
+    kd = norm(torch.randn(Tdec, hk, d, device=dev, generator=g))[:, sd.k0:sd.k1].contiguous()
+    vd = torch.randn(Tdec, hv, d, device=dev, generator=g).index_select(1, hs).contiguous()
+    gd = (-torch.nn.functional.softplus(torch.randn(Tdec, hv, device=dev, generator=g))).index_select(1, hs).contiguous()
+    bd = torch.sigmoid(torch.randn(Tdec, hv, device=dev, generator=g)).index_select(1, hs).contiguous()
+    od = torch.empty(Tdec, sd.hv, d, device=dev)
+    gdec = torch.empty(world, sd.hv * d, device=dev)
+    fdec = torch.empty(Tdec, hv * d, device=dev)
+
+    def steps_local():
+        for t in range(Tdec):
+            nm.delta_step(st, qd[t], kd[t], vd[t], gd[t], bd[t], sd.hk, out=od[t])
+
+    def steps():
+        for t in range(Tdec):
+            nm.delta_step(st, qd[t], kd[t], vd[t], gd[t], bd[t], sd.hk, out=od[t])
+            rk.gather(od[t], gdec)
+            rk.to_rows(gdec, fdec[t], world, R, sd.hk * d * 4)
+
+    ms_sl = rk.graph_ms(steps_local, 5, 1) / Tdec
+    ms_s = rk.graph_ms(steps, 5, 1) / Tdec
+    bytes_ = 2 * hv * d * d * 4 + 2 * hk * d * 4 + 2 * hv * d * 4 + 2 * hv * 4
+    gbs_local = bytes_ / world / (ms_sl * 1e-3) / 1e9
+    res["decode"] = {"us_per_step": ms_s * 1e3, "value": bytes_ / (ms_s * 1e-3) / 1e9, "unit": "GB/s",
+                     "tok_per_s": 1 / (ms_s * 1e-3), "recurrence_only_us_per_step": ms_sl * 1e3,
+                     "roofline": {"bound": "hbm", "achieved": gbs_local, "peak": p["hbm"], "frac": gbs_local / p["hbm"],
+                                  "per": "GPU, recurrent update alone", "note": "state is L2-resident between steps"}}
+    return {"workload": "config 3: gated delta rule, 16 k / 32 v heads, d128, T 8192 prefill + 256 decode steps",
+            "parallelism": f"key-head groups x{world} (value head h with key head h % 16), outputs all-gathered",
+            "method": "prefill: 3 eager calls with CUDA events; decode: 256 steps in one CUDA graph, each step "
+                      "= recurrent update + ncclAllGather + head-to-row permutation; time = max over ranks", **res}
+
+
+def sharded_config4(rk):
+    """Config 4 across ranks: prefill by KV head (with more ranks than KV heads,
+    the two ranks of a KV head split its query heads); decode by KV head and,
+    past four ranks, by batch half.  Head outputs are all-gathered into rows."""
+    from hero_b200 import nm
+    from hero_b200.shard import decode_shard, kv_shard
+
+    torch, dev, world = rk.torch, rk.dev, rk.world
+    hq, hkv, dh, W, S = 8, 4, 256, 1024, 8192
+    sp = kv_shard(rk.rank, world, hkv, hq)
+    hkv_l, hq_l = sp.kv1 - sp.kv0, sp.q1 - sp.q0
+    g = torch.Generator(device=dev)
+    g.manual_seed(4)
+    rms = lambda x: x / x.float().pow(2).mean(dim=-1, keepdim=True).add(1e-6).sqrt()
+    q = rms(torch.randn(S, hq, dh, device=dev, generator=g))[:, sp.q0:sp.q1].reshape(S, hq_l * dh).to(torch.bfloat16)
+    k = rms(torch.randn(S, hkv, dh, device=dev, generator=g))[:, sp.kv0:sp.kv1].reshape(S, hkv_l * dh).to(torch.bfloat16)
+    v = torch.randn(S, hkv, dh, device=dev, generator=g)[:, sp.kv0:sp.kv1].reshape(S, hkv_l * dh).to(torch.bfloat16)
+    o = torch.empty(S, hq_l * dh, device=dev, dtype=torch.bfloat16)
+    gathered = torch.empty(world, S, hq_l * dh, device=dev, dtype=torch.bfloat16)
+    full = torch.empty(S, hq * dh, device=dev, dtype=torch.bfloat16)
+    local = [nm.LocalAttentionCache(hkv_l, dh, W, capacity=S + W, dtype="bf16", device=dev.index) for _ in range(5)]
+    glob = nm.FullAttentionCache(hkv_l, dh, capacity=S, dtype="bf16", device=dev.index)
+
+    def layer(c, gather):
+        c.reset()
+        nm.append_attend(c, 0, k, v, q, None, out=o)
+        if gather:
+            rk.gather(o, gathered)
+            rk.to_rows(gathered, full, world, S, hq_l * dh * 2)
+
+    ms_l = rk.event_ms(lambda: [layer(c, False) for c in local + [glob]], 3)
+    ms = rk.event_ms(lambda: [layer(c, True) for c in local + [glob]], 3)
+    pairs_g = S * (S + 1) // 2
+    pairs_l = W * (W + 1) // 2 + (S - W) * W
+    flops = 4.0 * dh * hq * (pairs_g + 5 * pairs_l)
+    p = peaks()
+    tf = flops / (ms * 1e-3) / 1e12
+    tf_local = flops / world / (ms_l * 1e-3) / 1e12
+    res = {"prefill": {"ms_per_group": ms, "value": tf, "unit": "TFLOP/s", "tok_per_s": S / (ms * 1e-3),
+                       "attention_only_ms_per_group": ms_l,
+                       "parallelism": (f"kv-head shards x{world}" if world <= hkv else
+                                       f"kv-head shards x{hkv}, query heads of each group split x{world // hkv}"),
+                       "roofline": {"bound": "tensor", "achieved": tf_local, "peak": p["bf16"],
+                                    "frac": tf_local / p["bf16"], "per": "GPU, attention alone"}}}
+    del local, glob, q, k, v, o, gathered, full
+    B, L = 16, 32768
+    ds = decode_shard(rk.rank, world, hkv, hq, B)
+    sh = ds.heads
+    hkv_d, hq_d, Bl = sh.kv1 - sh.kv0, sh.q1 - sh.q0, ds.b1 - ds.b0
+    gcaches, lcaches = [], []
+    for b_ in range(B):
+        kk = torch.randn(L, hkv, dh, device=dev, generator=g)
+        vv = torch.randn(L, hkv, dh, device=dev, generator=g)
+        if not ds.b0 <= b_ < ds.b1:  # every rank draws every sequence, keeps its own
+            del kk, vv
+            continue
+        kk = kk[:, sh.kv0:sh.kv1].reshape(L, hkv_d * dh).to(torch.bfloat16)
+        vv = vv[:, sh.kv0:sh.kv1].reshape(L, hkv_d * dh).to(torch.bfloat16)
+        c = nm.FullAttentionCache(hkv_d, dh, capacity=L, dtype="bf16", device=dev.index)
+        c.append(0, kk, vv)
+        gcaches.append(c)
+        lc = nm.LocalAttentionCache(hkv_d, dh, W, capacity=2 * W, dtype="bf16", device=dev.index)
+        lc.append(L - W, kk[L - W:], vv[L - W:])
+        lcaches.append(lc)
+        del kk, vv
+    qd = torch.randn(B, hq, dh, device=dev, generator=g)[ds.b0:ds.b1, sh.q0:sh.q1].reshape(Bl, hq_d * dh)
+    qd = qd.to(torch.bfloat16).contiguous()
+    od = torch.empty(Bl, hq_d * dh, device=dev, dtype=torch.float32)
+    gd = torch.empty(world, Bl, hq_d * dh, device=dev, dtype=torch.float32)
+    fd = torch.empty(B, hq * dh, device=dev, dtype=torch.float32)
+
+    def decode(caches, gather):
+        nm.attend_batch(caches, qd, None, out=od)
+        if gather:
+            rk.gather(od, gd)
+            for part in range(ds.parts):
+                rk.to_rows(gd[part * ds.kv_world:(part + 1) * ds.kv_world], fd[part * Bl:(part + 1) * Bl],
+                           ds.kv_world, Bl, hq_d * dh * 4)
+
+    ms_g_l = rk.graph_ms(lambda: decode(gcaches, False), 10, 2)
+    ms_g = rk.graph_ms(lambda: decode(gcaches, True), 10, 2)
+    ms_w = rk.graph_ms(lambda: decode(lcaches, True), 10, 20)
+    bytes_g = B * L * hkv * dh * 2 * 2
+    bytes_l = B * W * hkv * dh * 2 * 2
+    grp_ms = ms_g + 5 * ms_w
+    gbs_local = bytes_g / world / (ms_g_l * 1e-3) / 1e9
+    res["decode"] = {"global_us": ms_g * 1e3, "local_us": ms_w * 1e3, "global_attention_only_us": ms_g_l * 1e3,
+                     "global_GBps": bytes_g / (ms_g * 1e-3) / 1e9, "local_GBps": bytes_l / (ms_w * 1e-3) / 1e9,
+                     "group_tok_per_s": B / (grp_ms * 1e-3), "value": (bytes_g + 5 * bytes_l) / (grp_ms * 1e-3) / 1e9,
+                     "unit": "GB/s",
+                     "parallelism": f"kv-head shards x{ds.kv_world}" + (f", batch parts x{ds.parts}" if ds.parts > 1
+                                                                       else ""),
+                     "roofline": {"bound": "hbm", "achieved": gbs_local, "peak": p["hbm"], "frac": gbs_local / p["hbm"],
+                                  "per": "GPU, global layer attention alone"}}
+    return {"workload": "config 4: Gemma hybrid bf16, 8q/4kv, d256, scale 1, 5 local (W=1024) : 1 global",
+            "method": "prefill: 3 eager groups with CUDA events; decode: CUDA graphs; each layer's head outputs "
+                      "all-gathered (NCCL) and permuted into rows; time = max over ranks", **res}
+
+
+def sharded_config5(rk):
+    """Config 5 split by KV head, as the configuration names it: each rank holds
+    its KV heads of all 64 ragged f16 caches; the [64][64*128] output is
+    all-gathered over NVLink."""
+    from hero_b200 import nm
+    from hero_b200.shard import decode_shard
+
+    torch, dev, world = rk.torch, rk.dev, rk.world
+    B, hq, hkv, dh = 64, 64, 8, 128
+    lens = ragged_lengths(1, B, 4096, 131072)
+    ds = decode_shard(rk.rank, world, hkv, hq, B)
+    sh = ds.heads
+    hkv_l, hq_l, Bl = sh.kv1 - sh.kv0, sh.q1 - sh.q0, ds.b1 - ds.b0
+    g = torch.Generator(device=dev)
+    g.manual_seed(5 + rk.rank)
+    caches = []
+    for L in lens[ds.b0:ds.b1]:
+        c = nm.FullAttentionCache(hkv_l, dh, capacity=L, dtype="f16", device=dev.index)
+        chunk = 32768
+        for s0 in range(0, L, chunk):
+            n = min(chunk, L - s0)
+            c.append(s0, torch.randn(n, hkv_l * dh, device=dev, generator=g).half(),
+                     torch.randn(n, hkv_l * dh, device=dev, generator=g).half())
+        caches.append(c)
+    q = torch.randn(Bl, hq_l * dh, device=dev, generator=g).half()
+    out = torch.empty(Bl, hq_l * dh, device=dev, dtype=torch.float32)
+    gathered = torch.empty(world, Bl, hq_l * dh, device=dev, dtype=torch.float32)
+    full = torch.empty(B, hq * dh, device=dev, dtype=torch.float32)
+    scale = 1 / math.sqrt(dh)
+
+    def step(gather):
+        nm.attend_batch(caches, q, scale, out=out)
+        if gather:
+            rk.gather(out, gathered)
+            for part in range(ds.parts):
+                rk.to_rows(gathered[part * ds.kv_world:(part + 1) * ds.kv_world], full[part * Bl:(part + 1) * Bl],
+                           ds.kv_world, Bl, hq_l * dh * 4)
+
+    ms_l = rk.graph_ms(lambda: step(False), 5, 1)
+    ms = rk.graph_ms(lambda: step(True), 5, 1)
+    bytes_ = 4096 * sum(lens) + 2 * B * hq * dh * 2
+    gbs = bytes_ / (ms * 1e-3) / 1e9
+    gbs_local = bytes_ / world / (ms_l * 1e-3) / 1e9
+    p = peaks()
+    return {"workload": "config 5: batch 64 ragged (U[4096,131072], seed 1) decode, 64q/8kv, d128, f16 cache",
+            "parallelism": f"kv-head shards x{ds.kv_world}" + (f", batch parts x{ds.parts}" if ds.parts > 1 else ""),
+            "value": gbs, "unit": "GB/s", "ms_per_call": ms, "tok_per_s": B / (ms * 1e-3),
+            "attention_only_ms": ms_l, "kv_bytes": 4096 * sum(lens),
+            "roofline": {"bound": "hbm", "achieved": gbs_local, "peak": p["hbm"], "frac": gbs_local / p["hbm"],
+                         "per": "GPU, attention kernel alone"},
+            "method": "one call per CUDA graph replay: attention + ncclAllGather of the [64][64*128] fp32 output "
+                      "+ head-to-row permutation; time = max over ranks"}
+
+
+def sharded_extras(torch, dist, dev, rank, world):
+    """The other configurations on `world` GPUs.  Every rank runs the same
+    steps; a failure on any rank is agreed on (one collective that every rank
+    reaches) and reported as that extra's error, so the ranks stay in step."""
+    extra = {}
+    rk = Ranks(torch, dist, dev, rank, world)
+    for name, fn in (("config1", sharded_config1), ("config3", sharded_config3), ("config4", sharded_config4),
+                     ("config5", sharded_config5)):
+        err = None
+        try:
+            res = fn(rk)
+        except Exception as e:  # report, never hide, a failing extra
+            res, err = None, f"{type(e).__name__}: {str(e)[:200]}"
+        if not rk.all_ok(err is None):
+            res = {"error": err or "failed on another rank"}
+        extra[name] = res
+        torch.cuda.synchronize(dev)
+        torch.cuda.empty_cache()
+    rk.close()
+    return extra
+
+
 # ---------------------------------------------------------------- main
 
 def main():
@@ -949,6 +1338,9 @@ def main():
             except Exception as e:  # report, never hide, a failing extra
                 extra[name] = {"error": f"{type(e).__name__}: {str(e)[:200]}"}
             torch.cuda.empty_cache()
+    if world > 1 and not args.no_extra:
+        torch.cuda.empty_cache()
+        extra = sharded_extras(torch, dist, dev, rank, world)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         ref = RefSample(full=True)
