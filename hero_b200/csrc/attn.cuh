@@ -56,6 +56,9 @@ __device__ __forceinline__ void load_row_chunk(const typename dev::Elem<DT>::T* 
     } else if constexpr (DT == NMG_F32 && PER == 8) {
         unpack16<DT>(*(const uint4*)(row + lane * PER), out);
         unpack16<DT>(*(const uint4*)(row + lane * PER + 4), out + 4);
+    } else if constexpr (DT != NMG_F32 && PER == 16) {
+        unpack16<DT>(*(const uint4*)(row + lane * PER), out);
+        unpack16<DT>(*(const uint4*)(row + lane * PER + 8), out + 8);
     } else if constexpr (DT != NMG_F32 && PER == 4) {
         const uint2 raw = *(const uint2*)(row + lane * PER);
         float tmp[8];

@@ -398,12 +398,14 @@ int dispatch_split(int kvdt, int dh, int gt, const SplitArgs& a, dim3 grid, cuda
             case 64: return dispatch_g<NMG_F16, 64>(gt, a, grid, s);
             case 128: return dispatch_g<NMG_F16, 128>(gt, a, grid, s);
             case 256: return dispatch_g<NMG_F16, 256>(gt, a, grid, s);
+            case 512: return dispatch_g<NMG_F16, 512>(gt, a, grid, s);
         }
     } else {
         switch (dh) {
             case 64: return dispatch_g<NMG_BF16, 64>(gt, a, grid, s);
             case 128: return dispatch_g<NMG_BF16, 128>(gt, a, grid, s);
             case 256: return dispatch_g<NMG_BF16, 256>(gt, a, grid, s);
+            case 512: return dispatch_g<NMG_BF16, 512>(gt, a, grid, s);
         }
     }
     return set_error(NMG_UNSUPPORTED, "attention: head_dim %d with cache dtype %d is not built", dh, kvdt);
