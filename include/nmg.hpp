@@ -5,17 +5,24 @@
 //   LocalAttentionCache<Hkv, HeadDim>      (nm/src/attention.hpp:252-395)
 //   the per-layer softmax reduction         (nm/src/qwen35.hpp:360-382, nm/src/gemma4.hpp:211-235, ...)
 //   DeltaNetState<Heads, Dk, Dv>, gated_delta_step (nm/src/recurrent.hpp:117-177)
+//   scaled_dot_product_attention<Heads, Dqk, Dv>  (nm/src/attention.hpp:123-139)
+//   Qwen35State<C>, Gemma4_12BCache / Gemma4E4BCache (nm/src/qwen35.hpp:206-241,
+//                                                     nm/src/gemma4.hpp:343-378, :734-762)
 // for the types below, which keep the method names and throw the same
 // exception types; storage and arithmetic live on the GPU behind include/nmg.h.
+// The per-layer state owners need C++20 (the reference engine's language level).
 // Rows are device pointers in the reference's token-major layout
 // [rows][heads * head_dim]; every call takes the CUDA stream it runs on.
 #pragma once
 
+#include <array>
 #include <cstddef>
 #include <cstdint>
 #include <stdexcept>
 #include <string>
 #include <utility>
+#include <variant>
+#include <vector>
 
 #include "nmg.h"
 
@@ -247,6 +254,41 @@ void attention_gate(size_t tokens, const float* query_gate, void* attended, Dtyp
     check(nmg_attn_gate(int64_t(tokens), int(Hq), int(HeadDim), query_gate, attended, int(dtype), stream));
 }
 
+// One decode query per cache -- the reference keeps one cache per sequence,
+// so a batch is a list of caches of one shape.  queries [batch][Hq * HeadDim];
+// queries_at[b] is query b's position (nullptr: each cache's newest row);
+// score_scale nullptr is the Gemma form.
+template <size_t Hq, class Cache>
+void attend_batch(const Cache* const* caches, size_t batch, const size_t* queries_at, const void* queries,
+                  Dtype q_dtype, const float* score_scale, void* out, Dtype out_dtype, void* stream) {
+    static_assert(Hq % Cache::kv_heads == 0, "query heads must be a whole number of GQA groups");
+    std::vector<const nmg_kv_cache*> handles(batch);
+    std::vector<int64_t> at(queries_at ? batch : 0);
+    for (size_t b = 0; b < batch; ++b) {
+        handles[b] = caches[b]->handle();
+        if (queries_at) at[b] = int64_t(queries_at[b]);
+    }
+    check(nmg_attend_batch(handles.data(), int(batch), queries_at ? at.data() : nullptr, int(Hq), queries,
+                           int(q_dtype), score_scale ? *score_scale : 1.f, score_scale ? 1 : 0, out, int(out_dtype),
+                           stream));
+}
+
+// softmax_rows(scale * Q K^T) V per head with no mask (the vision tower's
+// attention): queries [tq][Heads * Dqk], keys / values [tk][Heads * Dqk], all
+// in `dtype`; out [tq][Heads * Dv].  The K/V row mismatch the reference
+// checks cannot arise here (one tk for both); tk == 0 is invalid_argument.
+template <size_t Heads, size_t QueryKeyDim, size_t ValueDim>
+void scaled_dot_product_attention(const void* queries, const void* keys, const void* values, Dtype dtype, size_t tq,
+                                  size_t tk, float scale, void* out, Dtype out_dtype, void* stream) {
+    static_assert(QueryKeyDim == ValueDim, "the device kernel takes equal query/key and value widths");
+    check(nmg_sdpa(int(Heads), int(QueryKeyDim), queries, keys, values, int(dtype), int64_t(tq), int64_t(tk), scale,
+                   out, int(out_dtype), stream));
+}
+
+// Waits for `stream` and throws std::runtime_error if a kernel since the last
+// call gave up a bounded device-side wait.
+inline void device_status(int device, void* stream) { check(nmg_device_status(device, stream)); }
+
 // gated_delta_step<Dk, Dv> (recurrent.hpp:146-177) on one device head block;
 // gate and beta are device scalars.
 template <size_t Dk, size_t Dv>
@@ -254,5 +296,149 @@ void gated_delta_step(float* state, const float* q, const float* k, const float*
                       const float* beta, float* out, void* stream) {
     check(nmg_gated_delta_step(state, int(Dk), int(Dv), q, k, v, gate, beta, out, stream));
 }
+
+#if __cplusplus >= 202002L
+// ---- per-layer state owners ---------------------------------------------------
+//
+// The reference's prefix states hold every layer's carried state in one
+// object whose token count the model advances.  Here each entry is device
+// memory allocated once, at construction: attention caches get `capacity`
+// rows (the reference's full caches grow without bound up to C::CTX; a device
+// cache is sized up front), local caches `local_capacity` physical rows
+// (>= the window; one batch of up to local_capacity - window + 1 rows is
+// attended as a whole).  clear() forgets everything derived, in place, where
+// the reference's PrefixCache::clear (transformer.hpp:157-163) assigns a
+// fresh state; the device memory is kept.
+
+// Qwen35State<C> (qwen35.hpp:206-241) for a Qwen 3.5 config type C (the
+// reference's Qwen35_4BConfig, ...): attention layers own a
+// FullAttentionCache<Hkv, HEAD_DIM>, recurrent layers (C::is_recurrent) a
+// causal-conv history over the packed [q | k | v] channels and a DeltaNetState.
+template <class C>
+class Qwen35State {
+public:
+    static constexpr size_t conv_channels = 2 * C::KEY_HEADS * C::KEY_HEAD_DIM + C::VALUE_HEADS * C::VALUE_HEAD_DIM;
+    using AttentionEntry = FullAttentionCache<C::Hkv, C::HEAD_DIM>;
+    struct RecurrentEntry {
+        CausalConv1dState<conv_channels, C::CONV_WIDTH> conv;
+        DeltaNetState<C::VALUE_HEADS, C::KEY_HEAD_DIM, C::VALUE_HEAD_DIM> delta;
+        explicit RecurrentEntry(int device) : conv(device), delta(device) {}
+    };
+
+    explicit Qwen35State(size_t capacity = C::CTX, Dtype kv_dtype = Dtype::bf16, int device = 0) {
+        for (size_t layer = 0; layer < C::L; ++layer) {
+            if (C::is_recurrent(layer))
+                entries_[layer].template emplace<RecurrentEntry>(device);
+            else
+                entries_[layer].template emplace<AttentionEntry>(capacity, kv_dtype, device);
+        }
+    }
+    Qwen35State(const Qwen35State&) = delete;
+    Qwen35State& operator=(const Qwen35State&) = delete;
+
+    size_t tokens() const { return tokens_; }
+    void advance(size_t count) {
+        if (count > C::CTX - tokens_) throw std::length_error("Qwen35State: context exhausted");
+        tokens_ += count;
+    }
+    // std::bad_variant_access for a layer of the other kind, as in the reference.
+    AttentionEntry& attention(size_t layer) { return std::get<AttentionEntry>(entries_.at(layer)); }
+    RecurrentEntry& recurrent(size_t layer) { return std::get<RecurrentEntry>(entries_.at(layer)); }
+
+    void clear(void* stream) {
+        for (auto& e : entries_) {
+            if (auto* a = std::get_if<AttentionEntry>(&e)) a->reset();
+            if (auto* r = std::get_if<RecurrentEntry>(&e)) {
+                r->conv.clear(stream);
+                r->delta.clear(stream);
+            }
+        }
+        tokens_ = 0;
+    }
+
+    static constexpr size_t recurrent_floats_per_layer() {
+        return DeltaNetState<C::VALUE_HEADS, C::KEY_HEAD_DIM, C::VALUE_HEAD_DIM>::floats;
+    }
+    static constexpr size_t attention_floats_per_token_per_layer() { return 2 * C::Hkv * C::HEAD_DIM; }
+
+private:
+    std::array<std::variant<std::monostate, AttentionEntry, RecurrentEntry>, C::L> entries_;
+    size_t tokens_ = 0;
+};
+
+namespace detail {
+template <class C>
+constexpr size_t local_kv_heads() {
+    if constexpr (requires { C::LOCAL_HKV; }) return C::LOCAL_HKV;
+    else return C::Hkv;
+}
+template <class C>
+constexpr size_t full_kv_heads() {
+    if constexpr (requires { C::FULL_HKV; }) return C::FULL_HKV;
+    else return C::Hkv;
+}
+template <class C>
+constexpr bool is_full(size_t layer) {
+    return C::attention_type(layer) == decltype(C::attention_type(layer))::Full;
+}
+// The layer whose cache a shared-KV layer reads: the last layer of the same
+// attention type that owns its cache (Gemma 4 E4B: 22 for local layers, 23 for
+// full ones, gemma4.hpp:371-374).
+template <class C>
+constexpr size_t kv_source(size_t layer) {
+    if (!C::uses_shared_kv(layer)) return layer;
+    for (size_t s = layer; s-- > 0;)
+        if (!C::uses_shared_kv(s) && is_full<C>(s) == is_full<C>(layer)) return s;
+    return layer;
+}
+}  // namespace detail
+
+// Gemma4_12BCache (gemma4.hpp:734-762) and Gemma4E4BCache (gemma4.hpp:343-378)
+// for a Gemma 4 text config type C: local layers own a sliding-window ring of
+// C::LOCAL_WINDOW, full layers an append-only cache; layers that read another
+// layer's K/V (C::uses_shared_kv) own nothing and resolve to their source.
+// K/V heads per kind come from C::LOCAL_HKV / C::FULL_HKV (12B) or C::Hkv (E4B).
+template <class C>
+class Gemma4Cache {
+public:
+    using Local = LocalAttentionCache<detail::local_kv_heads<C>(), C::LOCAL_HEAD_DIM>;
+    using Full = FullAttentionCache<detail::full_kv_heads<C>(), C::FULL_HEAD_DIM>;
+
+    explicit Gemma4Cache(size_t capacity = C::CTX, size_t local_capacity = 2 * C::LOCAL_WINDOW,
+                         Dtype kv_dtype = Dtype::bf16, int device = 0) {
+        for (size_t layer = 0; layer < C::L; ++layer) {
+            if (C::uses_shared_kv(layer)) continue;
+            if (detail::is_full<C>(layer))
+                entries_[layer].template emplace<Full>(capacity, kv_dtype, device);
+            else
+                entries_[layer].template emplace<Local>(C::LOCAL_WINDOW, local_capacity, kv_dtype, device);
+        }
+    }
+    Gemma4Cache(const Gemma4Cache&) = delete;
+    Gemma4Cache& operator=(const Gemma4Cache&) = delete;
+
+    size_t tokens() const { return tokens_; }
+    void advance(size_t count) {
+        if (count > C::CTX - tokens_) throw std::length_error("Gemma4Cache: context exhausted");
+        tokens_ += count;
+    }
+    Local& local(size_t layer) { return std::get<Local>(entries_.at(detail::kv_source<C>(layer))); }
+    const Local& local(size_t layer) const { return std::get<Local>(entries_.at(detail::kv_source<C>(layer))); }
+    Full& full(size_t layer) { return std::get<Full>(entries_.at(detail::kv_source<C>(layer))); }
+    const Full& full(size_t layer) const { return std::get<Full>(entries_.at(detail::kv_source<C>(layer))); }
+
+    void clear() {
+        for (auto& e : entries_) {
+            if (auto* l = std::get_if<Local>(&e)) l->reset();
+            if (auto* f = std::get_if<Full>(&e)) f->reset();
+        }
+        tokens_ = 0;
+    }
+
+private:
+    std::array<std::variant<std::monostate, Local, Full>, C::L> entries_;
+    size_t tokens_ = 0;
+};
+#endif  // C++20
 
 }  // namespace nmg
