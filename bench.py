@@ -253,6 +253,191 @@ class RefSample:
         return total
 
 
+class RefConfigs:
+    """The reference's own code (oracle/_ref) on bounded samples of configs 1,
+    3, 4 and 5, timed on the host in the units of the GPU numbers they sit
+    beside; the C restatement (oracle/) stands in where the reference library
+    was not built.  Inputs are seeded N(0,1) rows of each configuration's
+    shapes; every timed region covers the reduction (or recurrence) only."""
+
+    def __init__(self, min_seconds=0.5):
+        import oracle
+
+        self.oracle = oracle
+        self.threads = os.cpu_count() or 1
+        os.environ.setdefault("NM_THREADS", str(self.threads))
+        self.min_seconds = min_seconds
+        self.R = oracle.ref()
+        if self.R is not None:
+            c_int, c_i64, c_f, c_p = ctypes.c_int, ctypes.c_int64, ctypes.c_float, ctypes.c_void_p
+            self.R.nmref_decode_sample.argtypes = [c_int, c_int, c_p, c_p, c_i64, c_p, c_int, c_f, c_int, c_i64, c_i64,
+                                                   c_p, ctypes.POINTER(ctypes.c_double)]
+            self.R.nmref_prefill_sample.argtypes = [c_int, c_int, c_p, c_p, c_i64, c_p, c_int, c_p, c_i64, c_f, c_int,
+                                                    c_i64, c_p, ctypes.POINTER(ctypes.c_double)]
+            self.R.nmref_delta_timed.argtypes = [c_int, c_int, c_int, c_p, c_i64, c_int, c_p, c_p, c_p, c_p, c_p, c_p,
+                                                 ctypes.POINTER(ctypes.c_double)]
+            self.kind, self.cores = "reference", int(self.R.nmref_threads())
+        else:
+            self.kind, self.cores = "port", self.threads
+
+    def _rows(self, seed, stream, rows, width):
+        return self.oracle.normal(seed, stream, rows * width).reshape(rows, width)
+
+    def decode_seconds(self, k, v, q, hkv, dh, hq, scale, window):
+        """Seconds per reduction of one query at the newest of k's rows: one
+        call to size the sample, then one of about min_seconds (each call
+        fills its cache untimed, so calls are few)."""
+        rows = k.shape[0]
+        reps = 1
+        for attempt in range(2):
+            if self.R is not None:
+                out = np.zeros(hq * dh, np.float32)
+                sec = ctypes.c_double()
+                st = self.R.nmref_decode_sample(hkv, dh, k.ctypes.data, v.ctypes.data, rows, q.ctypes.data, hq,
+                                                float(scale or 1.0), 0 if scale is None else 1, window, reps,
+                                                out.ctypes.data, ctypes.byref(sec))
+                if st != 0:
+                    raise RuntimeError(f"reference decode sample failed ({st})")
+                total = sec.value
+            else:
+                kw = dict(use_scale=False) if scale is None else dict(scale=np.float32(scale))
+                t0 = time.perf_counter()
+                for _ in range(reps):
+                    self.oracle.attend(k, v, 0, window, hkv, dh, q.reshape(1, -1), hq, rows - 1, threads=self.threads,
+                                       **kw)
+                total = time.perf_counter() - t0
+            if total >= self.min_seconds or reps >= 4096 or attempt == 1:
+                return total / reps
+            reps = int(min(4096, max(2, math.ceil(self.min_seconds / max(total, 1e-6)))))
+
+    def prefill_seconds(self, k, v, q, hkv, dh, hq, scale, window, start, n):
+        """Seconds to reduce query rows [start, start + n) over the causal prefix of k's rows."""
+        if self.R is not None:
+            out = np.zeros_like(q)
+            sec = ctypes.c_double()
+            blocks = np.array([start, n], np.int64)
+            st = self.R.nmref_prefill_sample(hkv, dh, k.ctypes.data, v.ctypes.data, k.shape[0], q.ctypes.data, hq,
+                                             blocks.ctypes.data, 1, float(scale or 1.0), 0 if scale is None else 1,
+                                             window, out.ctypes.data, ctypes.byref(sec))
+            if st != 0:
+                raise RuntimeError(f"reference prefill sample failed ({st})")
+            return sec.value
+        kw = dict(use_scale=False) if scale is None else dict(scale=np.float32(scale))
+        t0 = time.perf_counter()
+        self.oracle.attend(k[:start + n], v[:start + n], 0, window, hkv, dh, q[start:start + n], hq, start,
+                           threads=self.threads, **kw)
+        return time.perf_counter() - t0
+
+    def line(self, value, unit, sample, cores=None):
+        return {"value": value, "unit": unit, "cores": cores or self.cores, "kind": self.kind, "sample": sample}
+
+    def config1(self):
+        hq, hkv, dh, L = 16, 8, 128, 1024
+        k, v = self._rows(101, 1, L, hkv * dh), self._rows(101, 2, L, hkv * dh)
+        q = self._rows(101, 3, 1, hq * dh)
+        sec = self.decode_seconds(k, v, q, hkv, dh, hq, 1 / math.sqrt(dh), 0)
+        bytes_ = 2 * L * hkv * dh * 4 + 2 * hq * dh * 4
+        return self.line(bytes_ / sec / 1e9, "GB/s",
+                         f"config 1 decode (fp32 cache of 1024 rows), {sec * 1e6:.0f} us per call, reduction only")
+
+    def config3(self):
+        hv, hk, d, T = 32, 16, 128, 256
+        o = self.oracle
+        q = o.l2_normalize(self._rows(103, 1, T * hk, d).reshape(T, hk, d)) * np.float32(1 / math.sqrt(d))
+        k = o.l2_normalize(self._rows(103, 2, T * hk, d).reshape(T, hk, d))
+        v = self._rows(103, 3, T * hv, d).reshape(T, hv, d)
+        g = (-np.log1p(np.exp(o.normal(103, 4, T * hv).astype(np.float64)))).astype(np.float32).reshape(T, hv)
+        b = (1 / (1 + np.exp(-o.normal(103, 5, T * hv).astype(np.float64)))).astype(np.float32).reshape(T, hv)
+        q, k = np.ascontiguousarray(q, np.float32), np.ascontiguousarray(k, np.float32)
+        state = np.zeros((hv, d, d), np.float32)
+        out = np.zeros((T, hv, d), np.float32)
+        if self.R is not None:
+            sec = ctypes.c_double()
+            st = self.R.nmref_delta_timed(hv, d, d, state.ctypes.data, T, hk, q.ctypes.data, k.ctypes.data,
+                                          v.ctypes.data, g.ctypes.data, b.ctypes.data, out.ctypes.data,
+                                          ctypes.byref(sec))
+            if st != 0:
+                raise RuntimeError(f"reference delta sample failed ({st})")
+            total = sec.value
+        else:
+            t0 = time.perf_counter()
+            o.delta_run(state, q, k, v, g, b, hk)
+            total = time.perf_counter() - t0
+        per_tok = total / T
+        step_bytes = 2 * hv * d * d * 4 + 2 * hk * d * 4 + 2 * hv * d * 4 + 2 * hv * 4
+        sample = (f"{T} tokens of the 32-value-head recurrence (the reference runs it token by token on one thread: "
+                  f"{per_tok * 1e6:.0f} us per token)")
+        return {"prefill": self.line(1 / per_tok, "tok/s", sample, cores=1),
+                "decode": self.line(step_bytes / per_tok / 1e9, "GB/s", sample, cores=1)}
+
+    def config4(self):
+        hq, hkv, dh, W, S = 8, 4, 256, 1024, 8192
+        def rms(x):  # per-head RMS norm, unit gain (the configuration's QK-RMSNorm)
+            h = x.reshape(-1, dh)
+            return (h / np.sqrt(np.einsum("ij,ij->i", h, h)[:, None] / np.float32(dh) + np.float32(1e-6))).reshape(x.shape)
+
+        k, v = rms(self._rows(104, 1, S, hkv * dh)), self._rows(104, 2, S, hkv * dh)
+        q = rms(self._rows(104, 3, S, hq * dh))
+        n = 32  # the last 32 query rows: global layer (all earlier keys) and a local layer (1024)
+        sg = self.prefill_seconds(k, v, q, hkv, dh, hq, None, 0, S - n, n)
+        sl = self.prefill_seconds(k, v, q, hkv, dh, hq, None, W, S - n, n)
+        pairs_g = sum(r + 1 for r in range(S - n, S))
+        flops = 4.0 * dh * hq * (pairs_g + 5 * n * W)
+        res = {"prefill": self.line(flops / (sg + 5 * sl) / 1e12, "TFLOP/s",
+                                    f"config 4 prefill rows [{S - n}, {S}) of one global and five local (W=1024) "
+                                    "layers, reduction only")}
+        L = 32768
+        kd, vd = rms(self._rows(104, 4, L, hkv * dh)), self._rows(104, 5, L, hkv * dh)
+        qd = rms(self._rows(104, 6, 1, hq * dh))
+        dg = self.decode_seconds(kd, vd, qd, hkv, dh, hq, None, 0)
+        dl = self.decode_seconds(kd, vd, qd, hkv, dh, hq, None, W)
+        bytes_ = L * hkv * dh * 4 * 2 + 5 * W * hkv * dh * 4 * 2
+        res["decode"] = self.line(bytes_ / (dg + 5 * dl) / 1e9, "GB/s",
+                                  "config 4 decode of one sequence (32768 fp32 rows: one global + five local layers), "
+                                  f"{(dg + 5 * dl) * 1e3:.2f} ms per token per 6-layer group")
+        return res
+
+    def config5(self):
+        hq, hkv, dh = 64, 8, 128
+        lens = [min(ragged_lengths(1, 64, 4096, 131072)[:4])]  # the shortest of the first four
+        total_s, total_b = 0.0, 0
+        for i, L in enumerate(lens):
+            k, v = self._rows(105, 2 * i, L, hkv * dh), self._rows(105, 2 * i + 1, L, hkv * dh)
+            q = self._rows(105, 100 + i, 1, hq * dh)
+            total_s += self.decode_seconds(k, v, q, hkv, dh, hq, 1 / math.sqrt(dh), 0)
+            total_b += L * hkv * dh * 4 * 2 + 2 * hq * dh * 4
+            del k, v
+        return self.line(total_b / total_s / 1e9, "GB/s",
+                         f"config 5 decode of one of its sequences ({lens[0]} cached rows, the shortest of the first "
+                         "four; fp32), reduction only")
+
+
+def cpu_baselines(extra):
+    """Adds a cpu_baseline beside each single-GPU extra (rank 0, N = 1)."""
+    ref = RefConfigs()
+    for name, key, fn in (("config1", None, ref.config1), ("config3", None, ref.config3),
+                          ("config4", None, ref.config4), ("config5", None, ref.config5)):
+        ent = extra.get(name)
+        if not isinstance(ent, dict) or "error" in ent:
+            continue
+        try:
+            cb = fn()
+        except Exception as e:  # report, never hide, a failing sample
+            ent["cpu_baseline"] = {"error": f"{type(e).__name__}: {str(e)[:200]}"}
+            continue
+        if name == "config3":
+            if isinstance(ent.get("prefill_chunk64"), dict):
+                ent["prefill_chunk64"]["cpu_baseline"] = cb["prefill"]
+            if isinstance(ent.get("decode"), dict):
+                ent["decode"]["cpu_baseline"] = cb["decode"]
+        elif name == "config4":
+            for part in ("prefill", "decode"):
+                if isinstance(ent.get(part), dict):
+                    ent[part]["cpu_baseline"] = cb[part]
+        else:
+            ent["cpu_baseline"] = cb
+
+
 def reference_arm(args, rank, world):
     if rank != 0:
         return
@@ -1342,6 +1527,8 @@ def main():
         torch.cuda.empty_cache()
         extra = sharded_extras(torch, dist, dev, rank, world)
     cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu and extra:
+        cpu_baselines(extra)
     if rank == 0 and world == 1 and not args.no_cpu:
         ref = RefSample(full=True)
         ref.run()  # warm-up

@@ -244,6 +244,29 @@ int prefill_sample(const float* k, const float* v, size_t rows, const float* q, 
     });
 }
 
+// Timed sample of single-token decode: the cache is filled with `rows` rows
+// (untimed), then one query at position rows - 1 is reduced `reps` times
+// (timed, seconds_out = the total); window > 0 narrows the visible rows as a
+// Gemma local layer's ring does.  q / out are one [hq*Dh] row.
+template <size_t Hkv, size_t Dh>
+int decode_sample(const float* k, const float* v, size_t rows, const float* q, size_t hq, float scale, bool use_scale,
+                  size_t window, size_t reps, float* out, double* seconds_out) {
+    constexpr size_t W = Hkv * Dh;
+    return guarded([&] {
+        FullAttentionCache<Hkv, Dh> cache;
+        for (size_t r = 0; r < rows; ++r) cache.append(Position{r}, vec_from<W>(k + r * W), vec_from<W>(v + r * W));
+        const Position at{rows - 1};
+        const auto t0 = std::chrono::steady_clock::now();
+        for (size_t i = 0; i < reps; ++i) {
+            if (window == 0)
+                reduce<Hkv, Dh>(cache, q, 1, hq, at, scale, use_scale, out);
+            else
+                reduce_window<Hkv, Dh>(cache, window, q, 1, hq, at, scale, use_scale, out);
+        }
+        *seconds_out = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+    });
+}
+
 }  // namespace
 
 #define NMREF_ATTN_SHAPES(X) \
@@ -307,6 +330,18 @@ int nmref_prefill_sample(int hkv, int dh, const float* k, const float* v, int64_
     if (hkv == H && dh == D)                                                                                      \
         return prefill_sample<H, D>(k, v, size_t(rows), q, size_t(hq), blocks, size_t(nblocks), scale, use_scale != 0, \
                                     size_t(window), out, seconds);
+    NMREF_ATTN_SHAPES(X)
+#undef X
+    return 100;
+}
+
+int nmref_decode_sample(int hkv, int dh, const float* k, const float* v, int64_t rows, const float* q, int hq,
+                        float scale, int use_scale, int64_t window, int64_t reps, float* out, double* seconds) {
+    if (rows <= 0 || reps <= 0) return 1;
+#define X(H, D)                                                                                                     \
+    if (hkv == H && dh == D)                                                                                        \
+        return decode_sample<H, D>(k, v, size_t(rows), q, size_t(hq), scale, use_scale != 0, size_t(window), size_t(reps), \
+                                   out, seconds);
     NMREF_ATTN_SHAPES(X)
 #undef X
     return 100;
