@@ -1202,8 +1202,8 @@ def sharded_config1(rk):
             rk.gather(outs[i], gathered)
             rk.to_rows(gathered, full, world, 1, hq_l * dh * 4)
 
-    ms_local = rk.graph_ms(local, 20, 5) / NC
-    ms = rk.graph_ms(whole, 20, 5) / NC
+    ms_local = rk.graph_ms(local, 20, 1) / NC
+    ms = rk.graph_ms(whole, 20, 1) / NC
     bytes_ = 2 * rows * hkv * dh * 4 + 2 * hq * dh * 4
     p = peaks()
     gbs = bytes_ / (ms * 1e-3) / 1e9
