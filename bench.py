@@ -1508,6 +1508,18 @@ def main():
     import hero_b200
 
     hero_b200.lib()  # fail loudly before any work if the CUDA library is missing
+    if args.only and args.only != "c2" and world > 1:
+        sharded = {"c1": sharded_config1, "c3": sharded_config3, "c4": sharded_config4, "c5": sharded_config5}
+        if args.only not in sharded:
+            raise SystemExit(f"--only {args.only} runs on one GPU")
+        rk = Ranks(torch, dist, dev, rank, world)
+        res = sharded[args.only](rk)
+        rk.close()
+        if rank == 0:
+            print(json.dumps({"only": args.only, "n_gpus": world, **res}), flush=True)
+        dist.barrier()
+        dist.destroy_process_group()
+        return
     if args.only and args.only != "c2":
         fn = {"c1": extra_config1, "c3": extra_config3, "c4": extra_config4, "c5": extra_config5,
               "io": extra_attn_io, "vit": extra_vit}[args.only]
