@@ -287,7 +287,9 @@ int decode_sample(const float* k, const float* v, size_t rows, const float* q, s
     X(8, 128)                \
     X(1, 256)                \
     X(2, 256)                \
-    X(4, 256)
+    X(4, 256)                \
+    X(1, 512)                \
+    X(2, 512)
 
 #define NMREF_DELTA_SHAPES(X) \
     X(1, 2, 2)                \

@@ -146,7 +146,9 @@ def _same(got, want):
 
 @needs_ref
 @pytest.mark.parametrize("hq,hkv,dh,rows,qrows,scale", [(16, 8, 128, 300, 4, True), (8, 4, 256, 200, 3, False),
-                                                        (2, 1, 2, 5, 2, True), (64, 8, 128, 129, 1, True)])
+                                                        (2, 1, 2, 5, 2, True), (64, 8, 128, 129, 1, True),
+                                                        # Gemma 4 full-attention layers (head_dim 512): 12B, E4B
+                                                        (16, 1, 512, 150, 3, False), (8, 2, 512, 90, 2, False)])
 def test_oracle_equals_reference_full(hq, hkv, dh, rows, qrows, scale):
     k = oracle.normal(11, 1, rows * hkv * dh).reshape(rows, -1)
     v = oracle.normal(11, 2, rows * hkv * dh).reshape(rows, -1)
