@@ -598,7 +598,9 @@ def bench_prefill(args, torch, dist, rank, world, dev):
     for i in range(R):
         step(i, kev[i])
     barrier()
-    kernel_ms = sum(a.elapsed_time(b) for a, b in kev) / R
+    kernel_each = [a.elapsed_time(b) for a, b in kev]
+    kernel_ms = sum(kernel_each) / R
+    kernel_pct = {f"p{q}": float(np.percentile(kernel_each, q)) for q in (10, 50, 90)}
     # the timed region: exactly args.steps steps, replayed from one graph
     graph = capture(step, args.steps, args.warmup)
     graph.replay()  # untimed first replay
@@ -725,6 +727,7 @@ def bench_prefill(args, torch, dist, rank, world, dev):
     roof = {"bound": "tensor", "kernel": "attn_prefill_kernel<128,bf16>", "achieved": achieved, "peak": p["bf16"],
             "unit": "TFLOP/s", "frac": achieved / p["bf16"], "peak_src": f"{p['src']} bf16 dense (burst)",
             "traffic": ncu_traffic("attn_prefill_c2"), "kernel_ms": kernel_ms,
+            "kernel_ms_percentiles": {**kernel_pct, "launches": R, "rank": 0 if world == 1 else rank},
             "algorithmic_unit": "4*head_dim*q_heads per visible (query,key) pair; 8,390,656 pairs"}
     launches = args.steps * 2
     return {"value": value, "ms_per_step": ms_step, "tok_per_s": S / (ms_step * 1e-3), "roofline": roof,
