@@ -1172,7 +1172,7 @@ class Ranks:
         self.comm.close()
 
 
-def sharded_config1(rk):
+def sharded_config1(rk, small=False):
     """Config 1 split by KV head: each rank reduces its heads of the query
     over its share of the fp32 cache, then the head outputs are all-gathered
     and laid into the [1][16*128] row."""
@@ -1183,7 +1183,7 @@ def sharded_config1(rk):
     hq, hkv, dh, rows = 16, 8, 128, 1024
     sh = kv_shard(rk.rank, world, hkv, hq)
     hkv_l, hq_l = sh.kv1 - sh.kv0, sh.q1 - sh.q0
-    NC = 20 * world  # rotated caches: NC * 8.4 MB / world per GPU > L2
+    NC = 2 if small else 20 * world  # rotated caches: NC * 8.4 MB / world per GPU > L2
     caches, qs, outs = [], [], []
     for _ in range(NC):
         c = nm.FullAttentionCache(hkv_l, dh, capacity=rows, device=dev.index)
@@ -1220,7 +1220,7 @@ def sharded_config1(rk):
                       "outputs + head-to-row permutation; time = max over ranks"}
 
 
-def sharded_config3(rk):
+def sharded_config3(rk, small=False):
     """Config 3 split by key-head group: a rank owns key heads [k0, k1) and the
     value heads that read them (h % 16), so prefill and decode run with no
     exchange; the head outputs are all-gathered into [T][32*128] rows."""
@@ -1228,7 +1228,7 @@ def sharded_config3(rk):
     from hero_b200.shard import delta_shard
 
     torch, dev, world = rk.torch, rk.dev, rk.world
-    hv, hk, d, T, Tdec = 32, 16, 128, 8192, 256
+    hv, hk, d, T, Tdec = (32, 16, 128, 512, 8) if small else (32, 16, 128, 8192, 256)
     sd = delta_shard(rk.rank, world, hk, hv)
     hs = torch.tensor(sd.v_heads, device=dev)
     R = hv // hk
@@ -1300,7 +1300,7 @@ def sharded_config3(rk):
                       "= recurrent update + ncclAllGather + head-to-row permutation; time = max over ranks", **res}
 
 
-def sharded_config4(rk):
+def sharded_config4(rk, small=False):
     """Config 4 across ranks: prefill by KV head (with more ranks than KV heads,
     the two ranks of a KV head split its query heads); decode by KV head and,
     past four ranks, by batch half.  Head outputs are all-gathered into rows."""
@@ -1308,7 +1308,7 @@ def sharded_config4(rk):
     from hero_b200.shard import decode_shard, kv_shard
 
     torch, dev, world = rk.torch, rk.dev, rk.world
-    hq, hkv, dh, W, S = 8, 4, 256, 1024, 8192
+    hq, hkv, dh, W, S = (8, 4, 256, 1024, 1536) if small else (8, 4, 256, 1024, 8192)
     sp = kv_shard(rk.rank, world, hkv, hq)
     hkv_l, hq_l = sp.kv1 - sp.kv0, sp.q1 - sp.q0
     g = torch.Generator(device=dev)
@@ -1345,7 +1345,7 @@ def sharded_config4(rk):
                        "roofline": {"bound": "tensor", "achieved": tf_local, "peak": p["bf16"],
                                     "frac": tf_local / p["bf16"], "per": "GPU, attention alone"}}}
     del local, glob, q, k, v, o, gathered, full
-    B, L = 16, 32768
+    B, L = (16, 2048) if small else (16, 32768)
     ds = decode_shard(rk.rank, world, hkv, hq, B)
     sh = ds.heads
     hkv_d, hq_d, Bl = sh.kv1 - sh.kv0, sh.q1 - sh.q0, ds.b1 - ds.b0
@@ -1399,7 +1399,7 @@ def sharded_config4(rk):
                       "all-gathered (NCCL) and permuted into rows; time = max over ranks", **res}
 
 
-def sharded_config5(rk):
+def sharded_config5(rk, small=False):
     """Config 5 split by KV head, as the configuration names it: each rank holds
     its KV heads of all 64 ragged f16 caches; the [64][64*128] output is
     all-gathered over NVLink."""
@@ -1409,6 +1409,8 @@ def sharded_config5(rk):
     torch, dev, world = rk.torch, rk.dev, rk.world
     B, hq, hkv, dh = 64, 64, 8, 128
     lens = ragged_lengths(1, B, 4096, 131072)
+    if small:  # profiling size: 8 sequences of at most 8192 rows
+        B, lens = 8, [min(L, 8192) for L in lens[:8]]
     ds = decode_shard(rk.rank, world, hkv, hq, B)
     sh = ds.heads
     hkv_l, hq_l, Bl = sh.kv1 - sh.kv0, sh.q1 - sh.q0, ds.b1 - ds.b0
@@ -1516,7 +1518,7 @@ def main():
         if args.only not in sharded:
             raise SystemExit(f"--only {args.only} runs on one GPU")
         rk = Ranks(torch, dist, dev, rank, world)
-        res = sharded[args.only](rk)
+        res = sharded[args.only](rk, small=args.small)
         rk.close()
         if rank == 0:
             print(json.dumps({"only": args.only, "n_gpus": world, **res}), flush=True)
