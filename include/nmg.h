@@ -120,7 +120,7 @@ NMG_API int nmg_kv_read_row(const nmg_kv_cache* cache, int64_t chronological_row
 
 /* Forget every row (a new sequence on the same device storage), the device
  * counterpart of dropping a PrefixState's carried caches
- * (src/transformer.hpp:139-142).  No device work. */
+ * (src/transformer.hpp:154-160).  No device work. */
 NMG_API int nmg_kv_reset(nmg_kv_cache* cache);
 
 /* Raw device storage, for callers that fuse their own producer. */

@@ -307,7 +307,7 @@ void gated_delta_step(float* state, const float* q, const float* k, const float*
 // cache is sized up front), local caches `local_capacity` physical rows
 // (>= the window; one batch of up to local_capacity - window + 1 rows is
 // attended as a whole).  clear() forgets everything derived, in place, where
-// the reference's PrefixCache::clear (transformer.hpp:157-163) assigns a
+// the reference's PrefixCache::clear (transformer.hpp:154-160) assigns a
 // fresh state; the device memory is kept.
 
 // Qwen35State<C> (qwen35.hpp:206-241) for a Qwen 3.5 config type C (the
