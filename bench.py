@@ -1088,6 +1088,10 @@ def extra_config5(torch, dev, small=False):
 
 # ---------------------------------------------------------------- extras (N>1)
 
+class OtherRankFailed(RuntimeError):
+    pass
+
+
 class Ranks:
     """The ranks of a multi-GPU extra: barriers, max-over-ranks timing, and
     the all-gather of equal per-rank blocks followed by the head-to-row
@@ -1115,6 +1119,15 @@ class Ranks:
         t = self.torch.tensor([0 if ok else 1], device=self.dev, dtype=self.torch.int32)
         self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
         return int(t.item()) == 0
+
+    def checkpoint(self):
+        """Every rank of an extra passes here together: after each phase's
+        allocations (before its collectives) and at its end.  A rank that
+        failed on its own since the last checkpoint meets the others here with
+        all_ok(False) instead, and every rank then stops the extra; each rank
+        so takes the same collective steps whichever ranks failed."""
+        if not self.all_ok(True):
+            raise OtherRankFailed("failed on another rank")
 
     def gather(self, send, gathered):
         self.comm.allgather(send, gathered, self.cur())
@@ -1166,6 +1179,11 @@ class Ranks:
         self.barrier()
         return self.max_over(a.elapsed_time(b) / reps)[0]
 
+    def release(self):
+        """Between extras: wait for this GPU, return the freed blocks."""
+        self.torch.cuda.synchronize(self.dev)
+        self.torch.cuda.empty_cache()
+
     def close(self):
         self.torch.cuda.synchronize(self.dev)
         self.dist.barrier()
@@ -1205,12 +1223,14 @@ def sharded_config1(rk, small=False):
             rk.gather(outs[i], gathered)
             rk.to_rows(gathered, full, world, 1, hq_l * dh * 4)
 
+    rk.checkpoint()
     ms_local = rk.graph_ms(local, 20, 1) / NC
     ms = rk.graph_ms(whole, 20, 1) / NC
     bytes_ = 2 * rows * hkv * dh * 4 + 2 * hq * dh * 4
     p = peaks()
     gbs = bytes_ / (ms * 1e-3) / 1e9
     gbs_local = bytes_ / world / (ms_local * 1e-3) / 1e9
+    rk.checkpoint()
     return {"workload": "config 1: decode, fp32, 16q/8kv, d128, 1024 cached", "parallelism": f"kv-head shards x{world}",
             "value": gbs, "unit": "GB/s", "us_per_call": ms * 1e3, "tok_per_s": 1 / (ms * 1e-3),
             "attention_only_us": ms_local * 1e3,
@@ -1254,6 +1274,7 @@ def sharded_config3(rk, small=False):
         rk.gather(out, gathered)
         rk.to_rows(gathered, full, world, T * R, sd.hk * d * 4)
 
+    rk.checkpoint()
     ms_pl = rk.event_ms(prefill_local, 3)
     ms_p = rk.event_ms(prefill, 3)
     C = 64
@@ -1286,6 +1307,7 @@ def sharded_config3(rk, small=False):
             rk.gather(od[t], gdec)
             rk.to_rows(gdec, fdec[t], world, R, sd.hk * d * 4)
 
+    rk.checkpoint()
     ms_sl = rk.graph_ms(steps_local, 5, 1) / Tdec
     ms_s = rk.graph_ms(steps, 5, 1) / Tdec
     bytes_ = 2 * hv * d * d * 4 + 2 * hk * d * 4 + 2 * hv * d * 4 + 2 * hv * 4
@@ -1294,6 +1316,7 @@ def sharded_config3(rk, small=False):
                      "tok_per_s": 1 / (ms_s * 1e-3), "recurrence_only_us_per_step": ms_sl * 1e3,
                      "roofline": {"bound": "hbm", "achieved": gbs_local, "peak": p["hbm"], "frac": gbs_local / p["hbm"],
                                   "per": "GPU, recurrent update alone", "note": "state is L2-resident between steps"}}
+    rk.checkpoint()
     return {"workload": "config 3: gated delta rule, 16 k / 32 v heads, d128, T 8192 prefill + 256 decode steps",
             "parallelism": f"key-head groups x{world} (value head h with key head h % 16), outputs all-gathered",
             "method": "prefill: 3 eager calls with CUDA events; decode: 256 steps in one CUDA graph, each step "
@@ -1330,6 +1353,7 @@ def sharded_config4(rk, small=False):
             rk.gather(o, gathered)
             rk.to_rows(gathered, full, world, S, hq_l * dh * 2)
 
+    rk.checkpoint()
     ms_l = rk.event_ms(lambda: [layer(c, False) for c in local + [glob]], 3)
     ms = rk.event_ms(lambda: [layer(c, True) for c in local + [glob]], 3)
     pairs_g = S * (S + 1) // 2
@@ -1379,6 +1403,7 @@ def sharded_config4(rk, small=False):
                 rk.to_rows(gd[part * ds.kv_world:(part + 1) * ds.kv_world], fd[part * Bl:(part + 1) * Bl],
                            ds.kv_world, Bl, hq_d * dh * 4)
 
+    rk.checkpoint()
     ms_g_l = rk.graph_ms(lambda: decode(gcaches, False), 10, 2)
     ms_g = rk.graph_ms(lambda: decode(gcaches, True), 10, 2)
     ms_w = rk.graph_ms(lambda: decode(lcaches, True), 10, 20)
@@ -1394,6 +1419,7 @@ def sharded_config4(rk, small=False):
                                                                        else ""),
                      "roofline": {"bound": "hbm", "achieved": gbs_local, "peak": p["hbm"], "frac": gbs_local / p["hbm"],
                                   "per": "GPU, global layer attention alone"}}
+    rk.checkpoint()
     return {"workload": "config 4: Gemma hybrid bf16, 8q/4kv, d256, scale 1, 5 local (W=1024) : 1 global",
             "method": "prefill: 3 eager groups with CUDA events; decode: CUDA graphs; each layer's head outputs "
                       "all-gathered (NCCL) and permuted into rows; time = max over ranks", **res}
@@ -1439,12 +1465,14 @@ def sharded_config5(rk, small=False):
                 rk.to_rows(gathered[part * ds.kv_world:(part + 1) * ds.kv_world], full[part * Bl:(part + 1) * Bl],
                            ds.kv_world, Bl, hq_l * dh * 4)
 
+    rk.checkpoint()
     ms_l = rk.graph_ms(lambda: step(False), 5, 1)
     ms = rk.graph_ms(lambda: step(True), 5, 1)
     bytes_ = 4096 * sum(lens) + 2 * B * hq * dh * 2
     gbs = bytes_ / (ms * 1e-3) / 1e9
     gbs_local = bytes_ / world / (ms_l * 1e-3) / 1e9
     p = peaks()
+    rk.checkpoint()
     return {"workload": "config 5: batch 64 ragged (U[4096,131072], seed 1) decode, 64q/8kv, d128, f16 cache",
             "parallelism": f"kv-head shards x{ds.kv_world}" + (f", batch parts x{ds.parts}" if ds.parts > 1 else ""),
             "value": gbs, "unit": "GB/s", "ms_per_call": ms, "tok_per_s": B / (ms * 1e-3),
@@ -1457,22 +1485,21 @@ def sharded_config5(rk, small=False):
 
 def sharded_extras(torch, dist, dev, rank, world):
     """The other configurations on `world` GPUs.  Every rank runs the same
-    steps; a failure on any rank is agreed on (one collective that every rank
-    reaches) and reported as that extra's error, so the ranks stay in step."""
+    steps; a failure on any rank stops that extra on every rank at the next
+    checkpoint (Ranks.checkpoint) and is reported as its error."""
     extra = {}
     rk = Ranks(torch, dist, dev, rank, world)
     for name, fn in (("config1", sharded_config1), ("config3", sharded_config3), ("config4", sharded_config4),
                      ("config5", sharded_config5)):
-        err = None
         try:
             res = fn(rk)
+        except OtherRankFailed as e:
+            res = {"error": str(e)}
         except Exception as e:  # report, never hide, a failing extra
-            res, err = None, f"{type(e).__name__}: {str(e)[:200]}"
-        if not rk.all_ok(err is None):
-            res = {"error": err or "failed on another rank"}
+            res = {"error": f"{type(e).__name__}: {str(e)[:200]}"}
+            rk.all_ok(False)  # meets the other ranks at their next checkpoint
         extra[name] = res
-        torch.cuda.synchronize(dev)
-        torch.cuda.empty_cache()
+        rk.release()
     rk.close()
     return extra
 

@@ -119,6 +119,9 @@ class FakeRanks(bench.Ranks):
         fn()
         return 1.0
 
+    def release(self):
+        pass
+
     def close(self):
         pass
 
@@ -141,3 +144,81 @@ def test_sharded_extra_host_logic(fake_nm, name, world):
         res = getattr(bench, name)(rk, small=True)
         assert rk.gathers > 0, "every extra gathers its head outputs"
         assert "workload" in res and "error" not in res
+
+
+_REAL_ALL_OK = bench.Ranks.all_ok
+
+
+class GlooRanks(FakeRanks):
+    """FakeRanks whose agreement steps are real collectives (two gloo ranks)."""
+
+    def __init__(self, rank, world, dist):
+        super().__init__(rank, world)
+        self.dist = dist
+
+    def all_ok(self, ok):
+        return _REAL_ALL_OK(self, ok)
+
+
+def _rank_protocol(rank, world, port, results):
+    import os
+    from datetime import timedelta
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path.insert(0, root)
+    import torch.distributed as dist
+
+    import hero_b200
+
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=timedelta(seconds=60))
+    try:
+        nm = FakeNm()
+        hero_b200.nm = nm
+        sys.modules["hero_b200.nm"] = nm
+        if rank == 1:  # fails alone while setting up config 3 (before its first checkpoint)
+            def broken_state(*a, **k):
+                raise MemoryError("injected")
+            nm.DeltaNetState = broken_state
+        if rank == 0:  # fails alone between config 4's prefill and decode phases (its 6th ring)
+            made, local = [0], nm.LocalAttentionCache
+
+            def sixth_ring_fails(*a, **k):
+                made[0] += 1
+                if made[0] == 6:
+                    raise ValueError("injected")
+                return local(*a, **k)
+            nm.LocalAttentionCache = sixth_ring_fails
+        real = {n: getattr(bench, n) for n in ("sharded_config1", "sharded_config3", "sharded_config4",
+                                                "sharded_config5")}
+        for n, fn in real.items():  # the small variants
+            setattr(bench, n, lambda rk, fn=fn: fn(rk, small=True))
+        rk = GlooRanks(rank, world, dist)
+        bench.Ranks = lambda *a: rk
+        extra = bench.sharded_extras(None, dist, None, rank, world)
+        results[rank] = {k: ("error" in v) for k, v in extra.items()}
+    finally:
+        dist.destroy_process_group()
+
+
+def test_one_rank_failing_stops_that_extra_on_every_rank():
+    import socket
+
+    import torch.multiprocessing as mp
+
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    results = ctx.Manager().dict()
+    procs = [ctx.Process(target=_rank_protocol, args=(r, 2, port, results)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=180)
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    want = {"config1": False, "config3": True, "config4": True, "config5": False}
+    assert dict(results) == {0: want, 1: want}
