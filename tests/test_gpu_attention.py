@@ -117,6 +117,22 @@ def test_errors_match_the_reference(dev):
         nm.attend(nm.FullAttentionCache(2, 2, capacity=2), T([[1, 0]], dev), 0)
 
 
+def test_empty_inputs_do_nothing(dev):
+    # Zero rows append nothing and reduce nothing; zero tokens leave the delta state as it was.
+    cache = nm.FullAttentionCache(2, 128, capacity=4, dtype="bf16")
+    z = torch.empty(0, 2 * 128, device=dev, dtype=torch.bfloat16)
+    cache.append(0, z, z)
+    assert cache.size() == 0
+    q0 = torch.empty(0, 4 * 128, device=dev, dtype=torch.bfloat16)
+    assert nm.append_attend(cache, 0, z, z, q0, 0.1).shape == (0, 4 * 128)
+    assert cache.size() == 0
+    st = nm.DeltaNetState(2, 128, 128)
+    before = st.tensor().clone()
+    e = lambda *shape: torch.empty(*shape, device=dev)
+    out = nm.delta_prefill(st, e(0, 1, 128), e(0, 1, 128), e(0, 2, 128), e(0, 2), e(0, 2), 1, chunk=64)
+    assert out.shape == (0, 2, 128) and torch.equal(st.tensor(), before)
+
+
 def test_visible_rows_exhaustive_box(dev):
     # property_tests.cpp:318-338 through the device cache's bookkeeping
     for width in range(1, 5):
