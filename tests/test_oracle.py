@@ -255,6 +255,23 @@ def test_golden_fixtures_exist():
     assert len(glob.glob(os.path.join(GOLDEN, "*.npz"))) >= 6
 
 
+@needs_ref
+def test_golden_fixtures_reproduce_from_the_reference(tmp_path, capsys):
+    # The committed fixtures are what tests/golden/make_golden.py writes from
+    # the reference build today: rerun it into a scratch directory and compare.
+    src = open(os.path.join(GOLDEN, "make_golden.py")).read()
+    scratch = tmp_path / "golden"
+    scratch.mkdir()
+    exec(compile(src, "make_golden.py", "exec"), {"__file__": str(scratch / "make_golden.py"), "__name__": "__main__"})
+    committed = sorted(glob.glob(os.path.join(GOLDEN, "*.npz")))
+    assert sorted(p.name for p in scratch.glob("*.npz")) == [os.path.basename(p) for p in committed]
+    for p in committed:
+        a, b = np.load(p), np.load(scratch / os.path.basename(p))
+        assert set(a.files) == set(b.files), p
+        for key in a.files:
+            assert np.array_equal(a[key], b[key]), (p, key)
+
+
 @pytest.mark.skipif(oracle.ref() is None, reason="reference library not built")
 @pytest.mark.parametrize("heads,tq,tk,scale", [(12, 40, 360, 1.0), (4, 37, 300, 0.125)])
 def test_dense_attention_is_the_reference_sdpa(heads, tq, tk, scale):
