@@ -86,3 +86,31 @@ def test_fp32_cache_at_head_dim_512_is_refused(dev):
     cache.append(0, x, x)
     with pytest.raises(Unsupported):
         nm.attend(cache, torch.randn(1, DH, device=dev), 3, 1.0)
+
+
+def test_gemma_full_layer_prologue_then_attend(dev):
+    # A Gemma 4 E4B full-attention layer on a bf16 cache: per-head RMS norm and
+    # partial RoPE (1/4 of 512 planes, base 1e6, gemma4.hpp:397) written into the
+    # cache by the prologue, then the reduction at head_dim 512 with scale 1.
+    hq, hkv, Tt = 8, 2, 24
+    x = oracle.normal(23, 1, Tt * hq * DH).reshape(Tt, hq * DH) * np.float32(2)
+    k = oracle.normal(23, 2, Tt * hkv * DH).reshape(Tt, hkv * DH) * np.float32(3)
+    v = oracle.normal(23, 3, Tt * hkv * DH).reshape(Tt, hkv * DH)
+    qg = oracle.normal(23, 4, DH) * np.float32(0.5) + np.float32(1)
+    kg = oracle.normal(23, 5, DH) * np.float32(0.5) + np.float32(1)
+    f32 = lambda a: torch.from_numpy(np.ascontiguousarray(a, dtype=np.float32)).to(dev)
+    cache = nm.FullAttentionCache(hkv, DH, capacity=32, dtype="bf16")
+    Q = nm.attn_prologue(cache, 0, f32(x), f32(k), f32(v), f32(qg), f32(kg), 1e-6, 1000000, 1, 4, gated=False,
+                         v_norm=True)
+    assert Q.dtype == torch.bfloat16 and cache.size() == Tt
+    # the prepared values are the oracle's, rounded to the cache's bf16
+    wq, wk, wv = oracle.attn_prologue(x, k, v, qg, kg, hq, hkv, DH, 0, 1e-6, 1000000, 1, 4, gated=False, v_norm=True)
+    keys = np.stack([np.concatenate([cache.key(r, h).numpy() for h in range(hkv)]) for r in range(Tt)])
+    vals = np.stack([np.concatenate([cache.value(r, h).numpy() for h in range(hkv)]) for r in range(Tt)])
+    qv = Q.float().cpu().numpy()
+    for got, want in ((qv, wq), (keys, wk), (vals, wv)):
+        assert np.all(np.abs(got - want) <= 2.0 ** -7 * np.maximum(np.abs(want), 2.0 ** -14) + 1e-5)
+    # and the reduction over exactly what the device holds matches the oracle's
+    out = nm.attend(cache, Q, 0, None, out_dtype=torch.float32).cpu().numpy()
+    assert_close(out, oracle.attend(keys, vals, 0, 0, hkv, DH, qv, hq, 0, use_scale=False),
+                 what="Gemma full layer at head_dim 512")
