@@ -121,6 +121,9 @@ struct SplitCfg {
     static constexpr int C_OFF = P_OFF + WARPS * G * 32 * 4;
     static constexpr int BAR_OFF = ((C_OFF + WARPS * G * (DH + 2) * 4) + 15) / 16 * 16;
     static constexpr int SMEM = BAR_OFF + 64;
+    // dynamic plus the kernel's static arrays (ticket flag, merge scratch) within 227 KB
+    static_assert(SMEM + 4 * (WARPS + 256 + 1) <= 232448, "shared memory budget");
+    static_assert(!BULK || (ROWB % 16 == 0 && (Q_OFF % 16) == 0), "bulk copies move 16-byte multiples");
 };
 
 template <int KVDT, int DH, int G, int WARPS>
