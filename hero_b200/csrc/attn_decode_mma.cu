@@ -110,6 +110,7 @@ struct MmaCfg {
     static constexpr int C_OFF = 0;
     static constexpr int BAR_OFF = Q_OFF + 16 * Q_PITCH;
     static constexpr int SMEM = BAR_OFF + 64 + 1024;            // + alignment slack
+    static_assert(SMEM <= 232448, "shared memory budget");
 };
 
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
