@@ -137,7 +137,9 @@ NMG_API int nmg_kv_storage(const nmg_kv_cache* cache, void** keys, void** values
  * over the cache's visible_rows(first_query + t) as the cache stands now.
  * q: device [rows][hq*head_dim] in q_dtype; out: device [rows][hq*head_dim] in
  * out_dtype.  Dispatches to the tcgen05 flash kernel for 16-bit caches with
- * head_dim 128/256 and many rows, and to the split-KV decode kernel otherwise.
+ * head_dim 64/128/256 and many rows, and to the split-KV decode kernels
+ * otherwise (head_dim 1..256 in powers of two for fp32 caches; 64, 128, 256
+ * and 512 for 16-bit caches; NMG_UNSUPPORTED for any other).
  * NMG_RUNTIME_ERROR if any query sees no key (checked on the host first). */
 NMG_API int nmg_attend(const nmg_kv_cache* cache, int hq, const void* q, int q_dtype, int64_t rows, int64_t first_query,
                float scale, int use_scale, void* out, int out_dtype, void* stream);
