@@ -61,17 +61,11 @@ def peaks():
 
 
 def ncu_traffic(name):
-    """dram bytes per launch from a committed ncu summary (profiles/<name>.md), or None."""
-    path = os.path.join(ROOT, "profiles", name + ".md")
-    if not os.path.exists(path):
+    """DRAM bytes per launch of a workload's dominant kernel from profiles/traffic.json, or None."""
+    try:
+        return float(json.load(open(os.path.join(ROOT, "profiles", "traffic.json")))[name]["dram_bytes_per_launch"])
+    except (OSError, KeyError, TypeError, ValueError):
         return None
-    for line in open(path):
-        if line.strip().startswith("dram_bytes_per_launch:"):
-            try:
-                return float(line.split(":", 1)[1].strip().split()[0])
-            except ValueError:
-                return None
-    return None
 
 
 # ---------------------------------------------------------------- clocks
@@ -453,7 +447,7 @@ def reference_arm(args, rank, world):
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * float(np.mean(secs)),
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": config2_desc(world),
+            "config": {**config2_desc(world), "rotating_sets": c2_rotating_sets(world)},
             "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": ref.cores, "kind": ref.kind,
                              "sample": ref.sample},
             "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -466,6 +460,13 @@ def c2_sample_flops(rows_per_block=256):
     b0, b1 = S // 2 - rows_per_block // 2, S - rows_per_block
     pairs = sum(r + 1 for r in range(b0, b0 + rows_per_block)) + sum(r + 1 for r in range(b1, S))
     return 4.0 * DH2 * HQ2 * pairs
+
+
+def c2_rotating_sets(world):
+    """Input sets the headline rotates over so that one rotation exceeds the L2 (3x its 126 MB)."""
+    hq_l, hkv_l = HQ2 // world, max(1, HKV2 // world)
+    set_bytes = S2 * (hq_l * DH2 * 2 * 2 + hkv_l * DH2 * 2 * 4)
+    return int(min(64, max(4, math.ceil(3 * L2_BYTES / set_bytes))))
 
 
 def config2_desc(world):
@@ -519,8 +520,7 @@ def bench_prefill(args, torch, dist, rank, world, dev):
     sh = kv_shard(rank, world, hkv, hq)
     hkv_l, hq_l = sh.kv1 - sh.kv0, sh.q1 - sh.q0
     scale = 1.0 / math.sqrt(dh)
-    set_bytes = S * (hq_l * dh * 2 * 2 + hkv_l * dh * 2 * 4)
-    R = int(min(64, max(4, math.ceil(3 * L2_BYTES / set_bytes))))
+    R = c2_rotating_sets(world)
     g = torch.Generator(device=dev)
     g.manual_seed(1234 + rank)
     sets = []
@@ -620,6 +620,7 @@ def bench_prefill(args, torch, dist, rank, world, dev):
         ms, kernel_ms = float(tt[0]), float(tt[1])
     ms_step = ms / args.steps
     value = c2_flops() / (ms_step * 1e-3) / 1e12
+    parity = sharded_parity(torch, dist, dev, rank, world, sets[0], step, shared) if comm is not None else None
     collective = None
     if comm is not None:
         n_cmp = max(3, args.steps // 4)
@@ -734,7 +735,41 @@ def bench_prefill(args, torch, dist, rank, world, dev):
             "collective": collective,
             "e2e": {"value": c2_flops() / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
-            "clocks": clk.summary(), "gpu_launches": launches, "rotating_sets": R}
+            "clocks": clk.summary(), "gpu_launches": launches, "rotating_sets": R, "parity": parity}
+
+
+def sharded_parity(torch, dist, dev, rank, world, set0, step, shared):
+    """Correctness of one sharded step: every rank runs step 0 (its heads of every
+    row stored into all ranks' buffer 0), the ranks all-gather their inputs, and
+    rank 0 compares the assembled rows with one GPU's unsharded attention of the
+    same inputs (fp32 output).  A row element passes within the north star's
+    2e-3 plus the bf16 rounding of the sharded output (2^-8 of its magnitude)."""
+    from hero_b200 import nm
+
+    q, k, v = set0[0], set0[1], set0[2]
+    step(0)
+    dist.barrier()
+    torch.cuda.synchronize(dev)
+    got = shared[0].tensor().float() if rank == 0 else None
+    parts = [[torch.empty_like(x) for _ in range(world)] for x in (q, k, v)]
+    for lst, x in zip(parts, (q, k, v)):
+        dist.all_gather(lst, x)
+    res = None
+    if rank == 0:
+        Q, K, V = (torch.cat(lst, dim=1) for lst in parts)
+        cache = nm.FullAttentionCache(HKV2, DH2, capacity=S2, dtype="bf16", device=dev.index)
+        cache.append(0, K, V)
+        ref = nm.attend(cache, Q, 0, 1.0 / math.sqrt(DH2), out_dtype=torch.float32)
+        err = (got - ref).abs()
+        ok = bool((err <= 2e-3 + ref.abs() * 2.0 ** -8).all().item())
+        rel = float((got - ref).norm() / ref.norm())
+        res = {"ok": ok, "max_abs": float(err.max()), "rel_l2": rel,
+               "vs": "one GPU's unsharded attention of the gathered inputs, fp32 output",
+               "rule": "|sharded - ref| <= 2e-3 + 2^-8 |ref| for every element"}
+        del cache
+    torch.cuda.synchronize(dev)
+    dist.barrier()
+    return res
 
 
 # ---------------------------------------------------------------- extras (N=1)
@@ -1506,6 +1541,46 @@ def sharded_extras(torch, dist, dev, rank, world):
 
 # ---------------------------------------------------------------- main
 
+def _sig(x, n=4):
+    return float(f"{x:.{n}g}") if isinstance(x, (int, float)) and math.isfinite(x) else x
+
+
+def summarize_extras(extra):
+    """One short entry per measured workload of `extra`: its value and unit, the
+    roofline fraction of its dominant kernel, the CPU baseline beside it and the
+    parity verdict (multi-GPU), small enough to keep the headline line compact."""
+    out = {}
+
+    def visit(path, ent):
+        if not isinstance(ent, dict):
+            return
+        if "error" in ent:
+            out[path] = {"error": str(ent["error"])[:120]}
+            return
+        roof = ent.get("roofline") if isinstance(ent.get("roofline"), dict) else None
+        if "value" in ent or roof:
+            e = {}
+            if "value" in ent:
+                e["value"], e["unit"] = _sig(ent["value"]), ent.get("unit") or (roof or {}).get("unit")
+            elif "ms" in ent:
+                e["ms"] = _sig(ent["ms"])
+            if roof and "frac" in roof:
+                e["frac"] = _sig(roof["frac"], 3)
+            cb = ent.get("cpu_baseline")
+            if isinstance(cb, dict) and "value" in cb:
+                e["cpu"] = [_sig(cb["value"]), cb.get("unit"), cb.get("cores")]
+            if isinstance(ent.get("parity"), dict):
+                e["parity_ok"] = ent["parity"].get("ok")
+            out[path] = e
+        for k, v in ent.items():
+            if isinstance(v, dict) and k not in ("roofline", "cpu_baseline", "parity", "clocks", "collective"):
+                visit(f"{path}.{k}", v)
+
+    for name, ent in extra.items():
+        visit(name, ent)
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -1583,14 +1658,23 @@ def main():
                "kind": ref.kind, "sample": ref.sample + f", {len(secs)} timed runs",
                "seconds_per_sample": float(np.mean(secs))}
     if rank == 0:
+        # The measured extras in full on their own line first; the headline
+        # line last, compact, with a one-entry-per-workload summary of them.
+        if extra:
+            print(json.dumps({"bench_extras": extra, "n_gpus": world}), flush=True)
         line = {"metric": METRIC, "value": res["value"], "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": res["ms_per_step"], "higher_is_better": True,
                 "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (torch.randn, seeded)",
                 "config": {**config2_desc(world), "rotating_sets": res["rotating_sets"]},
                 "tok_per_s": res["tok_per_s"], "roofline": res["roofline"], "cpu_baseline": cpu, "e2e": res["e2e"],
-                "clocks": res["clocks"], "gpu_launches": res["gpu_launches"], "extra": extra}
+                "clocks": res["clocks"], "gpu_launches": res["gpu_launches"]}
+        if res.get("parity") is not None:
+            line["parity_ok"] = res["parity"]["ok"]
+            line["parity"] = res["parity"]
         if res.get("collective"):
             line["collective"] = res["collective"]
+        if extra:
+            line["extra_summary"] = summarize_extras(extra)
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()

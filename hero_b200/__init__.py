@@ -6,8 +6,8 @@ operator interface over that ABI.
 """
 from ._lib import (  # noqa: F401
     BF16, F16, F32, CommError, CudaError, DeviceTimeout, InvalidArgument, LengthError, LogicError, NmgError,
-    NoVisibleKeys, OutOfRange, Unsupported, lib,
+    NoVisibleKeys, OutOfRange, Unsupported, ValueOverflow, lib,
 )
 
 __all__ = ["lib", "nm", "NmgError", "InvalidArgument", "OutOfRange", "NoVisibleKeys", "LengthError", "LogicError",
-           "CudaError", "DeviceTimeout", "CommError", "Unsupported", "F32", "F16", "BF16"]
+           "CudaError", "DeviceTimeout", "CommError", "Unsupported", "ValueOverflow", "F32", "F16", "BF16"]

@@ -14,7 +14,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libnmg.so")
 
 OK, INVALID_ARGUMENT, OUT_OF_RANGE, RUNTIME_ERROR, LENGTH_ERROR, LOGIC_ERROR = 0, 1, 2, 3, 4, 5
-CUDA_ERROR, DEVICE_TIMEOUT, COMM_ERROR, UNSUPPORTED = 6, 7, 8, 9
+CUDA_ERROR, DEVICE_TIMEOUT, COMM_ERROR, UNSUPPORTED, VALUE_OVERFLOW = 6, 7, 8, 9, 10
 F32, F16, BF16 = 0, 1, 2
 
 
@@ -72,8 +72,14 @@ class Unsupported(NmgError, NotImplementedError):
     status = UNSUPPORTED
 
 
+class ValueOverflow(NmgError, ArithmeticError):
+    """A V value beyond fp16's range reached a bf16 cache (which keeps V as fp16)."""
+
+    status = VALUE_OVERFLOW
+
+
 _ERRORS = {c.status: c for c in (InvalidArgument, OutOfRange, NoVisibleKeys, LengthError, LogicError, CudaError,
-                                 DeviceTimeout, CommError, Unsupported)}
+                                 DeviceTimeout, CommError, Unsupported, ValueOverflow)}
 
 _lock = threading.Lock()
 _lib = None
@@ -87,6 +93,7 @@ _i64p = ctypes.POINTER(ctypes.c_int64)
 # name -> (argtypes)
 SIGNATURES = {
     "nmg_device_status": [_i32, _vp],
+    "nmg_selftest_wait_timeout": [_i32, _i32, _vp],
     "nmg_kv_create": [_i32, _i32, _i32, _i64, _i64, _i32, ctypes.POINTER(_vp)],
     "nmg_kv_destroy": [_vp],
     "nmg_kv_append": [_vp, _i64, _vp, _vp, _i64, _i32, _vp],

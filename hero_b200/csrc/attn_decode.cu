@@ -361,13 +361,9 @@ int launch_split(const SplitArgs& a, dim3 grid, cudaStream_t s) {
     constexpr int W = warps_for<KVDT, DH, G>();
     using C = SplitCfg<KVDT, DH, G, W>;
     auto kern = attn_split_kernel<KVDT, DH, G, W>;
-    static unsigned attr_set = 0;  // one bit per device
-    int dev_id = 0;
-    NMG_CUDA_TRY(cudaGetDevice(&dev_id));
-    if (!(attr_set & (1u << (dev_id & 31)))) {
-        NMG_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
-        attr_set |= 1u << (dev_id & 31);
-    }
+    static std::atomic<uint64_t> attr_set{0};  // one bit per device
+    const int st = set_smem_once(kern, C::SMEM, attr_set);
+    if (st != NMG_OK) return st;
     kern<<<grid, W * 32, C::SMEM, s>>>(a);
     NMG_CUDA_TRY(cudaGetLastError());
     return NMG_OK;
@@ -594,11 +590,15 @@ int attend_batch_split(const nmg_kv_cache* const* caches, int batch, const int64
 // The array is shared by every call in the process on a given device and keeps
 // what the last call left; calls whose kernels overlap on that device (two
 // streams, two host threads) race on it and must be serialised by the caller.
+//
+// Layout: [0, 256) the path's error word (a wait that gave up raises it; only
+// nmg_device_status reads and clears it), then the row tickets (cleared by
+// every call), then the split partials.
 namespace nmg {
 namespace {
 
 constexpr size_t kNoallocScratchBytes = size_t(4) << 20;  // 4 MiB per device, held until exit
-constexpr size_t kNoallocFlagBytes = 256;                   // device-side wait flag, then the counters
+constexpr size_t kNoallocFlagBytes = 256;                   // the error word, then the tickets
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoallocScratchBytes];
 
@@ -622,6 +622,20 @@ int noalloc_scratch(int device, void** ptr) {
 }
 
 }  // namespace
+
+int* noalloc_error_word(int device) {
+    if (device < 0 || device >= 64) return nullptr;
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    return (int*)g_noalloc_addr[device];
+}
+
+int noalloc_error_word_init(int device, int** word) {
+    void* base = nullptr;
+    const int st = noalloc_scratch(device, &base);
+    *word = (int*)base;
+    return st;
+}
+
 }  // namespace nmg
 
 extern "C" int nmg_attend_noalloc(const nmg_kv_cache* c, int hq, const void* q, int q_dtype, int64_t rows,
@@ -650,7 +664,6 @@ extern "C" int nmg_attend_noalloc(const nmg_kv_cache* c, int hq, const void* q, 
     void* base = nullptr;
     int st = noalloc_scratch(c->device, &base);
     if (st == NMG_OK) {
-        // Same work split as nmg_attend's decode path.
         const int gtot = hq / c->hkv, gt = pick_gt(gtot), zdim = gtot / gt;
         int64_t longest = 0, total_keys = 0;
         for (int64_t t = 0; t < rows; ++t) {
@@ -658,17 +671,27 @@ extern "C" int nmg_attend_noalloc(const nmg_kv_cache* c, int hq, const void* q, 
             longest = std::max(longest, sp.hi - sp.lo + 1);
             total_keys += sp.hi - sp.lo + 1;
         }
-        const int64_t split_len = pick_split_len(total_keys * c->hkv * zdim, warps_runtime(c->dtype, c->dh));
+        // Work items the fixed array holds after the error word and the
+        // tickets; nmg_attend's split length when they fit, otherwise longer
+        // splits (fewer partials) so that every row's splits fit.
+        const int warps = warps_runtime(c->dtype, c->dh);
+        const int64_t tile = 32 * warps;
+        const int64_t cnt_bytes = rows * c->hkv * zdim * 4;
+        const int64_t cnt_span = (cnt_bytes + 255) / 256 * 256;
+        const int64_t item_bytes = (int64_t)c->hkv * zdim * gt * (c->dh + 2) * 4;
+        const int64_t avail = (int64_t)kNoallocScratchBytes - (int64_t)kNoallocFlagBytes - cnt_span;
+        const int64_t max_items = avail > 0 ? avail / item_bytes : 0;
+        const int64_t splits_cap = max_items / rows;
+        int64_t split_len = pick_split_len(total_keys * c->hkv * zdim, warps);
+        if (splits_cap >= 1 && (longest + split_len - 1) / split_len > splits_cap)
+            split_len = ((longest + splits_cap - 1) / splits_cap + tile - 1) / tile * tile;
         const int64_t max_splits = (longest + split_len - 1) / split_len;
         const int64_t work = rows * max_splits;
-        const int64_t cnt_bytes = rows * c->hkv * zdim * 4;
-        const size_t need = kNoallocFlagBytes + (size_t)(cnt_bytes + 255) / 256 * 256 +
-                            (size_t)work * c->hkv * zdim * gt * (c->dh + 2) * 4;
-        if (need > kNoallocScratchBytes || work > (int64_t)0x7FFFFFFF) {
+        if (splits_cap < 1 || work > max_items || work > (int64_t)0x7FFFFFFF) {
             st = set_error(NMG_LENGTH_ERROR,
-                           "nmg_attend_noalloc: this call needs %zu bytes of scratch, more than the fixed %zu; "
-                           "use nmg_attend or fewer query rows",
-                           need, kNoallocScratchBytes);
+                           "nmg_attend_noalloc: %lld query rows need more scratch than the fixed %zu bytes hold "
+                           "(at most %lld rows of %d query heads at head_dim %d); use nmg_attend or fewer rows",
+                           (long long)rows, kNoallocScratchBytes, (long long)max_items, hq, c->dh);
         } else {
             SplitArgs a;  // on the stack: nothing is allocated
             a.mode = 0;
@@ -694,12 +717,12 @@ extern "C" int nmg_attend_noalloc(const nmg_kv_cache* c, int hq, const void* q, 
             a.out = out;
             a.out_dtype = out_dtype;
             a.scale = use_scale ? scale : 1.f;
-            a.err = (int*)base;
+            a.err = (int*)base;  // never cleared here: nmg_device_status reports it
             a.counters = (int*)((char*)base + kNoallocFlagBytes);
-            a.part = (float*)((char*)base + kNoallocFlagBytes + (cnt_bytes + 255) / 256 * 256);
+            a.part = (float*)((char*)base + kNoallocFlagBytes + cnt_span);
             // The row tickets must start at zero; a kernel that gave up a
-            // wait may have left some set, so clear them (and the flag).
-            cudaError_t e = cudaMemsetAsync(base, 0, kNoallocFlagBytes + (size_t)cnt_bytes, (cudaStream_t)stream);
+            // wait may have left some set, so clear them (not the error word).
+            cudaError_t e = cudaMemsetAsync(a.counters, 0, (size_t)cnt_bytes, (cudaStream_t)stream);
             if (e != cudaSuccess)
                 st = set_error(NMG_CUDA_ERROR, "nmg_attend_noalloc: cudaMemsetAsync: %s", cudaGetErrorString(e));
             else

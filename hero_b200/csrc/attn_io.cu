@@ -51,6 +51,7 @@ struct QkArgs {
     int64_t slots, slot0, row0, kv_rows;  // tokens row0 .. kv_rows-1 are written, token row0 to slot0
     int64_t T, position, rows;
     int hq, hkv, dh, q_dtype, kv_dtype, q_pair, v_norm;
+    int* err;  // device error flag: a bf16 cache's V overflowing fp16
     int idx32;  // row and slot arithmetic fits 32 bits (one divide instead of a 64-bit sequence)
     float eps;
     float inv_freq[kMaxPlanes];
@@ -70,15 +71,17 @@ __device__ __forceinline__ void load_vec(const float* p, float* x) {
 }
 
 // VW values to element i.. of a row buffer of dtype dt (v_cache: the V rule of
-// a bf16 cache, bf16-rounded values stored as fp16).
+// a bf16 cache, bf16-rounded values stored as fp16).  Returns true when such a
+// V value overflowed fp16.
 template <int VW>
-__device__ __forceinline__ void store_vec(void* base, int dt, int64_t i, const float* x, bool v_cache) {
+__device__ __forceinline__ bool store_vec(void* base, int dt, int64_t i, const float* x, bool v_cache) {
+    bool overflow = false;
     if (dt == NMG_F32) {
         float* p = (float*)base + i;
         if constexpr (VW == 4) *reinterpret_cast<float4*>(p) = make_float4(x[0], x[1], x[2], x[3]);
         else if constexpr (VW == 2) *reinterpret_cast<float2*>(p) = make_float2(x[0], x[1]);
         else *p = x[0];
-        return;
+        return overflow;
     }
     uint32_t b[VW];
     if (dt == NMG_BF16 && !v_cache && VW >= 2) {
@@ -97,8 +100,7 @@ __device__ __forceinline__ void store_vec(void* base, int dt, int64_t i, const f
 #pragma unroll
         for (int w = 0; w < VW; ++w) {
             if (dt == NMG_BF16)
-                b[w] = v_cache ? dev::f32_to_f16_bits(dev::bf16_bits_to_f32(dev::f32_to_bf16_bits(x[w])))
-                               : dev::f32_to_bf16_bits(x[w]);
+                b[w] = v_cache ? cache_v_bits(x[w], overflow) : dev::f32_to_bf16_bits(x[w]);
             else
                 b[w] = dev::f32_to_f16_bits(x[w]);
         }
@@ -107,6 +109,7 @@ __device__ __forceinline__ void store_vec(void* base, int dt, int64_t i, const f
     if constexpr (VW == 4) *reinterpret_cast<uint2*>(p) = make_uint2(b[0] | (b[1] << 16), b[2] | (b[3] << 16));
     else if constexpr (VW == 2) *reinterpret_cast<uint32_t*>(p) = b[0] | (b[1] << 16);
     else *p = (uint16_t)b[0];
+    return overflow;
 }
 
 // The row space is token-major: token t's rows are its Hq Q heads, its Hkv K
@@ -153,8 +156,11 @@ __device__ __forceinline__ void finish_row(const QkArgs& a, const Row& w, float 
     constexpr int J = 2 * M;
     const int kv_dt = a.slots ? a.kv_dtype : NMG_F32;
     if (w.kind == 2 && !a.v_norm) {
+        bool overflow = false;
 #pragma unroll
-        for (int j = 0; j < J; ++j) store_vec<VW>(a.v_dst, kv_dt, w.dst + 32 * VW * j + VW * lane, x[j], true);
+        for (int j = 0; j < J; ++j)
+            overflow |= store_vec<VW>(a.v_dst, kv_dt, w.dst + 32 * VW * j + VW * lane, x[j], true);
+        if (overflow && a.err) atomicOr(a.err, dev::kErrF16Overflow);
         return;
     }
     float ss = 0.f;
@@ -165,12 +171,14 @@ __device__ __forceinline__ void finish_row(const QkArgs& a, const Row& w, float 
     ss = dev::warp_sum(ss);
     const float inv = 1.f / sqrtf(ss / (float)a.dh + a.eps);  // components.hpp:174, :212
     if (w.kind == 2) {
+        bool overflow = false;
 #pragma unroll
         for (int j = 0; j < J; ++j) {
 #pragma unroll
             for (int e = 0; e < VW; ++e) x[j][e] *= inv;
-            store_vec<VW>(a.v_dst, kv_dt, w.dst + 32 * VW * j + VW * lane, x[j], true);
+            overflow |= store_vec<VW>(a.v_dst, kv_dt, w.dst + 32 * VW * j + VW * lane, x[j], true);
         }
+        if (overflow && a.err) atomicOr(a.err, dev::kErrF16Overflow);
         return;
     }
     const float* gamma = w.kind == 0 ? a.q_gamma : a.k_gamma;
@@ -338,6 +346,7 @@ struct KvDst {
     void* v = nullptr;  // null: V is left to the caller (prepare without v_norm)
     int dtype = NMG_F32;
     int64_t slots = 0, slot0 = 0, row0 = 0, rows = 0;
+    int* err = nullptr;  // the device error flag (a cache destination)
 };
 
 template <int VW, int M>
@@ -394,6 +403,7 @@ int launch_prepare(const char* who, int hq, int hkv, int dh, int64_t position, i
     a.q_pair = q_gated ? 2 : 1;
     a.v_norm = v_norm ? 1 : 0;
     a.eps = eps;
+    a.err = d.err;
     a.rows = T * (int64_t)(hq + (d.v ? 2 : 1) * hkv);
     a.idx32 = a.rows < (1ll << 31) && d.slot0 + T < (1ll << 31) && d.slots < (1ll << 31) ? 1 : 0;
     // RotaryEmbedding's table (attention.hpp:76-80): double pow, then fp32;
@@ -466,9 +476,12 @@ extern "C" int nmg_attn_prologue(nmg_kv_cache* cache, int hq, int64_t position, 
     if (T <= 0) return T < 0 ? set_error(NMG_INVALID_ARGUMENT, "nmg_attn_prologue: negative rows") : NMG_OK;
     if (!q || !k || !v || !q_gamma || !k_gamma || !q_out)  // before the cache's bookkeeping moves
         return set_error(NMG_INVALID_ARGUMENT, "nmg_attn_prologue: null argument");
+    int* err = nullptr;  // made with the cache, so no allocation here
+    int st = device_error_flag(cache->device, &err);
+    if (st != NMG_OK) return st;
     int64_t accepted = 0;
     int deferred = NMG_OK;
-    int st = kv_append_begin(cache, position, T, &accepted, &deferred);
+    st = kv_append_begin(cache, position, T, &accepted, &deferred);
     if (st != NMG_OK) return st;
     int prev = 0;
     NMG_CUDA_TRY(cudaGetDevice(&prev));
@@ -478,6 +491,7 @@ extern "C" int nmg_attn_prologue(nmg_kv_cache* cache, int hq, int64_t position, 
     d.v = cache->v;
     d.dtype = cache->dtype;
     d.slots = cache->slots;
+    d.err = err;
     d.rows = accepted;
     kv_append_slots(cache, position, accepted, &d.row0, &d.slot0);
     st = launch_prepare("nmg_attn_prologue", hq, cache->hkv, cache->dh, position, T, q, q_gated, k, v, q_gamma, k_gamma,

@@ -782,13 +782,9 @@ template <int DH, bool BF16>
 int launch_prefill(const PrefillArgs& a, dim3 grid, cudaStream_t s) {
     using C = PfCfg<DH>;
     auto kern = attn_prefill_kernel<DH, BF16>;
-    static unsigned attr_set = 0;
-    int dev_id = 0;
-    NMG_CUDA_TRY(cudaGetDevice(&dev_id));
-    if (!(attr_set & (1u << (dev_id & 31)))) {
-        NMG_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
-        attr_set |= 1u << (dev_id & 31);
-    }
+    static std::atomic<uint64_t> attr_set{0};  // one bit per device
+    const int st = set_smem_once(kern, C::SMEM, attr_set);
+    if (st != NMG_OK) return st;
     kern<<<grid, C::THREADS, C::SMEM, s>>>(a);
     NMG_CUDA_TRY(cudaGetLastError());
     return NMG_OK;

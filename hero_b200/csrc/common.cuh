@@ -13,6 +13,8 @@
 #include <cuda_fp16.h>
 #include <stdint.h>
 
+#include <atomic>
+
 #include "../../include/nmg.h"
 
 // ---------------------------------------------------------------- host side
@@ -44,11 +46,32 @@ int device_staging(int device, size_t bytes, void** ptr);
 // that takes a ticket returns it to zero before it exits, so the pool is all
 // zeros between launches; nothing else may write it.
 int device_tickets(int device, size_t bytes, void** ptr);
-// A zero-initialised int32 error flag per device (device-side wait timeouts).
+// A zero-initialised int32 error flag per device.  Kernels OR bits into it
+// (dev::kErrWaitTimeout, dev::kErrF16Overflow); nmg_device_status reports them.
 int device_error_flag(int device, int** flag);
-// Copies the device error flag back (synchronising `stream`), clears it, and
-// turns a non-zero value into NMG_DEVICE_TIMEOUT.
+// Copies the device error flags back (synchronising `stream`), clears them,
+// and turns a raised bit into NMG_DEVICE_TIMEOUT or NMG_VALUE_OVERFLOW.  Reads
+// only flags that already exist: it allocates nothing.
 int check_device_flag(int device, cudaStream_t stream);
+// The no-allocation decode path's own error word (inside its fixed device
+// array), or null when that path never ran on `device`; _init looks it up
+// (no allocation) with `device` current.
+int* noalloc_error_word(int device);
+int noalloc_error_word_init(int device, int** word);
+
+// cudaFuncSetAttribute(MaxDynamicSharedMemorySize) once per device and kernel;
+// `done` holds one bit per device (devices 64 and up set it on every call).
+// Safe to call from several host threads.
+template <typename Kernel>
+int set_smem_once(Kernel kern, int bytes, std::atomic<uint64_t>& done) {
+    int dev_id = 0;
+    NMG_CUDA_TRY(cudaGetDevice(&dev_id));
+    const uint64_t bit = dev_id < 64 ? (uint64_t(1) << dev_id) : 0;
+    if (bit && (done.load(std::memory_order_acquire) & bit)) return NMG_OK;
+    NMG_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+    if (bit) done.fetch_or(bit, std::memory_order_acq_rel);
+    return NMG_OK;
+}
 
 // cuTensorMapEncodeTiled through the runtime's driver entry point (no -lcuda);
 // null when the driver does not provide it.
@@ -64,7 +87,9 @@ EncodeTiledFn encode_tiled_fn();
 namespace nmg {
 namespace dev {
 
-constexpr int kErrWaitTimeout = 1;
+// Bits of the device error flag.
+constexpr int kErrWaitTimeout = 1;  // a bounded wait gave up
+constexpr int kErrF16Overflow = 2;  // a finite bf16 V value beyond fp16's range reached a bf16 cache
 constexpr long long kMaxPolls = 1ll << 22;  // ~ a second or so of polling before giving up
 
 // fp32 -> bf16, round to nearest even, quiet NaN (core.hpp:92-100).
@@ -194,12 +219,16 @@ __device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
 // remaining work and fall through to their normal exit.  A phase that has
 // already completed is seen by the non-blocking probe, which costs far less
 // than a try_wait.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err_flag) {
+template <long long kPolls>
+__device__ __forceinline__ bool mbar_wait_n(uint64_t* bar, uint32_t parity, int* err_flag) {
     if (mbar_test_wait(bar, parity)) return true;
-    for (long long i = 0; i < kMaxPolls; ++i)
+    for (long long i = 0; i < kPolls; ++i)
         if (mbar_try_wait(bar, parity)) return true;
-    if (err_flag) atomicExch(err_flag, kErrWaitTimeout);
+    if (err_flag) atomicOr(err_flag, kErrWaitTimeout);
     return false;
+}
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err_flag) {
+    return mbar_wait_n<kMaxPolls>(bar, parity, err_flag);
 }
 
 // Untiled bulk copy global -> shared, completion counted on `bar` in bytes.

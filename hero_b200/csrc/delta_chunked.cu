@@ -760,13 +760,9 @@ int delta_prefill_chunked(nmg_delta_state* st, int hk, int64_t T, const float* q
     sa.nchunks = nchunks;
     sa.err = err;
 
-    static unsigned attr_set = 0;
-    const unsigned dbit = 1u << (st->device & 31);
-    if (!(attr_set & dbit)) {
-        NMG_CUDA_TRY(cudaFuncSetAttribute(delta_wy_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, P1_SMEM));
-        NMG_CUDA_TRY(cudaFuncSetAttribute(delta_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, P2_SMEM));
-        attr_set |= dbit;
-    }
+    static std::atomic<uint64_t> wy_set{0}, scan_set{0};  // one bit per device
+    if ((rc = set_smem_once(delta_wy_kernel, P1_SMEM, wy_set)) != NMG_OK) return rc;
+    if ((rc = set_smem_once(delta_scan_kernel, P2_SMEM, scan_set)) != NMG_OK) return rc;
     // one CTA per (key head, chunk), the key heads of a chunk side by side
     delta_wy_kernel<<<(unsigned)((int64_t)nchunks * hk), 128, P1_SMEM, stream>>>(wa);
     NMG_CUDA_TRY(cudaGetLastError());

@@ -24,8 +24,9 @@ namespace {
 template <int SRC, int DST>
 __global__ void kv_append_kernel(const void* __restrict__ keys, const void* __restrict__ values, void* __restrict__ kc,
                                  void* __restrict__ vc, int64_t rows, int64_t src_row0, int hkv, int dh, int64_t slots,
-                                 int64_t slot0) {
+                                 int64_t slot0, int* __restrict__ err) {
     const int chunks = (dh + 7) / 8;
+    bool overflow = false;
     const int64_t total = rows * hkv * chunks;
     for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
         const int c = (int)(t % chunks);
@@ -43,10 +44,11 @@ __global__ void kv_append_kernel(const void* __restrict__ keys, const void* __re
                 const float kf = dev::load_as_f32(keys, SRC, src + d0 + e);
                 const float vf = dev::load_as_f32(values, SRC, src + d0 + e);
                 dev::store_from_f32(kc, DST, dst + d0 + e, kf);
-                store_cache_v(vc, DST, dst + d0 + e, vf);
+                store_cache_v(vc, DST, dst + d0 + e, vf, overflow);
             }
         }
     }
+    if (overflow) atomicOr(err, dev::kErrF16Overflow);
 }
 
 // Same-dtype fast path: 16-byte vector copies when a head row is a multiple of
@@ -54,8 +56,10 @@ __global__ void kv_append_kernel(const void* __restrict__ keys, const void* __re
 template <bool V_TO_F16>
 __global__ void kv_append_copy16_kernel(const uint4* __restrict__ keys, const uint4* __restrict__ values,
                                         uint4* __restrict__ kc, uint4* __restrict__ vc, int64_t rows, int64_t src_row0,
-                                        int hkv, int vecs_per_head, int64_t slots, int64_t slot0) {
+                                        int hkv, int vecs_per_head, int64_t slots, int64_t slot0,
+                                        int* __restrict__ err) {
     const int64_t total = rows * hkv * vecs_per_head;
+    bool overflow = false;
     for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
         const int c = (int)(t % vecs_per_head);
         const int64_t rh = t / vecs_per_head;
@@ -70,25 +74,26 @@ __global__ void kv_append_copy16_kernel(const uint4* __restrict__ keys, const ui
             uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
-                const uint32_t lo = dev::f32_to_f16_bits(dev::bf16_bits_to_f32(w[i] & 0xFFFFu));
-                const uint32_t hi = dev::f32_to_f16_bits(dev::bf16_bits_to_f32(w[i] >> 16));
+                const uint32_t lo = cache_v_from_bf16(w[i] & 0xFFFFu, overflow);
+                const uint32_t hi = cache_v_from_bf16(w[i] >> 16, overflow);
                 w[i] = lo | (hi << 16);
             }
             v = make_uint4(w[0], w[1], w[2], w[3]);
         }
         vc[dst] = v;
     }
+    if (V_TO_F16 && overflow) atomicOr(err, dev::kErrF16Overflow);
 }
 
 template <int SRC>
 int launch_append(int dst, const void* k, const void* v, void* kc, void* vc, int64_t rows, int64_t row0, int hkv,
-                  int dh, int64_t slots, int64_t slot0, cudaStream_t s, int blocks) {
+                  int dh, int64_t slots, int64_t slot0, cudaStream_t s, int blocks, int* err) {
     if (dst == NMG_F32)
-        kv_append_kernel<SRC, NMG_F32><<<blocks, 256, 0, s>>>(k, v, kc, vc, rows, row0, hkv, dh, slots, slot0);
+        kv_append_kernel<SRC, NMG_F32><<<blocks, 256, 0, s>>>(k, v, kc, vc, rows, row0, hkv, dh, slots, slot0, err);
     else if (dst == NMG_F16)
-        kv_append_kernel<SRC, NMG_F16><<<blocks, 256, 0, s>>>(k, v, kc, vc, rows, row0, hkv, dh, slots, slot0);
+        kv_append_kernel<SRC, NMG_F16><<<blocks, 256, 0, s>>>(k, v, kc, vc, rows, row0, hkv, dh, slots, slot0, err);
     else
-        kv_append_kernel<SRC, NMG_BF16><<<blocks, 256, 0, s>>>(k, v, kc, vc, rows, row0, hkv, dh, slots, slot0);
+        kv_append_kernel<SRC, NMG_BF16><<<blocks, 256, 0, s>>>(k, v, kc, vc, rows, row0, hkv, dh, slots, slot0, err);
     return NMG_OK;
 }
 
@@ -102,6 +107,10 @@ int kv_append_device(nmg_kv_cache* c, int64_t first_position, const void* keys, 
     int64_t row0 = 0, slot0 = 0;
     kv_append_slots(c, first_position, rows, &row0, &slot0);
     const int64_t write = rows - row0;
+    // Created with the cache (nmg_kv_create), so this never allocates.
+    int* err = nullptr;
+    const int fst = device_error_flag(c->device, &err);
+    if (fst != NMG_OK) return fst;
     int prev = 0;
     NMG_CUDA_TRY(cudaGetDevice(&prev));
     if (prev != c->device) NMG_CUDA_TRY(cudaSetDevice(c->device));
@@ -113,23 +122,23 @@ int kv_append_device(nmg_kv_cache* c, int64_t first_position, const void* keys, 
         if (c->vdtype != c->dtype)
             kv_append_copy16_kernel<true><<<blocks, 256, 0, stream>>>((const uint4*)keys, (const uint4*)values,
                                                                       (uint4*)c->k, (uint4*)c->v, write, row0, c->hkv,
-                                                                      vecs, c->slots, slot0);
+                                                                      vecs, c->slots, slot0, err);
         else
             kv_append_copy16_kernel<false><<<blocks, 256, 0, stream>>>((const uint4*)keys, (const uint4*)values,
                                                                        (uint4*)c->k, (uint4*)c->v, write, row0, c->hkv,
-                                                                       vecs, c->slots, slot0);
+                                                                       vecs, c->slots, slot0, err);
     } else {
         const int64_t work = write * c->hkv * ((c->dh + 7) / 8);
         const int blocks = (int)((work + 255) / 256 < 148 * 16 ? (work + 255) / 256 : 148 * 16);
         if (src_dtype == NMG_F32)
             launch_append<NMG_F32>(c->dtype, keys, values, c->k, c->v, write, row0, c->hkv, c->dh, c->slots, slot0,
-                                   stream, blocks);
+                                   stream, blocks, err);
         else if (src_dtype == NMG_F16)
             launch_append<NMG_F16>(c->dtype, keys, values, c->k, c->v, write, row0, c->hkv, c->dh, c->slots, slot0,
-                                   stream, blocks);
+                                   stream, blocks, err);
         else
             launch_append<NMG_BF16>(c->dtype, keys, values, c->k, c->v, write, row0, c->hkv, c->dh, c->slots, slot0,
-                                    stream, blocks);
+                                    stream, blocks, err);
     }
     NMG_CUDA_TRY(cudaGetLastError());
     if (prev != c->device) NMG_CUDA_TRY(cudaSetDevice(prev));
@@ -167,6 +176,11 @@ extern "C" int nmg_kv_create(int hkv, int head_dim, int dtype, int64_t window, i
     // Zeroed like the reference's ring storage (attention.hpp:363-372).
     if (e == cudaSuccess) e = cudaMemset(c->k, 0, bytes);
     if (e == cudaSuccess) e = cudaMemset(c->v, 0, bytes);
+    // The device's error flag, which appends raise on fp16 overflow of V:
+    // created here so that no later call (possibly under stream capture)
+    // has to allocate it.
+    int* flag = nullptr;
+    if (e == cudaSuccess && nmg::device_error_flag(device, &flag) != NMG_OK) e = cudaErrorMemoryAllocation;
     cudaSetDevice(prev);
     if (e != cudaSuccess) {
         if (c->k) cudaFree(c->k);

@@ -74,11 +74,22 @@ inline void kv_append_slots(const nmg_kv_cache* c, int64_t first, int64_t rows, 
     *slot0 = ((first + *row0 - c->base) % c->slots + c->slots) % c->slots;
 }
 
-// A value stored into a cache of dtype `cache_dtype`.  A bf16 cache holds
-// bf16 values and keeps V as fp16: round to bf16 first, then convert exactly.
-__device__ __forceinline__ void store_cache_v(void* vc, int cache_dtype, int64_t i, float x) {
+// A bf16 cache's V element: x rounded to bf16, then held as fp16 (exact for
+// magnitudes in fp16's normal range).  `overflow` is set when a finite value
+// lands on +-inf (bf16 magnitude 65536 or more; fp16's largest is 65504).
+__device__ __forceinline__ uint16_t cache_v_from_bf16(uint32_t b, bool& overflow) {
+    const uint16_t h = dev::f32_to_f16_bits(dev::bf16_bits_to_f32(b));
+    overflow |= (h & 0x7FFFu) == 0x7C00u && (b & 0x7F80u) != 0x7F80u;
+    return h;
+}
+__device__ __forceinline__ uint16_t cache_v_bits(float x, bool& overflow) {
+    return cache_v_from_bf16(dev::f32_to_bf16_bits(x), overflow);
+}
+
+// A value stored into a V buffer of a cache of dtype `cache_dtype`.
+__device__ __forceinline__ void store_cache_v(void* vc, int cache_dtype, int64_t i, float x, bool& overflow) {
     if (cache_dtype == NMG_BF16)
-        ((uint16_t*)vc)[i] = dev::f32_to_f16_bits(dev::bf16_bits_to_f32(dev::f32_to_bf16_bits(x)));
+        ((uint16_t*)vc)[i] = cache_v_bits(x, overflow);
     else
         dev::store_from_f32(vc, cache_dtype, i, x);
 }

@@ -91,16 +91,29 @@ int device_error_flag(int device, int** flag) {
 }
 
 int check_device_flag(int device, cudaStream_t stream) {
-    int* flag = nullptr;
-    int st = device_error_flag(device, &flag);
-    if (st != NMG_OK) return st;
-    int host = 0;
-    NMG_CUDA_TRY(cudaMemcpyAsync(&host, flag, sizeof(int), cudaMemcpyDeviceToHost, stream));
-    NMG_CUDA_TRY(cudaStreamSynchronize(stream));
-    if (host != 0) {
-        NMG_CUDA_TRY(cudaMemsetAsync(flag, 0, sizeof(int), stream));
-        return set_error(NMG_DEVICE_TIMEOUT, "a device-side wait gave up (code %d)", host);
+    int* lib_flag = nullptr;
+    {
+        std::lock_guard<std::mutex> lk(g_mu);
+        if ((int)g_dev.size() > device) lib_flag = g_dev[device].error_flag;
     }
+    int* words[2] = {lib_flag, noalloc_error_word(device)};
+    int raised = 0;
+    for (int* w : words) {
+        if (!w) continue;  // never created: nothing on this device could have raised it
+        int host = 0;
+        NMG_CUDA_TRY(cudaMemcpyAsync(&host, w, sizeof(int), cudaMemcpyDeviceToHost, stream));
+        NMG_CUDA_TRY(cudaStreamSynchronize(stream));
+        if (host != 0) NMG_CUDA_TRY(cudaMemsetAsync(w, 0, sizeof(int), stream));
+        raised |= host;
+    }
+    if (raised) NMG_CUDA_TRY(cudaStreamSynchronize(stream));
+    if (raised & dev::kErrWaitTimeout)
+        return set_error(NMG_DEVICE_TIMEOUT, "a device-side wait gave up (flags 0x%x)", raised);
+    if (raised & dev::kErrF16Overflow)
+        return set_error(NMG_VALUE_OVERFLOW,
+                         "a V value beyond fp16's range (bf16 magnitude >= 65536) was appended to a bf16 cache, which keeps V as "
+                         "fp16; it was stored as +-inf");
+    if (raised) return set_error(NMG_RUNTIME_ERROR, "device flag 0x%x", raised);
     return NMG_OK;
 }
 
@@ -116,7 +129,40 @@ EncodeTiledFn encode_tiled_fn() {
     return fn;
 }
 
+namespace {
+
+// Waits on an mbarrier that nothing arrives on, with a short poll limit: the
+// wait gives up, raises the timeout bit of `flag` and the kernel returns,
+// exactly as a kernel whose producer stalled would.  No copy is in flight.
+__global__ void wait_timeout_selftest_kernel(int* flag) {
+    __shared__ __align__(8) uint64_t bar;
+    if (threadIdx.x == 0) {
+        dev::mbar_init(&bar, 1);
+        dev::fence_mbar_init();
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) dev::mbar_wait_n<4096>(&bar, 0, flag);
+}
+
+}  // namespace
+
 }  // namespace nmg
+
+extern "C" int nmg_selftest_wait_timeout(int device, int target, void* stream) {
+    if (target != 0 && target != 1) return nmg::set_error(NMG_INVALID_ARGUMENT, "nmg_selftest_wait_timeout: target %d", target);
+    int prev = 0;
+    NMG_CUDA_TRY(cudaGetDevice(&prev));
+    if (prev != device) NMG_CUDA_TRY(cudaSetDevice(device));
+    int* flag = nullptr;
+    int st = target == 0 ? nmg::device_error_flag(device, &flag) : nmg::noalloc_error_word_init(device, &flag);
+    if (st == NMG_OK) {
+        nmg::wait_timeout_selftest_kernel<<<1, 32, 0, (cudaStream_t)stream>>>(flag);
+        const cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess) st = nmg::set_error(NMG_CUDA_ERROR, "nmg_selftest_wait_timeout: %s", cudaGetErrorString(e));
+    }
+    if (prev != device) cudaSetDevice(prev);
+    return st;
+}
 
 extern "C" const char* nmg_last_error(void) { return nmg::g_last_error; }
 extern "C" const char* nmg_version(void) { return "nmg 0.1 sm_100a"; }

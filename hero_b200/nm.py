@@ -59,7 +59,8 @@ def _dev(t: torch.Tensor) -> torch.Tensor:
 
 
 def device_status(device: int = 0) -> None:
-    """Synchronise and raise DeviceTimeout if a kernel gave up a bounded device-side wait."""
+    """Synchronise; raise DeviceTimeout if a kernel gave up a bounded device-side wait, or
+    ValueOverflow if a V value beyond fp16's range was appended to a bf16 cache."""
     call("nmg_device_status", int(device), _stream(device))
 
 

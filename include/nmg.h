@@ -14,6 +14,7 @@
  *   NMG_DEVICE_TIMEOUT     7  a bounded device-side wait gave up
  *   NMG_COMM_ERROR         8  an NCCL call failed
  *   NMG_UNSUPPORTED        9  shape / dtype combination not built
+ *   NMG_VALUE_OVERFLOW    10  std::overflow_error    (a V value a bf16 cache cannot hold)
  *
  * nmg_last_error() returns the message of the last failure on this thread.
  * The exception types are the ones the reference throws at the cited lines;
@@ -52,6 +53,7 @@ extern "C" {
 #define NMG_DEVICE_TIMEOUT 7
 #define NMG_COMM_ERROR 8
 #define NMG_UNSUPPORTED 9
+#define NMG_VALUE_OVERFLOW 10
 
 /* Element types.  The reference computes in fp32 (Scalar = float,
  * src/core.hpp:31) and rounds to fp16/bf16 with src/core.hpp:61-100; the
@@ -63,12 +65,24 @@ extern "C" {
 NMG_API const char* nmg_last_error(void);
 NMG_API const char* nmg_version(void);
 
-/* Synchronises the current stream of `device` work issued through this
- * library (the legacy default stream is used when stream is NULL) and reports
- * NMG_DEVICE_TIMEOUT if any kernel since the last call gave up a bounded
- * device-side wait (a kernel that gives up returns early instead of hanging).
- * Clears the flag. */
+/* Synchronises `stream` (the legacy default stream when NULL) and reports
+ * what kernels on `device` flagged since the last call, then clears it:
+ *   NMG_DEVICE_TIMEOUT  a kernel gave up a bounded device-side wait (it
+ *                       returned early instead of hanging; its output is not
+ *                       valid), including kernels of nmg_attend_noalloc;
+ *   NMG_VALUE_OVERFLOW  a finite V value whose bf16 rounding has magnitude
+ *                       65536 or more was appended to a bf16 cache, which
+ *                       keeps V as fp16 (largest finite 65504): the stored
+ *                       value became +-inf.
+ * Allocates nothing. */
 NMG_API int nmg_device_status(int device, void* stream);
+
+/* Diagnostic (no counterpart in the reference): launches one kernel that waits
+ * on a barrier nothing completes, with a short poll limit, so the wait gives up
+ * and raises the timeout flag exactly as a stalled kernel would; target 0 is
+ * the library's flag, target 1 the no-allocation path's.  The kernel returns;
+ * nmg_device_status then reports NMG_DEVICE_TIMEOUT. */
+NMG_API int nmg_selftest_wait_timeout(int device, int target, void* stream);
 
 /* ---- device KV cache -------------------------------------------------------
  *

@@ -39,6 +39,7 @@ inline void check(int status) {
         case NMG_OUT_OF_RANGE: throw std::out_of_range(msg);
         case NMG_LENGTH_ERROR: throw std::length_error(msg);
         case NMG_LOGIC_ERROR: throw std::logic_error(msg);
+        case NMG_VALUE_OVERFLOW: throw std::overflow_error(msg);
         default: throw std::runtime_error(msg);  // no visible key, CUDA, NCCL, device timeout
     }
 }
