@@ -41,11 +41,12 @@
 #include <vector>
 #include <stdio.h>
 
-#include "attn.cuh"
-#include "tcgen05.cuh"
+#include "prefill.cuh"
 
 namespace nmg {
 namespace {
+
+using namespace pf;
 
 template <int DH>
 struct PfCfg {
@@ -84,144 +85,6 @@ struct PfCfg {
     static_assert(SMEM <= 232448, "shared memory budget");
     static_assert(STATS_OFF % 8 == 0 && STAGE_OFF % 16 == 0, "vector accesses");
 };
-
-constexpr int kMaxFanout = 8;
-constexpr int kMaxItems = 2048;  // work items of a split launch
-constexpr int kMaxTiles = 1024;  // query tiles of a split launch
-
-struct PrefillArgs {
-    CUtensorMap tm_q;  // (d, head, row) over q [rows][hq*DH]
-    CUtensorMap tm_k;  // (d, hkv*slots) over the cache
-    CUtensorMap tm_v;
-    int64_t rows, first_query, window, floor_pos, newest, base, slots;
-    int hq, hkv, g;
-    float scale_log2;
-    // Output row t of this call goes to outs[i] + t * out_row_elems + out_col0
-    // (elements) for every i < nout: the caller's buffer and, when the heads
-    // are sharded across GPUs, the other GPUs' buffers (peer pointers), so
-    // the gather of head outputs rides on the epilogue's stores.
-    void* outs[kMaxFanout];
-    int nout;
-    int64_t out_row_elems, out_col0;
-    int out_dtype;
-    int* err;
-    // Work list: n_work = (n_items or ntiles) * hq units, heaviest first,
-    // head fastest.  Key splits (n_items > 0): unit u takes items[u / hq] =
-    // tile << 12 | split << 6 | nsplit, key blocks [split * split_blocks,
-    // +split_blocks) of the tile's range.  A split tile's units leave (O, m,
-    // l) partials in part (slot part_base[tile] + split of head h: [BM][DH +
-    // 4] fp32, O then m, l, with rows padded to 16 bytes) and the last one to
-    // finish (ticket per head and tile) merges them.  n_items == 0: one unit
-    // per (tile, head), unit u = tile ntiles - 1 - u / hq of head u % hq.
-    int64_t n_work;
-    int n_items, split_blocks, nparts, ntiles;
-    float* part;
-    int* tickets;
-    uint32_t items[kMaxItems];
-    uint32_t part_base[kMaxTiles];
-};
-
-__device__ __forceinline__ float ex2(float x) {
-    float y;
-    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-    return y;
-}
-
-__device__ __forceinline__ uint32_t pack2(float lo, float hi, bool bf16) {
-    if (bf16) {
-        __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
-        return *reinterpret_cast<uint32_t*>(&v);
-    }
-    __half2 v = __floats2half2_rn(lo, hi);
-    return *reinterpret_cast<uint32_t*>(&v);
-}
-
-// Output conversions with the reference's rounding (dev::f32_to_bf16_bits,
-// dev::f32_to_f16_bits), for two values packed low first.
-__device__ __forceinline__ uint32_t pack_out(float lo, float hi, int dtype) {
-    if (dtype == NMG_BF16) return (uint32_t)dev::f32_to_bf16_bits(lo) | ((uint32_t)dev::f32_to_bf16_bits(hi) << 16);
-    return (uint32_t)dev::f32_to_f16_bits(lo) | ((uint32_t)dev::f32_to_f16_bits(hi) << 16);
-}
-// The same without branches for the values the epilogue meets almost
-// always; a warp with any other value takes pack_out instead.
-//   bf16: round to nearest even, which the hardware conversion gives for
-//         every value but NaN (the reference quiets NaN its own way).
-//   f16:  results in the normal range (fp32 exponent 113..142), where the
-//         reference rounds half up on bit 12 of the mantissa.
-__device__ __forceinline__ bool bf16_fast_ok(float x) { return x == x; }
-__device__ __forceinline__ bool f16_fast_ok(float x) { return ((__float_as_uint(x) >> 23) & 0xFFu) - 113u <= 29u; }
-__device__ __forceinline__ uint32_t pack_bf16_fast(float lo, float hi) {
-    uint32_t r;
-    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
-    return r;
-}
-__device__ __forceinline__ uint32_t f16_fast(float x) {
-    const uint32_t b = __float_as_uint(x);
-    const uint32_t h = ((b >> 16) & 0x8000u) | ((((b >> 23) & 0xFFu) - 112u) << 10) | ((b >> 13) & 0x3FFu);
-    return h + ((b >> 12) & 1u);
-}
-__device__ __forceinline__ uint32_t pack_f16_fast(float lo, float hi) { return f16_fast(lo) | (f16_fast(hi) << 16); }
-
-// AND of `v` over the `count` threads that meet on named barrier `id`.
-__device__ __forceinline__ bool bar_and(int id, int count, bool v) {
-    uint32_t r;
-    asm volatile(
-        "{\n\t.reg .pred p, q;\n\t"
-        "setp.ne.u32 q, %1, 0;\n\t"
-        "bar.red.and.pred p, %2, %3, q;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(r)
-        : "r"((uint32_t)v), "r"(id), "r"(count)
-        : "memory");
-    return r != 0;
-}
-
-__device__ __forceinline__ int64_t vis_lo(const PrefillArgs& a, int64_t q) {
-    int64_t lo = a.floor_pos;
-    if (a.window > 0 && q - a.window + 1 > lo) lo = q - a.window + 1;
-    return lo;
-}
-__device__ __forceinline__ int64_t vis_hi(const PrefillArgs& a, int64_t q) { return q < a.newest ? q : a.newest; }
-
-// One unit of work: a query tile (or a key split of one) of one head.
-struct Work {
-    int h, tile, split, nsplit, nblk;
-    int64_t t0, t_last, j_begin, full_lo, full_hi;
-};
-
-// The k-th unit of this CTA.  CTAs walk the heavy-first list in snake order
-// (k even: unit k * G + b, k odd: k * G + G - 1 - b), which evens out the
-// per-CTA totals of a list sorted by decreasing work.  Every role of the CTA
-// decodes the same sequence.
-template <int BM, int BN>
-__device__ __forceinline__ bool decode_work(const PrefillArgs& a, int k, Work& w) {
-    const int G = gridDim.x, b = blockIdx.x;
-    const int64_t idx = (int64_t)k * G + ((k & 1) ? G - 1 - b : b);
-    if (idx >= a.n_work) return false;
-    w.h = (int)(idx % a.hq);
-    const int it = (int)(idx / a.hq);
-    if (a.n_items > 0) {
-        const uint32_t item = a.items[it];
-        w.tile = (int)(item >> 12);
-        w.split = (int)((item >> 6) & 63u);
-        w.nsplit = (int)(item & 63u);
-    } else {
-        w.tile = a.ntiles - 1 - it;
-        w.split = 0;
-        w.nsplit = 1;
-    }
-    w.t0 = (int64_t)w.tile * BM;
-    w.t_last = (w.t0 + BM < a.rows ? w.t0 + BM : a.rows) - 1;
-    const int64_t q_first = a.first_query + w.t0, q_last = a.first_query + w.t_last;
-    const int64_t u_lo = vis_lo(a, q_first) - a.base, u_hi = vis_hi(a, q_last) - a.base;
-    const int nblk_all = (int)(u_hi / BN + 1 - u_lo / BN);
-    w.j_begin = u_lo / BN + (int64_t)w.split * a.split_blocks;
-    w.nblk = w.nsplit == 1 ? nblk_all : min(a.split_blocks, nblk_all - w.split * a.split_blocks);
-    // A block needs no mask when every row of the tile sees all of it.
-    w.full_lo = vis_lo(a, q_last);
-    w.full_hi = vis_hi(a, q_first);
-    return true;
-}
 
 template <int DH, bool BF16>
 __global__ void __launch_bounds__(PfCfg<DH>::THREADS, 1) attn_prefill_kernel(const __grid_constant__ PrefillArgs a) {
@@ -584,8 +447,6 @@ __global__ void __launch_bounds__(PfCfg<DH>::THREADS, 1) attn_prefill_kernel(con
         const int eid = threadIdx.x - 32 * C::EPI_WARP0;  // 0 .. 127
         const uint32_t t_lane = tmem + ((uint32_t)(quad * 32) << 16);
         uint4* stage = (uint4*)(smem + C::STAGE_OFF + (warp - C::EPI_WARP0) * 4096);  // [32 rows][8 chunks]
-        const int oes = a.out_dtype == NMG_F32 ? 4 : 2;
-        const int cpc = 128 / oes;  // output columns per 128-byte row piece
         int kn = 0;
         for (int k = 0; decode_work<BM, BN>(a, k, w); ++k) {
             if (w.nblk <= 0) continue;
@@ -602,93 +463,9 @@ __global__ void __launch_bounds__(PfCfg<DH>::THREADS, 1) attn_prefill_kernel(con
             const float l_row = st.x, m_run = st.y;
             const int valid_rows = (int)(w.t_last - w.t0 + 1);
             if (w.nsplit == 1) {
-                // Normalise 128 bytes of output per row at a time, stage the
-                // warp's 32 rows, then store whole 128-byte row pieces (four
-                // rows per instruction) to every output.
-                const float inv = 1.f / l_row;
-                const int64_t row_bytes = a.out_row_elems * oes;
-                const int64_t base_off =
-                    ((w.t0 + quad * 32 + (lane >> 3)) * a.out_row_elems + a.out_col0 + (int64_t)w.h * DH) * oes +
-                    (lane & 7) * 16;
-#pragma unroll 1
-                for (int c0 = 0; c0 < DH; c0 += cpc) {
-                    uint32_t r[64];
-                    tc::ld_32x32b_x32(t_lane + o_col + c0, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
-                    if (oes == 2) tc::ld_32x32b_x32(t_lane + o_col + c0 + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
-#pragma unroll
-                    for (int e = 0; e < 64; ++e)
-                        if (e < cpc) r[e] = __float_as_uint(__uint_as_float(r[e]) * inv);
-                    auto f = [&](int e) { return __uint_as_float(r[e]); };
-                    if (oes == 4) {
-#pragma unroll
-                        for (int j = 0; j < 8; ++j)
-                            stage[lane * 8 + (j ^ (lane & 7))] = make_uint4(r[4 * j], r[4 * j + 1],
-                                                                            r[4 * j + 2], r[4 * j + 3]);
-                    } else {
-                        const bool bf = a.out_dtype == NMG_BF16;
-                        bool fast = true;
-#pragma unroll
-                        for (int e = 0; e < 64; ++e) fast &= bf ? bf16_fast_ok(f(e)) : f16_fast_ok(f(e));
-                        if (!__all_sync(0xffffffffu, fast)) {
-#pragma unroll
-                            for (int j = 0; j < 8; ++j)
-                                stage[lane * 8 + (j ^ (lane & 7))] =
-                                    make_uint4(pack_out(f(8 * j), f(8 * j + 1), a.out_dtype), pack_out(f(8 * j + 2), f(8 * j + 3), a.out_dtype),
-                                               pack_out(f(8 * j + 4), f(8 * j + 5), a.out_dtype), pack_out(f(8 * j + 6), f(8 * j + 7), a.out_dtype));
-                        } else if (bf) {
-#pragma unroll
-                            for (int j = 0; j < 8; ++j)
-                                stage[lane * 8 + (j ^ (lane & 7))] =
-                                    make_uint4(pack_bf16_fast(f(8 * j), f(8 * j + 1)), pack_bf16_fast(f(8 * j + 2), f(8 * j + 3)),
-                                               pack_bf16_fast(f(8 * j + 4), f(8 * j + 5)), pack_bf16_fast(f(8 * j + 6), f(8 * j + 7)));
-                        } else {
-#pragma unroll
-                            for (int j = 0; j < 8; ++j)
-                                stage[lane * 8 + (j ^ (lane & 7))] =
-                                    make_uint4(pack_f16_fast(f(8 * j), f(8 * j + 1)), pack_f16_fast(f(8 * j + 2), f(8 * j + 3)),
-                                               pack_f16_fast(f(8 * j + 4), f(8 * j + 5)), pack_f16_fast(f(8 * j + 6), f(8 * j + 7)));
-                        }
-                    }
-                    if (c0 + cpc >= DH) {  // O and the statistics are read: the buffer is free
-                        tc::fence_before_sync();
-                        dev::mbar_arrive(&o_free[ob]);
-                    }
-                    __syncwarp();
-                    uint4 v[8];
-#pragma unroll
-                    for (int m = 0; m < 8; ++m) {
-                        const int rr = m * 4 + (lane >> 3);
-                        v[m] = stage[rr * 8 + ((lane & 7) ^ (rr & 7))];
-                    }
-                    __syncwarp();
-                    for (int o = 0; o < a.nout; ++o) {
-                        unsigned char* p = (unsigned char*)a.outs[o] + base_off + c0 * oes;
-#pragma unroll
-                        for (int m = 0; m < 8; ++m)
-                            if (quad * 32 + m * 4 + (lane >> 3) < valid_rows) *(uint4*)(p + m * 4 * row_bytes) = v[m];
-                    }
-                }
-                // No fence: a caller that reads the rows on another GPU orders
-                // these stores with a stream-ordered barrier (nmg_comm_barrier),
-                // which starts only after this grid, stores included, has completed.
+                store_rows<DH>(a, w, w.h, t_lane, o_col, l_row, quad, lane, stage, &o_free[ob]);
             } else {
-                // A split of a tile: leave the unnormalised O with its m and l
-                // (base-2 units), and the last split of the tile merges them.
-                float* mine = a.part + (((int64_t)w.h * a.nparts + a.part_base[w.tile] + w.split) * BM + row) * (DH + 4);
-#pragma unroll 1
-                for (int c = 0; c < DH / 32; ++c) {
-                    uint32_t r[32];
-                    tc::ld_32x32b_x32(t_lane + o_col + c * 32, r);
-                    float4* dst = (float4*)(mine + c * 32);
-#pragma unroll
-                    for (int e = 0; e < 8; ++e)
-                        dst[e] = make_float4(__uint_as_float(r[4 * e]), __uint_as_float(r[4 * e + 1]),
-                                             __uint_as_float(r[4 * e + 2]), __uint_as_float(r[4 * e + 3]));
-                }
-                mine[DH] = m_run;
-                mine[DH + 1] = l_row;
-                tc::fence_before_sync();
-                dev::mbar_arrive(&o_free[ob]);
+                store_partial<DH>(a, w, w.h, row, t_lane, o_col, m_run, l_row, &o_free[ob]);
                 __threadfence();
                 asm volatile("bar.sync 1, 128;" ::: "memory");
                 if (eid == 0) {
@@ -703,64 +480,7 @@ __global__ void __launch_bounds__(PfCfg<DH>::THREADS, 1) attn_prefill_kernel(con
                 asm volatile("bar.sync 1, 128;" ::: "memory");  // every thread has read the flag
                 if (last) {
                     __threadfence();
-                    const float* base = a.part + ((int64_t)w.h * a.nparts + a.part_base[w.tile]) * BM * (DH + 4);
-                    const int64_t slot = (int64_t)BM * (DH + 4);
-                    // One thread per row: the row's maximum and sum over the
-                    // splits first, then 16-column chunks in which every
-                    // split's loads are independent of its weight, so each
-                    // split costs about one L2 round trip per chunk.
-                    const int rr = eid;
-                    if (rr < valid_rows) {
-                        const float* rowp = base + rr * (DH + 4);
-                        float M = -INFINITY;
-#pragma unroll 4
-                        for (int sp = 0; sp < w.nsplit; ++sp) M = fmaxf(M, __ldcg(rowp + sp * slot + DH));
-                        float L = 0.f;
-#pragma unroll 4
-                        for (int sp = 0; sp < w.nsplit; ++sp) {
-                            const float m = __ldcg(rowp + sp * slot + DH);
-                            if (m != -INFINITY) L = fmaf(ex2(m - M), __ldcg(rowp + sp * slot + DH + 1), L);
-                        }
-                        const float inv = 1.f / L;
-                        const int64_t off0 = ((w.t0 + rr) * a.out_row_elems + a.out_col0 + (int64_t)w.h * DH) * oes;
-#pragma unroll 1
-                        for (int c = 0; c < DH / 16; ++c) {
-                            float o[16];
-#pragma unroll
-                            for (int e = 0; e < 16; ++e) o[e] = 0.f;
-#pragma unroll 1
-                            for (int sp = 0; sp < w.nsplit; ++sp) {
-                                const float* rp = rowp + sp * slot;
-                                float4 v[4];
-#pragma unroll
-                                for (int e = 0; e < 4; ++e) v[e] = __ldcg((const float4*)(rp + c * 16) + e);
-                                const float m = __ldcg(rp + DH);
-                                const float wgt = m == -INFINITY ? 0.f : ex2(m - M);
-#pragma unroll
-                                for (int e = 0; e < 4; ++e) {
-                                    o[4 * e] = fmaf(wgt, v[e].x, o[4 * e]), o[4 * e + 1] = fmaf(wgt, v[e].y, o[4 * e + 1]);
-                                    o[4 * e + 2] = fmaf(wgt, v[e].z, o[4 * e + 2]), o[4 * e + 3] = fmaf(wgt, v[e].w, o[4 * e + 3]);
-                                }
-                            }
-                            const int64_t off = off0 + (int64_t)c * 16 * oes;
-                            for (int oi = 0; oi < a.nout; ++oi) {
-                                unsigned char* dst = (unsigned char*)a.outs[oi] + off;
-                                if (a.out_dtype == NMG_F32) {
-#pragma unroll
-                                    for (int e = 0; e < 4; ++e)
-                                        ((float4*)dst)[e] = make_float4(o[4 * e] * inv, o[4 * e + 1] * inv,
-                                                                        o[4 * e + 2] * inv, o[4 * e + 3] * inv);
-                                } else {
-#pragma unroll
-                                    for (int e = 0; e < 2; ++e)
-                                        ((uint4*)dst)[e] = make_uint4(pack_out(o[8 * e] * inv, o[8 * e + 1] * inv, a.out_dtype),
-                                                                      pack_out(o[8 * e + 2] * inv, o[8 * e + 3] * inv, a.out_dtype),
-                                                                      pack_out(o[8 * e + 4] * inv, o[8 * e + 5] * inv, a.out_dtype),
-                                                                      pack_out(o[8 * e + 6] * inv, o[8 * e + 7] * inv, a.out_dtype));
-                                }
-                            }
-                        }
-                    }
+                    if (eid < valid_rows) merge_row<DH>(a, w, w.h, eid);
                 }
             }
             ++kn;
@@ -898,6 +618,10 @@ int attend_rows_prefill(const nmg_kv_cache* c, int hq, const void* q, int q_dtyp
     a->hq = hq;
     a->hkv = c->hkv;
     a->g = hq / c->hkv;
+    // Two query heads of one GQA group a unit (they share every K/V block)
+    // where the group is even; one head a unit otherwise.
+    const bool pair = dh == 128 && a->g % 2 == 0;
+    a->hunits = pair ? hq / 2 : hq;
     a->scale_log2 = scale * 1.4426950408889634f;
     // Key splits when one CTA per query tile would leave the GPU's 148 SMs
     // waiting on the heaviest tiles (a causal tile sees as many key blocks
@@ -911,7 +635,7 @@ int attend_rows_prefill(const nmg_kv_cache* c, int hq, const void* q, int q_dtyp
     a->ntiles = ntiles;
     a->part = nullptr;
     a->tickets = nullptr;
-    if (ntiles <= kMaxTiles && (int64_t)ntiles * hq < 2 * 148) {
+    if (ntiles <= kMaxTiles && (int64_t)ntiles * a->hunits < 2 * 148) {
         std::vector<int> nb(ntiles);
         int64_t total = 0;
         int maxb = 0;
@@ -921,7 +645,7 @@ int attend_rows_prefill(const nmg_kv_cache* c, int hq, const void* q, int q_dtyp
             if (window > 0 && qf - window + 1 > lo) lo = qf - window + 1;
             const int64_t hi = ql < newest ? ql : newest;
             nb[t] = (int)((hi - c->base) / bn + 1 - (lo - c->base) / bn);
-            total += (int64_t)nb[t] * hq;
+            total += (int64_t)nb[t] * a->hunits;
             maxb = std::max(maxb, nb[t]);
         }
         int sb = (int)std::max<int64_t>(8, (total + 2 * 148 - 1) / (2 * 148));
@@ -941,8 +665,8 @@ int attend_rows_prefill(const nmg_kv_cache* c, int hq, const void* q, int q_dtyp
             // split plan charged kSplitItemBlocks per item for its partial
             // store and merge.
             std::vector<int> whole, pieces;
-            for (int t = 0; t < ntiles; ++t) whole.insert(whole.end(), hq, nb[t]);
-            for (const auto& it : items) pieces.insert(pieces.end(), hq, it.first);
+            for (int t = 0; t < ntiles; ++t) whole.insert(whole.end(), a->hunits, nb[t]);
+            for (const auto& it : items) pieces.insert(pieces.end(), a->hunits, it.first);
             const double m0 = (double)lpt_makespan(whole, 148);
             const double m1 = (double)lpt_makespan(pieces, 148) + kSplitItemBlocks * (double)pieces.size() / 148.0;
             if ((int)items.size() <= kMaxItems && m1 < m0) {
@@ -972,11 +696,13 @@ int attend_rows_prefill(const nmg_kv_cache* c, int hq, const void* q, int q_dtyp
     int st = device_error_flag(c->device, &a->err);
     if (st == NMG_OK) {
         // Persistent CTAs, one per SM, walk the unit list (heaviest first).
-        a->n_work = (int64_t)(a->n_items > 0 ? a->n_items : ntiles) * hq;
+        a->n_work = (int64_t)(a->n_items > 0 ? a->n_items : ntiles) * a->hunits;
         int nsm = 148;
         if (cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, c->device) != cudaSuccess) nsm = 148;
         const dim3 grid((unsigned)std::min<int64_t>(a->n_work, nsm));
-        if (dh == 64)
+        if (pair)
+            st = launch_prefill_pair(*a, dh, c->dtype == NMG_BF16, grid, stream);
+        else if (dh == 64)
             st = c->dtype == NMG_BF16 ? launch_prefill<64, true>(*a, grid, stream) : launch_prefill<64, false>(*a, grid, stream);
         else if (dh == 128)
             st = c->dtype == NMG_BF16 ? launch_prefill<128, true>(*a, grid, stream) : launch_prefill<128, false>(*a, grid, stream);
