@@ -19,13 +19,16 @@
 //                 O_t += P_t V  (M=128, N=128, K=128), A = P_t from TMEM
 //   warp 2      TMA producer for V blocks (2 stages, released after P_B.V)
 //   warp 3      idle (the next warps start on TMEM lane quadrant 0)
-//   warps 4-7   softmax of tile A, warps 8-11 softmax of tile B: one thread
-//               per row, all 128 keys of a block (maximum over both column
-//               halves, then base-2 exponentials, P as packed fp16 over the
-//               first half of the S columns), rescaling O in TMEM only when
-//               the running max grows by more than 2^8
-//   warps 12-15 epilogue: normalise and store each finished unit's rows of
-//               both heads (or leave key-split partials and merge them)
+//   warps 4-7   tile A, warps 8-11 tile B, one thread per row: the softmax
+//               of every key block (all 128 scores of the row in registers
+//               from one TMEM load, the block maximum, base-2 exponentials,
+//               P as packed fp16 over the first half of the S columns, O in
+//               TMEM rescaled only when the running max grows by more than
+//               2^8), then the unit's epilogue: normalise and store the
+//               tile's rows (or leave key-split partials and merge them).
+//               The other tile's softmax keeps the tensor core busy meanwhile.
+//
+// 384 threads, so each holds 168 registers: a whole score row fits.
 //
 // TMEM: S_A, S_B, O_A, O_B, 128 columns each.  S_t(g) is issued after
 // P_t(g-1).V, so its completion also means the previous P.V into O_t has
@@ -53,22 +56,21 @@ struct PairCfg {
     static constexpr int Q_OFF = 0;  // tile A, then tile B
     static constexpr int K_OFF = Q_OFF + 2 * Q_BYTES;
     static constexpr int V_OFF = K_OFF + KST * K_BYTES;
-    static constexpr int STAGE_OFF = V_OFF + VST * V_BYTES;  // 4 epilogue warps x 32 rows x 128 B
-    static constexpr int BAR_OFF = STAGE_OFF + 4 * 32 * 128;
+    static constexpr int STAGE_OFF = V_OFF + VST * V_BYTES;  // 2 tiles x 4 warps x 32 rows x 128 B
+    static constexpr int BAR_OFF = STAGE_OFF + 2 * 4 * 32 * 128;
     // q_full, q_empty, k_full/k_empty[KST], v_full/v_empty[VST],
-    // per tile: s_full, p_full, o_final, o_free, l_full
-    static constexpr int NBARS = 2 + 2 * KST + 2 * VST + 2 * 5;
-    static constexpr int FLAGS_OFF = BAR_OFF + NBARS * 8;  // TMEM address, abort flag, last-split flag
-    static constexpr int STATS_OFF = FLAGS_OFF + 16;       // float2 [2][BM]: a unit's (l, m) per row and tile
-    static constexpr int SMEM = STATS_OFF + 2 * BM * 8 + 1024;  // + slack to align the base to 1024
-    static constexpr int THREADS = 512;
-    static constexpr int SOFTMAX_WARP0 = 4, EPI_WARP0 = 12;
+    // per tile: s_full, p_full, o_final, o_free
+    static constexpr int NBARS = 2 + 2 * KST + 2 * VST + 2 * 4;
+    static constexpr int FLAGS_OFF = BAR_OFF + NBARS * 8;  // TMEM address, abort flag, last-split flags [2]
+    static constexpr int SMEM = FLAGS_OFF + 16 + 1024;     // + slack to align the base to 1024
+    static constexpr int THREADS = 384;
+    static constexpr int SOFTMAX_WARP0 = 4;
     static constexpr uint32_t TMEM_COLS = 512;
     static constexpr uint32_t O_COL = 2 * BN;  // O_t at O_COL + t * DH; S_t at t * BN
     static_assert(O_COL + 2 * DH <= TMEM_COLS, "TMEM budget");
     static_assert(SMEM <= 232448, "shared memory budget");
     static_assert(Q_OFF % 1024 == 0 && K_OFF % 1024 == 0 && V_OFF % 1024 == 0, "128-byte swizzle atoms");
-    static_assert(STATS_OFF % 8 == 0 && STAGE_OFF % 16 == 0, "vector accesses");
+    static_assert(STAGE_OFF % 16 == 0 && BAR_OFF % 8 == 0, "vector and mbarrier accesses");
 };
 
 template <bool BF16>
@@ -87,12 +89,10 @@ __global__ void __launch_bounds__(PairCfg::THREADS, 1) attn_prefill_pair_kernel(
     uint64_t* s_full = v_empty + VST;  // [2] per tile, once per key block
     uint64_t* p_full = s_full + 2;     // [2] per tile, once per key block (128 softmax threads)
     uint64_t* o_final = p_full + 2;    // [2] a unit's last P.V of the tile
-    uint64_t* o_free = o_final + 2;    // [2] the epilogue has read the tile's O and statistics
-    uint64_t* l_full = o_free + 2;     // [2] the softmax has left the tile's (l, m)
+    uint64_t* o_free = o_final + 2;    // [2] the tile's epilogue has read O (128 threads)
     uint32_t* tmem_slot = (uint32_t*)(smem + C::FLAGS_OFF);
     volatile int* abort_flag = (volatile int*)(smem + C::FLAGS_OFF + 4);
-    volatile int* last_flag = (volatile int*)(smem + C::FLAGS_OFF + 8);
-    float2* stats = (float2*)(smem + C::STATS_OFF);
+    volatile int* last_flag = (volatile int*)(smem + C::FLAGS_OFF + 8);  // [2] per tile
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
@@ -112,10 +112,9 @@ __global__ void __launch_bounds__(PairCfg::THREADS, 1) attn_prefill_pair_kernel(
             dev::mbar_init(&p_full[t], 128);
             dev::mbar_init(&o_final[t], 1);
             dev::mbar_init(&o_free[t], 128);
-            dev::mbar_init(&l_full[t], 128);
+            last_flag[t] = 0;
         }
         *abort_flag = 0;
-        *last_flag = 0;
         dev::fence_mbar_init();
     }
     if (warp == 1) {
@@ -285,23 +284,35 @@ __global__ void __launch_bounds__(PairCfg::THREADS, 1) attn_prefill_pair_kernel(
                 for (int t = 0; t < 2; ++t)
                     if (!issue_pv(t, g - 1, pv_first, pv_last, pv_use)) break;
         }
-    } else if (warp == 3) {
-        // idle: keeps the softmax and epilogue warps aligned to TMEM lane quadrants
-    } else if (warp < C::EPI_WARP0) {
-        // ---------------------------------------------------- softmax warps
+    } else if (warp >= C::SOFTMAX_WARP0) {
+        // ------------------------------------------- softmax + epilogue warps
         const int t = (warp - C::SOFTMAX_WARP0) >> 2;  // tile A (0) or B (1)
         const int quad = warp & 3;                     // TMEM lane quadrant this warp may access
         const int row = quad * 32 + lane;
+        const int gid = row;                           // 0 .. 127 within the tile's warps
         const uint32_t t_lane = tmem + ((uint32_t)(quad * 32) << 16);
         const uint32_t s_col = t * BN, o_col = C::O_COL + t * DH;
+        uint4* stage = (uint4*)(smem + C::STAGE_OFF + (warp - C::SOFTMAX_WARP0) * 4096);  // [32 rows][8 chunks]
+        const float sl2 = a.scale_log2;
         uint32_t g = 0;
         int kn = 0;
         bool ok = true;
         for (int k = 0; ok && decode_work<BM, BN>(a, k, w); ++k) {
             if (w.nblk <= 0) continue;
             const int use = kn;
-            const int64_t qpos = a.first_query + w.t0 + row;
-            const int64_t lo = vis_lo(a, qpos), hi = vis_hi(a, qpos);
+            // This row's visible keys, relative to the unit's first key block
+            // (clamped: only comparisons against 0 .. nblk * BN matter), and
+            // the blocks [i_full0, i_full1] every row of the tile sees whole.
+            int lo_rel, hi_rel, i_full0, i_full1;
+            {
+                const int64_t qpos = a.first_query + w.t0 + row;
+                const int64_t p_first = a.base + w.j_begin * BN;
+                const int64_t span = (int64_t)w.nblk * BN + 1;
+                lo_rel = (int)max((int64_t)-1, min(span, vis_lo(a, qpos) - p_first));
+                hi_rel = (int)max((int64_t)-1, min(span, vis_hi(a, qpos) - p_first));
+                i_full0 = (int)min((int64_t)w.nblk, max((int64_t)0, (w.full_lo - p_first + BN - 1) / BN));
+                i_full1 = (int)max((int64_t)-1, min((int64_t)w.nblk, (w.full_hi - p_first + 1) / BN) - 1);
+            }
             float m_run = -INFINITY, l_run = 0.f;
             for (int i = 0; i < w.nblk; ++i, ++g) {
                 // Waits are voted warp-wide so the .sync.aligned TMEM accesses
@@ -311,50 +322,30 @@ __global__ void __launch_bounds__(PairCfg::THREADS, 1) attn_prefill_pair_kernel(
                     break;
                 }
                 tc::fence_after_sync();
-                const int64_t p0 = a.base + (w.j_begin + i) * BN;  // position of the block's key 0
-                // Keys [k_lo, k_hi) of the block are visible to this row; the
-                // mask is applied only on blocks some row of the tile cannot
-                // fully see (a warp-uniform branch).
-                const bool masked = !(p0 >= w.full_lo && p0 + BN - 1 <= w.full_hi);
-                int k_lo = 0, k_hi = BN;
-                if (masked) {
-                    k_lo = (int)max((int64_t)0, min((int64_t)BN, lo - p0));
-                    k_hi = (int)max((int64_t)0, min((int64_t)BN, hi - p0 + 1));
+                // The row's 128 raw scores, one TMEM load.  The maximum is
+                // taken before scaling (scale_log2 > 0); the scale is folded
+                // into each exponent's FFMA.
+                float x[BN];
+                {
+                    uint32_t r[BN];
+                    tc::ld_32x32b_x128(t_lane + s_col, r);
+#pragma unroll
+                    for (int e = 0; e < BN; ++e) x[e] = __uint_as_float(r[e]);
                 }
-                // Raw scores: the maximum is taken before scaling (scale_log2 > 0)
-                // and the scale is folded into the exponent's FFMA below.  Keys
-                // 64..127 first (32 at a time, for the maximum only), then 0..63,
-                // which stay in registers.  Four independent max chains.
-                float x[64];
-                float mb4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-                auto scores = [&](auto mask_tag) {
-                    constexpr bool M = decltype(mask_tag)::value;
+                // Keys [k_lo, k_hi) of the block are visible to this row; the
+                // mask applies only on blocks some row of the tile cannot fully
+                // see (a warp-uniform branch).
+                if (i < i_full0 || i > i_full1) {
+                    const int k_lo = max(0, min(BN, lo_rel - i * BN));
+                    const int k_hi = max(0, min(BN, hi_rel - i * BN + 1));
 #pragma unroll
-                    for (int c = 2; c < 4; ++c) {
-                        uint32_t r[32];
-                        tc::ld_32x32b_x32(t_lane + s_col + c * 32, r);
+                    for (int e = 0; e < BN; ++e)
+                        if (e < k_lo || e >= k_hi) x[e] = -INFINITY;
+                }
+                float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-                        for (int e = 0; e < 32; ++e) {
-                            float v = __uint_as_float(r[e]);
-                            if (M && (c * 32 + e < k_lo || c * 32 + e >= k_hi)) v = -INFINITY;
-                            mb4[e & 3] = fmaxf(mb4[e & 3], v);
-                        }
-                    }
-                    uint32_t r[64];
-                    tc::ld_32x32b_x64(t_lane + s_col, r);
-#pragma unroll
-                    for (int e = 0; e < 64; ++e) {
-                        x[e] = __uint_as_float(r[e]);
-                        if (M && (e < k_lo || e >= k_hi)) x[e] = -INFINITY;
-                        mb4[e & 3] = fmaxf(mb4[e & 3], x[e]);
-                    }
-                };
-                if (masked)
-                    scores(std::true_type{});
-                else
-                    scores(std::false_type{});
-                float mb = fmaxf(fmaxf(mb4[0], mb4[1]), fmaxf(mb4[2], mb4[3]));
-                mb *= a.scale_log2;
+                for (int e = 0; e < BN; ++e) mx[e & 3] = fmaxf(mx[e & 3], x[e]);
+                const float mb = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * sl2;
                 const float m_new = fmaxf(m_run, mb);
                 const bool rescale = m_new > m_run + 8.0f;  // also true for the first finite block
                 float alpha = 1.f;
@@ -363,9 +354,26 @@ __global__ void __launch_bounds__(PairCfg::THREADS, 1) attn_prefill_pair_kernel(
                     m_run = m_new;
                 }
                 const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
+                // P as fp16 pairs: keys 2j, 2j + 1 -> column j of S_t (every
+                // score is in registers), 32 keys per store; four sum chains.
+                float sm[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+                for (int c = 0; c < BN / 32; ++c) {
+                    uint32_t pk[16];
+#pragma unroll
+                    for (int e = 0; e < 32; e += 2) {
+                        const float pa = ex2(fmaf(x[c * 32 + e], sl2, -m_use));
+                        const float pb = ex2(fmaf(x[c * 32 + e + 1], sl2, -m_use));
+                        sm[(e >> 1) & 3] += pa + pb;
+                        pk[e / 2] = pack2(pa, pb, false);
+                    }
+                    tc::st_32x32b_x16(t_lane + s_col + c * 16, pk);
+                }
+                l_run = l_run * alpha + ((sm[0] + sm[1]) + (sm[2] + sm[3]));
                 // O_t holds the blocks before this one (S_t(g) completing means
                 // P_t(g-1).V has landed); within a unit it is rescaled only when
-                // the running max grew by more than 2^8.
+                // the running max grew by more than 2^8, after the scores are
+                // consumed and before P_t(g).V may start.
                 if (i >= 1 && __any_sync(0xffffffffu, rescale)) {
 #pragma unroll 1
                     for (int c = 0; c < DH / 32; ++c) {
@@ -376,114 +384,37 @@ __global__ void __launch_bounds__(PairCfg::THREADS, 1) attn_prefill_pair_kernel(
                         tc::st_32x32b_x32(t_lane + o_col + c * 32, r);
                     }
                 }
-                // P as fp16 pairs: keys 2j, 2j + 1 -> column j of S_t, over
-                // columns whose scores were read already.  Keys 0..63 from
-                // registers, then 64..127 again from TMEM, 32 at a time.  Four
-                // independent sum chains.
-                float sum4[4] = {0.f, 0.f, 0.f, 0.f};
-                const float sl2 = a.scale_log2;
-#pragma unroll
-                for (int c = 0; c < 2; ++c) {
-                    uint32_t pk[16];
-#pragma unroll
-                    for (int e = 0; e < 32; e += 2) {
-                        const float pa = ex2(fmaf(x[c * 32 + e], sl2, -m_use));
-                        const float pb = ex2(fmaf(x[c * 32 + e + 1], sl2, -m_use));
-                        sum4[(e >> 1) & 3] += pa + pb;
-                        pk[e / 2] = pack2(pa, pb, false);
-                    }
-                    tc::st_32x32b_x16(t_lane + s_col + c * 16, pk);
-                }
-                auto exps_hi = [&](auto mask_tag) {
-                    constexpr bool M = decltype(mask_tag)::value;
-#pragma unroll
-                    for (int c = 2; c < 4; ++c) {
-                        uint32_t r[32];
-                        tc::ld_32x32b_x32(t_lane + s_col + c * 32, r);
-                        uint32_t pk[16];
-#pragma unroll
-                        for (int e = 0; e < 32; e += 2) {
-                            float va = __uint_as_float(r[e]), vb = __uint_as_float(r[e + 1]);
-                            if (M && (c * 32 + e < k_lo || c * 32 + e >= k_hi)) va = -INFINITY;
-                            if (M && (c * 32 + e + 1 < k_lo || c * 32 + e + 1 >= k_hi)) vb = -INFINITY;
-                            const float pa = ex2(fmaf(va, sl2, -m_use)), pb = ex2(fmaf(vb, sl2, -m_use));
-                            sum4[(e >> 1) & 3] += pa + pb;
-                            pk[e / 2] = pack2(pa, pb, false);
-                        }
-                        tc::st_32x32b_x16(t_lane + s_col + c * 16, pk);
-                    }
-                };
-                if (masked)
-                    exps_hi(std::true_type{});
-                else
-                    exps_hi(std::false_type{});
-                const float sum = (sum4[0] + sum4[1]) + (sum4[2] + sum4[3]);
-                l_run = l_run * alpha + sum;
                 tc::wait_st();
                 tc::fence_before_sync();
                 dev::mbar_arrive(&p_full[t]);
             }
             if (!ok) break;
-            // The epilogue has read the tile's statistics of the previous unit.
-            if (use >= 1 && !__all_sync(0xffffffffu, wait(&o_free[t], (use - 1) & 1))) break;
-            stats[t * BM + row] = make_float2(l_run, m_run);
-            dev::mbar_arrive(&l_full[t]);
-            ++kn;
-        }
-    } else {
-        // ---------------------------------------------------- epilogue warps
-        // One warp per TMEM lane quadrant: normalise a unit's O rows of both
-        // heads and store them (or leave split partials and merge), while the
-        // softmax warps already work on the next unit.
-        const int quad = warp & 3;
-        const int row = quad * 32 + lane;
-        const int eid = threadIdx.x - 32 * C::EPI_WARP0;  // 0 .. 127
-        const uint32_t t_lane = tmem + ((uint32_t)(quad * 32) << 16);
-        uint4* stage = (uint4*)(smem + C::STAGE_OFF + (warp - C::EPI_WARP0) * 4096);  // [32 rows][8 chunks]
-        int kn = 0;
-        bool ok = true;
-        for (int k = 0; ok && decode_work<BM, BN>(a, k, w); ++k) {
-            if (w.nblk <= 0) continue;
-            const int use = kn;
-            for (int t = 0; t < 2; ++t) {
-                // Waits are bounded, so all four warps reach the vote; a tile is
-                // skipped by all of them or by none.
-                bool have = wait(&l_full[t], use & 1);
-                have = wait(&o_final[t], use & 1) && have;
-                if (!bar_and(1, 128, __all_sync(0xffffffffu, have))) {
-                    ok = false;
-                    break;
-                }
-                tc::fence_after_sync();
-                const float2 st = stats[t * BM + row];
-                const uint32_t o_col = C::O_COL + t * DH;
-                if (w.nsplit == 1)
-                    store_rows<DH>(a, w, 2 * w.h + t, t_lane, o_col, st.x, quad, lane, stage, &o_free[t]);
-                else
-                    store_partial<DH>(a, w, 2 * w.h + t, row, t_lane, o_col, st.y, st.x, &o_free[t]);
-            }
-            if (!ok) break;
-            if (w.nsplit > 1) {
-                // The last split of the tile (ticket per head pair and tile) merges both heads.
+            // ---- the unit's epilogue for this tile, once its last P.V is in O_t.
+            // Waits are bounded, so the four warps reach the vote together and
+            // skip the tile together (the split path meets on named barriers).
+            const int bar_id = 1 + t;
+            if (!bar_and(bar_id, 128, __all_sync(0xffffffffu, wait(&o_final[t], use & 1)))) break;
+            tc::fence_after_sync();
+            const int head = 2 * w.h + t;
+            if (w.nsplit == 1) {
+                store_rows<DH>(a, w, head, t_lane, o_col, l_run, quad, lane, stage, &o_free[t]);
+            } else {
+                store_partial<DH>(a, w, head, row, t_lane, o_col, m_run, l_run, &o_free[t]);
                 __threadfence();
-                asm volatile("bar.sync 1, 128;" ::: "memory");
-                if (eid == 0) {
-                    int* ticket = a.tickets + (int64_t)w.h * a.ntiles + w.tile;
+                asm volatile("bar.sync %0, 128;" ::"r"(bar_id) : "memory");
+                if (gid == 0) {
+                    int* ticket = a.tickets + (int64_t)head * a.ntiles + w.tile;
                     const int prev = atomicAdd(ticket, 1);
                     const bool last = prev == w.nsplit - 1;
                     if (last) *ticket = 0;  // ready for the next launch
-                    *last_flag = last;
+                    last_flag[t] = last;
                 }
-                asm volatile("bar.sync 1, 128;" ::: "memory");
-                const bool last = *last_flag;
-                asm volatile("bar.sync 1, 128;" ::: "memory");  // every thread has read the flag
+                asm volatile("bar.sync %0, 128;" ::"r"(bar_id) : "memory");
+                const bool last = last_flag[t];
+                asm volatile("bar.sync %0, 128;" ::"r"(bar_id) : "memory");  // every thread has read the flag
                 if (last) {
                     __threadfence();
-                    const int valid_rows = (int)(w.t_last - w.t0 + 1);
-                    if (eid < valid_rows) {
-                        merge_row<DH>(a, w, 2 * w.h, eid);
-                        merge_row<DH>(a, w, 2 * w.h + 1, eid);
-                    }
+                    if (gid <= (int)(w.t_last - w.t0)) merge_row<DH>(a, w, head, gid);
                 }
             }
             ++kn;

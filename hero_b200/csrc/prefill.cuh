@@ -174,40 +174,39 @@ __device__ __forceinline__ void store_rows(const PrefillArgs& a, const Work& w, 
         ((w.t0 + quad * 32 + (lane >> 3)) * a.out_row_elems + a.out_col0 + (int64_t)head * DH) * oes + (lane & 7) * 16;
 #pragma unroll 1
     for (int c0 = 0; c0 < DH; c0 += cpc) {
-        uint32_t r[64];
-        tc::ld_32x32b_x32(t_lane + o_col + c0, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
-        if (oes == 2) tc::ld_32x32b_x32(t_lane + o_col + c0 + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
+        // 32 columns per TMEM load: 8 stage chunks of fp32, or 4 of 16-bit values.
+#pragma unroll 1
+        for (int h = 0; h < cpc / 32; ++h) {
+            uint32_t r[32];
+            tc::ld_32x32b_x32(t_lane + o_col + c0 + 32 * h, r);
 #pragma unroll
-        for (int e = 0; e < 64; ++e)
-            if (e < cpc) r[e] = __float_as_uint(__uint_as_float(r[e]) * inv);
-        auto f = [&](int e) { return __uint_as_float(r[e]); };
-        if (oes == 4) {
-#pragma unroll
-            for (int j = 0; j < 8; ++j)
-                stage[lane * 8 + (j ^ (lane & 7))] = make_uint4(r[4 * j], r[4 * j + 1], r[4 * j + 2], r[4 * j + 3]);
-        } else {
-            const bool bf = a.out_dtype == NMG_BF16;
-            bool fast = true;
-#pragma unroll
-            for (int e = 0; e < 64; ++e) fast &= bf ? bf16_fast_ok(f(e)) : f16_fast_ok(f(e));
-            if (!__all_sync(0xffffffffu, fast)) {
+            for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * inv);
+            auto f = [&](int e) { return __uint_as_float(r[e]); };
+            if (oes == 4) {
 #pragma unroll
                 for (int j = 0; j < 8; ++j)
-                    stage[lane * 8 + (j ^ (lane & 7))] =
-                        make_uint4(pack_out(f(8 * j), f(8 * j + 1), a.out_dtype), pack_out(f(8 * j + 2), f(8 * j + 3), a.out_dtype),
-                                   pack_out(f(8 * j + 4), f(8 * j + 5), a.out_dtype), pack_out(f(8 * j + 6), f(8 * j + 7), a.out_dtype));
-            } else if (bf) {
-#pragma unroll
-                for (int j = 0; j < 8; ++j)
-                    stage[lane * 8 + (j ^ (lane & 7))] =
-                        make_uint4(pack_bf16_fast(f(8 * j), f(8 * j + 1)), pack_bf16_fast(f(8 * j + 2), f(8 * j + 3)),
-                                   pack_bf16_fast(f(8 * j + 4), f(8 * j + 5)), pack_bf16_fast(f(8 * j + 6), f(8 * j + 7)));
+                    stage[lane * 8 + (j ^ (lane & 7))] = make_uint4(r[4 * j], r[4 * j + 1], r[4 * j + 2], r[4 * j + 3]);
             } else {
+                const bool bf = a.out_dtype == NMG_BF16;
+                bool fast = true;
 #pragma unroll
-                for (int j = 0; j < 8; ++j)
-                    stage[lane * 8 + (j ^ (lane & 7))] =
-                        make_uint4(pack_f16_fast(f(8 * j), f(8 * j + 1)), pack_f16_fast(f(8 * j + 2), f(8 * j + 3)),
-                                   pack_f16_fast(f(8 * j + 4), f(8 * j + 5)), pack_f16_fast(f(8 * j + 6), f(8 * j + 7)));
+                for (int e = 0; e < 32; ++e) fast &= bf ? bf16_fast_ok(f(e)) : f16_fast_ok(f(e));
+                const bool all_fast = __all_sync(0xffffffffu, fast);
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const int chunk = 4 * h + j;
+                    uint4 v;
+                    if (!all_fast)
+                        v = make_uint4(pack_out(f(8 * j), f(8 * j + 1), a.out_dtype), pack_out(f(8 * j + 2), f(8 * j + 3), a.out_dtype),
+                                       pack_out(f(8 * j + 4), f(8 * j + 5), a.out_dtype), pack_out(f(8 * j + 6), f(8 * j + 7), a.out_dtype));
+                    else if (bf)
+                        v = make_uint4(pack_bf16_fast(f(8 * j), f(8 * j + 1)), pack_bf16_fast(f(8 * j + 2), f(8 * j + 3)),
+                                       pack_bf16_fast(f(8 * j + 4), f(8 * j + 5)), pack_bf16_fast(f(8 * j + 6), f(8 * j + 7)));
+                    else
+                        v = make_uint4(pack_f16_fast(f(8 * j), f(8 * j + 1)), pack_f16_fast(f(8 * j + 2), f(8 * j + 3)),
+                                       pack_f16_fast(f(8 * j + 4), f(8 * j + 5)), pack_f16_fast(f(8 * j + 6), f(8 * j + 7)));
+                    stage[lane * 8 + (chunk ^ (lane & 7))] = v;
+                }
             }
         }
         if (c0 + cpc >= DH) {  // O and the statistics are read: the buffer is free
