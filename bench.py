@@ -927,6 +927,27 @@ def extra_config3(torch, dev, small=False):
                      "roofline": {"bound": "hbm", "achieved": gbs, "peak": p["hbm"], "frac": gbs / p["hbm"],
                                   "bytes_per_step": bytes_, "note": "2 MB state is L2-resident between steps"}}
     del qd, kd, vd, gd, bd, od
+    # Batched decode: one token for each of 64 sequences (each its own 2 MB
+    # state; 128 MB of states, past the L2), one launch per step.
+    B = 8 if small else 64
+    states = [nm.DeltaNetState(hv, d, d, device=dev.index) for _ in range(B)]
+    for st_b in states:
+        st_b.tensor().normal_(0.0, 0.05, generator=g)
+    qb = norm(torch.randn(B, hk, d, device=dev, generator=g)) / math.sqrt(d)
+    kb = norm(torch.randn(B, hk, d, device=dev, generator=g))
+    vb = torch.randn(B, hv, d, device=dev, generator=g)
+    gb = -torch.nn.functional.softplus(torch.randn(B, hv, device=dev, generator=g))
+    bb = torch.sigmoid(torch.randn(B, hv, device=dev, generator=g))
+    ob = torch.empty(B, hv, d, device=dev)
+    ms_b = graph_time(torch, dev, lambda: nm.delta_step_batch(states, qb, kb, vb, gb, bb, hk, out=ob), 5, 8)
+    bytes_b = B * bytes_
+    gbs_b = bytes_b / (ms_b * 1e-3) / 1e9
+    res["decode_batch"] = {"batch": B, "us_per_step": ms_b * 1e3, "value": gbs_b, "unit": "GB/s",
+                           "tok_per_s": B / (ms_b * 1e-3),
+                           "roofline": {"bound": "hbm", "achieved": gbs_b, "peak": p["hbm"], "frac": gbs_b / p["hbm"],
+                                        "bytes_per_step": bytes_b, "kernel": "delta_step_batch_kernel",
+                                        "note": f"{B} sequences x 32 value heads, states {B * 2} MB (> L2)"}}
+    del states, qb, kb, vb, gb, bb, ob
     # the steps either side of the recurrence over the same T tokens: conv +
     # SiLU + L2 norms + gates from the packed projection, and the gated RMS norm
     C, W = 2 * hk * d + hv * d, 4

@@ -118,6 +118,7 @@ SIGNATURES = {
     "nmg_delta_head": [_vp, _i32, ctypes.POINTER(_vp)],
     "nmg_gated_delta_step": [_vp, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp],
     "nmg_delta_step": [_vp, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp],
+    "nmg_delta_step_batch": [ctypes.POINTER(_vp), _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp],
     "nmg_delta_prefill": [_vp, _i32, _i64, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _vp],
     "nmg_conv_create": [_i32, _i32, _i32, ctypes.POINTER(_vp)],
     "nmg_conv_destroy": [_vp],

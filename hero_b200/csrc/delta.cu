@@ -10,6 +10,8 @@
 // S), which is how both kernels split a head across threads and CTAs.
 #include <math.h>
 
+#include <algorithm>
+
 #include "delta.cuh"
 
 namespace nmg {
@@ -73,6 +75,85 @@ __global__ void __launch_bounds__(128) delta_step_kernel(float* __restrict__ sta
     o += __shfl_xor_sync(0xffffffffu, o, 8);
     o += __shfl_xor_sync(0xffffffffu, o, 16);
     if (rg == 0 && cv) out[(int64_t)h * dv + j] = o;
+}
+
+// ---- one token of many sequences ---------------------------------------------
+// The decode step of a batch of sequences, each with its own state (one
+// DeltaNetState per sequence, as the reference keeps one per PrefixState).
+// grid (dv / 64, heads, sequences); 128 threads; CTA = 64 value columns of
+// one head of one sequence.  Warp w owns columns 16w .. 16w + 15; lane =
+// (4-column group cg = lane & 3) x (row group rg = lane >> 2, 16 key rows), so
+// each thread streams 16 float4 of state (64 B runs per row, 8 rows per warp
+// instruction) and both reductions over the 128 key rows are three
+// xor-shuffles.  The state is read and written once: HBM-bound when the
+// batch's states exceed L2.
+constexpr int kMaxStepBatch = 128;  // sequences per launch carried in the parameter block
+
+struct StepBatchArgs {
+    float* state[kMaxStepBatch];  // [heads][128][dv] per sequence
+    const float* q;               // [B][hk][128]
+    const float* k;
+    const float* v;               // [B][heads][dv]
+    const float* gate;            // [B][heads]
+    const float* beta;
+    float* out;                   // [B][heads][dv]
+    int heads, hk, dv, seq0;      // seq0: this launch's first sequence within the batch
+};
+
+__global__ void __launch_bounds__(128) delta_step_batch_kernel(const __grid_constant__ StepBatchArgs a) {
+    constexpr int DK = 128, RPT = 16;
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    __shared__ float ks[DK], qs[DK];
+    const int h = blockIdx.y, bl = blockIdx.z, b = a.seq0 + bl;
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const int cg = lane & 3, rg = lane >> 2;
+    const int j0 = blockIdx.x * 64 + w * 16 + cg * 4;  // first of this thread's 4 value columns
+    const int kh = h % a.hk;
+    const int64_t hb = (int64_t)b * a.heads + h;
+    {
+        const int64_t qk = ((int64_t)b * a.hk + kh) * DK + threadIdx.x;
+        ks[threadIdx.x] = __ldg(a.k + qk);
+        qs[threadIdx.x] = __ldg(a.q + qk);
+    }
+    float* S = a.state[bl] + ((int64_t)h * DK + rg * RPT) * a.dv + j0;
+    float4 s[RPT];
+#pragma unroll
+    for (int r = 0; r < RPT; ++r) s[r] = __ldcs((const float4*)(S + (int64_t)r * a.dv));
+    const float decay = __expf(__ldg(a.gate + hb));
+    const float bt = __ldg(a.beta + hb);
+    const float4 vj = __ldg((const float4*)(a.v + hb * a.dv + j0));
+    __syncthreads();
+    float4 part = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int r = 0; r < RPT; ++r) {
+        const float kr = ks[rg * RPT + r];
+        s[r].x *= decay, s[r].y *= decay, s[r].z *= decay, s[r].w *= decay;
+        part.x = fmaf(s[r].x, kr, part.x), part.y = fmaf(s[r].y, kr, part.y);
+        part.z = fmaf(s[r].z, kr, part.z), part.w = fmaf(s[r].w, kr, part.w);
+    }
+#pragma unroll
+    for (int o = 4; o < 32; o <<= 1) {
+        part.x += __shfl_xor_sync(0xffffffffu, part.x, o), part.y += __shfl_xor_sync(0xffffffffu, part.y, o);
+        part.z += __shfl_xor_sync(0xffffffffu, part.z, o), part.w += __shfl_xor_sync(0xffffffffu, part.w, o);
+    }
+    const float4 d = make_float4((vj.x - part.x) * bt, (vj.y - part.y) * bt, (vj.z - part.z) * bt, (vj.w - part.w) * bt);
+    float4 o4 = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int r = 0; r < RPT; ++r) {
+        const float kr = ks[rg * RPT + r], qr = qs[rg * RPT + r];
+        s[r].x = fmaf(kr, d.x, s[r].x), s[r].y = fmaf(kr, d.y, s[r].y);
+        s[r].z = fmaf(kr, d.z, s[r].z), s[r].w = fmaf(kr, d.w, s[r].w);
+        o4.x = fmaf(s[r].x, qr, o4.x), o4.y = fmaf(s[r].y, qr, o4.y);
+        o4.z = fmaf(s[r].z, qr, o4.z), o4.w = fmaf(s[r].w, qr, o4.w);
+        __stcs((float4*)(S + (int64_t)r * a.dv), s[r]);
+    }
+#pragma unroll
+    for (int o = 4; o < 32; o <<= 1) {
+        o4.x += __shfl_xor_sync(0xffffffffu, o4.x, o), o4.y += __shfl_xor_sync(0xffffffffu, o4.y, o);
+        o4.z += __shfl_xor_sync(0xffffffffu, o4.z, o), o4.w += __shfl_xor_sync(0xffffffffu, o4.w, o);
+    }
+    if (rg == 0) *(float4*)(a.out + hb * a.dv + j0) = o4;
 }
 
 // Launch with programmatic stream serialisation (the kernel waits on its
@@ -305,4 +386,47 @@ extern "C" int nmg_delta_prefill(nmg_delta_state* st, int hk, int64_t T, const f
         r = nmg::delta_prefill_chunked(st, hk, T, q, k, v, gate, beta, out, chunk, (cudaStream_t)stream);
     if (prev != st->device) cudaSetDevice(prev);
     return r;
+}
+
+extern "C" int nmg_delta_step_batch(nmg_delta_state* const* states, int batch, int hk, const float* q, const float* k,
+                                    const float* v, const float* gate, const float* beta, float* out, void* stream) {
+    if (!states || batch < 0) return set_error(NMG_INVALID_ARGUMENT, "nmg_delta_step_batch: bad batch");
+    if (batch == 0) return NMG_OK;
+    const nmg_delta_state* s0 = states[0];
+    if (!s0) return set_error(NMG_INVALID_ARGUMENT, "nmg_delta_step_batch: null state");
+    if (hk <= 0 || hk > s0->heads) return set_error(NMG_INVALID_ARGUMENT, "nmg_delta_step_batch: bad key-head count %d", hk);
+    if (!q || !k || !v || !gate || !beta || !out) return set_error(NMG_INVALID_ARGUMENT, "nmg_delta_step_batch: null tensor");
+    for (int b = 0; b < batch; ++b) {
+        const nmg_delta_state* st = states[b];
+        if (!st || st->heads != s0->heads || st->dk != s0->dk || st->dv != s0->dv || st->device != s0->device)
+            return set_error(NMG_INVALID_ARGUMENT, "nmg_delta_step_batch: states differ in shape or device");
+    }
+    const int heads = s0->heads, dk = s0->dk, dv = s0->dv;
+    cudaStream_t s = (cudaStream_t)stream;
+    int prev = 0;
+    NMG_CUDA_TRY(cudaGetDevice(&prev));
+    if (prev != s0->device) NMG_CUDA_TRY(cudaSetDevice(s0->device));
+    int st = NMG_OK;
+    const bool vec = dk == 128 && dv % 64 == 0 && !(((uintptr_t)v | (uintptr_t)out) & 15);
+    if (vec) {
+        nmg::StepBatchArgs* a = new nmg::StepBatchArgs();
+        a->q = q, a->k = k, a->v = v, a->gate = gate, a->beta = beta, a->out = out;
+        a->heads = heads, a->hk = hk, a->dv = dv;
+        for (int b0 = 0; b0 < batch && st == NMG_OK; b0 += nmg::kMaxStepBatch) {
+            const int nb = std::min(nmg::kMaxStepBatch, batch - b0);
+            for (int i = 0; i < nb; ++i) a->state[i] = states[b0 + i]->data;
+            a->seq0 = b0;
+            const cudaError_t e = nmg::launch_pdl(nmg::delta_step_batch_kernel, dim3(dv / 64, heads, nb), dim3(128), s, *a);
+            if (e != cudaSuccess) st = set_error(NMG_CUDA_ERROR, "nmg_delta_step_batch: launch: %s", cudaGetErrorString(e));
+        }
+        delete a;
+    } else {
+        // Other shapes: the one-sequence step per sequence.
+        for (int b = 0; b < batch && st == NMG_OK; ++b) {
+            const int64_t qo = (int64_t)b * hk * dk, vo = (int64_t)b * heads * dv, go = (int64_t)b * heads;
+            st = nmg_delta_step(states[b], hk, q + qo, k + qo, v + vo, gate + go, beta + go, out + vo, stream);
+        }
+    }
+    if (prev != s0->device) cudaSetDevice(prev);
+    return st;
 }

@@ -341,6 +341,19 @@ def delta_step(state: DeltaNetState, q, k, v, gate, beta, hk: int, *, out=None) 
     return out
 
 
+def delta_step_batch(states, q, k, v, gate, beta, hk: int, *, out=None) -> torch.Tensor:
+    """One decode token for each sequence of a batch, each with its own state:
+    q,k [B,hk,dk], v [B,heads,dv], gate/beta [B,heads]; returns [B,heads,dv]."""
+    n = len(states)
+    s0 = states[0]
+    if out is None:
+        out = torch.empty(n, s0.heads, s0.dv, dtype=torch.float32, device=v.device)
+    arr = (ctypes.c_void_p * n)(*[st.handle.value for st in states])
+    call("nmg_delta_step_batch", arr, n, int(hk), _ptr(_dev(q)), _ptr(_dev(k)), _ptr(_dev(v)), _ptr(_dev(gate)),
+         _ptr(_dev(beta)), _ptr(out), _stream(v.device))
+    return out
+
+
 def delta_prefill(state: DeltaNetState, q, k, v, gate, beta, hk: int, *, chunk: int = 64, out=None) -> torch.Tensor:
     """T tokens of the recurrence: q,k [T,hk,dk], v [T,heads,dv], gate/beta [T,heads]."""
     T = v.shape[0]

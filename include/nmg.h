@@ -220,6 +220,17 @@ NMG_API int nmg_gated_delta_step(float* state_head, int dk, int dv, const float*
 NMG_API int nmg_delta_step(nmg_delta_state* state, int hk, const float* q, const float* k, const float* v, const float* gate,
                    const float* beta, float* out, void* stream);
 
+/* One decode token for each of `batch` sequences, each with its own state
+ * (the reference keeps one DeltaNetState per sequence's PrefixState and runs
+ * the head loop of qwen35.hpp:449-454 per sequence; this is that loop over a
+ * batch of sequences in one launch).  states[b]: handles of equal shape on one
+ * device; q,k: [batch][hk][dk]; v: [batch][heads][dv]; gate/beta:
+ * [batch][heads]; out: [batch][heads][dv].  Dk = 128 with Dv a multiple of 64
+ * (16-byte aligned v and out) streams the states in one kernel; other shapes
+ * run nmg_delta_step per sequence. */
+NMG_API int nmg_delta_step_batch(nmg_delta_state* const* states, int batch, int hk, const float* q, const float* k,
+                                 const float* v, const float* gate, const float* beta, float* out, void* stream);
+
 /* T tokens of the same recurrence (qwen35.hpp:436-456 over a prefill batch):
  * q,k: [T][hk][dk], v: [T][heads][dv], gate/beta: [T][heads],
  * out: [T][heads][dv].  chunk = 0 runs the token-sequential kernel; chunk = 64

@@ -183,6 +183,16 @@ private:
     nmg_delta_state* h_ = nullptr;
 };
 
+// One decode token for each of `batch` sequences, each with its own state
+// (the head loop of qwen35.hpp:449-454 run for a batch of sequences at once).
+template <size_t Heads, size_t Dk, size_t Dv>
+void delta_step_batch(DeltaNetState<Heads, Dk, Dv>* const* states, size_t batch, size_t hk, const float* q,
+                      const float* k, const float* v, const float* gate, const float* beta, float* out, void* stream) {
+    std::vector<nmg_delta_state*> hs(batch);
+    for (size_t b = 0; b < batch; ++b) hs[b] = states[b]->handle();
+    check(nmg_delta_step_batch(hs.data(), int(batch), int(hk), q, k, v, gate, beta, out, stream));
+}
+
 // CausalConv1dState<Channels, Width> (recurrent.hpp:63-110): the carried last
 // Width - 1 inputs of the depthwise causal conv, on the device.
 template <size_t Channels, size_t Width>

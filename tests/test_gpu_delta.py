@@ -170,3 +170,41 @@ def test_decode_attention_after_chunked_prefill(dev, dtype):
     for _ in range(2):
         got = nm.attend(cache, T(qq, dev).to(tdt), rows - 1, dh ** -0.5, out_dtype=torch.float32).cpu().numpy()
         assert_close(got, want, what=f"{dtype} decode after chunked prefill")
+
+
+@pytest.mark.parametrize("batch,steps", [(5, 3), (130, 1)])
+def test_step_batch_matches_oracle_per_sequence(dev, batch, steps):
+    # Decode steps for a batch of sequences, each with its own (non-zero)
+    # state: the batched kernel against the reference recurrence, sequence by
+    # sequence; 130 sequences take two launches.
+    hv, hk, d = 32, 16, 128
+    states, host = [], []
+    for b in range(batch):
+        s0 = _random_state(1000 + b, hv, d)
+        st = nm.DeltaNetState(hv, d, d)
+        st.tensor().copy_(T(s0, dev))
+        states.append(st)
+        host.append(s0)
+    for t in range(steps):
+        q, k, v, g, bt = delta_inputs(500 + t, batch, hk, hv, d)  # token axis used as the batch axis
+        out = nm.delta_step_batch(states, T(q, dev), T(k, dev), T(v, dev), T(g, dev), T(bt, dev), hk).cpu().numpy()
+        for b in range(batch):
+            wo, host[b] = oracle.delta_run(host[b], q[b:b + 1], k[b:b + 1], v[b:b + 1], g[b:b + 1], bt[b:b + 1], hk)
+            assert_close(out[b], wo[0], what=f"step {t} sequence {b}")
+    for b in (0, batch // 2, batch - 1):
+        assert_close(states[b].tensor().cpu().numpy(), host[b], what=f"state of sequence {b}")
+
+
+def test_step_batch_other_shapes_run_per_sequence(dev):
+    # Dv = 96 is not built for the batched kernel: the same result through the
+    # one-sequence step, launched per sequence.
+    hv, hk, dk, dv, batch = 4, 2, 64, 96, 3
+    states = [nm.DeltaNetState(hv, dk, dv) for _ in range(batch)]
+    q, k, _, g, bt = delta_inputs(77, batch, hk, hv, dk)
+    v = oracle.normal(77, 9, batch * hv * dv).reshape(batch, hv, dv)
+    out = nm.delta_step_batch(states, T(q, dev), T(k, dev), T(v, dev), T(g, dev), T(bt, dev), hk).cpu().numpy()
+    for b in range(batch):
+        wo, ws = oracle.delta_run(np.zeros((hv, dk, dv), np.float32), q[b:b + 1], k[b:b + 1], v[b:b + 1],
+                                  g[b:b + 1], bt[b:b + 1], hk)
+        assert_close(out[b], wo[0], what=f"sequence {b}")
+        assert_close(states[b].tensor().cpu().numpy(), ws, what=f"state {b}")
