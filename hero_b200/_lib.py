@@ -15,7 +15,7 @@ LIB_PATH = os.path.join(HERE, "libnmg.so")
 
 OK, INVALID_ARGUMENT, OUT_OF_RANGE, RUNTIME_ERROR, LENGTH_ERROR, LOGIC_ERROR = 0, 1, 2, 3, 4, 5
 CUDA_ERROR, DEVICE_TIMEOUT, COMM_ERROR, UNSUPPORTED, VALUE_OVERFLOW = 6, 7, 8, 9, 10
-F32, F16, BF16 = 0, 1, 2
+F32, F16, BF16, Q8_0 = 0, 1, 2, 3
 
 
 class NmgError(Exception):
@@ -106,6 +106,7 @@ SIGNATURES = {
     "nmg_kv_end_batch_retention": [_vp],
     "nmg_kv_read_row": [_vp, _i64, _i32, ctypes.POINTER(_f32), ctypes.POINTER(_f32), _vp],
     "nmg_kv_storage": [_vp, ctypes.POINTER(_vp), ctypes.POINTER(_vp), _i64p],
+    "nmg_kv_scales": [_vp, ctypes.POINTER(_vp), ctypes.POINTER(_vp), _i64p],
     "nmg_kv_reset": [_vp],
     "nmg_attend": [_vp, _i32, _vp, _i32, _i64, _i64, _f32, _i32, _vp, _i32, _vp],
     "nmg_append_attend": [_vp, _i64, _vp, _vp, _i32, _i32, _vp, _i32, _i64, _f32, _i32, _vp, _i32, _vp],

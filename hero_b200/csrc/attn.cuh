@@ -168,12 +168,14 @@ int attend_batch_split(const nmg_kv_cache* const* caches, int batch, const int64
 // 64 elements x box_rows rows with the 128-byte swizzle (attn_prefill_sm100.cu).
 int make_kv_tensor_maps(const nmg_kv_cache* c, int box_rows, CUtensorMap* k, CUtensorMap* v);
 
-// Tensor-core (mma.sync) split-KV decode for 16-bit caches (attn_decode_mma.cu).
+// Tensor-core (mma.sync) split-KV decode for 16-bit caches with a query of the
+// cache's dtype, and for Q8_0 caches with any query dtype (attn_decode_mma.cu).
 bool decode_mma_supported(const nmg_kv_cache* c, int q_dtype);
-int attend_rows_mma(const nmg_kv_cache* c, int hq, const void* q, int64_t rows, int64_t first_query, int64_t window,
-                    int64_t floor_pos, int64_t newest, float scale, void* out, int out_dtype, cudaStream_t stream);
+int attend_rows_mma(const nmg_kv_cache* c, int hq, const void* q, int q_dtype, int64_t rows, int64_t first_query,
+                    int64_t window, int64_t floor_pos, int64_t newest, float scale, void* out, int out_dtype,
+                    cudaStream_t stream);
 int attend_batch_mma(const nmg_kv_cache* const* caches, int batch, const int64_t* queries_at, int hq, const void* q,
-                     float scale, void* out, int out_dtype, cudaStream_t stream);
+                     int q_dtype, float scale, void* out, int out_dtype, cudaStream_t stream);
 
 // tcgen05 flash prefill (attn_prefill_sm100.cu).  Returns NMG_UNSUPPORTED
 // when the shape is not one it was built for.

@@ -38,8 +38,10 @@ int dispatch_rows(const nmg_kv_cache* c, int hq, const void* q, int q_dtype, int
         st = nmg::attend_rows_prefill(c, hq, q, q_dtype, rows, first_query, window, floor_pos, newest, scale, &out, 1,
                                       (int64_t)hq * c->dh, 0, out_dtype, stream);
     else if (nmg::decode_mma_supported(c, q_dtype))
-        st = nmg::attend_rows_mma(c, hq, q, rows, first_query, window, floor_pos, newest, scale, out, out_dtype,
+        st = nmg::attend_rows_mma(c, hq, q, q_dtype, rows, first_query, window, floor_pos, newest, scale, out, out_dtype,
                                   stream);
+    else if (c->dtype == NMG_Q8_0)
+        st = set_error(NMG_UNSUPPORTED, "attention over a Q8_0 cache: head_dim %d is not built", c->dh);
     else
         st = nmg::attend_rows_split(c, hq, q, q_dtype, rows, first_query, window, floor_pos, newest, scale, out,
                                     out_dtype, stream, nullptr, 0);
@@ -175,8 +177,10 @@ extern "C" int nmg_attend_batch(const nmg_kv_cache* const* caches, int batch, co
     bool mma = true;
     for (int b = 0; b < batch; ++b) mma = mma && nmg::decode_mma_supported(caches[b], q_dtype);
     if (mma)
-        st = nmg::attend_batch_mma(caches, batch, queries_at, hq, q, use_scale ? scale : 1.f, out, out_dtype,
+        st = nmg::attend_batch_mma(caches, batch, queries_at, hq, q, q_dtype, use_scale ? scale : 1.f, out, out_dtype,
                                    (cudaStream_t)stream);
+    else if (c0->dtype == NMG_Q8_0)
+        st = set_error(NMG_UNSUPPORTED, "attention over Q8_0 caches: head_dim %d is not built", c0->dh);
     else
         st = nmg::attend_batch_split(caches, batch, queries_at, hq, q, q_dtype, use_scale ? scale : 1.f, out, out_dtype,
                                      (cudaStream_t)stream);

@@ -380,6 +380,7 @@ int dispatch_g(int gt, const SplitArgs& a, dim3 grid, cudaStream_t s) {
 }
 
 int dispatch_split(int kvdt, int dh, int gt, const SplitArgs& a, dim3 grid, cudaStream_t s) {
+    if (kvdt == NMG_Q8_0) return set_error(NMG_UNSUPPORTED, "split-KV attention: Q8_0 caches are not built");
     if (kvdt == NMG_F32) {
         switch (dh) {
             case 1: return dispatch_g<NMG_F32, 1>(gt, a, grid, s);
@@ -643,6 +644,7 @@ extern "C" int nmg_attend_noalloc(const nmg_kv_cache* c, int hq, const void* q, 
                                   void* stream) {
     using namespace nmg;
     if (!c) return set_error(NMG_INVALID_ARGUMENT, "nmg_attend_noalloc: null cache");
+    if (c->dtype == NMG_Q8_0) return set_error(NMG_UNSUPPORTED, "nmg_attend_noalloc: Q8_0 caches are not supported");
     if (hq <= 0 || hq % c->hkv != 0)
         return set_error(NMG_INVALID_ARGUMENT, "attention: %d query heads is not a multiple of %d K/V heads", hq, c->hkv);
     if (!dtype_valid(q_dtype) || !dtype_valid(out_dtype)) return set_error(NMG_INVALID_ARGUMENT, "attention: bad dtype");

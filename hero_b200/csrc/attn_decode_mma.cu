@@ -35,9 +35,20 @@ struct MmaSeq {
     int32_t work_first, nsplit, qrow, map;
 };
 
+// A Q8_0 cache's int8 quants [hkv][slots][DH] and fp16 scales [hkv][slots][DH / 32].
+struct Q8Src {
+    const int8_t* k;
+    const int8_t* v;
+    const uint16_t* ks;  // scale row of slot s of head h: h * sstride + s
+    const uint16_t* vs;
+    int64_t sstride;
+};
+
 struct MmaArgs {
     CUtensorMap tm_k[kMmaMaxBatch];  // K of each distinct cache, (d, hkv*slots)
     CUtensorMap tm_v[kMmaMaxBatch];
+    Q8Src q8[kMmaMaxBatch];          // the same caches when they are Q8_0 (no tensor maps then)
+    int q_dtype;                     // Q8_0 caches: the query's dtype, staged as fp16
     int mode;  // 0: one cache, rows first_query..; 1: table
     int hkv, hq, gtot, zdim;
     int64_t blocks_per_split;
@@ -95,22 +106,29 @@ __device__ __forceinline__ bool mma_row(const MmaArgs& a, int64_t w, MmaRow& r) 
     return r.s < r.nsplit;
 }
 
-template <int DH>
+template <int DH, bool Q8 = false>
 struct MmaCfg {
     // head_dim 256: one stage, so two CTAs fit an SM and overlap each other's
     // loads (measured: sliding-window decode 24.8 -> 18.6 us, global 372 -> 362 us
     // against two stages at one CTA per SM)
-    static constexpr int STAGES = DH <= 128 ? 3 : 1;
-    static constexpr int TILE_BYTES = KT * DH * 2;  // one of K or V
-    static constexpr int STAGE_BYTES = 2 * TILE_BYTES;
+    static constexpr int STAGES = Q8 ? (DH <= 128 ? 4 : 2) : (DH <= 128 ? 3 : 1);
+    static constexpr int TILE_BYTES = KT * DH * 2;  // one of K or V as fp16 / bf16
+    // Q8_0: a stage holds the raw tile (K quants, V quants, K scales, V scales);
+    // the fp16 K and V tiles the MMAs read are one buffer after the stages.
+    static constexpr int Q8_QBYTES = KT * DH, Q8_SBYTES = KT * (DH / 32) * 2;
+    static constexpr int STAGE_BYTES = Q8 ? 2 * (Q8_QBYTES + Q8_SBYTES) : 2 * TILE_BYTES;
+    static constexpr int F16_OFF = STAGES * STAGE_BYTES;  // Q8_0 only
+    static constexpr int LOAD_END = Q8 ? F16_OFF + 2 * TILE_BYTES : STAGES * STAGE_BYTES;
     // The warp merge ([4][16][DH + 2] fp32) reuses the stage memory, idle by then.
     static constexpr int MERGE_BYTES = (4 * 16 * (DH + 2) * 4 + 1023) / 1024 * 1024;
-    static constexpr int Q_OFF = STAGES * STAGE_BYTES > MERGE_BYTES ? STAGES * STAGE_BYTES : MERGE_BYTES;  // 16 x DH query rows
+    static constexpr int Q_OFF = LOAD_END > MERGE_BYTES ? LOAD_END : MERGE_BYTES;  // 16 x DH query rows
     static constexpr int Q_PITCH = DH * 2 + 16;                 // bytes per staged query row
     static constexpr int C_OFF = 0;
     static constexpr int BAR_OFF = Q_OFF + 16 * Q_PITCH;
     static constexpr int SMEM = BAR_OFF + 64 + 1024;            // + alignment slack
     static_assert(SMEM <= 232448, "shared memory budget");
+    static_assert(!Q8 || (Q8_QBYTES % 16 == 0 && Q8_SBYTES % 16 == 0 && F16_OFF % 1024 == 0),
+                  "bulk copies move 16-byte multiples; the fp16 tiles keep the 128-byte swizzle atoms aligned");
 };
 
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
@@ -159,9 +177,9 @@ __device__ __forceinline__ uint32_t tile_off(int key, int chunk) {
     return (uint32_t)((chunk >> 3) * (KT * 128) + key * 128 + (((chunk & 7) ^ (key & 7)) << 4));
 }
 
-template <int DH, bool BF16>
+template <int DH, bool BF16, bool Q8 = false>
 __global__ void __launch_bounds__(128) attn_decode_mma_kernel(const __grid_constant__ MmaArgs a) {
-    using C = MmaCfg<DH>;
+    using C = MmaCfg<DH, Q8>;
     constexpr int ST = C::STAGES;
     extern __shared__ unsigned char smem_raw[];
     unsigned char* smem = (unsigned char*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -190,7 +208,18 @@ __global__ void __launch_bounds__(128) attn_decode_mma_kernel(const __grid_const
     for (int i = tid; i < 16 * (DH / 8); i += 128) {
         const int g = i / (DH / 8), c8 = i % (DH / 8);
         uint4 v = make_uint4(0, 0, 0, 0);
-        if (g < G) v = *(const uint4*)((const uint16_t*)a.q + (r.qrow * (int64_t)a.hq + qh0 + g) * DH + c8 * 8);
+        if constexpr (Q8) {  // the query as fp16, from whatever dtype it came in
+            if (g < G) {
+                const int64_t q0 = (r.qrow * (int64_t)a.hq + qh0 + g) * DH + c8 * 8;
+                uint32_t w[4];
+#pragma unroll
+                for (int u = 0; u < 4; ++u)
+                    w[u] = pack_h2(dev::load_as_f32(a.q, a.q_dtype, q0 + 2 * u), dev::load_as_f32(a.q, a.q_dtype, q0 + 2 * u + 1));
+                v = make_uint4(w[0], w[1], w[2], w[3]);
+            }
+        } else if (g < G) {
+            v = *(const uint4*)((const uint16_t*)a.q + (r.qrow * (int64_t)a.hq + qh0 + g) * DH + c8 * 8);
+        }
         *(uint4*)(smem + C::Q_OFF + g * C::Q_PITCH + c8 * 16) = v;
     }
     __syncthreads();
@@ -201,10 +230,23 @@ __global__ void __launch_bounds__(128) attn_decode_mma_kernel(const __grid_const
             const int32_t row = (int32_t)(h * r.slots + u0 % r.slots);
             dev::fence_proxy_async_smem();
             dev::mbar_arrive_expect_tx(&full[st], C::STAGE_BYTES);
+            if constexpr (Q8) {
+                // 64 consecutive slots of the head: contiguous quant rows and scales
+                // (the buffers carry 64 spare rows past the last head).
+                const Q8Src& q8 = a.q8[r.map];
+                unsigned char* dst = smem + st * C::STAGE_BYTES;
+                dev::bulk_g2s(dst, q8.k + (int64_t)row * DH, C::Q8_QBYTES, &full[st]);
+                dev::bulk_g2s(dst + C::Q8_QBYTES, q8.v + (int64_t)row * DH, C::Q8_QBYTES, &full[st]);
+                const int64_t srow = (int64_t)h * q8.sstride + u0 % r.slots;
+                dev::bulk_g2s(dst + 2 * C::Q8_QBYTES, q8.ks + srow * (DH / 32), C::Q8_SBYTES, &full[st]);
+                dev::bulk_g2s(dst + 2 * C::Q8_QBYTES + C::Q8_SBYTES, q8.vs + srow * (DH / 32), C::Q8_SBYTES, &full[st]);
+            } else {
 #pragma unroll
-            for (int c = 0; c < DH / 64; ++c) {
-                dev::tma_load_2d(smem + st * C::STAGE_BYTES + c * KT * 128, tmk, c * 64, row, &full[st]);
-                dev::tma_load_2d(smem + st * C::STAGE_BYTES + C::TILE_BYTES + c * KT * 128, tmv, c * 64, row, &full[st]);
+                for (int c = 0; c < DH / 64; ++c) {
+                    dev::tma_load_2d(smem + st * C::STAGE_BYTES + c * KT * 128, tmk, c * 64, row, &full[st]);
+                    dev::tma_load_2d(smem + st * C::STAGE_BYTES + C::TILE_BYTES + c * KT * 128, tmv, c * 64, row,
+                                     &full[st]);
+                }
             }
         }
     };
@@ -237,7 +279,34 @@ __global__ void __launch_bounds__(128) attn_decode_mma_kernel(const __grid_const
             aborted = true;
             break;
         }
-        const uint32_t kbase = dev::smem_u32(smem + st * C::STAGE_BYTES);
+        uint32_t kbase = dev::smem_u32(smem + st * C::STAGE_BYTES);
+        if constexpr (Q8) {
+            // scale * quant of every K and V value of the tile, as fp16 into the
+            // swizzled layout the MMA loop reads; 8 values (one 16-byte chunk)
+            // at a time, consecutive threads on consecutive chunks of a row.
+            const unsigned char* raw = smem + st * C::STAGE_BYTES;
+            unsigned char* f16 = smem + C::F16_OFF;
+#pragma unroll 2
+            for (int i = tid; i < 2 * KT * (DH / 8); i += 128) {
+                const int mat = i / (KT * (DH / 8)), rem = i % (KT * (DH / 8));
+                const int key = rem / (DH / 8), c8 = rem % (DH / 8);
+                const uint2 q = *(const uint2*)(raw + mat * C::Q8_QBYTES + key * DH + c8 * 8);
+                const uint16_t sb = *(const uint16_t*)(raw + 2 * C::Q8_QBYTES + mat * C::Q8_SBYTES +
+                                                       (key * (DH / 32) + c8 / 4) * 2);
+                const float sc = dev::f16_bits_to_f32(sb);
+                const uint32_t qw[2] = {q.x, q.y};
+                uint32_t w[4];
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const int32_t b0 = (int32_t)(qw[u >> 1] << (24 - 16 * (u & 1))) >> 24;
+                    const int32_t b1 = (int32_t)(qw[u >> 1] << (16 - 16 * (u & 1))) >> 24;
+                    w[u] = pack_h2(sc * (float)b0, sc * (float)b1);
+                }
+                *(uint4*)(f16 + mat * C::TILE_BYTES + tile_off<DH>(key, c8)) = make_uint4(w[0], w[1], w[2], w[3]);
+            }
+            __syncthreads();
+            kbase = dev::smem_u32(f16);
+        }
         const uint32_t vbase = kbase + C::TILE_BYTES;
         const int key0 = wid * 16;  // this warp's keys within the tile
 
@@ -386,10 +455,10 @@ __global__ void __launch_bounds__(128) attn_decode_mma_kernel(const __grid_const
     if (tid == 0) a.counters[cnt_idx] = 0;
 }
 
-template <int DH, bool BF16>
+template <int DH, bool BF16, bool Q8 = false>
 int launch_mma(const MmaArgs& a, dim3 grid, cudaStream_t s) {
-    using C = MmaCfg<DH>;
-    auto kern = attn_decode_mma_kernel<DH, BF16>;
+    using C = MmaCfg<DH, Q8>;
+    auto kern = attn_decode_mma_kernel<DH, BF16, Q8>;
     static std::atomic<uint64_t> attr_set{0};  // one bit per device
     const int st = set_smem_once(kern, C::SMEM, attr_set);
     if (st != NMG_OK) return st;
@@ -400,6 +469,14 @@ int launch_mma(const MmaArgs& a, dim3 grid, cudaStream_t s) {
 
 int dispatch_mma(const nmg_kv_cache* c, const MmaArgs& a, dim3 grid, cudaStream_t s) {
     const bool bf = c->dtype == NMG_BF16;
+    if (c->dtype == NMG_Q8_0) {
+        switch (c->dh) {
+            case 64: return launch_mma<64, false, true>(a, grid, s);
+            case 128: return launch_mma<128, false, true>(a, grid, s);
+            case 256: return launch_mma<256, false, true>(a, grid, s);
+        }
+        return set_error(NMG_UNSUPPORTED, "Q8_0 decode: head_dim %d", c->dh);
+    }
     switch (c->dh) {
         case 64: return bf ? launch_mma<64, true>(a, grid, s) : launch_mma<64, false>(a, grid, s);
         case 128: return bf ? launch_mma<128, true>(a, grid, s) : launch_mma<128, false>(a, grid, s);
@@ -435,17 +512,28 @@ int mma_scratch(int device, int64_t work, int hkv, int zdim, int dh, int64_t cou
 }  // namespace
 
 bool decode_mma_supported(const nmg_kv_cache* c, int q_dtype) {
-    if (c->dtype == NMG_F32 || q_dtype != c->dtype) return false;
+    if (c->dtype != NMG_Q8_0 && (c->dtype == NMG_F32 || q_dtype != c->dtype)) return false;
     if (c->dh != 64 && c->dh != 128 && c->dh != 256) return false;
     if (c->window > 0 && c->slots % KT != 0) return false;  // a tile must not straddle the ring end
     if ((int64_t)c->hkv * c->slots > 0x7FFFFFFF) return false;
     return true;
 }
 
-int attend_rows_mma(const nmg_kv_cache* c, int hq, const void* q, int64_t rows, int64_t first_query, int64_t window,
-                    int64_t floor_pos, int64_t newest, float scale, void* out, int out_dtype, cudaStream_t stream) {
+// Where the kernel reads cache i: tensor maps of a 16-bit cache, raw pointers of a Q8_0 one.
+static int kv_sources(const nmg_kv_cache* c, MmaArgs* a, int i) {
+    if (c->dtype == NMG_Q8_0) {
+        a->q8[i] = Q8Src{(const int8_t*)c->k, (const int8_t*)c->v, (const uint16_t*)c->ks, (const uint16_t*)c->vs,
+                         c->sstride};
+        return NMG_OK;
+    }
+    return make_kv_tensor_maps(c, KT, &a->tm_k[i], &a->tm_v[i]);
+}
+
+int attend_rows_mma(const nmg_kv_cache* c, int hq, const void* q, int q_dtype, int64_t rows, int64_t first_query,
+                    int64_t window, int64_t floor_pos, int64_t newest, float scale, void* out, int out_dtype,
+                    cudaStream_t stream) {
     MmaArgs* a = new MmaArgs();
-    int st = make_kv_tensor_maps(c, KT, &a->tm_k[0], &a->tm_v[0]);
+    int st = kv_sources(c, a, 0);
     const int gtot = hq / c->hkv;
     const int zdim = (gtot + 15) / 16;
     int64_t longest = 0, total_blocks = 0;
@@ -478,6 +566,7 @@ int attend_rows_mma(const nmg_kv_cache* c, int hq, const void* q, int64_t rows, 
         a->max_splits = (int32_t)max_splits;
         a->nseq = 0;
         a->q = q;
+        a->q_dtype = q_dtype;
         a->out = out;
         a->out_dtype = out_dtype;
         a->scale_log2 = scale * 1.4426950408889634f;
@@ -488,7 +577,7 @@ int attend_rows_mma(const nmg_kv_cache* c, int hq, const void* q, int64_t rows, 
 }
 
 int attend_batch_mma(const nmg_kv_cache* const* caches, int batch, const int64_t* queries_at, int hq, const void* q,
-                     float scale, void* out, int out_dtype, cudaStream_t stream) {
+                     int q_dtype, float scale, void* out, int out_dtype, cudaStream_t stream) {
     const nmg_kv_cache* c0 = caches[0];
     const int gtot = hq / c0->hkv;
     const int zdim = (gtot + 15) / 16;
@@ -521,7 +610,7 @@ int attend_batch_mma(const nmg_kv_cache* const* caches, int batch, const int64_t
         int64_t w = 0;
         for (int i = 0; st == NMG_OK && i < nb; ++i) {
             const nmg_kv_cache* c = caches[b0 + i];
-            st = make_kv_tensor_maps(c, KT, &a->tm_k[i], &a->tm_v[i]);
+            st = kv_sources(c, a, i);
             MmaSeq& e = a->seq[i];
             e.base = c->base;
             e.slots = c->slots;
@@ -542,6 +631,7 @@ int attend_batch_mma(const nmg_kv_cache* const* caches, int batch, const int64_t
         a->blocks_per_split = bps;
         a->nseq = nb;
         a->q = q;
+        a->q_dtype = q_dtype;
         a->out = out;
         a->out_dtype = out_dtype;
         a->scale_log2 = scale * 1.4426950408889634f;

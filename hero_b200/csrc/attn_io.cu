@@ -476,6 +476,20 @@ extern "C" int nmg_attn_prologue(nmg_kv_cache* cache, int hq, int64_t position, 
     if (T <= 0) return T < 0 ? set_error(NMG_INVALID_ARGUMENT, "nmg_attn_prologue: negative rows") : NMG_OK;
     if (!q || !k || !v || !q_gamma || !k_gamma || !q_out)  // before the cache's bookkeeping moves
         return set_error(NMG_INVALID_ARGUMENT, "nmg_attn_prologue: null argument");
+    if (cache->dtype == NMG_Q8_0) {
+        // A Q8_0 cache quantises whole rows on append: prepare K (and V) in
+        // fp32 staging, then append them through the quantiser.
+        const int64_t n = T * cache->hkv * cache->dh;
+        void* stage = nullptr;
+        int st = device_staging(cache->device, (size_t)n * 4 * (v_norm ? 2 : 1), &stage);
+        if (st != NMG_OK) return st;
+        float* ks = (float*)stage;
+        float* vs = v_norm ? ks + n : nullptr;
+        st = nmg_attn_prepare(hq, cache->hkv, cache->dh, position, T, q, q_gated, k, v, q_gamma, k_gamma, v_norm, eps,
+                              rope_base, rotary_num, rotary_den, q_out, q_dtype, ks, vs, stream);
+        if (st != NMG_OK) return st;
+        return nmg_kv_append(cache, position, ks, v_norm ? (const void*)vs : (const void*)v, T, NMG_F32, stream);
+    }
     int* err = nullptr;  // made with the cache, so no allocation here
     int st = device_error_flag(cache->device, &err);
     if (st != NMG_OK) return st;

@@ -85,6 +85,58 @@ __global__ void kv_append_copy16_kernel(const uint4* __restrict__ keys, const ui
     if (V_TO_F16 && overflow) atomicOr(err, dev::kErrF16Overflow);
 }
 
+// Q8_0 append: one warp per (row, head); lane l takes values 4l .. 4l + 3 of
+// each 128-value group, so a 32-value block is 8 lanes and its maximum three
+// xor-shuffles.  quantize_row_q8_0 (nm/src/quant_i8.hpp:69-81) exactly:
+// d = amax / 127, id = d ? 1 / d : 0, the scale stored as fp16 with the
+// reference's rounding, q = roundf(x * id).
+template <int SRC>
+__global__ void kv_append_q8_kernel(const void* __restrict__ keys, const void* __restrict__ values,
+                                    int8_t* __restrict__ kq, int8_t* __restrict__ vq, uint16_t* __restrict__ ks,
+                                    uint16_t* __restrict__ vs, int64_t rows, int64_t src_row0, int hkv, int dh,
+                                    int64_t slots, int64_t sstride, int64_t slot0, int* __restrict__ err) {
+    const int lane = threadIdx.x & 31;
+    const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    bool overflow = false;
+    for (int64_t wi = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5); wi < rows * hkv; wi += nwarps) {
+        const int h = (int)(wi % hkv);
+        const int64_t r = wi / hkv;
+        const int64_t slot = (slot0 + r) % slots;
+        const int64_t src = (src_row0 + r) * (int64_t)hkv * dh + (int64_t)h * dh;
+        const int64_t dst = (int64_t)h * slots + slot, sdst = (int64_t)h * sstride + slot;
+        for (int g0 = 0; g0 < dh; g0 += 128) {
+            const int e0 = g0 + 4 * lane;
+            const bool in = e0 < dh;
+#pragma unroll
+            for (int which = 0; which < 2; ++which) {
+                const void* in_rows = which ? values : keys;
+                float x[4];
+                float amax = 0.f;
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    x[u] = in ? dev::load_as_f32(in_rows, SRC, src + e0 + u) : 0.f;
+                    amax = fmaxf(amax, fabsf(x[u]));
+                }
+                amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+                amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+                amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 4));
+                if (!in) continue;
+                const float d = amax / 127.f;
+                const float id = d != 0.f ? 1.f / d : 0.f;
+                uint32_t packed = 0;
+#pragma unroll
+                for (int u = 0; u < 4; ++u) packed |= ((uint32_t)(uint8_t)(int8_t)(int)roundf(x[u] * id)) << (8 * u);
+                int8_t* q = which ? vq : kq;
+                uint16_t* sc = which ? vs : ks;
+                *(uint32_t*)(q + dst * dh + e0) = packed;
+                if ((lane & 7) == 0) sc[sdst * (dh / 32) + e0 / 32] = dev::f32_to_f16_bits(d);
+                overflow |= amax > 65504.f;  // the attention kernels take scale * quant as fp16
+            }
+        }
+    }
+    if (overflow) atomicOr(err, dev::kErrF16Overflow);
+}
+
 template <int SRC>
 int launch_append(int dst, const void* k, const void* v, void* kc, void* vc, int64_t rows, int64_t row0, int hkv,
                   int dh, int64_t slots, int64_t slot0, cudaStream_t s, int blocks, int* err) {
@@ -114,6 +166,24 @@ int kv_append_device(nmg_kv_cache* c, int64_t first_position, const void* keys, 
     int prev = 0;
     NMG_CUDA_TRY(cudaGetDevice(&prev));
     if (prev != c->device) NMG_CUDA_TRY(cudaSetDevice(c->device));
+    if (c->dtype == NMG_Q8_0) {
+        const int64_t warps = write * c->hkv;
+        const int blocks = (int)((warps + 7) / 8 < 148 * 16 ? (warps + 7) / 8 : 148 * 16);
+        int8_t *kq = (int8_t*)c->k, *vq = (int8_t*)c->v;
+        uint16_t *ks = (uint16_t*)c->ks, *vs = (uint16_t*)c->vs;
+        if (src_dtype == NMG_F32)
+            kv_append_q8_kernel<NMG_F32><<<blocks, 256, 0, stream>>>(keys, values, kq, vq, ks, vs, write, row0, c->hkv,
+                                                                      c->dh, c->slots, c->sstride, slot0, err);
+        else if (src_dtype == NMG_F16)
+            kv_append_q8_kernel<NMG_F16><<<blocks, 256, 0, stream>>>(keys, values, kq, vq, ks, vs, write, row0, c->hkv,
+                                                                      c->dh, c->slots, c->sstride, slot0, err);
+        else
+            kv_append_q8_kernel<NMG_BF16><<<blocks, 256, 0, stream>>>(keys, values, kq, vq, ks, vs, write, row0,
+                                                                       c->hkv, c->dh, c->slots, c->sstride, slot0, err);
+        NMG_CUDA_TRY(cudaGetLastError());
+        if (prev != c->device) NMG_CUDA_TRY(cudaSetDevice(prev));
+        return NMG_OK;
+    }
     const int es = dtype_size(c->dtype);
     if (src_dtype == c->dtype && (c->dh * es) % 16 == 0 && ((uintptr_t)keys % 16) == 0 && ((uintptr_t)values % 16) == 0) {
         const int vecs = c->dh * es / 16;
@@ -154,7 +224,9 @@ extern "C" int nmg_kv_create(int hkv, int head_dim, int dtype, int64_t window, i
     if (!out) return set_error(NMG_INVALID_ARGUMENT, "nmg_kv_create: null out");
     *out = nullptr;
     if (hkv <= 0 || head_dim <= 0) return set_error(NMG_INVALID_ARGUMENT, "nmg_kv_create: hkv and head_dim must be positive");
-    if (!nmg::dtype_valid(dtype)) return set_error(NMG_INVALID_ARGUMENT, "nmg_kv_create: bad dtype %d", dtype);
+    if (!nmg::cache_dtype_valid(dtype)) return set_error(NMG_INVALID_ARGUMENT, "nmg_kv_create: bad dtype %d", dtype);
+    if (dtype == NMG_Q8_0 && head_dim % 32 != 0)
+        return set_error(NMG_UNSUPPORTED, "nmg_kv_create: a Q8_0 cache needs head_dim a multiple of 32");
     if (window < 0) return set_error(NMG_INVALID_ARGUMENT, "LocalAttentionCache: window must be positive");
     if (capacity <= 0) return set_error(NMG_INVALID_ARGUMENT, "nmg_kv_create: capacity must be positive");
     if (window > 0 && capacity < window)
@@ -170,12 +242,23 @@ extern "C" int nmg_kv_create(int hkv, int head_dim, int dtype, int64_t window, i
     int prev = 0;
     cudaError_t e = cudaGetDevice(&prev);
     if (e == cudaSuccess) e = cudaSetDevice(device);
-    const size_t bytes = (size_t)hkv * (size_t)capacity * (size_t)head_dim * nmg::dtype_size(dtype);
+    // A Q8_0 cache's kernels stream whole 64-row tiles with bulk copies, so its
+    // buffers carry 64 zeroed rows past the last head's slots.
+    const size_t rows_alloc = (size_t)hkv * (size_t)capacity + (dtype == NMG_Q8_0 ? 64 : 0);
+    const size_t bytes = rows_alloc * (size_t)head_dim * nmg::cache_elem_size(dtype);
     if (e == cudaSuccess) e = cudaMalloc(&c->k, bytes);
     if (e == cudaSuccess) e = cudaMalloc(&c->v, bytes);
     // Zeroed like the reference's ring storage (attention.hpp:363-372).
     if (e == cudaSuccess) e = cudaMemset(c->k, 0, bytes);
     if (e == cudaSuccess) e = cudaMemset(c->v, 0, bytes);
+    if (dtype == NMG_Q8_0) {
+        c->sstride = (capacity + 63) / 64 * 64;
+        const size_t sbytes = ((size_t)hkv * (size_t)c->sstride + 64) * (size_t)(head_dim / 32) * 2;
+        if (e == cudaSuccess) e = cudaMalloc(&c->ks, sbytes);
+        if (e == cudaSuccess) e = cudaMalloc(&c->vs, sbytes);
+        if (e == cudaSuccess) e = cudaMemset(c->ks, 0, sbytes);
+        if (e == cudaSuccess) e = cudaMemset(c->vs, 0, sbytes);
+    }
     // The device's error flag, which appends raise on fp16 overflow of V:
     // created here so that no later call (possibly under stream capture)
     // has to allocate it.
@@ -185,6 +268,8 @@ extern "C" int nmg_kv_create(int hkv, int head_dim, int dtype, int64_t window, i
     if (e != cudaSuccess) {
         if (c->k) cudaFree(c->k);
         if (c->v) cudaFree(c->v);
+        if (c->ks) cudaFree(c->ks);
+        if (c->vs) cudaFree(c->vs);
         delete c;
         return set_error(NMG_CUDA_ERROR, "nmg_kv_create: %s", cudaGetErrorString(e));
     }
@@ -199,6 +284,8 @@ extern "C" int nmg_kv_destroy(nmg_kv_cache* c) {
     cudaSetDevice(c->device);
     cudaFree(c->k);
     cudaFree(c->v);
+    if (c->ks) cudaFree(c->ks);
+    if (c->vs) cudaFree(c->vs);
     cudaSetDevice(prev);
     delete c;
     return NMG_OK;
@@ -349,9 +436,30 @@ extern "C" int nmg_kv_read_row(const nmg_kv_cache* c, int64_t row, int head, flo
     const char* who = c->window ? "LocalAttentionCache" : "FullAttentionCache";
     if (head < 0 || head >= c->hkv) return set_error(NMG_OUT_OF_RANGE, "%s: K/V head out of range", who);
     if (row < 0 || row >= c->size) return set_error(NMG_OUT_OF_RANGE, "%s: row out of range", who);
-    const int es = nmg::dtype_size(c->dtype);
+    const int es = nmg::cache_elem_size(c->dtype);
     const int64_t slot = c->slot_of(c->oldest + row);
     const size_t off = ((size_t)head * c->slots + slot) * c->dh * es;
+    if (c->dtype == NMG_Q8_0) {  // key(row, head) of a Q8_0 cache: scale * quant, exactly
+        const int nb = c->dh / 32;
+        std::vector<int8_t> kq(c->dh), vq(c->dh);
+        std::vector<uint16_t> kd(nb), vd(nb);
+        const size_t soff = ((size_t)head * c->sstride + slot) * nb * 2;
+        int prev = 0;
+        NMG_CUDA_TRY(cudaGetDevice(&prev));
+        NMG_CUDA_TRY(cudaSetDevice(c->device));
+        cudaStream_t s = (cudaStream_t)stream;
+        NMG_CUDA_TRY(cudaMemcpyAsync(kq.data(), (const char*)c->k + off, c->dh, cudaMemcpyDeviceToHost, s));
+        NMG_CUDA_TRY(cudaMemcpyAsync(vq.data(), (const char*)c->v + off, c->dh, cudaMemcpyDeviceToHost, s));
+        NMG_CUDA_TRY(cudaMemcpyAsync(kd.data(), (const char*)c->ks + soff, nb * 2, cudaMemcpyDeviceToHost, s));
+        NMG_CUDA_TRY(cudaMemcpyAsync(vd.data(), (const char*)c->vs + soff, nb * 2, cudaMemcpyDeviceToHost, s));
+        NMG_CUDA_TRY(cudaStreamSynchronize(s));
+        NMG_CUDA_TRY(cudaSetDevice(prev));
+        for (int d = 0; d < c->dh; ++d) {
+            if (key_out) key_out[d] = __half2float(__ushort_as_half(kd[d / 32])) * (float)kq[d];
+            if (value_out) value_out[d] = __half2float(__ushort_as_half(vd[d / 32])) * (float)vq[d];
+        }
+        return NMG_OK;
+    }
     std::vector<unsigned char> kb((size_t)c->dh * es), vb((size_t)c->dh * es);
     int prev = 0;
     NMG_CUDA_TRY(cudaGetDevice(&prev));
@@ -396,5 +504,14 @@ extern "C" int nmg_kv_storage(const nmg_kv_cache* c, void** keys, void** values,
     if (keys) *keys = c->k;
     if (values) *values = c->v;
     if (slots) *slots = c->slots;
+    return NMG_OK;
+}
+
+extern "C" int nmg_kv_scales(const nmg_kv_cache* c, void** key_scales, void** value_scales, int64_t* rows_per_head) {
+    if (!c) return set_error(NMG_INVALID_ARGUMENT, "nmg_kv_scales: null cache");
+    if (c->dtype != NMG_Q8_0) return set_error(NMG_INVALID_ARGUMENT, "nmg_kv_scales: not a Q8_0 cache");
+    if (key_scales) *key_scales = c->ks;
+    if (value_scales) *value_scales = c->vs;
+    if (rows_per_head) *rows_per_head = c->sstride;
     return NMG_OK;
 }

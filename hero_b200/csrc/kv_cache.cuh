@@ -23,6 +23,13 @@ struct nmg_kv_cache {
     int64_t slots = 0;   // physical rows per head
     void* k = nullptr;
     void* v = nullptr;
+    // NMG_Q8_0: fp16 block scales [hkv][slots][dh / 32] of K and V (k, v hold
+    // the int8 quants [hkv][slots][dh]).
+    void* ks = nullptr;
+    void* vs = nullptr;
+    // Scale rows per head (slots rounded up to 64): every 64-row tile of
+    // scales starts 512-byte aligned and stays inside its head.
+    int64_t sstride = 0;
 
     int64_t size = 0;    // logical rows (reference size())
     int64_t oldest = 0;  // position of chronological row 0
@@ -39,6 +46,9 @@ struct nmg_kv_cache {
 namespace nmg {
 
 inline int v_dtype_for(int dtype) { return dtype == NMG_BF16 ? NMG_F16 : dtype; }
+inline bool cache_dtype_valid(int dtype) { return dtype_valid(dtype) || dtype == NMG_Q8_0; }
+// Bytes of one cached element (the int8 quants of a Q8_0 cache).
+inline int cache_elem_size(int dtype) { return dtype == NMG_Q8_0 ? 1 : dtype_size(dtype); }
 
 // Half-open visible position range of a query for a cache as it stands:
 // [max(q - window + 1, floor), min(q, newest)] in positions.

@@ -30,7 +30,7 @@ from dataclasses import dataclass
 import torch
 
 from . import _lib
-from ._lib import BF16, F16, F32, call
+from ._lib import BF16, F16, F32, Q8_0, call
 
 _DT = {torch.float32: F32, torch.float16: F16, torch.bfloat16: BF16}
 _TORCH = {F32: torch.float32, F16: torch.float16, BF16: torch.bfloat16}
@@ -40,7 +40,7 @@ def dtype_code(dt) -> int:
     if isinstance(dt, int):
         return dt
     if isinstance(dt, str):
-        return {"f32": F32, "fp32": F32, "f16": F16, "fp16": F16, "bf16": BF16}[dt]
+        return {"f32": F32, "fp32": F32, "f16": F16, "fp16": F16, "bf16": BF16, "q8_0": Q8_0}[dt]
     return _DT[dt]
 
 
@@ -161,6 +161,26 @@ class _Cache:
         k, v, s = ctypes.c_void_p(), ctypes.c_void_p(), ctypes.c_int64()
         call("nmg_kv_storage", self._h, ctypes.byref(k), ctypes.byref(v), ctypes.byref(s))
         return k.value, v.value, s.value
+
+    def q8_blocks(self, head: int):
+        """A Q8_0 cache's raw blocks of one K/V head, as host arrays: (K quants
+        [slots, head_dim] int8, K scales [slots, head_dim/32] fp16 bits, V quants,
+        V scales)."""
+        kp, vp, slots = self.storage()
+        ks, vs, sr = ctypes.c_void_p(), ctypes.c_void_p(), ctypes.c_int64()
+        call("nmg_kv_scales", self._h, ctypes.byref(ks), ctypes.byref(vs), ctypes.byref(sr))
+        n, nb = slots * self.head_dim, slots * (self.head_dim // 32)
+        nbs = sr.value * (self.head_dim // 32)  # scale rows per head: slots rounded up to 64
+
+        def grab(ptr, count, dtype, off):
+            t = _from_ptr(ptr + off * torch.tensor([], dtype=dtype).element_size(), count, self.device, dtype)
+            return t.cpu().numpy().copy()
+
+        h = int(head)
+        return (grab(kp, n, torch.int8, h * n).reshape(slots, -1),
+                grab(ks.value, nb, torch.int16, h * nbs).view("u2").reshape(slots, -1),
+                grab(vp, n, torch.int8, h * n).reshape(slots, -1),
+                grab(vs.value, nb, torch.int16, h * nbs).view("u2").reshape(slots, -1))
 
 
 class FullAttentionCache(_Cache):
@@ -305,7 +325,8 @@ class DeltaNetState:
 def _from_ptr(ptr: int, n: int, device: int, dtype=torch.float32) -> torch.Tensor:
     """Wrap n device values at ptr as a tensor (the owner keeps them alive)."""
     typestr, view = {torch.float32: ("<f4", None), torch.float16: ("<f2", None),
-                     torch.bfloat16: ("<i2", torch.bfloat16)}[dtype]
+                     torch.bfloat16: ("<i2", torch.bfloat16), torch.int8: ("|i1", None),
+                     torch.int16: ("<i2", None)}[dtype]
 
     class _Holder:
         def __init__(self, p, n, dev):

@@ -61,6 +61,11 @@ extern "C" {
 #define NMG_F32 0
 #define NMG_F16 1
 #define NMG_BF16 2
+/* Cache storage only: K and V as Q8_0 blocks (32 int8 quants and an fp16
+ * scale), the format the reference plans behind its append / key / value
+ * seam (INFERENCE_PLAN.md, P1.3), quantised as quantize_row_q8_0
+ * (src/quant_i8.hpp:69-81).  Queries, inputs and outputs stay F32/F16/BF16. */
+#define NMG_Q8_0 3
 
 NMG_API const char* nmg_last_error(void);
 NMG_API const char* nmg_version(void);
@@ -91,7 +96,8 @@ NMG_API int nmg_selftest_wait_timeout(int device, int target, void* stream);
  * (src/attention.hpp:252-395) when window > 0.
  *
  * Device layout: K and V are separate buffers [hkv][slots][head_dim] in
- * `dtype`; the position p lives in slot (p - first position ever appended)
+ * `dtype` (NMG_Q8_0: int8 quants, plus fp16 scales, one per 32 values, and
+ * head_dim a multiple of 32); the position p lives in slot (p - first position ever appended)
  * mod slots.  `capacity` is the number of slots.  A full cache fails with
  * NMG_LENGTH_ERROR once more than `capacity` rows were appended.  A local
  * cache keeps logical rows exactly as the reference (window-sized ring, batch
@@ -139,6 +145,14 @@ NMG_API int nmg_kv_reset(nmg_kv_cache* cache);
 
 /* Raw device storage, for callers that fuse their own producer. */
 NMG_API int nmg_kv_storage(const nmg_kv_cache* cache, void** keys, void** values, int64_t* slots);
+
+/* The block scales of an NMG_Q8_0 cache: fp16 bit patterns
+ * [hkv][rows_per_head][head_dim/32] (rows_per_head = slots rounded up to 64;
+ * slot s of head h is row h * rows_per_head + s) beside the int8 quants of
+ * nmg_kv_storage ([hkv][slots][head_dim]); a cached value is scale * quant
+ * (fp16_to_fp32(d) * qs, src/quant.hpp:59-62).  NMG_INVALID_ARGUMENT for other
+ * cache dtypes. */
+NMG_API int nmg_kv_scales(const nmg_kv_cache* cache, void** key_scales, void** value_scales, int64_t* rows_per_head);
 
 /* ---- attention ---------------------------------------------------------------
  *

@@ -28,7 +28,7 @@
 
 namespace nmg {
 
-enum class Dtype : int { f32 = NMG_F32, f16 = NMG_F16, bf16 = NMG_BF16 };
+enum class Dtype : int { f32 = NMG_F32, f16 = NMG_F16, bf16 = NMG_BF16, q8_0 = NMG_Q8_0 };  // q8_0: cache storage only
 
 // Status -> the exception type the reference throws in the same situation.
 inline void check(int status) {

@@ -103,6 +103,7 @@ def lib():
             L.nmo_bf16_to_fp32.restype = ctypes.c_float
             L.nmo_fp16_to_fp32.argtypes = [ctypes.c_uint16]
             L.nmo_fp16_to_fp32.restype = ctypes.c_float
+            L.nmo_quantize_q8_0.argtypes = [_f32p, _i64, ctypes.c_void_p, ctypes.c_void_p]
             _lib = L
     return _lib
 
@@ -146,6 +147,7 @@ def ref():
                 R.nmref_bf16_to_fp32.restype = ctypes.c_float
                 R.nmref_fp16_to_fp32.argtypes = [ctypes.c_uint16]
                 R.nmref_fp16_to_fp32.restype = ctypes.c_float
+                R.nmref_quantize_q8_0.argtypes = [_f32p, _i64, ctypes.c_void_p, ctypes.c_void_p]
                 _ref = R
     return _ref
 
@@ -197,6 +199,26 @@ def from_fp16_bits(h: np.ndarray) -> np.ndarray:
 
 def round_fp16(x: np.ndarray) -> np.ndarray:
     return from_fp16_bits(fp16_bits(x))
+
+
+def quantize_q8_0(x, use_ref=False):
+    """quantize_row_q8_0 (src/quant_i8.hpp:69-81) of each row of x (last axis a
+    multiple of 32): returns (int8 quants, shape of x; fp16 scale bits, one per
+    32 values).  use_ref runs the reference's own function (oracle/_ref)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    n = x.size
+    qs = np.empty(n, np.int8)
+    d = np.empty(n // 32, np.uint16)
+    fn = ref().nmref_quantize_q8_0 if use_ref else lib().nmo_quantize_q8_0
+    fn(_fp(x.reshape(-1)), n, qs.ctypes.data, d.ctypes.data)
+    return qs.reshape(x.shape), d.reshape(x.shape[:-1] + (x.shape[-1] // 32,))
+
+
+def dequantize_q8_0(qs, d):
+    """The values a Q8_0 block holds: fp16 scale (core.hpp:34-59) times each int8 quant."""
+    scale = from_fp16_bits(np.asarray(d, np.uint16))
+    q = np.asarray(qs, np.int8).astype(np.float32)
+    return (q.reshape(q.shape[:-1] + (-1, 32)) * scale[..., None]).reshape(q.shape).astype(np.float32)
 
 
 # ---- the arithmetic -------------------------------------------------------------

@@ -31,6 +31,7 @@
  *   nmo_attn_prologue       src/qwen35.hpp:343-352, src/gemma4.hpp:206-209, :676-680
  *   nmo_attn_gate           src/qwen35.hpp:390-393
  *   nmo_fp32_to_bf16 etc.   src/core.hpp:34-100
+ *   nmo_quantize_q8_0       src/quant_i8.hpp:69-81 (quantize_row_q8_0: Q8_0 blocks of 32)
  *
  * Inputs are plain row-major fp32 arrays in the reference's own layouts:
  * activations [rows][heads*dim] (heads contiguous inside a row), cached K/V
@@ -487,4 +488,21 @@ void nmo_attn_prologue(int64_t T, int hq, int hkv, int dh, int64_t position, con
 void nmo_attn_gate(int64_t T, int hq, int dh, const float* qg, float* a) {
     for (int64_t r = 0; r < T * hq; ++r)
         for (int i = 0; i < dh; ++i) a[(size_t)r * dh + i] *= nmo_sigmoid(qg[((size_t)2 * r + 1) * dh + i]);
+}
+
+/* quantize_row_q8_0 (src/quant_i8.hpp:69-81) over n values, n a multiple of 32:
+ * per block amax = max |x|, d = amax / 127, id = d ? 1 / d : 0, the scale kept
+ * as fp16 (core.hpp:61-79 rounding), q = roundf(x * id) as int8. */
+void nmo_quantize_q8_0(const float* x, int64_t n, int8_t* qs, uint16_t* dbits) {
+    for (int64_t b = 0; b < n / 32; ++b) {
+        float amax = 0.f;
+        for (int j = 0; j < 32; ++j) {
+            const float ax = fabsf(x[b * 32 + j]);
+            amax = amax < ax ? ax : amax; /* std::max(amax, ax) */
+        }
+        const float d = amax / 127.f;
+        const float id = d != 0.f ? 1.f / d : 0.f;
+        dbits[b] = nmo_fp32_to_fp16(d);
+        for (int j = 0; j < 32; ++j) qs[b * 32 + j] = (int8_t)roundf(x[b * 32 + j] * id);
+    }
 }

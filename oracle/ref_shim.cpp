@@ -20,6 +20,7 @@
 #include "attention.hpp"
 #include "components.hpp"
 #include "recurrent.hpp"
+#include "quant_i8.hpp"
 
 #include <chrono>
 #include <cstdint>
@@ -511,5 +512,16 @@ float nmref_bf16_to_fp32(uint16_t b) { return bf16_to_fp32(b); }
 float nmref_fp16_to_fp32(uint16_t h) { return fp16_to_fp32(h); }
 
 int nmref_threads(void) { return int(nm_num_threads()); }
+
+// quantize_row_q8_0 (quant_i8.hpp:69-81) over n values (a multiple of 32):
+// int8 quants and the fp16 bit pattern of each 32-value block's scale.
+void nmref_quantize_q8_0(const float* x, int64_t n, int8_t* qs, uint16_t* d) {
+    std::vector<block_q8_0> blocks((size_t)n / QK8_0);
+    quantize_row_q8_0(x, blocks.data(), (size_t)n);
+    for (size_t b = 0; b < blocks.size(); ++b) {
+        d[b] = blocks[b].d;
+        for (int j = 0; j < QK8_0; ++j) qs[b * QK8_0 + j] = blocks[b].qs[j];
+    }
+}
 
 }  // extern "C"

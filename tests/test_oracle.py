@@ -287,3 +287,38 @@ def test_dense_attention_is_the_reference_sdpa(heads, tq, tk, scale):
     assert oracle.ref().nmref_sdpa(heads, d, tq, tk, fp(q), fp(k), fp(v), scale, fp(want)) == 0
     got = oracle.attend(k, v, 0, 0, heads, d, q, heads, tk - 1, scale=np.float32(scale))
     np.testing.assert_allclose(got, want, rtol=2e-6, atol=2e-6)
+
+
+def _q8_cases():
+    rng = np.random.default_rng(8)
+    rows = [rng.standard_normal(4096).astype(np.float32),
+            (rng.standard_normal(4096) * 1e-3).astype(np.float32),
+            (rng.standard_normal(4096) * 3e4).astype(np.float32),
+            np.zeros(64, np.float32)]
+    # values on exact half-steps of the block scale: x = (k + 0.5) * amax / 127
+    amax = np.float32(1.7)
+    ties = (np.arange(-127, 127, dtype=np.float32)[:224] + np.float32(0.5)) * (amax / np.float32(127))
+    ties[0] = -amax
+    rows.append(ties.astype(np.float32))
+    return rows
+
+
+@pytest.mark.skipif(oracle.ref() is None, reason="reference build (oracle/_ref) not present")
+def test_q8_0_quantiser_matches_the_reference_bit_for_bit():
+    # quantize_row_q8_0 (quant_i8.hpp:69-81): the C restatement against the
+    # reference's own function, every quant and every fp16 scale.
+    for x in _q8_cases():
+        q0, d0 = oracle.quantize_q8_0(x)
+        q1, d1 = oracle.quantize_q8_0(x, use_ref=True)
+        assert np.array_equal(q0, q1) and np.array_equal(d0, d1)
+
+
+def test_q8_0_round_trip_error_is_half_a_step():
+    x = _q8_cases()[0].reshape(-1, 32)
+    q, d = oracle.quantize_q8_0(x)
+    back = oracle.dequantize_q8_0(q, d)
+    # quants are taken against the fp32 scale amax / 127, the block keeps its
+    # fp16 rounding: half a step plus 127 times that rounding
+    d32 = (np.abs(x).max(axis=1) / np.float32(127)).astype(np.float32)[:, None]
+    d16 = oracle.from_fp16_bits(d)[:, None]
+    assert np.all(np.abs(back - x) <= 0.5 * d32 + 127 * np.abs(d16 - d32) + 1e-7)
