@@ -284,23 +284,27 @@ __global__ void __launch_bounds__(128) attn_decode_mma_kernel(const __grid_const
             // scale * quant of every K and V value of the tile, as fp16 into the
             // swizzled layout the MMA loop reads; 8 values (one 16-byte chunk)
             // at a time, consecutive threads on consecutive chunks of a row.
+            // A quant q becomes the fp16 1152 + q by placing q ^ 0x80 under
+            // the exponent byte 0x64 (exact), the bias comes off exactly, and
+            // the multiply by the fp16 scale rounds the exact product once.
             const unsigned char* raw = smem + st * C::STAGE_BYTES;
             unsigned char* f16 = smem + C::F16_OFF;
-#pragma unroll 2
+            const __half2 bias = __float2half2_rn(1152.f);
+#pragma unroll 4
             for (int i = tid; i < 2 * KT * (DH / 8); i += 128) {
                 const int mat = i / (KT * (DH / 8)), rem = i % (KT * (DH / 8));
                 const int key = rem / (DH / 8), c8 = rem % (DH / 8);
                 const uint2 q = *(const uint2*)(raw + mat * C::Q8_QBYTES + key * DH + c8 * 8);
                 const uint16_t sb = *(const uint16_t*)(raw + 2 * C::Q8_QBYTES + mat * C::Q8_SBYTES +
                                                        (key * (DH / 32) + c8 / 4) * 2);
-                const float sc = dev::f16_bits_to_f32(sb);
-                const uint32_t qw[2] = {q.x, q.y};
+                const __half2 sc = __halves2half2(__ushort_as_half(sb), __ushort_as_half(sb));
+                const uint32_t qw[2] = {q.x ^ 0x80808080u, q.y ^ 0x80808080u};
                 uint32_t w[4];
 #pragma unroll
                 for (int u = 0; u < 4; ++u) {
-                    const int32_t b0 = (int32_t)(qw[u >> 1] << (24 - 16 * (u & 1))) >> 24;
-                    const int32_t b1 = (int32_t)(qw[u >> 1] << (16 - 16 * (u & 1))) >> 24;
-                    w[u] = pack_h2(sc * (float)b0, sc * (float)b1);
+                    const uint32_t biased = __byte_perm(qw[u >> 1], 0x64646464u, (u & 1) ? 0x4342u : 0x4140u);
+                    const __half2 v = __hmul2(__hsub2(*reinterpret_cast<const __half2*>(&biased), bias), sc);
+                    w[u] = *reinterpret_cast<const uint32_t*>(&v);
                 }
                 *(uint4*)(f16 + mat * C::TILE_BYTES + tile_off<DH>(key, c8)) = make_uint4(w[0], w[1], w[2], w[3]);
             }
