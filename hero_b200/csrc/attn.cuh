@@ -164,11 +164,11 @@ int attend_rows_split(const nmg_kv_cache* c, int hq, const void* q, int q_dtype,
 int attend_batch_split(const nmg_kv_cache* const* caches, int batch, const int64_t* queries_at, int hq, const void* q,
                        int q_dtype, float scale, void* out, int out_dtype, cudaStream_t stream);
 
-// Cluster-merged decode over fp32 caches (attn_decode_cluster.cu), taken by
-// the two functions above when cluster_decode_fits says so.  `units` counts
-// (query row, K/V head, head subgroup) triples, `total_keys` the visible keys
-// summed over the rows.
-bool cluster_decode_fits(const nmg_kv_cache* c, int64_t units, int64_t total_keys);
+// Decode over fp32 caches at head_dim 128 / 256 (attn_decode_cluster.cu):
+// 8-warp CTAs whose key splits merge across a thread-block cluster (short
+// decodes) or through global partials and a ticket (long ones).  The two
+// functions above hand these caches over when fp32_decode_fits says so.
+bool fp32_decode_fits(const nmg_kv_cache* c);
 int attend_rows_cluster(const nmg_kv_cache* c, int hq, const void* q, int q_dtype, int64_t rows, int64_t first_query,
                         int64_t window, int64_t floor_pos, int64_t newest, float scale, void* out, int out_dtype,
                         cudaStream_t stream);

@@ -471,7 +471,7 @@ int attend_rows_split(const nmg_kv_cache* c, int hq, const void* q, int q_dtype,
         if (n > longest) longest = n;
         total_keys += n;
     }
-    if (!caller_scratch && cluster_decode_fits(c, rows * c->hkv * zdim, total_keys))
+    if (!caller_scratch && fp32_decode_fits(c))
         return attend_rows_cluster(c, hq, q, q_dtype, rows, first_query, window, floor_pos, newest, scale, out,
                                    out_dtype, stream);
     const int warps = warps_runtime(c->dtype, c->dh);
@@ -525,7 +525,7 @@ int attend_batch_split(const nmg_kv_cache* const* caches, int batch, const int64
         spans[b] = visible_span(qpos, c->window, c->oldest, c->newest());
         total_keys += spans[b].hi - spans[b].lo + 1;
     }
-    if (cluster_decode_fits(c0, (int64_t)batch * c0->hkv * zdim, total_keys))
+    if (fp32_decode_fits(c0))
         return attend_batch_cluster(caches, batch, queries_at, hq, q, q_dtype, scale, out, out_dtype, stream);
     const int warps = warps_runtime(c0->dtype, c0->dh);
     const int64_t split_len = pick_split_len(total_keys * c0->hkv * zdim, warps);

@@ -1,12 +1,13 @@
-"""The cluster-merged fp32 decode against the oracle.
+"""The fp32 decode kernel (cluster merge and ticket merge) against the oracle.
 
-fp32 caches at head_dim 128 / 256 decode through one launch whose key splits
-meet in distributed shared memory.  Checked here across GQA groups 1-8 (and
+fp32 caches at head_dim 128 / 256 decode on 8-warp CTAs whose key splits meet
+in distributed shared memory (short decodes) or through global partials and a
+ticket (long decodes over few heads).  Checked here across GQA groups 1-8 (and
 an odd group), split counts from one to eight (short caches leave splits
-empty), query rows that each see a different window of a wrapped ring, a
-ragged batch of sequences, fp16 / bf16 queries and outputs, and repeat calls,
-all against the reference reduction (qwen35.hpp:360-382, gemma4.hpp:593-615)
-within max abs 2e-3 / rel L2 1e-3.
+empty), query rows that each see a different window of a wrapped ring, ragged
+batches, fp16 / bf16 queries and outputs, and repeat calls, all against the
+reference reduction (qwen35.hpp:360-382, gemma4.hpp:593-615) within max abs
+2e-3 / rel L2 1e-3.
 """
 import numpy as np
 import pytest
@@ -98,15 +99,37 @@ def test_repeat_calls_agree_bit_for_bit(dev):
         assert torch.equal(nm.attend(cache, q, L - 1, 0.1), first)
 
 
-def test_long_fp32_decode_keeps_the_split_path(dev):
-    # One row over 20,000 fp32 keys (82 MB): too few (row, head) units to fill
-    # the GPU with eight splits each, so the ticket-merged split kernel runs;
-    # it must agree with the oracle as before.
+def test_long_fp32_decode_ticket_merge(dev):
+    # One row over 20,000 fp32 keys (82 MB): too few (row, head) units for
+    # clusters to fill the GPU, so the splits merge through global partials
+    # and a ticket; the tickets return to zero, so repeat calls agree exactly.
     hq, hkv, dh, L = 16, 8, 128, 20000
     k, v = _rows(95, 1, L, hkv * dh), _rows(95, 2, L, hkv * dh)
     q = _rows(95, 3, 1, hq * dh)
     cache = nm.FullAttentionCache(hkv, dh, capacity=L, dtype="f32")
     cache.append(0, _t(k, dev), _t(v, dev))
-    out = nm.attend(cache, _t(q, dev), L - 1, 0.0883883, out_dtype=torch.float32).cpu().numpy()
+    qd = _t(q, dev)
+    out = nm.attend(cache, qd, L - 1, 0.0883883, out_dtype=torch.float32)
     want = oracle.attend(k, v, 0, 0, hkv, dh, q, hq, L - 1, scale=np.float32(0.0883883))
-    assert_close(out, want, what="20000 fp32 keys")
+    assert_close(out.cpu().numpy(), want, what="20000 fp32 keys")
+    for _ in range(2):
+        assert torch.equal(nm.attend(cache, qd, L - 1, 0.0883883, out_dtype=torch.float32), out)
+
+
+def test_ragged_pair_ticket_merge(dev):
+    # Two sequences (9000 and 300 rows) at head_dim 256: the short one leaves
+    # most of its splits empty.
+    hq, hkv, dh = 8, 4, 256
+    lens = [9000, 300]
+    caches, kv = [], []
+    for i, L in enumerate(lens):
+        k, v = _rows(97 + i, 1, L, hkv * dh), _rows(97 + i, 2, L, hkv * dh)
+        c = nm.FullAttentionCache(hkv, dh, capacity=L, dtype="f32")
+        c.append(0, _t(k, dev), _t(v, dev))
+        caches.append(c)
+        kv.append((k, v))
+    q = _rows(99, 3, 2, hq * dh, 0.1)
+    out = nm.attend_batch(caches, _t(q, dev), None, out_dtype=torch.float32).cpu().numpy()
+    for b, L in enumerate(lens):
+        want = oracle.attend(kv[b][0], kv[b][1], 0, 0, hkv, dh, q[b:b + 1], hq, L - 1, use_scale=False)
+        assert_close(out[b:b + 1], want, what=f"sequence {b} ({L} rows)")
