@@ -860,7 +860,8 @@ def extra_config1(torch, dev, small=False):
     return {"workload": "config 1: decode, fp32, 16q/8kv, d128, 1024 cached", "value": gbs, "unit": "GB/s",
             "us_per_call": ms * 1e3, "tok_per_s": 1 / (ms * 1e-3),
             "roofline": {"bound": "hbm", "achieved": gbs, "peak": p["hbm"], "frac": gbs / p["hbm"],
-                         "bytes_per_call": bytes_},
+                         "bytes_per_call": bytes_, "traffic": ncu_traffic("attn_decode_c1"),
+                         "kernel": "attn_cluster_kernel<128, 2> (8-CTA clusters)"},
             "method": f"{NC} caches (168 MB > L2) rotated in a CUDA graph; kernel time per call"}
 
 
