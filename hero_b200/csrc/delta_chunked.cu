@@ -420,7 +420,8 @@ struct ScanArgs {
 //   MMA2  D2   = R^T [T;MT]^T       A = R^T (TMEM),  B = [T;MT] image  -> D^T | (M T R)^T
 //   MMA3  S^T += (f D)^T K          A = (f D)^T,     B = K^T image     (S^T pre-scaled by exp(G_last))
 // Warpgroup 0 runs the chain (R, f D, MMA issue); warpgroup 1 rescales the
-// state between MMA1 and MMA3 and forms O = e (Q S) + M T R; warp 8 loads.
+// state between MMA1 and MMA3 and forms O = e (Q S) + M T R, reading M T R
+// before it lets MMA3 / MMA1 run; warp 8 loads.
 constexpr int kCols = 128;  // value columns per CTA (TMEM lanes)
 constexpr uint32_t kVTile = kC * kCols * 4;  // 4 boxes of 32 columns x 64 tokens
 constexpr uint32_t TM_S = 0, TM_P = 128, TM_RD = 256, TM_D2 = 320;  // TMEM columns
@@ -435,7 +436,7 @@ static_assert(P2_SMEM <= 227 * 1024, "phase-2 shared memory");
 
 enum : int {
     B_KQ_FULL, B_KQ_EMPTY, B_KT_FULL, B_KT_EMPTY, B_TM_FULL, B_TM_EMPTY, B_VA_FULL0, B_VA_FULL1, B_VA_EMPTY0,
-    B_VA_EMPTY1, B_MMA1, B_MMA2, B_MMA3, B_SCALED, B_ODONE, B_COUNT
+    B_VA_EMPTY1, B_MMA1, B_MMA2, B_MMA3, B_SCALED, B_COUNT
 };
 
 __device__ __forceinline__ void named_bar(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
@@ -456,7 +457,6 @@ __global__ void __launch_bounds__(288, 1) delta_scan_kernel(const __grid_constan
         dev::mbar_init(&bar[B_VA_EMPTY0], 2);
         dev::mbar_init(&bar[B_VA_EMPTY1], 2);
         dev::mbar_init(&bar[B_SCALED], 4);
-        dev::mbar_init(&bar[B_ODONE], 4);
         *abort_flag = 0;
         dev::fence_mbar_init();
         dev::prefetch_tensormap(&a.tm_v);
@@ -566,9 +566,8 @@ __global__ void __launch_bounds__(288, 1) delta_scan_kernel(const __grid_constan
                 tc::wait_st();
                 tc::fence_before_sync();
                 named_bar(1, 128);
-                if (tid == 0) {  // MMA2 (after O has read the previous M T R)
+                if (tid == 0) {  // MMA2 (warpgroup 1 read the previous M T R before the state went on)
                     tc::fence_after_sync();
-                    if (c >= 1) wait(B_ODONE, (uint32_t)(c - 1) & 1u);
                     wait(B_TM_FULL, ph);
 #pragma unroll
                     for (int kk = 0; kk < kC / 8; ++kk)
@@ -600,7 +599,7 @@ __global__ void __launch_bounds__(288, 1) delta_scan_kernel(const __grid_constan
                 if (tid == 0) {  // MMA3 (onto the rescaled state), then the next chunk's MMA1
                     tc::fence_after_sync();
                     dev::mbar_arrive(&bar[B_VA_EMPTY0 + s]);
-                    wait(B_SCALED, ph);
+                    wait(B_SCALED, ph);  // warpgroup 1: state rescaled and M T R read
                     wait(B_KT_FULL, ph);
 #pragma unroll
                     for (int kk = 0; kk < kC / 8; ++kk)
@@ -621,14 +620,6 @@ __global__ void __launch_bounds__(288, 1) delta_scan_kernel(const __grid_constan
                 wait(B_VA_FULL0 + s, (uint32_t)(c >> 1) & 1u);
                 wait(B_MMA1, ph);
                 tc::fence_after_sync();
-                float o[kC];  // e_t (Q S)[t][j], then + (M T R)[t][j]
-#pragma unroll
-                for (int half = 0; half < 2; ++half) {
-                    uint32_t x[32];
-                    tc::ld_32x32b_x32(tmem + lanes + TM_P + 64 + 32 * half, x);
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) o[32 * half + i] = AUX[64 + 32 * half + i] * __uint_as_float(x[i]);
-                }
                 const float gamma = AUX[192];
 #pragma unroll
                 for (int b = 0; b < 4; ++b) {  // S^T <- exp(G_last) S^T before MMA3 adds the chunk
@@ -638,12 +629,18 @@ __global__ void __launch_bounds__(288, 1) delta_scan_kernel(const __grid_constan
                     for (int i = 0; i < 32; ++i) v[i] = __float_as_uint(gamma * __uint_as_float(v[i]));
                     tc::st_32x32b_x32(tmem + lanes + TM_S + 32 * b, v);
                 }
-                tc::wait_st();
-                tc::fence_before_sync();
-                __syncwarp();
-                if (lane == 0) dev::mbar_arrive(&bar[B_SCALED]);
+                float o[kC];  // e_t (Q S)[t][j], then + (M T R)[t][j]
+#pragma unroll
+                for (int half = 0; half < 2; ++half) {
+                    uint32_t x[32];
+                    tc::ld_32x32b_x32(tmem + lanes + TM_P + 64 + 32 * half, x);
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) o[32 * half + i] = AUX[64 + 32 * half + i] * __uint_as_float(x[i]);
+                }
                 wait(B_MMA2, ph);
                 tc::fence_after_sync();
+                // M T R, read before MMA3 / MMA1 run: a TMEM load queued behind
+                // those MMAs waits for them, and the next chunk's MMA2 rewrites it
 #pragma unroll
                 for (int half = 0; half < 2; ++half) {
                     uint32_t y[32];
@@ -651,9 +648,10 @@ __global__ void __launch_bounds__(288, 1) delta_scan_kernel(const __grid_constan
 #pragma unroll
                     for (int i = 0; i < 32; ++i) o[32 * half + i] += __uint_as_float(y[i]);
                 }
+                tc::wait_st();
                 tc::fence_before_sync();
                 __syncwarp();
-                if (lane == 0) dev::mbar_arrive(&bar[B_ODONE]);
+                if (lane == 0) dev::mbar_arrive(&bar[B_SCALED]);
                 if (tid == 128) dev::mbar_arrive(&bar[B_VA_EMPTY0 + s]);
                 if (col_ok) {
                     const int64_t t0 = (int64_t)c * kC;
