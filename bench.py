@@ -60,6 +60,51 @@ def peaks():
         return {"hbm": 6650.0, "bf16": 1590.0, "bf16_sustained": 1400.0, "src": "fallback"}
 
 
+_RATES = {}
+
+
+def tensor_rates():
+    """tf32 and bf16 tcgen05 rates from an issue loop on every SM
+    (hero_b200/libnmg_rate.so: back-to-back M = 128 x N = 128 MMAs into one
+    TMEM accumulator, cycles per MMA and the SM clock measured in the kernel).
+    The tf32 roofline peak is the measured bf16 peak (MEASURED_PEAKS.json)
+    times the issue loop's tf32 / bf16 FLOP-per-cycle ratio.  Measured once per
+    process; None where the probe library or a GPU is missing."""
+    if "r" in _RATES:
+        return _RATES["r"]
+    out = None
+    try:
+        import ctypes
+
+        lib = ctypes.CDLL(os.path.join(ROOT, "hero_b200", "libnmg_rate.so"))
+        fn = lib.nmg_rate_tensor
+        fn.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.POINTER(ctypes.c_double),
+                       ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_int)]
+        res = {}
+        for kind, name, kdim in ((0, "tf32", 8), (1, "bf16", 16)):
+            cyc, ghz, sms = ctypes.c_double(), ctypes.c_double(), ctypes.c_int()
+            if fn(kind, 128, 4096, ctypes.byref(cyc), ctypes.byref(ghz), ctypes.byref(sms)) != 0:
+                raise RuntimeError("rate probe failed")
+            flop = 2.0 * 128 * 128 * kdim
+            res[name] = {"cycles_per_mma": cyc.value, "sm_ghz": ghz.value,
+                         "tflops": flop / cyc.value * ghz.value * 1e9 * sms.value / 1e12}
+        ratio = (2.0 * 128 * 128 * 8 / res["tf32"]["cycles_per_mma"]) / (2.0 * 128 * 128 * 16 / res["bf16"]["cycles_per_mma"])
+        out = {"issue_loop": res, "tf32_over_bf16": ratio, "tf32_peak": peaks()["bf16"] * ratio,
+               "method": "tcgen05 issue loop, M=128 N=128, one CTA per SM (hero_b200/csrc/tensor_rate.cu)"}
+    except Exception as e:  # no GPU or no probe library: the caller falls back and says so
+        out = None
+    _RATES["r"] = out
+    return out
+
+
+def tf32_peak_and_note():
+    r = tensor_rates()
+    if r:
+        return r["tf32_peak"], (f"tf32 peak = measured bf16 peak x {r['tf32_over_bf16']:.3f}, the tf32/bf16 "
+                                f"FLOP-per-cycle ratio of a tcgen05 issue loop (M=128, N=128)")
+    return peaks()["bf16"] / 2, "tf32 peak taken as half the measured bf16 peak (issue-loop probe unavailable)"
+
+
 def ncu_traffic(name):
     """DRAM bytes per launch of a workload's dominant kernel from profiles/traffic.json, or None."""
     try:
@@ -903,11 +948,12 @@ def extra_config3(torch, dev, small=False):
             C = chunk
             alg = (5 * 2 * C * C * d + 3 * 2 * C * d * d + 2 * C ** 3 / 3) * hv * (T // C)
             tf = alg / (ms * 1e-3) / 1e12
-            tf32_peak = peaks()["bf16"] / 2  # tf32 runs at half the bf16 rate
+            tf32_peak, note = tf32_peak_and_note()
             res[f"prefill_chunk{chunk}"].update(
                 {"tflops_chunked_alg": tf, "alg_flop": alg,
                  "roofline": {"bound": "tensor", "achieved": tf, "peak": tf32_peak, "unit": "TFLOP/s",
-                              "frac": tf / tf32_peak, "note": "tf32 peak taken as half the measured bf16 peak"}})
+                              "frac": tf / tf32_peak, "note": note,
+                              "tensor_rates": (tensor_rates() or {}).get("issue_loop")}})
     # 256 decode steps continue from the final state, graph-captured
     qd = norm(torch.randn(Tdec, hk, d, device=dev, generator=g)) / math.sqrt(d)
     kd = norm(torch.randn(Tdec, hk, d, device=dev, generator=g))
@@ -1390,13 +1436,13 @@ def sharded_config3(rk, small=False):
     C = 64
     alg = (5 * 2 * C * C * d + 3 * 2 * C * d * d + 2 * C ** 3 / 3) * hv * (T // C)
     p = peaks()
-    tf32_peak = p["bf16"] / 2
+    tf32_peak, note = tf32_peak_and_note()
     tf_local = alg / world / (ms_pl * 1e-3) / 1e12
     res = {"prefill_chunk64": {"ms": ms_p, "tok_per_s": T / (ms_p * 1e-3), "tflops_chunked_alg": alg / (ms_p * 1e-3) / 1e12,
                                "recurrence_only_ms": ms_pl,
                                "roofline": {"bound": "tensor", "achieved": tf_local, "peak": tf32_peak, "unit": "TFLOP/s",
                                             "frac": tf_local / tf32_peak, "per": "GPU, recurrence alone",
-                                            "note": "tf32 peak taken as half the measured bf16 peak"}}}
+                                            "note": note}}}
     del q, k, v, gate, beta, gathered, full
     qd = (norm(torch.randn(Tdec, hk, d, device=dev, generator=g)) / math.sqrt(d))[:, sd.k0:sd.k1].contiguous()
     kd = norm(torch.randn(Tdec, hk, d, device=dev, generator=g))[:, sd.k0:sd.k1].contiguous()
