@@ -974,6 +974,36 @@ def extra_config3(torch, dev, small=False):
                      "roofline": {"bound": "hbm", "achieved": gbs, "peak": p["hbm"], "frac": gbs / p["hbm"],
                                   "bytes_per_step": bytes_, "note": "2 MB state is L2-resident between steps"}}
     del qd, kd, vd, gd, bd, od
+    # The whole layer core per decode token (prologue -> step -> epilogue,
+    # qwen35.hpp:396-461 at T = 1): one fused launch against the three
+    # launches, each captured over a run of tokens in a CUDA graph.
+    Cc, Wc, Tt = 2 * hk * d + hv * d, 4, 64
+    conv1 = nm.ConvState(Cc, Wc, device=dev.index)
+    cwt = torch.randn(Cc, Wc, device=dev, generator=g) * 0.5
+    qkvt = torch.randn(Tt, Cc, device=dev, generator=g)
+    brt, art = torch.randn(Tt, hv, device=dev, generator=g), torch.randn(Tt, hv, device=dev, generator=g)
+    dtbt, dsct = torch.randn(hv, device=dev, generator=g), -torch.rand(hv, device=dev, generator=g)
+    zt, gmt = torch.randn(Tt, hv, d, device=dev, generator=g), torch.randn(d, device=dev, generator=g)
+    outt = torch.empty(Tt, hv, d, device=dev)
+
+    def fused():
+        for t in range(Tt):
+            nm.delta_decode_token(st, conv1, cwt, qkvt[t], brt[t], art[t], dtbt, dsct, hk, zt[t], gmt, 1e-6,
+                                  out=outt[t])
+
+    def three():
+        for t in range(Tt):
+            qx, kx, vx, bx, gx = nm.delta_prologue(conv1, cwt, qkvt[t:t + 1], brt[t:t + 1], art[t:t + 1], dtbt, dsct,
+                                                   hk, hv, d, d)
+            ox = nm.delta_step(st, qx[0], kx[0], vx[0], gx[0], bx[0], hk)
+            nm.delta_epilogue(ox[None], zt[t:t + 1], gmt, 1e-6, out=outt[t:t + 1])
+
+    us_f = graph_time(torch, dev, fused, 5, 1) / Tt * 1e3
+    us_3 = graph_time(torch, dev, three, 5, 1) / Tt * 1e3
+    res["decode_layer_token"] = {"us_fused": us_f, "us_three_launches": us_3, "tok_per_s": 1e6 / us_f,
+                                 "kernel": "delta_decode_kernel (one launch per layer and token)",
+                                 "note": f"{Tt} tokens of one sequence in a CUDA graph; 2 MB state, L2-resident"}
+    del conv1, cwt, qkvt, brt, art, zt, outt
     # Batched decode: one token for each of 64 sequences (each its own 2 MB
     # state; 128 MB of states, past the L2), one launch per step.
     B = 8 if small else 64

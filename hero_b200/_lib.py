@@ -128,6 +128,7 @@ SIGNATURES = {
     "nmg_conv_step": [_vp, _vp, _vp, _i64, _vp, _i32, _vp],
     "nmg_delta_prologue": [_vp, _vp, _i32, _i32, _i32, _i32, _i64] + [_vp] * 10 + [_vp],
     "nmg_delta_epilogue": [_i32, _i32, _i64, _vp, _vp, _vp, ctypes.c_float, _vp, _vp],
+    "nmg_delta_decode_token": [_vp, _vp, _vp, _i32] + [_vp] * 7 + [ctypes.c_float, _vp, _vp],
     "nmg_attn_prologue": [_vp, _i32, _i64, _i64, _vp, _i32, _vp, _vp, _vp, _vp, _i32, ctypes.c_float, ctypes.c_double,
                           _i32, _i32, _vp, _i32, _vp],
     "nmg_attn_prepare": [_i32, _i32, _i32, _i64, _i64, _vp, _i32, _vp, _vp, _vp, _vp, _i32, ctypes.c_float,

@@ -21,6 +21,7 @@
 #include <math.h>
 
 #include "common.cuh"
+#include "delta.cuh"
 
 struct nmg_conv_state {
     int channels = 0, width = 0, device = 0;
@@ -277,6 +278,155 @@ __global__ void __launch_bounds__(256) epilogue_kernel(const float* o, const flo
         case 8: CALL(8); break;  \
     }
 
+// ---- one decode token of a whole layer core in one launch -----------------
+// The prologue (conv + SiLU + L2 norms + gates), the recurrent step and the
+// gated output norm of qwen35.hpp:396-461 at T = 1.  One thread-block
+// cluster per key head kh: its CTAs are the (value head h = kh + r * Hk,
+// 32-column block) pairs that read that key head, so
+//   * every CTA forms q and k of kh itself (256 conv channels: cheap) and its
+//     own 32 v channels, from the conv history;
+//   * a cluster barrier orders every CTA's history reads before the history
+//     is advanced (q and k channels by ranks 0 and 1, v channels by their CTA);
+//   * the step runs as delta_step_kernel's (4 warps x 8 columns, 4 row groups
+//     of 32 key rows per column);
+//   * the per-head sum of squares of o meets across the head's CTAs through
+//     distributed shared memory (plain remote stores), then each CTA writes
+//     its 32 gated outputs.
+// Numerics follow the three separate kernels: the prologue's hardware-exp
+// SiLU and per-head norm, the step's __expf decay, the epilogue's IEEE SiLU.
+struct DecodeArgs {
+    float* state;             // [hv][128][dv]
+    float* hist;              // [W - 1][C]
+    const float* weights;     // [C][W]
+    const float* qkv;         // [C]
+    const float* beta_raw, *alpha_raw, *dt_bias, *decay_scale;  // [hv]
+    const float* z;           // [hv][dv]
+    const float* gamma;       // [dv]
+    float* out;               // [hv][dv]
+    int hk, hv, dv, cb;       // cb: 32-column blocks per value head
+    int64_t C;
+    float q_scale, eps;
+};
+
+__device__ __forceinline__ void cl_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+template <int W>
+__global__ void __launch_bounds__(128) delta_decode_kernel(const __grid_constant__ DecodeArgs a) {
+    constexpr int DK = 128, RPT = DK / 4;
+    __shared__ float qs[DK], ks[DK], vs[32], red[2][4], part[8];
+    __shared__ float gb[2];  // decay, beta
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    uint32_t rank, ncl;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(rank));
+    asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(ncl));
+    const int kh = blockIdx.x / ncl;
+    const int hr = rank / a.cb, cb = rank % a.cb;
+    const int h = kh + hr * a.hk;
+    const int t = threadIdx.x, lane = t & 31, w = t >> 5;
+
+    // prologue: q and k of key head kh (channel t of each), v channel t < 32
+    const int64_t cq = (int64_t)kh * DK + t, ck = (int64_t)a.hk * DK + kh * DK + t;
+    const int64_t cvc = 2ll * a.hk * DK + (int64_t)h * a.dv + cb * 32 + t;
+    float hq[kMaxWidth], hk_[kMaxWidth], hv_[kMaxWidth], wq[kMaxWidth], wk[kMaxWidth], wv[kMaxWidth];
+#pragma unroll
+    for (int i = 0; i < W; ++i) {
+        wq[i] = a.weights[cq * W + i];
+        wk[i] = a.weights[ck * W + i];
+        wv[i] = t < 32 ? a.weights[cvc * W + i] : 0.f;
+    }
+#pragma unroll
+    for (int i = 0; i < W - 1; ++i) {
+        hq[i] = a.hist[i * a.C + cq];
+        hk_[i] = a.hist[i * a.C + ck];
+        hv_[i] = t < 32 ? a.hist[i * a.C + cvc] : 0.f;
+    }
+    const float xq = a.qkv[cq], xk = a.qkv[ck], xv = t < 32 ? a.qkv[cvc] : 0.f;
+    float hq2[kMaxWidth], hk2[kMaxWidth], hv2[kMaxWidth];  // copies conv_step shifts; the originals are written back
+#pragma unroll
+    for (int i = 0; i < W - 1; ++i) hq2[i] = hq[i], hk2[i] = hk_[i], hv2[i] = hv_[i];
+    const float yq = silu_fast(conv_step<W>(wq, hq2, xq));
+    const float yk = silu_fast(conv_step<W>(wk, hk2, xk));
+    if (t < 32) vs[t] = silu_fast(conv_step<W>(wv, hv2, xv));
+    if (t == 0) {
+        gb[0] = __expf(a.decay_scale[h] * softplus_ref(a.alpha_raw[h] + a.dt_bias[h]));
+        gb[1] = sigmoid_ref(a.beta_raw[h]);
+    }
+    const float sq = dev::warp_sum(yq * yq), sk = dev::warp_sum(yk * yk);
+    if (lane == 0) red[0][w] = sq, red[1][w] = sk;
+    __syncthreads();
+    const float nq = 1.f / fmaxf(sqrtf(red[0][0] + red[0][1] + red[0][2] + red[0][3]), 1e-6f);
+    const float nk = 1.f / fmaxf(sqrtf(red[1][0] + red[1][1] + red[1][2] + red[1][3]), 1e-6f);
+    qs[t] = (yq * nq) * a.q_scale;
+    ks[t] = yk * nk;
+
+    // every CTA of the cluster has read the history: advance it
+    cl_sync();
+    if (W > 1) {
+        auto put = [&](int64_t c, const float* old, float x) {
+#pragma unroll
+            for (int i = 0; i + 1 < W - 1; ++i) a.hist[i * a.C + c] = old[i + 1];
+            a.hist[(int64_t)(W - 2) * a.C + c] = x;
+        };
+        if (t < 32) put(cvc, hv_, xv);
+        if (rank == 0) put(cq, hq, xq);
+        if (rank == (ncl > 1 ? 1u : 0u)) put(ck, hk_, xk);
+    }
+    __syncthreads();
+
+    // the recurrent step over this CTA's 32 columns
+    const int cg = lane & 7, rg = lane >> 3;
+    const int jl = w * 8 + cg, j = cb * 32 + jl;
+    const int i0 = rg * RPT;
+    float* S = a.state + ((int64_t)h * DK + i0) * a.dv + j;
+    const float decay = gb[0], b = gb[1], vj = vs[jl];
+    float s[RPT], part_s = 0.f;
+#pragma unroll
+    for (int r = 0; r < RPT; ++r) {
+        s[r] = S[(int64_t)r * a.dv] * decay;
+        part_s = fmaf(s[r], ks[i0 + r], part_s);
+    }
+    part_s += __shfl_xor_sync(0xffffffffu, part_s, 8);
+    part_s += __shfl_xor_sync(0xffffffffu, part_s, 16);
+    const float d = (vj - part_s) * b;
+    float o = 0.f;
+#pragma unroll
+    for (int r = 0; r < RPT; ++r) {
+        s[r] = fmaf(ks[i0 + r], d, s[r]);
+        o = fmaf(s[r], qs[i0 + r], o);
+        S[(int64_t)r * a.dv] = s[r];
+    }
+    o += __shfl_xor_sync(0xffffffffu, o, 8);
+    o += __shfl_xor_sync(0xffffffffu, o, 16);
+
+    // gated RMS norm over the head's dv columns, spread over a.cb CTAs
+    float ss = rg == 0 ? o * o : 0.f;
+    ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+    ss += __shfl_xor_sync(0xffffffffu, ss, 2);
+    ss += __shfl_xor_sync(0xffffffffu, ss, 4);
+    __syncthreads();
+    if (lane == 0) red[0][w] = ss;
+    __syncthreads();
+    if (t < a.cb) {  // push this CTA's partial to slot cb of every CTA of the head
+        const float mine = red[0][0] + red[0][1] + red[0][2] + red[0][3];
+        uint32_t dst;
+        asm volatile("mapa.shared::cluster.u32 %0, %1, %2;"
+                     : "=r"(dst)
+                     : "r"(dev::smem_u32(&part[cb])), "r"((uint32_t)(hr * a.cb + t)));
+        asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(dst), "f"(mine) : "memory");
+    }
+    cl_sync();
+    float tot = 0.f;
+    for (int i = 0; i < a.cb; ++i) tot += part[i];
+    const float inv = 1.f / sqrtf(tot / (float)a.dv + a.eps);
+    if (rg == 0) {
+        const int64_t oi = (int64_t)h * a.dv + j;
+        a.out[oi] = ((a.gamma[j] * o) * inv) * silu_ref(a.z[oi]);
+    }
+}
+
 int update_history(nmg_conv_state* s, const float* x, int64_t T, cudaStream_t stream) {
     if (s->width < 2) return NMG_OK;
     const dim3 grid((unsigned)((s->channels + 127) / 128));
@@ -425,5 +575,68 @@ extern "C" int nmg_delta_epilogue(int hv, int dv, int64_t T, const float* o, con
     else
         epilogue_kernel<33><<<grid, 256, 0, st>>>(o, z, gamma, eps, out, rows, dv);
     NMG_CUDA_TRY(cudaGetLastError());
+    return NMG_OK;
+}
+
+extern "C" int nmg_delta_decode_token(nmg_delta_state* st, nmg_conv_state* conv, const float* weights, int hk,
+                                      const float* qkv, const float* beta_raw, const float* alpha_raw,
+                                      const float* dt_bias, const float* decay_scale, const float* z,
+                                      const float* gamma, float eps, float* out, void* stream) {
+    if (!st || !conv) return set_error(NMG_INVALID_ARGUMENT, "nmg_delta_decode_token: null state");
+    const int hv = st->heads, dk = st->dk, dv = st->dv;
+    if (hk <= 0 || hv % hk != 0)
+        return set_error(NMG_INVALID_ARGUMENT, "nmg_delta_decode_token: Hv = %d is not a multiple of Hk = %d", hv, hk);
+    if ((int64_t)2 * hk * dk + (int64_t)hv * dv != conv->channels)
+        return set_error(NMG_INVALID_ARGUMENT, "nmg_delta_decode_token: conv state has %d channels, 2*Hk*Dk + Hv*Dv = %lld",
+                         conv->channels, (long long)(2ll * hk * dk + (int64_t)hv * dv));
+    if (!weights || !qkv || !beta_raw || !alpha_raw || !dt_bias || !decay_scale || !z || !gamma || !out)
+        return set_error(NMG_INVALID_ARGUMENT, "nmg_delta_decode_token: null argument");
+    if (conv->device != st->device) return set_error(NMG_INVALID_ARGUMENT, "nmg_delta_decode_token: states on two devices");
+    const int ratio = hv / hk, cbs = dv / 32;
+    if (dk != 128 || dv % 32 != 0 || ratio * cbs > 8)
+        return set_error(NMG_UNSUPPORTED,
+                         "nmg_delta_decode_token: built for Dk = 128 and (Hv/Hk) x (Dv/32) <= 8 (Dk %d, Dv %d, Hv/Hk %d)", dk,
+                         dv, ratio);
+    DecodeArgs a;
+    a.state = st->data;
+    a.hist = conv->hist;
+    a.weights = weights;
+    a.qkv = qkv;
+    a.beta_raw = beta_raw;
+    a.alpha_raw = alpha_raw;
+    a.dt_bias = dt_bias;
+    a.decay_scale = decay_scale;
+    a.z = z;
+    a.gamma = gamma;
+    a.out = out;
+    a.hk = hk;
+    a.hv = hv;
+    a.dv = dv;
+    a.cb = cbs;
+    a.C = conv->channels;
+    a.q_scale = 1.f / sqrtf((float)dk);  // qwen35.hpp:427
+    a.eps = eps;
+    int prev = 0;
+    NMG_CUDA_TRY(cudaGetDevice(&prev));
+    if (prev != st->device) NMG_CUDA_TRY(cudaSetDevice(st->device));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(hk * ratio * cbs), 1, 1);
+    cfg.blockDim = dim3(128, 1, 1);
+    cfg.stream = (cudaStream_t)stream;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = (unsigned)(ratio * cbs);
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    cudaError_t e = cudaErrorInvalidValue;
+#define NMG_DEC(WW) e = cudaLaunchKernelEx(&cfg, delta_decode_kernel<WW>, a)
+    NMG_CONV_WIDTHS(conv->width, NMG_DEC)
+#undef NMG_DEC
+    if (prev != st->device) cudaSetDevice(prev);
+    if (e != cudaSuccess) return set_error(NMG_CUDA_ERROR, "nmg_delta_decode_token: %s", cudaGetErrorString(e));
     return NMG_OK;
 }

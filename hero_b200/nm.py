@@ -514,6 +514,20 @@ def delta_epilogue(o, z, gamma, eps: float = 1e-6, *, out=None) -> torch.Tensor:
     return out
 
 
+def delta_decode_token(state: DeltaNetState, conv: ConvState, conv_weights, qkv, beta_raw, alpha_raw, dt_bias,
+                       decay_scale, hk: int, z, gamma, eps: float = 1e-6, *, out=None) -> torch.Tensor:
+    """One decode token of the layer core in one launch (qwen35.hpp:396-461 at
+    T = 1): delta_prologue, delta_step and delta_epilogue fused.  qkv
+    [2*hk*dk + hv*dv], beta_raw/alpha_raw [hv], z [hv, dv]; returns [hv, dv]."""
+    qkv = _dev(qkv)
+    if out is None:
+        out = torch.empty(state.heads, state.dv, dtype=torch.float32, device=qkv.device)
+    call("nmg_delta_decode_token", state.handle, conv.handle, _ptr(_dev(conv_weights)), int(hk), _ptr(qkv),
+         _ptr(_dev(beta_raw)), _ptr(_dev(alpha_raw)), _ptr(_dev(dt_bias)), _ptr(_dev(decay_scale)), _ptr(_dev(z)),
+         _ptr(_dev(gamma)), float(eps), _ptr(out), _stream(qkv.device))
+    return out
+
+
 # ---- multi-GPU: output rows assembled by the attention epilogue -------------
 
 class SharedRows:

@@ -332,6 +332,22 @@ NMG_API int nmg_delta_prologue(nmg_conv_state* conv, const float* conv_weights, 
 NMG_API int nmg_delta_epilogue(int hv, int dv, int64_t T, const float* o, const float* z, const float* gamma, float eps,
                                float* out, void* stream);
 
+/* One decode token of the linear-attention layer core in one launch
+ * (qwen35.hpp:396-461 at T = 1): the prologue of nmg_delta_prologue (conv +
+ * SiLU, per-key-head L2 norms, q's 1/sqrt(Dk), beta and the decay gate), the
+ * recurrent step of nmg_delta_step over every value head and the gated output
+ * norm of nmg_delta_epilogue, replacing those three launches per layer and
+ * token.  qkv: [2*Hk*Dk + Hv*Dv] ([q | k | v] channels); beta_raw, alpha_raw,
+ * dt_bias, decay_scale: [Hv]; z, out: [Hv][Dv]; gamma: [Dv].  The conv
+ * history and the state advance by the token.  Hv is the state's head count.
+ * Built for Dk = 128, Dv a multiple of 32 and (Hv/Hk) x (Dv/32) <= 8 (Qwen
+ * 3.5's 32 value / 16 key heads at 128); other shapes return NMG_UNSUPPORTED
+ * and take the three calls. */
+NMG_API int nmg_delta_decode_token(nmg_delta_state* state, nmg_conv_state* conv, const float* conv_weights, int hk,
+                                   const float* qkv, const float* beta_raw, const float* alpha_raw,
+                                   const float* dt_bias, const float* decay_scale, const float* z, const float* gamma,
+                                   float eps, float* out, void* stream);
+
 /* ---- multi-GPU: KV-head-group sharding + one all-gather --------------------
  *
  * The reference has no distributed backend (it runs par_for on one host).

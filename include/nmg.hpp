@@ -228,6 +228,16 @@ void delta_epilogue(size_t tokens, const float* o, const float* z, const float* 
                     void* stream) {
     check(nmg_delta_epilogue(int(Hv), int(Dv), int64_t(tokens), o, z, gamma, eps, out, stream));
 }
+// One decode token of the layer core (qwen35.hpp:396-461 at T = 1): the
+// prologue, the recurrent step and the gated output norm in one launch.
+template <size_t Hk, size_t Hv, size_t Dk, size_t Dv, size_t Width>
+void delta_decode_token(DeltaNetState<Hv, Dk, Dv>& state, CausalConv1dState<2 * Hk * Dk + Hv * Dv, Width>& conv,
+                        const float* conv_weights, const float* qkv, const float* beta_raw, const float* alpha_raw,
+                        const float* dt_bias, const float* decay_scale, const float* z, const float* gamma, float eps,
+                        float* out, void* stream) {
+    check(nmg_delta_decode_token(state.handle(), conv.handle(), conv_weights, int(Hk), qkv, beta_raw, alpha_raw,
+                                 dt_bias, decay_scale, z, gamma, eps, out, stream));
+}
 
 // Before an attention reduction: Q = rope(rmsnorm_per_head(q)) into q_out,
 // K = rope(rmsnorm_per_head(k)) and V (scale-free per-head RMS norm when
