@@ -203,7 +203,16 @@ __global__ void __launch_bounds__(128) attn_decode_mma_kernel(const __grid_const
     if (tid == 0) {
         for (int s = 0; s < ST; ++s) dev::mbar_init(&full[s], 1);
         dev::fence_mbar_init();
+        if constexpr (!Q8) {
+            dev::prefetch_tensormap(tmk);
+            dev::prefetch_tensormap(tmv);
+        }
     }
+    // Launched with programmatic stream serialisation: the set-up above
+    // overlaps the previous kernel's tail; q, the cache, the scratch partials
+    // and the tickets are touched only after its results are visible.
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     // Stage the query heads as 16-bit rows (rows past the group are zero).
     for (int i = tid; i < 16 * (DH / 8); i += 128) {
         const int g = i / (DH / 8), c8 = i % (DH / 8);
@@ -466,8 +475,17 @@ int launch_mma(const MmaArgs& a, dim3 grid, cudaStream_t s) {
     static std::atomic<uint64_t> attr_set{0};  // one bit per device
     const int st = set_smem_once(kern, C::SMEM, attr_set);
     if (st != NMG_OK) return st;
-    kern<<<grid, 128, C::SMEM, s>>>(a);
-    NMG_CUDA_TRY(cudaGetLastError());
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(128, 1, 1);
+    cfg.dynamicSmemBytes = C::SMEM;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    NMG_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, a));
     return NMG_OK;
 }
 
