@@ -200,8 +200,11 @@ __global__ void __launch_bounds__(128) attn_decode_mma_kernel(const __grid_const
     const CUtensorMap* tmk = &a.tm_k[r.map];
     const CUtensorMap* tmv = &a.tm_v[r.map];
 
+    // One stage (head_dim 256): K and V land on barriers of their own, so the
+    // next tile's K loads while this tile's softmax and P.V run.
+    constexpr bool SPLIT = ST == 1 && !Q8;
     if (tid == 0) {
-        for (int s = 0; s < ST; ++s) dev::mbar_init(&full[s], 1);
+        for (int s = 0; s < (SPLIT ? 2 : ST); ++s) dev::mbar_init(&full[s], 1);
         dev::fence_mbar_init();
         if constexpr (!Q8) {
             dev::prefetch_tensormap(tmk);
@@ -260,6 +263,19 @@ __global__ void __launch_bounds__(128) attn_decode_mma_kernel(const __grid_const
         }
     };
 
+    auto issue_half = [&](int t, int which) {  // SPLIT: K (0) or V (1) of tile t
+        if (tid == 0) {
+            const int64_t u0 = (jb + t) * KT;
+            const int32_t row = (int32_t)(h * r.slots + u0 % r.slots);
+            dev::fence_proxy_async_smem();
+            dev::mbar_arrive_expect_tx(&full[which], C::TILE_BYTES);
+#pragma unroll
+            for (int c = 0; c < DH / 64; ++c)
+                dev::tma_load_2d(smem + which * C::TILE_BYTES + c * KT * 128, which ? tmv : tmk, c * 64, row,
+                                 &full[which]);
+        }
+    };
+
     // A fragments of Q (m16k16 per 16 columns of d), rows g = lane/4 (+8).
     uint32_t qa[DH / 16][4];
     {
@@ -280,10 +296,14 @@ __global__ void __launch_bounds__(128) attn_decode_mma_kernel(const __grid_const
 
     bool aborted = false;
     for (int t = 0; t < ST - 1 && t < ntiles; ++t) issue(t, t);
+    if (SPLIT && ntiles > 0) {
+        issue_half(0, 0);
+        issue_half(0, 1);
+    }
     for (int t = 0; t < ntiles; ++t) {
         const int st = t % ST;
-        if (t + ST - 1 < ntiles) issue(t + ST - 1, (t + ST - 1) % ST);
-        const bool ok = dev::mbar_wait(&full[st], (t / ST) & 1, a.err);
+        if (!SPLIT && t + ST - 1 < ntiles) issue(t + ST - 1, (t + ST - 1) % ST);
+        const bool ok = dev::mbar_wait(&full[st], SPLIT ? (t & 1) : ((t / ST) & 1), a.err);
         if (__syncthreads_or(!ok)) {
             aborted = true;
             break;
@@ -335,6 +355,10 @@ __global__ void __launch_bounds__(128) attn_decode_mma_kernel(const __grid_const
             mma_16816<BF16>(sc[0], qa[kk], b0, b1);
             mma_16816<BF16>(sc[1], qa[kk], b2, b3);
         }
+        if constexpr (SPLIT) {  // every warp is done with K(t): fetch K(t + 1)
+            __syncthreads();
+            if (t + 1 < ntiles) issue_half(t + 1, 0);
+        }
         // mask + scale: accumulator element (row, key) with key = 8n + 2*(lane%4) + {0,1}
         const int64_t p_tile = r.base + (jb + t) * KT + key0;
         float mx[2] = {-INFINITY, -INFINITY};
@@ -382,6 +406,13 @@ __global__ void __launch_bounds__(128) attn_decode_mma_kernel(const __grid_const
             o[n][2] *= alpha[1];
             o[n][3] *= alpha[1];
         }
+        if constexpr (SPLIT) {
+            const bool okv = dev::mbar_wait(&full[1], t & 1, a.err);
+            if (__syncthreads_or(!okv)) {
+                aborted = true;
+                break;
+            }
+        }
         // O += P V: per 16 columns of d one ldmatrix.trans (x4) and two MMAs.
 #pragma unroll
         for (int dd = 0; dd < DH / 16; ++dd) {
@@ -394,6 +425,7 @@ __global__ void __launch_bounds__(128) attn_decode_mma_kernel(const __grid_const
             mma_16816<false>(o[2 * dd + 1], pfrag, b2, b3);
         }
         __syncthreads();  // the stage is refilled next iteration
+        if (SPLIT && t + 1 < ntiles) issue_half(t + 1, 1);
     }
     if (aborted) return;
 
