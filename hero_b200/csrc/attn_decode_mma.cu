@@ -49,6 +49,7 @@ struct MmaArgs {
     CUtensorMap tm_v[kMmaMaxBatch];
     Q8Src q8[kMmaMaxBatch];          // the same caches when they are Q8_0 (no tensor maps then)
     int q_dtype;                     // Q8_0 caches: the query's dtype, staged as fp16
+    int hn;                          // 1: heads in the MMA's N (subgroups of 8 heads), 0: in M (16)
     int mode;  // 0: one cache, rows first_query..; 1: table
     int hkv, hq, gtot, zdim;
     int64_t blocks_per_split;
@@ -177,7 +178,11 @@ __device__ __forceinline__ uint32_t tile_off(int key, int chunk) {
     return (uint32_t)((chunk >> 3) * (KT * 128) + key * 128 + (((chunk & 7) ^ (key & 7)) << 4));
 }
 
-template <int DH, bool BF16, bool Q8 = false>
+// HN (heads in N, groups of at most 8): S^T = K Q^T with the keys in the
+// MMA's M rows and the group's heads in its N = 8 columns, O^T += V^T P^T the
+// same way, so a group of 8 or fewer wastes at most 7 of 8 columns instead of
+// 15 of 16 rows and the O accumulator is half the size.
+template <int DH, bool BF16, bool Q8 = false, bool HN = false>
 __global__ void __launch_bounds__(128) attn_decode_mma_kernel(const __grid_constant__ MmaArgs a) {
     using C = MmaCfg<DH, Q8>;
     constexpr int ST = C::STAGES;
@@ -191,8 +196,9 @@ __global__ void __launch_bounds__(128) attn_decode_mma_kernel(const __grid_const
     const int h = blockIdx.y, z = blockIdx.z;
     MmaRow r;
     if (!mma_row(a, blockIdx.x, r)) return;
-    const int G = a.gtot - z * 16 < 16 ? a.gtot - z * 16 : 16;  // valid query heads of this subgroup
-    const int qh0 = h * a.gtot + z * 16;
+    constexpr int GZ = HN ? 8 : 16;  // query heads per subgroup
+    const int G = a.gtot - z * GZ < GZ ? a.gtot - z * GZ : GZ;  // valid query heads of this subgroup
+    const int qh0 = h * a.gtot + z * GZ;
     const int64_t u_lo = r.lo - r.base, u_hi = r.hi - r.base;
     const int64_t jb = u_lo / KT + r.s * a.blocks_per_split;
     const int64_t je = min(u_lo / KT + (r.s + 1) * a.blocks_per_split, u_hi / KT + 1);
@@ -276,9 +282,19 @@ __global__ void __launch_bounds__(128) attn_decode_mma_kernel(const __grid_const
         }
     };
 
-    // A fragments of Q (m16k16 per 16 columns of d), rows g = lane/4 (+8).
+    // Q fragments.  Rows form: A fragments (m16k16 per 16 columns of d), rows
+    // g = lane/4 (+8).  HN: B fragments (k16 x n8), head lane/4, dims
+    // 2*(lane%4) (+1, +8, +9) -- straight 32-bit reads of the staged rows.
     uint32_t qa[DH / 16][4];
-    {
+    uint32_t qb[DH / 16][2];
+    if constexpr (HN) {
+        const unsigned char* qrow = smem + C::Q_OFF + (lane >> 2) * C::Q_PITCH;
+#pragma unroll
+        for (int kk = 0; kk < DH / 16; ++kk) {
+            qb[kk][0] = *(const uint32_t*)(qrow + (kk * 16 + 2 * (lane & 3)) * 2);
+            qb[kk][1] = *(const uint32_t*)(qrow + (kk * 16 + 8 + 2 * (lane & 3)) * 2);
+        }
+    } else {
         const uint32_t qbase = dev::smem_u32(smem + C::Q_OFF);
 #pragma unroll
         for (int kk = 0; kk < DH / 16; ++kk) {
@@ -289,10 +305,14 @@ __global__ void __launch_bounds__(128) attn_decode_mma_kernel(const __grid_const
         }
     }
 
-    float o[DH / 8][4];
+    // O accumulators: rows form O[16 heads x DH] as DH / 8 n8 tiles; HN
+    // O^T[DH x 8 heads] as DH / 16 m16 tiles.
+    constexpr int NO = HN ? DH / 16 : DH / 8;
+    float o[NO][4];
 #pragma unroll
-    for (int n = 0; n < DH / 8; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
-    float m_r[2] = {-INFINITY, -INFINITY}, l_r[2] = {0.f, 0.f};  // rows lane/4 and lane/4 + 8
+    for (int n = 0; n < NO; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+    // rows form: rows lane/4 and lane/4 + 8; HN: heads 2*(lane%4) and 2*(lane%4) + 1
+    float m_r[2] = {-INFINITY, -INFINITY}, l_r[2] = {0.f, 0.f};
 
     bool aborted = false;
     for (int t = 0; t < ST - 1 && t < ntiles; ++t) issue(t, t);
@@ -343,68 +363,135 @@ __global__ void __launch_bounds__(128) attn_decode_mma_kernel(const __grid_const
         const uint32_t vbase = kbase + C::TILE_BYTES;
         const int key0 = wid * 16;  // this warp's keys within the tile
 
-        // S = Q K^T over this warp's 16 keys: two n8 tiles.
-        float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+        float st4[4] = {0.f, 0.f, 0.f, 0.f};  // HN: S^T[16 keys x 8 heads]
+        if constexpr (HN) {
 #pragma unroll
-        for (int kk = 0; kk < DH / 16; ++kk) {
-            // matrices: (keys 0-7, d lo), (keys 0-7, d hi), (keys 8-15, d lo), (keys 8-15, d hi)
-            const int key = key0 + (lane & 7) + (lane >> 4) * 8;
-            const int chunk = kk * 2 + ((lane >> 3) & 1);
-            uint32_t b0, b1, b2, b3;
-            ldsm_x4(kbase + tile_off<DH>(key, chunk), b0, b1, b2, b3);
-            mma_16816<BF16>(sc[0], qa[kk], b0, b1);
-            mma_16816<BF16>(sc[1], qa[kk], b2, b3);
+            for (int kk = 0; kk < DH / 16; ++kk) {
+                // A = K[16 keys x 16 dims]: (keys 0-7, d lo), (keys 8-15, d lo), (keys 0-7, d hi), (keys 8-15, d hi)
+                const int key = key0 + (lane & 7) + ((lane >> 3) & 1) * 8;
+                const int chunk = kk * 2 + (lane >> 4);
+                uint32_t ka[4];
+                ldsm_x4(kbase + tile_off<DH>(key, chunk), ka[0], ka[1], ka[2], ka[3]);
+                mma_16816<BF16>(st4, ka, qb[kk][0], qb[kk][1]);
+            }
+        }
+        float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+        if constexpr (!HN) {
+            // S = Q K^T over this warp's 16 keys: two n8 tiles.
+    #pragma unroll
+            for (int kk = 0; kk < DH / 16; ++kk) {
+                // matrices: (keys 0-7, d lo), (keys 0-7, d hi), (keys 8-15, d lo), (keys 8-15, d hi)
+                const int key = key0 + (lane & 7) + (lane >> 4) * 8;
+                const int chunk = kk * 2 + ((lane >> 3) & 1);
+                uint32_t b0, b1, b2, b3;
+                ldsm_x4(kbase + tile_off<DH>(key, chunk), b0, b1, b2, b3);
+                mma_16816<BF16>(sc[0], qa[kk], b0, b1);
+                mma_16816<BF16>(sc[1], qa[kk], b2, b3);
+            }
         }
         if constexpr (SPLIT) {  // every warp is done with K(t): fetch K(t + 1)
             __syncthreads();
             if (t + 1 < ntiles) issue_half(t + 1, 0);
         }
-        // mask + scale: accumulator element (row, key) with key = 8n + 2*(lane%4) + {0,1}
-        const int64_t p_tile = r.base + (jb + t) * KT + key0;
-        float mx[2] = {-INFINITY, -INFINITY};
-#pragma unroll
-        for (int n = 0; n < 2; ++n)
+        uint32_t pfrag[4];  // rows form: the P A fragment; HN: [0], [1] the P^T B fragment
+        if constexpr (HN) {
+            // mask + scale: st4[e] is (key lane/4 (+8 for e >= 2), head 2*(lane%4) + (e & 1))
+            const int64_t p_key = r.base + (jb + t) * KT + key0 + (lane >> 2);
+            float mx[2] = {-INFINITY, -INFINITY};
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
-                const int64_t pos = p_tile + 8 * n + 2 * (lane & 3) + (e & 1);
-                float x = sc[n][e] * a.scale_log2;
+                const int64_t pos = p_key + (e >> 1) * 8;
+                float x = st4[e] * a.scale_log2;
                 if (pos < r.lo || pos > r.hi) x = -INFINITY;
-                sc[n][e] = x;
-                mx[e >> 1] = fmaxf(mx[e >> 1], x);
+                st4[e] = x;
+                mx[e & 1] = fmaxf(mx[e & 1], x);
             }
-        float alpha[2];
+            float alpha[2];
 #pragma unroll
-        for (int hr = 0; hr < 2; ++hr) {
-            mx[hr] = fmaxf(mx[hr], __shfl_xor_sync(0xffffffffu, mx[hr], 1));
-            mx[hr] = fmaxf(mx[hr], __shfl_xor_sync(0xffffffffu, mx[hr], 2));
-            const float m_new = fmaxf(m_r[hr], mx[hr]);
-            alpha[hr] = (m_new == -INFINITY) ? 1.f : ex2f(m_r[hr] - m_new);  // ex2(-inf) = 0 for the first block
-            m_r[hr] = m_new;
-        }
-        float ps[2] = {0.f, 0.f};
-        uint32_t pa[4];
-#pragma unroll
-        for (int n = 0; n < 2; ++n) {
+            for (int hh = 0; hh < 2; ++hh) {  // over the 8 lanes that share the head pair
+                mx[hh] = fmaxf(mx[hh], __shfl_xor_sync(0xffffffffu, mx[hh], 4));
+                mx[hh] = fmaxf(mx[hh], __shfl_xor_sync(0xffffffffu, mx[hh], 8));
+                mx[hh] = fmaxf(mx[hh], __shfl_xor_sync(0xffffffffu, mx[hh], 16));
+                const float m_new = fmaxf(m_r[hh], mx[hh]);
+                alpha[hh] = (m_new == -INFINITY) ? 1.f : ex2f(m_r[hh] - m_new);
+                m_r[hh] = m_new;
+            }
             float p[4];
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
-                const float m = m_r[e >> 1];
-                p[e] = (m == -INFINITY) ? 0.f : ex2f(sc[n][e] - m);
-                ps[e >> 1] += p[e];
+                const float m = m_r[e & 1];
+                p[e] = (m == -INFINITY) ? 0.f : ex2f(st4[e] - m);
             }
-            pa[2 * n] = pack_h2(p[0], p[1]);      // row g, keys of n-tile n
-            pa[2 * n + 1] = pack_h2(p[2], p[3]);  // row g + 8
-        }
-        l_r[0] = l_r[0] * alpha[0] + ps[0];
-        l_r[1] = l_r[1] * alpha[1] + ps[1];
-        // A operand order for m16k16: a0 (g, k0-7) a1 (g+8, k0-7) a2 (g, k8-15) a3 (g+8, k8-15)
-        const uint32_t pfrag[4] = {pa[0], pa[1], pa[2], pa[3]};
+            l_r[0] = l_r[0] * alpha[0] + (p[0] + p[2]);
+            l_r[1] = l_r[1] * alpha[1] + (p[1] + p[3]);
+            // P^T as the B operand (k16 keys x n8 heads): lane L needs head
+            // n = L/4 at keys 2q, 2q+1 (+8, +9), q = L%4, which lanes 8q + n/2
+            // and 8q + 4 + n/2 hold (the n-th half of their packed pair).
+            const uint32_t pk01 = pack_h2(p[0], p[1]), pk23 = pack_h2(p[2], p[3]);
+            const int n = lane >> 2, q = lane & 3;
+            const int sa = 8 * q + (n >> 1), sb = sa + 4;
+            const uint32_t v0 = __shfl_sync(0xffffffffu, pk01, sa), v1 = __shfl_sync(0xffffffffu, pk01, sb);
+            const uint32_t v2 = __shfl_sync(0xffffffffu, pk23, sa), v3 = __shfl_sync(0xffffffffu, pk23, sb);
+            const uint32_t sel = (n & 1) ? 0x7632u : 0x5410u;
+            pfrag[0] = __byte_perm(v0, v1, sel);
+            pfrag[1] = __byte_perm(v2, v3, sel);
+            pfrag[2] = pfrag[3] = 0u;
 #pragma unroll
-        for (int n = 0; n < DH / 8; ++n) {
-            o[n][0] *= alpha[0];
-            o[n][1] *= alpha[0];
-            o[n][2] *= alpha[1];
-            o[n][3] *= alpha[1];
+            for (int dd = 0; dd < NO; ++dd) {  // o[dd][e] is (dim row, head 2*(lane%4) + (e & 1))
+                o[dd][0] *= alpha[0];
+                o[dd][1] *= alpha[1];
+                o[dd][2] *= alpha[0];
+                o[dd][3] *= alpha[1];
+            }
+        }
+        if constexpr (!HN) {
+            // mask + scale: accumulator element (row, key) with key = 8n + 2*(lane%4) + {0,1}
+            const int64_t p_tile = r.base + (jb + t) * KT + key0;
+            float mx[2] = {-INFINITY, -INFINITY};
+    #pragma unroll
+            for (int n = 0; n < 2; ++n)
+    #pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int64_t pos = p_tile + 8 * n + 2 * (lane & 3) + (e & 1);
+                    float x = sc[n][e] * a.scale_log2;
+                    if (pos < r.lo || pos > r.hi) x = -INFINITY;
+                    sc[n][e] = x;
+                    mx[e >> 1] = fmaxf(mx[e >> 1], x);
+                }
+            float alpha[2];
+    #pragma unroll
+            for (int hr = 0; hr < 2; ++hr) {
+                mx[hr] = fmaxf(mx[hr], __shfl_xor_sync(0xffffffffu, mx[hr], 1));
+                mx[hr] = fmaxf(mx[hr], __shfl_xor_sync(0xffffffffu, mx[hr], 2));
+                const float m_new = fmaxf(m_r[hr], mx[hr]);
+                alpha[hr] = (m_new == -INFINITY) ? 1.f : ex2f(m_r[hr] - m_new);  // ex2(-inf) = 0 for the first block
+                m_r[hr] = m_new;
+            }
+            float ps[2] = {0.f, 0.f};
+            uint32_t pa[4];
+    #pragma unroll
+            for (int n = 0; n < 2; ++n) {
+                float p[4];
+    #pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const float m = m_r[e >> 1];
+                    p[e] = (m == -INFINITY) ? 0.f : ex2f(sc[n][e] - m);
+                    ps[e >> 1] += p[e];
+                }
+                pa[2 * n] = pack_h2(p[0], p[1]);      // row g, keys of n-tile n
+                pa[2 * n + 1] = pack_h2(p[2], p[3]);  // row g + 8
+            }
+            l_r[0] = l_r[0] * alpha[0] + ps[0];
+            l_r[1] = l_r[1] * alpha[1] + ps[1];
+            // A operand order for m16k16: a0 (g, k0-7) a1 (g+8, k0-7) a2 (g, k8-15) a3 (g+8, k8-15)
+            pfrag[0] = pa[0], pfrag[1] = pa[1], pfrag[2] = pa[2], pfrag[3] = pa[3];
+    #pragma unroll
+            for (int n = 0; n < DH / 8; ++n) {
+                o[n][0] *= alpha[0];
+                o[n][1] *= alpha[0];
+                o[n][2] *= alpha[1];
+                o[n][3] *= alpha[1];
+            }
         }
         if constexpr (SPLIT) {
             const bool okv = dev::mbar_wait(&full[1], t & 1, a.err);
@@ -413,43 +500,80 @@ __global__ void __launch_bounds__(128) attn_decode_mma_kernel(const __grid_const
                 break;
             }
         }
-        // O += P V: per 16 columns of d one ldmatrix.trans (x4) and two MMAs.
+        if constexpr (HN) {
+            // O^T += V^T P^T: per 16 dims one ldmatrix.trans (x4) of V and one MMA.
 #pragma unroll
-        for (int dd = 0; dd < DH / 16; ++dd) {
-            // matrices: (keys 0-7, d lo), (keys 8-15, d lo), (keys 0-7, d hi), (keys 8-15, d hi)
-            const int key = key0 + (lane & 7) + ((lane >> 3) & 1) * 8;
-            const int chunk = dd * 2 + (lane >> 4);
-            uint32_t b0, b1, b2, b3;
-            ldsm_x4_t(vbase + tile_off<DH>(key, chunk), b0, b1, b2, b3);
-            mma_16816<false>(o[2 * dd], pfrag, b0, b1);
-            mma_16816<false>(o[2 * dd + 1], pfrag, b2, b3);
+            for (int dd = 0; dd < NO; ++dd) {
+                // A = V^T[16 dims x 16 keys]: (d lo, keys 0-7), (d hi, keys 0-7), (d lo, keys 8-15), (d hi, keys 8-15)
+                const int key = key0 + (lane & 7) + (lane >> 4) * 8;
+                const int chunk = dd * 2 + ((lane >> 3) & 1);
+                uint32_t va[4];
+                ldsm_x4_t(vbase + tile_off<DH>(key, chunk), va[0], va[1], va[2], va[3]);
+                mma_16816<false>(o[dd], va, pfrag[0], pfrag[1]);
+            }
+        } else {
+            // O += P V: per 16 columns of d one ldmatrix.trans (x4) and two MMAs.
+    #pragma unroll
+            for (int dd = 0; dd < DH / 16; ++dd) {
+                // matrices: (keys 0-7, d lo), (keys 8-15, d lo), (keys 0-7, d hi), (keys 8-15, d hi)
+                const int key = key0 + (lane & 7) + ((lane >> 3) & 1) * 8;
+                const int chunk = dd * 2 + (lane >> 4);
+                uint32_t b0, b1, b2, b3;
+                ldsm_x4_t(vbase + tile_off<DH>(key, chunk), b0, b1, b2, b3);
+                mma_16816<false>(o[2 * dd], pfrag, b0, b1);
+                mma_16816<false>(o[2 * dd + 1], pfrag, b2, b3);
+            }
         }
         __syncthreads();  // the stage is refilled next iteration
         if (SPLIT && t + 1 < ntiles) issue_half(t + 1, 1);
     }
     if (aborted) return;
 
-    // ---- merge the 4 warps: row sums over the quad, then through shared memory
-#pragma unroll
-    for (int hr = 0; hr < 2; ++hr) {
-        l_r[hr] += __shfl_xor_sync(0xffffffffu, l_r[hr], 1);
-        l_r[hr] += __shfl_xor_sync(0xffffffffu, l_r[hr], 2);
-    }
-    const int g0 = lane >> 2;
+    // ---- merge the 4 warps: row sums over the lanes that share a row (head),
+    // then through shared memory as [head][DH + 2] per warp
     float* cw = cs + wid * 16 * (DH + 2);
+    if constexpr (HN) {
 #pragma unroll
-    for (int n = 0; n < DH / 8; ++n) {
-        const int c0 = 8 * n + 2 * (lane & 3);
-        cw[g0 * (DH + 2) + c0] = o[n][0];
-        cw[g0 * (DH + 2) + c0 + 1] = o[n][1];
-        cw[(g0 + 8) * (DH + 2) + c0] = o[n][2];
-        cw[(g0 + 8) * (DH + 2) + c0 + 1] = o[n][3];
-    }
-    if ((lane & 3) == 0) {
-        cw[g0 * (DH + 2) + DH] = m_r[0];
-        cw[g0 * (DH + 2) + DH + 1] = l_r[0];
-        cw[(g0 + 8) * (DH + 2) + DH] = m_r[1];
-        cw[(g0 + 8) * (DH + 2) + DH + 1] = l_r[1];
+        for (int hh = 0; hh < 2; ++hh) {
+            l_r[hh] += __shfl_xor_sync(0xffffffffu, l_r[hh], 4);
+            l_r[hh] += __shfl_xor_sync(0xffffffffu, l_r[hh], 8);
+            l_r[hh] += __shfl_xor_sync(0xffffffffu, l_r[hh], 16);
+        }
+        const int h0 = 2 * (lane & 3), d0 = lane >> 2;
+#pragma unroll
+        for (int dd = 0; dd < NO; ++dd) {
+            cw[h0 * (DH + 2) + 16 * dd + d0] = o[dd][0];
+            cw[(h0 + 1) * (DH + 2) + 16 * dd + d0] = o[dd][1];
+            cw[h0 * (DH + 2) + 16 * dd + d0 + 8] = o[dd][2];
+            cw[(h0 + 1) * (DH + 2) + 16 * dd + d0 + 8] = o[dd][3];
+        }
+        if (d0 == 0) {
+            cw[h0 * (DH + 2) + DH] = m_r[0];
+            cw[h0 * (DH + 2) + DH + 1] = l_r[0];
+            cw[(h0 + 1) * (DH + 2) + DH] = m_r[1];
+            cw[(h0 + 1) * (DH + 2) + DH + 1] = l_r[1];
+        }
+    } else {
+#pragma unroll
+        for (int hr = 0; hr < 2; ++hr) {
+            l_r[hr] += __shfl_xor_sync(0xffffffffu, l_r[hr], 1);
+            l_r[hr] += __shfl_xor_sync(0xffffffffu, l_r[hr], 2);
+        }
+        const int g0 = lane >> 2;
+#pragma unroll
+        for (int n = 0; n < NO; ++n) {
+            const int c0 = 8 * n + 2 * (lane & 3);
+            cw[g0 * (DH + 2) + c0] = o[n][0];
+            cw[g0 * (DH + 2) + c0 + 1] = o[n][1];
+            cw[(g0 + 8) * (DH + 2) + c0] = o[n][2];
+            cw[(g0 + 8) * (DH + 2) + c0 + 1] = o[n][3];
+        }
+        if ((lane & 3) == 0) {
+            cw[g0 * (DH + 2) + DH] = m_r[0];
+            cw[g0 * (DH + 2) + DH + 1] = l_r[0];
+            cw[(g0 + 8) * (DH + 2) + DH] = m_r[1];
+            cw[(g0 + 8) * (DH + 2) + DH + 1] = l_r[1];
+        }
     }
     __syncthreads();
 
@@ -500,10 +624,10 @@ __global__ void __launch_bounds__(128) attn_decode_mma_kernel(const __grid_const
     if (tid == 0) a.counters[cnt_idx] = 0;
 }
 
-template <int DH, bool BF16, bool Q8 = false>
-int launch_mma(const MmaArgs& a, dim3 grid, cudaStream_t s) {
+template <int DH, bool BF16, bool Q8, bool HN>
+int launch_mma_hn(const MmaArgs& a, dim3 grid, cudaStream_t s) {
     using C = MmaCfg<DH, Q8>;
-    auto kern = attn_decode_mma_kernel<DH, BF16, Q8>;
+    auto kern = attn_decode_mma_kernel<DH, BF16, Q8, HN>;
     static std::atomic<uint64_t> attr_set{0};  // one bit per device
     const int st = set_smem_once(kern, C::SMEM, attr_set);
     if (st != NMG_OK) return st;
@@ -519,6 +643,11 @@ int launch_mma(const MmaArgs& a, dim3 grid, cudaStream_t s) {
     cfg.numAttrs = 1;
     NMG_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, a));
     return NMG_OK;
+}
+
+template <int DH, bool BF16, bool Q8 = false>
+int launch_mma(const MmaArgs& a, dim3 grid, cudaStream_t s) {
+    return a.hn ? launch_mma_hn<DH, BF16, Q8, true>(a, grid, s) : launch_mma_hn<DH, BF16, Q8, false>(a, grid, s);
 }
 
 int dispatch_mma(const nmg_kv_cache* c, const MmaArgs& a, dim3 grid, cudaStream_t s) {
@@ -538,6 +667,9 @@ int dispatch_mma(const nmg_kv_cache* c, const MmaArgs& a, dim3 grid, cudaStream_
     }
     return set_error(NMG_UNSUPPORTED, "tensor-core decode: head_dim %d", c->dh);
 }
+
+// Groups of at most 8 query heads put the heads in the MMA's N dimension.
+int mma_heads_in_n(int gtot) { return gtot <= 8 ? 1 : 0; }
 
 int64_t mma_blocks_per_split(int64_t total_blocks) {
     // About 6 CTAs per SM of work, at most 128 tiles (8192 keys) per split.
@@ -589,7 +721,9 @@ int attend_rows_mma(const nmg_kv_cache* c, int hq, const void* q, int q_dtype, i
     MmaArgs* a = new MmaArgs();
     int st = kv_sources(c, a, 0);
     const int gtot = hq / c->hkv;
-    const int zdim = (gtot + 15) / 16;
+    const int hn = mma_heads_in_n(gtot);
+    const int zdim = hn ? 1 : (gtot + 15) / 16;
+    a->hn = hn;
     int64_t longest = 0, total_blocks = 0;
     for (int64_t t = 0; st == NMG_OK && t < rows; ++t) {
         const VisibleSpan sp = visible_span(first_query + t, window, floor_pos, newest);
@@ -634,7 +768,8 @@ int attend_batch_mma(const nmg_kv_cache* const* caches, int batch, const int64_t
                      int q_dtype, float scale, void* out, int out_dtype, cudaStream_t stream) {
     const nmg_kv_cache* c0 = caches[0];
     const int gtot = hq / c0->hkv;
-    const int zdim = (gtot + 15) / 16;
+    const int hn = mma_heads_in_n(gtot);
+    const int zdim = hn ? 1 : (gtot + 15) / 16;
     std::vector<VisibleSpan> spans(batch);
     int64_t total_blocks = 0;
     for (int b = 0; b < batch; ++b) {
@@ -678,6 +813,7 @@ int attend_batch_mma(const nmg_kv_cache* const* caches, int batch, const int64_t
         }
         if (st != NMG_OK) break;
         a->mode = 1;
+        a->hn = hn;
         a->hkv = c0->hkv;
         a->hq = hq;
         a->gtot = gtot;
