@@ -50,6 +50,8 @@ struct MmaArgs {
     Q8Src q8[kMmaMaxBatch];          // the same caches when they are Q8_0 (no tensor maps then)
     int q_dtype;                     // Q8_0 caches: the query's dtype, staged as fp16
     int hn;                          // 1: heads in the MMA's N (subgroups of 8 heads), 0: in M (16)
+    int cl;                          // > 1: every row has cl splits, one thread-block cluster, merged
+                                     // through distributed shared memory; 0: ticket merge
     int mode;  // 0: one cache, rows first_query..; 1: table
     int hkv, hq, gtot, zdim;
     int64_t blocks_per_split;
@@ -128,6 +130,7 @@ struct MmaCfg {
     static constexpr int BAR_OFF = Q_OFF + 16 * Q_PITCH;
     static constexpr int SMEM = BAR_OFF + 64 + 1024;            // + alignment slack
     static_assert(SMEM <= 232448, "shared memory budget");
+    static_assert(8 * (DH + 2) * 4 <= 16 * Q_PITCH, "a cluster-merge partial of 8 heads fits the staged-q region");
     static_assert(!Q8 || (Q8_QBYTES % 16 == 0 && Q8_SBYTES % 16 == 0 && F16_OFF % 1024 == 0),
                   "bulk copies move 16-byte multiples; the fp16 tiles keep the 128-byte swizzle atoms aligned");
 };
@@ -195,6 +198,8 @@ __global__ void __launch_bounds__(128) attn_decode_mma_kernel(const __grid_const
     const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
     const int h = blockIdx.y, z = blockIdx.z;
     MmaRow r;
+    // Under the cluster merge the host gives every row exactly a.cl splits,
+    // so every CTA of the grid has work and reaches the cluster barriers.
     if (!mma_row(a, blockIdx.x, r)) return;
     constexpr int GZ = HN ? 8 : 16;  // query heads per subgroup
     const int G = a.gtot - z * GZ < GZ ? a.gtot - z * GZ : GZ;  // valid query heads of this subgroup
@@ -527,7 +532,14 @@ __global__ void __launch_bounds__(128) attn_decode_mma_kernel(const __grid_const
         __syncthreads();  // the stage is refilled next iteration
         if (SPLIT && t + 1 < ntiles) issue_half(t + 1, 1);
     }
-    if (aborted) return;
+    if (aborted) {
+        if (!a.cl) return;
+        // the cluster's other CTAs wait at its barriers: offer an empty partial
+#pragma unroll
+        for (int n = 0; n < NO; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+        m_r[0] = m_r[1] = -INFINITY;
+        l_r[0] = l_r[1] = 0.f;
+    }
 
     // ---- merge the 4 warps: row sums over the lanes that share a row (head),
     // then through shared memory as [head][DH + 2] per warp
@@ -578,6 +590,8 @@ __global__ void __launch_bounds__(128) attn_decode_mma_kernel(const __grid_const
     __syncthreads();
 
     const bool single = r.nsplit == 1;
+    const bool clm = a.cl > 1;  // cluster merge
+    float* xp = (float*)(smem + C::Q_OFF);  // cluster merge: this CTA's partial [G][DH + 2] (the staged q is done)
     const int64_t cnt_idx = (r.qrow * (int64_t)a.hkv + h) * a.zdim + z;
     float* my_part = a.part + ((((int64_t)blockIdx.x) * a.hkv + h) * a.zdim + z) * (int64_t)(16 * (DH + 2));
     for (int i = tid; i < G * DH; i += 128) {
@@ -597,14 +611,54 @@ __global__ void __launch_bounds__(128) attn_decode_mma_kernel(const __grid_const
         if (single) {
             dev::store_from_f32(a.out, a.out_dtype, (r.qrow * (int64_t)a.hq + qh0 + g) * DH + d, O / L);
         } else {
-            my_part[g * (DH + 2) + d] = O;
+            float* dst = clm ? xp : my_part;
+            dst[g * (DH + 2) + d] = O;
             if (d == 0) {
-                my_part[g * (DH + 2) + DH] = M;
-                my_part[g * (DH + 2) + DH + 1] = L;
+                dst[g * (DH + 2) + DH] = M;
+                dst[g * (DH + 2) + DH + 1] = L;
             }
         }
     }
     if (single) return;
+    if (clm) {
+        // every split's partial is in its CTA's shared memory: CTA s of the
+        // cluster combines items [s * share, ...) of the G x DH over the splits
+        asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+        uint32_t rank;
+        asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(rank));
+        const int ncl = a.cl, items = G * DH, share = (items + ncl - 1) / ncl;
+        const uint32_t xbase = dev::smem_u32(xp);
+        for (int i = (int)rank * share + tid; i < min(items, ((int)rank + 1) * share); i += 128) {
+            const int g = i / DH, d = i % DH;
+            float Ms[8], Ls[8], Os[8], M = -INFINITY;
+#pragma unroll
+            for (int sp = 0; sp < 8; ++sp) {
+                Ms[sp] = -INFINITY, Ls[sp] = 0.f, Os[sp] = 0.f;
+                if (sp < ncl) {
+                    uint32_t ra;
+                    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(xbase), "r"((uint32_t)sp));
+                    const uint32_t rg = ra + (uint32_t)(g * (DH + 2)) * 4u;
+                    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(Ms[sp]) : "r"(rg + DH * 4) : "memory");
+                    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(Ls[sp]) : "r"(rg + (DH + 1) * 4) : "memory");
+                    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(Os[sp]) : "r"(rg + d * 4) : "memory");
+                    M = fmaxf(M, Ms[sp]);
+                }
+            }
+            float L = 0.f, O = 0.f;
+#pragma unroll
+            for (int sp = 0; sp < 8; ++sp)
+                if (Ms[sp] != -INFINITY) {
+                    const float f = ex2f(Ms[sp] - M);
+                    L = fmaf(Ls[sp], f, L);
+                    O = fmaf(Os[sp], f, O);
+                }
+            dev::store_from_f32(a.out, a.out_dtype, (r.qrow * (int64_t)a.hq + qh0 + g) * DH + d,
+                                L > 0.f ? O / L : 0.f);
+        }
+        // no CTA leaves while another may still read its partial
+        asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+        return;
+    }
 
     __threadfence();
     __syncthreads();
@@ -636,11 +690,18 @@ int launch_mma_hn(const MmaArgs& a, dim3 grid, cudaStream_t s) {
     cfg.blockDim = dim3(128, 1, 1);
     cfg.dynamicSmemBytes = C::SMEM;
     cfg.stream = s;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
+    if (a.cl > 1) {  // the splits of a row as one cluster
+        attr[1].id = cudaLaunchAttributeClusterDimension;
+        attr[1].val.clusterDim.x = (unsigned)a.cl;
+        attr[1].val.clusterDim.y = 1;
+        attr[1].val.clusterDim.z = 1;
+        cfg.numAttrs = 2;
+    }
     NMG_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, a));
     return NMG_OK;
 }
@@ -734,6 +795,14 @@ int attend_rows_mma(const nmg_kv_cache* c, int hq, const void* q, int q_dtype, i
     const int64_t bps = mma_blocks_per_split(total_blocks * c->hkv * zdim);
     const int64_t max_splits = (longest + bps - 1) / bps;
     const int64_t work = rows * max_splits;
+    // every row with the same split count (2..8), heads in N: merge through a cluster
+    bool uniform = hn && max_splits >= 2 && max_splits <= 8;
+    for (int64_t t = 0; uniform && t < rows; ++t) {
+        const VisibleSpan sp = visible_span(first_query + t, window, floor_pos, newest);
+        const int64_t nb = (sp.hi - c->base) / KT - (sp.lo - c->base) / KT + 1;
+        uniform = (nb + bps - 1) / bps == max_splits;
+    }
+    a->cl = uniform ? (int)max_splits : 0;
     if (st == NMG_OK && work > 0x7FFFFFFF) st = set_error(NMG_UNSUPPORTED, "decode: too many work items");
     if (st == NMG_OK) st = mma_scratch(c->device, work, c->hkv, zdim, c->dh, rows, &a->part, &a->counters);
     if (st == NMG_OK) st = device_error_flag(c->device, &a->err);
@@ -787,6 +856,10 @@ int attend_batch_mma(const nmg_kv_cache* const* caches, int batch, const int64_t
         nsplit[b] = (int32_t)((nb + bps - 1) / bps);
         all_work += nsplit[b];
     }
+    // every sequence with the same split count (2..8), heads in N: merge through a cluster
+    bool uniform = hn && nsplit[0] >= 2 && nsplit[0] <= 8;
+    for (int b = 1; uniform && b < batch; ++b) uniform = nsplit[b] == nsplit[0];
+    const int cl = uniform ? nsplit[0] : 0;
     float* part = nullptr;
     int* counters = nullptr;
     int st = mma_scratch(c0->device, all_work, c0->hkv, zdim, c0->dh, batch, &part, &counters);
@@ -814,6 +887,7 @@ int attend_batch_mma(const nmg_kv_cache* const* caches, int batch, const int64_t
         if (st != NMG_OK) break;
         a->mode = 1;
         a->hn = hn;
+        a->cl = cl;
         a->hkv = c0->hkv;
         a->hq = hq;
         a->gtot = gtot;
