@@ -524,4 +524,104 @@ void nmref_quantize_q8_0(const float* x, int64_t n, int8_t* qs, uint16_t* d) {
     }
 }
 
+
+// ---- quantised weights (quant.hpp, quant_i8.hpp) -------------------------
+// Packed activation blocks as the reference lays them out: quantize_row_q8_0
+// (34-byte block_q8_0) and quantize_row_q8_K (292-byte block_q8_K).
+void nmref_quantize_row_q8_0_blocks(const float* x, int64_t n, void* out) {
+    quantize_row_q8_0(x, static_cast<block_q8_0*>(out), (size_t)n);
+}
+void nmref_quantize_row_q8_K(const float* x, int64_t n, void* out) {
+    quantize_row_q8_K(x, static_cast<block_q8_K*>(out), (size_t)n);
+}
+// The weight-side quantisers the reference's tests build fixtures with.
+void nmref_quantize_q8_0_weights(const float* x, int64_t n, void* out) {
+    quantize_q8_0(x, static_cast<block_q8_0*>(out), (size_t)n);
+}
+void nmref_quantize_q4_0_weights(const float* x, int64_t n, void* out) {
+    quantize_q4_0(x, static_cast<block_q4_0*>(out), (size_t)n);
+}
+
+// One weight row's integer dot against a quantised activation row, through
+// the reference's own vec_dot_* (the scalar ggml-generic clones on hosts
+// without ARM dotprod).
+float nmref_vec_dot_i8(int type, int64_t n, const void* w, const void* act) {
+    switch (GT(type)) {
+        case GT::Q8_0:
+            return vec_dot_q8_0_q8_0((size_t)n, (const block_q8_0*)w, (const block_q8_0*)act);
+        case GT::Q4_0:
+            return vec_dot_q4_0_q8_0((size_t)n, (const block_q4_0*)w, (const block_q8_0*)act);
+        case GT::Q4_K:
+            return vec_dot_q4_K_q8_K((size_t)n, (const block_q4_K*)w, (const block_q8_K*)act);
+        case GT::Q6_K:
+            return vec_dot_q6_K_q8_K((size_t)n, (const block_q6_K*)w, (const block_q8_K*)act);
+        default:
+            return NAN;
+    }
+}
+
+// One weight row against fp32 activations: the dot_block_* sum of
+// Weight::matvec's fp32-activation branch (quant_i8.hpp:394-427).
+float nmref_dot_fp32(int type, int64_t n, const void* w, const float* x) {
+    Scalar acc = 0;
+    switch (GT(type)) {
+        case GT::Q8_0:
+            for (size_t i = 0; i < (size_t)n / QK8_0; ++i) acc += dot_block_q8_0(((const block_q8_0*)w)[i], x + i * QK8_0);
+            break;
+        case GT::Q4_0:
+            for (size_t i = 0; i < (size_t)n / QK4_0; ++i) acc += dot_block_q4_0(((const block_q4_0*)w)[i], x + i * QK4_0);
+            break;
+        case GT::Q4_K:
+            for (size_t i = 0; i < (size_t)n / QK_K; ++i) acc += dot_block_q4_K(((const block_q4_K*)w)[i], x + i * QK_K);
+            break;
+        case GT::Q5_K:
+            for (size_t i = 0; i < (size_t)n / QK_K; ++i) acc += dot_block_q5_K(((const block_q5_K*)w)[i], x + i * QK_K);
+            break;
+        case GT::Q6_K:
+            for (size_t i = 0; i < (size_t)n / QK_K; ++i) acc += dot_block_q6_K(((const block_q6_K*)w)[i], x + i * QK_K);
+            break;
+        default:
+            return NAN;
+    }
+    return acc;
+}
+
+int nmref_dequant(int type, const void* src, float* dst, int64_t n) {
+    return guarded([&] { dequant_to_f32(GT(type), src, dst, (size_t)n); });
+}
+
+}  // extern "C"
+
+namespace {
+template <size_t In, size_t Out>
+int weight_product(int type, const void* w, int64_t rows, const float* x, float* y) {
+    return guarded([&] {
+        const Weight<In, Out> weight(GT(type), w, std::shared_ptr<const void>());
+        if (rows == 1) {
+            const Vec<In> v = vec_from<In>(x);
+            const Vec<Out> r = weight.matvec(VecView<In>(v));
+            for (size_t o = 0; o < Out; ++o) y[o] = r[o];
+            return;
+        }
+        const Matrix<In> m = Matrix<In>::from_row_major(std::vector<Scalar>(x, x + (size_t)rows * In));
+        const Matrix<Out> r = weight.matmul(m.view());
+        for (size_t i = 0; i < (size_t)rows; ++i)
+            for (size_t o = 0; o < Out; ++o) y[i * Out + o] = r.row(i)[o];
+    });
+}
+}  // namespace
+
+extern "C" {
+
+// Weight<In,Out>::matvec (rows == 1) or ::matmul itself, for the shapes the
+// tests use; 100 for a shape that is not instantiated here.  Which activation
+// path runs is the reference's own choice (NM_FP32_ACT, read once).
+int nmref_weight_product(int type, int64_t in, int64_t out, const void* w, int64_t rows, const float* x, float* y) {
+#define X(I, O) \
+    if (in == I && out == O) return weight_product<I, O>(type, w, rows, x, y);
+    X(256, 40) X(512, 24) X(1024, 16) X(2048, 8)
+#undef X
+    return 100;
+}
+
 }  // extern "C"
