@@ -146,6 +146,14 @@ SIGNATURES = {
     "nmg_ipc_close": [_vp],
     "nmg_attend_fanout": [_vp, _i32, _vp, _i32, _i64, _i64, _f32, _i32, ctypes.POINTER(_vp), _i32, _i64, _i64, _i32,
                           _vp],
+    "nmg_weight_row_bytes": [_i32, _i64, ctypes.POINTER(_i64)],
+    "nmg_weight_create": [_i32, _i64, _i64, _vp, _i32, _i32, ctypes.POINTER(_vp)],
+    "nmg_weight_destroy": [_vp],
+    "nmg_weight_info": [_vp, ctypes.POINTER(_i32), ctypes.POINTER(_i64), ctypes.POINTER(_i64)],
+    "nmg_weight_matvec": [_vp, _vp, _vp, _i32, _vp],
+    "nmg_weight_matmul": [_vp, _i64, _vp, _vp, _i32, _vp],
+    "nmg_weight_gather_rows": [_vp, _vp, _i64, _vp, _vp],
+    "nmg_quantize_activations": [_i32, _i64, _i64, _vp, _vp, _vp],
 }
 
 

@@ -17,7 +17,7 @@ struct Pool {
     size_t bytes = 0;
 };
 struct DeviceResources {
-    Pool scratch, staging, tickets;
+    Pool scratch, staging, tickets, weight_act;
     int* error_flag = nullptr;
 };
 std::mutex g_mu;
@@ -73,6 +73,11 @@ int device_tickets(int device, size_t bytes, void** ptr) {
 int device_staging(int device, size_t bytes, void** ptr) {
     std::lock_guard<std::mutex> lk(g_mu);
     return grow(device, resources(device).staging, bytes, ptr);
+}
+
+int weight_act_scratch(int device, size_t bytes, void** ptr) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    return grow(device, resources(device).weight_act, bytes, ptr);
 }
 
 int device_error_flag(int device, int** flag) {

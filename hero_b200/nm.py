@@ -25,8 +25,10 @@ host.
 from __future__ import annotations
 
 import ctypes
+import os
 from dataclasses import dataclass
 
+import numpy as np
 import torch
 
 from . import _lib
@@ -525,6 +527,122 @@ def delta_decode_token(state: DeltaNetState, conv: ConvState, conv_weights, qkv,
     call("nmg_delta_decode_token", state.handle, conv.handle, _ptr(_dev(conv_weights)), int(hk), _ptr(qkv),
          _ptr(_dev(beta_raw)), _ptr(_dev(alpha_raw)), _ptr(_dev(dt_bias)), _ptr(_dev(decay_scale)), _ptr(_dev(z)),
          _ptr(_dev(gamma)), float(eps), _ptr(out), _stream(qkv.device))
+    return out
+
+
+# ---- quantised projections (src/quant.hpp, src/quant_i8.hpp) -----------------
+
+class GT:
+    """GGUF tensor types (src/quant.hpp:18-27); Q8_K is the activation block type."""
+    F32, F16, Q4_0, Q8_0, Q4_K, Q5_K, Q6_K, Q8_K, BF16 = 0, 1, 2, 8, 12, 13, 14, 15, 30
+
+
+def type_size_bytes(gt: int, nelem: int) -> int:
+    """Bytes of `nelem` values stored as `gt` (src/quant.hpp:89-108)."""
+    b = ctypes.c_int64()
+    call("nmg_weight_row_bytes", int(gt), int(nelem), ctypes.byref(b))
+    return b.value
+
+
+def _fp32_act_default() -> bool:
+    e = os.environ.get("NM_FP32_ACT", "")
+    return bool(e) and e[0] != "0"
+
+
+class Weight:
+    """Weight<In,Out> over GGUF bytes (src/quant.hpp:439-487), held on the device.
+
+    ``data``: ``out * type_size_bytes(gt, in_features)`` bytes, one row per
+    output, as a numpy/bytes buffer (host) or a uint8 CUDA tensor.  Products
+    follow the reference's activation handling: quantised Q8_0/Q8_K
+    activations and integer block dots for Q8_0, Q4_0, Q4_K and Q6_K, fp32
+    otherwise; ``fp32_act`` (default: the NM_FP32_ACT environment variable,
+    src/quant_i8.hpp:343-349) selects the fp32-activation path for every type."""
+
+    def __init__(self, gt: int, in_features: int, out_features: int, data, device: int = 0,
+                 fp32_act: bool | None = None):
+        self.gt, self.in_features, self.out_features, self.device = int(gt), int(in_features), int(out_features), int(device)
+        self.fp32_act = _fp32_act_default() if fp32_act is None else bool(fp32_act)
+        h = ctypes.c_void_p()
+        if isinstance(data, torch.Tensor):
+            if not data.is_cuda:
+                data = data.contiguous().numpy()
+            else:
+                data = data.contiguous()
+                call("nmg_weight_create", self.gt, self.in_features, self.out_features, ctypes.c_void_p(data.data_ptr()),
+                     1, self.device, ctypes.byref(h))
+        if not h.value:
+            buf = np.ascontiguousarray(np.frombuffer(data, dtype=np.uint8) if isinstance(data, (bytes, bytearray))
+                                       else np.asarray(data).view(np.uint8).reshape(-1))
+            call("nmg_weight_create", self.gt, self.in_features, self.out_features, ctypes.c_void_p(buf.ctypes.data), 0,
+                 self.device, ctypes.byref(h))
+        self._h = h
+
+    def __del__(self):
+        h = getattr(self, "_h", None)
+        if h is not None and h.value:
+            try:
+                _lib.lib().nmg_weight_destroy(h)
+            except Exception:
+                pass
+            self._h = None
+
+    @property
+    def handle(self):
+        return self._h
+
+    def type(self) -> int:
+        t = ctypes.c_int()
+        call("nmg_weight_info", self._h, ctypes.byref(t), None, None)
+        return t.value
+
+    def row_bytes(self) -> int:
+        return type_size_bytes(self.gt, self.in_features)
+
+    def _act(self) -> int:
+        return 1 if self.fp32_act else 0
+
+    def matvec(self, x: torch.Tensor, *, out: torch.Tensor | None = None) -> torch.Tensor:
+        """y[out] = W x for a device fp32 x[in] (src/quant_i8.hpp:351-428)."""
+        x = _dev(x).float().contiguous()
+        if x.numel() != self.in_features:
+            raise ValueError(f"matvec: {x.numel()} values for In={self.in_features}")
+        if out is None:
+            out = torch.empty(self.out_features, dtype=torch.float32, device=x.device)
+        call("nmg_weight_matvec", self._h, _ptr(x), _ptr(out), self._act(), _stream(x.device))
+        return out
+
+    def matmul(self, x: torch.Tensor, *, out: torch.Tensor | None = None) -> torch.Tensor:
+        """Y[rows][out] for device fp32 X[rows][in] (src/quant_i8.hpp:430-514)."""
+        x = _dev(x).float().contiguous()
+        if x.dim() != 2 or x.shape[1] != self.in_features:
+            raise ValueError(f"matmul: activations {tuple(x.shape)} for In={self.in_features}")
+        if out is None:
+            out = torch.empty(x.shape[0], self.out_features, dtype=torch.float32, device=x.device)
+        call("nmg_weight_matmul", self._h, int(x.shape[0]), _ptr(x), _ptr(out), self._act(), _stream(x.device))
+        return out
+
+    def gather_rows(self, rows) -> torch.Tensor:
+        """Rows dequantised to fp32 [len(rows)][in] (src/quant.hpp:469-475)."""
+        ids = np.ascontiguousarray(np.asarray(rows, dtype=np.int32).reshape(-1))
+        out = torch.empty(len(ids), self.in_features, dtype=torch.float32, device=f"cuda:{self.device}")
+        call("nmg_weight_gather_rows", self._h, ctypes.c_void_p(ids.ctypes.data), len(ids), _ptr(out),
+             _stream(self.device))
+        return out
+
+    def dequant_row(self, o: int) -> torch.Tensor:
+        return self.gather_rows([o])[0]
+
+
+def quantize_activations(x: torch.Tensor, act_type: int) -> torch.Tensor:
+    """quantize_row_q8_0 / quantize_row_q8_K of each row of device fp32 x
+    [rows][n]: the reference's packed blocks as a uint8 tensor [rows][bytes]."""
+    x = _dev(x).float().contiguous()
+    x2 = x.view(-1, x.shape[-1])
+    rb = type_size_bytes(act_type, x2.shape[1])
+    out = torch.empty(x2.shape[0], rb, dtype=torch.uint8, device=x.device)
+    call("nmg_quantize_activations", int(act_type), int(x2.shape[0]), int(x2.shape[1]), _ptr(x2), _ptr(out),
+         _stream(x.device))
     return out
 
 

@@ -389,6 +389,54 @@ NMG_API int nmg_attend_fanout(const nmg_kv_cache* cache, int hq, const void* q, 
                               int64_t first_query, float scale, int use_scale, void* const* outs, int nout,
                               int64_t out_row_elems, int64_t out_col0, int out_dtype, void* stream);
 
+/* ---- quantised projections (src/quant.hpp, src/quant_i8.hpp) ----------------
+ *
+ * Weight<In,Out> over GGUF tensors (quant.hpp:439-487): one row of `in`
+ * values per output, stored as GGUF blocks.  Type codes are GGUF's
+ * (quant.hpp:18-27).  F16 and BF16 rows are widened to fp32 at creation, as
+ * the reference's loader does; everything else stays in its block format. */
+#define NMG_GT_F32 0
+#define NMG_GT_F16 1
+#define NMG_GT_Q4_0 2
+#define NMG_GT_Q8_0 8
+#define NMG_GT_Q4_K 12
+#define NMG_GT_Q5_K 13
+#define NMG_GT_Q6_K 14
+#define NMG_GT_Q8_K 15 /* activation blocks only */
+#define NMG_GT_BF16 30
+/* Activation handling of a product: the reference's default (activations
+ * quantised to Q8_0 / Q8_K once per row and integer block dots, for Q8_0,
+ * Q4_0, Q4_K and Q6_K; fp32 otherwise) or its NM_FP32_ACT path (fp32
+ * activations against blocks dequantised inside the dot, every type). */
+#define NMG_ACT_DEFAULT 0
+#define NMG_ACT_FP32 1
+typedef struct nmg_weight nmg_weight;
+/* type_size_bytes (quant.hpp:89-108): bytes of one row of `in` values;
+ * NMG_INVALID_ARGUMENT for an unknown type or a row that is not whole blocks. */
+NMG_API int nmg_weight_row_bytes(int type, int64_t in, int64_t* bytes);
+/* The Weight(GT, data, keepalive) constructor (quant.hpp:456-460): `data`
+ * holds out * row_bytes GGUF bytes, on the host or (data_on_device != 0) on
+ * `device`; the weight keeps its own device copy.  NMG_UNSUPPORTED for fp32
+ * rows whose length is not a multiple of 4. */
+NMG_API int nmg_weight_create(int type, int64_t in, int64_t out, const void* data, int data_on_device, int device,
+                              nmg_weight** w);
+NMG_API int nmg_weight_destroy(nmg_weight* w);
+/* type() (F16/BF16 report NMG_GT_F32, as stored), In, Out. */
+NMG_API int nmg_weight_info(const nmg_weight* w, int* type, int64_t* in, int64_t* out);
+/* Weight::matvec (quant_i8.hpp:351-428): y[out] = W x, device fp32 x[in]
+ * (16-byte aligned) and y[out]. */
+NMG_API int nmg_weight_matvec(const nmg_weight* w, const float* x, float* y, int act, void* stream);
+/* Weight::matmul (quant_i8.hpp:430-514): y[rows][out] for x[rows][in]. */
+NMG_API int nmg_weight_matmul(const nmg_weight* w, int64_t rows, const float* x, float* y, int act, void* stream);
+/* Weight::gather_rows (quant.hpp:469-475): rows[0..n) (host indices, each
+ * < out, else NMG_OUT_OF_RANGE) dequantised to device fp32 out[n][in], bit
+ * for bit dequant_to_f32.  Returns once the indices were consumed. */
+NMG_API int nmg_weight_gather_rows(const nmg_weight* w, const int32_t* rows, int64_t n, float* out, void* stream);
+/* quantize_row_q8_0 / quantize_row_q8_K (quant_i8.hpp:38-81) of rows x n
+ * device fp32 values into the reference's packed blocks (34-byte block_q8_0,
+ * 292-byte block_q8_K) at device `blocks`. */
+NMG_API int nmg_quantize_activations(int act_type, int64_t rows, int64_t n, const float* x, void* blocks, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

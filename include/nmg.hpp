@@ -18,6 +18,7 @@
 #include <array>
 #include <cstddef>
 #include <cstdint>
+#include <cstdlib>
 #include <stdexcept>
 #include <string>
 #include <utility>
@@ -309,6 +310,62 @@ void scaled_dot_product_attention(const void* queries, const void* keys, const v
 // Waits for `stream` and throws std::runtime_error if a kernel since the last
 // call gave up a bounded device-side wait.
 inline void device_status(int device, void* stream) { check(nmg_device_status(device, stream)); }
+
+// GGUF tensor types (quant.hpp:18-27).
+enum class GT : uint32_t {
+    F32 = NMG_GT_F32,
+    F16 = NMG_GT_F16,
+    Q4_0 = NMG_GT_Q4_0,
+    Q8_0 = NMG_GT_Q8_0,
+    Q4_K = NMG_GT_Q4_K,
+    Q5_K = NMG_GT_Q5_K,
+    Q6_K = NMG_GT_Q6_K,
+    BF16 = NMG_GT_BF16,
+};
+
+inline size_t type_size_bytes(GT t, size_t nelem) {  // quant.hpp:89-108
+    int64_t b = 0;
+    check(nmg_weight_row_bytes(int(t), int64_t(nelem), &b));
+    return size_t(b);
+}
+
+// Weight<In,Out> (quant.hpp:439-487) with its GGUF bytes resident on the
+// device.  matvec / matmul take device fp32 activations and write device fp32
+// outputs; fp32_act selects the NM_FP32_ACT path (the default follows that
+// environment variable, as the reference reads it, quant_i8.hpp:343-349).
+template <size_t In, size_t Out>
+class Weight {
+public:
+    Weight(GT type, const void* host_data, int device = 0) : type_(type) {
+        check(nmg_weight_create(int(type), int64_t(In), int64_t(Out), host_data, 0, device, &h_));
+        const char* e = std::getenv("NM_FP32_ACT");
+        fp32_act_ = e && e[0] && e[0] != '0';
+    }
+    Weight(const Weight&) = delete;
+    Weight& operator=(const Weight&) = delete;
+    ~Weight() { nmg_weight_destroy(h_); }
+    GT type() const { return type_; }
+    size_t row_bytes() const { return type_size_bytes(type_, In); }
+    void set_fp32_act(bool on) { fp32_act_ = on; }
+    // y[Out] = W x
+    void matvec(const float* x, float* y, void* stream) const {
+        check(nmg_weight_matvec(h_, x, y, fp32_act_ ? NMG_ACT_FP32 : NMG_ACT_DEFAULT, stream));
+    }
+    // y[rows][Out] for x[rows][In]
+    void matmul(const float* x, size_t rows, float* y, void* stream) const {
+        check(nmg_weight_matmul(h_, int64_t(rows), x, y, fp32_act_ ? NMG_ACT_FP32 : NMG_ACT_DEFAULT, stream));
+    }
+    // rows dequantised to fp32 [rows.size()][In] on the device
+    void gather_rows(const std::vector<int32_t>& rows, float* out, void* stream) const {
+        check(nmg_weight_gather_rows(h_, rows.data(), int64_t(rows.size()), out, stream));
+    }
+    nmg_weight* handle() const { return h_; }
+
+private:
+    GT type_;
+    bool fp32_act_ = false;
+    nmg_weight* h_ = nullptr;
+};
 
 // gated_delta_step<Dk, Dv> (recurrent.hpp:146-177) on one device head block;
 // gate and beta are device scalars.

@@ -257,12 +257,14 @@ def test_golden_fixtures_exist():
 
 @needs_ref
 def test_golden_fixtures_reproduce_from_the_reference(tmp_path, capsys):
-    # The committed fixtures are what tests/golden/make_golden.py writes from
-    # the reference build today: rerun it into a scratch directory and compare.
-    src = open(os.path.join(GOLDEN, "make_golden.py")).read()
+    # The committed fixtures are what tests/golden/make_golden.py and
+    # make_quant_golden.py write from the reference build today: rerun them
+    # into a scratch directory and compare.
     scratch = tmp_path / "golden"
     scratch.mkdir()
-    exec(compile(src, "make_golden.py", "exec"), {"__file__": str(scratch / "make_golden.py"), "__name__": "__main__"})
+    for script in ("make_golden.py", "make_quant_golden.py"):
+        src = open(os.path.join(GOLDEN, script)).read()
+        exec(compile(src, script, "exec"), {"__file__": str(scratch / script), "__name__": "__main__"})
     committed = sorted(glob.glob(os.path.join(GOLDEN, "*.npz")))
     assert sorted(p.name for p in scratch.glob("*.npz")) == [os.path.basename(p) for p in committed]
     for p in committed:
