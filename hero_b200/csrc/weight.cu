@@ -73,11 +73,14 @@ bool has_i8(int t) { return t == GT_Q8_0 || t == GT_Q4_0 || t == GT_Q4_K || t ==
 
 // Device planes of one weight (row strides in bytes / elements).
 struct Planes {
-    const uint8_t* qs;   // quants / nibbles / low nibbles; F32: the fp32 rows
-    const uint8_t* hi;   // Q5_K high bits, Q6_K high pairs
-    const uint8_t* meta; // Q4_K/Q5_K d,dmin,scales; Q6_K int8 scales (16 B per superblock)
-    const uint16_t* d;   // Q8_0/Q4_0 block scales, Q6_K superblock d (fp16 bits)
-    int64_t qs_row, hi_row, meta_row, d_row;
+    const uint8_t* qs;    // quants / nibbles / low nibbles; F32: the fp32 rows
+    const uint8_t* hi;    // Q5_K high bits, Q6_K high pairs
+    const uint32_t* meta; // per superblock 4 words: Q4_K/Q5_K word g = the 6-bit scales and
+                          // mins of sub-blocks 2g, 2g+1 (sc lo, sc hi, m lo, m hi bytes);
+                          // Q6_K word 2h+k = the int8 scales 8h+k, 8h+2+k, 8h+4+k, 8h+6+k
+    const uint16_t* d;    // Q8_0/Q4_0 block scales, Q6_K superblock d (fp16 bits)
+    const uint32_t* dd;   // Q4_K/Q5_K superblock d | dmin << 16 (fp16 bits)
+    int64_t qs_row, hi_row, meta_row, d_row, dd_row;  // bytes / words / elements per row
 };
 
 }  // namespace
@@ -95,8 +98,8 @@ namespace {
 
 // ---- re-lay the GGUF blocks into planes (one thread per block) ------------
 __global__ void repack_kernel(const uint8_t* __restrict__ src, int type, int64_t out, int64_t nb, int64_t src_row,
-                              uint8_t* qs, uint8_t* hi, uint8_t* meta, uint16_t* dp, int64_t qs_row, int64_t hi_row,
-                              int64_t meta_row, int64_t d_row) {
+                              uint8_t* qs, uint8_t* hi, uint32_t* meta, uint16_t* dp, uint32_t* ddp, int64_t qs_row,
+                              int64_t hi_row, int64_t meta_row, int64_t d_row, int64_t dd_row) {
     const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
     if (i >= out * nb) return;
     const int64_t o = i / nb, b = i % nb;
@@ -112,18 +115,38 @@ __global__ void repack_kernel(const uint8_t* __restrict__ src, int type, int64_t
             for (int j = 0; j < 16; ++j) qs[o * qs_row + 16 * b + j] = s[2 + j];
             break;
         case GT_Q4_K:
-            for (int j = 0; j < 16; ++j) meta[o * meta_row + 16 * b + j] = s[j];
-            for (int j = 0; j < 128; ++j) qs[o * qs_row + 128 * b + j] = s[16 + j];
+        case GT_Q5_K: {
+            // get_scale_min_k4 (quant.hpp:154-162) once, at rest
+            const uint8_t* q = s + 4;
+            int sc[8], mn[8];
+            for (int j = 0; j < 8; ++j) {
+                if (j < 4) {
+                    sc[j] = q[j] & 63;
+                    mn[j] = q[j + 4] & 63;
+                } else {
+                    sc[j] = (q[j + 4] & 0xF) | ((q[j - 4] >> 6) << 4);
+                    mn[j] = (q[j + 4] >> 4) | ((q[j] >> 6) << 4);
+                }
+            }
+            for (int g = 0; g < 4; ++g)
+                meta[o * meta_row + 4 * b + g] = (uint32_t)sc[2 * g] | ((uint32_t)sc[2 * g + 1] << 8) |
+                                                 ((uint32_t)mn[2 * g] << 16) | ((uint32_t)mn[2 * g + 1] << 24);
+            ddp[o * dd_row + b] = (uint32_t)u16(0) | ((uint32_t)u16(2) << 16);
+            const int qoff = type == GT_Q5_K ? 48 : 16;
+            if (type == GT_Q5_K)
+                for (int j = 0; j < 32; ++j) hi[o * hi_row + 32 * b + j] = s[16 + j];
+            for (int j = 0; j < 128; ++j) qs[o * qs_row + 128 * b + j] = s[qoff + j];
             break;
-        case GT_Q5_K:
-            for (int j = 0; j < 16; ++j) meta[o * meta_row + 16 * b + j] = s[j];
-            for (int j = 0; j < 32; ++j) hi[o * hi_row + 32 * b + j] = s[16 + j];
-            for (int j = 0; j < 128; ++j) qs[o * qs_row + 128 * b + j] = s[48 + j];
-            break;
+        }
         case GT_Q6_K:
             for (int j = 0; j < 128; ++j) qs[o * qs_row + 128 * b + j] = s[j];
             for (int j = 0; j < 64; ++j) hi[o * hi_row + 64 * b + j] = s[128 + j];
-            for (int j = 0; j < 16; ++j) meta[o * meta_row + 16 * b + j] = s[192 + j];
+            for (int hk = 0; hk < 4; ++hk) {
+                const int h = hk >> 1, k = hk & 1;
+                uint32_t wv = 0;
+                for (int r = 0; r < 4; ++r) wv |= (uint32_t)s[192 + 8 * h + 2 * r + k] << (8 * r);
+                meta[o * meta_row + 4 * b + hk] = wv;
+            }
             dp[o * d_row + b] = u16(208);
             break;
     }
@@ -150,28 +173,21 @@ struct ActPlanes {
     int16_t* bsums;
 };
 
-// quantize_row_q8_0 (quant_i8.hpp:69-81): one warp per block of 32, a value
-// per lane.  d = amax / 127 and 1 / d are IEEE divisions; the scale is kept as
-// fp16 (core.hpp:61-79 rounding, f32_to_f16_bits); q = roundf(x * id).
-// `packed` (optional) receives the reference's 34-byte blocks.
-__global__ void act_q8_0_kernel(const float* __restrict__ x, int64_t blocks, ActPlanes a, uint8_t* packed) {
-    const int lane = threadIdx.x & 31;
-    const int64_t w0 = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
-    const int64_t nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
-    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-    for (int64_t b = w0; b < blocks; b += nw) {
-        const float v = x[b * 32 + lane];
-        const float amax = dev::warp_max(fabsf(v));
-        const float d = amax / 127.f;
-        const float id = d != 0.f ? 1.f / d : 0.f;
-        const uint16_t h = dev::f32_to_f16_bits(d);
-        const int8_t q = (int8_t)roundf(v * id);
-        a.qs[b * 32 + lane] = q;
-        if (lane == 0) a.d[b] = dev::f16_bits_to_f32(h);
-        if (packed) {
-            packed[b * 34 + 2 + lane] = (uint8_t)q;
-            if (lane < 2) packed[b * 34 + lane] = (uint8_t)(h >> (8 * lane));
-        }
+// quantize_row_q8_0 (quant_i8.hpp:69-81) of one block of 32 by one warp, a
+// value per lane.  d = amax / 127 and 1 / d are IEEE divisions; the scale is
+// kept as fp16 (core.hpp:61-79 rounding, f32_to_f16_bits); q = roundf(x * id).
+// `packed` (optional) receives the reference's 34-byte block.
+__device__ __forceinline__ void quant_block_q8_0(float v, int lane, int8_t* qs, float* d, uint8_t* packed) {
+    const float amax = dev::warp_max(fabsf(v));
+    const float dd = amax / 127.f;
+    const float id = dd != 0.f ? 1.f / dd : 0.f;
+    const uint16_t h = dev::f32_to_f16_bits(dd);
+    const int8_t q = (int8_t)roundf(v * id);
+    qs[lane] = q;
+    if (lane == 0) *d = dev::f16_bits_to_f32(h);
+    if (packed) {
+        packed[2 + lane] = (uint8_t)q;
+        if (lane < 2) packed[lane] = (uint8_t)(h >> (8 * lane));
     }
 }
 
@@ -184,10 +200,76 @@ __device__ __forceinline__ int nearest_int_fma(float iscale, float x) {
     return (__float_as_int(s) & 0x007fffff) - 0x00400000;
 }
 
-// quantize_row_q8_K (quant_i8.hpp:38-67): one warp per block of 256, eight
-// consecutive values per lane.  The value of largest magnitude is the first
-// one on ties (strict > in index order); iscale = -127 / max; q = min(127,
-// nearest(iscale * x)); d = 1 / iscale; bsums over 16-value groups.
+// quantize_row_q8_K (quant_i8.hpp:38-67) of one block of 256 by one warp,
+// eight consecutive values per lane.  The value of largest magnitude is the
+// first one on ties (strict > in index order); iscale = -127 / max; q =
+// min(127, nearest(iscale * x)); d = 1 / iscale; bsums over 16-value groups.
+__device__ __forceinline__ void quant_block_q8_k(float4 x0, float4 x1, int lane, int8_t* qs, float* d, int16_t* bsums,
+                                                 uint8_t* packed) {
+    const float v[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+    float amax = 0.f, mx = 0.f;
+    int idx = 1 << 30;
+    for (int i = 0; i < 8; ++i) {
+        const float ax = fabsf(v[i]);
+        if (ax > amax) {
+            amax = ax;
+            mx = v[i];
+            idx = 8 * lane + i;
+        }
+    }
+    for (int s = 16; s; s >>= 1) {
+        const float oa = __shfl_xor_sync(0xffffffffu, amax, s);
+        const float om = __shfl_xor_sync(0xffffffffu, mx, s);
+        const int oi = __shfl_xor_sync(0xffffffffu, idx, s);
+        if (oa > amax || (oa == amax && oi < idx)) {
+            amax = oa;
+            mx = om;
+            idx = oi;
+        }
+    }
+    int8_t q[8];
+    float dd = 0.f;
+    if (amax != 0.f) {
+        const float iscale = -127.f / mx;
+        for (int i = 0; i < 8; ++i) {
+            const int t = nearest_int_fma(iscale, v[i]);
+            q[i] = (int8_t)(t < 127 ? t : 127);
+        }
+        dd = 1.f / iscale;
+    } else {
+        for (int i = 0; i < 8; ++i) q[i] = 0;
+    }
+    int sum = 0;
+    for (int i = 0; i < 8; ++i) sum += q[i];
+    sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+    uint32_t lo = 0, hi = 0;
+    for (int i = 0; i < 4; ++i) {
+        lo |= (uint32_t)(uint8_t)q[i] << (8 * i);
+        hi |= (uint32_t)(uint8_t)q[4 + i] << (8 * i);
+    }
+    reinterpret_cast<uint2*>(qs)[lane] = make_uint2(lo, hi);
+    if (lane == 0) *d = dd;
+    if (!(lane & 1)) bsums[lane >> 1] = (int16_t)sum;
+    if (packed) {
+        for (int i = 0; i < 8; ++i) packed[4 + 8 * lane + i] = (uint8_t)q[i];
+        if (lane < 4) packed[lane] = (uint8_t)(__float_as_uint(dd) >> (8 * lane));
+        if (!(lane & 1)) {
+            packed[260 + lane] = (uint8_t)(sum & 0xFF);
+            packed[261 + lane] = (uint8_t)((sum >> 8) & 0xFF);
+        }
+    }
+}
+
+// Activation rows quantised to global planes: a warp per block.
+__global__ void act_q8_0_kernel(const float* __restrict__ x, int64_t blocks, ActPlanes a, uint8_t* packed) {
+    const int lane = threadIdx.x & 31;
+    const int64_t w0 = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+    const int64_t nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    for (int64_t b = w0; b < blocks; b += nw)
+        quant_block_q8_0(x[b * 32 + lane], lane, a.qs + b * 32, a.d + b, packed ? packed + b * 34 : nullptr);
+}
+
 __global__ void act_q8_k_kernel(const float* __restrict__ x, int64_t blocks, ActPlanes a, uint8_t* packed) {
     const int lane = threadIdx.x & 31;
     const int64_t w0 = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
@@ -195,60 +277,8 @@ __global__ void act_q8_k_kernel(const float* __restrict__ x, int64_t blocks, Act
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     for (int64_t b = w0; b < blocks; b += nw) {
         const float4* xp = reinterpret_cast<const float4*>(x + b * 256 + 8 * lane);
-        const float4 x0 = xp[0], x1 = xp[1];
-        const float v[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
-        float amax = 0.f, mx = 0.f;
-        int idx = 1 << 30;
-        for (int i = 0; i < 8; ++i) {
-            const float ax = fabsf(v[i]);
-            if (ax > amax) {
-                amax = ax;
-                mx = v[i];
-                idx = 8 * lane + i;
-            }
-        }
-        for (int s = 16; s; s >>= 1) {
-            const float oa = __shfl_xor_sync(0xffffffffu, amax, s);
-            const float om = __shfl_xor_sync(0xffffffffu, mx, s);
-            const int oi = __shfl_xor_sync(0xffffffffu, idx, s);
-            if (oa > amax || (oa == amax && oi < idx)) {
-                amax = oa;
-                mx = om;
-                idx = oi;
-            }
-        }
-        int8_t q[8];
-        float d = 0.f;
-        if (amax != 0.f) {
-            const float iscale = -127.f / mx;
-            for (int i = 0; i < 8; ++i) {
-                const int t = nearest_int_fma(iscale, v[i]);
-                q[i] = (int8_t)(t < 127 ? t : 127);
-            }
-            d = 1.f / iscale;
-        } else {
-            for (int i = 0; i < 8; ++i) q[i] = 0;
-        }
-        int sum = 0;
-        for (int i = 0; i < 8; ++i) sum += q[i];
-        sum += __shfl_xor_sync(0xffffffffu, sum, 1);
-        uint32_t lo = 0, hi = 0;
-        for (int i = 0; i < 4; ++i) {
-            lo |= (uint32_t)(uint8_t)q[i] << (8 * i);
-            hi |= (uint32_t)(uint8_t)q[4 + i] << (8 * i);
-        }
-        reinterpret_cast<uint2*>(a.qs + b * 256)[lane] = make_uint2(lo, hi);
-        if (lane == 0) a.d[b] = d;
-        if (!(lane & 1)) a.bsums[b * 16 + (lane >> 1)] = (int16_t)sum;
-        if (packed) {
-            uint8_t* pb = packed + b * 292;
-            for (int i = 0; i < 8; ++i) pb[4 + 8 * lane + i] = (uint8_t)q[i];
-            if (lane < 4) pb[lane] = (uint8_t)(__float_as_uint(d) >> (8 * lane));
-            if (!(lane & 1)) {
-                pb[260 + lane] = (uint8_t)(sum & 0xFF);
-                pb[261 + lane] = (uint8_t)((sum >> 8) & 0xFF);
-            }
-        }
+        quant_block_q8_k(xp[0], xp[1], lane, a.qs + b * 256, a.d + b, a.bsums + b * 16,
+                         packed ? packed + b * 292 : nullptr);
     }
 }
 
@@ -275,21 +305,6 @@ __device__ __forceinline__ uint4 ld16_stream(const void* p) {
 }
 __device__ __forceinline__ float h2f(uint32_t bits) { return dev::f16_bits_to_f32(bits & 0xFFFF); }
 
-// (scale, min) pair j of a K-quant superblock from its 12 scale bytes, held in
-// the words s1..s3 (bytes 4..15 of the superblock header): get_scale_min_k4
-// (quant.hpp:154-162).
-__device__ __forceinline__ void k4_scale_min(const uint4& meta, int j, int& sc, int& m) {
-    const uint32_t w[3] = {meta.y, meta.z, meta.w};
-    auto byte = [&](int i) { return (int)((w[i >> 2] >> (8 * (i & 3))) & 0xFF); };
-    if (j < 4) {
-        sc = byte(j) & 63;
-        m = byte(j + 4) & 63;
-    } else {
-        sc = (byte(j + 4) & 0xF) | ((byte(j - 4) >> 6) << 4);
-        m = (byte(j + 4) >> 4) | ((byte(j) >> 6) << 4);
-    }
-}
-
 // Chunks: the unit one lane takes per step.  Q8_0 16 values (16 B), Q4_0 a
 // block of 32 (16 B of nibbles), Q4_K/Q5_K 32 values (16 B of nibbles: 16 of
 // sub-block 2g, 16 of 2g+1), Q6_K 64 values (16 B from each half of the low
@@ -301,8 +316,8 @@ __host__ __device__ constexpr int chunk_values() {
 
 template <int TYPE>
 struct WChunk {
-    uint4 q, q2, h, m;
-    uint32_t d;
+    uint4 q, q2, h;
+    uint32_t m, d;  // the lane's scale word and block scale(s)
 };
 
 template <int TYPE>
@@ -313,7 +328,8 @@ __device__ __forceinline__ WChunk<TYPE> load_chunk(const Planes& P, int64_t o, i
         w.d = P.d[o * P.d_row + (TYPE == GT_Q8_0 ? (c >> 1) : c)];
     } else if constexpr (TYPE == GT_Q4_K || TYPE == GT_Q5_K) {
         w.q = ld16_stream(P.qs + o * P.qs_row + 16 * c);
-        w.m = ld16(P.meta + o * P.meta_row + 16 * (c >> 3));
+        w.m = P.meta[o * P.meta_row + 4 * (c >> 3) + ((c >> 1) & 3)];
+        w.d = P.dd[o * P.dd_row + (c >> 3)];
         if constexpr (TYPE == GT_Q5_K) w.h = ld16_stream(P.hi + o * P.hi_row + 32 * (c >> 3) + 16 * (c & 1));
     } else if constexpr (TYPE == GT_Q6_K) {
         const int64_t sb = c >> 2, h = (c >> 1) & 1, k = c & 1;
@@ -321,7 +337,7 @@ __device__ __forceinline__ WChunk<TYPE> load_chunk(const Planes& P, int64_t o, i
         w.q = ld16_stream(ql);
         w.q2 = ld16_stream(ql + 32);
         w.h = ld16_stream(P.hi + o * P.hi_row + 64 * sb + 32 * h + 16 * k);
-        w.m = ld16(P.meta + o * P.meta_row + 16 * sb);
+        w.m = P.meta[o * P.meta_row + 4 * sb + (c & 3)];
         w.d = P.d[o * P.d_row + sb];
     } else {
         w.q = ld16_stream(P.qs + o * P.qs_row + 16 * c);
@@ -369,10 +385,8 @@ __device__ __forceinline__ void i8_chunk(const WChunk<TYPE>& w, int64_t c, const
         const int64_t sb = c >> 3;
         const int g = (int)((c >> 1) & 3), h = (int)(c & 1);
         const int64_t e0 = 256 * sb + 64 * g + 16 * h;
-        int sc1, m1, sc2, m2;
-        k4_scale_min(w.m, 2 * g, sc1, m1);
-        k4_scale_min(w.m, 2 * g + 1, sc2, m2);
-        const float dd = h2f(w.m.x), dm = h2f(w.m.x >> 16);
+        const int sc1 = w.m & 0xFF, sc2 = (w.m >> 8) & 0xFF, m1 = (w.m >> 16) & 0xFF, m2 = w.m >> 24;
+        const float dd = h2f(w.d), dm = h2f(w.d >> 16);
         const uint32_t lo[4] = {w.q.x & 0x0F0F0F0Fu, w.q.y & 0x0F0F0F0Fu, w.q.z & 0x0F0F0F0Fu, w.q.w & 0x0F0F0F0Fu};
         const uint32_t hi[4] = {(w.q.x >> 4) & 0x0F0F0F0Fu, (w.q.y >> 4) & 0x0F0F0F0Fu, (w.q.z >> 4) & 0x0F0F0F0Fu,
                                 (w.q.w >> 4) & 0x0F0F0F0Fu};
@@ -399,13 +413,9 @@ __device__ __forceinline__ void i8_chunk(const WChunk<TYPE>& w, int64_t c, const
             u[2][i] = ((qa[i] >> 4) & 0x0F0F0F0Fu) | (qh[i] & 0x30303030u);
             u[3][i] = ((qb[i] >> 4) & 0x0F0F0F0Fu) | ((qh[i] >> 2) & 0x30303030u);
         }
-        const uint32_t scw[4] = {w.m.x, w.m.y, w.m.z, w.m.w};
         int sc[4];
 #pragma unroll
-        for (int r = 0; r < 4; ++r) {
-            const int j = 8 * h + 2 * r + k;
-            sc[r] = (int)(int8_t)((scw[j >> 2] >> (8 * (j & 3))) & 0xFF);
-        }
+        for (int r = 0; r < 4; ++r) sc[r] = (int)(int8_t)((w.m >> (8 * r)) & 0xFF);
         const float dw = h2f(w.d);
         const int64_t e0 = 256 * sb + 128 * h + 16 * k;
 #pragma unroll
@@ -451,10 +461,8 @@ __device__ __forceinline__ int64_t dequant_chunk(const WChunk<TYPE>& w, int64_t 
         const int64_t sb = c >> 3;
         const int g = (int)((c >> 1) & 3), h = (int)(c & 1);
         e0 = 256 * sb + 64 * g + 16 * h;
-        int sc1, m1, sc2, m2;
-        k4_scale_min(w.m, 2 * g, sc1, m1);
-        k4_scale_min(w.m, 2 * g + 1, sc2, m2);
-        const float dd = h2f(w.m.x), dm = h2f(w.m.x >> 16);
+        const int sc1 = w.m & 0xFF, sc2 = (w.m >> 8) & 0xFF, m1 = (w.m >> 16) & 0xFF, m2 = w.m >> 24;
+        const float dd = h2f(w.d), dm = h2f(w.d >> 16);
         const float d1 = dd * (float)sc1, f1 = dm * (float)m1, d2 = dd * (float)sc2, f2 = dm * (float)m2;
         const uint32_t q[4] = {w.q.x, w.q.y, w.q.z, w.q.w};
         const uint32_t hb[4] = {w.h.x, w.h.y, w.h.z, w.h.w};
@@ -476,12 +484,10 @@ __device__ __forceinline__ int64_t dequant_chunk(const WChunk<TYPE>& w, int64_t 
         e0 = 256 * sb + 128 * h + 16 * k;
         const uint32_t qa[4] = {w.q.x, w.q.y, w.q.z, w.q.w}, qb[4] = {w.q2.x, w.q2.y, w.q2.z, w.q2.w};
         const uint32_t qh[4] = {w.h.x, w.h.y, w.h.z, w.h.w};
-        const uint32_t scw[4] = {w.m.x, w.m.y, w.m.z, w.m.w};
         const float dw = h2f(w.d);
 #pragma unroll
         for (int r = 0; r < 4; ++r) {
-            const int j = 8 * h + 2 * r + k;
-            const float ds = dw * (float)(int8_t)((scw[j >> 2] >> (8 * (j & 3))) & 0xFF);
+            const float ds = dw * (float)(int8_t)((w.m >> (8 * r)) & 0xFF);
 #pragma unroll
             for (int i = 0; i < 16; ++i) {
                 const uint32_t lw = (r & 1) ? qb[i >> 2] : qa[i >> 2];
@@ -527,49 +533,127 @@ __device__ __forceinline__ void f32_chunk(const WChunk<TYPE>& w, int64_t c, cons
     }
 }
 
-// One warp per output row streams the row's chunks (lane-consecutive 16-byte
-// loads, U chunks per lane in flight); the first loads are issued before
-// griddepcontrol.wait, so under a programmatic launch they overlap the
-// activation quantiser.  Up to T activation rows reuse every loaded chunk.
+// Persistent product kernel.  Warp w of CTA b takes output rows
+// o = b * 8 + w + k * (8 * gridDim.x) and streams each row in groups of 32 * U
+// chunks (lane-consecutive 16-byte loads); the group stream runs on across
+// the warp's rows with a register double buffer, so the next group's loads
+// (of this row or the next) are in flight while the current one is reduced.
+// The first group is requested before griddepcontrol.wait: under a
+// programmatic launch the weight stream starts while the previous kernel
+// finishes.  Up to T activation rows reuse every loaded chunk.  With FUSE the
+// CTA quantises its activation rows into shared memory itself (no separate
+// quantiser launch); otherwise they come quantised from global planes.
 constexpr int kMvWarps = 8;
 
 template <int TYPE, int T, bool I8>
-__global__ void __launch_bounds__(kMvWarps * 32) mv_kernel(MvArgs a) {
-    constexpr int U = (TYPE == GT_Q6_K || T >= 4) ? (T >= 8 ? 1 : 2) : 4;
+__host__ __device__ constexpr int mv_unroll() {
+    return (T >= 8 || (!I8 && TYPE == GT_Q6_K && T > 1)) ? 1 : (T >= 4 || TYPE == GT_Q6_K || TYPE == GT_Q5_K) ? 2 : 4;
+}
+
+template <int TYPE>
+__host__ __device__ constexpr int act_block() {
+    return (TYPE == GT_Q4_K || TYPE == GT_Q6_K) ? 256 : 32;
+}
+
+__host__ __device__ constexpr int64_t align16(int64_t v) { return (v + 15) & ~int64_t(15); }
+
+// Shared-memory bytes of `rows` quantised activation rows of `in` values.
+template <int TYPE>
+__host__ __device__ constexpr int64_t fused_act_bytes(int rows, int64_t in) {
+    return align16(rows * in) + align16(4 * rows * (in / act_block<TYPE>())) +
+           (act_block<TYPE>() == 256 ? align16(2 * rows * (in / 16)) : 0);
+}
+
+template <int TYPE, int T, bool I8, bool FUSE>
+__global__ void __launch_bounds__(kMvWarps * 32, (TYPE == GT_Q6_K || TYPE == GT_Q5_K || T > 1) ? 2 : 3)
+    mv_kernel(MvArgs a) {
+    constexpr int U = mv_unroll<TYPE, T, I8>();
+    extern __shared__ __align__(16) uint8_t act_smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int64_t o = (int64_t)blockIdx.x * kMvWarps + warp;
-    const bool live = o < a.out;
-    const int64_t nch = a.in / chunk_values<TYPE>();
+    const int nch = (int)(a.in / chunk_values<TYPE>());
+    const int G = (nch + 32 * U - 1) / (32 * U);
+    const int64_t stride = (int64_t)gridDim.x * kMvWarps;
+    const int64_t o0 = (int64_t)blockIdx.x * kMvWarps + warp;
+    const int nrows = o0 < a.out ? (int)((a.out - o0 + stride - 1) / stride) : 0;
+    WChunk<TYPE> w[U], wn[U];
+    auto load_group = [&](int row, int grp, WChunk<TYPE>(&dst)[U]) {
+        const int64_t o = o0 + row * stride;
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int c = grp * (32 * U) + lane + 32 * u;
+            if (c < nch) dst[u] = load_chunk<TYPE>(a.w, o, c);
+        }
+    };
+    if (nrows > 0) load_group(0, 0, w);
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    // the next kernel may be scheduled as this one's CTAs retire; it still
+    // waits for all of this grid before reading what it wrote
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    MvArgs b = a;
+    if constexpr (FUSE) {
+        constexpr int BL = act_block<TYPE>();
+        int8_t* qs = (int8_t*)act_smem;
+        float* d = (float*)(act_smem + align16(T * a.in));
+        int16_t* bs = (int16_t*)(act_smem + align16(T * a.in) + align16(4 * T * (a.in / BL)));
+        // each warp takes NB consecutive blocks per step with all their loads
+        // issued before the first reduction (the loads are L2 round trips)
+        const int blocks = (int)(a.rows * (a.in / BL));
+        constexpr int NB = BL == 256 ? 4 : 8;
+        for (int b0 = warp * NB; b0 < blocks; b0 += kMvWarps * NB) {
+            if constexpr (BL == 256) {
+                float4 xv[NB][2];
+#pragma unroll
+                for (int k = 0; k < NB; ++k)
+                    if (b0 + k < blocks) {
+                        const float4* xp = reinterpret_cast<const float4*>(a.x + (int64_t)(b0 + k) * 256 + 8 * lane);
+                        xv[k][0] = xp[0], xv[k][1] = xp[1];
+                    }
+#pragma unroll
+                for (int k = 0; k < NB; ++k)
+                    if (b0 + k < blocks)
+                        quant_block_q8_k(xv[k][0], xv[k][1], lane, qs + (b0 + k) * 256, d + b0 + k, bs + (b0 + k) * 16,
+                                         nullptr);
+            } else {
+                float xv[NB];
+#pragma unroll
+                for (int k = 0; k < NB; ++k)
+                    if (b0 + k < blocks) xv[k] = a.x[(int64_t)(b0 + k) * 32 + lane];
+#pragma unroll
+                for (int k = 0; k < NB; ++k)
+                    if (b0 + k < blocks) quant_block_q8_0(xv[k], lane, qs + (b0 + k) * 32, d + b0 + k, nullptr);
+            }
+        }
+        __syncthreads();
+        b.aq = qs, b.ad = d, b.ab = bs;
+    }
     float acc[T];
 #pragma unroll
     for (int t = 0; t < T; ++t) acc[t] = 0.f;
-    bool waited = false;
-    for (int64_t c0 = 0; c0 < nch; c0 += 32 * U) {
-        WChunk<TYPE> w[U];
+    int row = 0, grp = 0;
+    while (row < nrows) {
+        int nrow = row, ngrp = grp + 1;
+        if (ngrp == G) ngrp = 0, ++nrow;
+        if (nrow < nrows) load_group(nrow, ngrp, wn);
 #pragma unroll
         for (int u = 0; u < U; ++u) {
-            const int64_t c = c0 + lane + 32 * u;
-            if (live && c < nch) w[u] = load_chunk<TYPE>(a.w, o, c);
-        }
-        if (!waited) {
-            asm volatile("griddepcontrol.wait;" ::: "memory");
-            waited = true;
-        }
-#pragma unroll
-        for (int u = 0; u < U; ++u) {
-            const int64_t c = c0 + lane + 32 * u;
-            if (live && c < nch) {
-                if constexpr (I8) i8_chunk<TYPE, T>(w[u], c, a, acc);
-                else f32_chunk<TYPE, T>(w[u], c, a, acc);
+            const int c = grp * (32 * U) + lane + 32 * u;
+            if (c < nch) {
+                if constexpr (I8) i8_chunk<TYPE, T>(w[u], c, b, acc);
+                else f32_chunk<TYPE, T>(w[u], c, b, acc);
             }
         }
-    }
-    if (!waited) asm volatile("griddepcontrol.wait;" ::: "memory");
-    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+        if (ngrp == 0) {
+            const int64_t o = o0 + row * stride;
 #pragma unroll
-    for (int t = 0; t < T; ++t) {
-        const float s = dev::warp_sum(acc[t]);
-        if (live && lane == 0 && t < a.rows) a.y[t * a.out + o] = s;
+            for (int t = 0; t < T; ++t) {
+                const float sum = dev::warp_sum(acc[t]);
+                if (lane == 0 && t < a.rows) a.y[t * a.out + o] = sum;
+                acc[t] = 0.f;
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) w[u] = wn[u];
+        row = nrow, grp = ngrp;
     }
 }
 
@@ -591,29 +675,77 @@ __global__ void dequant_rows_kernel(Planes P, int64_t in, const int32_t* __restr
 
 #define NMG_WEIGHT_TYPES(X) X(GT_F32) X(GT_Q8_0) X(GT_Q4_0) X(GT_Q4_K) X(GT_Q5_K) X(GT_Q6_K)
 
-template <int TYPE, int T>
-cudaError_t launch_mv_t(const MvArgs& a, bool i8, cudaStream_t st) {
+int sm_count() {
+    static int n = 0;
+    if (!n) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        if (n <= 0) n = 148;
+    }
+    return n;
+}
+
+template <int TYPE, int T, bool I8, bool FUSE>
+cudaError_t launch_mv_k(const MvArgs& a, cudaStream_t st) {
+    auto kern = mv_kernel<TYPE, T, I8, FUSE>;
+    const int smem = FUSE ? (int)fused_act_bytes<TYPE>(T, a.in) : 0;
+    static int cached_smem = -1, cached_blocks = 0;  // per instantiation
+    if (cached_smem != smem) {
+        int nb = 0;
+        cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, kern, kMvWarps * 32, smem);
+        if (e != cudaSuccess) return e;
+        cached_blocks = nb > 0 ? nb : 1;
+        cached_smem = smem;
+    }
+    const int64_t want = (a.out + kMvWarps - 1) / kMvWarps;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)((a.out + kMvWarps - 1) / kMvWarps));
+    cfg.gridDim = dim3((unsigned)std::min<int64_t>(want, (int64_t)cached_blocks * sm_count()));
     cfg.blockDim = dim3(kMvWarps * 32);
+    cfg.dynamicSmemBytes = (size_t)smem;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, a);
+}
+
+// Activation rows quantised inside every CTA: Q8_K rows (one warp reduction
+// per 256 values) of at most 4096 values, one or two rows.  Longer rows, and
+// Q8_0's reduction per 32 values, cost every CTA more up front than the
+// separate quantiser launch does.
+template <int TYPE>
+bool fuse_activations(int rows, int64_t in) {
+    return act_block<TYPE>() == 256 && rows <= 2 && in <= 4096;
+}
+
+template <int TYPE, int T>
+cudaError_t launch_mv_t(const MvArgs& a, bool i8, bool fuse, cudaStream_t st) {
     if constexpr (TYPE == GT_Q8_0 || TYPE == GT_Q4_0 || TYPE == GT_Q4_K || TYPE == GT_Q6_K) {
-        if (i8) return cudaLaunchKernelEx(&cfg, mv_kernel<TYPE, T, true>, a);
+        if (i8) {
+            if constexpr (T <= 2) {
+                if (fuse) return launch_mv_k<TYPE, T, true, true>(a, st);
+            }
+            return launch_mv_k<TYPE, T, true, false>(a, st);
+        }
     }
-    return cudaLaunchKernelEx(&cfg, mv_kernel<TYPE, T, false>, a);
+    return launch_mv_k<TYPE, T, false, false>(a, st);
 }
 
 template <int TYPE>
 cudaError_t launch_mv(const MvArgs& a, bool i8, cudaStream_t st) {
-    if (a.rows <= 1) return launch_mv_t<TYPE, 1>(a, i8, st);
-    if (a.rows <= 2) return launch_mv_t<TYPE, 2>(a, i8, st);
-    if (a.rows <= 4) return launch_mv_t<TYPE, 4>(a, i8, st);
-    return launch_mv_t<TYPE, 8>(a, i8, st);
+    const bool fuse = i8 && fuse_activations<TYPE>(a.rows, a.in);
+    if (a.rows <= 1) return launch_mv_t<TYPE, 1>(a, i8, fuse, st);
+    if (a.rows <= 2) return launch_mv_t<TYPE, 2>(a, i8, fuse, st);
+    if (a.rows <= 4) return launch_mv_t<TYPE, 4>(a, i8, false, st);
+    return launch_mv_t<TYPE, 8>(a, i8, false, st);
+}
+
+template <int TYPE>
+bool fuses(int64_t rows, int64_t in, bool i8) {
+    return i8 && rows <= 2 && fuse_activations<TYPE>((int)rows, in);
 }
 
 }  // namespace
@@ -675,17 +807,18 @@ extern "C" int nmg_weight_create(int type, int64_t in, int64_t out, const void* 
     w->out = out;
     w->device = device;
     // plane sizes (bytes per row)
-    int64_t qs_row = 0, hi_row = 0, meta_row = 0, d_row = 0;
+    int64_t qs_row = 0, hi_row = 0, meta_row = 0, d_row = 0, dd_row = 0;
     switch (w->type) {
         case GT_F32: qs_row = 4 * in; break;
         case GT_Q8_0: qs_row = in, d_row = in / 32; break;
         case GT_Q4_0: qs_row = in / 2, d_row = in / 32; break;
-        case GT_Q4_K: qs_row = in / 2, meta_row = in / 16; break;
-        case GT_Q5_K: qs_row = in / 2, hi_row = in / 8, meta_row = in / 16; break;
-        case GT_Q6_K: qs_row = in / 2, hi_row = in / 4, meta_row = in / 16, d_row = in / 256; break;
+        case GT_Q4_K: qs_row = in / 2, meta_row = in / 64, dd_row = in / 256; break;
+        case GT_Q5_K: qs_row = in / 2, hi_row = in / 8, meta_row = in / 64, dd_row = in / 256; break;
+        case GT_Q6_K: qs_row = in / 2, hi_row = in / 4, meta_row = in / 64, d_row = in / 256; break;
     }
     const size_t o_qs = 0, o_hi = align256(o_qs + (size_t)(qs_row * out)), o_meta = align256(o_hi + (size_t)(hi_row * out)),
-                 o_d = align256(o_meta + (size_t)(meta_row * out)), total = align256(o_d + (size_t)(2 * d_row * out));
+                 o_d = align256(o_meta + (size_t)(4 * meta_row * out)), o_dd = align256(o_d + (size_t)(2 * d_row * out)),
+                 total = align256(o_dd + (size_t)(4 * dd_row * out));
     DeviceGuard g(device);
     cudaError_t e = g.ok ? cudaSuccess : cudaErrorInvalidDevice;
     if (e == cudaSuccess) e = cudaMalloc(&w->base, total);
@@ -698,16 +831,17 @@ extern "C" int nmg_weight_create(int type, int64_t in, int64_t out, const void* 
     }
     if (e == cudaSuccess) {
         uint8_t* b = (uint8_t*)w->base;
-        w->p.qs = b + o_qs, w->p.hi = b + o_hi, w->p.meta = b + o_meta, w->p.d = (const uint16_t*)(b + o_d);
-        w->p.qs_row = qs_row, w->p.hi_row = hi_row, w->p.meta_row = meta_row, w->p.d_row = d_row;
+        w->p.qs = b + o_qs, w->p.hi = b + o_hi, w->p.meta = (const uint32_t*)(b + o_meta);
+        w->p.d = (const uint16_t*)(b + o_d), w->p.dd = (const uint32_t*)(b + o_dd);
+        w->p.qs_row = qs_row, w->p.hi_row = hi_row, w->p.meta_row = meta_row, w->p.d_row = d_row, w->p.dd_row = dd_row;
         if (wide) {
             const int64_t n = in * out;
             widen_kernel<<<(unsigned)((n + 255) / 256), 256>>>(src, type, n, (float*)b);
         } else {
             const int64_t nb = in / block_len(type), jobs = nb * out;
-            repack_kernel<<<(unsigned)((jobs + 255) / 256), 256>>>(src, type, out, nb, src_row, b + o_qs, b + o_hi,
-                                                                   b + o_meta, (uint16_t*)(b + o_d), qs_row, hi_row,
-                                                                   meta_row, d_row);
+            repack_kernel<<<(unsigned)((jobs + 255) / 256), 256>>>(
+                src, type, out, nb, src_row, b + o_qs, b + o_hi, (uint32_t*)(b + o_meta), (uint16_t*)(b + o_d),
+                (uint32_t*)(b + o_dd), qs_row, hi_row, meta_row, d_row, dd_row);
         }
         e = cudaGetLastError();
         if (e == cudaSuccess) e = cudaDeviceSynchronize();
@@ -784,7 +918,12 @@ extern "C" int nmg_weight_matmul(const nmg_weight* w, int64_t rows, const float*
     a.w = w->p;
     a.in = w->in;
     a.out = w->out;
-    if (i8) {
+    bool fused = false;
+#define NMG_FUSES(T) \
+    if (w->type == T) fused = fuses<T>(rows, w->in, i8);
+    NMG_WEIGHT_TYPES(NMG_FUSES)
+#undef NMG_FUSES
+    if (i8 && !fused) {
         const int atype = (w->type == GT_Q4_K || w->type == GT_Q6_K) ? GT_Q8_K : GT_Q8_0;
         ActPlanes ap;
         if (int rc = act_planes(w->device, atype, rows, w->in, &ap)) return rc;
@@ -797,7 +936,7 @@ extern "C" int nmg_weight_matmul(const nmg_weight* w, int64_t rows, const float*
         b.rows = (int)std::min<int64_t>(8, rows - r0);
         b.x = x + r0 * w->in;
         b.y = y + r0 * w->out;
-        if (i8) {
+        if (i8 && !fused) {
             b.aq = a.aq + r0 * w->in;
             b.ad = a.ad + r0 * (w->in / bl);
             if (a.ab) b.ab = a.ab + r0 * (w->in / 16);
