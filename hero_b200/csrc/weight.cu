@@ -32,69 +32,11 @@
 
 #include <algorithm>
 
-#include "common.cuh"
+#include "weight.cuh"
 
 namespace nmg {
 namespace {
-
-enum : int { GT_F32 = 0, GT_F16 = 1, GT_Q4_0 = 2, GT_Q8_0 = 8, GT_Q4_K = 12, GT_Q5_K = 13, GT_Q6_K = 14, GT_Q8_K = 15, GT_BF16 = 30 };
-
-__host__ __device__ int block_len(int t) {
-    switch (t) {
-        case GT_F32:
-        case GT_F16:
-        case GT_BF16: return 1;
-        case GT_Q4_0:
-        case GT_Q8_0: return 32;
-        case GT_Q4_K:
-        case GT_Q5_K:
-        case GT_Q6_K:
-        case GT_Q8_K: return 256;
-    }
-    return 0;
-}
-
-__host__ __device__ int block_bytes(int t) {
-    switch (t) {
-        case GT_F32: return 4;
-        case GT_F16:
-        case GT_BF16: return 2;
-        case GT_Q4_0: return 18;
-        case GT_Q8_0: return 34;
-        case GT_Q4_K: return 144;
-        case GT_Q5_K: return 176;
-        case GT_Q6_K: return 210;
-        case GT_Q8_K: return 292;
-    }
-    return 0;
-}
-
-bool has_i8(int t) { return t == GT_Q8_0 || t == GT_Q4_0 || t == GT_Q4_K || t == GT_Q6_K; }
-
-// Device planes of one weight (row strides in bytes / elements).
-struct Planes {
-    const uint8_t* qs;    // quants / nibbles / low nibbles; F32: the fp32 rows
-    const uint8_t* hi;    // Q5_K high bits, Q6_K high pairs
-    const uint32_t* meta; // per superblock 4 words: Q4_K/Q5_K word g = the 6-bit scales and
-                          // mins of sub-blocks 2g, 2g+1 (sc lo, sc hi, m lo, m hi bytes);
-                          // Q6_K word 2h+k = the int8 scales 8h+k, 8h+2+k, 8h+4+k, 8h+6+k
-    const uint16_t* d;    // Q8_0/Q4_0 block scales, Q6_K superblock d (fp16 bits)
-    const uint32_t* dd;   // Q4_K/Q5_K superblock d | dmin << 16 (fp16 bits)
-    int64_t qs_row, hi_row, meta_row, d_row, dd_row;  // bytes / words / elements per row
-};
-
-}  // namespace
-}  // namespace nmg
-
-struct nmg_weight {
-    int type = 0, device = 0;
-    int64_t in = 0, out = 0;
-    void* base = nullptr;
-    nmg::Planes p{};
-};
-
-namespace nmg {
-namespace {
+using namespace wq;
 
 // ---- re-lay the GGUF blocks into planes (one thread per block) ------------
 __global__ void repack_kernel(const uint8_t* __restrict__ src, int type, int64_t out, int64_t nb, int64_t src_row,
@@ -163,16 +105,6 @@ __global__ void widen_kernel(const uint8_t* __restrict__ src, int type, int64_t 
 }
 
 // ---- activation quantisers ------------------------------------------------
-// Device form of a quantised activation row: int8 quants [rows][in], the fp32
-// value of each block's scale [rows][in/block] (the fp16-rounded d for Q8_0,
-// as its dot reads it back; the fp32 d for Q8_K), and for Q8_K the int16 sums
-// of each 16 quants [rows][in/16].
-struct ActPlanes {
-    int8_t* qs;
-    float* d;
-    int16_t* bsums;
-};
-
 // quantize_row_q8_0 (quant_i8.hpp:69-81) of one block of 32 by one warp, a
 // value per lane.  d = amax / 127 and 1 / d are IEEE divisions; the scale is
 // kept as fp16 (core.hpp:61-79 rounding, f32_to_f16_bits); q = roundf(x * id).
@@ -757,6 +689,7 @@ int weight_act_scratch(int device, size_t bytes, void** ptr);
 }  // namespace nmg
 
 using namespace nmg;
+using namespace nmg::wq;
 
 namespace {
 
@@ -874,16 +807,19 @@ extern "C" int nmg_weight_info(const nmg_weight* w, int* type, int64_t* in, int6
 
 namespace {
 
-// Quantised activation planes for `rows` rows in the product scratch.
-int act_planes(int device, int atype, int64_t rows, int64_t in, ActPlanes* ap) {
+// Quantised activation planes for `rows` rows in the product scratch, plus
+// `extra` bytes after them (returned in *extra_ptr).
+int act_planes(int device, int atype, int64_t rows, int64_t in, ActPlanes* ap, size_t extra = 0,
+               void** extra_ptr = nullptr) {
     const int bl = atype == GT_Q8_K ? 256 : 32;
     const size_t qs = align256((size_t)(rows * in)), ds = align256((size_t)(rows * (in / bl) * 4)),
                  bs = atype == GT_Q8_K ? align256((size_t)(rows * (in / 16) * 2)) : 0;
     void* p = nullptr;
-    if (int rc = weight_act_scratch(device, qs + ds + bs, &p)) return rc;
+    if (int rc = weight_act_scratch(device, qs + ds + bs + extra, &p)) return rc;
     ap->qs = (int8_t*)p;
     ap->d = (float*)((uint8_t*)p + qs);
     ap->bsums = atype == GT_Q8_K ? (int16_t*)((uint8_t*)p + qs + ds) : nullptr;
+    if (extra_ptr) *extra_ptr = (uint8_t*)p + qs + ds + bs;
     return NMG_OK;
 }
 
@@ -923,14 +859,25 @@ extern "C" int nmg_weight_matmul(const nmg_weight* w, int64_t rows, const float*
     if (w->type == T) fused = fuses<T>(rows, w->in, i8);
     NMG_WEIGHT_TYPES(NMG_FUSES)
 #undef NMG_FUSES
+    const bool mm = i8 && rows > 8 && mm_supported(w->type);
+    const int splits = mm ? mm_splits(w, rows) : 1;
+    void* part = nullptr;
     if (i8 && !fused) {
         const int atype = (w->type == GT_Q4_K || w->type == GT_Q6_K) ? GT_Q8_K : GT_Q8_0;
         ActPlanes ap;
-        if (int rc = act_planes(w->device, atype, rows, w->in, &ap)) return rc;
+        const size_t extra = splits > 1 ? (size_t)splits * rows * w->out * 4 : 0;
+        if (int rc = act_planes(w->device, atype, rows, w->in, &ap, extra, &part)) return rc;
         NMG_CUDA_TRY(launch_act(atype, x, rows, w->in, ap, nullptr, st));
         a.aq = ap.qs, a.ad = ap.d, a.ab = ap.bsums;
     }
     const int bl = (w->type == GT_Q4_K || w->type == GT_Q6_K) ? 256 : 32;
+    if (mm) {
+        // long batches: int8 tensor-core tiles over the quantised activations
+        ActPlanes ap = {const_cast<int8_t*>(a.aq), const_cast<float*>(a.ad), const_cast<int16_t*>(a.ab)};
+        cudaError_t e = launch_mm(w, rows, ap, (float*)part, y, st);
+        if (e != cudaSuccess) return set_error(NMG_CUDA_ERROR, "nmg_weight_matmul: %s", cudaGetErrorString(e));
+        return NMG_OK;
+    }
     for (int64_t r0 = 0; r0 < rows; r0 += 8) {
         MvArgs b = a;
         b.rows = (int)std::min<int64_t>(8, rows - r0);

@@ -87,6 +87,19 @@ def test_products_match_the_oracle(dev, t, rows):
     assert_close(got32, Q.matmul(t, w, x, fp32_act=True, threads=8), what=f"{Q.NAMES.get(t)} fp32 act rows {rows}")
 
 
+@pytest.mark.parametrize("t", (Q.Q8_0, Q.Q4_0, Q.Q4_K, Q.Q6_K))
+@pytest.mark.parametrize("rows,n,out", [(200, 2048, 300), (129, 2080, 136), (512, 4096, 1024)])
+def test_tensor_core_batches_match_the_oracle(dev, t, rows, n, out):
+    """Batches past 8 rows take the int8 tensor-core tiles: partial row and
+    output tiles, and (Q8_0/Q4_0) rows that end inside a 256-value superblock."""
+    if n % Q.BLOCK[t][0]:
+        pytest.skip("row is not whole blocks of this type")
+    w = Q.random_weight(t, out, n, seed=90 + t)
+    x = oracle.normal(91 + t, 1, rows * n).reshape(rows, n)
+    got = nm.Weight(t, n, out, w).matmul(_t(x, dev)).cpu().numpy()
+    assert_close(got, Q.matmul(t, w, x, threads=16), what=f"{Q.NAMES[t]} {rows}x{n}->{out}")
+
+
 @pytest.mark.parametrize("t", (Q.Q8_0, Q.Q4_0, Q.Q4_K, Q.Q5_K, Q.Q6_K))
 def test_products_match_the_reference_fixture(dev, gold, t):
     name = Q.NAMES[t]
