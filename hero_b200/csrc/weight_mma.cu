@@ -227,50 +227,62 @@ __device__ __forceinline__ void ab_async(const MmArgs& a, int64_t t0, int64_t o0
     }
 }
 
-// Scales of superblock kb into the stage's metadata (plain loads and stores).
+// Scales of superblock kb for the stage's metadata: fetched into registers
+// ahead of the stage's compute, stored after it.
 //   am[r][0..8]: Q8_0 activations: the 8 block scales; Q8_K: d, then the 8
 //                sub-block quant sums (bsums pairs) as int bits
 //   bm[o][0..8]: Q8_0/Q4_0: the 8 block scales; Q4_K: the 4 scale words, d,
 //                dmin; Q6_K: the 4 scale words, d
 template <int TYPE>
-__device__ __forceinline__ void meta_load(const MmArgs& a, int64_t t0, int64_t o0, int kb, int tid, float* am,
-                                          float* bm) {
+struct MetaRegs {
+    float a[5], b[5];
+};
+
+template <int TYPE>
+__device__ __forceinline__ void meta_fetch(const MmArgs& a, int64_t t0, int64_t o0, int kb, int tid, MetaRegs<TYPE>& M) {
     constexpr bool K = TYPE == GT_Q4_K || TYPE == GT_Q6_K;
-    for (int id = tid; id < kBM * 9; id += kThreads) {
-        const int r = id / 9, j = id % 9;
-        const int64_t t = t0 + r;
-        float v = 0.f;
-        if (t < a.rows) {
-            if constexpr (K) {
-                if (j == 0) {
-                    v = a.ad[t * (a.in / 256) + kb];
-                } else {
-                    const int16_t* bs = a.ab + t * (a.in / 16) + 16 * (int64_t)kb + 2 * (j - 1);
-                    v = __int_as_float((int)bs[0] + (int)bs[1]);
+#pragma unroll
+    for (int i = 0; i < 5; ++i) {
+        const int id = tid + kThreads * i;
+        float va = 0.f, vb = 0.f;
+        if (id < kBM * 9) {
+            const int r = id / 9, j = id % 9;
+            const int64_t t = t0 + r, o = o0 + r;
+            if (t < a.rows) {
+                if constexpr (K) {
+                    if (j == 0) {
+                        va = a.ad[t * (a.in / 256) + kb];
+                    } else {
+                        const int16_t* bs = a.ab + t * (a.in / 16) + 16 * (int64_t)kb + 2 * (j - 1);
+                        va = __int_as_float((int)bs[0] + (int)bs[1]);
+                    }
+                } else if (j < 8 && (int64_t)kb * 8 + j < a.in / 32) {
+                    va = a.ad[t * (a.in / 32) + 8 * (int64_t)kb + j];
                 }
-            } else if (j < 8 && (int64_t)kb * 8 + j < a.in / 32) {
-                v = a.ad[t * (a.in / 32) + 8 * (int64_t)kb + j];
+            }
+            if (o < a.out) {
+                if constexpr (TYPE == GT_Q8_0 || TYPE == GT_Q4_0) {
+                    if (j < 8 && (int64_t)kb * 8 + j < a.in / 32) vb = h2f(a.w.d[o * a.w.d_row + 8 * (int64_t)kb + j]);
+                } else if (j < 4) {
+                    vb = __uint_as_float(a.w.meta[o * a.w.meta_row + 4 * (int64_t)kb + j]);
+                } else if (TYPE == GT_Q4_K && j < 6) {
+                    const uint32_t dd = a.w.dd[o * a.w.dd_row + kb];
+                    vb = h2f(j == 4 ? dd : dd >> 16);
+                } else if (TYPE == GT_Q6_K && j == 4) {
+                    vb = h2f(a.w.d[o * a.w.d_row + kb]);
+                }
             }
         }
-        am[id] = v;
+        M.a[i] = va, M.b[i] = vb;
     }
-    for (int id = tid; id < kBN * 9; id += kThreads) {
-        const int r = id / 9, j = id % 9;
-        const int64_t o = o0 + r;
-        float v = 0.f;
-        if (o < a.out) {
-            if constexpr (TYPE == GT_Q8_0 || TYPE == GT_Q4_0) {
-                if (j < 8 && (int64_t)kb * 8 + j < a.in / 32) v = h2f(a.w.d[o * a.w.d_row + 8 * (int64_t)kb + j]);
-            } else if (j < 4) {
-                v = __uint_as_float(a.w.meta[o * a.w.meta_row + 4 * (int64_t)kb + j]);
-            } else if (TYPE == GT_Q4_K && j < 6) {
-                const uint32_t dd = a.w.dd[o * a.w.dd_row + kb];
-                v = h2f(j == 4 ? dd : dd >> 16);
-            } else if (TYPE == GT_Q6_K && j == 4) {
-                v = h2f(a.w.d[o * a.w.d_row + kb]);
-            }
-        }
-        bm[id] = v;
+}
+
+template <int TYPE>
+__device__ __forceinline__ void meta_store(int tid, const MetaRegs<TYPE>& M, float* am, float* bm) {
+#pragma unroll
+    for (int i = 0; i < 5; ++i) {
+        const int id = tid + kThreads * i;
+        if (id < kBM * 9) am[id] = M.a[i], bm[id] = M.b[i];
     }
 }
 
@@ -318,7 +330,9 @@ __global__ void __launch_bounds__(kThreads, 1) mm_kernel(MmArgs a) {
         b_fetch<TYPE>(a, o0, kb0, tid, R);
         b_store<TYPE>(Bs(0), tid, R);
     }
-    meta_load<TYPE>(a, t0, o0, kb0, tid, Am(0), Bm(0));
+    MetaRegs<TYPE> M;
+    meta_fetch<TYPE>(a, t0, o0, kb0, tid, M);
+    meta_store<TYPE>(tid, M, Am(0), Bm(0));
     cp_wait_all();
     __syncthreads();
 
@@ -329,12 +343,14 @@ __global__ void __launch_bounds__(kThreads, 1) mm_kernel(MmArgs a) {
             ab_async<TYPE>(a, t0, o0, kb0 + kb + 1, tid, As(sn), Bs(sn));
             cp_commit();
             if constexpr (b_tasks<TYPE>() > 0) b_fetch<TYPE>(a, o0, kb0 + kb + 1, tid, R);
+            if constexpr (K) meta_fetch<TYPE>(a, t0, o0, kb0 + kb + 1, tid, M);  // Q8_0/Q4_0: no registers to spare
         }
         const uint32_t abase = smem_addr(As(s)), bbase = smem_addr(Bs(s));
         const float* am = Am(s);
         const float* bm = Bm(s);
-#pragma unroll 1
-        for (int kk = 0; kk < 8; ++kk) {
+        // one 32-value step; the K-quant kinds overlap two steps (their
+        // epilogue is lighter, so the registers allow it)
+        auto step = [&](int kk) {
             uint32_t af[4][4], bf[2][4];
 #pragma unroll
             for (int mt = 0; mt < 4; ++mt) {
@@ -400,42 +416,72 @@ __global__ void __launch_bounds__(kThreads, 1) mm_kernel(MmArgs a) {
                     }
                 }
             }
+                };
+        if constexpr (K) {
+#pragma unroll 2
+            for (int kk = 0; kk < 8; ++kk) step(kk);
+        } else {
+#pragma unroll 1
+            for (int kk = 0; kk < 8; ++kk) step(kk);
         }
         if constexpr (K) {
-            // superblock end: (d_w d_x) isum, minus (dmin_w d_x) sum_j m_j bsum_j for Q4_K
+            // superblock end: (d_w d_x) isum, minus (dmin_w d_x) sum_j m_j bsum_j
+            // for Q4_K; the mins sum is four dp2a per output (int16 pairs of
+            // row sums against the column's packed 6-bit mins).
+            float cd[4][2], cm[4][2];
+            uint32_t mp[4][2][2];
+#pragma unroll
+            for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+                for (int e = 0; e < 2; ++e) {
+                    const float* b = bm + (wn * 32 + nt * 8 + 2 * q + e) * 9;
+                    cd[nt][e] = b[4];
+                    if constexpr (TYPE == GT_Q4_K) {
+                        cm[nt][e] = b[5];
+                        // mins m_0..m_7 sit in bytes 2 and 3 of words 0..3
+                        const uint32_t w0 = __float_as_uint(b[0]), w1 = __float_as_uint(b[1]);
+                        const uint32_t w2 = __float_as_uint(b[2]), w3 = __float_as_uint(b[3]);
+                        mp[nt][e][0] = __byte_perm(w0, w1, 0x7632);
+                        mp[nt][e][1] = __byte_perm(w2, w3, 0x7632);
+                    }
+                }
 #pragma unroll
             for (int mt = 0; mt < 4; ++mt)
 #pragma unroll
                 for (int hf = 0; hf < 2; ++hf) {
                     const float* ar = am + (wm * 64 + mt * 16 + g + 8 * hf) * 9;
                     const float dx = ar[0];
+                    uint32_t bp[4] = {0, 0, 0, 0};
+                    if constexpr (TYPE == GT_Q4_K) {
 #pragma unroll
-                    for (int nt = 0; nt < 4; ++nt)
+                        for (int j = 0; j < 4; ++j)
+                            bp[j] = (uint32_t)(__float_as_int(ar[1 + 2 * j]) & 0xFFFF) |
+                                    ((uint32_t)__float_as_int(ar[2 + 2 * j]) << 16);
+                    }
+#pragma unroll
+                    for (int nt = 0; nt < 4; ++nt) {
+                        float v[2];
 #pragma unroll
                         for (int e = 0; e < 2; ++e) {
-                            const float* b = bm + (wn * 32 + nt * 8 + 2 * q + e) * 9;
                             const int idx = 2 * hf + e;
-                            float v = (b[4] * dx) * (float)isum[mt][nt][idx];  // |isum| may pass 2^22: a conversion
+                            v[e] = (cd[nt][e] * dx) * (float)isum[mt][nt][idx];  // |isum| may pass 2^22
                             if constexpr (TYPE == GT_Q4_K) {
-                                int msum = 0;
-#pragma unroll
-                                for (int j = 0; j < 8; ++j) {
-                                    const uint32_t wv = __float_as_uint(b[j >> 1]);
-                                    msum += (int)((wv >> (16 + 8 * (j & 1))) & 0xFF) * __float_as_int(ar[1 + j]);
-                                }
-                                v -= (b[5] * dx) * (float)msum;
+                                int msum = __dp2a_lo((int)bp[0], (int)mp[nt][e][0], 0);
+                                msum = __dp2a_hi((int)bp[1], (int)mp[nt][e][0], msum);
+                                msum = __dp2a_lo((int)bp[2], (int)mp[nt][e][1], msum);
+                                msum = __dp2a_hi((int)bp[3], (int)mp[nt][e][1], msum);
+                                v[e] -= (cm[nt][e] * dx) * (float)msum;
                             }
-                            uint64_t& pr = acc2[mt][nt][hf];
-                            const float old = __uint_as_float((uint32_t)(pr >> (32 * e)));
-                            const uint64_t nv = (uint64_t)__float_as_uint(old + v) << (32 * e);
-                            pr = (pr & (0xFFFFFFFF00000000ull >> (32 * e))) | nv;
                             isum[mt][nt][idx] = 0;
                         }
+                        acc2[mt][nt][hf] = add2(acc2[mt][nt][hf], f2(v[0], v[1]));
+                    }
                 }
         }
         if (more) {
             if constexpr (b_tasks<TYPE>() > 0) b_store<TYPE>(Bs(sn), tid, R);
-            meta_load<TYPE>(a, t0, o0, kb0 + kb + 1, tid, Am(sn), Bm(sn));
+            if constexpr (!K) meta_fetch<TYPE>(a, t0, o0, kb0 + kb + 1, tid, M);
+            meta_store<TYPE>(tid, M, Am(sn), Bm(sn));
             cp_wait_all();
         }
         __syncthreads();
