@@ -105,6 +105,27 @@ def tf32_peak_and_note():
     return peaks()["bf16"] / 2, "tf32 peak taken as half the measured bf16 peak (issue-loop probe unavailable)"
 
 
+def imma_rate():
+    """The warp-level int8 MMA issue rate (mma.sync m16n8k32, 16 warps per SM,
+    register operands; hero_b200/libnmg_rate.so) in TOPS, the ceiling of the
+    projection GEMM's instruction; None without the probe library or a GPU."""
+    if "imma" in _RATES:
+        return _RATES["imma"]
+    out = None
+    try:
+        import ctypes
+
+        lib = ctypes.CDLL(os.path.join(ROOT, "hero_b200", "libnmg_rate.so"))
+        lib.nmg_rate_imma.argtypes = [ctypes.c_int, ctypes.POINTER(ctypes.c_double)]
+        t = ctypes.c_double()
+        if lib.nmg_rate_imma(2048, ctypes.byref(t)) == 0:
+            out = t.value
+    except Exception:
+        out = None
+    _RATES["imma"] = out
+    return out
+
+
 def ncu_traffic(name):
     """DRAM bytes per launch of a workload's dominant kernel from profiles/traffic.json, or None."""
     try:
@@ -370,6 +391,32 @@ class RefConfigs:
     def line(self, value, unit, sample, cores=None):
         return {"value": value, "unit": unit, "cores": cores or self.cores, "kind": self.kind, "sample": sample}
 
+    def projections(self):
+        """The oracle's restatement of Weight::matvec / matmul (the reference
+        library instantiates no model-sized Weight), on all host threads: one
+        token through a layer's six projections, and 16 rows through them."""
+        from oracle import quant as Q
+
+        ws = [(gt, n, o, synthetic_gguf(gt, o, n, i)) for i, (_, gt, n, o) in enumerate(PROJ_LAYER)]
+        wbytes = sum(w.size for *_, w in ws)
+        x = {n: self._rows(12, 1, 16, n) for n in (4096, 12288)}
+
+        def run(rows):
+            t = time.perf_counter()
+            for gt, n, o, w in ws:
+                Q.matmul(gt, w, x[n][:rows], threads=self.threads)
+            return time.perf_counter() - t
+
+        run(1)
+        secs = [run(1) for _ in range(3)]
+        dec = float(np.median(secs))
+        pre = run(16)
+        ops = 2.0 * 16 * sum(n * o for _, n, o, _ in ws)
+        return {"decode": {**self.line(wbytes / dec / 1e9, "GB/s", f"one token through the 6 projections, "
+                                       f"{dec * 1e3:.1f} ms", cores=self.threads), "kind": "port"},
+                "prefill": {**self.line(ops / pre / 1e12, "TOPS", f"16 rows through the 6 projections, "
+                                        f"{pre * 1e3:.0f} ms", cores=self.threads), "kind": "port"}}
+
     def config1(self):
         hq, hkv, dh, L = 16, 8, 128, 1024
         k, v = self._rows(101, 1, L, hkv * dh), self._rows(101, 2, L, hkv * dh)
@@ -455,7 +502,8 @@ def cpu_baselines(extra):
     """Adds a cpu_baseline beside each single-GPU extra (rank 0, N = 1)."""
     ref = RefConfigs()
     for name, key, fn in (("config1", None, ref.config1), ("config3", None, ref.config3),
-                          ("config4", None, ref.config4), ("config5", None, ref.config5)):
+                          ("config4", None, ref.config4), ("config5", None, ref.config5),
+                          ("projections", None, ref.projections)):
         ent = extra.get(name)
         if not isinstance(ent, dict) or "error" in ent:
             continue
@@ -469,6 +517,10 @@ def cpu_baselines(extra):
                 ent["prefill_chunk64"]["cpu_baseline"] = cb["prefill"]
             if isinstance(ent.get("decode"), dict):
                 ent["decode"]["cpu_baseline"] = cb["decode"]
+        elif name == "projections":
+            for part in ("decode", "prefill"):
+                if isinstance(ent.get(part), dict):
+                    ent[part]["cpu_baseline"] = cb[part]
         elif name == "config4":
             for part in ("prefill", "decode"):
                 if isinstance(ent.get(part), dict):
@@ -1226,6 +1278,92 @@ def extra_config4(torch, dev, small=False):
     return {"workload": "config 4: Gemma hybrid bf16, 8q/4kv, d256, scale 1, 5 local (W=1024) : 1 global", **res}
 
 
+# Qwen3.5-9B (qwen35.hpp:62-83, D = 4096, FF = 12288) projections of one
+# delta-rule layer in a Q4_K_M-style mix: in-projection qkv (D -> 2*2048 +
+# 4096 conv channels), z (D -> 4096), out (4096 -> D), MLP gate and up
+# (D -> FF) in Q4_K, MLP down (FF -> D) in Q6_K.
+PROJ_LAYER = (("qkv", 12, 4096, 8192), ("z", 12, 4096, 4096), ("out", 12, 4096, 4096), ("gate", 12, 4096, 12288),
+              ("up", 12, 4096, 12288), ("down", 14, 12288, 4096))
+_GGUF_BLOCK = {2: (32, 18), 8: (32, 34), 12: (256, 144), 13: (256, 176), 14: (256, 210)}
+
+
+def synthetic_gguf(gt, out, n, seed):
+    """Random GGUF block bytes [out][row bytes] with fp16 scale fields sized so
+    a weight is about 1 / sqrt(n) (random quant bytes, as the reference's quant
+    tests draw them)."""
+    bl, bb = _GGUF_BLOCK[gt]
+    rng = np.random.default_rng(seed)
+    w = rng.integers(0, 256, size=(out, n // bl, bb), dtype=np.uint8)
+    s = 1.0 / math.sqrt(n)
+
+    def put(off, v):
+        h = np.asarray(v, np.float16).view(np.uint16)
+        w[:, :, off], w[:, :, off + 1] = (h & 0xFF).astype(np.uint8), (h >> 8).astype(np.uint8)
+
+    u = rng.uniform(0.5, 1.5, size=(out, n // bl))
+    if gt == 8:
+        put(0, s / 74 * u)
+    elif gt == 2:
+        put(0, s / 4.6 * u)
+    elif gt == 12:
+        put(0, s / 317 * u)
+        put(2, s / 317 * 7.5 * u)
+    elif gt == 14:
+        put(208, s / 1369 * u)
+    return w.reshape(out, -1)
+
+
+def extra_projections(torch, dev, small=False):
+    """The quantised projections of Qwen3.5-9B delta-rule layers (weights
+    resident on the device): decode (one token, Weight::matvec for each of the
+    six projections, weights streamed from HBM: two layers' weights, 271 MB,
+    alternate past the L2) and prefill (4096 tokens, Weight::matmul on the int8
+    tensor-core tiles)."""
+    from hero_b200 import nm
+
+    layers = 1 if small else 2
+    Ws = [[nm.Weight(gt, n, o, synthetic_gguf(gt, o, n, 100 * l + i), device=dev.index)
+           for i, (_, gt, n, o) in enumerate(PROJ_LAYER)] for l in range(layers)]
+    wbytes = sum((n // _GGUF_BLOCK[gt][0]) * _GGUF_BLOCK[gt][1] * o for _, gt, n, o in PROJ_LAYER)
+    g = torch.Generator(device=dev)
+    g.manual_seed(11)
+    T = 256 if small else 4096
+    x = {n: torch.randn(T, n, device=dev, generator=g) for n in (4096, 12288)}
+    y = {o: torch.empty(T, o, device=dev) for o in (4096, 8192, 12288)}
+
+    def decode():
+        for Wl in Ws:
+            for W, (_, gt, n, o) in zip(Wl, PROJ_LAYER):
+                W.matvec(x[n][0], out=y[o][0])
+
+    ms = graph_time(torch, dev, decode, 10, 5) / layers
+    gbs = wbytes / (ms * 1e-3) / 1e9
+    p = peaks()
+    res = {"workload": "Qwen3.5-9B delta-layer projections (qkv, z, out, gate, up in Q4_K; down in Q6_K), "
+                       f"{wbytes / 1e6:.1f} MB of GGUF weights per layer, {layers} layers alternating",
+           "decode": {"value": gbs, "unit": "GB/s", "us_per_layer": ms * 1e3, "weight_bytes": wbytes,
+                      "roofline": {"bound": "hbm", "achieved": gbs, "peak": p["hbm"], "frac": gbs / p["hbm"],
+                                   "kernel": "mv_kernel (activation quantiser fused or a launch ahead of it)"},
+                      "method": "6 matvecs per layer captured in a CUDA graph with programmatic launches, "
+                                f"{layers} layers' weights in turn, 5 passes per graph, 10 replays"}}
+    ops = 2.0 * T * sum(n * o for _, _, n, o in PROJ_LAYER)
+
+    def prefill():
+        for W, (_, gt, n, o) in zip(Ws[0], PROJ_LAYER):
+            W.matmul(x[n], out=y[o])
+
+    msp = graph_time(torch, dev, prefill, 3, 2)
+    tops = ops / (msp * 1e-3) / 1e12
+    ceil = imma_rate()
+    res["prefill"] = {"value": tops, "unit": "TOPS", "ms_per_layer": msp, "rows": T,
+                      "roofline": {"bound": "tensor", "achieved": tops, "peak": ceil, "unit": "TOPS",
+                                   "frac": (tops / ceil) if ceil else None,
+                                   "peak_note": "measured mma.sync m16n8k32 int8 issue rate (libnmg_rate.so); "
+                                                "tcgen05 int8 nominal is 4500 TOPS",
+                                   "kernel": "mm_kernel (int8 mma.sync tiles, per-block fp32 scaling)"}}
+    return res
+
+
 def extra_config5(torch, dev, small=False):
     from hero_b200 import nm
 
@@ -1758,7 +1896,7 @@ def main():
     ap.add_argument("--impl", default="nmg", choices=["nmg", "reference"])
     ap.add_argument("--no-extra", action="store_true", help="headline only")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
-    ap.add_argument("--only", choices=["c1", "c2", "c3", "c4", "c5", "io", "vit"],
+    ap.add_argument("--only", choices=["c1", "c2", "c3", "c4", "c5", "io", "vit", "proj"],
                     help="run one workload alone (profiling); prints its own JSON line")
     ap.add_argument("--small", action="store_true", help="with --only: profiling-sized variant")
     args = ap.parse_args()
@@ -1798,14 +1936,15 @@ def main():
         return
     if args.only and args.only != "c2":
         fn = {"c1": extra_config1, "c3": extra_config3, "c4": extra_config4, "c5": extra_config5,
-              "io": extra_attn_io, "vit": extra_vit}[args.only]
+              "io": extra_attn_io, "vit": extra_vit, "proj": extra_projections}[args.only]
         print(json.dumps({"only": args.only, "small": args.small, **fn(torch, dev, small=args.small)}), flush=True)
         return
     res = bench_prefill(args, torch, dist, rank, world, dev)
     extra = {}
     if world == 1 and not args.no_extra and not args.only:
         for name, fn in (("config1", extra_config1), ("config3", extra_config3), ("config4", extra_config4),
-                         ("config5", extra_config5), ("attn_io", extra_attn_io), ("vit", extra_vit)):
+                         ("config5", extra_config5), ("attn_io", extra_attn_io), ("vit", extra_vit),
+                         ("projections", extra_projections)):
             try:
                 extra[name] = fn(torch, dev)
             except Exception as e:  # report, never hide, a failing extra

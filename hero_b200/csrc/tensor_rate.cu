@@ -116,3 +116,57 @@ extern "C" __attribute__((visibility("default"))) int nmg_rate_tensor(int kind, 
     delete[] h;
     return (int)e;
 }
+
+// The warp-level integer MMA rate: every warp of 16 per SM issues `reps`
+// rounds of 8 independent mma.sync m16n8k32 s8 x s8 -> s32 on register
+// operands (the instruction the quantised projection GEMM issues).  Timed with
+// CUDA events around one launch; returns tera-ops per second.
+namespace nmg {
+namespace {
+
+__global__ void __launch_bounds__(512) imma_rate_kernel(int reps, int* sink) {
+    int c[8][4] = {};
+    const uint32_t a0 = threadIdx.x, a1 = a0 * 3u, a2 = a0 * 5u, a3 = a0 * 7u, b0 = a0 * 11u, b1 = a0 * 13u;
+    for (int i = 0; i < reps; ++i) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+            asm volatile(
+                "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+                : "+r"(c[j][0]), "+r"(c[j][1]), "+r"(c[j][2]), "+r"(c[j][3])
+                : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+    }
+    int s = 0;
+    for (int j = 0; j < 8; ++j) s += c[j][0] ^ c[j][3];
+    if (s == 0x7fffffff) sink[0] = s;  // keeps the loop live
+}
+
+}  // namespace
+}  // namespace nmg
+
+extern "C" __attribute__((visibility("default"))) int nmg_rate_imma(int reps, double* tops) {
+    if (reps < 1 || !tops) return (int)cudaErrorInvalidValue;
+    int dev = 0, nsm = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return (int)e;
+    int* sink = nullptr;
+    cudaEvent_t t0 = nullptr, t1 = nullptr;
+    e = cudaMalloc(&sink, sizeof(int));
+    if (e == cudaSuccess) e = cudaEventCreate(&t0);
+    if (e == cudaSuccess) e = cudaEventCreate(&t1);
+    if (e == cudaSuccess) {
+        nmg::imma_rate_kernel<<<nsm, 512>>>(reps, sink);  // warm-up
+        cudaEventRecord(t0);
+        nmg::imma_rate_kernel<<<nsm, 512>>>(reps, sink);
+        cudaEventRecord(t1);
+        e = cudaEventSynchronize(t1);
+    }
+    if (e == cudaSuccess) e = cudaGetLastError();
+    float ms = 0.f;
+    if (e == cudaSuccess) e = cudaEventElapsedTime(&ms, t0, t1);
+    if (e == cudaSuccess) *tops = (double)nsm * 16 * reps * 8 * (2.0 * 16 * 8 * 32) / (ms * 1e-3) / 1e12;
+    if (t0) cudaEventDestroy(t0);
+    if (t1) cudaEventDestroy(t1);
+    if (sink) cudaFree(sink);
+    return (int)e;
+}

@@ -252,27 +252,41 @@ struct WChunk {
     uint32_t m, d;  // the lane's scale word and block scale(s)
 };
 
+// One output row's plane pointers (64-bit arithmetic once per row; the
+// chunk offsets inside a row are 32-bit).
+struct RowPtr {
+    const uint8_t* qs;
+    const uint8_t* hi;
+    const uint32_t* meta;
+    const uint16_t* d;
+    const uint32_t* dd;
+};
+
+__device__ __forceinline__ RowPtr row_ptr(const Planes& P, int64_t o) {
+    return {P.qs + o * P.qs_row, P.hi + o * P.hi_row, P.meta + o * P.meta_row, P.d + o * P.d_row, P.dd + o * P.dd_row};
+}
+
 template <int TYPE>
-__device__ __forceinline__ WChunk<TYPE> load_chunk(const Planes& P, int64_t o, int64_t c) {
+__device__ __forceinline__ WChunk<TYPE> load_chunk(const RowPtr& r, int c) {
     WChunk<TYPE> w;
     if constexpr (TYPE == GT_Q8_0 || TYPE == GT_Q4_0) {
-        w.q = ld16_stream(P.qs + o * P.qs_row + 16 * c);
-        w.d = P.d[o * P.d_row + (TYPE == GT_Q8_0 ? (c >> 1) : c)];
+        w.q = ld16_stream(r.qs + 16 * c);
+        w.d = r.d[TYPE == GT_Q8_0 ? (c >> 1) : c];
     } else if constexpr (TYPE == GT_Q4_K || TYPE == GT_Q5_K) {
-        w.q = ld16_stream(P.qs + o * P.qs_row + 16 * c);
-        w.m = P.meta[o * P.meta_row + 4 * (c >> 3) + ((c >> 1) & 3)];
-        w.d = P.dd[o * P.dd_row + (c >> 3)];
-        if constexpr (TYPE == GT_Q5_K) w.h = ld16_stream(P.hi + o * P.hi_row + 32 * (c >> 3) + 16 * (c & 1));
+        w.q = ld16_stream(r.qs + 16 * c);
+        w.m = r.meta[4 * (c >> 3) + ((c >> 1) & 3)];
+        w.d = r.dd[c >> 3];
+        if constexpr (TYPE == GT_Q5_K) w.h = ld16_stream(r.hi + 32 * (c >> 3) + 16 * (c & 1));
     } else if constexpr (TYPE == GT_Q6_K) {
-        const int64_t sb = c >> 2, h = (c >> 1) & 1, k = c & 1;
-        const uint8_t* ql = P.qs + o * P.qs_row + 128 * sb + 64 * h + 16 * k;
+        const int sb = c >> 2, h = (c >> 1) & 1, k = c & 1;
+        const uint8_t* ql = r.qs + 128 * sb + 64 * h + 16 * k;
         w.q = ld16_stream(ql);
         w.q2 = ld16_stream(ql + 32);
-        w.h = ld16_stream(P.hi + o * P.hi_row + 64 * sb + 32 * h + 16 * k);
-        w.m = P.meta[o * P.meta_row + 4 * sb + (c & 3)];
-        w.d = P.d[o * P.d_row + sb];
+        w.h = ld16_stream(r.hi + 64 * sb + 32 * h + 16 * k);
+        w.m = r.meta[4 * sb + (c & 3)];
+        w.d = r.d[sb];
     } else {
-        w.q = ld16_stream(P.qs + o * P.qs_row + 16 * c);
+        w.q = ld16_stream(r.qs + 16 * c);
     }
     return w;
 }
@@ -287,8 +301,8 @@ __device__ __forceinline__ int dot16(const uint32_t (&wq)[4], const uint4& a) {
 // Integer path: the chunk's exact block sums against each activation row,
 // scaled in fp32 as the reference's vec_dot_* does per block.
 template <int TYPE, int T>
-__device__ __forceinline__ void i8_chunk(const WChunk<TYPE>& w, int64_t c, const MvArgs& a, float (&acc)[T]) {
-    const int64_t in = a.in;
+__device__ __forceinline__ void i8_chunk(const WChunk<TYPE>& w, int c, const MvArgs& a, float (&acc)[T]) {
+    const int in = (int)a.in;
     if constexpr (TYPE == GT_Q8_0) {
         const uint32_t wq[4] = {w.q.x, w.q.y, w.q.z, w.q.w};
         const float dw = h2f(w.d);
@@ -314,9 +328,9 @@ __device__ __forceinline__ void i8_chunk(const WChunk<TYPE>& w, int64_t c, const
             acc[t] += (float)s * dw * a.ad[t * (in >> 5) + c];
         }
     } else if constexpr (TYPE == GT_Q4_K) {
-        const int64_t sb = c >> 3;
-        const int g = (int)((c >> 1) & 3), h = (int)(c & 1);
-        const int64_t e0 = 256 * sb + 64 * g + 16 * h;
+        const int sb = c >> 3;
+        const int g = (c >> 1) & 3, h = c & 1;
+        const int e0 = 256 * sb + 64 * g + 16 * h;
         const int sc1 = w.m & 0xFF, sc2 = (w.m >> 8) & 0xFF, m1 = (w.m >> 16) & 0xFF, m2 = w.m >> 24;
         const float dd = h2f(w.d), dm = h2f(w.d >> 16);
         const uint32_t lo[4] = {w.q.x & 0x0F0F0F0Fu, w.q.y & 0x0F0F0F0Fu, w.q.z & 0x0F0F0F0Fu, w.q.w & 0x0F0F0F0Fu};
@@ -333,8 +347,8 @@ __device__ __forceinline__ void i8_chunk(const WChunk<TYPE>& w, int64_t c, const
             acc[t] += (dd * dx) * (float)isum - (dm * dx) * (float)msum;
         }
     } else if constexpr (TYPE == GT_Q6_K) {
-        const int64_t sb = c >> 2;
-        const int h = (int)((c >> 1) & 1), k = (int)(c & 1);
+        const int sb = c >> 2;
+        const int h = (c >> 1) & 1, k = c & 1;
         const uint32_t qa[4] = {w.q.x, w.q.y, w.q.z, w.q.w}, qb[4] = {w.q2.x, w.q2.y, w.q2.z, w.q2.w};
         const uint32_t qh[4] = {w.h.x, w.h.y, w.h.z, w.h.w};
         uint32_t u[4][4];
@@ -349,7 +363,7 @@ __device__ __forceinline__ void i8_chunk(const WChunk<TYPE>& w, int64_t c, const
 #pragma unroll
         for (int r = 0; r < 4; ++r) sc[r] = (int)(int8_t)((w.m >> (8 * r)) & 0xFF);
         const float dw = h2f(w.d);
-        const int64_t e0 = 256 * sb + 128 * h + 16 * k;
+        const int e0 = 256 * sb + 128 * h + 16 * k;
 #pragma unroll
         for (int t = 0; t < T; ++t) {
             if (t >= a.rows) break;
@@ -370,8 +384,8 @@ __device__ __forceinline__ float4 ldx4(const float* p) { return *reinterpret_cas
 // Q6_K's (d * scale) * q, which is evaluated in that order).  Returns the
 // element index of v[0]; chunk_off gives the others.
 template <int TYPE>
-__device__ __forceinline__ int64_t dequant_chunk(const WChunk<TYPE>& w, int64_t c, float (&v)[chunk_values<TYPE>()]) {
-    int64_t e0 = c * chunk_values<TYPE>();
+__device__ __forceinline__ int dequant_chunk(const WChunk<TYPE>& w, int c, float (&v)[chunk_values<TYPE>()]) {
+    int e0 = c * chunk_values<TYPE>();
     if constexpr (TYPE == GT_F32) {
         v[0] = __uint_as_float(w.q.x), v[1] = __uint_as_float(w.q.y), v[2] = __uint_as_float(w.q.z);
         v[3] = __uint_as_float(w.q.w);
@@ -390,8 +404,8 @@ __device__ __forceinline__ int64_t dequant_chunk(const WChunk<TYPE>& w, int64_t 
             v[i + 16] = dw * (float)((b >> 4) - 8);
         }
     } else if constexpr (TYPE == GT_Q4_K || TYPE == GT_Q5_K) {
-        const int64_t sb = c >> 3;
-        const int g = (int)((c >> 1) & 3), h = (int)(c & 1);
+        const int sb = c >> 3;
+        const int g = (c >> 1) & 3, h = c & 1;
         e0 = 256 * sb + 64 * g + 16 * h;
         const int sc1 = w.m & 0xFF, sc2 = (w.m >> 8) & 0xFF, m1 = (w.m >> 16) & 0xFF, m2 = w.m >> 24;
         const float dd = h2f(w.d), dm = h2f(w.d >> 16);
@@ -411,8 +425,8 @@ __device__ __forceinline__ int64_t dequant_chunk(const WChunk<TYPE>& w, int64_t 
             v[i + 16] = d2 * (float)hi - f2;  // elements e0 + 32 + i   (sub-block 2g+1)
         }
     } else if constexpr (TYPE == GT_Q6_K) {
-        const int64_t sb = c >> 2;
-        const int h = (int)((c >> 1) & 1), k = (int)(c & 1);
+        const int sb = c >> 2;
+        const int h = (c >> 1) & 1, k = c & 1;
         e0 = 256 * sb + 128 * h + 16 * k;
         const uint32_t qa[4] = {w.q.x, w.q.y, w.q.z, w.q.w}, qb[4] = {w.q2.x, w.q2.y, w.q2.z, w.q2.w};
         const uint32_t qh[4] = {w.h.x, w.h.y, w.h.z, w.h.w};
@@ -444,14 +458,14 @@ __host__ __device__ constexpr int chunk_off(int i) {
 
 // fp32-activation path: dequantised chunk values times each activation row.
 template <int TYPE, int T>
-__device__ __forceinline__ void f32_chunk(const WChunk<TYPE>& w, int64_t c, const MvArgs& a, float (&acc)[T]) {
+__device__ __forceinline__ void f32_chunk(const WChunk<TYPE>& w, int c, const MvArgs& a, float (&acc)[T]) {
     constexpr int NV = chunk_values<TYPE>();
     float v[NV];
-    const int64_t e0 = dequant_chunk<TYPE>(w, c, v);
+    const int e0 = dequant_chunk<TYPE>(w, c, v);
 #pragma unroll
     for (int t = 0; t < T; ++t) {
         if (t >= a.rows) break;
-        const float* xr = a.x + t * a.in + e0;
+        const float* xr = a.x + t * (int)a.in + e0;
         float s = 0.f;
 #pragma unroll
         for (int i = 0; i < NV; i += 4) {
@@ -509,11 +523,11 @@ __global__ void __launch_bounds__(kMvWarps * 32, (TYPE == GT_Q6_K || TYPE == GT_
     const int nrows = o0 < a.out ? (int)((a.out - o0 + stride - 1) / stride) : 0;
     WChunk<TYPE> w[U], wn[U];
     auto load_group = [&](int row, int grp, WChunk<TYPE>(&dst)[U]) {
-        const int64_t o = o0 + row * stride;
+        const RowPtr rp = row_ptr(a.w, o0 + row * stride);
 #pragma unroll
         for (int u = 0; u < U; ++u) {
             const int c = grp * (32 * U) + lane + 32 * u;
-            if (c < nch) dst[u] = load_chunk<TYPE>(a.w, o, c);
+            if (c < nch) dst[u] = load_chunk<TYPE>(rp, c);
         }
     };
     if (nrows > 0) load_group(0, 0, w);
@@ -596,10 +610,11 @@ __global__ void dequant_rows_kernel(Planes P, int64_t in, const int32_t* __restr
     const int64_t nch = in / chunk_values<TYPE>();
     const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
     if (i >= n * nch) return;
-    const int64_t r = i / nch, c = i % nch;
-    const WChunk<TYPE> w = load_chunk<TYPE>(P, ids[r], c);
+    const int64_t r = i / nch;
+    const int c = (int)(i % nch);
+    const WChunk<TYPE> w = load_chunk<TYPE>(row_ptr(P, ids[r]), c);
     float v[chunk_values<TYPE>()];
-    const int64_t e0 = dequant_chunk<TYPE>(w, c, v);
+    const int e0 = dequant_chunk<TYPE>(w, c, v);
     float* dst = out + r * in + e0;
 #pragma unroll
     for (int j = 0; j < chunk_values<TYPE>(); ++j) dst[chunk_off<TYPE>(j)] = v[j];
