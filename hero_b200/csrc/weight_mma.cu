@@ -31,7 +31,10 @@ namespace nmg {
 namespace wq {
 namespace {
 
-constexpr int kBM = 128, kBN = 128, kKS = 256, kThreads = 256;
+constexpr int kBM = 128, kBN = 128, kKS = 256;
+constexpr int kMT = 2;                            // m16 tiles per warp: warp tile 32 x 32
+constexpr int kThreads = 32 * (kBM / (16 * kMT)) * 4;  // 4 x 4 warps
+constexpr int kMetaN = (kBM * 9 + kThreads - 1) / kThreads;
 constexpr int kTile = kBM * kKS;                 // bytes of one int8 operand tile
 constexpr int kAMeta = kBM * 9 * 4;              // per row: 8 block scales (Q8_0) or d + 8 bsum pairs (Q8_K)
 constexpr int kBMeta = kBN * 9 * 4;              // per output: 8 block scales, or packed scales + d (+ dmin)
@@ -116,13 +119,13 @@ __device__ __forceinline__ uint64_t i2f2(int a, int b) {
 // (one 16-byte unit per task, 4 tasks per thread) before unpacking it.
 template <int TYPE>
 struct BRegs {
-    uint4 q[4], q2[4], h[4];
+    uint4 q[1024 / kThreads], q2[1024 / kThreads], h[1024 / kThreads];
 };
 
 // Number of register-staged 16-byte weight units a thread carries per stage.
 template <int TYPE>
 __host__ __device__ constexpr int b_tasks() {
-    return TYPE == GT_Q6_K ? 2 : TYPE == GT_Q8_0 ? 0 : 4;
+    return TYPE == GT_Q6_K ? 512 / kThreads : TYPE == GT_Q8_0 ? 0 : 1024 / kThreads;
 }
 
 // Fetch this thread's weight units of superblock kb into registers.
@@ -235,14 +238,14 @@ __device__ __forceinline__ void ab_async(const MmArgs& a, int64_t t0, int64_t o0
 //                dmin; Q6_K: the 4 scale words, d
 template <int TYPE>
 struct MetaRegs {
-    float a[5], b[5];
+    float a[kMetaN], b[kMetaN];
 };
 
 template <int TYPE>
 __device__ __forceinline__ void meta_fetch(const MmArgs& a, int64_t t0, int64_t o0, int kb, int tid, MetaRegs<TYPE>& M) {
     constexpr bool K = TYPE == GT_Q4_K || TYPE == GT_Q6_K;
 #pragma unroll
-    for (int i = 0; i < 5; ++i) {
+    for (int i = 0; i < kMetaN; ++i) {
         const int id = tid + kThreads * i;
         float va = 0.f, vb = 0.f;
         if (id < kBM * 9) {
@@ -280,7 +283,7 @@ __device__ __forceinline__ void meta_fetch(const MmArgs& a, int64_t t0, int64_t 
 template <int TYPE>
 __device__ __forceinline__ void meta_store(int tid, const MetaRegs<TYPE>& M, float* am, float* bm) {
 #pragma unroll
-    for (int i = 0; i < 5; ++i) {
+    for (int i = 0; i < kMetaN; ++i) {
         const int id = tid + kThreads * i;
         if (id < kBM * 9) am[id] = M.a[i], bm[id] = M.b[i];
     }
@@ -299,7 +302,7 @@ __global__ void __launch_bounds__(kThreads, 1) mm_kernel(MmArgs a) {
     constexpr bool K = TYPE == GT_Q4_K || TYPE == GT_Q6_K;
     extern __shared__ __align__(128) uint8_t smem[];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int wm = warp >> 2, wn = warp & 3;  // 2 x 4 warps, 64 x 32 each
+    const int wm = warp >> 2, wn = warp & 3;  // 4 x 4 warps, 32 x 32 each
     const int g = lane >> 2, q = lane & 3;
     const int64_t o0 = (int64_t)blockIdx.x * kBN, t0 = (int64_t)blockIdx.y * kBM;
     const int nk_all = (int)((a.in + kKS - 1) / kKS);
@@ -311,10 +314,10 @@ __global__ void __launch_bounds__(kThreads, 1) mm_kernel(MmArgs a) {
     auto Bm = [&](int s) { return reinterpret_cast<float*>(smem + s * kStage + 2 * kTile + kAMeta); };
 
     // acc2[mt][nt][h]: the pair (cols 2q, 2q+1) of row g + 8h, as float2 bits
-    uint64_t acc2[4][4][2];
-    int isum[4][4][4];
+    uint64_t acc2[kMT][4][2];
+    int isum[kMT][4][4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
+    for (int i = 0; i < kMT; ++i)
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
             acc2[i][j][0] = acc2[i][j][1] = 0;
@@ -348,13 +351,13 @@ __global__ void __launch_bounds__(kThreads, 1) mm_kernel(MmArgs a) {
         const uint32_t abase = smem_addr(As(s)), bbase = smem_addr(Bs(s));
         const float* am = Am(s);
         const float* bm = Bm(s);
-        // one 32-value step; the K-quant kinds overlap two steps (their
-        // epilogue is lighter, so the registers allow it)
+        // one 32-value step; Q4_K overlaps two steps (its epilogue is the
+        // lightest, so the registers allow it)
         auto step = [&](int kk) {
-            uint32_t af[4][4], bf[2][4];
+            uint32_t af[kMT][4], bf[2][4];
 #pragma unroll
-            for (int mt = 0; mt < 4; ++mt) {
-                const int r = wm * 64 + mt * 16 + (lane & 7) + 8 * ((lane >> 3) & 1);
+            for (int mt = 0; mt < kMT; ++mt) {
+                const int r = wm * (16 * kMT) + mt * 16 + (lane & 7) + 8 * ((lane >> 3) & 1);
                 ldsm4(abase + swz(r, 2 * kk + (lane >> 4)), af[mt]);
             }
 #pragma unroll
@@ -385,11 +388,11 @@ __global__ void __launch_bounds__(kThreads, 1) mm_kernel(MmArgs a) {
                     }
                 }
 #pragma unroll
-            for (int mt = 0; mt < 4; ++mt) {
+            for (int mt = 0; mt < kMT; ++mt) {
                 float rs[2] = {0.f, 0.f};
                 if constexpr (!K) {
-                    rs[0] = am[(wm * 64 + mt * 16 + g) * 9 + kk];
-                    rs[1] = am[(wm * 64 + mt * 16 + g + 8) * 9 + kk];
+                    rs[0] = am[(wm * (16 * kMT) + mt * 16 + g) * 9 + kk];
+                    rs[1] = am[(wm * (16 * kMT) + mt * 16 + g + 8) * 9 + kk];
                 }
 #pragma unroll
                 for (int nt = 0; nt < 4; ++nt) {
@@ -417,7 +420,7 @@ __global__ void __launch_bounds__(kThreads, 1) mm_kernel(MmArgs a) {
                 }
             }
                 };
-        if constexpr (K) {
+        if constexpr (TYPE == GT_Q4_K) {
 #pragma unroll 2
             for (int kk = 0; kk < 8; ++kk) step(kk);
         } else {
@@ -446,10 +449,10 @@ __global__ void __launch_bounds__(kThreads, 1) mm_kernel(MmArgs a) {
                     }
                 }
 #pragma unroll
-            for (int mt = 0; mt < 4; ++mt)
+            for (int mt = 0; mt < kMT; ++mt)
 #pragma unroll
                 for (int hf = 0; hf < 2; ++hf) {
-                    const float* ar = am + (wm * 64 + mt * 16 + g + 8 * hf) * 9;
+                    const float* ar = am + (wm * (16 * kMT) + mt * 16 + g + 8 * hf) * 9;
                     const float dx = ar[0];
                     uint32_t bp[4] = {0, 0, 0, 0};
                     if constexpr (TYPE == GT_Q4_K) {
@@ -488,10 +491,10 @@ __global__ void __launch_bounds__(kThreads, 1) mm_kernel(MmArgs a) {
     }
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 #pragma unroll
-    for (int mt = 0; mt < 4; ++mt)
+    for (int mt = 0; mt < kMT; ++mt)
 #pragma unroll
         for (int hf = 0; hf < 2; ++hf) {
-            const int64_t t = t0 + wm * 64 + mt * 16 + g + 8 * hf;
+            const int64_t t = t0 + wm * (16 * kMT) + mt * 16 + g + 8 * hf;
             if (t >= a.rows) continue;
 #pragma unroll
             for (int nt = 0; nt < 4; ++nt) {
