@@ -48,22 +48,32 @@ namespace {
 
 using namespace pf;
 
-template <int DH>
+template <int DH, int BN_>
 struct PfCfg {
     static constexpr int BM = 128;
-    static constexpr int BN = DH == 256 ? 64 : 128;
-    static constexpr int KST = DH == 256 ? 2 : 3;  // K stages (K is released as soon as S is computed)
-    static constexpr int VST = 2;  // V stages (released after P.V)
+    static constexpr int BN = BN_;
+    // K and V stream through shared memory in pieces, each with its own full
+    // and empty barrier.  At head_dim 256 with 128-key blocks a block's K is
+    // four pieces of 64 dimensions (an S MMA group frees each as it
+    // completes) and its V two pieces of 64 keys, so a ring of one block each
+    // still overlaps the loads with the MMAs; otherwise a piece is a block.
+    static constexpr bool WIDE = DH == 256 && BN == 128;
+    static constexpr int KP = WIDE ? 4 : 1;             // K pieces per block
+    static constexpr int KRING = WIDE ? 4 : (DH == 256 ? 2 : 3);  // K ring, in pieces
+    static constexpr int VP = WIDE ? 2 : 1;             // V pieces per block
+    static constexpr int VRING = 2;                     // V ring, in pieces
+    static constexpr int KDIMS = DH / KP;               // dimensions of a K piece
+    static constexpr int VROWS = BN / VP;               // keys of a V piece
     static constexpr int Q_BYTES = BM * DH * 2;
-    static constexpr int K_BYTES = BN * DH * 2;
-    static constexpr int V_BYTES = BN * DH * 2;
+    static constexpr int K_BYTES = BN * KDIMS * 2;      // one K piece
+    static constexpr int V_BYTES = VROWS * DH * 2;      // one V piece
     static constexpr int Q_OFF = 0;
     static constexpr int K_OFF = Q_OFF + Q_BYTES;
-    static constexpr int V_OFF = K_OFF + KST * K_BYTES;
-    static constexpr int BAR_OFF = V_OFF + VST * V_BYTES;
-    // q_full, q_empty, k_full/k_empty[KST], v_full/v_empty[VST], s_full[2], p_full[2], o_done,
+    static constexpr int V_OFF = K_OFF + KRING * K_BYTES;
+    static constexpr int BAR_OFF = V_OFF + VRING * V_BYTES;
+    // q_full, q_empty, k_full/k_empty[KRING], v_full/v_empty[VRING], s_full[2], p_full[2], o_done,
     // o_final[2], o_free[2], l_full[2], quad[4]
-    static constexpr int NBARS = 2 + 2 * KST + 2 * VST + 2 + 2 + 1 + 2 + 2 + 2 + 4;
+    static constexpr int NBARS = 2 + 2 * KRING + 2 * VRING + 2 + 2 + 1 + 2 + 2 + 2 + 4;
     static constexpr int FLAGS_OFF = BAR_OFF + NBARS * 8;  // TMEM address, abort flag, last-split flag
     // Softmax warps per TMEM lane quadrant: each owns PART_N keys of a score
     // row and PART_D columns of its output row.
@@ -84,22 +94,24 @@ struct PfCfg {
     static_assert(O_COL + OBUF * DH <= 512, "TMEM budget");
     static_assert(SMEM <= 232448, "shared memory budget");
     static_assert(STATS_OFF % 8 == 0 && STAGE_OFF % 16 == 0, "vector accesses");
+    static_assert(KDIMS % 64 == 0 && VROWS % 16 == 0 && K_BYTES % 1024 == 0 && V_BYTES % 1024 == 0, "pieces");
 };
 
-template <int DH, bool BF16>
-__global__ void __launch_bounds__(PfCfg<DH>::THREADS, 1) attn_prefill_kernel(const __grid_constant__ PrefillArgs a) {
-    using C = PfCfg<DH>;
-    constexpr int BM = C::BM, BN = C::BN, KST = C::KST, VST = C::VST, OBUF = C::OBUF;
+template <int DH, int BN_, bool BF16>
+__global__ void __launch_bounds__(PfCfg<DH, BN_>::THREADS, 1) attn_prefill_kernel(const __grid_constant__ PrefillArgs a) {
+    using C = PfCfg<DH, BN_>;
+    constexpr int BM = C::BM, BN = C::BN, KRING = C::KRING, VRING = C::VRING, OBUF = C::OBUF;
+    constexpr int KP = C::KP, VP = C::VP;
     extern __shared__ unsigned char smem_raw[];
     unsigned char* smem = (unsigned char*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     uint64_t* bars = (uint64_t*)(smem + C::BAR_OFF);
     uint64_t* q_full = bars;
     uint64_t* q_empty = q_full + 1;  // completes once per unit: its last S has read Q
     uint64_t* k_full = q_empty + 1;
-    uint64_t* k_empty = k_full + KST;
-    uint64_t* v_full = k_empty + KST;
-    uint64_t* v_empty = v_full + VST;
-    uint64_t* s_full = v_empty + VST;  // [2]
+    uint64_t* k_empty = k_full + KRING;
+    uint64_t* v_full = k_empty + KRING;
+    uint64_t* v_empty = v_full + VRING;
+    uint64_t* s_full = v_empty + VRING;  // [2]
     // p_full[b] completes once per block of parity b: the softmax can never be
     // two phases ahead of the MMA thread's wait on it.
     uint64_t* p_full = s_full + 2;    // [2]
@@ -118,11 +130,11 @@ __global__ void __launch_bounds__(PfCfg<DH>::THREADS, 1) attn_prefill_kernel(con
     if (threadIdx.x == 0) {
         dev::mbar_init(q_full, 1);
         dev::mbar_init(q_empty, 1);
-        for (int s = 0; s < KST; ++s) {
+        for (int s = 0; s < KRING; ++s) {
             dev::mbar_init(&k_full[s], 1);
             dev::mbar_init(&k_empty[s], 1);
         }
-        for (int s = 0; s < VST; ++s) {
+        for (int s = 0; s < VRING; ++s) {
             dev::mbar_init(&v_full[s], 1);
             dev::mbar_init(&v_empty[s], 1);
         }
@@ -186,17 +198,22 @@ __global__ void __launch_bounds__(PfCfg<DH>::THREADS, 1) attn_prefill_kernel(con
 #pragma unroll
                         for (int c = 0; c < DH / 64; ++c) dev::tma_prefetch_3d(&a.tm_q, c * 64, nx.h, (int32_t)nx.t0);
                 }
-                for (int i = 0; i < w.nblk; ++i, ++g) {
-                    const int s = g % KST;
-                    if (g >= KST && !wait(&k_empty[s], ((g / KST) - 1) & 1)) {
-                        ok = false;
-                        break;
-                    }
-                    dev::mbar_arrive_expect_tx(&k_full[s], C::K_BYTES);
+                for (int i = 0; ok && i < w.nblk; ++i, ++g) {
                     const int32_t row = kv_row(w, i);
+#pragma unroll 1
+                    for (int p = 0; p < KP; ++p) {
+                        const uint32_t gp = g * KP + p;  // K pieces loaded so far
+                        const int s = gp % KRING;
+                        if (gp >= KRING && !wait(&k_empty[s], ((gp / KRING) - 1) & 1)) {
+                            ok = false;
+                            break;
+                        }
+                        dev::mbar_arrive_expect_tx(&k_full[s], C::K_BYTES);
 #pragma unroll
-                    for (int c = 0; c < DH / 64; ++c)
-                        dev::tma_load_2d(smem + C::K_OFF + s * C::K_BYTES + c * BN * 128, &a.tm_k, c * 64, row, &k_full[s]);
+                        for (int c = 0; c < C::KDIMS / 64; ++c)
+                            dev::tma_load_2d(smem + C::K_OFF + s * C::K_BYTES + c * BN * 128, &a.tm_k,
+                                             p * C::KDIMS + c * 64, row, &k_full[s]);
+                    }
                 }
                 ++kn;
             }
@@ -208,17 +225,22 @@ __global__ void __launch_bounds__(PfCfg<DH>::THREADS, 1) attn_prefill_kernel(con
             uint32_t g = 0;
             bool ok = true;
             for (int k = 0; ok && decode_work<BM, BN>(a, k, w); ++k) {
-                for (int i = 0; i < w.nblk; ++i, ++g) {
-                    const int s = g % VST;
-                    if (g >= VST && !wait(&v_empty[s], ((g / VST) - 1) & 1)) {
-                        ok = false;
-                        break;
-                    }
-                    dev::mbar_arrive_expect_tx(&v_full[s], C::V_BYTES);
+                for (int i = 0; ok && i < w.nblk; ++i, ++g) {
                     const int32_t row = kv_row(w, i);
+#pragma unroll 1
+                    for (int p = 0; p < VP; ++p) {
+                        const uint32_t gp = g * VP + p;  // V pieces loaded so far
+                        const int s = gp % VRING;
+                        if (gp >= VRING && !wait(&v_empty[s], ((gp / VRING) - 1) & 1)) {
+                            ok = false;
+                            break;
+                        }
+                        dev::mbar_arrive_expect_tx(&v_full[s], C::V_BYTES);
 #pragma unroll
-                    for (int c = 0; c < DH / 64; ++c)
-                        dev::tma_load_2d(smem + C::V_OFF + s * C::V_BYTES + c * BN * 128, &a.tm_v, c * 64, row, &v_full[s]);
+                        for (int c = 0; c < DH / 64; ++c)
+                            dev::tma_load_2d(smem + C::V_OFF + s * C::V_BYTES + c * C::VROWS * 128, &a.tm_v, c * 64,
+                                             row + p * C::VROWS, &v_full[s]);
+                    }
                 }
             }
         }
@@ -232,24 +254,30 @@ __global__ void __launch_bounds__(PfCfg<DH>::THREADS, 1) attn_prefill_kernel(con
             // Descriptors are built once; each MMA only advances a start address.
             const uint64_t q_desc = tc::smem_desc_sw128(sbase + C::Q_OFF, 16, 1024);
             const uint64_t k_desc = tc::smem_desc_sw128(sbase + C::K_OFF, 16, 1024);
-            const uint64_t v_desc = tc::smem_desc_sw128(sbase + C::V_OFF, BN * 128, 1024);
+            const uint64_t v_desc = tc::smem_desc_sw128(sbase + C::V_OFF, C::VROWS * 128, 1024);
             // P_gg . V_gg into O buffer ob; `first` starts the accumulator, the
             // unit's last P.V completes o_final[ob] instead of o_done.
             auto issue_pv = [&](uint32_t gg, bool first, bool last, int ob, int use) -> bool {
-                const int s = gg % VST;
                 if (!wait(&p_full[gg & 1], (gg >> 1) & 1)) return false;
-                if (!wait(&v_full[s], (gg / VST) & 1)) return false;
                 // the epilogue of the buffer's previous unit has read O
                 if (first && use >= 1 && !wait(&o_free[ob], (use - 1) & 1)) return false;
-                tc::fence_after_sync();
                 const uint32_t p_tmem = tmem + (gg & 1) * BN;  // P overwrote S, 2 values per column
-                const uint64_t vs = tc::desc_advance(v_desc, s * C::V_BYTES);
 #pragma unroll
-                for (int k = 0; k < BN / 16; ++k)
-                    tc::mma_f16_ts(tmem + C::O_COL + ob * DH, p_tmem + k * 8, tc::desc_advance(vs, k * 2048), idesc_o,
-                                   (!first || k > 0) ? 1u : 0u);
+                for (int p = 0; p < VP; ++p) {
+                    const uint32_t gp = gg * VP + p;
+                    const int s = gp % VRING;
+                    if (!wait(&v_full[s], (gp / VRING) & 1)) return false;
+                    tc::fence_after_sync();
+                    const uint64_t vs = tc::desc_advance(v_desc, s * C::V_BYTES);
+#pragma unroll
+                    for (int kq = 0; kq < C::VROWS / 16; ++kq) {
+                        const int k = p * (C::VROWS / 16) + kq;  // 16-key step of the block
+                        tc::mma_f16_ts(tmem + C::O_COL + ob * DH, p_tmem + k * 8, tc::desc_advance(vs, kq * 2048),
+                                       idesc_o, (!first || k > 0) ? 1u : 0u);
+                    }
+                    tc::commit(&v_empty[s]);
+                }
                 tc::commit(last ? &o_final[ob] : o_done);
-                tc::commit(&v_empty[s]);
                 return true;
             };
             // One stream over all units: S_g, then P_{g-1}.V, so the next
@@ -265,22 +293,31 @@ __global__ void __launch_bounds__(PfCfg<DH>::THREADS, 1) attn_prefill_kernel(con
                 if (w.nblk <= 0) continue;
                 const int ob = kn % OBUF, use = kn / OBUF;
                 if (!wait(q_full, kn & 1)) break;
-                for (int i = 0; i < w.nblk; ++i, ++g) {
-                    const int s = g % KST, sb = g & 1;
-                    if (!wait(&k_full[s], (g / KST) & 1)) {
-                        ok = false;
-                        break;
-                    }
-                    tc::fence_after_sync();
+                for (int i = 0; ok && i < w.nblk; ++i, ++g) {
+                    const int sb = g & 1;
                     // S_g overwrites buffer sb, which held P_{g-2}; P_{g-2}.V was issued
                     // earlier and the tensor pipe executes in order.
-                    const uint64_t ks = tc::desc_advance(k_desc, s * C::K_BYTES);
 #pragma unroll
-                    for (int kk = 0; kk < DH / 16; ++kk)
-                        tc::mma_f16_ss(tmem + sb * BN, tc::desc_advance(q_desc, (kk / 4) * BM * 128 + (kk % 4) * 32),
-                                       tc::desc_advance(ks, (kk / 4) * BN * 128 + (kk % 4) * 32), idesc_s, kk > 0 ? 1u : 0u);
+                    for (int p = 0; p < KP; ++p) {
+                        const uint32_t gp = g * KP + p;
+                        const int s = gp % KRING;
+                        if (!wait(&k_full[s], (gp / KRING) & 1)) {
+                            ok = false;
+                            break;
+                        }
+                        tc::fence_after_sync();
+                        const uint64_t ks = tc::desc_advance(k_desc, s * C::K_BYTES);
+#pragma unroll
+                        for (int kq = 0; kq < C::KDIMS / 16; ++kq) {
+                            const int kk = p * (C::KDIMS / 16) + kq;  // 16-dimension step of the head
+                            tc::mma_f16_ss(tmem + sb * BN, tc::desc_advance(q_desc, (kk / 4) * BM * 128 + (kk % 4) * 32),
+                                           tc::desc_advance(ks, (kq / 4) * BN * 128 + (kq % 4) * 32), idesc_s,
+                                           kk > 0 ? 1u : 0u);
+                        }
+                        tc::commit(&k_empty[s]);
+                    }
+                    if (!ok) break;
                     tc::commit(&s_full[sb]);
-                    tc::commit(&k_empty[s]);
                     if (i == w.nblk - 1) tc::commit(q_empty);
                     if (pend && !issue_pv(g - 1, pv_first, pv_last, pv_ob, pv_use)) {
                         ok = false;
@@ -498,10 +535,10 @@ __global__ void __launch_bounds__(PfCfg<DH>::THREADS, 1) attn_prefill_kernel(con
 // ------------------------------------------------------------------ host side
 
 
-template <int DH, bool BF16>
+template <int DH, int BN, bool BF16>
 int launch_prefill(const PrefillArgs& a, dim3 grid, cudaStream_t s) {
-    using C = PfCfg<DH>;
-    auto kern = attn_prefill_kernel<DH, BF16>;
+    using C = PfCfg<DH, BN>;
+    auto kern = attn_prefill_kernel<DH, BN, BF16>;
     static std::atomic<uint64_t> attr_set{0};  // one bit per device
     const int st = set_smem_once(kern, C::SMEM, attr_set);
     if (st != NMG_OK) return st;
@@ -555,11 +592,14 @@ int make_kv_tensor_maps(const nmg_kv_cache* c, int box_rows, CUtensorMap* k, CUt
     return NMG_OK;
 }
 
+// Keys per block of the one-head kernel: 128, or 64 at head_dim 256 when the
+// cache's slots are not a multiple of 128 (a block never straddles a head).
+static int prefill_block_keys(const nmg_kv_cache* c) { return c->dh == 256 && c->slots % 128 != 0 ? 64 : 128; }
+
 bool prefill_supported(const nmg_kv_cache* c, int hq, int q_dtype, int64_t rows) {
     if (c->dtype == NMG_F32 || q_dtype != c->dtype) return false;
     if (c->dh != 64 && c->dh != 128 && c->dh != 256) return false;
-    const int bn = c->dh == 256 ? 64 : 128;
-    if (c->slots % bn != 0) return false;
+    if (c->slots % prefill_block_keys(c) != 0) return false;
     if (rows < 64) return false;
     if ((int64_t)c->hkv * c->slots > 0x7FFFFFFF) return false;
     return encode_tiled_fn() != nullptr;
@@ -593,11 +633,16 @@ int attend_rows_prefill(const nmg_kv_cache* c, int hq, const void* q, int q_dtyp
             return set_error(NMG_CUDA_ERROR, "prefill: Q tensor map (%d)", (int)r);
         }
     }
-    const int bn = dh == 256 ? 64 : 128;
+    // Two query heads of one GQA group a unit (they share every K/V block)
+    // where the group is even; one head a unit otherwise.
+    const bool pair = dh == 128 && (hq / c->hkv) % 2 == 0;
+    const int bn = pair ? 128 : prefill_block_keys(c);
+    // Rows per V copy: a V piece is half a 128-key block at head_dim 256.
+    const int v_rows = !pair && dh == 256 && bn == 128 ? 64 : bn;
     for (int which = 0; which < 2; ++which) {
         cuuint64_t dims[2] = {(cuuint64_t)dh, (cuuint64_t)c->hkv * (cuuint64_t)c->slots};
         cuuint64_t strides[1] = {(cuuint64_t)dh * 2};
-        cuuint32_t box[2] = {64, (cuuint32_t)bn};
+        cuuint32_t box[2] = {64, (cuuint32_t)(which ? v_rows : bn)};
         cuuint32_t es[2] = {1, 1};
         const CUtensorMapDataType wdt = which ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : dt;
         CUresult r = enc(which ? &a->tm_v : &a->tm_k, wdt, 2, which ? c->v : c->k, dims, strides, box, es,
@@ -618,9 +663,6 @@ int attend_rows_prefill(const nmg_kv_cache* c, int hq, const void* q, int q_dtyp
     a->hq = hq;
     a->hkv = c->hkv;
     a->g = hq / c->hkv;
-    // Two query heads of one GQA group a unit (they share every K/V block)
-    // where the group is even; one head a unit otherwise.
-    const bool pair = dh == 128 && a->g % 2 == 0;
     a->hunits = pair ? hq / 2 : hq;
     a->scale_log2 = scale * 1.4426950408889634f;
     // Key splits when one CTA per query tile would leave the GPU's 148 SMs
@@ -703,11 +745,17 @@ int attend_rows_prefill(const nmg_kv_cache* c, int hq, const void* q, int q_dtyp
         if (pair)
             st = launch_prefill_pair(*a, dh, c->dtype == NMG_BF16, grid, stream);
         else if (dh == 64)
-            st = c->dtype == NMG_BF16 ? launch_prefill<64, true>(*a, grid, stream) : launch_prefill<64, false>(*a, grid, stream);
+            st = c->dtype == NMG_BF16 ? launch_prefill<64, 128, true>(*a, grid, stream)
+                                      : launch_prefill<64, 128, false>(*a, grid, stream);
         else if (dh == 128)
-            st = c->dtype == NMG_BF16 ? launch_prefill<128, true>(*a, grid, stream) : launch_prefill<128, false>(*a, grid, stream);
+            st = c->dtype == NMG_BF16 ? launch_prefill<128, 128, true>(*a, grid, stream)
+                                      : launch_prefill<128, 128, false>(*a, grid, stream);
+        else if (bn == 128)
+            st = c->dtype == NMG_BF16 ? launch_prefill<256, 128, true>(*a, grid, stream)
+                                      : launch_prefill<256, 128, false>(*a, grid, stream);
         else
-            st = c->dtype == NMG_BF16 ? launch_prefill<256, true>(*a, grid, stream) : launch_prefill<256, false>(*a, grid, stream);
+            st = c->dtype == NMG_BF16 ? launch_prefill<256, 64, true>(*a, grid, stream)
+                                      : launch_prefill<256, 64, false>(*a, grid, stream);
     }
     delete a;
     return st;

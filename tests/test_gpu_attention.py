@@ -442,6 +442,22 @@ def test_prefill_head_dim_256_window_many_units(dev):
         assert_close(out[r0:r1], want, what=f"rows {r0}:{r1}")
 
 
+@pytest.mark.parametrize("dtype,slots,window", [("bf16", 1856, 256), ("f16", 1856, 0), ("f16", 1920, 700)])
+def test_prefill_head_dim_256_block_sizes(dev, dtype, slots, window):
+    # head_dim 256 runs 128-key blocks (K in four 64-dimension pieces, V in two
+    # 64-key pieces) when the cache's slots are a multiple of 128, and 64-key
+    # blocks otherwise (1856 = 29 x 64); both against the oracle.
+    hq, hkv, dh, S = 8, 4, 256, 1500
+    k, v, q = rnd(dtype, 44, 1, (S, hkv * dh)), rnd(dtype, 44, 2, (S, hkv * dh)), rnd(dtype, 44, 3, (S, hq * dh))
+    cache = (nm.LocalAttentionCache(hkv, dh, window, capacity=slots, dtype=dtype) if window
+             else nm.FullAttentionCache(hkv, dh, capacity=slots, dtype=dtype))
+    out = nm.append_attend(cache, 0, TD(k, dev, dtype), TD(v, dev, dtype), TD(q, dev, dtype), None,
+                           out_dtype=torch.float32).cpu().numpy()
+    for r0, r1 in ((0, 192), (640, 800), (S - 200, S)):
+        want = oracle.attend(k[:r1], v[:r1], 0, window, hkv, dh, q[r0:r1], hq, r0, use_scale=False)
+        assert_close(out[r0:r1], want, what=f"{dtype} slots {slots} rows {r0}:{r1}")
+
+
 @pytest.mark.parametrize("dtype,window", [("bf16", 0), ("f16", 0), ("bf16", 200)])
 def test_prefill_head_dim_64_matches_oracle(dev, dtype, window):
     # head_dim 64 through the tensor-core kernel (128-key blocks, P.V with N = 64).
