@@ -8,8 +8,10 @@
 //
 //   warp 0      TMA producer for Q (one tile per unit; the next unit's tile
 //               is prefetched into L2) and K blocks (3-stage ring; a K stage
-//               is released as soon as its S MMA completes)
-//   warp 2      TMA producer for V blocks (2-stage ring, released after P.V)
+//               is released as soon as its S MMA completes; at head_dim 256
+//               a ring of four 64-dimension pieces, one block)
+//   warp 2      TMA producer for V blocks (2-stage ring, released after P.V;
+//               at head_dim 256 two 64-key pieces, one block)
 //               (cp.async.bulk.tensor, 128-byte swizzle, one CTA per copy)
 //   warp 1      allocates TMEM and issues tcgen05.mma from one thread, one
 //               stream over all units:
