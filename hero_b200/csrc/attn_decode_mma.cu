@@ -47,7 +47,7 @@ struct Q8Src {
 struct MmaArgs {
     CUtensorMap tm_k[kMmaMaxBatch];  // K of each distinct cache, (d, hkv*slots)
     CUtensorMap tm_v[kMmaMaxBatch];
-    Q8Src q8[kMmaMaxBatch];          // the same caches when they are Q8_0 (no tensor maps then)
+    Q8Src q8[kMmaMaxBatch];          // the same caches when they are Q8_0 (tensor maps of the quants at head_dim 128)
     int q_dtype;                     // Q8_0 caches: the query's dtype, staged as fp16
     int hn;                          // 1: heads in the MMA's N (subgroups of 8 heads), 0: in M (16)
     int cl;                          // > 1: every row has cl splits, one thread-block cluster, merged
@@ -109,19 +109,26 @@ __device__ __forceinline__ bool mma_row(const MmaArgs& a, int64_t w, MmaRow& r) 
     return r.s < r.nsplit;
 }
 
-template <int DH, bool Q8 = false>
+// Q8_0 tiles at head_dim 128 with the heads in N become MMA fragments in
+// registers, straight from the quants (no fp16 copy of the tile).
+constexpr bool q8_in_registers(int dh, bool q8, bool hn) { return q8 && hn && dh == 128; }
+
+template <int DH, bool Q8 = false, bool Q8R = false>
 struct MmaCfg {
     // head_dim 256: one stage, so two CTAs fit an SM and overlap each other's
     // loads (measured: sliding-window decode 24.8 -> 18.6 us, global 372 -> 362 us
-    // against two stages at one CTA per SM)
-    static constexpr int STAGES = Q8 ? (DH <= 128 ? 4 : 2) : (DH <= 128 ? 3 : 1);
+    // against two stages at one CTA per SM).  Q8_0 tiles read in registers:
+    // two stages, so four CTAs (128 registers each) share an SM (config-5
+    // shape: 2.16 ms with four stages at three CTAs per SM, 1.92 ms with two
+    // at four, 2.03 ms with five at 96 registers)
+    static constexpr int STAGES = Q8R ? 2 : Q8 ? (DH <= 128 ? 4 : 2) : (DH <= 128 ? 3 : 1);
     static constexpr int TILE_BYTES = KT * DH * 2;  // one of K or V as fp16 / bf16
     // Q8_0: a stage holds the raw tile (K quants, V quants, K scales, V scales);
     // the fp16 K and V tiles the MMAs read are one buffer after the stages.
     static constexpr int Q8_QBYTES = KT * DH, Q8_SBYTES = KT * (DH / 32) * 2;
     static constexpr int STAGE_BYTES = Q8 ? 2 * (Q8_QBYTES + Q8_SBYTES) : 2 * TILE_BYTES;
-    static constexpr int F16_OFF = STAGES * STAGE_BYTES;  // Q8_0 only
-    static constexpr int LOAD_END = Q8 ? F16_OFF + 2 * TILE_BYTES : STAGES * STAGE_BYTES;
+    static constexpr int F16_OFF = STAGES * STAGE_BYTES;  // Q8_0 converted through shared memory only
+    static constexpr int LOAD_END = Q8 && !Q8R ? F16_OFF + 2 * TILE_BYTES : STAGES * STAGE_BYTES;
     // The warp merge ([4][16][DH + 2] fp32) reuses the stage memory, idle by then.
     static constexpr int MERGE_BYTES = (4 * 16 * (DH + 2) * 4 + 1023) / 1024 * 1024;
     static constexpr int Q_OFF = LOAD_END > MERGE_BYTES ? LOAD_END : MERGE_BYTES;  // 16 x DH query rows
@@ -133,6 +140,8 @@ struct MmaCfg {
     static_assert(8 * (DH + 2) * 4 <= 16 * Q_PITCH, "a cluster-merge partial of 8 heads fits the staged-q region");
     static_assert(!Q8 || (Q8_QBYTES % 16 == 0 && Q8_SBYTES % 16 == 0 && F16_OFF % 1024 == 0),
                   "bulk copies move 16-byte multiples; the fp16 tiles keep the 128-byte swizzle atoms aligned");
+    static_assert(!Q8R || (DH == 128 && Q8_QBYTES % 1024 == 0 && STAGE_BYTES % 1024 == 0),
+                  "the swizzled quant tiles start on 1024-byte boundaries, one 128-byte row per key");
 };
 
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
@@ -187,7 +196,8 @@ __device__ __forceinline__ uint32_t tile_off(int key, int chunk) {
 // 15 of 16 rows and the O accumulator is half the size.
 template <int DH, bool BF16, bool Q8 = false, bool HN = false>
 __global__ void __launch_bounds__(128) attn_decode_mma_kernel(const __grid_constant__ MmaArgs a) {
-    using C = MmaCfg<DH, Q8>;
+    constexpr bool Q8R = q8_in_registers(DH, Q8, HN);
+    using C = MmaCfg<DH, Q8, Q8R>;
     constexpr int ST = C::STAGES;
     extern __shared__ unsigned char smem_raw[];
     unsigned char* smem = (unsigned char*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -217,7 +227,7 @@ __global__ void __launch_bounds__(128) attn_decode_mma_kernel(const __grid_const
     if (tid == 0) {
         for (int s = 0; s < (SPLIT ? 2 : ST); ++s) dev::mbar_init(&full[s], 1);
         dev::fence_mbar_init();
-        if constexpr (!Q8) {
+        if constexpr (!Q8 || Q8R) {
             dev::prefetch_tensormap(tmk);
             dev::prefetch_tensormap(tmv);
         }
@@ -258,8 +268,13 @@ __global__ void __launch_bounds__(128) attn_decode_mma_kernel(const __grid_const
                 // (the buffers carry 64 spare rows past the last head).
                 const Q8Src& q8 = a.q8[r.map];
                 unsigned char* dst = smem + st * C::STAGE_BYTES;
-                dev::bulk_g2s(dst, q8.k + (int64_t)row * DH, C::Q8_QBYTES, &full[st]);
-                dev::bulk_g2s(dst + C::Q8_QBYTES, q8.v + (int64_t)row * DH, C::Q8_QBYTES, &full[st]);
+                if constexpr (Q8R) {  // quants through the 128-byte swizzle: one 128-byte row per key
+                    dev::tma_load_2d(dst, tmk, 0, row, &full[st]);
+                    dev::tma_load_2d(dst + C::Q8_QBYTES, tmv, 0, row, &full[st]);
+                } else {
+                    dev::bulk_g2s(dst, q8.k + (int64_t)row * DH, C::Q8_QBYTES, &full[st]);
+                    dev::bulk_g2s(dst + C::Q8_QBYTES, q8.v + (int64_t)row * DH, C::Q8_QBYTES, &full[st]);
+                }
                 const int64_t srow = (int64_t)h * q8.sstride + u0 % r.slots;
                 dev::bulk_g2s(dst + 2 * C::Q8_QBYTES, q8.ks + srow * (DH / 32), C::Q8_SBYTES, &full[st]);
                 dev::bulk_g2s(dst + 2 * C::Q8_QBYTES + C::Q8_SBYTES, q8.vs + srow * (DH / 32), C::Q8_SBYTES, &full[st]);
@@ -292,7 +307,21 @@ __global__ void __launch_bounds__(128) attn_decode_mma_kernel(const __grid_const
     // 2*(lane%4) (+1, +8, +9) -- straight 32-bit reads of the staged rows.
     uint32_t qa[DH / 16][4];
     uint32_t qb[DH / 16][2];
-    if constexpr (HN) {
+    if constexpr (Q8R) {
+        // The K fragments below take each lane's 8 consecutive quants of a
+        // 32-value block as MMA columns 2q, 2q+1, 2q+8, 2q+9 of two k16 steps
+        // (q = lane % 4): the query's dimensions are permuted to match, one
+        // 16-byte read per block.
+        const unsigned char* qrow = smem + C::Q_OFF + (lane >> 2) * C::Q_PITCH;
+#pragma unroll
+        for (int b = 0; b < DH / 32; ++b) {
+            const uint4 w = *(const uint4*)(qrow + (32 * b + 8 * (lane & 3)) * 2);
+            qb[2 * b][0] = w.x;
+            qb[2 * b][1] = w.y;
+            qb[2 * b + 1][0] = w.z;
+            qb[2 * b + 1][1] = w.w;
+        }
+    } else if constexpr (HN) {
         const unsigned char* qrow = smem + C::Q_OFF + (lane >> 2) * C::Q_PITCH;
 #pragma unroll
         for (int kk = 0; kk < DH / 16; ++kk) {
@@ -334,7 +363,7 @@ __global__ void __launch_bounds__(128) attn_decode_mma_kernel(const __grid_const
             break;
         }
         uint32_t kbase = dev::smem_u32(smem + st * C::STAGE_BYTES);
-        if constexpr (Q8) {
+        if constexpr (Q8 && !Q8R) {
             // scale * quant of every K and V value of the tile, as fp16 into the
             // swizzled layout the MMA loop reads; 8 values (one 16-byte chunk)
             // at a time, consecutive threads on consecutive chunks of a row.
@@ -369,7 +398,44 @@ __global__ void __launch_bounds__(128) attn_decode_mma_kernel(const __grid_const
         const int key0 = wid * 16;  // this warp's keys within the tile
 
         float st4[4] = {0.f, 0.f, 0.f, 0.f};  // HN: S^T[16 keys x 8 heads]
-        if constexpr (HN) {
+        [[maybe_unused]] const __half2 q8_bias = __float2half2_rn(1152.f);
+        if constexpr (Q8R) {
+            // A = K[16 keys x 16 dims] from the quants: lane (g, q) reads 8
+            // quants of keys g and g + 8 per 32-value block (one 8-byte load
+            // each, conflict-free under the swizzle), turns them into fp16
+            // scale * quant exactly as the shared-memory conversion does, and
+            // feeds two k16 steps.
+            const unsigned char* stg = smem + st * C::STAGE_BYTES;
+            const unsigned char* ksc = stg + 2 * C::Q8_QBYTES;
+            const int g = lane >> 2, qd = lane & 3, ra = key0 + g;
+            const uint2 sa = *(const uint2*)(ksc + ra * (DH / 32) * 2);        // 4 fp16 scales of key ra
+            const uint2 sb = *(const uint2*)(ksc + (ra + 8) * (DH / 32) * 2);  // and of key ra + 8
+#pragma unroll
+            for (int b = 0; b < DH / 32; ++b) {
+                const uint32_t off = (uint32_t)ra * 128 + ((((2 * b + (qd >> 1)) ^ (ra & 7))) << 4) + (qd & 1) * 8;
+                const uint2 wa = *(const uint2*)(stg + off), wb = *(const uint2*)(stg + off + 8 * 128);
+                const uint32_t sel = (b & 1) ? 0x3232u : 0x1010u;
+                const uint32_t s2a = __byte_perm(b < 2 ? sa.x : sa.y, 0, sel);
+                const uint32_t s2b = __byte_perm(b < 2 ? sb.x : sb.y, 0, sel);
+                const __half2 sca = *reinterpret_cast<const __half2*>(&s2a);
+                const __half2 scb = *reinterpret_cast<const __half2*>(&s2b);
+                auto deq = [&](uint32_t x, uint32_t pick, __half2 sc) -> uint32_t {
+                    const uint32_t biased = __byte_perm(x, 0x64646464u, pick);
+                    const __half2 v = __hmul2(__hsub2(*reinterpret_cast<const __half2*>(&biased), q8_bias), sc);
+                    return *reinterpret_cast<const uint32_t*>(&v);
+                };
+#pragma unroll
+                for (int h2 = 0; h2 < 2; ++h2) {  // k16 steps 2b and 2b + 1
+                    const uint32_t xa = (h2 ? wa.y : wa.x) ^ 0x80808080u, xb = (h2 ? wb.y : wb.x) ^ 0x80808080u;
+                    uint32_t ka[4];
+                    ka[0] = deq(xa, 0x4140u, sca);  // key g,     columns 2q, 2q+1
+                    ka[1] = deq(xb, 0x4140u, scb);  // key g + 8
+                    ka[2] = deq(xa, 0x4342u, sca);  // key g,     columns 2q+8, 2q+9
+                    ka[3] = deq(xb, 0x4342u, scb);  // key g + 8
+                    mma_16816<false>(st4, ka, qb[2 * b + h2][0], qb[2 * b + h2][1]);
+                }
+            }
+        } else if constexpr (HN) {
 #pragma unroll
             for (int kk = 0; kk < DH / 16; ++kk) {
                 // A = K[16 keys x 16 dims]: (keys 0-7, d lo), (keys 8-15, d lo), (keys 0-7, d hi), (keys 8-15, d hi)
@@ -505,7 +571,52 @@ __global__ void __launch_bounds__(128) attn_decode_mma_kernel(const __grid_const
                 break;
             }
         }
-        if constexpr (HN) {
+        if constexpr (Q8R) {
+            // A = V^T[16 dims x 16 keys] from the quants.  Lane (g, q) reads the
+            // 4 quants at dims 32p + 4g .. + 3 of keys 2q, 2q+1, 2q+8, 2q+9 (one
+            // 32-bit load each, conflict-free under the swizzle): bytes 0 and 1
+            // are rows g and g + 8 of dim tile 2p, bytes 2 and 3 those of tile
+            // 2p + 1 -- the O^T rows carry that dimension order into the merge.
+            const unsigned char* stg = smem + st * C::STAGE_BYTES;
+            const unsigned char* vqt = stg + C::Q8_QBYTES;
+            const unsigned char* vsc = stg + 2 * C::Q8_QBYTES + C::Q8_SBYTES;
+            const int g = lane >> 2, k0 = key0 + 2 * (lane & 3);
+            uint2 s4[4];  // 4 fp16 scales of keys k0, k0 + 1, k0 + 8, k0 + 9
+#pragma unroll
+            for (int i = 0; i < 4; ++i) s4[i] = *(const uint2*)(vsc + (k0 + (i & 1) + 8 * (i >> 1)) * (DH / 32) * 2);
+#pragma unroll
+            for (int p = 0; p < DH / 32; ++p) {
+                const int c = 2 * p + (g >> 2);
+                const uint32_t o0 = (uint32_t)k0 * 128 + ((c ^ (k0 & 7)) << 4) + (g & 3) * 4;
+                const uint32_t o1 = (uint32_t)(k0 + 1) * 128 + ((c ^ ((k0 + 1) & 7)) << 4) + (g & 3) * 4;
+                const uint32_t x0 = *(const uint32_t*)(vqt + o0) ^ 0x80808080u;
+                const uint32_t x1 = *(const uint32_t*)(vqt + o1) ^ 0x80808080u;
+                const uint32_t x2 = *(const uint32_t*)(vqt + o0 + 8 * 128) ^ 0x80808080u;
+                const uint32_t x3 = *(const uint32_t*)(vqt + o1 + 8 * 128) ^ 0x80808080u;
+                const uint32_t ssel = (p & 1) ? 0x7632u : 0x5410u;
+                const uint32_t s01 = __byte_perm(p < 2 ? s4[0].x : s4[0].y, p < 2 ? s4[1].x : s4[1].y, ssel);
+                const uint32_t s23 = __byte_perm(p < 2 ? s4[2].x : s4[2].y, p < 2 ? s4[3].x : s4[3].y, ssel);
+                const __half2 sc01 = *reinterpret_cast<const __half2*>(&s01);
+                const __half2 sc23 = *reinterpret_cast<const __half2*>(&s23);
+                auto deq = [&](uint32_t x, uint32_t pick, __half2 sc) -> uint32_t {
+                    const uint32_t biased = __byte_perm(x, 0x64646464u, pick);
+                    const __half2 v = __hmul2(__hsub2(*reinterpret_cast<const __half2*>(&biased), q8_bias), sc);
+                    return *reinterpret_cast<const uint32_t*>(&v);
+                };
+#pragma unroll
+                for (int j = 0; j < 2; ++j) {  // dim tiles 2p (bytes 0, 1) and 2p + 1 (bytes 2, 3)
+                    // the two keys of a pair side by side: byte i of key k0 next to byte i of key k0 + 1
+                    const uint32_t i01 = __byte_perm(x0, x1, j ? 0x7362u : 0x5140u);
+                    const uint32_t i23 = __byte_perm(x2, x3, j ? 0x7362u : 0x5140u);
+                    uint32_t va[4];
+                    va[0] = deq(i01, 0x4140u, sc01);  // row g,     keys 2q, 2q+1
+                    va[1] = deq(i01, 0x4342u, sc01);  // row g + 8
+                    va[2] = deq(i23, 0x4140u, sc23);  // row g,     keys 2q+8, 2q+9
+                    va[3] = deq(i23, 0x4342u, sc23);  // row g + 8
+                    mma_16816<false>(o[2 * p + j], va, pfrag[0], pfrag[1]);
+                }
+            }
+        } else if constexpr (HN) {
             // O^T += V^T P^T: per 16 dims one ldmatrix.trans (x4) of V and one MMA.
 #pragma unroll
             for (int dd = 0; dd < NO; ++dd) {
@@ -554,10 +665,13 @@ __global__ void __launch_bounds__(128) attn_decode_mma_kernel(const __grid_const
         const int h0 = 2 * (lane & 3), d0 = lane >> 2;
 #pragma unroll
         for (int dd = 0; dd < NO; ++dd) {
-            cw[h0 * (DH + 2) + 16 * dd + d0] = o[dd][0];
-            cw[(h0 + 1) * (DH + 2) + 16 * dd + d0] = o[dd][1];
-            cw[h0 * (DH + 2) + 16 * dd + d0 + 8] = o[dd][2];
-            cw[(h0 + 1) * (DH + 2) + 16 * dd + d0 + 8] = o[dd][3];
+            // dims of rows d0 and d0 + 8 of tile dd (Q8R: 32p + 4 d0 + 2j (+1), dd = 2p + j)
+            const int dlo = Q8R ? 32 * (dd >> 1) + 4 * d0 + 2 * (dd & 1) : 16 * dd + d0;
+            const int dhi = Q8R ? dlo + 1 : dlo + 8;
+            cw[h0 * (DH + 2) + dlo] = o[dd][0];
+            cw[(h0 + 1) * (DH + 2) + dlo] = o[dd][1];
+            cw[h0 * (DH + 2) + dhi] = o[dd][2];
+            cw[(h0 + 1) * (DH + 2) + dhi] = o[dd][3];
         }
         if (d0 == 0) {
             cw[h0 * (DH + 2) + DH] = m_r[0];
@@ -680,7 +794,7 @@ __global__ void __launch_bounds__(128) attn_decode_mma_kernel(const __grid_const
 
 template <int DH, bool BF16, bool Q8, bool HN>
 int launch_mma_hn(const MmaArgs& a, dim3 grid, cudaStream_t s) {
-    using C = MmaCfg<DH, Q8>;
+    using C = MmaCfg<DH, Q8, q8_in_registers(DH, Q8, HN)>;
     auto kern = attn_decode_mma_kernel<DH, BF16, Q8, HN>;
     static std::atomic<uint64_t> attr_set{0};  // one bit per device
     const int st = set_smem_once(kern, C::SMEM, attr_set);
@@ -766,12 +880,31 @@ bool decode_mma_supported(const nmg_kv_cache* c, int q_dtype) {
     return true;
 }
 
+// Tensor maps of a Q8_0 cache's quants at head_dim 128: rows of 128 int8
+// (the 64 spare rows included), 64-row boxes under the 128-byte swizzle.
+static int make_q8_tensor_maps(const nmg_kv_cache* c, CUtensorMap* k, CUtensorMap* v) {
+    EncodeTiledFn enc = encode_tiled_fn();
+    if (!enc) return set_error(NMG_UNSUPPORTED, "cuTensorMapEncodeTiled unavailable");
+    if (((uintptr_t)c->k & 15) || ((uintptr_t)c->v & 15)) return set_error(NMG_UNSUPPORTED, "unaligned cache");
+    cuuint64_t dims[2] = {(cuuint64_t)c->dh, (cuuint64_t)c->hkv * (cuuint64_t)c->slots + 64};
+    cuuint64_t strides[1] = {(cuuint64_t)c->dh};
+    cuuint32_t box[2] = {128u, (cuuint32_t)KT};
+    cuuint32_t estr[2] = {1, 1};
+    for (int which = 0; which < 2; ++which) {
+        const CUresult r = enc(which ? v : k, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, which ? c->v : c->k, dims, strides, box,
+                               estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (r != CUDA_SUCCESS) return set_error(NMG_CUDA_ERROR, "Q8_0 quant tensor map (%d)", (int)r);
+    }
+    return NMG_OK;
+}
+
 // Where the kernel reads cache i: tensor maps of a 16-bit cache, raw pointers of a Q8_0 one.
 static int kv_sources(const nmg_kv_cache* c, MmaArgs* a, int i) {
     if (c->dtype == NMG_Q8_0) {
         a->q8[i] = Q8Src{(const int8_t*)c->k, (const int8_t*)c->v, (const uint16_t*)c->ks, (const uint16_t*)c->vs,
                          c->sstride};
-        return NMG_OK;
+        return c->dh == 128 ? make_q8_tensor_maps(c, &a->tm_k[i], &a->tm_v[i]) : NMG_OK;
     }
     return make_kv_tensor_maps(c, KT, &a->tm_k[i], &a->tm_v[i]);
 }

@@ -91,10 +91,11 @@ def test_batched_decode_config5_shape(dev, q_dtype):
         assert_close(out[b:b + 1], want, what=f"sequence {b} ({L} rows)")
 
 
-@pytest.mark.parametrize("dh,hq,hkv", [(64, 4, 2), (256, 8, 4)])
+@pytest.mark.parametrize("dh,hq,hkv", [(64, 4, 2), (128, 8, 2), (128, 32, 2), (256, 8, 4)])
 def test_rows_and_window_decode(dev, dh, hq, hkv):
     # Several query rows over a wrapped sliding-window Q8_0 cache (scale 1, the
-    # Gemma form), and head dims 64 and 256.
+    # Gemma form), at head dims 64, 128 (groups of 4, fragments built from the
+    # quants in registers, and of 16, converted through shared memory) and 256.
     W, cap, total = 300, 512, 1400
     k, v = _rows(71, total, hkv * dh), _rows(72, total, hkv * dh)
     q = _rows(73, 5, hq * dh, 0.1)
