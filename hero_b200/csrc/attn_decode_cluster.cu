@@ -232,6 +232,19 @@ __global__ void __launch_bounds__(256, 1) attn_cluster_kernel(const __grid_const
     if (tid == 0) {
         for (int s = 0; s < stages; ++s) dev::mbar_init(&full[s], 1);
         dev::fence_mbar_init();
+        // This split's K and V rows towards L2 while the previous kernel
+        // finishes: a hint only (a row that kernel still writes is read again
+        // after the wait below, from L2, where the write lands).
+        if (k_end > k_begin) {
+            const int64_t nk = k_end - k_begin;
+            const int64_t run1 = min(nk, r.slots - slot_begin);
+            dev::bulk_prefetch_l2(kh + slot_begin * DH, (uint32_t)(run1 * C::ROWB));
+            dev::bulk_prefetch_l2(vh + slot_begin * DH, (uint32_t)(run1 * C::ROWB));
+            if (nk > run1) {
+                dev::bulk_prefetch_l2(kh, (uint32_t)((nk - run1) * C::ROWB));
+                dev::bulk_prefetch_l2(vh, (uint32_t)((nk - run1) * C::ROWB));
+            }
+        }
     }
     // Launched with programmatic stream serialisation: everything above
     // overlaps the previous kernel's tail; no input (cache, q) is read before

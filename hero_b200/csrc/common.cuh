@@ -267,6 +267,13 @@ __device__ __forceinline__ void tma_prefetch_3d(const CUtensorMap* map, int32_t 
                  : "memory");
 }
 
+// Prefetch `bytes` of global memory into L2 (address 16-byte aligned, size a
+// multiple of 16).  Only a hint: L2 is where device memory is kept coherent,
+// so a later read still sees whatever a kernel writes there in between.
+__device__ __forceinline__ void bulk_prefetch_l2(const void* gmem, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(gmem), "r"(bytes) : "memory");
+}
+
 // Untiled bulk copy shared -> global in the thread's bulk group; both
 // addresses 16-byte aligned, `bytes` a multiple of 16.
 __device__ __forceinline__ void bulk_s2g(void* gmem_dst, const void* smem_src, uint32_t bytes) {
