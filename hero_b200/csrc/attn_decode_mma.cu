@@ -113,11 +113,13 @@ __device__ __forceinline__ bool mma_row(const MmaArgs& a, int64_t w, MmaRow& r) 
 // registers, straight from the quants (no fp16 copy of the tile).
 constexpr bool q8_in_registers(int dh, bool q8, bool hn) { return q8 && hn && dh == 128; }
 
-template <int DH, bool Q8 = false, bool Q8R = false>
+template <int DH, bool Q8 = false, bool Q8R = false, bool HN = false>
 struct MmaCfg {
-    // head_dim 256: one stage, so two CTAs fit an SM and overlap each other's
-    // loads (measured: sliding-window decode 24.8 -> 18.6 us, global 372 -> 362 us
-    // against two stages at one CTA per SM).  Q8_0 tiles read in registers:
+    // head_dim 256: one stage, so several CTAs fit an SM and overlap each
+    // other's loads (measured: sliding-window decode 24.8 -> 18.6 us, global
+    // 372 -> 362 us against two stages at one CTA per SM; heads in N, whose
+    // merge records and staged query need half the rows, fit three: global
+    // 336 -> 324 us).  Q8_0 tiles read in registers:
     // two stages, so four CTAs (128 registers each) share an SM (config-5
     // shape: 2.16 ms with four stages at three CTAs per SM, 1.92 ms with two
     // at four, 2.03 ms with five at 96 registers)
@@ -129,15 +131,18 @@ struct MmaCfg {
     static constexpr int STAGE_BYTES = Q8 ? 2 * (Q8_QBYTES + Q8_SBYTES) : 2 * TILE_BYTES;
     static constexpr int F16_OFF = STAGES * STAGE_BYTES;  // Q8_0 converted through shared memory only
     static constexpr int LOAD_END = Q8 && !Q8R ? F16_OFF + 2 * TILE_BYTES : STAGES * STAGE_BYTES;
-    // The warp merge ([4][16][DH + 2] fp32) reuses the stage memory, idle by then.
-    static constexpr int MERGE_BYTES = (4 * 16 * (DH + 2) * 4 + 1023) / 1024 * 1024;
-    static constexpr int Q_OFF = LOAD_END > MERGE_BYTES ? LOAD_END : MERGE_BYTES;  // 16 x DH query rows
+    // Query heads per subgroup: rows of the staged query and of each warp's merge record.
+    static constexpr int QR = HN ? 8 : 16;
+    // The warp merge ([4][QR][DH + 2] fp32) and, heads in N, the cluster-merge
+    // partial ([8][DH + 2] fp32, at XP_OFF) reuse the stage memory, idle by then.
+    static constexpr int XP_OFF = 4 * QR * (DH + 2) * 4;
+    static constexpr int MERGE_BYTES = (XP_OFF + (HN ? 8 * (DH + 2) * 4 : 0) + 1023) / 1024 * 1024;
+    static constexpr int Q_OFF = LOAD_END > MERGE_BYTES ? LOAD_END : MERGE_BYTES;  // QR x DH query rows
     static constexpr int Q_PITCH = DH * 2 + 16;                 // bytes per staged query row
     static constexpr int C_OFF = 0;
-    static constexpr int BAR_OFF = Q_OFF + 16 * Q_PITCH;
+    static constexpr int BAR_OFF = Q_OFF + QR * Q_PITCH;
     static constexpr int SMEM = BAR_OFF + 64 + 1024;            // + alignment slack
     static_assert(SMEM <= 232448, "shared memory budget");
-    static_assert(8 * (DH + 2) * 4 <= 16 * Q_PITCH, "a cluster-merge partial of 8 heads fits the staged-q region");
     static_assert(!Q8 || (Q8_QBYTES % 16 == 0 && Q8_SBYTES % 16 == 0 && F16_OFF % 1024 == 0),
                   "bulk copies move 16-byte multiples; the fp16 tiles keep the 128-byte swizzle atoms aligned");
     static_assert(!Q8R || (DH == 128 && Q8_QBYTES % 1024 == 0 && STAGE_BYTES % 1024 == 0),
@@ -197,7 +202,7 @@ __device__ __forceinline__ uint32_t tile_off(int key, int chunk) {
 template <int DH, bool BF16, bool Q8 = false, bool HN = false>
 __global__ void __launch_bounds__(128) attn_decode_mma_kernel(const __grid_constant__ MmaArgs a) {
     constexpr bool Q8R = q8_in_registers(DH, Q8, HN);
-    using C = MmaCfg<DH, Q8, Q8R>;
+    using C = MmaCfg<DH, Q8, Q8R, HN>;
     constexpr int ST = C::STAGES;
     extern __shared__ unsigned char smem_raw[];
     unsigned char* smem = (unsigned char*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -238,7 +243,7 @@ __global__ void __launch_bounds__(128) attn_decode_mma_kernel(const __grid_const
     asm volatile("griddepcontrol.wait;" ::: "memory");
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     // Stage the query heads as 16-bit rows (rows past the group are zero).
-    for (int i = tid; i < 16 * (DH / 8); i += 128) {
+    for (int i = tid; i < C::QR * (DH / 8); i += 128) {
         const int g = i / (DH / 8), c8 = i % (DH / 8);
         uint4 v = make_uint4(0, 0, 0, 0);
         if constexpr (Q8) {  // the query as fp16, from whatever dtype it came in
@@ -654,7 +659,7 @@ __global__ void __launch_bounds__(128) attn_decode_mma_kernel(const __grid_const
 
     // ---- merge the 4 warps: row sums over the lanes that share a row (head),
     // then through shared memory as [head][DH + 2] per warp
-    float* cw = cs + wid * 16 * (DH + 2);
+    float* cw = cs + wid * C::QR * (DH + 2);
     if constexpr (HN) {
 #pragma unroll
         for (int hh = 0; hh < 2; ++hh) {
@@ -705,17 +710,17 @@ __global__ void __launch_bounds__(128) attn_decode_mma_kernel(const __grid_const
 
     const bool single = r.nsplit == 1;
     const bool clm = a.cl > 1;  // cluster merge
-    float* xp = (float*)(smem + C::Q_OFF);  // cluster merge: this CTA's partial [G][DH + 2] (the staged q is done)
+    float* xp = (float*)(smem + C::XP_OFF);  // cluster merge (heads in N): this CTA's partial [G][DH + 2]
     const int64_t cnt_idx = (r.qrow * (int64_t)a.hkv + h) * a.zdim + z;
     float* my_part = a.part + ((((int64_t)blockIdx.x) * a.hkv + h) * a.zdim + z) * (int64_t)(16 * (DH + 2));
     for (int i = tid; i < G * DH; i += 128) {
         const int g = i / DH, d = i % DH;
         float M = -INFINITY;
-        for (int w2 = 0; w2 < 4; ++w2) M = fmaxf(M, cs[(w2 * 16 + g) * (DH + 2) + DH]);
+        for (int w2 = 0; w2 < 4; ++w2) M = fmaxf(M, cs[(w2 * C::QR + g) * (DH + 2) + DH]);
         float L = 0.f, O = 0.f;
         if (M != -INFINITY) {
             for (int w2 = 0; w2 < 4; ++w2) {
-                const float* c = cs + (w2 * 16 + g) * (DH + 2);
+                const float* c = cs + (w2 * C::QR + g) * (DH + 2);
                 if (c[DH] == -INFINITY) continue;
                 const float f = ex2f(c[DH] - M);
                 L += c[DH + 1] * f;
@@ -794,7 +799,7 @@ __global__ void __launch_bounds__(128) attn_decode_mma_kernel(const __grid_const
 
 template <int DH, bool BF16, bool Q8, bool HN>
 int launch_mma_hn(const MmaArgs& a, dim3 grid, cudaStream_t s) {
-    using C = MmaCfg<DH, Q8, q8_in_registers(DH, Q8, HN)>;
+    using C = MmaCfg<DH, Q8, q8_in_registers(DH, Q8, HN), HN>;
     auto kern = attn_decode_mma_kernel<DH, BF16, Q8, HN>;
     static std::atomic<uint64_t> attr_set{0};  // one bit per device
     const int st = set_smem_once(kern, C::SMEM, attr_set);
@@ -846,13 +851,16 @@ int dispatch_mma(const nmg_kv_cache* c, const MmaArgs& a, dim3 grid, cudaStream_
 // Groups of at most 8 query heads put the heads in the MMA's N dimension.
 int mma_heads_in_n(int gtot) { return gtot <= 8 ? 1 : 0; }
 
-int64_t mma_blocks_per_split(int64_t total_blocks) {
+int64_t mma_blocks_per_split(int64_t total_blocks, int dh) {
     // About 6 CTAs per SM of work, at most 128 tiles (8192 keys) per split.
     // Small launches (a sliding window, a short cache) still give each CTA up
-    // to 4 tiles while that leaves a CTA per SM: a CTA of one tile pays its
-    // load latency with nothing to overlap it and adds a split to merge.
+    // to 4 tiles while that leaves a CTA per SM (two at head_dim 256, where
+    // three CTAs share an SM and a launch of one per SM would leave SMs idle:
+    // config-4 window decode 16.0 us at 4 tiles per CTA, 15.1 at 3): a CTA of
+    // one tile pays its load latency with nothing to overlap it and adds a
+    // split to merge.
     int64_t b = total_blocks / (148 * 6);
-    b = std::max<int64_t>(b, std::min<int64_t>(4, total_blocks / 148));
+    b = std::max<int64_t>(b, std::min<int64_t>(4, total_blocks / (148 * (dh == 256 ? 2 : 1))));
     return std::max<int64_t>(1, std::min<int64_t>(128, b));
 }
 
@@ -925,7 +933,7 @@ int attend_rows_mma(const nmg_kv_cache* c, int hq, const void* q, int q_dtype, i
         longest = std::max(longest, nb);
         total_blocks += nb;
     }
-    const int64_t bps = mma_blocks_per_split(total_blocks * c->hkv * zdim);
+    const int64_t bps = mma_blocks_per_split(total_blocks * c->hkv * zdim, c->dh);
     const int64_t max_splits = (longest + bps - 1) / bps;
     const int64_t work = rows * max_splits;
     // every row with the same split count (2..8), heads in N: merge through a cluster
@@ -980,7 +988,7 @@ int attend_batch_mma(const nmg_kv_cache* const* caches, int batch, const int64_t
         spans[b] = visible_span(qpos, c->window, c->oldest, c->newest());
         total_blocks += (spans[b].hi - c->base) / KT - (spans[b].lo - c->base) / KT + 1;
     }
-    const int64_t bps = mma_blocks_per_split(total_blocks * c0->hkv * zdim);
+    const int64_t bps = mma_blocks_per_split(total_blocks * c0->hkv * zdim, c0->dh);
     int64_t all_work = 0;
     std::vector<int32_t> nsplit(batch);
     for (int b = 0; b < batch; ++b) {
