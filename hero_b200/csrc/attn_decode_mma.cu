@@ -242,25 +242,6 @@ __global__ void __launch_bounds__(128) attn_decode_mma_kernel(const __grid_const
     // and the tickets are touched only after its results are visible.
     asm volatile("griddepcontrol.wait;" ::: "memory");
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-    // Stage the query heads as 16-bit rows (rows past the group are zero).
-    for (int i = tid; i < C::QR * (DH / 8); i += 128) {
-        const int g = i / (DH / 8), c8 = i % (DH / 8);
-        uint4 v = make_uint4(0, 0, 0, 0);
-        if constexpr (Q8) {  // the query as fp16, from whatever dtype it came in
-            if (g < G) {
-                const int64_t q0 = (r.qrow * (int64_t)a.hq + qh0 + g) * DH + c8 * 8;
-                uint32_t w[4];
-#pragma unroll
-                for (int u = 0; u < 4; ++u)
-                    w[u] = pack_h2(dev::load_as_f32(a.q, a.q_dtype, q0 + 2 * u), dev::load_as_f32(a.q, a.q_dtype, q0 + 2 * u + 1));
-                v = make_uint4(w[0], w[1], w[2], w[3]);
-            }
-        } else if (g < G) {
-            v = *(const uint4*)((const uint16_t*)a.q + (r.qrow * (int64_t)a.hq + qh0 + g) * DH + c8 * 8);
-        }
-        *(uint4*)(smem + C::Q_OFF + g * C::Q_PITCH + c8 * 16) = v;
-    }
-    __syncthreads();
 
     auto issue = [&](int t, int st) {
         if (tid == 0) {
@@ -306,6 +287,33 @@ __global__ void __launch_bounds__(128) attn_decode_mma_kernel(const __grid_const
                                  &full[which]);
         }
     };
+
+    // The first tiles' copies go out before the query is staged, so their
+    // latency overlaps the query loads (thread 0 initialised the barriers).
+    for (int t = 0; t < ST - 1 && t < ntiles; ++t) issue(t, t);
+    if (SPLIT && ntiles > 0) {
+        issue_half(0, 0);
+        issue_half(0, 1);
+    }
+    // Stage the query heads as 16-bit rows (rows past the group are zero).
+    for (int i = tid; i < C::QR * (DH / 8); i += 128) {
+        const int g = i / (DH / 8), c8 = i % (DH / 8);
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if constexpr (Q8) {  // the query as fp16, from whatever dtype it came in
+            if (g < G) {
+                const int64_t q0 = (r.qrow * (int64_t)a.hq + qh0 + g) * DH + c8 * 8;
+                uint32_t w[4];
+#pragma unroll
+                for (int u = 0; u < 4; ++u)
+                    w[u] = pack_h2(dev::load_as_f32(a.q, a.q_dtype, q0 + 2 * u), dev::load_as_f32(a.q, a.q_dtype, q0 + 2 * u + 1));
+                v = make_uint4(w[0], w[1], w[2], w[3]);
+            }
+        } else if (g < G) {
+            v = *(const uint4*)((const uint16_t*)a.q + (r.qrow * (int64_t)a.hq + qh0 + g) * DH + c8 * 8);
+        }
+        *(uint4*)(smem + C::Q_OFF + g * C::Q_PITCH + c8 * 16) = v;
+    }
+    __syncthreads();
 
     // Q fragments.  Rows form: A fragments (m16k16 per 16 columns of d), rows
     // g = lane/4 (+8).  HN: B fragments (k16 x n8), head lane/4, dims
@@ -354,11 +362,6 @@ __global__ void __launch_bounds__(128) attn_decode_mma_kernel(const __grid_const
     float m_r[2] = {-INFINITY, -INFINITY}, l_r[2] = {0.f, 0.f};
 
     bool aborted = false;
-    for (int t = 0; t < ST - 1 && t < ntiles; ++t) issue(t, t);
-    if (SPLIT && ntiles > 0) {
-        issue_half(0, 0);
-        issue_half(0, 1);
-    }
     for (int t = 0; t < ntiles; ++t) {
         const int st = t % ST;
         if (!SPLIT && t + ST - 1 < ntiles) issue(t + ST - 1, (t + ST - 1) % ST);
