@@ -859,7 +859,8 @@ int64_t mma_blocks_per_split(int64_t total_blocks, int dh) {
     // Small launches (a sliding window, a short cache) still give each CTA up
     // to 4 tiles while that leaves a CTA per SM (two at head_dim 256, where
     // three CTAs share an SM and a launch of one per SM would leave SMs idle:
-    // config-4 window decode 16.0 us at 4 tiles per CTA, 15.1 at 3): a CTA of
+    // config-4 window decode 15.8 us at 4 tiles per CTA, 14.7 at 3, 19.6 at 2,
+    // which no longer fits one wave): a CTA of
     // one tile pays its load latency with nothing to overlap it and adds a
     // split to merge.
     int64_t b = total_blocks / (148 * 6);
