@@ -1241,13 +1241,17 @@ def extra_config4(torch, dev, small=False):
     # the group's five sliding-window layers, each its own caches: 5 x 67 MB
     # of windows, so consecutive window decodes do not find their rows in L2
     NL = 5
-    gcaches, lsets = [], [[] for _ in range(NL)]
+    gcaches, lsets, q8caches = [], [[] for _ in range(NL)], []
     for b_ in range(B):
         kk = torch.randn(L, hkv * dh, device=dev, generator=g).to(torch.bfloat16)
         vv = torch.randn(L, hkv * dh, device=dev, generator=g).to(torch.bfloat16)
         c = nm.FullAttentionCache(hkv, dh, capacity=L, dtype="bf16", device=dev.index)
         c.append(0, kk, vv)
         gcaches.append(c)
+        # the same rows in a Q8_0 cache (quantised on append) for the global layer
+        c8 = nm.FullAttentionCache(hkv, dh, capacity=L, dtype="q8_0", device=dev.index)
+        c8.append(0, kk, vv)
+        q8caches.append(c8)
         for li in range(NL):
             lc = nm.LocalAttentionCache(hkv, dh, W, capacity=2 * W, dtype="bf16", device=dev.index)
             lo = L - W - li * W  # a different window of rows per layer
@@ -1275,6 +1279,16 @@ def extra_config4(torch, dev, small=False):
                                         "kernel": "sliding-window layer decode (one cluster per row's splits)",
                                         "note": f"{NL} layers' window caches ({NL * bytes_l / 1e6:.0f} MB > L2) "
                                                 "decoded in turn"}}
+    try:  # the global layer over Q8_0 caches of the same rows (136 bytes per 128 values: int8 + fp16 scales)
+        ms8 = graph_time(torch, dev, lambda: nm.attend_batch(q8caches, qd, None, out=od), 10, 2)
+        bytes8 = B * L * hkv * (dh + dh // 32 * 2) * 2
+        gb8 = bytes8 / (ms8 * 1e-3) / 1e9
+        res["decode"]["q8_0"] = {"global_us": ms8 * 1e3, "time_vs_bf16": ms8 / ms_g, "bytes_vs_bf16": bytes8 / bytes_g,
+                                 "value": gb8, "unit": "GB/s",
+                                 "roofline": {"bound": "hbm", "achieved": gb8, "peak": p["hbm"], "frac": gb8 / p["hbm"],
+                                              "kernel": "attn_decode_mma_kernel<256, Q8_0>, global layer"}}
+    except Exception as e:  # report, never hide, a failing part
+        res["decode"]["q8_0"] = {"error": f"{type(e).__name__}: {str(e)[:200]}"}
     return {"workload": "config 4: Gemma hybrid bf16, 8q/4kv, d256, scale 1, 5 local (W=1024) : 1 global", **res}
 
 

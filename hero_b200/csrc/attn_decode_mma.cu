@@ -109,9 +109,9 @@ __device__ __forceinline__ bool mma_row(const MmaArgs& a, int64_t w, MmaRow& r) 
     return r.s < r.nsplit;
 }
 
-// Q8_0 tiles at head_dim 128 with the heads in N become MMA fragments in
-// registers, straight from the quants (no fp16 copy of the tile).
-constexpr bool q8_in_registers(int dh, bool q8, bool hn) { return q8 && hn && dh == 128; }
+// Q8_0 tiles at head_dim 128 and 256 with the heads in N become MMA fragments
+// in registers, straight from the quants (no fp16 copy of the tile).
+constexpr bool q8_in_registers(int dh, bool q8, bool hn) { return q8 && hn && (dh == 128 || dh == 256); }
 
 template <int DH, bool Q8 = false, bool Q8R = false, bool HN = false>
 struct MmaCfg {
@@ -145,8 +145,8 @@ struct MmaCfg {
     static_assert(SMEM <= 232448, "shared memory budget");
     static_assert(!Q8 || (Q8_QBYTES % 16 == 0 && Q8_SBYTES % 16 == 0 && F16_OFF % 1024 == 0),
                   "bulk copies move 16-byte multiples; the fp16 tiles keep the 128-byte swizzle atoms aligned");
-    static_assert(!Q8R || (DH == 128 && Q8_QBYTES % 1024 == 0 && STAGE_BYTES % 1024 == 0),
-                  "the swizzled quant tiles start on 1024-byte boundaries, one 128-byte row per key");
+    static_assert(!Q8R || (DH % 128 == 0 && Q8_QBYTES % 1024 == 0 && STAGE_BYTES % 1024 == 0),
+                  "the swizzled quant tiles start on 1024-byte boundaries, 128-byte rows per key and box");
 };
 
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
@@ -254,9 +254,12 @@ __global__ void __launch_bounds__(128) attn_decode_mma_kernel(const __grid_const
                 // (the buffers carry 64 spare rows past the last head).
                 const Q8Src& q8 = a.q8[r.map];
                 unsigned char* dst = smem + st * C::STAGE_BYTES;
-                if constexpr (Q8R) {  // quants through the 128-byte swizzle: one 128-byte row per key
-                    dev::tma_load_2d(dst, tmk, 0, row, &full[st]);
-                    dev::tma_load_2d(dst + C::Q8_QBYTES, tmv, 0, row, &full[st]);
+                if constexpr (Q8R) {  // quants through the 128-byte swizzle: boxes of 128 dims, a 128-byte row per key
+#pragma unroll
+                    for (int c = 0; c < DH / 128; ++c) {
+                        dev::tma_load_2d(dst + c * KT * 128, tmk, c * 128, row, &full[st]);
+                        dev::tma_load_2d(dst + C::Q8_QBYTES + c * KT * 128, tmv, c * 128, row, &full[st]);
+                    }
                 } else {
                     dev::bulk_g2s(dst, q8.k + (int64_t)row * DH, C::Q8_QBYTES, &full[st]);
                     dev::bulk_g2s(dst + C::Q8_QBYTES, q8.v + (int64_t)row * DH, C::Q8_QBYTES, &full[st]);
@@ -416,15 +419,21 @@ __global__ void __launch_bounds__(128) attn_decode_mma_kernel(const __grid_const
             const unsigned char* stg = smem + st * C::STAGE_BYTES;
             const unsigned char* ksc = stg + 2 * C::Q8_QBYTES;
             const int g = lane >> 2, qd = lane & 3, ra = key0 + g;
-            const uint2 sa = *(const uint2*)(ksc + ra * (DH / 32) * 2);        // 4 fp16 scales of key ra
-            const uint2 sb = *(const uint2*)(ksc + (ra + 8) * (DH / 32) * 2);  // and of key ra + 8
+            uint32_t sa[DH / 64], sb[DH / 64];  // the fp16 scales of keys ra and ra + 8, two per word
+#pragma unroll
+            for (int i = 0; i < DH / 64; ++i) {
+                sa[i] = *(const uint32_t*)(ksc + ra * (DH / 32) * 2 + 4 * i);
+                sb[i] = *(const uint32_t*)(ksc + (ra + 8) * (DH / 32) * 2 + 4 * i);
+            }
 #pragma unroll
             for (int b = 0; b < DH / 32; ++b) {
-                const uint32_t off = (uint32_t)ra * 128 + ((((2 * b + (qd >> 1)) ^ (ra & 7))) << 4) + (qd & 1) * 8;
+                // block b: box b / 4 (128 dims), 16-byte chunk 2 (b % 4) + q / 2 of the key's row
+                const uint32_t off = (uint32_t)(b >> 2) * (KT * 128) + (uint32_t)ra * 128 +
+                                     ((((2 * (b & 3) + (qd >> 1)) ^ (ra & 7))) << 4) + (qd & 1) * 8;
                 const uint2 wa = *(const uint2*)(stg + off), wb = *(const uint2*)(stg + off + 8 * 128);
                 const uint32_t sel = (b & 1) ? 0x3232u : 0x1010u;
-                const uint32_t s2a = __byte_perm(b < 2 ? sa.x : sa.y, 0, sel);
-                const uint32_t s2b = __byte_perm(b < 2 ? sb.x : sb.y, 0, sel);
+                const uint32_t s2a = __byte_perm(sa[b >> 1], 0, sel);
+                const uint32_t s2b = __byte_perm(sb[b >> 1], 0, sel);
                 const __half2 sca = *reinterpret_cast<const __half2*>(&s2a);
                 const __half2 scb = *reinterpret_cast<const __half2*>(&s2b);
                 auto deq = [&](uint32_t x, uint32_t pick, __half2 sc) -> uint32_t {
@@ -589,21 +598,26 @@ __global__ void __launch_bounds__(128) attn_decode_mma_kernel(const __grid_const
             const unsigned char* vqt = stg + C::Q8_QBYTES;
             const unsigned char* vsc = stg + 2 * C::Q8_QBYTES + C::Q8_SBYTES;
             const int g = lane >> 2, k0 = key0 + 2 * (lane & 3);
-            uint2 s4[4];  // 4 fp16 scales of keys k0, k0 + 1, k0 + 8, k0 + 9
+            uint32_t s4[4][DH / 64];  // the fp16 scales of keys k0, k0 + 1, k0 + 8, k0 + 9, two per word
 #pragma unroll
-            for (int i = 0; i < 4; ++i) s4[i] = *(const uint2*)(vsc + (k0 + (i & 1) + 8 * (i >> 1)) * (DH / 32) * 2);
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int w2 = 0; w2 < DH / 64; ++w2)
+                    s4[i][w2] = *(const uint32_t*)(vsc + (k0 + (i & 1) + 8 * (i >> 1)) * (DH / 32) * 2 + 4 * w2);
 #pragma unroll
             for (int p = 0; p < DH / 32; ++p) {
-                const int c = 2 * p + (g >> 2);
-                const uint32_t o0 = (uint32_t)k0 * 128 + ((c ^ (k0 & 7)) << 4) + (g & 3) * 4;
-                const uint32_t o1 = (uint32_t)(k0 + 1) * 128 + ((c ^ ((k0 + 1) & 7)) << 4) + (g & 3) * 4;
+                // dims 32p + 4g: box p / 4 (128 dims), 16-byte chunk 2 (p % 4) + g / 4 of the key's row
+                const int c = 2 * (p & 3) + (g >> 2);
+                const uint32_t box = (uint32_t)(p >> 2) * (KT * 128);
+                const uint32_t o0 = box + (uint32_t)k0 * 128 + ((c ^ (k0 & 7)) << 4) + (g & 3) * 4;
+                const uint32_t o1 = box + (uint32_t)(k0 + 1) * 128 + ((c ^ ((k0 + 1) & 7)) << 4) + (g & 3) * 4;
                 const uint32_t x0 = *(const uint32_t*)(vqt + o0) ^ 0x80808080u;
                 const uint32_t x1 = *(const uint32_t*)(vqt + o1) ^ 0x80808080u;
                 const uint32_t x2 = *(const uint32_t*)(vqt + o0 + 8 * 128) ^ 0x80808080u;
                 const uint32_t x3 = *(const uint32_t*)(vqt + o1 + 8 * 128) ^ 0x80808080u;
                 const uint32_t ssel = (p & 1) ? 0x7632u : 0x5410u;
-                const uint32_t s01 = __byte_perm(p < 2 ? s4[0].x : s4[0].y, p < 2 ? s4[1].x : s4[1].y, ssel);
-                const uint32_t s23 = __byte_perm(p < 2 ? s4[2].x : s4[2].y, p < 2 ? s4[3].x : s4[3].y, ssel);
+                const uint32_t s01 = __byte_perm(s4[0][p >> 1], s4[1][p >> 1], ssel);
+                const uint32_t s23 = __byte_perm(s4[2][p >> 1], s4[3][p >> 1], ssel);
                 const __half2 sc01 = *reinterpret_cast<const __half2*>(&s01);
                 const __half2 sc23 = *reinterpret_cast<const __half2*>(&s23);
                 auto deq = [&](uint32_t x, uint32_t pick, __half2 sc) -> uint32_t {
@@ -892,8 +906,9 @@ bool decode_mma_supported(const nmg_kv_cache* c, int q_dtype) {
     return true;
 }
 
-// Tensor maps of a Q8_0 cache's quants at head_dim 128: rows of 128 int8
-// (the 64 spare rows included), 64-row boxes under the 128-byte swizzle.
+// Tensor maps of a Q8_0 cache's quants at head_dim 128 or 256: rows of dh
+// int8 (the 64 spare rows included), boxes of 128 x 64 rows under the
+// 128-byte swizzle.
 static int make_q8_tensor_maps(const nmg_kv_cache* c, CUtensorMap* k, CUtensorMap* v) {
     EncodeTiledFn enc = encode_tiled_fn();
     if (!enc) return set_error(NMG_UNSUPPORTED, "cuTensorMapEncodeTiled unavailable");
@@ -916,7 +931,7 @@ static int kv_sources(const nmg_kv_cache* c, MmaArgs* a, int i) {
     if (c->dtype == NMG_Q8_0) {
         a->q8[i] = Q8Src{(const int8_t*)c->k, (const int8_t*)c->v, (const uint16_t*)c->ks, (const uint16_t*)c->vs,
                          c->sstride};
-        return c->dh == 128 ? make_q8_tensor_maps(c, &a->tm_k[i], &a->tm_v[i]) : NMG_OK;
+        return c->dh == 128 || c->dh == 256 ? make_q8_tensor_maps(c, &a->tm_k[i], &a->tm_v[i]) : NMG_OK;
     }
     return make_kv_tensor_maps(c, KT, &a->tm_k[i], &a->tm_v[i]);
 }

@@ -91,6 +91,27 @@ def test_batched_decode_config5_shape(dev, q_dtype):
         assert_close(out[b:b + 1], want, what=f"sequence {b} ({L} rows)")
 
 
+def test_batched_decode_gemma_global_shape(dev):
+    # Config 4's heads (8 query heads over 4 K/V heads, head_dim 256, scale 1)
+    # over ragged Q8_0 caches filled from bf16 rows: the fragments built from
+    # the quants in registers at head_dim 256, with key splits merged.
+    hq, hkv, dh = 8, 4, 256
+    lens = [9000, 130, 4097]
+    caches, kv = [], []
+    for i, L in enumerate(lens):
+        k, v = oracle.round_bf16(_rows(80 + i, L, hkv * dh)), oracle.round_bf16(_rows(90 + i, L, hkv * dh))
+        c = nm.FullAttentionCache(hkv, dh, capacity=L, dtype="q8_0")
+        c.append(0, torch.from_numpy(k).to(dev).bfloat16(), torch.from_numpy(v).to(dev).bfloat16())
+        caches.append(c)
+        kv.append((_deq(k, hkv, dh), _deq(v, hkv, dh)))
+    q = torch.from_numpy(_rows(99, len(lens), hq * dh, 0.1)).to(dev).bfloat16()
+    out = nm.attend_batch(caches, q, None, out_dtype=torch.float32).cpu().numpy()
+    qh = q.float().cpu().numpy()
+    for b, L in enumerate(lens):
+        want = oracle.attend(kv[b][0], kv[b][1], 0, 0, hkv, dh, qh[b:b + 1], hq, L - 1, use_scale=False)
+        assert_close(out[b:b + 1], want, what=f"sequence {b} ({L} rows)")
+
+
 @pytest.mark.parametrize("dh,hq,hkv", [(64, 4, 2), (128, 8, 2), (128, 32, 2), (256, 8, 4)])
 def test_rows_and_window_decode(dev, dh, hq, hkv):
     # Several query rows over a wrapped sliding-window Q8_0 cache (scale 1, the
