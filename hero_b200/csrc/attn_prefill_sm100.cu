@@ -637,7 +637,11 @@ int attend_rows_prefill(const nmg_kv_cache* c, int hq, const void* q, int q_dtyp
     }
     // Two query heads of one GQA group a unit (they share every K/V block)
     // where the group is even; one head a unit otherwise.
-    const bool pair = dh == 128 && (hq / c->hkv) % 2 == 0;
+    // Two heads per unit when the pair units alone fill the GPU; with fewer
+    // (a sharded launch's few heads) a pair unit's two heads would run in
+    // series on one SM, so the heaviest causal tile takes twice as long as
+    // with one head per unit.
+    const bool pair = dh == 128 && (hq / c->hkv) % 2 == 0 && (rows + 127) / 128 * (hq / 2) >= 148;
     const int bn = pair ? 128 : prefill_block_keys(c);
     // Rows per V copy: a V piece is half a 128-key block at head_dim 256.
     const int v_rows = !pair && dh == 256 && bn == 128 ? 64 : bn;

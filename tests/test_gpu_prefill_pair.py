@@ -1,10 +1,11 @@
 """The two prefill kernels against the oracle across the shapes that pick them.
 
 head_dim 128 with an even GQA group runs the two-head kernel (two query heads
-of one group per unit, sharing every K/V block); an odd group runs the
-one-head kernel.  Both are checked here on ragged tiles, sliding windows,
-chunked prefill into a cache that already holds rows, key splits (few heads)
-and many units per persistent CTA, all against the reference reduction
+of one group per unit, sharing every K/V block) when its units fill the GPU
+(query tiles x head pairs >= 148); an odd group, or fewer units (a sharded
+launch's few heads), runs the one-head kernel.  Both are checked here on
+ragged tiles, sliding windows, chunked prefill into a cache that already
+holds rows and many units per persistent CTA, all against the reference reduction
 (qwen35.hpp:360-382, gemma4.hpp:593-615) within max abs 2e-3 / rel L2 1e-3.
 """
 import numpy as np
@@ -27,7 +28,8 @@ def _dev(a, dev, code):
     return torch.from_numpy(np.ascontiguousarray(a)).to(dev).to(torch.bfloat16 if code == "bf16" else torch.float16)
 
 
-@pytest.mark.parametrize("hq,hkv,S,code", [(8, 4, 1000, "bf16"), (16, 2, 777, "f16"), (6, 2, 600, "bf16"),
+@pytest.mark.parametrize("hq,hkv,S,code", [(32, 8, 1200, "bf16"), (32, 4, 1150, "f16"),
+                                            (8, 4, 1000, "bf16"), (16, 2, 777, "f16"), (6, 2, 600, "bf16"),
                                            (4, 4, 300, "bf16"), (64, 8, 1280, "bf16")])
 def test_prefill_groups_match_oracle(dev, hq, hkv, S, code):
     dh = 128
@@ -44,10 +46,10 @@ def test_prefill_groups_match_oracle(dev, hq, hkv, S, code):
 def test_prefill_pair_chunked_into_a_filled_cache(dev):
     # Rows 500.. of a sequence whose first 500 rows are cached already: query
     # tiles start mid key block, and the first tile sees 4+ blocks.
-    hq, hkv, dh, S0, S1 = 8, 2, 128, 500, 700
+    hq, hkv, dh, S0, S1 = 32, 8, 128, 500, 1200  # 10 tiles x 16 head pairs: the two-head kernel
     S = S0 + S1
     k, v, q = _rnd("bf16", 7, 1, (S, hkv * dh)), _rnd("bf16", 7, 2, (S, hkv * dh)), _rnd("bf16", 7, 3, (S1, hq * dh))
-    cache = nm.FullAttentionCache(hkv, dh, capacity=1280, dtype="bf16")
+    cache = nm.FullAttentionCache(hkv, dh, capacity=1792, dtype="bf16")
     cache.append(0, _dev(k[:S0], dev, "bf16"), _dev(v[:S0], dev, "bf16"))
     out = nm.append_attend(cache, S0, _dev(k[S0:], dev, "bf16"), _dev(v[S0:], dev, "bf16"), _dev(q, dev, "bf16"),
                            0.09, out_dtype=torch.float32).cpu().numpy()
@@ -59,7 +61,7 @@ def test_prefill_pair_chunked_into_a_filled_cache(dev):
 def test_prefill_pair_sliding_window(dev, W):
     # A Gemma-style local layer (scale 1) through the two-head kernel: the
     # window's lower edge masks inside blocks and whole blocks drop out.
-    hq, hkv, dh, S = 8, 4, 128, 2500
+    hq, hkv, dh, S = 32, 16, 128, 2500  # 20 tiles x 16 head pairs: the two-head kernel
     k, v, q = _rnd("bf16", 9, 1, (S, hkv * dh)), _rnd("bf16", 9, 2, (S, hkv * dh)), _rnd("bf16", 9, 3, (S, hq * dh))
     q = q * np.float32(0.05)
     q = oracle.round_bf16(q).reshape(q.shape)
@@ -73,9 +75,9 @@ def test_prefill_pair_sliding_window(dev, W):
 
 
 def test_prefill_pair_key_splits_repeat_exactly(dev):
-    # Two query heads over 3000 causal rows: one head pair, so the heavy tiles
-    # are cut into key splits whose partials the last CTA merges for both
-    # heads; the tickets return to zero, so repeated calls agree bit for bit.
+    # Two query heads over 3000 causal rows: one head pair, too few units for
+    # the two-head kernel, so the heads run as units of their own; repeated
+    # calls agree bit for bit.
     hq, hkv, dh, S = 2, 1, 128, 3000
     k, v, q = _rnd("bf16", 11, 1, (S, hkv * dh)), _rnd("bf16", 11, 2, (S, hkv * dh)), _rnd("bf16", 11, 3, (S, hq * dh))
     cache = nm.FullAttentionCache(hkv, dh, capacity=3072, dtype="bf16")
